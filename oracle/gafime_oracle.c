@@ -1,0 +1,261 @@
+/*
+ * gafime_oracle.c -- CPU restatement of GAFIME's pair-scoring arithmetic.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker for the CUDA path: only
+ * tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg may load it.
+ * The product (gafime_b200/) never calls it and has no CPU fallback.
+ *
+ * Parity is pinned: tests/test_oracle.py checks every function here against
+ * golden vectors produced by the reference's own code (gafime_core.cpp and
+ * cpu_backend.cpp compiled unmodified by oracle/Makefile, and the reference's
+ * numpy metrics), committed under tests/golden/ with the script that made them.
+ *
+ * Three semantics are restated, each citing the reference lines it follows:
+ *
+ *  1. Raw-operator moments (kernel-API path, src/cpu/cpu_backend.cpp):
+ *     x = combine(a, b) evaluated in fp32 (cpu_backend.cpp:87-103), rows with
+ *     NaN x or y skipped (cpu_backend.cpp:274), sums of n, x, y, x^2, y^2, x*y
+ *     accumulated in fp64 (cpu_backend.cpp:276-293).  Unlike the reference the
+ *     six sums are returned in fp64 instead of being cast to float
+ *     (cpu_backend.cpp:296-307), and the divide epsilon is a parameter instead
+ *     of the literal 1e-8f (cpu_backend.cpp:94).
+ *
+ *  2. Pearson from the six sums (gafime/backends/native_cuda_backend.py:471-486).
+ *
+ *  3. Centred-product scoring (Selector / Engine / gafime_core path,
+ *     gafime_core/src/gafime_core.cpp:425-623): column means in fp64 in serial
+ *     row order (gafime_core.cpp:134-150), centred product in fp64
+ *     (gafime_core.cpp:571-577), Pearson via pearson_from_sums
+ *     (gafime_core.cpp:179-198) against the centred target
+ *     (gafime_core.cpp:486-497), mutual information with equal-width min/max
+ *     bins on both axes (gafime_core.cpp:200-226, 267-333).
+ *
+ * Data layout: X is column-major fp32, column f at X + f * ld, n rows.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define OR_MULT 0
+#define OR_ADD 1
+#define OR_SUB 2
+#define OR_DIV 3
+
+/* combine_cpu, cpu_backend.cpp:87-103, with the divide epsilon as a parameter. */
+static inline float or_combine(float a, float b, int op, float eps) {
+    switch (op) {
+        case OR_ADD: return a + b;
+        case OR_SUB: return a - b;
+        case OR_DIV: return a / (fabsf(b) < eps ? copysignf(eps, b) : b);
+        case OR_MULT:
+        default: return a * b;
+    }
+}
+
+/* Six fp64 sums of one pair: out = [n, sx, sy, sxx, syy, sxy].
+ * Follows gafime_fused_interaction_perpair_cpu (cpu_backend.cpp:229-295) for
+ * arity 2, identity unary ops and every row in the "train" split
+ * (val_fold_id = 255 never matches the all-zero mask the reference uploads,
+ * native_cuda_backend.py:344,371). */
+void gafime_oracle_pair_moments(const float* xa, const float* xb, const float* y,
+                                int64_t n, int op, float div_eps, double* out) {
+    double cn = 0, sx = 0, sy = 0, sxx = 0, syy = 0, sxy = 0;
+    for (int64_t r = 0; r < n; ++r) {
+        float x = or_combine(xa[r], xb[r], op, div_eps);
+        float yv = y[r];
+        if (isnan(x) || isnan(yv)) continue;
+        double xd = (double)x, yd = (double)yv;
+        cn += 1.0;
+        sx += xd;
+        sy += yd;
+        sxx += xd * xd;
+        syy += yd * yd;
+        sxy += xd * yd;
+    }
+    out[0] = cn; out[1] = sx; out[2] = sy; out[3] = sxx; out[4] = syy; out[5] = sxy;
+}
+
+/* _pearson_from_stats, native_cuda_backend.py:471-486. */
+double gafime_oracle_pearson_from_stats(const double* s) {
+    double n = s[0];
+    if (n <= 1.0) return 0.0;
+    double var_x = s[3] - s[1] * s[1] / n;
+    double var_y = s[4] - s[2] * s[2] / n;
+    double cov = s[5] - s[1] * s[2] / n;
+    double denom_sq = var_x * var_y;
+    if (denom_sq <= 0.0) return 0.0;
+    return cov / sqrt(denom_sq);
+}
+
+/* Signed raw-operator Pearson for a list of pairs (i, j): x = X[:,i] op X[:,j].
+ * Pairs are independent; the loop over pairs is parallel when built with OpenMP. */
+void gafime_oracle_raw_pearson(const float* X, int64_t ld, const float* y, int64_t n,
+                               const int32_t* pi, const int32_t* pj, int64_t n_pairs,
+                               int op, float div_eps, double* out_r, double* out_stats) {
+#pragma omp parallel for schedule(dynamic, 16)
+    for (int64_t p = 0; p < n_pairs; ++p) {
+        double s[6];
+        gafime_oracle_pair_moments(X + (int64_t)pi[p] * ld, X + (int64_t)pj[p] * ld, y, n,
+                                   op, div_eps, s);
+        out_r[p] = gafime_oracle_pearson_from_stats(s);
+        if (out_stats) memcpy(out_stats + 6 * p, s, sizeof(s));
+    }
+}
+
+/* ---------------------------------------------------------------------------
+ * Centred-product semantics of gafime_core.score_combos.
+ * ------------------------------------------------------------------------- */
+
+/* compute_means, gafime_core.cpp:134-150: serial row order, fp64. */
+void gafime_oracle_column_means(const float* X, int64_t ld, int64_t n, int64_t f_count,
+                                double* means) {
+    for (int64_t f = 0; f < f_count; ++f) {
+        double sum = 0.0;
+        const float* col = X + f * ld;
+        for (int64_t r = 0; r < n; ++r) sum += (double)col[r];
+        means[f] = (n == 0) ? 0.0 : sum / (double)n;
+    }
+}
+
+/* pearson_from_sums, gafime_core.cpp:179-198. */
+static double or_pearson_from_sums(double sum_x, double sum_x2, double dot_xy, double var_y,
+                                   int64_t n) {
+    if (n == 0) return 0.0;
+    double mean_x = sum_x / (double)n;
+    double var_x = sum_x2 - (sum_x * mean_x);
+    if (var_x <= 0.0 || var_y <= 0.0) return 0.0;
+    double denom = sqrt(var_x * var_y);
+    if (denom == 0.0) return 0.0;
+    return dot_xy / denom;
+}
+
+/* build_bins, gafime_core.cpp:200-226 (fp64 values). Returns 0 when the
+ * values are constant or bins < 2, as the reference does. */
+static int or_build_bins(const double* v, int64_t n, int bins, int32_t* out) {
+    if (bins < 2 || n == 0) return 0;
+    double vmin = v[0], vmax = v[0];
+    for (int64_t i = 1; i < n; ++i) {
+        vmin = v[i] < vmin ? v[i] : vmin;
+        vmax = v[i] > vmax ? v[i] : vmax;
+    }
+    if (vmin == vmax) return 0;
+    double scale = (double)bins / (vmax - vmin);
+    for (int64_t i = 0; i < n; ++i) {
+        int b = (int)((v[i] - vmin) * scale);
+        if (b < 0) b = 0; else if (b >= bins) b = bins - 1;
+        out[i] = b;
+    }
+    return 1;
+}
+
+/* mutual_info_from_vector, gafime_core.cpp:267-333. */
+static double or_mutual_info(const double* x, int64_t n, int bins, const int32_t* y_bins,
+                             double* joint, double* p_x, double* p_y) {
+    if (bins < 2 || n == 0) return 0.0;
+    double xmin = x[0], xmax = x[0];
+    for (int64_t i = 1; i < n; ++i) {
+        xmin = x[i] < xmin ? x[i] : xmin;
+        xmax = x[i] > xmax ? x[i] : xmax;
+    }
+    if (xmin == xmax) return 0.0;
+    size_t b2 = (size_t)bins * (size_t)bins;
+    memset(joint, 0, b2 * sizeof(double));
+    memset(p_x, 0, (size_t)bins * sizeof(double));
+    memset(p_y, 0, (size_t)bins * sizeof(double));
+    double scale = (double)bins / (xmax - xmin);
+    for (int64_t i = 0; i < n; ++i) {
+        int xb = (int)((x[i] - xmin) * scale);
+        if (xb < 0) xb = 0; else if (xb >= bins) xb = bins - 1;
+        int yb = y_bins[i];
+        joint[(size_t)xb * bins + yb] += 1.0;
+        p_x[xb] += 1.0;
+        p_y[yb] += 1.0;
+    }
+    double inv_total = 1.0 / (double)n;
+    double inv_total_sq = inv_total * inv_total;
+    double mi = 0.0;
+    for (int bx = 0; bx < bins; ++bx) {
+        for (int by = 0; by < bins; ++by) {
+            double count = joint[(size_t)bx * bins + by];
+            if (count <= 0.0) continue;
+            double p = count * inv_total;
+            double expected = (p_x[bx] * p_y[by]) * inv_total_sq;
+            if (expected > 0.0) mi += p * log(p / expected);
+        }
+    }
+    return mi;
+}
+
+/* Centred-product scores for pairs (i, j) as gafime_core.score_combos computes
+ * them for 2-combos (gafime_core.cpp:531-618).  want_pearson / want_mi select
+ * the metrics; out_pearson / out_mi receive one value per pair (either may be
+ * NULL when not wanted).  X is column-major fp32 (exactly representable in
+ * fp64, so it equals the reference's float64 input of the same values). */
+int gafime_oracle_centred_scores(const float* X, int64_t ld, const float* y, int64_t n,
+                                 int64_t f_count, const int32_t* pi, const int32_t* pj,
+                                 int64_t n_pairs, int mi_bins, double* out_pearson,
+                                 double* out_mi) {
+    double* means = (double*)malloc((size_t)f_count * sizeof(double));
+    double* yc = (double*)malloc((size_t)n * sizeof(double));
+    double* yd = (double*)malloc((size_t)n * sizeof(double));
+    int32_t* y_bins = (int32_t*)malloc((size_t)n * sizeof(int32_t));
+    if (!means || !yc || !yd || !y_bins) {
+        free(means); free(yc); free(yd); free(y_bins);
+        return -3;
+    }
+    gafime_oracle_column_means(X, ld, n, f_count, means);
+    /* gafime_core.cpp:486-497 */
+    double sum_y = 0.0, sum_y2 = 0.0;
+    for (int64_t r = 0; r < n; ++r) {
+        yd[r] = (double)y[r];
+        sum_y += yd[r];
+        sum_y2 += yd[r] * yd[r];
+    }
+    double mean_y = (n == 0) ? 0.0 : sum_y / (double)n;
+    for (int64_t r = 0; r < n; ++r) yc[r] = yd[r] - mean_y;
+    double var_y = sum_y2 - sum_y * mean_y;
+    int mi_ready = 0;
+    if (out_mi) mi_ready = or_build_bins(yd, n, mi_bins, y_bins);
+
+    int status = 0;
+#pragma omp parallel
+    {
+        double* inter = (double*)malloc((size_t)n * sizeof(double));
+        size_t nb = mi_bins >= 2 ? (size_t)mi_bins : 2;
+        double* joint = (double*)malloc(nb * nb * sizeof(double));
+        double* p_x = (double*)malloc(nb * sizeof(double));
+        double* p_y = (double*)malloc(nb * sizeof(double));
+        if (!inter || !joint || !p_x || !p_y) {
+#pragma omp atomic write
+            status = -3;
+        } else {
+#pragma omp for schedule(dynamic, 8)
+            for (int64_t p = 0; p < n_pairs; ++p) {
+                const float* ca = X + (int64_t)pi[p] * ld;
+                const float* cb = X + (int64_t)pj[p] * ld;
+                double ma = means[pi[p]], mb = means[pj[p]];
+                double sum_x = 0.0, sum_x2 = 0.0, dot_xy = 0.0;
+                for (int64_t r = 0; r < n; ++r) {
+                    /* value = 1.0; value *= (a - ma); value *= (b - mb) */
+                    double v = 1.0;
+                    v *= ((double)ca[r] - ma);
+                    v *= ((double)cb[r] - mb);
+                    inter[r] = v;
+                    sum_x += v;
+                    sum_x2 += v * v;
+                    dot_xy += v * yc[r];
+                }
+                if (out_pearson) out_pearson[p] = or_pearson_from_sums(sum_x, sum_x2, dot_xy, var_y, n);
+                if (out_mi) {
+                    out_mi[p] = (mi_ready && mi_bins >= 2)
+                                    ? or_mutual_info(inter, n, mi_bins, y_bins, joint, p_x, p_y)
+                                    : 0.0;
+                }
+            }
+        }
+        free(inter); free(joint); free(p_x); free(p_y);
+    }
+    free(means); free(yc); free(yd); free(y_bins);
+    return status;
+}

@@ -1,0 +1,121 @@
+"""CPU oracle for the all-pairs scoring path -- TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg
+may import this module.  The product package (``gafime_b200``) never does and has
+no CPU fallback.
+
+The arithmetic lives in ``gafime_oracle.c`` (built into ``liboracle.so`` by the
+Makefile beside it); this file loads it with ctypes and adds the selection step:
+
+* ``raw_pearson``      -- kernel-API semantics (``src/cpu/cpu_backend.cpp:87-103,229-295``,
+  fp64 sums kept) + Pearson of ``native_cuda_backend.py:471-486``.
+* ``centred_scores``   -- ``gafime_core.score_combos`` semantics for 2-combos
+  (``gafime_core/src/gafime_core.cpp:425-623``): centred Pearson and equal-width MI.
+* ``topk``             -- stable selection by |score| descending
+  (``gafime/sklearn.py:62-71`` sorts by ``abs(metric)``), ties broken by the
+  normalised pair (i, j) ascending.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from typing import Optional, Tuple
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB: Optional[ctypes.CDLL] = None
+
+OP_IDS = {"multiply": 0, "add": 1, "subtract": 2, "divide": 3}
+
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+
+
+def build() -> str:
+    """Compile liboracle.so (idempotent) and return its path."""
+    path = os.path.join(_HERE, "liboracle.so")
+    src = os.path.join(_HERE, "gafime_oracle.c")
+    if not os.path.exists(path) or os.path.getmtime(path) < os.path.getmtime(src):
+        subprocess.run(["make", "-C", _HERE, "liboracle.so"], check=True,
+                       stdout=subprocess.DEVNULL)
+    return path
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        _LIB = ctypes.CDLL(build())
+        _LIB.gafime_oracle_raw_pearson.argtypes = [
+            _f32p, ctypes.c_int64, _f32p, ctypes.c_int64, _i32p, _i32p, ctypes.c_int64,
+            ctypes.c_int, ctypes.c_float, _f64p, ctypes.c_void_p]
+        _LIB.gafime_oracle_raw_pearson.restype = None
+        _LIB.gafime_oracle_centred_scores.argtypes = [
+            _f32p, ctypes.c_int64, _f32p, ctypes.c_int64, ctypes.c_int64, _i32p, _i32p,
+            ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+        _LIB.gafime_oracle_centred_scores.restype = ctypes.c_int
+        _LIB.gafime_oracle_pair_moments.argtypes = [
+            _f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, _f64p]
+        _LIB.gafime_oracle_pair_moments.restype = None
+    return _LIB
+
+
+def all_pairs(n_features: int) -> Tuple[np.ndarray, np.ndarray]:
+    """All pairs i < j in row-major upper-triangle order (the engine's pair order)."""
+    i, j = np.triu_indices(n_features, k=1)
+    return i.astype(np.int32), j.astype(np.int32)
+
+
+def _colmajor(X: np.ndarray) -> Tuple[np.ndarray, int, int, int]:
+    """Return a column-major float32 copy as a flat array plus (ld, n, F)."""
+    Xf = np.asarray(X, dtype=np.float32)
+    n, f = Xf.shape
+    flat = np.ascontiguousarray(Xf.T).reshape(-1)
+    return flat, n, n, f
+
+
+def raw_pearson(X: np.ndarray, y: np.ndarray, op: str, pi=None, pj=None,
+                div_eps: float = 1e-8, with_stats: bool = False):
+    """Signed Pearson r of x = X[:, i] op X[:, j] against y for each pair."""
+    flat, ld, n, f = _colmajor(X)
+    if pi is None:
+        pi, pj = all_pairs(f)
+    pi = np.ascontiguousarray(pi, dtype=np.int32)
+    pj = np.ascontiguousarray(pj, dtype=np.int32)
+    yv = np.ascontiguousarray(y, dtype=np.float32)
+    out = np.empty(len(pi), dtype=np.float64)
+    stats = np.empty((len(pi), 6), dtype=np.float64) if with_stats else None
+    lib().gafime_oracle_raw_pearson(
+        flat, ld, yv, n, pi, pj, len(pi), OP_IDS[op], np.float32(div_eps), out,
+        stats.ctypes.data if with_stats else None)
+    return (out, stats) if with_stats else out
+
+
+def centred_scores(X: np.ndarray, y: np.ndarray, pi=None, pj=None, pearson: bool = True,
+                   mi: bool = False, mi_bins: int = 16):
+    """(pearson, mi) arrays of the centred-product semantics of gafime_core."""
+    flat, ld, n, f = _colmajor(X)
+    if pi is None:
+        pi, pj = all_pairs(f)
+    pi = np.ascontiguousarray(pi, dtype=np.int32)
+    pj = np.ascontiguousarray(pj, dtype=np.int32)
+    yv = np.ascontiguousarray(y, dtype=np.float32)
+    out_p = np.empty(len(pi), dtype=np.float64) if pearson else None
+    out_m = np.empty(len(pi), dtype=np.float64) if mi else None
+    rc = lib().gafime_oracle_centred_scores(
+        flat, ld, yv, n, f, pi, pj, len(pi), int(mi_bins),
+        out_p.ctypes.data if pearson else None, out_m.ctypes.data if mi else None)
+    if rc != 0:
+        raise MemoryError("oracle allocation failed")
+    return out_p, out_m
+
+
+def topk(scores: np.ndarray, pi: np.ndarray, pj: np.ndarray, k: int, absolute: bool = True):
+    """Indices of the k best pairs: key (-|s|, min(i,j), max(i,j)) ascending."""
+    s = np.abs(scores) if absolute else np.asarray(scores)
+    lo = np.minimum(pi, pj)
+    hi = np.maximum(pi, pj)
+    order = np.lexsort((hi, lo, -s))
+    return order[:k]

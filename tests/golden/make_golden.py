@@ -1,0 +1,188 @@
+"""Generate the golden fixtures in this directory from the reference's own code.
+
+Run here, where the reference sources are present:
+
+    make -C oracle ref                      # compiles the reference's cpu_backend.cpp
+                                            # and gafime_core.cpp, unmodified, into oracle/_ref/
+    python tests/golden/make_golden.py [--ref /root/reference]
+
+Every expected value in the fixtures comes from the reference itself:
+
+* ``gafime_core.score_combos`` (gafime_core/src/gafime_core.cpp:425-623) for centred
+  Pearson and equal-width mutual information;
+* ``GafimeSelector.fit`` (gafime/sklearn.py:41-74) with ``backend='core'`` and
+  ``backend='python'`` for the end-to-end top-k;
+* the reference's numpy metrics (gafime/metrics/cpu_metrics.py) for the numpy twin;
+* ``gafime_fused_interaction_perpair_cpu`` (src/cpu/cpu_backend.cpp:229-310) for the
+  raw-operator 12-float statistics of all four operators.
+
+Inputs are stored beside the outputs, so the tests never depend on the random
+generator.  The fixtures are small (a few hundred KB in total).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import glob
+import hashlib
+import importlib.util
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+REF_BUILD = os.path.join(REPO, "oracle", "_ref")
+
+
+def _load_core():
+    path = glob.glob(os.path.join(REF_BUILD, "gafime_core*.so"))
+    if not path:
+        raise SystemExit("run `make -C oracle ref` first")
+    spec = importlib.util.spec_from_file_location("gafime_core", path[0])
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    sys.modules["gafime_core"] = mod  # CoreBackend imports it by this name
+    return mod
+
+
+def _load_cpu():
+    lib = ctypes.CDLL(os.path.join(REF_BUILD, "libgafime_cpu_ref.so"))
+    f = lib.gafime_fused_interaction_perpair_cpu
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_void_p,
+                  ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                  ctypes.c_void_p]
+    return lib
+
+
+def ref_raw_stats(lib, X: np.ndarray, y: np.ndarray, op: int) -> np.ndarray:
+    """12-float stats of every pair i<j from the unmodified reference CPU library."""
+    n, f = X.shape
+    cols = [np.ascontiguousarray(X[:, c], dtype=np.float32) for c in range(f)]
+    yv = np.ascontiguousarray(y, dtype=np.float32)
+    mask = np.zeros(n, dtype=np.uint8)
+    ops = np.zeros(2, dtype=np.int32)
+    inter = np.array([op], dtype=np.int32)
+    pi, pj = np.triu_indices(f, k=1)
+    out = np.zeros((len(pi), 12), dtype=np.float32)
+    for p, (i, j) in enumerate(zip(pi, pj)):
+        ptrs = (ctypes.c_void_p * 2)(cols[i].ctypes.data, cols[j].ctypes.data)
+        st = np.zeros(12, dtype=np.float32)
+        rc = lib.gafime_fused_interaction_perpair_cpu(
+            ptrs, yv.ctypes.data, mask.ctypes.data, ops.ctypes.data, 2, inter.ctypes.data,
+            255, n, st.ctypes.data)
+        assert rc == 0, rc
+        out[p] = st
+    return out
+
+
+def core_scores(core, X, y, metrics, mi_bins):
+    f = X.shape[1]
+    pi, pj = np.triu_indices(f, k=1)
+    combos = [(int(a), int(b)) for a, b in zip(pi, pj)]
+    idx, off = core.pack_combos(combos)
+    return np.asarray(core.score_combos(np.ascontiguousarray(X, dtype=np.float64),
+                                        np.ascontiguousarray(y, dtype=np.float64),
+                                        idx, off, list(metrics), mi_bins))
+
+
+def numpy_scores(X, y, mi_bins):
+    """The reference numpy Backend path: build_interaction_vector + cpu_metrics."""
+    from gafime.metrics import cpu_metrics
+    from gafime.utils.arrays import build_interaction_vector
+    X64 = np.ascontiguousarray(X, dtype=np.float64)
+    y64 = np.ascontiguousarray(y, dtype=np.float64)
+    f = X.shape[1]
+    pi, pj = np.triu_indices(f, k=1)
+    out = np.zeros((len(pi), 2))
+    for p, (a, b) in enumerate(zip(pi, pj)):
+        v = build_interaction_vector(X64, (int(a), int(b)))
+        out[p, 0] = cpu_metrics.pearson_corr(v, y64)
+        out[p, 1] = cpu_metrics.mutual_info(v, y64, bins=mi_bins)
+    return out
+
+
+def selector_top(X, y, k, backend):
+    from gafime.sklearn import GafimeSelector
+    sel = GafimeSelector(k=k, backend=backend, metric="pearson", operator="multiply")
+    sel.fit(X, y)
+    return np.array(sel.top_interactions_, dtype=np.int32)
+
+
+def sha(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    args = ap.parse_args()
+    sys.path.insert(0, args.ref)
+    core = _load_core()
+    cpu = _load_cpu()
+
+    # --- config 1: the README sklearn example at seed 0 --------------------------------
+    rng = np.random.default_rng(0)
+    X1 = rng.standard_normal((1000, 50)).astype(np.float32)
+    y1 = rng.binomial(1, 0.5, 1000).astype(np.float32)
+    c1 = core_scores(core, X1, y1, ("pearson", "mutual_info"), 16)
+    n1 = numpy_scores(X1, y1, 16)
+    top_core = selector_top(X1, y1, 5, "core")
+    top_py = selector_top(X1, y1, 5, "python")
+    np.savez_compressed(os.path.join(HERE, "config1_centred.npz"), X=X1, y=y1,
+                        core_scores=c1, numpy_scores=n1, selector_top_core=top_core,
+                        selector_top_python=top_py, x_sha=np.array(sha(X1)))
+    print("config1 top (core):", top_core.tolist(), "(python):", top_py.tolist())
+
+    # --- config-3 shape at small N: 3-class target, MI with 32 equal-width bins -------
+    rng = np.random.default_rng(0)
+    n3, f3 = 6000, 12
+    X3 = rng.standard_normal((n3, f3)).astype(np.float32)
+    e = rng.standard_normal((4, n3))
+    s0 = X3[:, 5].astype(np.float64) * X3[:, 9] + 0.5 * e[0]
+    s1 = X3[:, 1].astype(np.float64) + X3[:, 7] + 0.5 * e[1]
+    s2 = e[2] + 0.5 * e[3]
+    y3 = np.argmax(np.stack([s0, s1, s2]), axis=0).astype(np.float32)
+    m32 = core_scores(core, X3, y3, ("pearson", "mutual_info"), 32)
+    m16 = core_scores(core, X3, y3, ("mutual_info",), 16)
+    np.savez_compressed(os.path.join(HERE, "mi_3class.npz"), X=X3, y=y3, core_b32=m32,
+                        core_b16=m16)
+
+    # --- raw operators (kernel-API semantics), normal + lognormal columns -------------
+    rng = np.random.default_rng(0)
+    nr = 4096
+    Xn = rng.standard_normal((nr, 6))
+    Xl = rng.lognormal(0.0, 1.0, (nr, 6))
+    Xr = np.hstack([Xn, Xl]).astype(np.float32)
+    logit = 2.0 * Xr[:, 1].astype(np.float64) * Xr[:, 4] - 1.5 * Xr[:, 7] / (np.abs(Xr[:, 2]) + 1) \
+        + rng.standard_normal(nr)
+    yr = (rng.random(nr) < 1.0 / (1.0 + np.exp(-logit))).astype(np.float32)
+    # a few divisors within 1e-8 of zero exercise the safe-divide clamp
+    Xr[17, 3] = 0.0
+    Xr[33, 5] = -3e-9
+    raw = np.stack([ref_raw_stats(cpu, Xr, yr, op) for op in range(4)])
+    np.savez_compressed(os.path.join(HERE, "raw_ops.npz"), X=Xr, y=yr, ref_stats=raw)
+
+    # --- edge cases: constant column, tiny N, a NaN row -------------------------------
+    Xe = np.array([[1.0, 2.0, 5.0, 0.5],
+                   [2.0, 2.0, 4.0, -1.0],
+                   [3.0, 2.0, 3.0, 2.0],
+                   [4.0, 2.0, 2.0, 0.0],
+                   [5.0, 2.0, 1.0, 1.5],
+                   [6.0, 2.0, 0.0, -0.5],
+                   [7.0, 2.0, 1.0, 3.0]], dtype=np.float32)
+    ye = np.array([0, 1, 0, 1, 1, 0, 1], dtype=np.float32)
+    ce = core_scores(core, Xe, ye, ("pearson", "mutual_info"), 4)
+    rawe = np.stack([ref_raw_stats(cpu, Xe, ye, op) for op in range(4)])
+    Xnan = Xe.copy()
+    Xnan[3, 0] = np.nan
+    rawnan = np.stack([ref_raw_stats(cpu, Xnan, ye, op) for op in range(4)])
+    np.savez_compressed(os.path.join(HERE, "edge.npz"), X=Xe, y=ye, core_scores=ce,
+                        ref_stats=rawe, X_nan=Xnan, ref_stats_nan=rawnan)
+    print("wrote fixtures to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,78 @@
+"""Pin the CPU oracle against golden vectors made by the reference's own code.
+
+The fixtures come from tests/golden/make_golden.py (gafime_core.score_combos,
+GafimeSelector.fit, the reference numpy metrics and cpu_backend.cpp compiled
+unmodified).  If the oracle disagrees with them it cannot be trusted as the
+checker of the CUDA path.
+"""
+import numpy as np
+import pytest
+
+OPS = ["multiply", "add", "subtract", "divide"]
+
+
+def test_config1_centred_pearson_matches_gafime_core(golden, oracle):
+    g = golden("config1_centred.npz")
+    p, m = oracle.centred_scores(g["X"], g["y"], pearson=True, mi=True, mi_bins=16)
+    # Same operation order as gafime_core.cpp -> bit-identical doubles.
+    np.testing.assert_array_equal(p, g["core_scores"][:, 0])
+    np.testing.assert_array_equal(m, g["core_scores"][:, 1])
+    # The reference's numpy twin agrees to rounding.
+    np.testing.assert_allclose(p, g["numpy_scores"][:, 0], rtol=0, atol=1e-14)
+    np.testing.assert_allclose(m, g["numpy_scores"][:, 1], rtol=0, atol=1e-12)
+
+
+def test_config1_topk_matches_selector(golden, oracle):
+    g = golden("config1_centred.npz")
+    pi, pj = oracle.all_pairs(g["X"].shape[1])
+    p, _ = oracle.centred_scores(g["X"], g["y"])
+    top = oracle.topk(p, pi, pj, 5)
+    got = {(int(min(a, b)), int(max(a, b))) for a, b in zip(pi[top], pj[top])}
+    for key in ("selector_top_core", "selector_top_python"):
+        want = {(int(min(a, b)), int(max(a, b))) for a, b in g[key]}
+        assert got == want
+    # Known answer from the reference run: (3,15) is the best pair.
+    assert (int(pi[top[0]]), int(pj[top[0]])) == (3, 15)
+
+
+@pytest.mark.parametrize("bins,key", [(32, "core_b32"), (16, "core_b16")])
+def test_mi_3class_matches_gafime_core(golden, oracle, bins, key):
+    g = golden("mi_3class.npz")
+    _, m = oracle.centred_scores(g["X"], g["y"], pearson=False, mi=True, mi_bins=bins)
+    col = 1 if key == "core_b32" else 0
+    np.testing.assert_array_equal(m, g[key][:, col])
+
+
+@pytest.mark.parametrize("op_id,op", list(enumerate(OPS)))
+def test_raw_op_stats_match_cpu_backend(golden, oracle, op_id, op):
+    """The oracle keeps fp64 sums; the reference casts them to float32, so each
+    stat must agree to within one float32 rounding of the fp64 value."""
+    g = golden("raw_ops.npz")
+    r, st = oracle.raw_pearson(g["X"], g["y"], op, div_eps=1e-8, with_stats=True)
+    ref = g["ref_stats"][op_id][:, :6].astype(np.float64)
+    np.testing.assert_array_equal(st.astype(np.float32), ref.astype(np.float32))
+    # The validation half of the reference stats is empty (val_fold_id=255).
+    assert np.all(g["ref_stats"][op_id][:, 6:] == 0)
+
+
+def test_edge_cases_match_reference(golden, oracle):
+    g = golden("edge.npz")
+    p, m = oracle.centred_scores(g["X"], g["y"], pearson=True, mi=True, mi_bins=4)
+    np.testing.assert_array_equal(p, g["core_scores"][:, 0])
+    np.testing.assert_array_equal(m, g["core_scores"][:, 1])
+    # constant column 1 -> Pearson 0 and MI 0 for every pair touching it
+    pi, pj = oracle.all_pairs(4)
+    touch = (pi == 1) | (pj == 1)
+    assert np.all(p[touch] == 0) and np.all(m[touch] == 0)
+    for op_id, op in enumerate(OPS):
+        _, st = oracle.raw_pearson(g["X"], g["y"], op, with_stats=True)
+        np.testing.assert_array_equal(st.astype(np.float32), g["ref_stats"][op_id][:, :6])
+        _, stn = oracle.raw_pearson(g["X_nan"], g["y"], op, with_stats=True)
+        np.testing.assert_array_equal(stn.astype(np.float32), g["ref_stats_nan"][op_id][:, :6])
+
+
+def test_topk_tie_order_is_pair_ascending(oracle):
+    s = np.array([0.5, -0.5, 0.2, 0.5])
+    pi = np.array([3, 0, 1, 0], dtype=np.int32)
+    pj = np.array([4, 2, 2, 1], dtype=np.int32)
+    assert oracle.topk(s, pi, pj, 3).tolist() == [3, 1, 0]
