@@ -1,0 +1,558 @@
+#!/usr/bin/env python
+"""All-pairs feature-pair x row scoring throughput on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload config2]
+                    [--impl ours|reference]
+
+One step = one pass of the hot path over the workload: column statistics, the
+pair-moment kernels, the scoring epilogue with top-k, the device merge, the D2H of
+the k best pairs per operator and, with N > 1 processes, the NCCL all-gather of
+every shard's candidates plus the deterministic merge.  Inputs are resident in
+HBM when the timed region starts (``value``); ``e2e`` repeats the step through
+the C ABI from pinned host buffers (upload inside the timed region).
+
+Multi-GPU: launched with torchrun, one process per GPU; each rank holds the full
+column-major matrix and scores its share of the pair tiles (strong scaling of a
+fixed job).  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import glob
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC_NAME = "feature-pair×row evals/sec"
+
+# ---------------------------------------------------------------- workloads --
+# Seeded synthetic stand-ins with the shapes and value distributions of the five
+# benchmark configurations (no public dataset is involved).
+
+
+def make_config1():
+    """1,000 x 50 N(0,1), Bernoulli(0.5) target, seed 0 (the README sklearn example)."""
+    rng = np.random.default_rng(0)
+    X = rng.standard_normal((1000, 50)).astype(np.float32)
+    y = rng.binomial(1, 0.5, 1000).astype(np.float32)
+    return X, y
+
+
+def make_config2(n: int = 1_000_000):
+    """n x 256: 128 N(0,1) + 128 lognormal(0,1) columns; y ~ Bernoulli(sigmoid(
+    2 x3 x17 - 1.5 x40 / (|x91| + 1) + N(0,1)))."""
+    rng = np.random.default_rng(0)
+    Xn = rng.standard_normal((n, 128))
+    Xl = rng.lognormal(0.0, 1.0, (n, 128))
+    X = np.hstack([Xn, Xl]).astype(np.float32)
+    del Xn, Xl
+    Xd = X.astype(np.float64, copy=False)
+    logit = 2.0 * Xd[:, 3] * Xd[:, 17] - 1.5 * Xd[:, 40] / (np.abs(Xd[:, 91]) + 1.0) \
+        + rng.standard_normal(n)
+    y = (rng.random(n) < 1.0 / (1.0 + np.exp(-logit))).astype(np.float32)
+    return X, y
+
+
+def make_config3(n: int = 4_000_000):
+    """n x 128 N(0,1); y = argmax(x5 x9 + 0.5 e0, x12 + x60 + 0.5 e1, e2 + 0.5 e3)."""
+    rng = np.random.default_rng(0)
+    X = rng.standard_normal((n, 128)).astype(np.float32)
+    e = rng.standard_normal((4, n))
+    s0 = X[:, 5].astype(np.float64) * X[:, 9] + 0.5 * e[0]
+    s1 = X[:, 12].astype(np.float64) + X[:, 60] + 0.5 * e[1]
+    s2 = e[2] + 0.5 * e[3]
+    y = np.argmax(np.stack([s0, s1, s2]), axis=0).astype(np.float32)
+    return X, y
+
+
+def fill_config4(packed: np.ndarray, n: int):
+    """Banking-style table written column by column into packed[(F+1), n]:
+    256 Zipf(1.1) integer codes (cardinality U[2,1000]) then 256 N(0,1);
+    y = 0.5 c7 x300 + 0.3 x301 x302 + N(0,1)."""
+    rng = np.random.default_rng(0)
+    for c in range(256):
+        kc = int(rng.integers(2, 1001))
+        p = (np.arange(kc) + 1.0) ** -1.1
+        cdf = np.cumsum(p / p.sum())
+        packed[c] = np.minimum(np.searchsorted(cdf, rng.random(n)), kc - 1).astype(np.float32)
+    for c in range(256, 512):
+        packed[c] = rng.standard_normal(n, dtype=np.float32)
+    y = 0.5 * packed[7].astype(np.float64) * packed[300] + 0.3 * packed[301].astype(np.float64) * packed[302] \
+        + rng.standard_normal(n)
+    packed[512] = y.astype(np.float32)
+
+
+def fill_config5(packed: np.ndarray, n: int):
+    """2048 N(0,1) columns written column by column; 16 planted pairs with
+    |beta| in linspace(0.05, 0.5); Bernoulli(sigmoid(sum beta x_a x_b)) target."""
+    rng = np.random.default_rng(0)
+    f = packed.shape[0] - 1
+    for c in range(f):
+        packed[c] = rng.standard_normal(n, dtype=np.float32)
+    idx = rng.permutation(f)[:32].reshape(16, 2)
+    beta = np.linspace(0.05, 0.5, 16) * rng.choice([-1.0, 1.0], 16)
+    logit = np.zeros(n)
+    for (a, b), w in zip(idx, beta):
+        logit += w * packed[a].astype(np.float64) * packed[b]
+    packed[f] = (rng.random(n) < 1.0 / (1.0 + np.exp(-logit))).astype(np.float32)
+    return idx
+
+
+WORKLOADS = {
+    "config1": dict(n=1000, f=50, ops=["multiply"], metric="pearson", center=True, k=5, eps=1e-8,
+                    bins=16, desc="1,000 x 50 N(0,1), Bernoulli(0.5), centred multiply, |Pearson|, k=5"),
+    "config2": dict(n=1_000_000, f=256, ops=["multiply", "add", "subtract", "divide"],
+                    metric="pearson", center=False, k=100, eps=1e-6, bins=16,
+                    desc="1e6 x 256 (128 N(0,1) + 128 lognormal) fp32, {mul,add,sub,div eps=1e-6}, "
+                         "|Pearson|, k=100 per operator"),
+    "config3": dict(n=4_000_000, f=128, ops=["multiply"], metric="mutual_info", center=True, k=50,
+                    eps=1e-8, bins=32, desc="4e6 x 128 N(0,1), 3-class y, centred multiply, "
+                                            "MI 32 equal-width bins, k=50"),
+    "config4": dict(n=10_000_000, f=512, ops=["multiply"], metric="pearson", center=False, k=1000,
+                    eps=1e-8, bins=16, desc="1e7 x 512 (256 Zipf codes + 256 N(0,1)), multiply, "
+                                            "|Pearson|, k=1000"),
+    "config5": dict(n=2_000_000, f=2048, ops=["multiply"], metric="pearson", center=False, k=1000,
+                    eps=1e-8, bins=16, desc="2e6 x 2048 N(0,1), 16 planted pairs, multiply, "
+                                            "|Pearson|, k=1000"),
+}
+
+
+def build_packed(name: str, packed: np.ndarray):
+    w = WORKLOADS[name]
+    n, f = w["n"], w["f"]
+    if name in ("config1", "config2", "config3"):
+        X, y = {"config1": make_config1, "config2": make_config2, "config3": make_config3}[name]()
+        packed[:f] = X.T
+        packed[f] = y
+    elif name == "config4":
+        fill_config4(packed, n)
+    else:
+        fill_config5(packed, n)
+
+
+# ------------------------------------------------------------------ helpers --
+
+
+def algorithmic_flops_per_pair_row(metric: str) -> float:
+    """Three pair moments (sum x, sum x^2, sum x*y): 6 FLOP per pair-row per moment
+    group (multiply; add/subtract reuse sum a*b of the same group; divide has its own)."""
+    return 6.0
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            d = json.load(fh)
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# Per-launch DRAM traffic of the dominant kernel from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum); see profiles/ for the command.
+NCU_TRAFFIC_BYTES = {}
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.device)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------- CPU arm ----
+
+
+def _ref_cpu_lib():
+    path = os.path.join(REPO, "oracle", "_ref", "libgafime_cpu_ref.so")
+    if not os.path.exists(path):
+        return None
+    lib = ctypes.CDLL(path)
+    f = lib.gafime_fused_interaction_perpair_cpu
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p, ctypes.c_void_p,
+                  ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                  ctypes.c_void_p]
+    return lib
+
+
+def _ref_core():
+    import importlib.util
+    paths = glob.glob(os.path.join(REPO, "oracle", "_ref", "gafime_core*.so"))
+    if not paths:
+        return None
+    spec = importlib.util.spec_from_file_location("gafime_core", paths[0])
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+class CpuArm:
+    """The reference's own CPU implementation of the path (oracle/_ref, compiled
+    unmodified from the reference sources), or the oracle port when it is absent."""
+
+    def __init__(self, name: str, packed: np.ndarray):
+        self.name = name
+        self.w = WORKLOADS[name]
+        self.packed = packed
+        n, f = self.w["n"], self.w["f"]
+        self.n, self.f = n, f
+        self.pi, self.pj = np.triu_indices(f, k=1)
+        self.rng = np.random.default_rng(1234)
+        self.cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+        self.kind = "reference"
+        self.mode = None
+        if self.w["metric"] == "pearson" and not self.w["center"]:
+            self.lib = _ref_cpu_lib()
+            self.mode = "perpair" if self.lib is not None else "port_raw"
+        else:
+            self.core = _ref_core()
+            self.mode = "core" if self.core is not None else "port_centred"
+        if self.mode.startswith("port"):
+            self.kind = "port"
+            from oracle import oracle as orc
+            self.orc = orc
+            self.cores = self.cores
+        self.mask = np.zeros(n, dtype=np.uint8)
+        self.y = np.ascontiguousarray(packed[f])
+        self._Xrow = None
+
+    def _pairs(self, count):
+        return self.rng.choice(len(self.pi), size=min(count, len(self.pi)), replace=False)
+
+    def run(self, pair_ops: int) -> float:
+        """Score pair_ops (pair, operator) units; returns pair-rows processed."""
+        ops = self.w["ops"]
+        sample = self._pairs(max(1, pair_ops // len(ops)))
+        n = self.n
+        if self.mode == "perpair":
+            st = np.zeros(12, dtype=np.float32)
+            ident = np.zeros(2, dtype=np.int32)
+            done = 0
+            for p in sample:
+                ptrs = (ctypes.c_void_p * 2)(self.packed[self.pi[p]].ctypes.data,
+                                             self.packed[self.pj[p]].ctypes.data)
+                for op in ops:
+                    inter = np.array([["multiply", "add", "subtract", "divide"].index(op)], dtype=np.int32)
+                    rc = self.lib.gafime_fused_interaction_perpair_cpu(
+                        ptrs, self.y.ctypes.data, self.mask.ctypes.data, ident.ctypes.data, 2,
+                        inter.ctypes.data, 255, n, st.ctypes.data)
+                    assert rc == 0
+                    done += n
+            return float(done)
+        if self.mode == "core":
+            if self._Xrow is None:
+                self._Xrow = np.ascontiguousarray(self.packed[:self.f].T, dtype=np.float64)
+                self._y64 = self.y.astype(np.float64)
+            combos = [(int(self.pi[p]), int(self.pj[p])) for p in sample]
+            idx, off = self.core.pack_combos(combos)
+            metric = "mutual_info" if self.w["metric"] == "mutual_info" else "pearson"
+            self.core.score_combos(self._Xrow, self._y64, idx, off, [metric], self.w["bins"])
+            return float(len(combos) * n)
+        Xcol = self.packed[:self.f].T
+        if self.mode == "port_raw":
+            for op in ops:
+                self.orc.raw_pearson(Xcol, self.y, op, self.pi[sample].astype(np.int32),
+                                     self.pj[sample].astype(np.int32), div_eps=self.w["eps"])
+            return float(len(sample) * len(ops) * n)
+        self.orc.centred_scores(Xcol, self.y, self.pi[sample].astype(np.int32),
+                                self.pj[sample].astype(np.int32),
+                                pearson=self.w["metric"] == "pearson",
+                                mi=self.w["metric"] == "mutual_info", mi_bins=self.w["bins"])
+        return float(len(sample) * n)
+
+    def calibrate(self, seconds: float) -> int:
+        """pair_ops units that take about `seconds` on this host."""
+        units = max(4, len(self.w["ops"]))
+        while True:
+            t0 = time.perf_counter()
+            self.run(units)
+            dt = time.perf_counter() - t0
+            if dt > 0.2 or units >= len(self.pi) * len(self.w["ops"]):
+                break
+            units *= 4
+        per = dt / units
+        return int(max(len(self.w["ops"]), min(len(self.pi) * len(self.w["ops"]), seconds / per)))
+
+    def measure(self, seconds: float):
+        units = self.calibrate(seconds)
+        t0 = time.perf_counter()
+        rows = self.run(units)
+        dt = time.perf_counter() - t0
+        return rows / dt, units, dt
+
+    def describe(self, units: int, dt: float) -> str:
+        n_pairs = max(1, units // len(self.w["ops"]))
+        what = {"perpair": "gafime_fused_interaction_perpair_cpu (src/cpu/cpu_backend.cpp, OpenMP over rows)",
+                "core": "gafime_core.score_combos (OpenMP over pairs)",
+                "port_raw": "oracle port raw_pearson", "port_centred": "oracle port centred_scores"}[self.mode]
+        return (f"{what}: {n_pairs} random pairs x {len(self.w['ops'])} operator(s) x "
+                f"{self.n} rows in {dt:.1f} s")
+
+
+# ------------------------------------------------------------------- main ---
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def run_reference(args):
+    world, rank, _ = dist_setup(args)
+    if rank != 0:
+        return 0
+    w = WORKLOADS[args.workload]
+    packed = np.empty((w["f"] + 1, w["n"]), dtype=np.float32)
+    build_packed(args.workload, packed)
+    arm = CpuArm(args.workload, packed)
+    # size one step to ~0.6 s so the whole --steps K --warmup W run ends in minutes
+    units = arm.calibrate(0.6)
+    for _ in range(args.warmup):
+        arm.run(units)
+    t0 = time.perf_counter()
+    rows = 0.0
+    for _ in range(args.steps):
+        rows += arm.run(units)
+    dt = time.perf_counter() - t0
+    value = rows / dt
+    line = {
+        "impl": "reference", "metric": METRIC_NAME, "value": value, "unit": "evals/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: {w['desc']}"},
+        "cpu_baseline": {"value": value, "unit": "evals/s", "cores": arm.cores, "kind": arm.kind,
+                         "sample": arm.describe(units, dt / max(1, args.steps)) + " per step"},
+        "e2e": {"value": value, "unit": "evals/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from gafime_b200 import _native
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    w = WORKLOADS[args.workload]
+    n, f, ops, k = w["n"], w["f"], w["ops"], w["k"]
+
+    packed_t = torch.empty((f + 1, n), dtype=torch.float32, pin_memory=True)
+    packed = packed_t.numpy()
+    build_packed(args.workload, packed)
+    mask = np.zeros(n, dtype=np.uint8)
+
+    bucket = _native.Bucket(n, f, device=local)
+    bucket.upload_packed(packed, mask)
+
+    def step():
+        res = bucket.topk(ops, k, metric=w["metric"], center=w["center"], div_eps=w["eps"],
+                          mi_bins=w["bins"], shard_id=rank, n_shards=world)
+        if world == 1:
+            return res
+        # all-gather every shard's candidates over NCCL, then the deterministic merge
+        flat = np.full((len(ops), 3, k), -1.0)
+        for o, op in enumerate(ops):
+            i, j, s = res[op]
+            flat[o, 0, :len(i)] = i
+            flat[o, 1, :len(j)] = j
+            flat[o, 2, :len(s)] = s
+        t = torch.from_numpy(flat.reshape(-1)).cuda()
+        out = torch.empty(world * t.numel(), dtype=torch.float64, device="cuda")
+        dist.all_gather_into_tensor(out, t)
+        allc = out.cpu().numpy().reshape(world, len(ops), 3, k)
+        merged = {}
+        for o, op in enumerate(ops):
+            c = allc[:, o].transpose(1, 0, 2).reshape(3, -1)
+            merged[op] = _native.merge_topk(c[0].astype(np.int32), c[1].astype(np.int32), c[2], k)
+        return merged
+
+    def timed(loop_fn, steps):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            loop_fn()
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ms = start.elapsed_time(end) / steps
+        if world > 1:
+            tt = torch.tensor([ms], dtype=torch.float64, device="cuda")
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        return ms
+
+    for _ in range(args.warmup):
+        result = step()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    _native.profile_enable(True)
+    ms = timed(step, args.steps)
+    _native.profile_enable(False)
+    mom_ms, mom_launches = _native.profile_read("pair_moments")
+    mi_ms, mi_launches = _native.profile_read("mi_pass2")
+    all_ms, all_launches = _native.profile_read("all")
+    clk = clocks.stop()
+    result = step()
+
+    # e2e: the same step through the C ABI from pinned host buffers, upload included
+    def e2e_step():
+        bucket.upload_packed(packed, mask)
+        return step()
+
+    for _ in range(max(1, args.warmup // 2)):
+        e2e_step()
+    e2e_ms = timed(e2e_step, args.steps)
+
+    pairs = f * (f - 1) // 2
+    evals = float(pairs) * n * len(ops)
+    value = evals / (ms / 1e3)
+    e2e_value = evals / (e2e_ms / 1e3)
+
+    # roofline of the dominant kernel
+    peaks, peak_kind = measured_peaks()
+    if w["metric"] == "pearson":
+        groups = len({"div" if o == "divide" else "mul" for o in ops})
+        my_pairs = pairs / world
+        launches_per_step = groups
+        avg_ms = mom_ms / max(1, mom_launches)
+        flops = algorithmic_flops_per_pair_row(w["metric"]) * my_pairs * n
+        achieved = flops / (avg_ms / 1e3) / 1e12
+        peak = peaks["bf16_tflops"]
+        roof = {"bound": "tensor", "kernel": "pair_moments (CUDA-core fp32, fp64 flush)",
+                "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "peak_source": f"bf16_tflops (burst) of {peak_kind} MEASURED_PEAKS.json",
+                "avg_launch_ms": avg_ms, "launches": mom_launches,
+                "algorithmic": f"6 FLOP per pair-row x {my_pairs:.0f} pairs x {n} rows per launch",
+                "traffic": NCU_TRAFFIC_BYTES.get((args.workload, "pair_moments"))}
+    else:
+        avg_ms = mi_ms / max(1, mi_launches)
+        my_pairs = pairs / world
+        # algorithmic bytes per launch: 13 B per pair-row (reference formulation,
+        # kernels.cu:2344-2347: x_i, x_j, y fp32 + mask u8)
+        bytes_ = 13.0 * my_pairs * n
+        achieved = bytes_ / (avg_ms / 1e3) / 1e9
+        peak = peaks["hbm_gbs"]
+        roof = {"bound": "hbm", "kernel": "mi_pass2 (joint histogram)", "achieved": achieved,
+                "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "peak_source": f"hbm_gbs of {peak_kind} MEASURED_PEAKS.json",
+                "avg_launch_ms": avg_ms, "launches": mi_launches,
+                "algorithmic": f"13 B per pair-row (effective) x {my_pairs:.0f} pairs x {n} rows",
+                "traffic": NCU_TRAFFIC_BYTES.get((args.workload, "mi_pass2"))}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        arm = CpuArm(args.workload, packed)
+        v, units, dt = arm.measure(args.cpu_seconds)
+        cpu = {"value": v, "unit": "evals/s", "cores": arm.cores, "kind": arm.kind,
+               "sample": arm.describe(units, dt)}
+
+    h2d = packed.nbytes + mask.nbytes
+    d2h = len(ops) * k * (4 + 4 + 8) + len(ops) * 4
+    line = {
+        "metric": METRIC_NAME, "value": value, "unit": "evals/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: {w['desc']}", "pairs": pairs, "rows": n,
+                   "operators": ops, "k": k, "parallelism": f"pair-tile shards x{world}",
+                   "accumulation": "fp32 products, fp64 sums",
+                   "l2": f"inputs larger than L2 ({packed.nbytes / 1e9:.2f} GB resident)"},
+        "roofline": roof,
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": "evals/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "gpu_launches": all_launches // max(1, args.steps),
+        "gpu_launches_timed_region": all_launches,
+        "clocks": clk,
+    }
+    if rank == 0:
+        top = {op: [(int(a), int(b), float(s)) for a, b, s in zip(*result[op])][:3] for op in ops}
+        line["top3"] = top
+        print(json.dumps(line), flush=True)
+    bucket.free()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)  # at least 3 untimed warm-up steps
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

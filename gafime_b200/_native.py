@@ -1,0 +1,264 @@
+"""ctypes binding of libgafime_cuda.so (the C ABI in include/gafime_b200.h).
+
+There is no CPU fallback: if the library is missing or no CUDA device is usable,
+``load()`` raises.  The argtypes mirror the reference's ctypes setup
+(gafime/backends/native_cuda_backend.py:97-157) for the shared symbols.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libgafime_cuda.so")
+
+# status codes, interfaces.h:32-38
+SUCCESS = 0
+ERRORS = {
+    -1: "GAFIME_ERROR_INVALID_ARGS",
+    -2: "GAFIME_ERROR_CUDA_NOT_AVAILABLE",
+    -3: "GAFIME_ERROR_OUT_OF_MEMORY",
+    -4: "GAFIME_ERROR_KERNEL_FAILED",
+    -5: "GAFIME_ERROR_PIPELINE_FULL",
+    -6: "GAFIME_ERROR_NO_RESULT",
+}
+
+# interaction ids, interfaces.h:83-88
+INTERACT = {"multiply": 0, "add": 1, "subtract": 2, "divide": 3, "max": 4, "min": 5}
+# metric ids, gafime_core.cpp:28-33
+METRIC = {"pearson": 0, "mutual_info": 2}
+MAX_K = 4096
+
+# Every symbol include/gafime_b200.h declares.
+EXPORTED = (
+    "gafime_cuda_available", "gafime_get_device_info", "gafime_get_gpu_config",
+    "gafime_tensor_core_available", "gafime_select_device",
+    "gafime_contiguous_bucket_alloc", "gafime_contiguous_bucket_upload",
+    "gafime_contiguous_bucket_compute", "gafime_contiguous_bucket_free",
+    "gafime_contiguous_bucket_info", "gafime_allpairs_topk", "gafime_allpairs_scores",
+    "gafime_topk_merge", "gafime_profile_enable", "gafime_profile_read",
+    "gafime_contiguous_bucket_stream",
+)
+
+# kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
+KERNEL_IDS = {"column_stats": 1, "pair_moments": 2, "epilogue_topk": 3, "merge": 4,
+              "mi_pass1": 5, "mi_pass2": 6, "mi_finish": 7, "legacy_pair": 8,
+              "finite_check": 9, "gram_tc": 10}
+
+
+class GafimeError(RuntimeError):
+    def __init__(self, fn: str, code: int):
+        super().__init__(f"{fn} failed: {ERRORS.get(code, code)} ({code})")
+        self.code = code
+
+
+_LIB: Optional[ctypes.CDLL] = None
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_ip = ctypes.POINTER(ctypes.c_int)
+_f = ctypes.c_float
+_i64 = ctypes.c_int64
+
+
+def _bind(lib: ctypes.CDLL) -> None:
+    sig = {
+        "gafime_cuda_available": ([], _i),
+        "gafime_get_device_info": ([_i, ctypes.c_char_p, _ip, _ip, _ip], _i),
+        "gafime_get_gpu_config": ([_ip, _ip, _ip, _ip, _ip, _ip, ctypes.c_char_p], _i),
+        "gafime_tensor_core_available": ([_ip], _i),
+        "gafime_select_device": ([_i], _i),
+        "gafime_contiguous_bucket_alloc": ([_i, _i, ctypes.POINTER(_vp)], _i),
+        "gafime_contiguous_bucket_upload": ([_vp, _vp, _vp], _i),
+        "gafime_contiguous_bucket_compute": ([_vp, _i, _i, _i, _i, _i, _i, _vp], _i),
+        "gafime_contiguous_bucket_free": ([_vp], _i),
+        "gafime_contiguous_bucket_info": ([_vp, _ip, _ip], _i),
+        "gafime_allpairs_topk": ([_vp, _vp, _i, _i, _i, _f, _i, _i, _i, _i, _vp, _vp, _vp, _vp], _i),
+        "gafime_allpairs_scores": ([_vp, _i, _i, _i, _f, _i, _vp], _i),
+        "gafime_topk_merge": ([_vp, _vp, _vp, _i64, _i, _vp, _vp, _vp, _vp], _i),
+        "gafime_profile_enable": ([_i], _i),
+        "gafime_profile_read": ([_i, ctypes.POINTER(ctypes.c_double), _ip], _i),
+        "gafime_contiguous_bucket_stream": ([_vp, ctypes.POINTER(_vp)], _i),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+
+
+def load(require_gpu: bool = True) -> ctypes.CDLL:
+    """Load libgafime_cuda.so; raise if it is missing or (by default) no GPU is usable."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python -m gafime_b200.build` "
+                "(this engine has no CPU fallback)")
+        lib = ctypes.CDLL(LIB_PATH)
+        _bind(lib)
+        _LIB = lib
+    if require_gpu and _LIB.gafime_cuda_available() != 1:
+        raise RuntimeError("no usable CUDA device: the gafime_b200 engine runs only on the GPU")
+    return _LIB
+
+
+def check(fn: str, code: int) -> None:
+    if code != SUCCESS:
+        raise GafimeError(fn, code)
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def select_device(device_id: int) -> None:
+    lib = load()
+    check("gafime_select_device", lib.gafime_select_device(int(device_id)))
+
+
+def device_info(device_id: int = 0) -> Dict[str, object]:
+    lib = load()
+    name = ctypes.create_string_buffer(256)
+    mem, major, minor = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    check("gafime_get_device_info", lib.gafime_get_device_info(
+        device_id, name, ctypes.byref(mem), ctypes.byref(major), ctypes.byref(minor)))
+    return {"name": name.value.decode(), "memory_mb": mem.value,
+            "compute_capability": (major.value, minor.value)}
+
+
+def pack_columns(X: np.ndarray, y: np.ndarray, out: Optional[np.ndarray] = None) -> np.ndarray:
+    """Host buffer [F0 | ... | F_{F-1} | y] (column-major fp32), the layout of
+    gafime_contiguous_bucket_upload (native_cuda_backend.py:339-342)."""
+    X = np.asarray(X)
+    n, f = X.shape
+    if out is None:
+        out = np.empty((f + 1, n), dtype=np.float32)
+    out[:f] = X.T
+    out[f] = np.asarray(y, dtype=np.float32)
+    return out
+
+
+class Bucket:
+    """Owns one ContiguousBucket: the feature columns + target resident on a GPU."""
+
+    def __init__(self, n_samples: int, n_features: int, device: Optional[int] = None):
+        self.lib = load()
+        if device is not None:
+            select_device(device)
+        self.n = int(n_samples)
+        self.f = int(n_features)
+        h = ctypes.c_void_p(0)
+        check("gafime_contiguous_bucket_alloc",
+              self.lib.gafime_contiguous_bucket_alloc(self.n, self.f, ctypes.byref(h)))
+        self.handle = h
+        self._mask = np.zeros(self.n, dtype=np.uint8)
+
+    # -- data ---------------------------------------------------------------------
+    def upload_packed(self, packed: np.ndarray, mask: Optional[np.ndarray] = None) -> None:
+        """Upload an (F+1) x n fp32 C-contiguous host buffer (ideally pinned)."""
+        if packed.dtype != np.float32 or not packed.flags.c_contiguous or packed.size != (self.f + 1) * self.n:
+            raise ValueError("packed must be a C-contiguous float32 array of (F+1)*n values")
+        m = self._mask if mask is None else np.ascontiguousarray(mask, dtype=np.uint8)
+        check("gafime_contiguous_bucket_upload",
+              self.lib.gafime_contiguous_bucket_upload(self.handle, _ptr(packed), _ptr(m)))
+
+    def upload(self, X: np.ndarray, y: np.ndarray, mask: Optional[np.ndarray] = None) -> None:
+        self.upload_packed(pack_columns(X, y), mask)
+
+    # -- scoring ------------------------------------------------------------------
+    def compute_pair(self, a: int, b: int, op_a: int = 0, op_b: int = 0, interact: int = 0,
+                     val_fold_id: int = 255) -> np.ndarray:
+        stats = np.zeros(12, dtype=np.float32)
+        check("gafime_contiguous_bucket_compute", self.lib.gafime_contiguous_bucket_compute(
+            self.handle, a, b, op_a, op_b, interact, val_fold_id, _ptr(stats)))
+        return stats
+
+    def topk(self, ops: Sequence[str], k: int, metric: str = "pearson", center: bool = False,
+             div_eps: float = 1e-8, mi_bins: int = 16, shard_id: int = 0,
+             n_shards: int = 1) -> Dict[str, Tuple[np.ndarray, np.ndarray, np.ndarray]]:
+        """Per operator: (i, j, signed score) of the k best pairs of this shard."""
+        ids = np.array([INTERACT[o] for o in ops], dtype=np.int32)
+        n_ops = len(ids)
+        oi = np.empty(n_ops * k, dtype=np.int32)
+        oj = np.empty(n_ops * k, dtype=np.int32)
+        os_ = np.empty(n_ops * k, dtype=np.float64)
+        cnt = np.zeros(n_ops, dtype=np.int32)
+        check("gafime_allpairs_topk", self.lib.gafime_allpairs_topk(
+            self.handle, _ptr(ids), n_ops, METRIC[metric], int(bool(center)), float(div_eps),
+            int(mi_bins), int(k), int(shard_id), int(n_shards), _ptr(oi), _ptr(oj), _ptr(os_),
+            _ptr(cnt)))
+        out = {}
+        for o, name in enumerate(ops):
+            c = int(cnt[o])
+            sl = slice(o * k, o * k + c)
+            out[name] = (oi[sl].copy(), oj[sl].copy(), os_[sl].copy())
+        return out
+
+    def scores(self, op: str = "multiply", metric: str = "pearson", center: bool = False,
+               div_eps: float = 1e-8, mi_bins: int = 16) -> np.ndarray:
+        """Signed score of every pair i<j in row-major upper-triangle order."""
+        P = self.f * (self.f - 1) // 2
+        out = np.empty(P, dtype=np.float64)
+        if P:
+            check("gafime_allpairs_scores", self.lib.gafime_allpairs_scores(
+                self.handle, INTERACT[op], METRIC[metric], int(bool(center)), float(div_eps),
+                int(mi_bins), _ptr(out)))
+        return out
+
+    def stream_ptr(self) -> int:
+        """cudaStream_t of this bucket (every call on it runs on this stream)."""
+        s = ctypes.c_void_p(0)
+        check("gafime_contiguous_bucket_stream",
+              self.lib.gafime_contiguous_bucket_stream(self.handle, ctypes.byref(s)))
+        return int(s.value or 0)
+
+    def free(self) -> None:
+        if getattr(self, "handle", None) is not None and self.handle.value:
+            self.lib.gafime_contiguous_bucket_free(self.handle)
+            self.handle = ctypes.c_void_p(0)
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.free()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def merge_topk(cand_i: np.ndarray, cand_j: np.ndarray, cand_score: np.ndarray, k: int):
+    """Deterministic merge of candidates from several shards (gafime_topk_merge)."""
+    lib = load(require_gpu=False)
+    ci = np.ascontiguousarray(cand_i, dtype=np.int32)
+    cj = np.ascontiguousarray(cand_j, dtype=np.int32)
+    cs = np.ascontiguousarray(cand_score, dtype=np.float64)
+    oi = np.empty(k, dtype=np.int32)
+    oj = np.empty(k, dtype=np.int32)
+    os_ = np.empty(k, dtype=np.float64)
+    cnt = ctypes.c_int(0)
+    check("gafime_topk_merge", lib.gafime_topk_merge(
+        _ptr(ci), _ptr(cj), _ptr(cs), len(ci), int(k), _ptr(oi), _ptr(oj), _ptr(os_),
+        ctypes.addressof(cnt)))
+    c = cnt.value
+    return oi[:c], oj[:c], os_[:c]
+
+
+def profile_enable(enable: bool = True) -> None:
+    """Start (and clear) or stop per-kernel CUDA-event timing inside the library."""
+    check("gafime_profile_enable", load().gafime_profile_enable(int(bool(enable))))
+
+
+def profile_read(kernel: str = "all") -> Tuple[float, int]:
+    """(total device ms, launches) recorded for one kernel name, or all kernels."""
+    kid = -1 if kernel == "all" else KERNEL_IDS[kernel]
+    ms = ctypes.c_double(0.0)
+    n = ctypes.c_int(0)
+    check("gafime_profile_read", load().gafime_profile_read(kid, ctypes.byref(ms), ctypes.byref(n)))
+    return ms.value, n.value

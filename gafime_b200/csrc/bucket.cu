@@ -1,0 +1,501 @@
+// bucket.cu -- device queries, the contiguous bucket (reference ABI), the legacy
+// single-pair 12-stat kernel, and the fp64 column statistics every all-pairs
+// scoring pass starts from.
+//
+// Reference behaviour mirrored here:
+//   gafime_contiguous_bucket_alloc/upload/compute/free/info  kernels.cu:2183-2556
+//   apply_op / combine (accurate libm forms of cpu_backend.cpp:30-103)
+//   12-stat layout, NaN-row skip, fold split              interfaces.h:110-123,
+//                                                         cpu_backend.cpp:261-293
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <new>
+
+#include "engine.h"
+
+namespace gafime {
+
+int status_from(cudaError_t e) {
+    if (e == cudaSuccess) return GAFIME_SUCCESS;
+    if (e == cudaErrorMemoryAllocation) return GAFIME_ERROR_OUT_OF_MEMORY;
+    if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) return GAFIME_ERROR_CUDA_NOT_AVAILABLE;
+    return GAFIME_ERROR_KERNEL_FAILED;
+}
+
+cudaError_t ensure(DeviceBuf& b, size_t bytes) {
+    if (b.bytes >= bytes && b.ptr) return cudaSuccess;
+    if (b.ptr) {
+        // Growing: queued kernels may still read the old buffer, so drain the device
+        // before freeing it.  Happens only when a call needs more scratch than any before.
+        cudaDeviceSynchronize();
+        cudaFree(b.ptr);
+        b.ptr = nullptr;
+        b.bytes = 0;
+    }
+    size_t want = bytes < 256 ? 256 : bytes;
+    cudaError_t e = cudaMalloc(&b.ptr, want);
+    if (e == cudaSuccess) b.bytes = want;
+    return e;
+}
+
+static void release(DeviceBuf& b) {
+    if (b.ptr) cudaFree(b.ptr);
+    b.ptr = nullptr;
+    b.bytes = 0;
+}
+
+// ------------------------------------------------------------- unary / combine --
+
+// Unary operators with the accurate math functions of the CPU reference
+// (cpu_backend.cpp:30-77); the 12-stat parity target is that CPU library.
+__device__ __forceinline__ float apply_op(float x, int op) {
+    switch (op) {
+        case GAFIME_OP_LOG: return logf(fabsf(x) + 1e-8f);
+        case GAFIME_OP_EXP: return expf(fminf(fmaxf(x, -20.0f), 20.0f));
+        case GAFIME_OP_SQRT: return sqrtf(fabsf(x));
+        case GAFIME_OP_TANH: {
+            float c = fminf(fmaxf(x, -10.0f), 10.0f);
+            float e2 = expf(2.0f * c);
+            return (e2 - 1.0f) / (e2 + 1.0f);
+        }
+        case GAFIME_OP_SIGMOID: {
+            float c = fminf(fmaxf(x, -20.0f), 20.0f);
+            return 1.0f / (1.0f + expf(-c));
+        }
+        case GAFIME_OP_SQUARE: return x * x;
+        case GAFIME_OP_NEGATE: return -x;
+        case GAFIME_OP_ABS: return fabsf(x);
+        case GAFIME_OP_INVERSE: return 1.0f / (fabsf(x) < 1e-8f ? copysignf(1e-8f, x) : x);
+        case GAFIME_OP_CUBE: return x * x * x;
+        case GAFIME_OP_ROLLING_MEAN:
+        case GAFIME_OP_ROLLING_STD: return __int_as_float(0x7fc00000);  // NaN: row skipped
+        case GAFIME_OP_IDENTITY:
+        default: return x;
+    }
+}
+
+__device__ __forceinline__ float combine_op(float a, float b, int t) {
+    switch (t) {
+        case GAFIME_INTERACT_ADD: return a + b;
+        case GAFIME_INTERACT_SUB: return a - b;
+        case GAFIME_INTERACT_DIV: return a / (fabsf(b) < 1e-8f ? copysignf(1e-8f, b) : b);
+        case GAFIME_INTERACT_MAX: return fmaxf(a, b);
+        case GAFIME_INTERACT_MIN: return fminf(a, b);
+        case GAFIME_INTERACT_MULT:
+        default: return __fmul_rn(a, b);
+    }
+}
+
+// --------------------------------------------------------------- reductions --
+
+// Fixed-order block reduction of NV doubles per thread (blockDim.x == 256).
+template <int NV>
+__device__ __forceinline__ void block_reduce_fixed(double (&v)[NV], double* smem /*[NV*256]*/) {
+    const int t = threadIdx.x;
+    #pragma unroll
+    for (int m = 0; m < NV; ++m) smem[m * 256 + t] = v[m];
+    __syncthreads();
+    for (int s = 128; s > 0; s >>= 1) {
+        if (t < s) {
+            #pragma unroll
+            for (int m = 0; m < NV; ++m) smem[m * 256 + t] += smem[m * 256 + t + s];
+        }
+        __syncthreads();
+    }
+    #pragma unroll
+    for (int m = 0; m < NV; ++m) v[m] = smem[m * 256];
+}
+
+// --------------------------------------------------- legacy single-pair stats --
+
+constexpr int kLegacyBlocks = 296;
+
+__global__ void __launch_bounds__(256) legacy_pair_stats_kernel(
+    const float* __restrict__ data, const uint8_t* __restrict__ mask, int64_t n, int64_t ld,
+    int64_t f, int fa, int fb, int op_a, int op_b, int interact, int val_fold_id,
+    double* __restrict__ partial /*[gridDim.x][12]*/) {
+    __shared__ double red[12 * 256];
+    const float* ca = data + (int64_t)fa * ld;
+    const float* cb = data + (int64_t)fb * ld;
+    const float* y = data + f * ld;
+    double acc[12];
+    #pragma unroll
+    for (int m = 0; m < 12; ++m) acc[m] = 0.0;
+    for (int64_t r = (int64_t)blockIdx.x * 256 + threadIdx.x; r < n; r += (int64_t)gridDim.x * 256) {
+        float x = combine_op(apply_op(ca[r], op_a), apply_op(cb[r], op_b), interact);
+        float yv = y[r];
+        if (isnan(x) || isnan(yv)) continue;
+        double xd = x, yd = yv;
+        int o = (mask[r] == val_fold_id) ? 6 : 0;
+        #pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            if (o == 6 * h) {
+                acc[6 * h + 0] += 1.0;
+                acc[6 * h + 1] += xd;
+                acc[6 * h + 2] += yd;
+                acc[6 * h + 3] += xd * xd;
+                acc[6 * h + 4] += yd * yd;
+                acc[6 * h + 5] += xd * yd;
+            }
+        }
+    }
+    block_reduce_fixed<12>(acc, red);
+    if (threadIdx.x == 0) {
+        #pragma unroll
+        for (int m = 0; m < 12; ++m) partial[blockIdx.x * 12 + m] = acc[m];
+    }
+}
+
+__global__ void sum_partials_kernel(const double* __restrict__ partial, int n_part, int width,
+                                    double* __restrict__ out) {
+    int m = threadIdx.x;
+    if (m >= width) return;
+    double s = 0.0;
+    for (int p = 0; p < n_part; ++p) s += partial[p * width + m];
+    out[m] = s;
+}
+
+// ------------------------------------------------------------ column stats --
+
+// Partial sums over one row split of one column: [0] sum x, [1] sum x^2,
+// [2] sum x*ycen (when ycen != nullptr).
+__global__ void __launch_bounds__(256) col_partial_kernel(
+    const float* __restrict__ x, int64_t ld, int64_t n, const float* __restrict__ ycen,
+    int64_t span, double* __restrict__ part /*[cols][splits][3]*/) {
+    __shared__ double red[3 * 256];
+    const int c = blockIdx.x, s = blockIdx.y, splits = gridDim.y;
+    const float* col = x + (int64_t)c * ld;
+    int64_t r0 = (int64_t)s * span;
+    int64_t r1 = r0 + span < n ? r0 + span : n;
+    double v[3] = {0.0, 0.0, 0.0};
+    for (int64_t r = r0 + threadIdx.x; r < r1; r += 256) {
+        double a = col[r];
+        v[0] += a;
+        v[1] += a * a;
+        if (ycen) v[2] += a * (double)ycen[r];
+    }
+    block_reduce_fixed<3>(v, red);
+    if (threadIdx.x == 0) {
+        double* o = part + ((int64_t)c * splits + s) * 3;
+        o[0] = v[0];
+        o[1] = v[1];
+        o[2] = v[2];
+    }
+}
+
+// colstats[c*4 + {0,1,2,3}] = {sum, sumsq, sum x*ycen, mean}
+__global__ void col_combine_kernel(const double* __restrict__ part, int cols, int splits,
+                                   int64_t n, double* __restrict__ colstats) {
+    int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= cols) return;
+    double v[3] = {0.0, 0.0, 0.0};
+    for (int s = 0; s < splits; ++s)
+        for (int m = 0; m < 3; ++m) v[m] += part[((int64_t)c * splits + s) * 3 + m];
+    colstats[c * 4 + 0] = v[0];
+    colstats[c * 4 + 1] = v[1];
+    colstats[c * 4 + 2] = v[2];
+    colstats[c * 4 + 3] = v[0] / (double)n;
+}
+
+// ystats = {n, sum y, var_y, mean y} from the target column's (sum, sumsq).
+// var_y = syy - sy^2/n as native_cuda_backend.py:481 and gafime_core.cpp:496.
+__global__ void ystats_kernel(const double* __restrict__ ycol, int64_t n, double* __restrict__ ystats) {
+    double dn = (double)n, sy = ycol[0], syy = ycol[1];
+    double mean = sy / dn;
+    ystats[0] = dn;
+    ystats[1] = sy;
+    ystats[2] = syy - sy * mean;
+    ystats[3] = mean;
+}
+
+__global__ void ycen_kernel(const float* __restrict__ y, int64_t n, int64_t ld,
+                            const double* __restrict__ ystats, float* __restrict__ ycen) {
+    double mean = ystats[3];
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < ld;
+         r += (int64_t)gridDim.x * blockDim.x)
+        ycen[r] = r < n ? (float)((double)y[r] - mean) : 0.0f;
+}
+
+// Centred copy fl32(x - mean) in the padded layout (pad rows stay zero).
+__global__ void xcen_kernel(const float* __restrict__ x, int64_t ld, int64_t n, int64_t f,
+                            const double* __restrict__ colstats, float* __restrict__ xc) {
+    int64_t total = f * ld;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        int64_t c = e / ld, r = e - c * ld;
+        xc[e] = r < n ? (float)((double)x[e] - colstats[c * 4 + 3]) : 0.0f;
+    }
+}
+
+__global__ void finite_kernel(const float* __restrict__ x, int64_t cols, int64_t ld, int64_t n,
+                              int* __restrict__ flag) {
+    int64_t total = cols * ld;
+    int bad = 0;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        int64_t r = e % ld;
+        if (r < n && !isfinite(x[e])) bad = 1;
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(flag, 1);
+}
+
+static int split_count(int64_t cols, int64_t n, int sm) {
+    int64_t want = (4 * (int64_t)sm + cols - 1) / cols;
+    int64_t max_by_rows = (n + 4095) / 4096;
+    if (want > max_by_rows) want = max_by_rows;
+    if (want < 1) want = 1;
+    if (want > 1024) want = 1024;
+    return (int)want;
+}
+
+// Column partial sums + combine for `cols` columns of `x` into colstats[cols*4].
+static cudaError_t column_sums(Bucket& b, const float* x, int64_t cols, const float* ycen,
+                               double* colstats) {
+    int splits = split_count(cols, b.n, b.sm_count);
+    int64_t span = (b.n + splits - 1) / splits;
+    span = (span + 255) / 256 * 256;
+    cudaError_t e = ensure(b.stats_part, (size_t)cols * splits * 3 * sizeof(double));
+    if (e != cudaSuccess) return e;
+    dim3 grid((unsigned)cols, (unsigned)splits);
+    col_partial_kernel<<<grid, 256, 0, b.stream>>>(x, b.ld, b.n, ycen, span,
+                                                   (double*)b.stats_part.ptr);
+    col_combine_kernel<<<(unsigned)((cols + 127) / 128), 128, 0, b.stream>>>(
+        (const double*)b.stats_part.ptr, (int)cols, splits, b.n, colstats);
+    return cudaGetLastError();
+}
+
+int compute_column_stats(Bucket& b, bool centred, ColumnStats& out) {
+    // stats buffer: [f*4] column stats, [4] y column sums, [4] ystats
+    cudaError_t e = ensure(b.stats, (size_t)(b.f * 4 + 8) * sizeof(double));
+    if (e == cudaSuccess) {
+        size_t need = (size_t)std::max<int64_t>(1 * split_count(1, b.n, b.sm_count),
+                                                b.f * split_count(b.f, b.n, b.sm_count));
+        e = ensure(b.stats_part, need * 3 * sizeof(double));
+    }
+    if (e == cudaSuccess) e = ensure(b.ycen, (size_t)b.ld * sizeof(float));
+    if (e != cudaSuccess) return status_from(e);
+    double* colstats = (double*)b.stats.ptr;
+    double* ycol = colstats + b.f * 4;
+    double* ystats = ycol + 4;
+    const float* y = b.d_data + b.f * b.ld;
+    float* ycen = (float*)b.ycen.ptr;
+    int blocks = 4 * b.sm_count;
+
+    e = column_sums(b, y, 1, nullptr, ycol);
+    if (e != cudaSuccess) return status_from(e);
+    ystats_kernel<<<1, 1, 0, b.stream>>>(ycol, b.n, ystats);
+    ycen_kernel<<<blocks, 256, 0, b.stream>>>(y, b.n, b.ld, ystats, ycen);
+    const float* xs = b.d_data;
+    if (centred) {
+        e = ensure(b.xcen, (size_t)b.f * b.ld * sizeof(float));
+        if (e != cudaSuccess) return status_from(e);
+        e = column_sums(b, b.d_data, b.f, nullptr, colstats);  // means of raw columns
+        if (e != cudaSuccess) return status_from(e);
+        xcen_kernel<<<blocks, 256, 0, b.stream>>>(b.d_data, b.ld, b.n, b.f, colstats,
+                                                   (float*)b.xcen.ptr);
+        xs = (const float*)b.xcen.ptr;
+    }
+    e = column_sums(b, xs, b.f, ycen, colstats);
+    if (e != cudaSuccess) return status_from(e);
+    out.d_col = colstats;
+    out.d_y = ystats;
+    out.d_x = xs;
+    out.d_ycen = ycen;
+    return GAFIME_SUCCESS;
+}
+
+int check_finite(Bucket& b, bool* all_finite) {
+    cudaError_t e = ensure(b.flags, 64);
+    if (e != cudaSuccess) return status_from(e);
+    int* flag = (int*)b.flags.ptr;
+    cudaMemsetAsync(flag, 0, sizeof(int), b.stream);
+    finite_kernel<<<4 * b.sm_count, 256, 0, b.stream>>>(b.d_data, b.f + 1, b.ld, b.n, flag);
+    int h = 0;
+    e = cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, b.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b.stream);
+    if (e != cudaSuccess) return status_from(e);
+    *all_finite = (h == 0);
+    return GAFIME_SUCCESS;
+}
+
+}  // namespace gafime
+
+using namespace gafime;
+
+// ================================================================== C ABI ====
+
+extern "C" {
+
+int gafime_cuda_available(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n > 0 ? 1 : 0;
+}
+
+int gafime_select_device(int device_id) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return GAFIME_ERROR_CUDA_NOT_AVAILABLE;
+    if (device_id < 0 || device_id >= n) return GAFIME_ERROR_INVALID_ARGS;
+    return status_from(cudaSetDevice(device_id));
+}
+
+int gafime_get_device_info(int device_id, char* name_out, int* memory_mb_out,
+                           int* compute_cap_major_out, int* compute_cap_minor_out) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return GAFIME_ERROR_CUDA_NOT_AVAILABLE;
+    if (device_id < 0 || device_id >= n) return GAFIME_ERROR_INVALID_ARGS;
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, device_id) != cudaSuccess) return GAFIME_ERROR_KERNEL_FAILED;
+    if (name_out) {
+        strncpy(name_out, p.name, 255);
+        name_out[255] = '\0';
+    }
+    if (memory_mb_out) *memory_mb_out = (int)(p.totalGlobalMem / (1024 * 1024));
+    if (compute_cap_major_out) *compute_cap_major_out = p.major;
+    if (compute_cap_minor_out) *compute_cap_minor_out = p.minor;
+    return GAFIME_SUCCESS;
+}
+
+int gafime_get_gpu_config(int* block_size_out, int* max_blocks_out, int* sm_count_out,
+                          int* compute_major_out, int* compute_minor_out, int* l2_cache_bytes_out,
+                          char* gpu_name_out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return GAFIME_ERROR_CUDA_NOT_AVAILABLE;
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, dev) != cudaSuccess) return GAFIME_ERROR_KERNEL_FAILED;
+    if (block_size_out) *block_size_out = 256;
+    if (max_blocks_out) *max_blocks_out = p.multiProcessorCount * 8;
+    if (sm_count_out) *sm_count_out = p.multiProcessorCount;
+    if (compute_major_out) *compute_major_out = p.major;
+    if (compute_minor_out) *compute_minor_out = p.minor;
+    if (l2_cache_bytes_out) *l2_cache_bytes_out = p.l2CacheSize;
+    if (gpu_name_out) {
+        strncpy(gpu_name_out, p.name, 255);
+        gpu_name_out[255] = '\0';
+    }
+    return GAFIME_SUCCESS;
+}
+
+int gafime_tensor_core_available(int* precision_mode) {
+    int dev = 0, major = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+        cudaGetLastError();
+        if (precision_mode) *precision_mode = 0;
+        return 0;
+    }
+    if (precision_mode) *precision_mode = major >= 10 ? 4 : 0;
+    return major >= 10 ? 1 : 0;
+}
+
+int gafime_contiguous_bucket_alloc(int n_samples, int n_features, ContiguousBucket* bucket_out) {
+    if (n_samples <= 0 || n_features <= 0 || !bucket_out) return GAFIME_ERROR_INVALID_ARGS;
+    if (!gafime_cuda_available()) return GAFIME_ERROR_CUDA_NOT_AVAILABLE;
+    Bucket* b = new (std::nothrow) Bucket();
+    if (!b) return GAFIME_ERROR_OUT_OF_MEMORY;
+    cudaGetDevice(&b->device);
+    cudaDeviceGetAttribute(&b->sm_count, cudaDevAttrMultiProcessorCount, b->device);
+    b->n = n_samples;
+    b->f = n_features;
+    b->ld = (b->n + kRowPad - 1) / kRowPad * kRowPad;
+    size_t bytes = (size_t)(b->f + 1) * (size_t)b->ld * sizeof(float);
+    cudaError_t e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMallocHost(&b->h_pinned, 64 * sizeof(double));
+    if (e == cudaSuccess) e = cudaMalloc(&b->d_data, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&b->d_mask, (size_t)b->n);
+    if (e == cudaSuccess) e = cudaMemsetAsync(b->d_data, 0, bytes, b->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(b->d_mask, 0, (size_t)b->n, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    if (e != cudaSuccess) {
+        int st = status_from(e);
+        gafime_contiguous_bucket_free(b);
+        cudaGetLastError();
+        return st;
+    }
+    *bucket_out = b;
+    return GAFIME_SUCCESS;
+}
+
+int gafime_contiguous_bucket_upload(ContiguousBucket bucket, const float* h_data,
+                                    const uint8_t* h_mask) {
+    if (!bucket || !h_data || !h_mask) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket* b = (Bucket*)bucket;
+    cudaSetDevice(b->device);
+    // One strided copy places every column (and y) at its padded offset.
+    cudaError_t e = cudaMemcpy2DAsync(b->d_data, (size_t)b->ld * sizeof(float), h_data,
+                                      (size_t)b->n * sizeof(float), (size_t)b->n * sizeof(float),
+                                      (size_t)(b->f + 1), cudaMemcpyHostToDevice, b->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(b->d_mask, h_mask, (size_t)b->n, cudaMemcpyHostToDevice, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    return status_from(e);
+}
+
+int gafime_contiguous_bucket_compute(ContiguousBucket bucket, int feature_a_idx, int feature_b_idx,
+                                     int op_a, int op_b, int interact_type, int val_fold_id,
+                                     float* h_stats_out) {
+    if (!bucket || !h_stats_out) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket* b = (Bucket*)bucket;
+    if (feature_a_idx < 0 || feature_a_idx >= b->f || feature_b_idx < 0 || feature_b_idx >= b->f)
+        return GAFIME_ERROR_INVALID_ARGS;
+    if (op_a < 0 || op_a > GAFIME_OP_ROLLING_STD || op_b < 0 || op_b > GAFIME_OP_ROLLING_STD ||
+        interact_type < 0 || interact_type > GAFIME_INTERACT_MIN)
+        return GAFIME_ERROR_INVALID_ARGS;
+    cudaSetDevice(b->device);
+    cudaError_t e = ensure(b->stats_part, (size_t)(kLegacyBlocks + 1) * 12 * sizeof(double));
+    if (e != cudaSuccess) return status_from(e);
+    double* part = (double*)b->stats_part.ptr;
+    double* total = part + kLegacyBlocks * 12;
+    KernelTimer timer(b->stream, GAFIME_KERNEL_LEGACY_PAIR);
+    legacy_pair_stats_kernel<<<kLegacyBlocks, 256, 0, b->stream>>>(
+        b->d_data, b->d_mask, b->n, b->ld, b->f, feature_a_idx, feature_b_idx, op_a, op_b,
+        interact_type, val_fold_id, part);
+    sum_partials_kernel<<<1, 32, 0, b->stream>>>(part, kLegacyBlocks, 12, total);
+    e = cudaGetLastError();
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(b->h_pinned, total, 12 * sizeof(double), cudaMemcpyDeviceToHost,
+                            b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    if (e != cudaSuccess) return status_from(e);
+    for (int m = 0; m < 12; ++m) h_stats_out[m] = (float)b->h_pinned[m];
+    return GAFIME_SUCCESS;
+}
+
+int gafime_contiguous_bucket_free(ContiguousBucket bucket) {
+    if (!bucket) return GAFIME_SUCCESS;
+    Bucket* b = (Bucket*)bucket;
+    cudaSetDevice(b->device);
+    if (b->stream) cudaStreamSynchronize(b->stream);
+    DeviceBuf* bufs[] = {&b->stats_part, &b->stats, &b->ycen, &b->xcen, &b->moments, &b->cands,
+                         &b->cands2, &b->scores, &b->flags, &b->tiles, &b->mi, &b->mi_hist};
+    for (DeviceBuf* d : bufs) release(*d);
+    if (b->d_data) cudaFree(b->d_data);
+    if (b->d_mask) cudaFree(b->d_mask);
+    if (b->h_pinned) cudaFreeHost(b->h_pinned);
+    if (b->stream) cudaStreamDestroy(b->stream);
+    delete b;
+    return GAFIME_SUCCESS;
+}
+
+int gafime_contiguous_bucket_stream(ContiguousBucket bucket, void** stream_out) {
+    if (!bucket || !stream_out) return GAFIME_ERROR_INVALID_ARGS;
+    *stream_out = (void*)((Bucket*)bucket)->stream;
+    return GAFIME_SUCCESS;
+}
+
+int gafime_contiguous_bucket_info(ContiguousBucket bucket, int* n_samples_out, int* n_features_out) {
+    if (!bucket) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket* b = (Bucket*)bucket;
+    if (n_samples_out) *n_samples_out = (int)b->n;
+    if (n_features_out) *n_features_out = (int)b->f;
+    return GAFIME_SUCCESS;
+}
+
+}  // extern "C"

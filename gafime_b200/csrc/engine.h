@@ -1,0 +1,144 @@
+// engine.h -- internal declarations of libgafime_cuda.so (not part of the ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "../../include/gafime_b200.h"
+
+namespace gafime {
+
+// Rows of every device column are padded to a multiple of this (zeros), so the
+// tiled kernels never see a partial chunk.  Zero rows add nothing to any sum of
+// products the all-pairs kernels form (x = a*g(b) with a = 0).
+constexpr int64_t kRowPad = 256;
+
+// Pair tiles of the CUDA-core moment kernel: kTile x kTile columns.
+constexpr int kTile = 64;
+constexpr int kTilePairs = kTile * kTile;
+
+// One candidate of the top-k selection: signed score + pair id (i * F + j).
+struct Cand {
+    double score;
+    uint32_t pid;
+    uint32_t pad;
+};
+constexpr uint32_t kNoPair = 0xFFFFFFFFu;
+
+// Device-side record of a pair tile: columns [bi*kTile, +kTile) x [bj*kTile, +kTile).
+struct TileCoord {
+    int bi, bj;
+};
+
+// Scratch buffers owned by a bucket and grown on demand (never shrunk until free).
+struct DeviceBuf {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+
+struct Bucket {
+    int device = 0;
+    int64_t n = 0;        // rows
+    int64_t f = 0;        // feature columns
+    int64_t ld = 0;       // padded rows per device column
+    float* d_data = nullptr;   // (f + 1) * ld floats: features then target
+    uint8_t* d_mask = nullptr; // n bytes
+    cudaStream_t stream = nullptr;
+    double* h_pinned = nullptr;  // small pinned staging for stats
+    int sm_count = 148;
+    // scratch
+    DeviceBuf stats_part, stats, ycen, xcen, moments, cands, cands2, scores, flags, tiles, mi,
+        mi_hist;
+};
+
+// Grow a scratch buffer to at least `bytes`; returns cudaSuccess or an error.
+cudaError_t ensure(DeviceBuf& b, size_t bytes);
+
+// Column statistics, all fp64 and deterministic (fixed reduction order).
+//   colstats[c*4 + 0] = sum x, [1] = sum x^2, [2] = sum x*ycen, [3] = mean
+//   ystats[0] = n, [1] = sum y, [2] = var_y = sum y^2 - (sum y)^2 / n, [3] = mean y
+// With centred=true the statistics describe the centred copy written to xcen.
+struct ColumnStats {
+    const double* d_col = nullptr;  // [f * 4]
+    const double* d_y = nullptr;    // [4]
+    const float* d_x = nullptr;     // matrix the pair kernels read (raw or centred)
+    const float* d_ycen = nullptr;  // fl32(y - mean y), zero padded
+    double h_y[4];
+};
+int compute_column_stats(Bucket& b, bool centred, ColumnStats& out);
+
+// Finite-input check over the first f columns + y; returns 1 if all finite.
+int check_finite(Bucket& b, bool* all_finite);
+
+// CUDA-core three-moment pair kernel (moments.cu).  For every pair (i, j) of the
+// listed tiles: S1 = sum a*g(b), S2 = sum (a*g(b))^2, S3 = sum a*g(b)*ycen with
+// a = X[:, i], b = X[:, j], g = identity (recip = false) or 1/safe(b).
+// Output layout: moments[((split * n_tiles + t) * 3 + m) * kTilePairs + li*kTile + lj].
+cudaError_t launch_pair_moments(const float* d_x, int64_t ld, const float* d_ycen, int64_t f,
+                                const TileCoord* d_tiles, int n_tiles, int splits,
+                                int64_t rows_per_split, bool recip, float eps, double* d_moments,
+                                cudaStream_t stream);
+
+// Scoring epilogue + per-tile top-k (select.cu).
+struct EpilogueArgs {
+    const double* moments;       // from launch_pair_moments (mul or div group)
+    int splits;
+    const TileCoord* tiles;
+    int n_tiles;
+    int64_t f;
+    const double* colstats;      // [f*4]
+    const double* ystats;        // [4]
+    int op;                      // GAFIME_INTERACT_*
+    int k_pad;                   // power of two >= k, <= 4096
+    Cand* cands;                 // [n_tiles * k_pad] for this op
+    double* all_scores;          // nullable, [P] triangle order
+};
+cudaError_t launch_epilogue_topk(const EpilogueArgs& a, cudaStream_t stream);
+
+// Merge n_lists sorted candidate lists of k_pad entries down to one (in place
+// ping-pong between buf and tmp); returns the buffer holding the final list.
+cudaError_t merge_candidates(Cand* buf, Cand* tmp, int n_lists, int k_pad, int n_groups,
+                             Cand** final_list, cudaStream_t stream);
+
+// Mutual-information scoring (mi.cu): centred product, equal-width bins.
+// cs must hold raw-column statistics (means of the uncentred columns).
+cudaError_t launch_mi_scores(Bucket& b, const ColumnStats& cs, bool centred, int op, float div_eps,
+                             int mi_bins, const TileCoord* d_tiles, int n_tiles, int k_pad,
+                             Cand* cands, double* all_scores, cudaStream_t stream);
+
+// Ranking used everywhere: |score| descending, NaN after every number, empty
+// slots last; ties by pair id ascending.
+__host__ __device__ inline double cand_rank(const Cand& c) {
+    if (c.pid == kNoPair) return -2.0;
+    double s = c.score;
+    if (s != s) return -1.0;
+    return s < 0 ? -s : s;
+}
+__host__ __device__ inline bool cand_before(const Cand& a, const Cand& b) {
+    double ra = cand_rank(a), rb = cand_rank(b);
+    if (ra != rb) return ra > rb;
+    return a.pid < b.pid;
+}
+
+// Map a CUDA error to the ABI status code.
+int status_from(cudaError_t e);
+
+// Brackets one kernel launch with CUDA events on its stream while profiling is
+// enabled (profile.cu); kernel ids are the GAFIME_KERNEL_* values of the ABI.
+class KernelTimer {
+  public:
+    KernelTimer(cudaStream_t stream, int kernel_id);
+    ~KernelTimer();
+    KernelTimer(const KernelTimer&) = delete;
+    KernelTimer& operator=(const KernelTimer&) = delete;
+
+  private:
+    cudaStream_t stream_;
+    int id_;
+    bool active_ = false;
+    cudaEvent_t start_{}, stop_{};
+};
+
+}  // namespace gafime

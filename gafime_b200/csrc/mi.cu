@@ -1,0 +1,437 @@
+// mi.cu -- all-pairs mutual information with equal-width bins.
+//
+// Semantics of gafime_core.score_combos for 2-combos (gafime_core.cpp:531-618):
+//   x_r = (a_r - mean_a) * (b_r - mean_b) in fp64           (gafime_core.cpp:571-577)
+//   y bins:  build_bins(y, bins)  min/max equal width        (gafime_core.cpp:200-226)
+//   x bins:  (int)((x - xmin) * bins / (xmax - xmin)), clamped   (gafime_core.cpp:277-304)
+//   MI = sum_{bx,by} p log(p / (p_x p_y)), natural log       (gafime_core.cpp:316-332)
+//   MI = 0 when xmin == xmax or y is constant.
+// With center = 0 the interaction is the kernel-API x = fl32(a op b)
+// (cpu_backend.cpp:87-103) and the same binning applies.
+//
+// Device plan (per call):
+//   y codes : y-bin of every row, remapped to the U bins that occur (exact: bins no row
+//             falls in contribute nothing);
+//   pass 1  : per-pair min / max of x over row splits, merged with 64-bit integer
+//             atomics on an order-preserving key (deterministic);
+//   pass 2  : each thread owns one pair and a private 16-bit joint histogram
+//             (bins x U) in shared memory; split results merge with integer atomics;
+//   finish  : MI per pair in fp64 in the reference's summation order, then the same
+//             bitonic top-k as the Pearson epilogue.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "engine.h"
+#include "select.cuh"
+
+namespace gafime {
+
+namespace {
+
+constexpr int kMiRows = 128;                 // rows per shared-memory chunk
+constexpr int64_t kMiMaxSplitRows = 32768;   // 16-bit counters cannot overflow
+
+__device__ __forceinline__ long long dkey(double v) {
+    long long b = __double_as_longlong(v);
+    return b >= 0 ? b : (b ^ 0x7FFFFFFFFFFFFFFFLL);
+}
+__device__ __forceinline__ double dval(long long k) {
+    return __longlong_as_double(k >= 0 ? k : (k ^ 0x7FFFFFFFFFFFFFFFLL));
+}
+
+__device__ __forceinline__ float combine_f(float a, float b, int op, float eps) {
+    switch (op) {
+        case GAFIME_INTERACT_ADD: return a + b;
+        case GAFIME_INTERACT_SUB: return a - b;
+        case GAFIME_INTERACT_DIV: return a / (fabsf(b) < eps ? copysignf(eps, b) : b);
+        default: return __fmul_rn(a, b);
+    }
+}
+__device__ __forceinline__ double combine_d(double a, double b, int op, double eps) {
+    switch (op) {
+        case GAFIME_INTERACT_ADD: return a + b;
+        case GAFIME_INTERACT_SUB: return a - b;
+        case GAFIME_INTERACT_DIV: return a / (fabs(b) < eps ? copysign(eps, b) : b);
+        default: return __dmul_rn(a, b);
+    }
+}
+
+struct MiArgs {
+    const float* x;
+    int64_t ld, n, f;
+    const double* colstats;   // mean at [c*4 + 3]
+    const TileCoord* tiles;
+    int n_tiles;
+    int op;
+    float eps;
+    int64_t rows_per_split;
+    long long* mm;            // [n_tiles][4096][2] keys: min, max
+    const uint8_t* ycode;     // [n] compact y-bin codes
+    int bins, U, hstride;     // hstride: 16-bit slots per pair in shared memory
+    unsigned* hist;           // [n_tiles][4096][bins * U]
+};
+
+// One CTA: one TS x TS block of pairs inside a 64 x 64 tile, one row split.
+template <int TS, int PASS, bool CENTRED>
+__global__ void __launch_bounds__(TS * TS) mi_pass_kernel(MiArgs a) {
+    using V = typename std::conditional<CENTRED, double, float>::type;
+    constexpr int SUBS = 64 / TS;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    V* As = reinterpret_cast<V*>(smem_raw);                  // [kMiRows][TS + 1]
+    V* Bs = As + kMiRows * (TS + 1);                         // [kMiRows][TS + 1]
+    uint8_t* ys = reinterpret_cast<uint8_t*>(Bs + kMiRows * (TS + 1));  // [kMiRows]
+    uint16_t* hs = reinterpret_cast<uint16_t*>(ys + kMiRows);           // [TS*TS][hstride]
+
+    const int t = blockIdx.x / (SUBS * SUBS), sub = blockIdx.x % (SUBS * SUBS);
+    const int si = sub / SUBS, sj = sub % SUBS;
+    const TileCoord tc = a.tiles[t];
+    if (tc.bi == tc.bj && si > sj) return;
+    const int64_t i0 = (int64_t)tc.bi * 64 + si * TS, j0 = (int64_t)tc.bj * 64 + sj * TS;
+    if (i0 >= a.f || j0 >= a.f) return;
+    const int tid = threadIdx.x;
+    const int li = tid / TS, lj = tid % TS;
+    const int64_t i = i0 + li, j = j0 + lj;
+    const bool valid = (i < j) && (j < a.f);
+    const int e = (si * TS + li) * 64 + (sj * TS + lj);
+    long long* mm = a.mm + ((int64_t)t * kTilePairs + e) * 2;
+
+    const int64_t r0 = (int64_t)blockIdx.y * a.rows_per_split;
+    const int64_t r1 = std::min<int64_t>(r0 + a.rows_per_split, a.n);
+
+    double mn = INFINITY, mx = -INFINITY;
+    double xmin = 0.0, scale = 0.0;
+    bool live = valid;
+    uint16_t* h = hs + tid * a.hstride;
+    if (PASS == 2) {
+        for (int c = 0; c < a.hstride; ++c) h[c] = 0;
+        if (valid) {
+            xmin = dval(mm[0]);
+            double xmax = dval(mm[1]);
+            live = xmax != xmin;
+            scale = (double)a.bins / (xmax - xmin);
+        }
+    }
+
+    for (int64_t rb = r0; rb < r1; rb += kMiRows) {
+        const int rows = (int)std::min<int64_t>(kMiRows, r1 - rb);
+        __syncthreads();
+        for (int q = tid; q < TS * kMiRows; q += TS * TS) {
+            int col = q / kMiRows, row = q % kMiRows;
+            V va = 0, vb = 0;
+            if (row < rows) {
+                int64_t ca = i0 + col, cb = j0 + col;
+                if (ca < a.f) {
+                    float raw = a.x[ca * a.ld + rb + row];
+                    if (CENTRED) va = (V)((double)raw - a.colstats[ca * 4 + 3]); else va = (V)raw;
+                }
+                if (cb < a.f) {
+                    float raw = a.x[cb * a.ld + rb + row];
+                    if (CENTRED) vb = (V)((double)raw - a.colstats[cb * 4 + 3]); else vb = (V)raw;
+                }
+            }
+            As[row * (TS + 1) + col] = va;
+            Bs[row * (TS + 1) + col] = vb;
+        }
+        if (PASS == 2)
+            for (int q = tid; q < rows; q += TS * TS) ys[q] = a.ycode[rb + q];
+        __syncthreads();
+        if (!live) continue;
+        for (int r = 0; r < rows; ++r) {
+            double xv;
+            if (CENTRED)
+                xv = combine_d((double)As[r * (TS + 1) + li], (double)Bs[r * (TS + 1) + lj], a.op, (double)a.eps);
+            else
+                xv = (double)combine_f((float)As[r * (TS + 1) + li], (float)Bs[r * (TS + 1) + lj], a.op, a.eps);
+            if (PASS == 1) {
+                mn = xv < mn ? xv : mn;
+                mx = xv > mx ? xv : mx;
+            } else {
+                int xb = (int)((xv - xmin) * scale);
+                xb = xb < 0 ? 0 : (xb >= a.bins ? a.bins - 1 : xb);
+                h[xb * a.U + ys[r]] += 1;
+            }
+        }
+    }
+    if (!valid) return;
+    if (PASS == 1) {
+        if (r1 > r0) {
+            atomicMin(&mm[0], dkey(mn));
+            atomicMax(&mm[1], dkey(mx));
+        }
+    } else if (live) {
+        unsigned* g = a.hist + ((int64_t)t * kTilePairs + e) * (a.bins * a.U);
+        for (int c = 0; c < a.bins * a.U; ++c)
+            if (h[c]) atomicAdd(&g[c], (unsigned)h[c]);
+    }
+}
+
+__global__ void mm_init_kernel(long long* mm, int64_t count) {
+    for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < count;
+         q += (int64_t)gridDim.x * blockDim.x) {
+        mm[2 * q] = 0x7FFFFFFFFFFFFFFFLL;
+        mm[2 * q + 1] = (long long)0x8000000000000000ULL;
+    }
+}
+
+// ---- y bins -----------------------------------------------------------------
+
+__global__ void ymm_kernel(const float* y, int64_t n, long long* ymm) {
+    double mn = INFINITY, mx = -INFINITY;
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n;
+         r += (int64_t)gridDim.x * blockDim.x) {
+        double v = y[r];
+        mn = v < mn ? v : mn;
+        mx = v > mx ? v : mx;
+    }
+    if (mn <= mx) {
+        atomicMin(&ymm[0], dkey(mn));
+        atomicMax(&ymm[1], dkey(mx));
+    }
+}
+
+__device__ __forceinline__ int ybin_of(double v, double ymin, double yscale, int bins) {
+    int b = (int)((v - ymin) * yscale);
+    return b < 0 ? 0 : (b >= bins ? bins - 1 : b);
+}
+
+__global__ void ycount_kernel(const float* y, int64_t n, const long long* ymm, int bins,
+                              unsigned* counts) {
+    double ymin = dval(ymm[0]), ymax = dval(ymm[1]);
+    if (!(ymax > ymin)) return;
+    double ys = (double)bins / (ymax - ymin);
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n;
+         r += (int64_t)gridDim.x * blockDim.x)
+        atomicAdd(&counts[ybin_of(y[r], ymin, ys, bins)], 1u);
+}
+
+// counts[bins] -> map[bins] (compact code or 255) and meta = {U, ready}
+__global__ void ymap_kernel(const unsigned* counts, const long long* ymm, int bins, int* map,
+                            int* meta) {
+    double ymin = dval(ymm[0]), ymax = dval(ymm[1]);
+    int ready = ymax > ymin;
+    int u = 0;
+    for (int b = 0; b < bins; ++b) map[b] = (ready && counts[b]) ? u++ : 255;
+    meta[0] = u;
+    meta[1] = ready;
+}
+
+__global__ void ycode_kernel(const float* y, int64_t n, const long long* ymm, int bins,
+                             const int* map, uint8_t* ycode) {
+    double ymin = dval(ymm[0]), ymax = dval(ymm[1]);
+    double ys = (double)bins / (ymax - ymin);
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n;
+         r += (int64_t)gridDim.x * blockDim.x)
+        ycode[r] = (uint8_t)map[ybin_of(y[r], ymin, ys, bins)];
+}
+
+// ---- finish: MI per pair + top-k ----------------------------------------------
+
+struct MiFinishArgs {
+    const TileCoord* tiles;
+    int n_tiles;
+    int64_t f, n;
+    const long long* mm;
+    const unsigned* hist;
+    const unsigned* ycounts;  // [bins] rows per y bin (p_y of the reference)
+    const int* map;           // [bins] compact codes
+    int bins, U, ready;
+    int k_pad;
+    Cand* cands;
+    double* all_scores;
+};
+
+__global__ void __launch_bounds__(256) mi_finish_kernel(MiFinishArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    Cand* s = reinterpret_cast<Cand*>(smem_raw);
+    __shared__ double py[256];
+    const int t = blockIdx.x;
+    const TileCoord tc = a.tiles[t];
+    for (int b = threadIdx.x; b < a.bins; b += blockDim.x) {
+        int c = a.map[b];
+        if (c != 255) py[c] = (double)a.ycounts[b];
+    }
+    __syncthreads();
+    const double inv_total = 1.0 / (double)a.n;
+    const double inv_total_sq = inv_total * inv_total;
+    for (int e = threadIdx.x; e < kTilePairs; e += blockDim.x) {
+        int li = e / kTile, lj = e % kTile;
+        int64_t i = (int64_t)tc.bi * kTile + li, j = (int64_t)tc.bj * kTile + lj;
+        Cand c;
+        c.pad = 0;
+        if (i < j && j < a.f) {
+            double mi = 0.0;
+            const long long* mm = a.mm + ((int64_t)t * kTilePairs + e) * 2;
+            if (a.ready && mm[0] != mm[1]) {
+                const unsigned* h = a.hist + ((int64_t)t * kTilePairs + e) * (a.bins * a.U);
+                for (int bx = 0; bx < a.bins; ++bx) {
+                    double px = 0.0;
+                    for (int u = 0; u < a.U; ++u) px += (double)h[bx * a.U + u];
+                    if (px == 0.0) continue;
+                    for (int u = 0; u < a.U; ++u) {
+                        double count = (double)h[bx * a.U + u];
+                        if (count <= 0.0) continue;
+                        double p = count * inv_total;
+                        double expected = (px * py[u]) * inv_total_sq;
+                        if (expected > 0.0) mi += p * log(p / expected);
+                    }
+                }
+            }
+            c.score = mi;
+            c.pid = (uint32_t)(i * a.f + j);
+            if (a.all_scores) a.all_scores[i * a.f - i * (i + 1) / 2 + (j - i - 1)] = mi;
+        } else {
+            c.score = 0.0;
+            c.pid = kNoPair;
+        }
+        s[e] = c;
+    }
+    if (a.cands == nullptr) return;
+    __syncthreads();
+    bitonic_sort(s, kTilePairs);
+    Cand* out = a.cands + (int64_t)t * a.k_pad;
+    for (int e = threadIdx.x; e < a.k_pad; e += blockDim.x) out[e] = s[e];
+}
+
+template <int TS, int PASS, bool CENTRED>
+cudaError_t launch_pass(const MiArgs& a, int splits, cudaStream_t stream) {
+    using V = typename std::conditional<CENTRED, double, float>::type;
+    size_t smem = 2 * sizeof(V) * kMiRows * (TS + 1) + kMiRows;
+    smem = (smem + 15) / 16 * 16;
+    if (PASS == 2) smem += (size_t)TS * TS * a.hstride * sizeof(uint16_t);
+    auto kern = mi_pass_kernel<TS, PASS, CENTRED>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((unsigned)(a.n_tiles * (64 / TS) * (64 / TS)), (unsigned)splits);
+    kern<<<grid, TS * TS, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+template <int TS, bool CENTRED>
+cudaError_t run_passes(const MiArgs& a, int splits, cudaStream_t stream) {
+    cudaError_t e;
+    {
+        KernelTimer timer(stream, GAFIME_KERNEL_MI_PASS1);
+        e = launch_pass<TS, 1, CENTRED>(a, splits, stream);
+    }
+    if (e == cudaSuccess) {
+        KernelTimer timer(stream, GAFIME_KERNEL_MI_PASS2);
+        e = launch_pass<TS, 2, CENTRED>(a, splits, stream);
+    }
+    return e;
+}
+
+}  // namespace
+
+cudaError_t launch_mi_scores(Bucket& b, const ColumnStats& cs, bool centred, int op, float div_eps,
+                             int mi_bins, const TileCoord* d_tiles, int n_tiles, int k_pad,
+                             Cand* cands, double* all_scores, cudaStream_t stream) {
+    const int bins = mi_bins;
+    // scratch layout in b.mi: ymm[2] | counts[256] | map[256] | meta[2] | ycode[ld] | mm
+    size_t off_ymm = 0, off_counts = 64, off_map = off_counts + 256 * 4, off_meta = off_map + 256 * 4;
+    size_t off_ycode = (off_meta + 64 + 255) / 256 * 256;
+    size_t off_mm = off_ycode + ((size_t)b.ld + 255) / 256 * 256;
+    size_t mm_bytes = (size_t)n_tiles * kTilePairs * 2 * sizeof(long long);
+    size_t mi_bytes = off_mm + (mm_bytes + 255) / 256 * 256;
+    cudaError_t e = ensure(b.mi, mi_bytes);
+    if (e != cudaSuccess) return e;
+    char* base = (char*)b.mi.ptr;
+    long long* ymm = (long long*)(base + off_ymm);
+    unsigned* counts = (unsigned*)(base + off_counts);
+    int* map = (int*)(base + off_map);
+    int* meta = (int*)(base + off_meta);
+    const float* y = b.d_data + b.f * b.ld;
+
+    // y bins and the compact code map (one small host sync to learn U)
+    long long init[2] = {0x7FFFFFFFFFFFFFFFLL, (long long)0x8000000000000000ULL};
+    e = cudaMemcpyAsync(ymm, init, sizeof(init), cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(counts, 0, 256 * 4, stream);
+    if (e != cudaSuccess) return e;
+    ymm_kernel<<<2 * b.sm_count, 256, 0, stream>>>(y, b.n, ymm);
+    ycount_kernel<<<2 * b.sm_count, 256, 0, stream>>>(y, b.n, ymm, bins, counts);
+    ymap_kernel<<<1, 1, 0, stream>>>(counts, ymm, bins, map, meta);
+    int hmeta[2] = {0, 0};
+    e = cudaMemcpyAsync(hmeta, meta, sizeof(hmeta), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return e;
+    const int U = std::max(1, hmeta[0]);
+    const int ready = hmeta[1];
+    if (bins * U > 768) return cudaErrorInvalidValue;  // joint histogram too large for shared memory
+
+    // the joint histograms live in their own buffer: growing it must not move the
+    // y-bin map written above
+    size_t hist_bytes = (size_t)n_tiles * kTilePairs * bins * U * sizeof(unsigned);
+    e = ensure(b.mi_hist, hist_bytes);
+    if (e != cudaSuccess) return e;
+    uint8_t* ycode = (uint8_t*)(base + off_ycode);
+    long long* mm = (long long*)(base + off_mm);
+    unsigned* hist = (unsigned*)b.mi_hist.ptr;
+
+    const double* means = cs.d_col;
+    if (ready) ycode_kernel<<<2 * b.sm_count, 256, 0, stream>>>(y, b.n, ymm, bins, map, ycode);
+    mm_init_kernel<<<2 * b.sm_count, 256, 0, stream>>>(mm, (int64_t)n_tiles * kTilePairs);
+    e = cudaMemsetAsync(hist, 0, hist_bytes, stream);
+    if (e != cudaSuccess) return e;
+
+    MiArgs a;
+    a.x = b.d_data;
+    a.ld = b.ld;
+    a.n = b.n;
+    a.f = b.f;
+    a.colstats = means;
+    a.tiles = d_tiles;
+    a.n_tiles = n_tiles;
+    a.op = op;
+    a.eps = div_eps;
+    a.mm = mm;
+    a.ycode = ycode;
+    a.bins = bins;
+    a.U = U;
+    a.hstride = ((bins * U + 1) / 2) * 2;
+    if (((a.hstride / 2) & 1) == 0) a.hstride += 2;  // odd word stride: spreads banks
+    a.hist = hist;
+    if (ready) {
+        int64_t per = std::min<int64_t>(kMiMaxSplitRows, (b.n + 1) / 2 + kMiRows);
+        per = std::max<int64_t>(kMiRows, (per + kMiRows - 1) / kMiRows * kMiRows);
+        int splits = (int)((b.n + per - 1) / per);
+        // aim for >= 4 resident CTAs per SM across the grid
+        int64_t ctas = (int64_t)n_tiles * 16 * splits;
+        while (ctas < 4 * b.sm_count && per > 4 * kMiRows) {
+            per = std::max<int64_t>(kMiRows, (per / 2 + kMiRows - 1) / kMiRows * kMiRows);
+            splits = (int)((b.n + per - 1) / per);
+            ctas = (int64_t)n_tiles * 16 * splits;
+        }
+        a.rows_per_split = per;
+        const bool small = bins * U <= 192;
+        if (centred)
+            e = small ? run_passes<16, true>(a, splits, stream) : run_passes<8, true>(a, splits, stream);
+        else
+            e = small ? run_passes<16, false>(a, splits, stream) : run_passes<8, false>(a, splits, stream);
+        if (e != cudaSuccess) return e;
+    }
+
+    MiFinishArgs fa;
+    fa.tiles = d_tiles;
+    fa.n_tiles = n_tiles;
+    fa.f = b.f;
+    fa.n = b.n;
+    fa.mm = mm;
+    fa.hist = hist;
+    fa.ycounts = counts;
+    fa.map = map;
+    fa.bins = bins;
+    fa.U = U;
+    fa.ready = ready;
+    fa.k_pad = k_pad;
+    fa.cands = cands;
+    fa.all_scores = all_scores;
+    size_t smem = sizeof(Cand) * kTilePairs;
+    cudaFuncSetAttribute(mi_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    KernelTimer timer(stream, GAFIME_KERNEL_MI_FINISH);
+    mi_finish_kernel<<<n_tiles, 256, smem, stream>>>(fa);
+    return cudaGetLastError();
+}
+
+}  // namespace gafime

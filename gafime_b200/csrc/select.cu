@@ -1,0 +1,184 @@
+// select.cu -- scoring epilogue fused with a block-level bitonic top-k, the
+// device merge of per-tile candidate lists, and the host merge across shards.
+//
+// Pearson from the moments (per pair, fp64), following the reference's
+// _pearson_from_stats (native_cuda_backend.py:471-486) and gafime_core's
+// pearson_from_sums (gafime_core.cpp:179-198):
+//     r = cov / sqrt(var_x * var_y),   r = 0 when n <= 1 or var_x*var_y <= 0
+// with, per operator (a = X[:, i], b = X[:, j], i < j; S* from moments.cu, per-column
+// sums Sa = sum a, Qa = sum a^2, Ua = sum a*ycen):
+//     multiply / divide : sum x = S1, sum x^2 = S2, cov = S3
+//     add               : sum x = Sa + Sb, sum x^2 = Qa + 2 S1 + Qb, cov = Ua + Ub
+//     subtract          : sum x = Sa - Sb, sum x^2 = Qa - 2 S1 + Qb, cov = Ua - Ub
+//     var_x = sum x^2 - (sum x)^2 / n
+// (cov uses ycen = y - mean y, so it equals sum xy - sum x sum y / n.)
+// Ranking: |score| descending, then pair id i*F + j ascending (the reference
+// sorts by abs(metric), gafime/sklearn.py:62-71; ties are ordered by pair).
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "engine.h"
+#include "select.cuh"
+
+namespace gafime {
+
+namespace {
+
+constexpr int kEpiThreads = 256;
+
+__device__ __forceinline__ double pearson(double n, double sx, double sxx, double cov, double var_y) {
+    if (n <= 1.0) return 0.0;
+    double var_x = sxx - sx * sx / n;
+    double d = var_x * var_y;
+    if (!(d > 0.0)) return 0.0;
+    return cov / sqrt(d);
+}
+
+__global__ void __launch_bounds__(kEpiThreads) epilogue_topk_kernel(EpilogueArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    Cand* s = reinterpret_cast<Cand*>(smem_raw);  // [kTilePairs]
+    const int t = blockIdx.x;
+    const TileCoord tc = a.tiles[t];
+    const double n = a.ystats[0], var_y = a.ystats[2];
+    const int64_t f = a.f;
+    for (int e = threadIdx.x; e < kTilePairs; e += kEpiThreads) {
+        int li = e / kTile, lj = e % kTile;
+        int64_t i = (int64_t)tc.bi * kTile + li, j = (int64_t)tc.bj * kTile + lj;
+        Cand c;
+        c.pad = 0;
+        if (i < j && j < f) {
+            double S1 = 0.0, S2 = 0.0, S3 = 0.0;
+            for (int sp = 0; sp < a.splits; ++sp) {
+                const double* m = a.moments + ((int64_t)sp * a.n_tiles + t) * 3 * kTilePairs;
+                S1 += m[e];
+                S2 += m[kTilePairs + e];
+                S3 += m[2 * kTilePairs + e];
+            }
+            double sx, sxx, cov;
+            if (a.op == GAFIME_INTERACT_ADD || a.op == GAFIME_INTERACT_SUB) {
+                double sg = a.op == GAFIME_INTERACT_ADD ? 1.0 : -1.0;
+                const double* ci = a.colstats + i * 4;
+                const double* cj = a.colstats + j * 4;
+                sx = ci[0] + sg * cj[0];
+                sxx = ci[1] + 2.0 * sg * S1 + cj[1];
+                cov = ci[2] + sg * cj[2];
+            } else {
+                sx = S1;
+                sxx = S2;
+                cov = S3;
+            }
+            c.score = pearson(n, sx, sxx, cov, var_y);
+            c.pid = (uint32_t)(i * f + j);
+            if (a.all_scores) {
+                int64_t p = i * f - i * (i + 1) / 2 + (j - i - 1);
+                a.all_scores[p] = c.score;
+            }
+        } else {
+            c.score = 0.0;
+            c.pid = kNoPair;
+        }
+        s[e] = c;
+    }
+    if (a.cands == nullptr) return;  // scores only (uniform across the block)
+    __syncthreads();
+    bitonic_sort(s, kTilePairs);
+    Cand* out = a.cands + (int64_t)t * a.k_pad;
+    for (int e = threadIdx.x; e < a.k_pad; e += kEpiThreads) out[e] = s[e];
+}
+
+// Each CTA merges `group` consecutive sorted lists (k_pad entries each) into the
+// k_pad best entries.  Lists beyond n_lists are treated as empty.
+__global__ void __launch_bounds__(1024) merge_kernel(const Cand* __restrict__ in, int n_lists,
+                                                     int k_pad, int group, Cand* __restrict__ out) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    Cand* s = reinterpret_cast<Cand*>(smem_raw);
+    const int g = blockIdx.x;
+    const int total = group * k_pad;
+    for (int e = threadIdx.x; e < total; e += blockDim.x) {
+        int l = g * group + e / k_pad;
+        if (l < n_lists) {
+            s[e] = in[(int64_t)l * k_pad + (e % k_pad)];
+        } else {
+            Cand c;
+            c.score = 0.0;
+            c.pid = kNoPair;
+            c.pad = 0;
+            s[e] = c;
+        }
+    }
+    __syncthreads();
+    bitonic_sort(s, total);
+    for (int e = threadIdx.x; e < k_pad; e += blockDim.x) out[(int64_t)g * k_pad + e] = s[e];
+}
+
+}  // namespace
+
+cudaError_t launch_epilogue_topk(const EpilogueArgs& a, cudaStream_t stream) {
+    if (a.n_tiles <= 0) return cudaSuccess;
+    size_t smem = sizeof(Cand) * kTilePairs;
+    cudaFuncSetAttribute(epilogue_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    epilogue_topk_kernel<<<a.n_tiles, kEpiThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t merge_candidates(Cand* buf, Cand* tmp, int n_lists, int k_pad, int n_groups_unused,
+                             Cand** final_list, cudaStream_t stream) {
+    (void)n_groups_unused;
+    // group * k_pad <= 8192 entries (128 KB of shared memory)
+    int group = std::max(2, 8192 / k_pad);
+    size_t smem = sizeof(Cand) * (size_t)group * k_pad;
+    cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    Cand* src = buf;
+    Cand* dst = tmp;
+    while (n_lists > 1) {
+        int out_lists = (n_lists + group - 1) / group;
+        merge_kernel<<<out_lists, 1024, smem, stream>>>(src, n_lists, k_pad, group, dst);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        std::swap(src, dst);
+        n_lists = out_lists;
+    }
+    *final_list = src;
+    return cudaSuccess;
+}
+
+}  // namespace gafime
+
+using namespace gafime;
+
+extern "C" int gafime_topk_merge(const int32_t* cand_i, const int32_t* cand_j,
+                                 const double* cand_score, int64_t n_cand, int k, int32_t* out_i,
+                                 int32_t* out_j, double* out_score, int* out_count) {
+    if (n_cand < 0 || k <= 0 || !out_i || !out_j || !out_score || !out_count) return GAFIME_ERROR_INVALID_ARGS;
+    if (n_cand > 0 && (!cand_i || !cand_j || !cand_score)) return GAFIME_ERROR_INVALID_ARGS;
+    struct E {
+        double s;
+        int32_t i, j;
+    };
+    std::vector<E> v;
+    v.reserve((size_t)n_cand);
+    for (int64_t c = 0; c < n_cand; ++c) {
+        if (cand_i[c] < 0 || cand_j[c] < 0) continue;  // empty slots
+        int32_t lo = std::min(cand_i[c], cand_j[c]), hi = std::max(cand_i[c], cand_j[c]);
+        v.push_back({cand_score[c], lo, hi});
+    }
+    auto rank = [](double s) { return s != s ? -1.0 : (s < 0 ? -s : s); };
+    std::sort(v.begin(), v.end(), [&](const E& a, const E& b) {
+        double ra = rank(a.s), rb = rank(b.s);
+        if (ra != rb) return ra > rb;
+        if (a.i != b.i) return a.i < b.i;
+        return a.j < b.j;
+    });
+    int m = (int)std::min<int64_t>((int64_t)k, (int64_t)v.size());
+    for (int c = 0; c < m; ++c) {
+        out_i[c] = v[c].i;
+        out_j[c] = v[c].j;
+        out_score[c] = v[c].s;
+    }
+    *out_count = m;
+    return GAFIME_SUCCESS;
+}

@@ -1,0 +1,203 @@
+/*
+ * gafime_b200.h -- C ABI of libgafime_cuda.so, the B200 (sm_100a) engine for
+ * GAFIME's all-pairs scoring path.
+ *
+ * Every symbol the reference's loaders bind on this path keeps its exact name,
+ * signature, status codes and ownership rules (reference: src/common/interfaces.h),
+ * so gafime/backends/native_cuda_backend.py and the Rust libloading callers can
+ * load this library in place of the reference's libgafime_cuda.so.  New entry
+ * points (all-pairs scoring, sharding, top-k merge) are marked NEW.
+ *
+ * Conventions (interfaces.h:32-38, kernels.cu:886-889):
+ *   - every function returns int: 0 success, negative GAFIME_ERROR_* on failure;
+ *     no C++ exception crosses the ABI;
+ *   - handles are opaque, owned by the library from *_alloc until *_free, and
+ *     *_free(NULL) succeeds;
+ *   - host pointers are borrowed for the duration of the call only;
+ *   - calls are synchronous: results are in the caller's buffers on return.
+ *   - a bucket remembers the CUDA device that was current at *_alloc and makes it
+ *     current for every later call on that bucket (the reference always used the
+ *     current device, kernels.cu:129-131).
+ */
+#ifndef GAFIME_B200_H
+#define GAFIME_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes -- interfaces.h:32-38 */
+#define GAFIME_SUCCESS 0
+#define GAFIME_ERROR_INVALID_ARGS -1
+#define GAFIME_ERROR_CUDA_NOT_AVAILABLE -2
+#define GAFIME_ERROR_OUT_OF_MEMORY -3
+#define GAFIME_ERROR_KERNEL_FAILED -4
+#define GAFIME_ERROR_PIPELINE_FULL -5
+#define GAFIME_ERROR_NO_RESULT -6
+
+/* Unary operators -- interfaces.h:57-73 */
+#define GAFIME_OP_IDENTITY 0
+#define GAFIME_OP_LOG 1
+#define GAFIME_OP_EXP 2
+#define GAFIME_OP_SQRT 3
+#define GAFIME_OP_TANH 4
+#define GAFIME_OP_SIGMOID 5
+#define GAFIME_OP_SQUARE 6
+#define GAFIME_OP_NEGATE 7
+#define GAFIME_OP_ABS 8
+#define GAFIME_OP_INVERSE 9
+#define GAFIME_OP_CUBE 10
+#define GAFIME_OP_ROLLING_MEAN 11
+#define GAFIME_OP_ROLLING_STD 12
+
+/* Interaction types -- interfaces.h:83-88 */
+#define GAFIME_INTERACT_MULT 0
+#define GAFIME_INTERACT_ADD 1
+#define GAFIME_INTERACT_SUB 2
+#define GAFIME_INTERACT_DIV 3
+#define GAFIME_INTERACT_MAX 4
+#define GAFIME_INTERACT_MIN 5
+
+/* 12-float stats layout -- interfaces.h:110-123 */
+#define GAFIME_STATS_SIZE 12
+
+/* NEW: metric ids, same numbering as gafime_core's MetricId (gafime_core.cpp:28-33) */
+#define GAFIME_METRIC_PEARSON 0
+#define GAFIME_METRIC_MUTUAL_INFO 2
+
+/* NEW: largest k the all-pairs top-k returns per operator */
+#define GAFIME_ALLPAIRS_MAX_K 4096
+
+typedef void* ContiguousBucket; /* interfaces.h:42 */
+
+/* ---------------------------------------------------------------- device ---- */
+
+/* interfaces.h:133 -- 1 when a CUDA device is usable, else 0. */
+int gafime_cuda_available(void);
+
+/* interfaces.h:144-150 -- name (>= 256 chars), total memory in MB, compute capability. */
+int gafime_get_device_info(int device_id, char* name_out, int* memory_mb_out,
+                           int* compute_cap_major_out, int* compute_cap_minor_out);
+
+/* interfaces.h:167-175 -- launch geometry of the current device. */
+int gafime_get_gpu_config(int* block_size_out, int* max_blocks_out, int* sm_count_out,
+                          int* compute_major_out, int* compute_minor_out,
+                          int* l2_cache_bytes_out, char* gpu_name_out);
+
+/* interfaces.h:607 -- 1 and *precision_mode = 4 (tcgen05 f16/bf16/tf32) on sm_100. */
+int gafime_tensor_core_available(int* precision_mode);
+
+/* NEW: make device_id current for the calling thread (cudaSetDevice). */
+int gafime_select_device(int device_id);
+
+/* ------------------------------------------------------- contiguous bucket ---- */
+
+/* interfaces.h:513-517 -- one device buffer for F feature columns + the target,
+ * column-major, plus a uint8 fold mask.  Rows are padded to a multiple of 256 on
+ * the device (zeros) so every tile of the all-pairs kernels is full. */
+int gafime_contiguous_bucket_alloc(int n_samples, int n_features, ContiguousBucket* bucket_out);
+
+/* interfaces.h:522-526 -- h_data = [F0 | F1 | ... | F_{F-1} | y], (F+1)*n floats,
+ * column-major; h_mask = n bytes (may not be NULL, as in the reference). */
+int gafime_contiguous_bucket_upload(ContiguousBucket bucket, const float* h_data,
+                                    const uint8_t* h_mask);
+
+/* interfaces.h:531-540 -- 12 stats of x = combine(op_a(F_a), op_b(F_b)), split by
+ * mask == val_fold_id.  Rows with NaN x or y are skipped (cpu_backend.cpp:274).
+ * Sums are accumulated in fp64 in a fixed order (deterministic), then cast to
+ * float for this float* output. */
+int gafime_contiguous_bucket_compute(ContiguousBucket bucket, int feature_a_idx,
+                                     int feature_b_idx, int op_a, int op_b,
+                                     int interact_type, int val_fold_id, float* h_stats_out);
+
+/* interfaces.h:545 */
+int gafime_contiguous_bucket_free(ContiguousBucket bucket);
+
+/* interfaces.h:550-554 */
+int gafime_contiguous_bucket_info(ContiguousBucket bucket, int* n_samples_out,
+                                  int* n_features_out);
+
+/* ------------------------------------------------------- NEW: all pairs ---- */
+
+/*
+ * NEW.  Score every pair i<j of the bucket's features (or, with n_shards > 1,
+ * this process's share of them) for n_ops interaction types and return the k
+ * best pairs per operator.  Replaces the reference's per-pair loop
+ * gafime/backends/native_cuda_backend.py:368-379 (one gafime_contiguous_bucket_compute
+ * launch + sync per pair) with one call.
+ *
+ *   interact_types  n_ops ids among GAFIME_INTERACT_MULT/ADD/SUB/DIV; x = F_i op F_j
+ *                   with i < j (subtract and divide are not commutative).
+ *   metric          GAFIME_METRIC_PEARSON (rank by |r|) or GAFIME_METRIC_MUTUAL_INFO.
+ *   center          0: raw kernel-API semantics (src/cpu/cpu_backend.cpp:229-295);
+ *                   1: columns centred by their fp64 means first (Selector / Engine /
+ *                      gafime_core semantics, gafime_core.cpp:570-577).
+ *   div_eps         safe-divide clamp |b| < eps -> copysign(eps, b) (reference 1e-8).
+ *   mi_bins         equal-width bins on the interaction and on y (gafime_core.cpp:200-333).
+ *   k               1..GAFIME_ALLPAIRS_MAX_K.
+ *   shard_id/n_shards  pair-tile sharding across processes (0/1 = everything).
+ *   out_i, out_j, out_score   [n_ops * k]: per operator, pairs ordered by |score|
+ *                   descending then (i, j) ascending; out_score is the signed score.
+ *   out_count       [n_ops]: entries written per operator (< k when fewer pairs).
+ *
+ * The input must be finite (the engine's coerce_inputs guarantees it,
+ * gafime/utils/arrays.py:26-30); non-finite values return GAFIME_ERROR_INVALID_ARGS.
+ * Results are bit-identical from run to run (fixed-order fp64 reductions).
+ */
+int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact_types, int n_ops,
+                         int metric, int center, float div_eps, int mi_bins, int k,
+                         int shard_id, int n_shards, int32_t* out_i, int32_t* out_j,
+                         double* out_score, int* out_count);
+
+/*
+ * NEW.  Signed score of every pair i<j for one operator, in row-major
+ * upper-triangle order (p = i*F - i*(i+1)/2 + j - i - 1), P = F*(F-1)/2 entries.
+ * Serves Backend.score_combos (gafime/backends/base.py:67-78) when the combo list
+ * is all pairs of the bucket's features.
+ */
+int gafime_allpairs_scores(ContiguousBucket bucket, int interact_type, int metric, int center,
+                           float div_eps, int mi_bins, double* out_scores);
+
+/*
+ * NEW.  Deterministic host merge of per-shard candidates (the step after the
+ * allgather of every shard's top-k): keeps the k best of n_cand entries by
+ * |score| descending then (i, j) ascending.  out_* hold min(k, n_cand) entries;
+ * *out_count receives that number.
+ */
+int gafime_topk_merge(const int32_t* cand_i, const int32_t* cand_j, const double* cand_score,
+                      int64_t n_cand, int k, int32_t* out_i, int32_t* out_j, double* out_score,
+                      int* out_count);
+
+/* ------------------------------------------------------ NEW: profiling ---- */
+
+/* Kernel ids of the timing registry. */
+#define GAFIME_KERNEL_COLUMN_STATS 1
+#define GAFIME_KERNEL_PAIR_MOMENTS 2
+#define GAFIME_KERNEL_EPILOGUE_TOPK 3
+#define GAFIME_KERNEL_MERGE 4
+#define GAFIME_KERNEL_MI_PASS1 5
+#define GAFIME_KERNEL_MI_PASS2 6
+#define GAFIME_KERNEL_MI_FINISH 7
+#define GAFIME_KERNEL_LEGACY_PAIR 8
+#define GAFIME_KERNEL_FINITE_CHECK 9
+#define GAFIME_KERNEL_GRAM_TC 10
+
+/* NEW.  enable = 1: from now on bracket every engine kernel launch with CUDA
+ * events on its stream; any previous records are dropped.  enable = 0: stop. */
+int gafime_profile_enable(int enable);
+
+/* NEW.  Total device milliseconds and number of launches recorded for one kernel
+ * id (kernel_id < 0: all kernels).  Waits for the recorded events. */
+int gafime_profile_read(int kernel_id, double* total_ms, int* launches);
+
+/* NEW.  The CUDA stream (cudaStream_t) every call on this bucket runs on, so a
+ * caller can order its own work or events against it. */
+int gafime_contiguous_bucket_stream(ContiguousBucket bucket, void** stream_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GAFIME_B200_H */

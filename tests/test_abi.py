@@ -1,0 +1,75 @@
+"""The C-ABI library builds, loads without a GPU and exports every declared symbol."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import REPO
+
+HEADER = os.path.join(REPO, "include", "gafime_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\bint\s+(gafime_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from gafime_b200 import build as gb
+    gb.build()
+    from gafime_b200 import _native
+    return _native.load(require_gpu=False)
+
+
+def test_header_declares_expected_entry_points():
+    syms = declared_symbols()
+    for s in ("gafime_contiguous_bucket_alloc", "gafime_contiguous_bucket_compute",
+              "gafime_allpairs_topk", "gafime_allpairs_scores", "gafime_topk_merge"):
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for s in declared_symbols():
+        assert hasattr(lib, s), s
+    from gafime_b200 import _native
+    assert set(_native.EXPORTED) == set(declared_symbols())
+
+
+def test_status_codes_match_reference_values():
+    text = open(HEADER).read()
+    codes = dict(re.findall(r"#define (GAFIME_(?:SUCCESS|ERROR_\w+)) (-?\d+)", text))
+    # interfaces.h:32-38
+    assert codes == {"GAFIME_SUCCESS": "0", "GAFIME_ERROR_INVALID_ARGS": "-1",
+                     "GAFIME_ERROR_CUDA_NOT_AVAILABLE": "-2", "GAFIME_ERROR_OUT_OF_MEMORY": "-3",
+                     "GAFIME_ERROR_KERNEL_FAILED": "-4", "GAFIME_ERROR_PIPELINE_FULL": "-5",
+                     "GAFIME_ERROR_NO_RESULT": "-6"}
+
+
+def test_no_gpu_paths_fail_loudly(lib):
+    from gafime_b200 import _native
+    if lib.gafime_cuda_available() == 1:
+        pytest.skip("a GPU is present")
+    h = ctypes.c_void_p(0)
+    assert lib.gafime_contiguous_bucket_alloc(10, 3, ctypes.byref(h)) == -2
+    with pytest.raises(RuntimeError):
+        _native.load(require_gpu=True)
+    # NULL handles / bad sizes are argument errors, never crashes
+    assert lib.gafime_contiguous_bucket_free(None) == 0
+    assert lib.gafime_contiguous_bucket_alloc(0, 3, ctypes.byref(h)) == -1
+    assert lib.gafime_allpairs_topk(None, None, 1, 0, 0, 1e-8, 16, 5, 0, 1, None, None, None, None) == -1
+
+
+def test_host_topk_merge_orders_by_abs_score_then_pair(lib):
+    from gafime_b200 import _native
+    ci = np.array([5, 0, 2, 1, -1], dtype=np.int32)
+    cj = np.array([1, 3, 4, 2, -1], dtype=np.int32)
+    cs = np.array([0.5, -0.5, 0.9, 0.1, 0.0])
+    i, j, s = _native.merge_topk(ci, cj, cs, 3)
+    assert list(zip(i.tolist(), j.tolist())) == [(2, 4), (0, 3), (1, 5)]
+    assert s.tolist() == [0.9, -0.5, 0.5]
+    i, j, s = _native.merge_topk(ci, cj, cs, 10)
+    assert len(i) == 4  # the empty slot (-1, -1) is dropped

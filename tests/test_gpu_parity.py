@@ -1,0 +1,229 @@
+"""Parity of the CUDA path (through the C ABI) with the oracle and the reference goldens.
+
+Tolerances (stated per test):
+  * Pearson: |r_gpu - r_oracle| <= 1e-4 * |r_oracle| + 1e-6 for every pair -- the
+    north-star bound is 1e-4 relative; the 1e-6 absolute floor covers pairs with
+    |r| ~ 1e-3 and below, where relative error is meaningless.
+  * MI: 1e-5 absolute.
+  * top-k: identical pair sets except pairs whose oracle score ties the k-th score
+    within the tolerance (tie class).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+OPS = ["multiply", "add", "subtract", "divide"]
+
+
+@pytest.fixture(scope="module")
+def native():
+    from gafime_b200 import _native
+    _native.load()
+    return _native
+
+
+def bucket_for(native, X, y):
+    b = native.Bucket(X.shape[0], X.shape[1])
+    b.upload(X, y)
+    return b
+
+
+def assert_pearson_close(got, want, rtol=1e-4, atol=1e-6):
+    err = np.abs(got - want)
+    bad = err > rtol * np.abs(want) + atol
+    assert not bad.any(), (np.flatnonzero(bad)[:10], got[bad][:5], want[bad][:5])
+
+
+def assert_topk_equivalent(gi, gj, want_scores, pi, pj, k, rtol=1e-4, atol=1e-6):
+    """GPU top-k (gi, gj) vs the oracle scores of all pairs: same set modulo ties."""
+    mag = np.abs(want_scores)
+    order = np.lexsort((pj, pi, -mag))
+    kth = mag[order[k - 1]]
+    tol = rtol * kth + atol
+    must = {(int(pi[p]), int(pj[p])) for p in order if mag[p] > kth + tol}
+    may = {(int(pi[p]), int(pj[p])) for p in order if mag[p] >= kth - tol}
+    got = {(int(a), int(b)) for a, b in zip(gi, gj)}
+    assert len(got) == k
+    assert must <= got, sorted(must - got)[:5]
+    assert got <= may, sorted(got - may)[:5]
+
+
+def test_config1_centred_pearson_matches_gafime_core(native, golden, oracle):
+    g = golden("config1_centred.npz")
+    with bucket_for(native, g["X"], g["y"]) as b:
+        s = b.scores("multiply", center=True)
+        assert_pearson_close(s, g["core_scores"][:, 0])
+        top = b.topk(["multiply"], 5, center=True)["multiply"]
+    got = {(int(i), int(j)) for i, j in zip(top[0], top[1])}
+    want = {(int(min(a, c)), int(max(a, c))) for a, c in g["selector_top_core"]}
+    assert got == want
+    assert (int(top[0][0]), int(top[1][0])) == (3, 15)
+
+
+def test_config1_mutual_info_matches_gafime_core(native, golden):
+    g = golden("config1_centred.npz")
+    with bucket_for(native, g["X"], g["y"]) as b:
+        m = b.scores("multiply", metric="mutual_info", center=True, mi_bins=16)
+    np.testing.assert_allclose(m, g["core_scores"][:, 1], rtol=0, atol=1e-5)
+
+
+@pytest.mark.parametrize("bins,key,col", [(32, "core_b32", 1), (16, "core_b16", 0)])
+def test_mi_3class_matches_gafime_core(native, golden, bins, key, col):
+    g = golden("mi_3class.npz")
+    with bucket_for(native, g["X"], g["y"]) as b:
+        m = b.scores("multiply", metric="mutual_info", center=True, mi_bins=bins)
+        top = b.topk(["multiply"], 10, metric="mutual_info", center=True, mi_bins=bins)["multiply"]
+    want = g[key][:, col]
+    np.testing.assert_allclose(m, want, rtol=0, atol=1e-5)
+    pi, pj = np.triu_indices(g["X"].shape[1], k=1)
+    assert_topk_equivalent(top[0], top[1], want, pi, pj, 10, rtol=0, atol=1e-5)
+
+
+@pytest.mark.parametrize("op", OPS)
+def test_raw_ops_match_oracle_and_reference_stats(native, golden, oracle, op):
+    g = golden("raw_ops.npz")
+    X, y = g["X"], g["y"]
+    want = oracle.raw_pearson(X, y, op, div_eps=1e-8)
+    with bucket_for(native, X, y) as b:
+        s = b.scores(op, div_eps=1e-8)
+        assert_pearson_close(s, want)
+        # legacy single-pair ABI: 12 float stats equal the reference library's
+        pi, pj = np.triu_indices(X.shape[1], k=1)
+        ref = g["ref_stats"][OPS.index(op)]
+        for p in range(0, len(pi), 7):
+            st = b.compute_pair(int(pi[p]), int(pj[p]), 0, 0, OPS.index(op), 255)
+            np.testing.assert_allclose(st, ref[p], rtol=2e-7, atol=0)
+
+
+@pytest.mark.parametrize("n,f", [(1000, 70), (20000, 129), (33, 5), (31, 2), (257, 64), (1, 3)])
+@pytest.mark.parametrize("center", [False, True])
+def test_all_ops_ragged_shapes(native, oracle, n, f, center):
+    rng = np.random.default_rng(n * 131 + f)
+    X = np.hstack([rng.standard_normal((n, f - f // 2)),
+                   rng.lognormal(0, 1, (n, f // 2))]).astype(np.float32)
+    y = (rng.random(n) < 0.4).astype(np.float32)
+    Xo = X - X.astype(np.float64).mean(axis=0) if center else X
+    with bucket_for(native, X, y) as b:
+        for op in OPS:
+            want = oracle.raw_pearson(np.asarray(Xo, dtype=np.float32), y, op, div_eps=1e-6)
+            got = b.scores(op, center=center, div_eps=1e-6)
+            assert_pearson_close(got, want, rtol=1e-4, atol=2e-6)
+            k = min(8, len(want))
+            top = b.topk([op], k, center=center, div_eps=1e-6)[op]
+            pi, pj = np.triu_indices(f, k=1)
+            assert_topk_equivalent(top[0], top[1], want, pi, pj, k, atol=2e-6)
+
+
+def test_multi_op_call_equals_single_op_calls(native):
+    rng = np.random.default_rng(5)
+    X = rng.standard_normal((5000, 90)).astype(np.float32)
+    y = (X[:, 3] * X[:, 40] + rng.standard_normal(5000) > 0).astype(np.float32)
+    with bucket_for(native, X, y) as b:
+        multi = b.topk(OPS, 25, div_eps=1e-6)
+        for op in OPS:
+            single = b.topk([op], 25, div_eps=1e-6)[op]
+            for a, c in zip(multi[op], single):
+                np.testing.assert_array_equal(a, c)
+        assert (int(multi["multiply"][0][0]), int(multi["multiply"][1][0])) == (3, 40)
+
+
+def test_deterministic_bitwise(native):
+    rng = np.random.default_rng(9)
+    X = rng.lognormal(0, 1, (30000, 100)).astype(np.float32)
+    y = rng.random(30000).astype(np.float32)
+    with bucket_for(native, X, y) as b:
+        a = [b.scores(op, div_eps=1e-6) for op in OPS]
+        c = [b.scores(op, div_eps=1e-6) for op in OPS]
+    for u, v in zip(a, c):
+        np.testing.assert_array_equal(u, v)
+
+
+def test_shards_merge_to_the_single_process_topk(native):
+    rng = np.random.default_rng(11)
+    X = rng.standard_normal((4000, 200)).astype(np.float32)
+    y = rng.standard_normal(4000).astype(np.float32)
+    with bucket_for(native, X, y) as b:
+        full = b.topk(["multiply", "divide"], 50, div_eps=1e-6)
+        for n_shards in (2, 3, 8):
+            parts = [b.topk(["multiply", "divide"], 50, div_eps=1e-6, shard_id=s, n_shards=n_shards)
+                     for s in range(n_shards)]
+            for op in ("multiply", "divide"):
+                ci = np.concatenate([p[op][0] for p in parts])
+                cj = np.concatenate([p[op][1] for p in parts])
+                cs = np.concatenate([p[op][2] for p in parts])
+                mi, mj, ms = native.merge_topk(ci, cj, cs, 50)
+                np.testing.assert_array_equal(mi, full[op][0])
+                np.testing.assert_array_equal(mj, full[op][1])
+                np.testing.assert_array_equal(ms, full[op][2])
+
+
+def test_non_finite_input_is_rejected(native):
+    X = np.ones((100, 4), dtype=np.float32)
+    X[5, 2] = np.nan
+    y = np.arange(100, dtype=np.float32)
+    with bucket_for(native, X, y) as b:
+        with pytest.raises(native.GafimeError) as e:
+            b.topk(["multiply"], 3)
+        assert e.value.code == -1
+        # the legacy single-pair path skips NaN rows like cpu_backend.cpp:274
+        st = b.compute_pair(2, 3)
+        assert st[0] == 99
+
+
+def test_legacy_fold_split_and_unary_ops(native, golden):
+    g = golden("edge.npz")
+    X, y = g["X_nan"], g["y"]
+    with bucket_for(native, X, y) as b:
+        for op in range(4):
+            st = b.compute_pair(0, 2, 0, 0, op, 255)
+            np.testing.assert_allclose(st, g["ref_stats_nan"][op][1], rtol=2e-7)  # pair (0, 2)
+    rng = np.random.default_rng(2)
+    X = rng.standard_normal((3000, 3)).astype(np.float32)
+    y = rng.standard_normal(3000).astype(np.float32)
+    mask = (np.arange(3000) % 5).astype(np.uint8)
+    with native.Bucket(3000, 3) as b:
+        b.upload(X, y, mask)
+        st = b.compute_pair(0, 1, 1, 6, 0, 2)   # log(|a|) * a^2, fold 2 held out
+    la = np.log(np.abs(X[:, 0]) + np.float32(1e-8)).astype(np.float32)
+    x = (la * (X[:, 1] * X[:, 1])).astype(np.float32).astype(np.float64)
+    val = mask == 2
+    for h, sel in ((0, ~val), (1, val)):
+        yy = y[sel].astype(np.float64)
+        xx = x[sel]
+        want = [sel.sum(), xx.sum(), yy.sum(), (xx * xx).sum(), (yy * yy).sum(), (xx * yy).sum()]
+        np.testing.assert_allclose(st[6 * h:6 * h + 6], want, rtol=1e-5, atol=1e-3)
+
+
+@pytest.fixture(scope="module")
+def config2():
+    from bench import make_config2
+    return make_config2()
+
+
+@pytest.mark.parametrize("op", OPS)
+def test_config2_full_size_properties(native, oracle, config2, op):
+    """Config 2 at full size (1e6 x 256, 128 normal + 128 lognormal): the k best pairs
+    and a random sample of others match the oracle pair by pair, and no sampled pair
+    outside the top-k beats the k-th score."""
+    X, y = config2
+    k = 100
+    with bucket_for(native, X, y) as b:
+        top = b.topk([op], k, div_eps=1e-6)[op]
+        allsc = b.scores(op, div_eps=1e-6)
+    gi, gj, gs = top
+    want = oracle.raw_pearson(X, y, op, gi.astype(np.int32), gj.astype(np.int32), div_eps=1e-6)
+    assert_pearson_close(gs, want)
+    rng = np.random.default_rng(0)
+    pi, pj = np.triu_indices(256, k=1)
+    sample = rng.choice(len(pi), 200, replace=False)
+    ws = oracle.raw_pearson(X, y, op, pi[sample].astype(np.int32), pj[sample].astype(np.int32),
+                            div_eps=1e-6)
+    assert_pearson_close(allsc[sample], ws)
+    kth = np.abs(gs[-1])
+    topset = {(int(a), int(c)) for a, c in zip(gi, gj)}
+    for p, w in zip(sample, ws):
+        if (int(pi[p]), int(pj[p])) not in topset:
+            assert abs(w) <= kth * (1 + 1e-4) + 1e-6
+    if op == "multiply":
+        assert (int(gi[0]), int(gj[0])) == (3, 17)
