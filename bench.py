@@ -159,7 +159,10 @@ def measured_peaks():
 
 # Per-launch DRAM traffic of the dominant kernel from one ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum); see profiles/ for the command.
-NCU_TRAFFIC_BYTES = {}
+NCU_TRAFFIC_BYTES = {
+    # profiles/pair_moments_config2.md: mul-group launch, 1.0298 GB read + 5.09 MB written
+    ("config2", "pair_moments"): 1.0349e9,
+}
 
 
 class ClockSampler:

@@ -62,7 +62,7 @@ using namespace gafime;
 
 extern "C" int gafime_profile_enable(int enable) {
     std::lock_guard<std::mutex> lk(g_mu);
-    clear_locked();
+    if (enable) clear_locked();  // a new profiling window starts empty; stopping keeps the records
     g_enabled.store(enable ? 1 : 0);
     return GAFIME_SUCCESS;
 }

@@ -184,8 +184,9 @@ int gafime_topk_merge(const int32_t* cand_i, const int32_t* cand_j, const double
 #define GAFIME_KERNEL_FINITE_CHECK 9
 #define GAFIME_KERNEL_GRAM_TC 10
 
-/* NEW.  enable = 1: from now on bracket every engine kernel launch with CUDA
- * events on its stream; any previous records are dropped.  enable = 0: stop. */
+/* NEW.  enable = 1: drop any previous records, then bracket every engine kernel
+ * launch with CUDA events on its stream.  enable = 0: stop recording (the records
+ * stay readable until the next enable = 1). */
 int gafime_profile_enable(int enable);
 
 /* NEW.  Total device milliseconds and number of launches recorded for one kernel
