@@ -40,7 +40,7 @@ EXPORTED = (
     "gafime_contiguous_bucket_compute", "gafime_contiguous_bucket_free",
     "gafime_contiguous_bucket_info", "gafime_allpairs_topk", "gafime_allpairs_scores",
     "gafime_topk_merge", "gafime_profile_enable", "gafime_profile_read",
-    "gafime_contiguous_bucket_stream",
+    "gafime_contiguous_bucket_stream", "gafime_allpairs_scores_noalloc",
 )
 
 # kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
@@ -82,6 +82,7 @@ def _bind(lib: ctypes.CDLL) -> None:
         "gafime_profile_enable": ([_i], _i),
         "gafime_profile_read": ([_i, ctypes.POINTER(ctypes.c_double), _ip], _i),
         "gafime_contiguous_bucket_stream": ([_vp, ctypes.POINTER(_vp)], _i),
+        "gafime_allpairs_scores_noalloc": ([_vp, _i64, _vp, _i, _i, _i, _f, _vp, _vp], _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

@@ -72,6 +72,18 @@ int compute_column_stats(Bucket& b, bool centred, ColumnStats& out);
 // Finite-input check over the first f columns + y; returns 1 if all finite.
 int check_finite(Bucket& b, bool* all_finite);
 
+// Column-statistics kernels of bucket.cu, declared for other translation units.
+__global__ void col_partial_kernel(const float* __restrict__ x, int64_t ld, int64_t n,
+                                   const float* __restrict__ ycen, int64_t span,
+                                   double* __restrict__ part);
+__global__ void col_combine_kernel(const double* __restrict__ part, int cols, int splits,
+                                   int64_t n, double* __restrict__ colstats);
+__global__ void ystats_kernel(const double* __restrict__ ycol, int64_t n, double* __restrict__ ystats);
+__global__ void ycen_kernel(const float* __restrict__ y, int64_t n, int64_t ld,
+                            const double* __restrict__ ystats, float* __restrict__ ycen);
+__global__ void finite_kernel(const float* __restrict__ x, int64_t cols, int64_t ld, int64_t n,
+                              int* __restrict__ flag);
+
 // CUDA-core three-moment pair kernel (moments.cu).  For every pair (i, j) of the
 // listed tiles: S1 = sum a*g(b), S2 = sum (a*g(b))^2, S3 = sum a*g(b)*ycen with
 // a = X[:, i], b = X[:, j], g = identity (recip = false) or 1/safe(b).

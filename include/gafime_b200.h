@@ -197,6 +197,48 @@ int gafime_profile_read(int kernel_id, double* total_ms, int* launches);
  * caller can order its own work or events against it. */
 int gafime_contiguous_bucket_stream(ContiguousBucket bucket, void** stream_out);
 
+/* ------------------------------------------- NEW: no device allocation ---- */
+
+/* Largest problem gafime_allpairs_scores_noalloc accepts. */
+#define GAFIME_NOALLOC_MAX_FEATURES 256
+#define GAFIME_NOALLOC_MAX_ROWS 2097152
+
+/*
+ * NEW -- no counterpart in the reference.  Signed Pearson score of every pair i<j
+ * (row-major upper-triangle order, as gafime_allpairs_scores, raw kernel-API
+ * semantics) for a matrix that is already on the GPU, without allocating any GPU
+ * memory: no cudaMalloc, no cudaFree, no allocating library call.
+ *
+ * For programs that own the GPU's memory themselves -- an arena or caching allocator
+ * that has reserved most of the device, or a host application that hands out device
+ * buffers it carved out of its own pool -- where a library that calls cudaMalloc can
+ * fail for lack of room, fragment the owner's pool, or stall other streams with the
+ * device-wide synchronisation cudaMalloc/cudaFree may imply.
+ *
+ *   d_x           device, column-major: column f at d_x + f*ld, 16-byte aligned;
+ *                 rows n_samples..ld-1 of every column must be zero.
+ *   ld            multiple of 256, n_samples <= ld <= GAFIME_NOALLOC_MAX_ROWS.
+ *   d_y           device, n_samples floats.
+ *   n_features    1..GAFIME_NOALLOC_MAX_FEATURES.
+ *   interact_type GAFIME_INTERACT_MULT/ADD/SUB/DIV;  div_eps as gafime_allpairs_topk.
+ *   d_scores_out  device, F*(F-1)/2 doubles, written on success.
+ *   stream        cudaStream_t to run on (NULL: the default stream); the call waits
+ *                 for it before returning.
+ *
+ * Sizes beyond the limits, a misaligned d_x or an ld that is not a multiple of 256
+ * return GAFIME_ERROR_INVALID_ARGS before any GPU work; non-finite input returns
+ * GAFIME_ERROR_INVALID_ARGS as gafime_allpairs_scores does.
+ *
+ * All intermediates live in one fixed 32 MiB __device__ array that every GPU loading
+ * the library holds until the process exits.  Every call reuses that array, so calls
+ * that overlap on the GPU (other streams or threads) race and must be serialised.
+ * The first call on each device looks the array's address up with
+ * cudaGetSymbolAddress; make it before any stream capture starts.
+ */
+int gafime_allpairs_scores_noalloc(const float* d_x, int64_t ld, const float* d_y, int n_samples,
+                                   int n_features, int interact_type, float div_eps,
+                                   double* d_scores_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
