@@ -12,8 +12,9 @@ HBM when the timed region starts (``value``); ``e2e`` repeats the step through
 the C ABI from pinned host buffers (upload inside the timed region).
 
 Multi-GPU: launched with torchrun, one process per GPU; each rank holds the full
-column-major matrix and scores its share of the pair tiles (strong scaling of a
-fixed job).  Rank 0 prints one JSON line.
+column-major matrix and scores its share of the pair tiles.  config2 scales weakly
+(F = 256 sqrt(N), ~32.7k pairs per GPU); config4/config5 are fixed jobs split across
+the GPUs (strong scaling).  Rank 0 prints one JSON line.
 """
 from __future__ import annotations
 
@@ -107,6 +108,27 @@ def fill_config5(packed: np.ndarray, n: int):
     return idx
 
 
+def fill_config2_scaled(packed: np.ndarray, n: int):
+    """Config 2's distributions at any width F >= 256, written column by column (one
+    seeded generator per column, so every rank builds the same matrix quickly): first half
+    N(0,1), second half lognormal(0,1); y ~ Bernoulli(sigmoid(2 x3 x17 - 1.5 x40 / (|x91| + 1)
+    + N(0,1))).  Used for weak scaling: at N GPUs F = 256 sqrt(N) keeps about 32.7k pairs
+    per GPU."""
+    f = packed.shape[0] - 1
+    for c in range(f):
+        r = np.random.default_rng(10_000 + c)
+        packed[c] = r.standard_normal(n, dtype=np.float32) if c < f // 2 else \
+            np.exp(r.standard_normal(n, dtype=np.float32))
+    r = np.random.default_rng(99)
+    x = {c: packed[c].astype(np.float64) for c in (3, 17, 40, 91)}
+    logit = 2.0 * x[3] * x[17] - 1.5 * x[40] / (np.abs(x[91]) + 1.0) + r.standard_normal(n)
+    packed[f] = (r.random(n) < 1.0 / (1.0 + np.exp(-logit))).astype(np.float32)
+
+
+def scaled_width(world: int) -> int:
+    return int(round(256 * world ** 0.5))
+
+
 WORKLOADS = {
     "config1": dict(n=1000, f=50, ops=["multiply"], metric="pearson", center=True, k=5, eps=1e-8,
                     bins=16, desc="1,000 x 50 N(0,1), Bernoulli(0.5), centred multiply, |Pearson|, k=5"),
@@ -129,7 +151,9 @@ WORKLOADS = {
 def build_packed(name: str, packed: np.ndarray):
     w = WORKLOADS[name]
     n, f = w["n"], w["f"]
-    if name in ("config1", "config2", "config3"):
+    if name == "config2" and packed.shape[0] - 1 != f:
+        fill_config2_scaled(packed, n)
+    elif name in ("config1", "config2", "config3"):
         X, y = {"config1": make_config1, "config2": make_config2, "config3": make_config3}[name]()
         packed[:f] = X.T
         packed[f] = y
@@ -246,7 +270,7 @@ class CpuArm:
         self.name = name
         self.w = WORKLOADS[name]
         self.packed = packed
-        n, f = self.w["n"], self.w["f"]
+        n, f = self.w["n"], packed.shape[0] - 1
         self.n, self.f = n, f
         self.pi, self.pj = np.triu_indices(f, k=1)
         self.rng = np.random.default_rng(1234)
@@ -356,7 +380,8 @@ def run_reference(args):
     if rank != 0:
         return 0
     w = WORKLOADS[args.workload]
-    packed = np.empty((w["f"] + 1, w["n"]), dtype=np.float32)
+    f = scaled_width(world) if (args.workload == "config2" and world > 1) else w["f"]
+    packed = np.empty((f + 1, w["n"]), dtype=np.float32)
     build_packed(args.workload, packed)
     arm = CpuArm(args.workload, packed)
     # size one step to ~0.6 s so the whole --steps K --warmup W run ends in minutes
@@ -372,9 +397,11 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": METRIC_NAME, "value": value, "unit": "evals/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True, "scaling": "strong",
+        "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
+        "scaling": "weak" if args.workload == "config2" else "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: {w['desc']}"},
+        "config": {"workload": f"{args.workload}: {w['desc']}" + (
+            f" weak-scaled to F = {f} columns" if f != w["f"] else ""), "features": f},
         "cpu_baseline": {"value": value, "unit": "evals/s", "cores": arm.cores, "kind": arm.kind,
                          "sample": arm.describe(units, dt / max(1, args.steps)) + " per step"},
         "e2e": {"value": value, "unit": "evals/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -396,6 +423,12 @@ def run_ours(args):
                                 device_id=torch.device("cuda", local))
     w = WORKLOADS[args.workload]
     n, f, ops, k = w["n"], w["f"], w["ops"], w["k"]
+    # config2 scales weakly: F grows as 256 sqrt(N) so each GPU keeps ~32.7k pairs;
+    # the other workloads are fixed jobs split across the GPUs (strong scaling).
+    weak = args.workload == "config2" and world > 1
+    if weak:
+        f = scaled_width(world)
+    scaling = "weak" if args.workload == "config2" else "strong"
 
     packed_t = torch.empty((f + 1, n), dtype=torch.float32, pin_memory=True)
     packed = packed_t.numpy()
@@ -518,8 +551,11 @@ def run_ours(args):
     line = {
         "metric": METRIC_NAME, "value": value, "unit": "evals/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.workload}: {w['desc']}", "pairs": pairs, "rows": n,
+        "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": (f"{args.workload}: {w['desc']}" if not weak else
+                                f"{args.workload} weak-scaled to F = 256 sqrt({world}) = {f} columns "
+                                f"({pairs} pairs, ~{pairs // world} per GPU), same distributions"),
+                   "features": f, "pairs": pairs, "rows": n,
                    "operators": ops, "k": k, "parallelism": f"pair-tile shards x{world}",
                    "accumulation": "fp32 products, fp64 sums",
                    "l2": f"inputs larger than L2 ({packed.nbytes / 1e9:.2f} GB resident)"},

@@ -40,7 +40,8 @@ EXPORTED = (
     "gafime_contiguous_bucket_compute", "gafime_contiguous_bucket_free",
     "gafime_contiguous_bucket_info", "gafime_allpairs_topk", "gafime_allpairs_scores",
     "gafime_topk_merge", "gafime_profile_enable", "gafime_profile_read",
-    "gafime_contiguous_bucket_stream", "gafime_allpairs_scores_noalloc",
+    "gafime_contiguous_bucket_stream", "gafime_allpairs_scores_noalloc", "gafime_unary_scores",
+    "gafime_shard_tiles",
 )
 
 # kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
@@ -83,6 +84,8 @@ def _bind(lib: ctypes.CDLL) -> None:
         "gafime_profile_read": ([_i, ctypes.POINTER(ctypes.c_double), _ip], _i),
         "gafime_contiguous_bucket_stream": ([_vp, ctypes.POINTER(_vp)], _i),
         "gafime_allpairs_scores_noalloc": ([_vp, _i64, _vp, _i, _i, _i, _f, _vp, _vp], _i),
+        "gafime_unary_scores": ([_vp, _i, _i, _vp], _i),
+        "gafime_shard_tiles": ([_i, _i, _i, _vp, _i, _ip], _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -209,6 +212,13 @@ class Bucket:
                 int(mi_bins), _ptr(out)))
         return out
 
+    def unary_scores(self, metric: str = "pearson", mi_bins: int = 16) -> np.ndarray:
+        """Score of every single raw column against the target (F entries)."""
+        out = np.empty(self.f, dtype=np.float64)
+        check("gafime_unary_scores", self.lib.gafime_unary_scores(
+            self.handle, METRIC[metric], int(mi_bins), _ptr(out)))
+        return out
+
     def stream_ptr(self) -> int:
         """cudaStream_t of this bucket (every call on it runs on this stream)."""
         s = ctypes.c_void_p(0)
@@ -263,3 +273,33 @@ def profile_read(kernel: str = "all") -> Tuple[float, int]:
     n = ctypes.c_int(0)
     check("gafime_profile_read", load().gafime_profile_read(kid, ctypes.byref(ms), ctypes.byref(n)))
     return ms.value, n.value
+
+
+TILE = 64
+
+
+def shard_tiles(n_features: int, shard_id: int, n_shards: int) -> np.ndarray:
+    """(bi, bj) pair tiles this shard scores (gafime_shard_tiles; host only)."""
+    lib = load(require_gpu=False)
+    nb = (n_features + TILE - 1) // TILE
+    cap = max(1, nb * (nb + 1) // 2)
+    out = np.zeros(2 * cap, dtype=np.int32)
+    cnt = ctypes.c_int(0)
+    check("gafime_shard_tiles", lib.gafime_shard_tiles(
+        int(n_features), int(shard_id), int(n_shards), _ptr(out), cap, ctypes.byref(cnt)))
+    return out[: 2 * cnt.value].reshape(-1, 2)
+
+
+def shard_pairs(n_features: int, shard_id: int, n_shards: int) -> Tuple[np.ndarray, np.ndarray]:
+    """All pairs (i, j), i < j, inside this shard's tiles."""
+    pi, pj = [], []
+    for bi, bj in shard_tiles(n_features, shard_id, n_shards):
+        ii = np.arange(bi * TILE, min((bi + 1) * TILE, n_features))
+        jj = np.arange(bj * TILE, min((bj + 1) * TILE, n_features))
+        I, J = np.meshgrid(ii, jj, indexing="ij")
+        keep = I < J
+        pi.append(I[keep])
+        pj.append(J[keep])
+    if not pi:
+        return np.zeros(0, np.int32), np.zeros(0, np.int32)
+    return np.concatenate(pi).astype(np.int32), np.concatenate(pj).astype(np.int32)

@@ -36,6 +36,8 @@ int64_t tile_pairs(int bi, int bj, int64_t f) {
     return ni * (ni - 1) / 2;
 }
 
+}  // namespace
+
 // Upper-triangle tiles of this shard.  Tiles are taken in row-major order and each
 // goes to the shard with the fewest pairs so far (ties: lowest shard id), so every
 // process derives the same assignment without communication.
@@ -55,6 +57,8 @@ std::vector<TileCoord> shard_tiles(int64_t f, int shard_id, int n_shards) {
         }
     return mine;
 }
+
+namespace {
 
 struct Plan {
     std::vector<TileCoord> tiles;
@@ -171,7 +175,7 @@ extern "C" int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact
         !out_count)
         return GAFIME_ERROR_INVALID_ARGS;
     if (metric != GAFIME_METRIC_PEARSON && metric != GAFIME_METRIC_MUTUAL_INFO) return GAFIME_ERROR_INVALID_ARGS;
-    if (metric == GAFIME_METRIC_MUTUAL_INFO && (mi_bins < 2 || mi_bins > 256)) return GAFIME_ERROR_INVALID_ARGS;
+    if (metric == GAFIME_METRIC_MUTUAL_INFO && (mi_bins < 2 || mi_bins > 255)) return GAFIME_ERROR_INVALID_ARGS;
     if (!(div_eps > 0.0f)) return GAFIME_ERROR_INVALID_ARGS;
     for (int o = 0; o < n_ops; ++o)
         if (!valid_op(interact_types[o])) return GAFIME_ERROR_INVALID_ARGS;
@@ -243,7 +247,7 @@ extern "C" int gafime_allpairs_scores(ContiguousBucket bucket, int interact_type
                                       int center, float div_eps, int mi_bins, double* out_scores) {
     if (!bucket || !out_scores || !valid_op(interact_type)) return GAFIME_ERROR_INVALID_ARGS;
     if (metric != GAFIME_METRIC_PEARSON && metric != GAFIME_METRIC_MUTUAL_INFO) return GAFIME_ERROR_INVALID_ARGS;
-    if (metric == GAFIME_METRIC_MUTUAL_INFO && (mi_bins < 2 || mi_bins > 256)) return GAFIME_ERROR_INVALID_ARGS;
+    if (metric == GAFIME_METRIC_MUTUAL_INFO && (mi_bins < 2 || mi_bins > 255)) return GAFIME_ERROR_INVALID_ARGS;
     if (!(div_eps > 0.0f)) return GAFIME_ERROR_INVALID_ARGS;
     Bucket& b = *(Bucket*)bucket;
     if (b.f >= 65536) return GAFIME_ERROR_INVALID_ARGS;
@@ -267,4 +271,67 @@ extern "C" int gafime_allpairs_scores(ContiguousBucket bucket, int interact_type
                         b.stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b.stream);
     return status_from(e);
+}
+
+namespace gafime {
+namespace {
+
+// gafime_core pearson_from_sums (gafime_core.cpp:179-198) on raw-column sums:
+// r = sum x*ycen / sqrt(var_x * var_y), var_x = sum x^2 - (sum x)^2 / n.
+__global__ void unary_pearson_kernel(const double* __restrict__ colstats,
+                                     const double* __restrict__ ystats, int64_t f,
+                                     double* __restrict__ out) {
+    int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= f) return;
+    double n = ystats[0], var_y = ystats[2];
+    double sx = colstats[c * 4], sxx = colstats[c * 4 + 1], dot = colstats[c * 4 + 2];
+    double r = 0.0;
+    if (n > 0.0) {
+        double var_x = sxx - sx * (sx / n);
+        if (var_x > 0.0 && var_y > 0.0) r = dot / sqrt(var_x * var_y);
+    }
+    out[c] = r;
+}
+
+}  // namespace
+}  // namespace gafime
+
+extern "C" int gafime_unary_scores(ContiguousBucket bucket, int metric, int mi_bins,
+                                   double* out_scores) {
+    if (!bucket || !out_scores) return GAFIME_ERROR_INVALID_ARGS;
+    if (metric != GAFIME_METRIC_PEARSON && metric != GAFIME_METRIC_MUTUAL_INFO) return GAFIME_ERROR_INVALID_ARGS;
+    if (metric == GAFIME_METRIC_MUTUAL_INFO && (mi_bins < 2 || mi_bins > 255)) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket& b = *(Bucket*)bucket;
+    cudaSetDevice(b.device);
+    ColumnStats cs;
+    int st = prepare(b, 0, GAFIME_METRIC_PEARSON, cs);
+    if (st != GAFIME_SUCCESS) return st;
+    cudaError_t e = ensure(b.scores, (size_t)std::max<int64_t>(b.f, 1) * sizeof(double));
+    if (e != cudaSuccess) return status_from(e);
+    double* d_out = (double*)b.scores.ptr;
+    if (metric == GAFIME_METRIC_PEARSON) {
+        unary_pearson_kernel<<<(unsigned)((b.f + 127) / 128), 128, 0, b.stream>>>(cs.d_col, cs.d_y, b.f, d_out);
+        e = cudaGetLastError();
+    } else {
+        e = launch_mi_unary(b, mi_bins, d_out, b.stream);
+    }
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(out_scores, d_out, (size_t)b.f * sizeof(double), cudaMemcpyDeviceToHost, b.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b.stream);
+    return status_from(e);
+}
+
+extern "C" int gafime_shard_tiles(int n_features, int shard_id, int n_shards, int32_t* out_tiles,
+                                  int max_tiles, int* out_count) {
+    if (n_features < 0 || n_shards < 1 || shard_id < 0 || shard_id >= n_shards || !out_count ||
+        max_tiles < 0 || (max_tiles > 0 && !out_tiles))
+        return GAFIME_ERROR_INVALID_ARGS;
+    std::vector<TileCoord> t = gafime::shard_tiles(n_features, shard_id, n_shards);
+    *out_count = (int)t.size();
+    if ((int)t.size() > max_tiles) return GAFIME_ERROR_INVALID_ARGS;
+    for (size_t q = 0; q < t.size(); ++q) {
+        out_tiles[2 * q] = t[q].bi;
+        out_tiles[2 * q + 1] = t[q].bj;
+    }
+    return GAFIME_SUCCESS;
 }

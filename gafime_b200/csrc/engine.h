@@ -50,7 +50,7 @@ struct Bucket {
     int sm_count = 148;
     // scratch
     DeviceBuf stats_part, stats, ycen, xcen, moments, cands, cands2, scores, flags, tiles, mi,
-        mi_hist;
+        mi_hist, mi_mm;
 };
 
 // Grow a scratch buffer to at least `bytes`; returns cudaSuccess or an error.
@@ -119,6 +119,14 @@ cudaError_t merge_candidates(Cand* buf, Cand* tmp, int n_lists, int k_pad, int n
 cudaError_t launch_mi_scores(Bucket& b, const ColumnStats& cs, bool centred, int op, float div_eps,
                              int mi_bins, const TileCoord* d_tiles, int n_tiles, int k_pad,
                              Cand* cands, double* all_scores, cudaStream_t stream);
+
+// Unary (single-feature) mutual information of every raw column against y
+// (gafime_core.cpp:559-569 with k == 1: the raw column, no centring).
+cudaError_t launch_mi_unary(Bucket& b, int mi_bins, double* d_out, cudaStream_t stream);
+
+// Upper-triangle 64 x 64 pair tiles assigned to one shard (allpairs.cu): tiles in
+// row-major order, each to the least-loaded shard by pair count, ties to the lowest id.
+std::vector<TileCoord> shard_tiles(int64_t f, int shard_id, int n_shards);
 
 // Ranking used everywhere: |score| descending, NaN after every number, empty
 // slots last; ties by pair id ascending.

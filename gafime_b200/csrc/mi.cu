@@ -325,52 +325,67 @@ cudaError_t run_passes(const MiArgs& a, int splits, cudaStream_t stream) {
 
 }  // namespace
 
-cudaError_t launch_mi_scores(Bucket& b, const ColumnStats& cs, bool centred, int op, float div_eps,
-                             int mi_bins, const TileCoord* d_tiles, int n_tiles, int k_pad,
-                             Cand* cands, double* all_scores, cudaStream_t stream) {
-    const int bins = mi_bins;
-    // scratch layout in b.mi: ymm[2] | counts[256] | map[256] | meta[2] | ycode[ld] | mm
+// y bins of the target: equal-width bins (gafime_core.cpp:200-226) remapped to the
+// U bins that occur.  One small host sync learns U.
+struct YBins {
+    long long* ymm;     // [2] order-preserving keys of min / max y
+    unsigned* counts;   // [256] rows per y bin (p_y of the reference)
+    int* map;           // [256] compact code per bin, 255 when unused
+    uint8_t* ycode;     // [n] compact code per row
+    int U = 1, ready = 0;
+};
+
+cudaError_t prepare_ybins(Bucket& b, int bins, YBins& yb, cudaStream_t stream) {
     size_t off_ymm = 0, off_counts = 64, off_map = off_counts + 256 * 4, off_meta = off_map + 256 * 4;
     size_t off_ycode = (off_meta + 64 + 255) / 256 * 256;
-    size_t off_mm = off_ycode + ((size_t)b.ld + 255) / 256 * 256;
-    size_t mm_bytes = (size_t)n_tiles * kTilePairs * 2 * sizeof(long long);
-    size_t mi_bytes = off_mm + (mm_bytes + 255) / 256 * 256;
-    cudaError_t e = ensure(b.mi, mi_bytes);
+    size_t bytes = off_ycode + ((size_t)b.ld + 255) / 256 * 256;
+    cudaError_t e = ensure(b.mi, bytes);
     if (e != cudaSuccess) return e;
     char* base = (char*)b.mi.ptr;
-    long long* ymm = (long long*)(base + off_ymm);
-    unsigned* counts = (unsigned*)(base + off_counts);
-    int* map = (int*)(base + off_map);
+    yb.ymm = (long long*)(base + off_ymm);
+    yb.counts = (unsigned*)(base + off_counts);
+    yb.map = (int*)(base + off_map);
     int* meta = (int*)(base + off_meta);
+    yb.ycode = (uint8_t*)(base + off_ycode);
     const float* y = b.d_data + b.f * b.ld;
-
-    // y bins and the compact code map (one small host sync to learn U)
     long long init[2] = {0x7FFFFFFFFFFFFFFFLL, (long long)0x8000000000000000ULL};
-    e = cudaMemcpyAsync(ymm, init, sizeof(init), cudaMemcpyHostToDevice, stream);
-    if (e == cudaSuccess) e = cudaMemsetAsync(counts, 0, 256 * 4, stream);
+    e = cudaMemcpyAsync(yb.ymm, init, sizeof(init), cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(yb.counts, 0, 256 * 4, stream);
     if (e != cudaSuccess) return e;
-    ymm_kernel<<<2 * b.sm_count, 256, 0, stream>>>(y, b.n, ymm);
-    ycount_kernel<<<2 * b.sm_count, 256, 0, stream>>>(y, b.n, ymm, bins, counts);
-    ymap_kernel<<<1, 1, 0, stream>>>(counts, ymm, bins, map, meta);
+    ymm_kernel<<<2 * b.sm_count, 256, 0, stream>>>(y, b.n, yb.ymm);
+    ycount_kernel<<<2 * b.sm_count, 256, 0, stream>>>(y, b.n, yb.ymm, bins, yb.counts);
+    ymap_kernel<<<1, 1, 0, stream>>>(yb.counts, yb.ymm, bins, yb.map, meta);
     int hmeta[2] = {0, 0};
     e = cudaMemcpyAsync(hmeta, meta, sizeof(hmeta), cudaMemcpyDeviceToHost, stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
     if (e != cudaSuccess) return e;
-    const int U = std::max(1, hmeta[0]);
-    const int ready = hmeta[1];
-    if (bins * U > 768) return cudaErrorInvalidValue;  // joint histogram too large for shared memory
+    yb.U = std::max(1, hmeta[0]);
+    yb.ready = hmeta[1];
+    if (yb.ready) ycode_kernel<<<2 * b.sm_count, 256, 0, stream>>>(y, b.n, yb.ymm, bins, yb.map, yb.ycode);
+    return cudaGetLastError();
+}
 
-    // the joint histograms live in their own buffer: growing it must not move the
-    // y-bin map written above
-    size_t hist_bytes = (size_t)n_tiles * kTilePairs * bins * U * sizeof(unsigned);
-    e = ensure(b.mi_hist, hist_bytes);
+cudaError_t launch_mi_scores(Bucket& b, const ColumnStats& cs, bool centred, int op, float div_eps,
+                             int mi_bins, const TileCoord* d_tiles, int n_tiles, int k_pad,
+                             Cand* cands, double* all_scores, cudaStream_t stream) {
+    const int bins = mi_bins;
+    YBins yb;
+    cudaError_t e = prepare_ybins(b, bins, yb, stream);
     if (e != cudaSuccess) return e;
-    uint8_t* ycode = (uint8_t*)(base + off_ycode);
-    long long* mm = (long long*)(base + off_mm);
+    const int U = yb.U, ready = yb.ready;
+    if (bins * U > 768) return cudaErrorInvalidValue;  // joint histogram too large for shared memory
+    // per-pair min/max keys and the joint histograms live in their own buffers
+    size_t mm_bytes = (size_t)n_tiles * kTilePairs * 2 * sizeof(long long);
+    size_t hist_bytes = (size_t)n_tiles * kTilePairs * bins * U * sizeof(unsigned);
+    e = ensure(b.mi_mm, mm_bytes);
+    if (e == cudaSuccess) e = ensure(b.mi_hist, hist_bytes);
+    if (e != cudaSuccess) return e;
+    long long* mm = (long long*)b.mi_mm.ptr;
     unsigned* hist = (unsigned*)b.mi_hist.ptr;
-
+    unsigned* counts = yb.counts;
+    int* map = yb.map;
+    uint8_t* ycode = yb.ycode;
     const double* means = cs.d_col;
-    if (ready) ycode_kernel<<<2 * b.sm_count, 256, 0, stream>>>(y, b.n, ymm, bins, map, ycode);
     mm_init_kernel<<<2 * b.sm_count, 256, 0, stream>>>(mm, (int64_t)n_tiles * kTilePairs);
     e = cudaMemsetAsync(hist, 0, hist_bytes, stream);
     if (e != cudaSuccess) return e;
@@ -431,6 +446,119 @@ cudaError_t launch_mi_scores(Bucket& b, const ColumnStats& cs, bool centred, int
     cudaFuncSetAttribute(mi_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     KernelTimer timer(stream, GAFIME_KERNEL_MI_FINISH);
     mi_finish_kernel<<<n_tiles, 256, smem, stream>>>(fa);
+    return cudaGetLastError();
+}
+
+// ---- unary mutual information (one raw column against y) -------------------
+
+namespace {
+
+__global__ void __launch_bounds__(256) unary_mm_kernel(const float* __restrict__ x, int64_t ld,
+                                                       int64_t n, int64_t rps, long long* mm) {
+    __shared__ double smn[256], smx[256];
+    const int c = blockIdx.x;
+    const int64_t r0 = (int64_t)blockIdx.y * rps, r1 = std::min<int64_t>(r0 + rps, n);
+    double mn = INFINITY, mx = -INFINITY;
+    for (int64_t r = r0 + threadIdx.x; r < r1; r += 256) {
+        double v = x[(int64_t)c * ld + r];
+        mn = v < mn ? v : mn;
+        mx = v > mx ? v : mx;
+    }
+    smn[threadIdx.x] = mn;
+    smx[threadIdx.x] = mx;
+    __syncthreads();
+    for (int s = 128; s > 0; s >>= 1) {
+        if (threadIdx.x < s) {
+            smn[threadIdx.x] = fmin(smn[threadIdx.x], smn[threadIdx.x + s]);
+            smx[threadIdx.x] = fmax(smx[threadIdx.x], smx[threadIdx.x + s]);
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0 && r1 > r0) {
+        atomicMin(&mm[2 * c], dkey(smn[0]));
+        atomicMax(&mm[2 * c + 1], dkey(smx[0]));
+    }
+}
+
+__global__ void __launch_bounds__(256) unary_hist_kernel(const float* __restrict__ x, int64_t ld,
+                                                         int64_t n, int64_t rps, const long long* mm,
+                                                         const uint8_t* ycode, int bins, int U,
+                                                         unsigned* hist) {
+    extern __shared__ unsigned h[];  // [bins * U]
+    const int c = blockIdx.x;
+    for (int q = threadIdx.x; q < bins * U; q += 256) h[q] = 0;
+    __syncthreads();
+    const double xmin = dval(mm[2 * c]), xmax = dval(mm[2 * c + 1]);
+    if (xmax != xmin) {
+        const double scale = (double)bins / (xmax - xmin);
+        const int64_t r0 = (int64_t)blockIdx.y * rps, r1 = std::min<int64_t>(r0 + rps, n);
+        for (int64_t r = r0 + threadIdx.x; r < r1; r += 256) {
+            int xb = (int)(((double)x[(int64_t)c * ld + r] - xmin) * scale);
+            xb = xb < 0 ? 0 : (xb >= bins ? bins - 1 : xb);
+            atomicAdd(&h[xb * U + ycode[r]], 1u);
+        }
+    }
+    __syncthreads();
+    for (int q = threadIdx.x; q < bins * U; q += 256)
+        if (h[q]) atomicAdd(&hist[(int64_t)c * bins * U + q], h[q]);
+}
+
+__global__ void unary_finish_kernel(int64_t f, int64_t n, const long long* mm, const unsigned* hist,
+                                    const unsigned* ycounts, const int* map, int bins, int U,
+                                    int ready, double* out) {
+    const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= f) return;
+    double py[256];
+    for (int b = 0; b < bins; ++b)
+        if (map[b] != 255) py[map[b]] = (double)ycounts[b];
+    const double inv_total = 1.0 / (double)n, inv_total_sq = inv_total * inv_total;
+    double mi = 0.0;
+    if (ready && mm[2 * c] != mm[2 * c + 1]) {
+        const unsigned* hc = hist + c * bins * U;
+        for (int bx = 0; bx < bins; ++bx) {
+            double px = 0.0;
+            for (int u = 0; u < U; ++u) px += (double)hc[bx * U + u];
+            if (px == 0.0) continue;
+            for (int u = 0; u < U; ++u) {
+                double count = (double)hc[bx * U + u];
+                if (count <= 0.0) continue;
+                double p = count * inv_total;
+                double expected = (px * py[u]) * inv_total_sq;
+                if (expected > 0.0) mi += p * log(p / expected);
+            }
+        }
+    }
+    out[c] = mi;
+}
+
+}  // namespace
+
+cudaError_t launch_mi_unary(Bucket& b, int mi_bins, double* d_out, cudaStream_t stream) {
+    YBins yb;
+    cudaError_t e = prepare_ybins(b, mi_bins, yb, stream);
+    if (e != cudaSuccess) return e;
+    const int U = yb.U, bins = mi_bins;
+    e = ensure(b.mi_mm, (size_t)b.f * 2 * sizeof(long long));
+    if (e == cudaSuccess) e = ensure(b.mi_hist, (size_t)b.f * bins * U * sizeof(unsigned));
+    if (e != cudaSuccess) return e;
+    long long* mm = (long long*)b.mi_mm.ptr;
+    unsigned* hist = (unsigned*)b.mi_hist.ptr;
+    mm_init_kernel<<<(unsigned)((b.f + 255) / 256), 256, 0, stream>>>(mm, b.f);
+    e = cudaMemsetAsync(hist, 0, (size_t)b.f * bins * U * sizeof(unsigned), stream);
+    if (e != cudaSuccess) return e;
+    if (yb.ready) {
+        int splits = (int)std::max<int64_t>(1, std::min<int64_t>((4 * b.sm_count + b.f - 1) / b.f,
+                                                                 (b.n + 16383) / 16384));
+        int64_t rps = (b.n + splits - 1) / splits;
+        dim3 grid((unsigned)b.f, (unsigned)splits);
+        unary_mm_kernel<<<grid, 256, 0, stream>>>(b.d_data, b.ld, b.n, rps, mm);
+        size_t smem = (size_t)bins * U * sizeof(unsigned);
+        cudaFuncSetAttribute(unary_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        unary_hist_kernel<<<grid, 256, smem, stream>>>(b.d_data, b.ld, b.n, rps, mm, yb.ycode, bins, U,
+                                                       hist);
+    }
+    unary_finish_kernel<<<(unsigned)((b.f + 127) / 128), 128, 0, stream>>>(
+        b.f, b.n, mm, hist, yb.counts, yb.map, bins, U, yb.ready, d_out);
     return cudaGetLastError();
 }
 

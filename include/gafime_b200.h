@@ -135,7 +135,7 @@ int gafime_contiguous_bucket_info(ContiguousBucket bucket, int* n_samples_out,
  *                   1: columns centred by their fp64 means first (Selector / Engine /
  *                      gafime_core semantics, gafime_core.cpp:570-577).
  *   div_eps         safe-divide clamp |b| < eps -> copysign(eps, b) (reference 1e-8).
- *   mi_bins         equal-width bins on the interaction and on y (gafime_core.cpp:200-333).
+ *   mi_bins         2..255 equal-width bins on the interaction and on y (gafime_core.cpp:200-333).
  *   k               1..GAFIME_ALLPAIRS_MAX_K.
  *   shard_id/n_shards  pair-tile sharding across processes (0/1 = everything).
  *   out_i, out_j, out_score   [n_ops * k]: per operator, pairs ordered by |score|
@@ -159,6 +159,27 @@ int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact_types, int
  */
 int gafime_allpairs_scores(ContiguousBucket bucket, int interact_type, int metric, int center,
                            float div_eps, int mi_bins, double* out_scores);
+
+/*
+ * NEW.  Score of every single feature (unary combo) against the target, F entries:
+ * Pearson of the raw column (pearson_from_sums, gafime_core.cpp:179-198) or equal-width
+ * mutual information of the raw column (gafime_core.cpp:559-569 with k == 1).  Serves
+ * the engine's unary stage (gafime/engine.py:39-51), which picks the features whose
+ * pairs are scored next.
+ */
+int gafime_unary_scores(ContiguousBucket bucket, int metric, int mi_bins, double* out_scores);
+
+/*
+ * NEW.  Host only.  The 64 x 64 pair tiles (block row bi, block column bj, bi <= bj;
+ * pairs i in [64 bi, 64 bi + 64) x j in [64 bj, 64 bj + 64), i < j) that shard shard_id
+ * of n_shards scores in gafime_allpairs_topk: tiles are taken in row-major order and
+ * each goes to the shard with the fewest pairs so far (ties: lowest id), so every
+ * process derives the same split without communicating.  out_tiles receives
+ * 2 * *out_count ints (bi, bj); returns GAFIME_ERROR_INVALID_ARGS with *out_count set
+ * when max_tiles is too small.
+ */
+int gafime_shard_tiles(int n_features, int shard_id, int n_shards, int32_t* out_tiles,
+                       int max_tiles, int* out_count);
 
 /*
  * NEW.  Deterministic host merge of per-shard candidates (the step after the

@@ -181,6 +181,35 @@ def main():
     rawnan = np.stack([ref_raw_stats(cpu, Xnan, ye, op) for op in range(4)])
     np.savez_compressed(os.path.join(HERE, "edge.npz"), X=Xe, y=ye, core_scores=ce,
                         ref_stats=rawe, X_nan=Xnan, ref_stats_nan=rawnan)
+    # --- engine report and planning (GafimeEngine.analyze, backend='core', pearson) -----
+    from gafime.config import ComputeBudget, EngineConfig
+    from gafime.engine import GafimeEngine
+    from gafime.planning.combinations import plan_higher_order, plan_unary
+    rng = np.random.default_rng(3)
+    Xg = rng.standard_normal((600, 12)).astype(np.float32)
+    yg = ((Xg[:, 2] * Xg[:, 7] + 0.5 * rng.standard_normal(600)) > 0).astype(np.float32)
+    for backend in ("core", "python"):
+        cfg = EngineConfig(backend=backend, metric_names=("pearson",),
+                           budget=ComputeBudget(max_comb_size=2, top_features_for_higher_k=8),
+                           num_repeats=3, permutation_tests=10)
+        rep = GafimeEngine(cfg).analyze(Xg, yg)
+        combos = [list(r.combo) + [-1] * (2 - len(r.combo)) for r in rep.interactions]
+        vals = [r.metrics["pearson"] for r in rep.interactions]
+        stab = [(r.metrics_mean["pearson"], r.metrics_std["pearson"]) for r in rep.stability]
+        pv = [r.p_values["pearson"] for r in rep.permutations]
+        if backend == "core":
+            np.savez_compressed(os.path.join(HERE, "engine_report.npz"), X=Xg, y=yg,
+                                combos=np.array(combos, dtype=np.int32), pearson=np.array(vals),
+                                stability=np.array(stab), p_values=np.array(pv),
+                                decision=np.array(rep.decision.signal_detected))
+    plans = {}
+    for seed in (0, 7, 11):
+        r = np.random.default_rng(seed)
+        u, _ = plan_unary(20, 8, r)
+        h, _ = plan_higher_order([int(i[0]) for i in u], 2, 9, r)
+        plans[f"unary_{seed}"] = np.array(u, dtype=np.int32).reshape(-1)
+        plans[f"pairs_{seed}"] = np.array(h, dtype=np.int32)
+    np.savez_compressed(os.path.join(HERE, "planning.npz"), **plans)
     print("wrote fixtures to", HERE)
 
 

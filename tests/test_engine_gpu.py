@@ -1,0 +1,89 @@
+"""The plugin mirror end to end on the GPU against the reference's own results."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def test_selector_top5_equals_reference_selector(golden):
+    from gafime_b200 import GafimeSelector
+    g = golden("config1_centred.npz")
+    sel = GafimeSelector(k=5).fit(g["X"], g["y"])
+    # same combos in the same (shuffled) orientation as the reference's top_interactions_
+    assert [tuple(map(int, c)) for c in sel.top_interactions_] == \
+        [tuple(map(int, c)) for c in g["selector_top_core"]]
+    assert sel.transform(g["X"]).shape == (1000, 55)
+
+
+def test_engine_report_matches_reference_engine(golden):
+    from gafime_b200 import EngineConfig, GafimeEngine
+    from gafime_b200.config import ComputeBudget
+    g = golden("engine_report.npz")
+    cfg = EngineConfig(metric_names=("pearson",),
+                       budget=ComputeBudget(max_comb_size=2, top_features_for_higher_k=8),
+                       num_repeats=3, permutation_tests=10)
+    rep = GafimeEngine(cfg).analyze(g["X"], g["y"])
+    combos = [list(r.combo) + [-1] * (2 - len(r.combo)) for r in rep.interactions]
+    assert combos == g["combos"].tolist()
+    got = np.array([r.metrics["pearson"] for r in rep.interactions])
+    np.testing.assert_array_less(np.abs(got - g["pearson"]), 1e-4 * np.abs(g["pearson"]) + 1e-6)
+    stab = np.array([(r.metrics_mean["pearson"], r.metrics_std["pearson"]) for r in rep.stability])
+    np.testing.assert_allclose(stab, g["stability"], rtol=1e-4, atol=1e-6)
+    pv = np.array([r.p_values["pearson"] for r in rep.permutations])
+    np.testing.assert_array_equal(pv, g["p_values"])
+    assert rep.decision.signal_detected == bool(g["decision"])
+    assert rep.backend.is_gpu
+
+
+def test_selector_in_sklearn_pipeline_and_grid_search():
+    from sklearn.linear_model import LogisticRegression
+    from sklearn.model_selection import GridSearchCV
+    from sklearn.pipeline import Pipeline
+    from gafime_b200 import GafimeSelector
+    rng = np.random.RandomState(42)
+    X = rng.randn(100, 10).astype(np.float32)
+    y = rng.randint(0, 2, size=100).astype(np.float32)
+    pipe = Pipeline([("miner", GafimeSelector(k=5)), ("clf", LogisticRegression())])
+    pipe.fit(X, y)
+    assert pipe.predict(X).shape == (100,)
+    grid = GridSearchCV(Pipeline([("miner", GafimeSelector()), ("clf", LogisticRegression())]),
+                        {"miner__k": [2, 4], "miner__metric": ["pearson"]}, cv=2)
+    grid.fit(X, y)
+    assert grid.best_params_["miner__k"] in (2, 4)
+
+
+@pytest.mark.parametrize("op", ["add", "subtract", "divide"])
+def test_score_operator_routes_the_operator(oracle, op):
+    """With score_operator=True every planned combo (a, b) is scored as x_a op x_b on raw
+    columns; each score matches the oracle and the selector keeps the best by |r|."""
+    from gafime_b200 import EngineConfig, GafimeEngine, GafimeSelector
+    from gafime_b200.config import ComputeBudget
+    rng = np.random.default_rng(4)
+    X = rng.lognormal(0, 1, (3000, 12)).astype(np.float32)
+    y = (X[:, 2] / X[:, 9] + rng.standard_normal(3000) > 1.0).astype(np.float32)
+    cfg = EngineConfig(metric_names=("pearson",), budget=ComputeBudget(max_comb_size=2),
+                       operator=op, center=False, num_repeats=0, permutation_tests=0)
+    rep = GafimeEngine(cfg).analyze(X, y)
+    pairs = [r for r in rep.interactions if len(r.combo) == 2]
+    a = np.array([r.combo[0] for r in pairs], np.int32)
+    b = np.array([r.combo[1] for r in pairs], np.int32)
+    want = oracle.raw_pearson(X, y, op, a, b, div_eps=1e-8)
+    got = np.array([r.metrics["pearson"] for r in pairs])
+    np.testing.assert_array_less(np.abs(got - want), 1e-4 * np.abs(want) + 1e-6)
+    sel = GafimeSelector(k=3, operator=op, score_operator=True).fit(X, y)
+    best = np.argsort(-np.abs(want), kind="stable")[:3]
+    assert [tuple(map(int, c)) for c in sel.top_interactions_] == \
+        [(int(a[p]), int(b[p])) for p in best]
+
+
+def test_mutual_info_metric_through_the_engine(golden):
+    from gafime_b200 import EngineConfig, GafimeEngine
+    from gafime_b200.config import ComputeBudget
+    g = golden("mi_3class.npz")
+    cfg = EngineConfig(metric_names=("mutual_info",), mi_bins=32, num_repeats=0, permutation_tests=0,
+                       budget=ComputeBudget(max_comb_size=2, top_features_for_higher_k=12))
+    rep = GafimeEngine(cfg).analyze(g["X"], g["y"])
+    pairs = {tuple(sorted(r.combo)): r.metrics["mutual_info"] for r in rep.interactions if len(r.combo) == 2}
+    pi, pj = np.triu_indices(12, k=1)
+    for p, (a, b) in enumerate(zip(pi, pj)):
+        assert abs(pairs[(int(a), int(b))] - g["core_b32"][p, 1]) <= 1e-5
