@@ -274,7 +274,6 @@ class CpuArm:
         self.n, self.f = n, f
         self.pi, self.pj = np.triu_indices(f, k=1)
         self.rng = np.random.default_rng(1234)
-        self.cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
         self.kind = "reference"
         self.mode = None
         if self.w["metric"] == "pearson" and not self.w["center"]:
@@ -287,7 +286,7 @@ class CpuArm:
             self.kind = "port"
             from oracle import oracle as orc
             self.orc = orc
-            self.cores = self.cores
+        self.cores = omp_threads_in_use()
         self.mask = np.zeros(n, dtype=np.uint8)
         self.y = np.ascontiguousarray(packed[f])
         self._Xrow = None
@@ -375,10 +374,25 @@ def dist_setup(args):
     return world, rank, local
 
 
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+def omp_threads_in_use() -> int:
+    """Threads the OpenMP runtime of the reference library will use."""
+    try:
+        gomp = ctypes.CDLL("libgomp.so.1")
+        return int(gomp.omp_get_max_threads())
+    except OSError:
+        return host_threads()
+
+
 def run_reference(args):
     world, rank, _ = dist_setup(args)
     if rank != 0:
         return 0
+    # torchrun pins OMP_NUM_THREADS=1; the reference's CPU path gets every host thread
+    os.environ["OMP_NUM_THREADS"] = str(host_threads())
     w = WORKLOADS[args.workload]
     f = scaled_width(world) if (args.workload == "config2" and world > 1) else w["f"]
     packed = np.empty((f + 1, w["n"]), dtype=np.float32)
@@ -541,6 +555,7 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        os.environ["OMP_NUM_THREADS"] = str(host_threads())
         arm = CpuArm(args.workload, packed)
         v, units, dt = arm.measure(args.cpu_seconds)
         cpu = {"value": v, "unit": "evals/s", "cores": arm.cores, "kind": arm.kind,
