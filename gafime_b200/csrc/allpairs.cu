@@ -38,23 +38,46 @@ int64_t tile_pairs(int bi, int bj, int64_t f) {
 
 }  // namespace
 
-// Upper-triangle tiles of this shard.  Tiles are taken in row-major order and each
-// goes to the shard with the fewest pairs so far (ties: lowest shard id), so every
-// process derives the same assignment without communication.
+// Upper-triangle 64 x 64 tiles of this shard.  The pair space is dealt out in
+// 128 x 128 blocks (the tensor-core Gram tile): blocks in decreasing pair count (ties in
+// row-major order), each to the shard with the fewest pairs so far (ties: lowest shard
+// id); a shard scores the 64-tiles inside its blocks.  Every process derives the same
+// split without communication.
 std::vector<TileCoord> shard_tiles(int64_t f, int shard_id, int n_shards) {
     int nb = (int)((f + kTile - 1) / kTile);
+    int nb2 = (nb + 1) / 2;
+    struct Block {
+        int64_t w;
+        int order, ns;
+        TileCoord sub[4];
+    };
+    std::vector<Block> blocks;
+    for (int BI = 0; BI < nb2; ++BI)
+        for (int BJ = BI; BJ < nb2; ++BJ) {
+            Block blk{0, (int)blocks.size(), 0, {}};
+            for (int da = 0; da < 2; ++da)
+                for (int db = 0; db < 2; ++db) {
+                    int bi = 2 * BI + da, bj = 2 * BJ + db;
+                    if (bi > bj || bi >= nb || bj >= nb) continue;
+                    int64_t p = tile_pairs(bi, bj, f);
+                    if (p == 0) continue;
+                    blk.sub[blk.ns++] = {bi, bj};
+                    blk.w += p;
+                }
+            if (blk.w > 0) blocks.push_back(blk);
+        }
+    std::stable_sort(blocks.begin(), blocks.end(),
+                     [](const Block& x, const Block& y) { return x.w > y.w; });
     std::vector<int64_t> load((size_t)n_shards, 0);
     std::vector<TileCoord> mine;
-    for (int bi = 0; bi < nb; ++bi)
-        for (int bj = bi; bj < nb; ++bj) {
-            int64_t w = tile_pairs(bi, bj, f);
-            if (w == 0) continue;
-            int best = 0;
-            for (int s = 1; s < n_shards; ++s)
-                if (load[(size_t)s] < load[(size_t)best]) best = s;
-            load[(size_t)best] += w;
-            if (best == shard_id) mine.push_back({bi, bj});
-        }
+    for (const Block& blk : blocks) {
+        int best = 0;
+        for (int s = 1; s < n_shards; ++s)
+            if (load[(size_t)s] < load[(size_t)best]) best = s;
+        load[(size_t)best] += blk.w;
+        if (best == shard_id)
+            for (int q = 0; q < blk.ns; ++q) mine.push_back(blk.sub[q]);
+    }
     return mine;
 }
 
@@ -119,18 +142,28 @@ int score_ops(Bucket& b, const ColumnStats& cs, const Plan& plan, const TileCoor
     if (e != cudaSuccess) return status_from(e);
     double* mom[2] = {(double*)b.moments.ptr, (double*)((char*)b.moments.ptr + group_bytes)};
     bool need[2] = {false, false};
+    int group_splits[2] = {plan.splits, plan.splits};
     for (int o = 0; o < n_ops; ++o) need[ops[o] == GAFIME_INTERACT_DIV ? 1 : 0] = true;
+    const bool tensor = gram_path_enabled(b);
     for (int g = 0; g < 2; ++g) {
         if (!need[g]) continue;
-        KernelTimer timer(b.stream, GAFIME_KERNEL_PAIR_MOMENTS);
-        e = launch_pair_moments(cs.d_x, b.ld, cs.d_ycen, b.f, d_tiles, nt, plan.splits,
-                                plan.rows_per_split, g == 1, div_eps, mom[g], b.stream);
-        if (e != cudaSuccess) return status_from(e);
+        if (tensor) {
+            int gerr = 0;
+            e = launch_gram_moments(b, cs, d_tiles, plan.tiles, g == 1, div_eps, mom[g], b.stream, &gerr);
+            if (e != cudaSuccess) return status_from(e);
+            if (gerr) return GAFIME_ERROR_KERNEL_FAILED;
+            group_splits[g] = 1;
+        } else {
+            KernelTimer timer(b.stream, GAFIME_KERNEL_PAIR_MOMENTS);
+            e = launch_pair_moments(cs.d_x, b.ld, cs.d_ycen, b.f, d_tiles, nt, plan.splits,
+                                    plan.rows_per_split, g == 1, div_eps, mom[g], b.stream);
+            if (e != cudaSuccess) return status_from(e);
+        }
     }
     for (int o = 0; o < n_ops; ++o) {
         EpilogueArgs a;
         a.moments = mom[ops[o] == GAFIME_INTERACT_DIV ? 1 : 0];
-        a.splits = plan.splits;
+        a.splits = group_splits[ops[o] == GAFIME_INTERACT_DIV ? 1 : 0];
         a.tiles = d_tiles;
         a.n_tiles = nt;
         a.f = b.f;

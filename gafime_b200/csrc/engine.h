@@ -50,7 +50,7 @@ struct Bucket {
     int sm_count = 148;
     // scratch
     DeviceBuf stats_part, stats, ycen, xcen, moments, cands, cands2, scores, flags, tiles, mi,
-        mi_hist, mi_mm;
+        mi_hist, mi_mm, gram;
 };
 
 // Grow a scratch buffer to at least `bytes`; returns cudaSuccess or an error.
@@ -92,6 +92,14 @@ cudaError_t launch_pair_moments(const float* d_x, int64_t ld, const float* d_yce
                                 const TileCoord* d_tiles, int n_tiles, int splits,
                                 int64_t rows_per_split, bool recip, float eps, double* d_moments,
                                 cudaStream_t stream);
+
+// Tensor-core pair moments (gram.cu): the same S1/S2/S3 as launch_pair_moments for the
+// shard's 64-tiles, computed as tcgen05 Gram tiles over 128-blocks; writes one split
+// (splits = 1) into d_moments.  *host_err != 0 reports a bounded wait that gave up.
+bool gram_path_enabled(const Bucket& b);
+cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoord* d_tiles64,
+                                const std::vector<TileCoord>& tiles64, bool recip, float eps,
+                                double* d_moments, cudaStream_t stream, int* host_err);
 
 // Scoring epilogue + per-tile top-k (select.cu).
 struct EpilogueArgs {

@@ -227,3 +227,38 @@ def test_config2_full_size_properties(native, oracle, config2, op):
             assert abs(w) <= kth * (1 + 1e-4) + 1e-6
     if op == "multiply":
         assert (int(gi[0]), int(gj[0])) == (3, 17)
+
+
+_CUDA_CORE_SCRIPT = r"""
+import sys, numpy as np
+sys.path.insert(0, sys.argv[1])
+from gafime_b200 import _native
+d = np.load(sys.argv[2])
+with _native.Bucket(d["X"].shape[0], d["X"].shape[1]) as b:
+    b.upload(d["X"], d["y"])
+    out = {op: b.scores(op, div_eps=1e-6) for op in ("multiply", "add", "subtract", "divide")}
+np.savez(sys.argv[3], **out)
+"""
+
+
+def test_tensor_core_moments_match_cuda_core_kernel(native, tmp_path):
+    """The tcgen05 Gram path (default) and the CUDA-core kernel (GAFIME_PAIR_MOMENTS=cuda-core,
+    a separate process) score the same pairs to the parity tolerance."""
+    import os
+    import subprocess
+    import sys
+    rng = np.random.default_rng(21)
+    n, f = 70_000, 300   # two full 128-blocks + a ragged one, 9 chunks of rows
+    X = np.hstack([rng.standard_normal((n, 150)), rng.lognormal(0, 1, (n, 150))]).astype(np.float32)
+    y = (X[:, 7] * X[:, 160] + rng.standard_normal(n) > 1.0).astype(np.float32)
+    src = tmp_path / "in.npz"
+    dst = tmp_path / "out.npz"
+    np.savez(src, X=X, y=y)
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, GAFIME_PAIR_MOMENTS="cuda-core")
+    subprocess.run([sys.executable, "-c", _CUDA_CORE_SCRIPT, repo, str(src), str(dst)], env=env,
+                   check=True, timeout=600)
+    ref = np.load(dst)
+    with bucket_for(native, X, y) as b:
+        for op in OPS:
+            assert_pearson_close(b.scores(op, div_eps=1e-6), ref[op])
