@@ -11,15 +11,16 @@
 // once per call (gram_prep_kernel), each column scaled by a power of two so its largest
 // magnitude is at most 2^14:
 //     XH = fp16(s a'),  XL = fp16(s a' - XH)          (2-term split, ~22 bits)
-//     QX = fp16(s_q a^2)                              (1 term: positive terms, no cancellation)
-//     WH/WL = 2-term split of s_w a' ycen             (the covariance needs ~fp32 accuracy)
-//     GH/GL/QG: the same for g(b) (divide only)
-// C uses one product (XH XH^T: its rounding is random and averages out over rows), Q one,
-// W three (WH.BH + WH.BL + WL.BH): five MMAs per 16-row step.
+//     QH/QL = 2-term split of s_q a^2
+//     WH/WL = 2-term split of s_w a' ycen
+//     GH/GL, GQH/GQL: the same for g(b) and g(b)^2 (divide only)
+// Each Gram is hi.hi + hi.lo + lo.hi (the lo.lo term is below fp32 rounding): nine MMAs per
+// 16-row step.  One fp16 term is not enough when a few rows dominate a sum (heavy tails,
+// near-zero divisors): their 2^-12 rounding would not average out.
 //
 // Pipeline per CTA (one tile x one row chunk of <= 8192 rows, so each fp32 accumulation
-// stays short): warp 0 issues TMA copies (2-D tensor maps, 64-byte swizzle, no multicast)
-// of 7 operand tiles per 32-row stage into a 4-stage ring; warp 1 issues the MMAs and
+// stays short): warp 0 issues TMA copies (2-D tensor maps, 32-byte swizzle, no multicast)
+// of 10 operand tiles per 16-row stage into a 5-stage ring; warp 1 issues the MMAs and
 // commits each stage back to its "empty" barrier; warps 2-5 drain TMEM (tcgen05.ld) into
 // fp32 partials [chunk][tile][C|Q|W][n][m] in HBM.  gram_reduce_kernel adds the chunks in
 // fp64 in a fixed order, undoes the scales and the centring, and writes the raw moments
@@ -47,17 +48,17 @@ namespace gafime {
 namespace {
 
 constexpr int kGT = 128;                      // Gram tile edge (columns)
-constexpr int kGK = 32;                       // rows per pipeline stage
-constexpr int kGStages = 4;
-constexpr int kOpBytes = kGT * kGK * 2;       // one operand tile: 128 columns x 32 rows fp16
-constexpr int kNumA = 4, kNumB = 3;
+constexpr int kGK = 16;                       // rows per pipeline stage (one MMA K step)
+constexpr int kGStages = 5;
+constexpr int kOpBytes = kGT * kGK * 2;       // one operand tile: 128 columns x 16 rows fp16
+constexpr int kNumA = 6, kNumB = 4;
 constexpr int kStageBytes = (kNumA + kNumB) * kOpBytes;
 constexpr int kGramThreads = 192;
 constexpr uint32_t kTmemCols = 512;
 constexpr long long kSpinLimit = 1LL << 24;
 constexpr int64_t kMaxChunkRows = 8192;
 
-enum Plane { P_XH = 0, P_XL, P_QX, P_WH, P_WL, P_GH, P_GL, P_QG, P_COUNT };
+enum Plane { P_XH = 0, P_XL, P_QH, P_QL, P_WH, P_WL, P_GH, P_GL, P_GQH, P_GQL, P_COUNT };
 
 struct GramMaps {
     CUtensorMap m[P_COUNT];
@@ -68,8 +69,8 @@ struct GramArgs {
     int n_tiles;
     int64_t chunk_rows;       // multiple of kGK
     int64_t rows;             // padded rows (ld)
-    int a_plane[kNumA];       // XH, QX, WH, WL
-    int b_plane[kNumB];       // XH|GH, QX|QG, XL|GL
+    int a_plane[kNumA];       // XH, XL, QH, QL, WH, WL
+    int b_plane[kNumB];       // XH|GH, XL|GL, QH|GQH, QL|GQL
     float* partial;           // [chunk][tile][3][128 n][128 m]
     int* err;
 };
@@ -118,11 +119,11 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// K-major operand tile with the 64-byte swizzle: rows of 64 B (32 fp16 along K), 8-row
-// groups 512 B apart (SBO), LBO unused (1), descriptor version 1, layout code 4.
+// K-major operand tile with the 32-byte swizzle: rows of 32 B (16 fp16 along K), 8-row
+// groups 256 B apart (SBO), LBO unused (1), descriptor version 1, layout code 6.
 __device__ __forceinline__ uint64_t umma_desc(uint32_t addr) {
-    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(256 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)6 << 61);
 }
 
 // kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N = 128, M = 128.
@@ -201,7 +202,7 @@ gram_tile_kernel(const __grid_constant__ GramMaps maps, const GramArgs a) {
 
     if (warp == 0) {
         if (lane == 0) {
-            // producer: 7 operand tiles per stage
+            // producer: 10 operand tiles per stage
             int issued = 0;
             bool ok = true;
             for (int k = 0; k < nk && ok; ++k) {
@@ -234,23 +235,21 @@ gram_tile_kernel(const __grid_constant__ GramMaps maps, const GramArgs a) {
                 if (!mbar_wait(full0 + 8 * s, (k / kGStages) & 1, a.err, 2)) break;
                 tc_fence_after();
                 const uint32_t st = smem0 + s * kStageBytes;
-                #pragma unroll
-                for (int kk = 0; kk < kGK / 16; ++kk) {
-                    const uint32_t off = kk * 32;  // 16 fp16 along K
-                    const uint64_t aXH = umma_desc(st + 0 * kOpBytes + off);
-                    const uint64_t aQ = umma_desc(st + 1 * kOpBytes + off);
-                    const uint64_t aWH = umma_desc(st + 2 * kOpBytes + off);
-                    const uint64_t aWL = umma_desc(st + 3 * kOpBytes + off);
-                    const uint64_t bH = umma_desc(st + 4 * kOpBytes + off);
-                    const uint64_t bQ = umma_desc(st + 5 * kOpBytes + off);
-                    const uint64_t bL = umma_desc(st + 6 * kOpBytes + off);
-                    const uint32_t acc = (k > 0 || kk > 0) ? 1u : 0u;
-                    umma(tmem + 0, aXH, bH, acc);      // C
-                    umma(tmem + 128, aQ, bQ, acc);     // Q
-                    umma(tmem + 256, aWH, bH, acc);    // W: hi x hi
-                    umma(tmem + 256, aWH, bL, 1u);     //    hi x lo
-                    umma(tmem + 256, aWL, bH, 1u);     //    lo x hi
-                }
+                const uint64_t aXH = umma_desc(st + 0 * kOpBytes), aXL = umma_desc(st + 1 * kOpBytes);
+                const uint64_t aQH = umma_desc(st + 2 * kOpBytes), aQL = umma_desc(st + 3 * kOpBytes);
+                const uint64_t aWH = umma_desc(st + 4 * kOpBytes), aWL = umma_desc(st + 5 * kOpBytes);
+                const uint64_t bH = umma_desc(st + 6 * kOpBytes), bL = umma_desc(st + 7 * kOpBytes);
+                const uint64_t bQH = umma_desc(st + 8 * kOpBytes), bQL = umma_desc(st + 9 * kOpBytes);
+                const uint32_t acc = k > 0 ? 1u : 0u;
+                umma(tmem + 0, aXH, bH, acc);      // C: hi x hi
+                umma(tmem + 0, aXH, bL, 1u);       //    hi x lo
+                umma(tmem + 0, aXL, bH, 1u);       //    lo x hi
+                umma(tmem + 128, aQH, bQH, acc);   // Q
+                umma(tmem + 128, aQH, bQL, 1u);
+                umma(tmem + 128, aQL, bQH, 1u);
+                umma(tmem + 256, aWH, bH, acc);    // W
+                umma(tmem + 256, aWH, bL, 1u);
+                umma(tmem + 256, aWL, bH, 1u);
                 umma_commit(empty0 + 8 * s);  // stage free once these MMAs have read it
             }
             umma_commit(accum);  // all issued MMAs complete (also on the error path)
@@ -427,29 +426,32 @@ __global__ void __launch_bounds__(256) gram_prep_kernel(const float* __restrict_
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
          e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t c = e / ld, r = e - c * ld;
-        __half xh = __float2half_rn(0.f), xl = xh, qx = xh, wh = xh, wl = xh, gh = xh, gl = xh, qg = xh;
+        const __half z = __float2half_rn(0.f);
+        __half xh = z, xl = z, qh = z, ql = z, wh = z, wl = z, gh = z, gl = z, gqh = z, gql = z;
         if (r < n) {
             const float xv = x[e];
             const double* sc = cs + c * 12;
             const double ap = (double)xv - colstats[c * 4 + 3];
             split16(ap * sc[0], xh, xl);
-            qx = __float2half_rn((float)((double)xv * (double)xv * sc[1]));
+            split16((double)xv * (double)xv * sc[1], qh, ql);
             split16(ap * (double)ycen[r] * sc[2], wh, wl);
             if (recip) {
                 const double g = safe_recip(xv, eps);
                 split16((g - sc[5]) * sc[3], gh, gl);
-                qg = __float2half_rn((float)(g * g * sc[4]));
+                split16(g * g * sc[4], gqh, gql);
             }
         }
         planes[P_XH * plane + e] = xh;
         planes[P_XL * plane + e] = xl;
-        planes[P_QX * plane + e] = qx;
+        planes[P_QH * plane + e] = qh;
+        planes[P_QL * plane + e] = ql;
         planes[P_WH * plane + e] = wh;
         planes[P_WL * plane + e] = wl;
         if (recip) {
             planes[P_GH * plane + e] = gh;
             planes[P_GL * plane + e] = gl;
-            planes[P_QG * plane + e] = qg;
+            planes[P_GQH * plane + e] = gqh;
+            planes[P_GQL * plane + e] = gql;
         }
     }
 }
@@ -541,7 +543,7 @@ bool make_plane_map(CUtensorMap* map, const __half* base, int64_t ld, int64_t f)
     cuuint32_t box[2] = {(cuuint32_t)kGK, (cuuint32_t)kGT};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)base, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -664,13 +666,11 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     ga.n_tiles = nt;
     ga.chunk_rows = chunk;
     ga.rows = ld;
-    ga.a_plane[0] = P_XH;
-    ga.a_plane[1] = P_QX;
-    ga.a_plane[2] = P_WH;
-    ga.a_plane[3] = P_WL;
-    ga.b_plane[0] = recip ? P_GH : P_XH;
-    ga.b_plane[1] = recip ? P_QG : P_QX;
-    ga.b_plane[2] = recip ? P_GL : P_XL;
+    const int a_planes[kNumA] = {P_XH, P_XL, P_QH, P_QL, P_WH, P_WL};
+    const int b_planes[kNumB] = {recip ? P_GH : P_XH, recip ? P_GL : P_XL, recip ? P_GQH : P_QH,
+                                 recip ? P_GQL : P_QL};
+    for (int o = 0; o < kNumA; ++o) ga.a_plane[o] = a_planes[o];
+    for (int o = 0; o < kNumB; ++o) ga.b_plane[o] = b_planes[o];
     ga.partial = partial;
     ga.err = d_err;
     const size_t smem = (size_t)kGStages * kStageBytes + 1024 + 256;
