@@ -154,7 +154,8 @@ def build_packed(name: str, packed: np.ndarray):
     if name == "config2" and packed.shape[0] - 1 != f:
         fill_config2_scaled(packed, n)
     elif name in ("config1", "config2", "config3"):
-        X, y = {"config1": make_config1, "config2": make_config2, "config3": make_config3}[name]()
+        X, y = make_config1() if name == "config1" else \
+            {"config2": make_config2, "config3": make_config3}[name](n=packed.shape[1])
         packed[:f] = X.T
         packed[f] = y
     elif name == "config4":
@@ -502,8 +503,11 @@ def run_ours(args):
     _native.profile_enable(True)
     ms = timed(step, args.steps)
     _native.profile_enable(False)
-    mom_ms, mom_launches = _native.profile_read("pair_moments")
-    mi_ms, mi_launches = _native.profile_read("mi_pass2")
+    kernel_ms = {}
+    for kname in _native.KERNEL_IDS:
+        kms, kl = _native.profile_read(kname)
+        if kl:
+            kernel_ms[kname] = {"ms_per_step": kms / args.steps, "launches": kl}
     all_ms, all_launches = _native.profile_read("all")
     clk = clocks.stop()
     result = step()
@@ -522,36 +526,39 @@ def run_ours(args):
     value = evals / (ms / 1e3)
     e2e_value = evals / (e2e_ms / 1e3)
 
-    # roofline of the dominant kernel
+    # roofline of the dominant kernel (largest device time in the timed region)
     peaks, peak_kind = measured_peaks()
-    if w["metric"] == "pearson":
-        groups = len({"div" if o == "divide" else "mul" for o in ops})
-        my_pairs = pairs / world
-        launches_per_step = groups
-        avg_ms = mom_ms / max(1, mom_launches)
+    dom = max(kernel_ms, key=lambda k: kernel_ms[k]["ms_per_step"]) if kernel_ms else None
+    my_pairs = pairs / world
+    roof = None
+    if dom in ("gram_tc", "pair_moments"):
+        d = kernel_ms[dom]
+        avg_ms = d["ms_per_step"] * args.steps / d["launches"]
         flops = algorithmic_flops_per_pair_row(w["metric"]) * my_pairs * n
         achieved = flops / (avg_ms / 1e3) / 1e12
         peak = peaks["bf16_tflops"]
-        roof = {"bound": "tensor", "kernel": "pair_moments (CUDA-core fp32, fp64 flush)",
+        roof = {"bound": "tensor",
+                "kernel": ("gram_tile_kernel (tcgen05 kind::f16, 2-term fp16 splits, TMEM fp32)"
+                           if dom == "gram_tc" else "pair_moments_kernel (CUDA-core fp32, fp64 flush)"),
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_source": f"bf16_tflops (burst) of {peak_kind} MEASURED_PEAKS.json",
-                "avg_launch_ms": avg_ms, "launches": mom_launches,
-                "algorithmic": f"6 FLOP per pair-row x {my_pairs:.0f} pairs x {n} rows per launch",
-                "traffic": NCU_TRAFFIC_BYTES.get((args.workload, "pair_moments"))}
-    else:
-        avg_ms = mi_ms / max(1, mi_launches)
-        my_pairs = pairs / world
-        # algorithmic bytes per launch: 13 B per pair-row (reference formulation,
-        # kernels.cu:2344-2347: x_i, x_j, y fp32 + mask u8)
+                "avg_launch_ms": avg_ms, "launches": d["launches"],
+                "algorithmic": f"6 FLOP per pair-row x {my_pairs:.0f} pairs x {n} rows per launch "
+                               "(one launch per moment group: multiply/add/subtract, divide)",
+                "traffic": NCU_TRAFFIC_BYTES.get((args.workload, dom))}
+    elif dom is not None:
+        d = kernel_ms[dom]
+        avg_ms = d["ms_per_step"] * args.steps / d["launches"]
+        # algorithmic bytes: 13 B per pair-row (x_i, x_j, y fp32 + mask u8, the reference's
+        # per-pair formulation, kernels.cu:2344-2347)
         bytes_ = 13.0 * my_pairs * n
         achieved = bytes_ / (avg_ms / 1e3) / 1e9
         peak = peaks["hbm_gbs"]
-        roof = {"bound": "hbm", "kernel": "mi_pass2 (joint histogram)", "achieved": achieved,
-                "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "peak_source": f"hbm_gbs of {peak_kind} MEASURED_PEAKS.json",
-                "avg_launch_ms": avg_ms, "launches": mi_launches,
-                "algorithmic": f"13 B per pair-row (effective) x {my_pairs:.0f} pairs x {n} rows",
-                "traffic": NCU_TRAFFIC_BYTES.get((args.workload, "mi_pass2"))}
+        roof = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": f"hbm_gbs of {peak_kind} MEASURED_PEAKS.json",
+                "avg_launch_ms": avg_ms, "launches": d["launches"],
+                "algorithmic": f"13 B per pair-row x {my_pairs:.0f} pairs x {n} rows per launch",
+                "traffic": NCU_TRAFFIC_BYTES.get((args.workload, dom))}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -578,6 +585,7 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "evals/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "kernels": kernel_ms,
         "gpu_launches": all_launches // max(1, args.steps),
         "gpu_launches_timed_region": all_launches,
         "clocks": clk,
@@ -601,8 +609,12 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="override the row count (small cases for profiling; not a bench line)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # at least 3 untimed warm-up steps
+    if args.rows:
+        WORKLOADS[args.workload] = dict(WORKLOADS[args.workload], n=args.rows)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

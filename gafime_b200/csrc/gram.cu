@@ -632,10 +632,13 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     if (e != cudaSuccess) return e;
 
     // operand statistics, scales and planes
-    absmax_kernel<<<2 * b.sm_count, 256, 0, stream>>>(cs.d_ycen, ld, d_absmax);
     int64_t span = ((n + splits - 1) / splits + 255) / 256 * 256;
-    gram_colstats_kernel<<<dim3((unsigned)f, (unsigned)splits), 256, 0, stream>>>(cs.d_x, ld, n, cs.d_ycen,
-                                                                                 recip ? 1 : 0, eps, span, colp);
+    {
+        KernelTimer timer(stream, GAFIME_KERNEL_GRAM_PREP);
+        absmax_kernel<<<2 * b.sm_count, 256, 0, stream>>>(cs.d_ycen, ld, d_absmax);
+        gram_colstats_kernel<<<dim3((unsigned)f, (unsigned)splits), 256, 0, stream>>>(
+            cs.d_x, ld, n, cs.d_ycen, recip ? 1 : 0, eps, span, colp);
+    }
     unsigned h_absmax = 0;
     e = cudaMemcpyAsync(&h_absmax, d_absmax, sizeof(unsigned), cudaMemcpyDeviceToHost, stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
@@ -652,8 +655,11 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     sa.recip = recip ? 1 : 0;
     sa.cs = d_cs;
     gram_scale_kernel<<<(unsigned)((f + 127) / 128), 128, 0, stream>>>(sa);
-    gram_prep_kernel<<<8 * b.sm_count, 256, 0, stream>>>(cs.d_x, ld, n, f, cs.d_ycen, cs.d_col, d_cs,
-                                                         recip ? 1 : 0, eps, planes);
+    {
+        KernelTimer timer(stream, GAFIME_KERNEL_GRAM_PREP);
+        gram_prep_kernel<<<8 * b.sm_count, 256, 0, stream>>>(cs.d_x, ld, n, f, cs.d_ycen, cs.d_col, d_cs,
+                                                             recip ? 1 : 0, eps, planes);
+    }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
 
@@ -697,7 +703,10 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     ra.cs = d_cs;
     ra.recip = recip ? 1 : 0;
     ra.moments = d_moments;
-    gram_reduce_kernel<<<(unsigned)tiles64.size(), 256, 0, stream>>>(ra);
+    {
+        KernelTimer timer(stream, GAFIME_KERNEL_GRAM_REDUCE);
+        gram_reduce_kernel<<<(unsigned)tiles64.size(), 256, 0, stream>>>(ra);
+    }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     int h_err = 0;

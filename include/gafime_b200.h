@@ -205,6 +205,8 @@ int gafime_topk_merge(const int32_t* cand_i, const int32_t* cand_j, const double
 #define GAFIME_KERNEL_LEGACY_PAIR 8
 #define GAFIME_KERNEL_FINITE_CHECK 9
 #define GAFIME_KERNEL_GRAM_TC 10
+#define GAFIME_KERNEL_GRAM_PREP 11
+#define GAFIME_KERNEL_GRAM_REDUCE 12
 
 /* NEW.  enable = 1: drop any previous records, then bracket every engine kernel
  * launch with CUDA events on its stream.  enable = 0: stop recording (the records
