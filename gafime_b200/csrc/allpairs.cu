@@ -149,7 +149,11 @@ int score_ops(Bucket& b, const ColumnStats& cs, const Plan& plan, const TileCoor
         if (!need[g]) continue;
         if (tensor) {
             int gerr = 0;
-            e = launch_gram_moments(b, cs, d_tiles, plan.tiles, g == 1, div_eps, mom[g], b.stream, &gerr);
+            // one operand preparation serves both groups when both are scored
+            const int prep = (g == 0 && need[1]) ? GRAM_PREP_BOTH : (g == 1 && need[0]) ? GRAM_PREP_DONE
+                                                                                      : GRAM_PREP_OWN;
+            e = launch_gram_moments(b, cs, d_tiles, plan.tiles, g == 1, div_eps, mom[g], b.stream, &gerr,
+                                    prep);
             if (e != cudaSuccess) return status_from(e);
             if (gerr) return GAFIME_ERROR_KERNEL_FAILED;
             group_splits[g] = 1;

@@ -7,9 +7,10 @@
 //     W = sum (a' ycen) b'    (ycen = y - mean y)
 // with g = identity (multiply; add / subtract reuse C) or g(b) = 1/safe(b) (divide).
 // They are computed by tcgen05.mma kind::f16 with fp32 accumulators in tensor memory
-// (TMEM columns 0-127: C, 128-255: Q, 256-383: W).  Operands are fp16 planes prepared
-// once per call (gram_prep_kernel), each column scaled by a power of two so its largest
-// magnitude is at most 2^14:
+// (TMEM columns 0-127: C, 128-255: Q, 256-383: W).  Operands are fp16 planes stored row-major
+// ([row][column], so a 16-row x 64-column TMA box is 16 runs of 128 B and the MMA reads
+// MN-major operands), prepared once per call by gram_prep_kernel with every column scaled by
+// a power of two so its largest magnitude is at most 2^14:
 //     XH = fp16(s a'),  XL = fp16(s a' - XH)          (2-term split, ~22 bits)
 //     QH/QL = 2-term split of s_q a^2
 //     WH/WL = 2-term split of s_w a' ycen
@@ -19,8 +20,8 @@
 // near-zero divisors): their 2^-12 rounding would not average out.
 //
 // Pipeline per CTA (one tile x one row chunk of <= 8192 rows, so each fp32 accumulation
-// stays short): warp 0 issues TMA copies (2-D tensor maps, 32-byte swizzle, no multicast)
-// of 10 operand tiles per 16-row stage into a 5-stage ring; warp 1 issues the MMAs and
+// stays short): warp 0 issues TMA copies (2-D tensor maps, 128-byte swizzle, no multicast)
+// of 10 operand tiles (two 64-column boxes each) per 16-row stage into a 5-stage ring; warp 1 issues the MMAs and
 // commits each stage back to its "empty" barrier; warps 2-5 drain TMEM (tcgen05.ld) into
 // fp32 partials [chunk][tile][C|Q|W][n][m] in HBM.  gram_reduce_kernel adds the chunks in
 // fp64 in a fixed order, undoes the scales and the centring, and writes the raw moments
@@ -119,16 +120,17 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// K-major operand tile with the 32-byte swizzle: rows of 32 B (16 fp16 along K), 8-row
-// groups 256 B apart (SBO), LBO unused (1), descriptor version 1, layout code 6.
+// MN-major operand tile, 128-byte swizzle: 64 columns (128 B) per swizzle row, 16 K rows;
+// the two 64-column halves of a 128-column tile are 2048 B apart (LBO) and the two 8-row K
+// groups 1024 B apart (SBO); descriptor version 1, layout code 2.
 __device__ __forceinline__ uint64_t umma_desc(uint32_t addr) {
-    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(256 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)6 << 61);
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(2048 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N = 128, M = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kGT >> 3) << 17) |
-                            ((uint32_t)(kGT >> 4) << 24);
+// kind::f16 instruction descriptor: D f32, A/B f16, both MN-major, N = 128, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (1u << 15) | (1u << 16) |
+                            ((uint32_t)(kGT >> 3) << 17) | ((uint32_t)(kGT >> 4) << 24);
 
 __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
     asm volatile(
@@ -212,13 +214,19 @@ gram_tile_kernel(const __grid_constant__ GramMaps maps, const GramArgs a) {
                 const uint32_t full = full0 + 8 * s;
                 mbar_expect_tx(full, (uint32_t)kStageBytes);
                 const uint32_t st = smem0 + s * kStageBytes;
-                const int x = (int)(r0 + (int64_t)k * kGK);
+                const int x = (int)(r0 + (int64_t)k * kGK);  // first row of the stage
                 #pragma unroll
                 for (int o = 0; o < kNumA; ++o)
-                    tma_load_2d(st + o * kOpBytes, &maps.m[a.a_plane[o]], full, x, tc.bi * kGT);
+                    #pragma unroll
+                    for (int h = 0; h < 2; ++h)
+                        tma_load_2d(st + o * kOpBytes + h * (kOpBytes / 2), &maps.m[a.a_plane[o]], full,
+                                    tc.bi * kGT + h * 64, x);
                 #pragma unroll
                 for (int o = 0; o < kNumB; ++o)
-                    tma_load_2d(st + (kNumA + o) * kOpBytes, &maps.m[a.b_plane[o]], full, x, tc.bj * kGT);
+                    #pragma unroll
+                    for (int h = 0; h < 2; ++h)
+                        tma_load_2d(st + (kNumA + o) * kOpBytes + h * (kOpBytes / 2), &maps.m[a.b_plane[o]],
+                                    full, tc.bj * kGT + h * 64, x);
                 ++issued;
             }
             if (!ok) {
@@ -345,8 +353,10 @@ __global__ void __launch_bounds__(256) gram_colstats_kernel(const float* __restr
 }
 
 // Per-column scales and statistics of the operands:
-//   cs[c*12 + 0..5]: s_x, s_q, s_w, s_g, s_qg (powers of two), mean g
+//   cs[c*12 + 0..4]: s_x, s_q, s_w, s_g, s_gq (powers of two)
+//   cs[c*12 + 5]: mean g rounded to fp32 (the value the planes subtract)
 //   cs[c*12 + 6..8]: sum g, sum g^2, sum g*ycen
+//   cs[c*12 + 9]: mean x rounded to fp32 (the value the planes subtract)
 struct GramScaleArgs {
     const GramColPart* part;
     int splits;
@@ -379,17 +389,19 @@ __global__ void gram_scale_kernel(GramScaleArgs a) {
         gmn = fmin(gmn, p.v[5]);
         gmx = fmax(gmx, p.v[6]);
     }
-    const double mu = a.colstats[c * 4 + 3];
-    const double dev = fmax(fabs(mx - mu), fabs(mu - mn));
+    const double mu = (double)(float)a.colstats[c * 4 + 3];
+    // the fp32 subtraction may round up by one ulp: a 2^-20 margin keeps |value| <= 2^14
+    const double dev = fmax(fabs(mx - mu), fabs(mu - mn)) * (1.0 + 1e-6);
     double* o = a.cs + c * 12;
     o[0] = pow2_scale(dev);
-    o[1] = pow2_scale(fmax(mx * mx, mn * mn));
-    o[2] = pow2_scale(dev * a.ycen_absmax);
+    o[1] = pow2_scale(fmax(mx * mx, mn * mn) * (1.0 + 1e-6));
+    o[2] = pow2_scale(dev * a.ycen_absmax * (1.0 + 1e-6));
+    o[9] = mu;
     if (a.recip) {
-        const double mug = sg / (double)a.n;
-        const double gdev = fmax(fabs(gmx - mug), fabs(mug - gmn));
+        const double mug = (double)(float)(sg / (double)a.n);
+        const double gdev = fmax(fabs(gmx - mug), fabs(mug - gmn)) * (1.0 + 1e-6);
         o[3] = pow2_scale(gdev);
-        o[4] = pow2_scale(fmax(gmx * gmx, gmn * gmn));
+        o[4] = pow2_scale(fmax(gmx * gmx, gmn * gmn) * (1.0 + 1e-6));
         o[5] = mug;
     } else {
         o[3] = o[4] = 1.0;
@@ -408,50 +420,81 @@ __global__ void absmax_kernel(const float* __restrict__ v, int64_t n, unsigned* 
     if ((threadIdx.x & 31) == 0) atomicMax(out_bits, __float_as_uint(m));  // non-negative floats order as uints
 }
 
-__device__ __forceinline__ void split16(double v, __half& hi, __half& lo) {
-    float f = (float)v;
-    hi = __float2half_rn(f);
-    lo = __float2half_rn(f - __half2float(hi));
+__device__ __forceinline__ void split16(float v, __half& hi, __half& lo) {
+    hi = __float2half_rn(v);
+    lo = __float2half_rn(v - __half2float(hi));  // v - hi is exact in fp32
 }
 
-// Write the fp16 operand planes (plane p of column c at planes + (p * f + c) * ld);
-// rows at or beyond n are zero in every plane.
-__global__ void __launch_bounds__(256) gram_prep_kernel(const float* __restrict__ x, int64_t ld, int64_t n,
-                                                        int64_t f, const float* __restrict__ ycen,
-                                                        const double* __restrict__ colstats,
-                                                        const double* __restrict__ cs, int recip, float eps,
-                                                        __half* __restrict__ planes) {
-    const int64_t total = f * ld;
-    const int64_t plane = f * ld;
-    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
-         e += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t c = e / ld, r = e - c * ld;
-        const __half z = __float2half_rn(0.f);
-        __half xh = z, xl = z, qh = z, ql = z, wh = z, wl = z, gh = z, gl = z, gqh = z, gql = z;
-        if (r < n) {
-            const float xv = x[e];
-            const double* sc = cs + c * 12;
-            const double ap = (double)xv - colstats[c * 4 + 3];
-            split16(ap * sc[0], xh, xl);
-            split16((double)xv * (double)xv * sc[1], qh, ql);
-            split16(ap * (double)ycen[r] * sc[2], wh, wl);
-            if (recip) {
-                const double g = safe_recip(xv, eps);
-                split16((g - sc[5]) * sc[3], gh, gl);
-                split16(g * g * sc[4], gqh, gql);
-            }
+struct GramPrepArgs {
+    const float* x;           // column-major, ld rows per column
+    int64_t ld, n, f, fp;     // fp: row length of the planes (f rounded up to 64)
+    const float* ycen;
+    const double* cs;
+    float eps;
+    int write_x, write_g;     // which plane groups to write
+    __half* planes;           // plane p: [ld][fp] at planes + p * ld * fp
+};
+
+// Column-major fp32 -> row-major fp16 planes through a 32 x 32 shared-memory transpose;
+// rows at or beyond n and columns at or beyond f are zero in every plane.
+__global__ void __launch_bounds__(256) gram_prep_kernel(GramPrepArgs a) {
+    __shared__ float xs[32][33];
+    __shared__ float ys[32];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int64_t n_ct = a.fp / 32, total = n_ct * (a.ld / 32);
+    const int64_t plane = a.ld * a.fp;
+    for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
+        const int64_t c0 = (t % n_ct) * 32, r0 = (t / n_ct) * 32;
+        __syncthreads();
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int64_t c = c0 + ty + 8 * k, r = r0 + tx;
+            xs[ty + 8 * k][tx] = (c < a.f && r < a.n) ? a.x[c * a.ld + r] : 0.0f;
         }
-        planes[P_XH * plane + e] = xh;
-        planes[P_XL * plane + e] = xl;
-        planes[P_QH * plane + e] = qh;
-        planes[P_QL * plane + e] = ql;
-        planes[P_WH * plane + e] = wh;
-        planes[P_WL * plane + e] = wl;
-        if (recip) {
-            planes[P_GH * plane + e] = gh;
-            planes[P_GL * plane + e] = gl;
-            planes[P_GQH * plane + e] = gqh;
-            planes[P_GQL * plane + e] = gql;
+        if (ty == 0) ys[tx] = a.ycen[r0 + tx];
+        __syncthreads();
+        const int64_t c = c0 + tx;
+        const bool cv = c < a.f;
+        float sx = 0, sq = 0, sw = 0, sg = 0, sgq = 0, mug = 0, mu = 0;
+        if (cv) {
+            const double* s = a.cs + c * 12;
+            sx = (float)s[0]; sq = (float)s[1]; sw = (float)s[2];
+            sg = (float)s[3]; sgq = (float)s[4]; mug = (float)s[5]; mu = (float)s[9];
+        }
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int64_t r = r0 + ty + 8 * k;
+            const bool v = cv && r < a.n;
+            const float xv = xs[tx][ty + 8 * k];
+            const int64_t o = r * a.fp + c;
+            const __half z = __float2half_rn(0.f);
+            if (a.write_x) {
+                __half xh = z, xl = z, qh = z, ql = z, wh = z, wl = z;
+                if (v) {
+                    const float ap = xv - mu;
+                    split16(ap * sx, xh, xl);
+                    split16(xv * xv * sq, qh, ql);
+                    split16(ap * ys[ty + 8 * k] * sw, wh, wl);
+                }
+                a.planes[P_XH * plane + o] = xh;
+                a.planes[P_XL * plane + o] = xl;
+                a.planes[P_QH * plane + o] = qh;
+                a.planes[P_QL * plane + o] = ql;
+                a.planes[P_WH * plane + o] = wh;
+                a.planes[P_WL * plane + o] = wl;
+            }
+            if (a.write_g) {
+                __half gh = z, gl = z, gqh = z, gql = z;
+                if (v) {
+                    const float gv = safe_recip(xv, a.eps);
+                    split16((gv - mug) * sg, gh, gl);
+                    split16(gv * gv * sgq, gqh, gql);
+                }
+                a.planes[P_GH * plane + o] = gh;
+                a.planes[P_GL * plane + o] = gl;
+                a.planes[P_GQH * plane + o] = gqh;
+                a.planes[P_GQL * plane + o] = gql;
+            }
         }
     }
 }
@@ -472,6 +515,8 @@ struct GramReduceArgs {
     double* moments;          // [1][n_tiles64][3][4096]
 };
 
+// grid (n_tiles64, 16): 256 pairs of one 64-tile per CTA, consecutive threads on
+// consecutive rows m of the partials (coalesced), chunks added in a fixed order.
 __global__ void __launch_bounds__(256) gram_reduce_kernel(GramReduceArgs a) {
     const int t = blockIdx.x;
     const TileCoord tc = a.tiles64[t];
@@ -479,45 +524,48 @@ __global__ void __launch_bounds__(256) gram_reduce_kernel(GramReduceArgs a) {
     const int t128 = a.lut[I * a.nb128 + J];
     const double n = (double)a.n;
     double* out = a.moments + (int64_t)t * 3 * kTilePairs;
-    for (int e = threadIdx.x; e < kTilePairs; e += blockDim.x) {
-        const int li = e / kTile, lj = e % kTile;
-        const int m = (tc.bi & 1) * kTile + li, nn = (tc.bj & 1) * kTile + lj;
-        const int64_t i = (int64_t)tc.bi * kTile + li, j = (int64_t)tc.bj * kTile + lj;
-        double S1 = 0.0, Q = 0.0, S3 = 0.0;
-        if (t128 >= 0 && i < a.f && j < a.f) {
-            double C = 0.0, W = 0.0;
-            for (int ch = 0; ch < a.n_chunks; ++ch) {
-                const float* p = a.partial + ((int64_t)ch * a.n_tiles128 + t128) * 3 * kGT * kGT +
-                                 (int64_t)nn * kGT + m;
-                C += (double)p[0];
-                Q += (double)p[(int64_t)kGT * kGT];
-                W += (double)p[(int64_t)2 * kGT * kGT];
-            }
-            const double* ci = a.cs + i * 12;
-            const double* cj = a.cs + j * 12;
-            const double mua = a.colstats[i * 4 + 3];
-            const double Sa = a.colstats[i * 4 + 0], Ua = a.colstats[i * 4 + 2];
-            double mub, Sb, Ub, sB, sQB;
-            if (a.recip) {
-                mub = cj[5]; Sb = cj[6]; Ub = cj[8]; sB = cj[3]; sQB = cj[4];
-            } else {
-                mub = a.colstats[j * 4 + 3]; Sb = a.colstats[j * 4 + 0]; Ub = a.colstats[j * 4 + 2];
-                sB = cj[0]; sQB = cj[1];
-            }
-            C /= ci[0] * sB;
-            Q /= ci[1] * sQB;
-            W /= ci[2] * sB;
-            // undo the centring: a = a' + mean_a, g(b) = b' + mean_b
-            const double sa_c = Sa - n * mua, sb_c = Sb - n * mub;   // sum a', sum b' (~0)
-            S1 = C + mua * sb_c + mub * sa_c + n * mua * mub;
-            // sum a b ycen = W + mean_a sum b' ycen + mean_b sum a' ycen + mean_a mean_b sum ycen;
-            // sum ycen is the rounding residue of fl32(y - mean y) (~1e-8 sqrt(n)) and is dropped.
-            S3 = W + mua * Ub + mub * Ua;
+    const int q = blockIdx.y * blockDim.x + threadIdx.x;   // 0 .. 4095
+    const int lj = q / kTile, li = q % kTile;
+    const int e = li * kTile + lj;
+    const int m = (tc.bi & 1) * kTile + li, nn = (tc.bj & 1) * kTile + lj;
+    const int64_t i = (int64_t)tc.bi * kTile + li, j = (int64_t)tc.bj * kTile + lj;
+    double S1 = 0.0, Q = 0.0, S3 = 0.0;
+    if (t128 >= 0 && i < a.f && j < a.f) {
+        double C = 0.0, W = 0.0;
+        const float* p = a.partial + (int64_t)t128 * 3 * kGT * kGT + (int64_t)nn * kGT + m;
+        const int64_t cstride = (int64_t)a.n_tiles128 * 3 * kGT * kGT;
+        #pragma unroll 4
+        for (int ch = 0; ch < a.n_chunks; ++ch) {
+            const float* pc = p + ch * cstride;
+            C += (double)pc[0];
+            Q += (double)pc[(int64_t)kGT * kGT];
+            W += (double)pc[(int64_t)2 * kGT * kGT];
         }
-        out[e] = S1;
-        out[kTilePairs + e] = Q;
-        out[2 * kTilePairs + e] = S3;
+        const double* ci = a.cs + i * 12;
+        const double* cj = a.cs + j * 12;
+        const double mua = ci[9];                 // the mean the planes subtracted (fp32)
+        const double Sa = a.colstats[i * 4 + 0], Ua = a.colstats[i * 4 + 2];
+        double mub, Sb, Ub, sB, sQB;
+        if (a.recip) {
+            mub = cj[5]; Sb = cj[6]; Ub = cj[8]; sB = cj[3]; sQB = cj[4];
+        } else {
+            mub = cj[9]; Sb = a.colstats[j * 4 + 0]; Ub = a.colstats[j * 4 + 2];
+            sB = cj[0]; sQB = cj[1];
+        }
+        C /= ci[0] * sB;
+        Q /= ci[1] * sQB;
+        W /= ci[2] * sB;
+        // undo the centring: a = a' + mean_a, g(b) = b' + mean_b
+        const double sa_c = Sa - n * mua, sb_c = Sb - n * mub;   // sum a', sum b' (~0)
+        S1 = C + mua * sb_c + mub * sa_c + n * mua * mub;
+        // sum a b ycen = W + mean_a sum b' ycen + mean_b sum a' ycen + mean_a mean_b sum ycen;
+        // sum ycen is the rounding residue of fl32(y - mean y) (~1e-8 sqrt(n)) and is dropped,
+        // which also makes sum a' ycen = sum a ycen.
+        S3 = W + mua * Ub + mub * Ua;
     }
+    out[e] = S1;
+    out[kTilePairs + e] = Q;
+    out[2 * kTilePairs + e] = S3;
 }
 
 // ---- host helpers ---------------------------------------------------------------------
@@ -535,15 +583,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-bool make_plane_map(CUtensorMap* map, const __half* base, int64_t ld, int64_t f) {
+bool make_plane_map(CUtensorMap* map, const __half* base, int64_t ld, int64_t fp) {
     auto enc = encode_fn();
     if (!enc) return false;
-    cuuint64_t dims[2] = {(cuuint64_t)ld, (cuuint64_t)f};
-    cuuint64_t strides[1] = {(cuuint64_t)ld * sizeof(__half)};
-    cuuint32_t box[2] = {(cuuint32_t)kGK, (cuuint32_t)kGT};
+    cuuint64_t dims[2] = {(cuuint64_t)fp, (cuuint64_t)ld};
+    cuuint64_t strides[1] = {(cuuint64_t)fp * sizeof(__half)};
+    cuuint32_t box[2] = {64, (cuuint32_t)kGK};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)base, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -576,9 +624,10 @@ bool gram_path_enabled(const Bucket& b) {
 
 cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoord* d_tiles64,
                                 const std::vector<TileCoord>& tiles64, bool recip, float eps,
-                                double* d_moments, cudaStream_t stream, int* host_err) {
+                                double* d_moments, cudaStream_t stream, int* host_err, int prep_mode) {
     *host_err = 0;
     const int64_t f = b.f, ld = b.ld, n = b.n;
+    const int64_t fp = (f + 63) / 64 * 64;
     const int nb128 = (int)((f + kGT - 1) / kGT);
     // 128-tiles that cover this shard's 64-tiles
     std::vector<int> lut((size_t)nb128 * nb128, -1);
@@ -599,9 +648,12 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     chunk = (chunk + kRowPad - 1) / kRowPad * kRowPad;
     const int n_chunks = (int)((ld + chunk - 1) / chunk);
 
-    // scratch: planes | partial | lut | tiles128 | colparts | cs | err/absmax
-    const int n_planes = recip ? P_COUNT : P_GH;  // the g planes exist only for divide
-    size_t planes_bytes = (size_t)n_planes * f * ld * sizeof(__half);
+    // scratch: planes | partial | lut | tiles128 | colparts | cs | err/absmax.  The plane
+    // region has room for the divide planes whenever this call or the next one needs them,
+    // so both moment groups of one scoring call see the same layout.
+    const bool g_planes = recip || prep_mode != GRAM_PREP_OWN;
+    const int n_planes = g_planes ? P_COUNT : P_GH;
+    size_t planes_bytes = (size_t)n_planes * fp * ld * sizeof(__half);
     size_t off_part = (planes_bytes + 255) / 256 * 256;
     size_t part_bytes = (size_t)n_chunks * nt * 3 * kGT * kGT * sizeof(float);
     size_t off_lut = (off_part + part_bytes + 255) / 256 * 256;
@@ -631,41 +683,57 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     if (e == cudaSuccess) e = cudaMemsetAsync(d_err, 0, 128, stream);
     if (e != cudaSuccess) return e;
 
-    // operand statistics, scales and planes
-    int64_t span = ((n + splits - 1) / splits + 255) / 256 * 256;
-    {
+    if (prep_mode != GRAM_PREP_DONE) {
+        // operand statistics, scales and planes (both groups' planes when asked)
+        const bool both = prep_mode == GRAM_PREP_BOTH;
+        int64_t span = ((n + splits - 1) / splits + 255) / 256 * 256;
+        {
+            KernelTimer timer(stream, GAFIME_KERNEL_GRAM_PREP);
+            e = cudaMemsetAsync(d_absmax, 0, sizeof(unsigned), stream);
+            if (e != cudaSuccess) return e;
+            absmax_kernel<<<2 * b.sm_count, 256, 0, stream>>>(cs.d_ycen, ld, d_absmax);
+            gram_colstats_kernel<<<dim3((unsigned)f, (unsigned)splits), 256, 0, stream>>>(
+                cs.d_x, ld, n, cs.d_ycen, (recip || both) ? 1 : 0, eps, span, colp);
+        }
+        unsigned h_absmax = 0;
+        e = cudaMemcpyAsync(&h_absmax, d_absmax, sizeof(unsigned), cudaMemcpyDeviceToHost, stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) return e;
+        float yabs = 0.0f;
+        memcpy(&yabs, &h_absmax, sizeof(float));
+        GramScaleArgs sa;
+        sa.part = colp;
+        sa.splits = splits;
+        sa.f = f;
+        sa.n = n;
+        sa.colstats = cs.d_col;
+        sa.ycen_absmax = (double)yabs;
+        sa.recip = (recip || both) ? 1 : 0;
+        sa.cs = d_cs;
+        GramPrepArgs pa;
+        pa.x = cs.d_x;
+        pa.ld = ld;
+        pa.n = n;
+        pa.f = f;
+        pa.fp = fp;
+        pa.ycen = cs.d_ycen;
+        pa.cs = d_cs;
+        pa.eps = eps;
+        pa.write_x = 1;
+        pa.write_g = (recip || both) ? 1 : 0;
+        pa.planes = planes;
         KernelTimer timer(stream, GAFIME_KERNEL_GRAM_PREP);
-        absmax_kernel<<<2 * b.sm_count, 256, 0, stream>>>(cs.d_ycen, ld, d_absmax);
-        gram_colstats_kernel<<<dim3((unsigned)f, (unsigned)splits), 256, 0, stream>>>(
-            cs.d_x, ld, n, cs.d_ycen, recip ? 1 : 0, eps, span, colp);
+        gram_scale_kernel<<<(unsigned)((f + 127) / 128), 128, 0, stream>>>(sa);
+        const int64_t prep_tiles = (fp / 32) * (ld / 32);
+        const int prep_blocks = (int)std::min<int64_t>(prep_tiles, 32 * (int64_t)b.sm_count);
+        gram_prep_kernel<<<prep_blocks, 256, 0, stream>>>(pa);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
     }
-    unsigned h_absmax = 0;
-    e = cudaMemcpyAsync(&h_absmax, d_absmax, sizeof(unsigned), cudaMemcpyDeviceToHost, stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
-    if (e != cudaSuccess) return e;
-    float yabs = 0.0f;
-    memcpy(&yabs, &h_absmax, sizeof(float));
-    GramScaleArgs sa;
-    sa.part = colp;
-    sa.splits = splits;
-    sa.f = f;
-    sa.n = n;
-    sa.colstats = cs.d_col;
-    sa.ycen_absmax = (double)yabs;
-    sa.recip = recip ? 1 : 0;
-    sa.cs = d_cs;
-    gram_scale_kernel<<<(unsigned)((f + 127) / 128), 128, 0, stream>>>(sa);
-    {
-        KernelTimer timer(stream, GAFIME_KERNEL_GRAM_PREP);
-        gram_prep_kernel<<<8 * b.sm_count, 256, 0, stream>>>(cs.d_x, ld, n, f, cs.d_ycen, cs.d_col, d_cs,
-                                                             recip ? 1 : 0, eps, planes);
-    }
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
 
     GramMaps maps;
     for (int p = 0; p < P_COUNT; ++p)
-        if (!make_plane_map(&maps.m[p], planes + (size_t)(p < n_planes ? p : 0) * f * ld, ld, f))
+        if (!make_plane_map(&maps.m[p], planes + (size_t)(p < n_planes ? p : 0) * fp * ld, ld, fp))
             return cudaErrorInvalidValue;
     GramArgs ga;
     ga.tiles = d_t128;
@@ -705,7 +773,7 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     ra.moments = d_moments;
     {
         KernelTimer timer(stream, GAFIME_KERNEL_GRAM_REDUCE);
-        gram_reduce_kernel<<<(unsigned)tiles64.size(), 256, 0, stream>>>(ra);
+        gram_reduce_kernel<<<dim3((unsigned)tiles64.size(), kTilePairs / 256), 256, 0, stream>>>(ra);
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
