@@ -110,11 +110,7 @@ bool valid_op(int op) { return op >= GAFIME_INTERACT_MULT && op <= GAFIME_INTERA
 // raw-column means, so it always asks for uncentred statistics.
 int prepare(Bucket& b, int center, int metric, ColumnStats& cs) {
     bool finite = true;
-    int st;
-    {
-        KernelTimer timer(b.stream, GAFIME_KERNEL_FINITE_CHECK);
-        st = check_finite(b, &finite);
-    }
+    int st = check_finite(b, &finite);  // computed at upload; a cached flag here
     if (st != GAFIME_SUCCESS) return st;
     if (!finite) return GAFIME_ERROR_INVALID_ARGS;
     KernelTimer timer(b.stream, GAFIME_KERNEL_COLUMN_STATS);

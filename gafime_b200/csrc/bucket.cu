@@ -308,17 +308,34 @@ int compute_column_stats(Bucket& b, bool centred, ColumnStats& out) {
     return GAFIME_SUCCESS;
 }
 
+// Whole-buffer check with float4 loads: pad rows are zero, so every element can be tested.
+__global__ void finite4_kernel(const float4* __restrict__ x, int64_t n4, int* __restrict__ flag) {
+    int bad = 0;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n4; e += (int64_t)gridDim.x * blockDim.x) {
+        float4 v = x[e];
+        bad |= !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(flag, 1);
+}
+
+// Checks the bucket's features and target once per upload (the result is kept until the
+// next upload replaces the data).
 int check_finite(Bucket& b, bool* all_finite) {
+    if (b.finite_state >= 0) {
+        *all_finite = b.finite_state == 1;
+        return GAFIME_SUCCESS;
+    }
     cudaError_t e = ensure(b.flags, 64);
     if (e != cudaSuccess) return status_from(e);
     int* flag = (int*)b.flags.ptr;
     cudaMemsetAsync(flag, 0, sizeof(int), b.stream);
-    finite_kernel<<<4 * b.sm_count, 256, 0, b.stream>>>(b.d_data, b.f + 1, b.ld, b.n, flag);
+    finite4_kernel<<<4 * b.sm_count, 256, 0, b.stream>>>((const float4*)b.d_data, (b.f + 1) * b.ld / 4, flag);
     int h = 0;
     e = cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, b.stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b.stream);
     if (e != cudaSuccess) return status_from(e);
     *all_finite = (h == 0);
+    b.finite_state = *all_finite ? 1 : 0;
     return GAFIME_SUCCESS;
 }
 
@@ -435,7 +452,12 @@ int gafime_contiguous_bucket_upload(ContiguousBucket bucket, const float* h_data
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(b->d_mask, h_mask, (size_t)b->n, cudaMemcpyHostToDevice, b->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
-    return status_from(e);
+    if (e != cudaSuccess) return status_from(e);
+    // validate the new data at ingest: the all-pairs calls accept finite input only
+    b->finite_state = -1;
+    bool finite = true;
+    KernelTimer timer(b->stream, GAFIME_KERNEL_FINITE_CHECK);
+    return check_finite(*b, &finite);
 }
 
 int gafime_contiguous_bucket_compute(ContiguousBucket bucket, int feature_a_idx, int feature_b_idx,

@@ -47,6 +47,7 @@ struct Bucket {
     uint8_t* d_mask = nullptr; // n bytes
     cudaStream_t stream = nullptr;
     double* h_pinned = nullptr;  // small pinned staging for stats
+    int finite_state = -1;       // -1 unknown, 0 some value is NaN/inf, 1 all finite (per upload)
     int sm_count = 148;
     // scratch
     DeviceBuf stats_part, stats, ycen, xcen, moments, cands, cands2, scores, flags, tiles, mi,
@@ -69,7 +70,7 @@ struct ColumnStats {
 };
 int compute_column_stats(Bucket& b, bool centred, ColumnStats& out);
 
-// Finite-input check over the first f columns + y; returns 1 if all finite.
+// Finite-input check over the features and y, run once per upload and cached.
 int check_finite(Bucket& b, bool* all_finite);
 
 // Column-statistics kernels of bucket.cu, declared for other translation units.

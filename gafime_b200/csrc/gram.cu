@@ -435,65 +435,91 @@ struct GramPrepArgs {
     __half* planes;           // plane p: [ld][fp] at planes + p * ld * fp
 };
 
-// Column-major fp32 -> row-major fp16 planes through a 32 x 32 shared-memory transpose;
-// rows at or beyond n and columns at or beyond f are zero in every plane.
+struct ColConst {
+    float sx, sq, sw, sg, sgq, mug, mu;
+    bool valid;
+};
+
+__device__ __forceinline__ ColConst col_const(const double* cs, int64_t c, int64_t f) {
+    ColConst k{0, 0, 0, 0, 0, 0, 0, c < f};
+    if (k.valid) {
+        const double* s = cs + c * 12;
+        k.sx = (float)s[0]; k.sq = (float)s[1]; k.sw = (float)s[2];
+        k.sg = (float)s[3]; k.sgq = (float)s[4]; k.mug = (float)s[5]; k.mu = (float)s[9];
+    }
+    return k;
+}
+
+// Column-major fp32 -> row-major fp16 planes through a 64-column x 32-row shared-memory
+// tile; each thread writes two adjacent columns (__half2, 128 B per warp store).  Rows at or
+// beyond n and columns at or beyond f are zero in every plane.
 __global__ void __launch_bounds__(256) gram_prep_kernel(GramPrepArgs a) {
-    __shared__ float xs[32][33];
+    __shared__ __align__(8) float xs[32][66];   // [row][column], even pitch for float2 reads
     __shared__ float ys[32];
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-    const int64_t n_ct = a.fp / 32, total = n_ct * (a.ld / 32);
+    const int64_t n_ct = a.fp / 64, total = n_ct * (a.ld / 32);
     const int64_t plane = a.ld * a.fp;
     for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
-        const int64_t c0 = (t % n_ct) * 32, r0 = (t / n_ct) * 32;
+        const int64_t c0 = (t % n_ct) * 64, r0 = (t / n_ct) * 32;
         __syncthreads();
         #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < 8; ++k) {
             const int64_t c = c0 + ty + 8 * k, r = r0 + tx;
-            xs[ty + 8 * k][tx] = (c < a.f && r < a.n) ? a.x[c * a.ld + r] : 0.0f;
+            xs[tx][ty + 8 * k] = (c < a.f && r < a.n) ? a.x[c * a.ld + r] : 0.0f;
         }
         if (ty == 0) ys[tx] = a.ycen[r0 + tx];
         __syncthreads();
-        const int64_t c = c0 + tx;
-        const bool cv = c < a.f;
-        float sx = 0, sq = 0, sw = 0, sg = 0, sgq = 0, mug = 0, mu = 0;
-        if (cv) {
-            const double* s = a.cs + c * 12;
-            sx = (float)s[0]; sq = (float)s[1]; sw = (float)s[2];
-            sg = (float)s[3]; sgq = (float)s[4]; mug = (float)s[5]; mu = (float)s[9];
-        }
+        const int64_t c = c0 + 2 * tx;
+        const ColConst k0 = col_const(a.cs, c, a.f), k1 = col_const(a.cs, c + 1, a.f);
         #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const int64_t r = r0 + ty + 8 * k;
-            const bool v = cv && r < a.n;
-            const float xv = xs[tx][ty + 8 * k];
+            const int rr = ty + 8 * k;
+            const int64_t r = r0 + rr;
+            const bool rv = r < a.n;
+            const float2 xv = *reinterpret_cast<const float2*>(&xs[rr][2 * tx]);
+            const float yv = ys[rr];
             const int64_t o = r * a.fp + c;
+            const bool v0 = rv && k0.valid, v1 = rv && k1.valid;
             const __half z = __float2half_rn(0.f);
             if (a.write_x) {
-                __half xh = z, xl = z, qh = z, ql = z, wh = z, wl = z;
-                if (v) {
-                    const float ap = xv - mu;
-                    split16(ap * sx, xh, xl);
-                    split16(xv * xv * sq, qh, ql);
-                    split16(ap * ys[ty + 8 * k] * sw, wh, wl);
+                __half h[6][2];
+                #pragma unroll
+                for (int q = 0; q < 6; ++q) h[q][0] = h[q][1] = z;
+                if (v0) {
+                    const float ap = xv.x - k0.mu;
+                    split16(ap * k0.sx, h[0][0], h[1][0]);
+                    split16(xv.x * xv.x * k0.sq, h[2][0], h[3][0]);
+                    split16(ap * yv * k0.sw, h[4][0], h[5][0]);
                 }
-                a.planes[P_XH * plane + o] = xh;
-                a.planes[P_XL * plane + o] = xl;
-                a.planes[P_QH * plane + o] = qh;
-                a.planes[P_QL * plane + o] = ql;
-                a.planes[P_WH * plane + o] = wh;
-                a.planes[P_WL * plane + o] = wl;
+                if (v1) {
+                    const float ap = xv.y - k1.mu;
+                    split16(ap * k1.sx, h[0][1], h[1][1]);
+                    split16(xv.y * xv.y * k1.sq, h[2][1], h[3][1]);
+                    split16(ap * yv * k1.sw, h[4][1], h[5][1]);
+                }
+                const int pl[6] = {P_XH, P_XL, P_QH, P_QL, P_WH, P_WL};
+                #pragma unroll
+                for (int q = 0; q < 6; ++q)
+                    *reinterpret_cast<__half2*>(&a.planes[pl[q] * plane + o]) = __halves2half2(h[q][0], h[q][1]);
             }
             if (a.write_g) {
-                __half gh = z, gl = z, gqh = z, gql = z;
-                if (v) {
-                    const float gv = safe_recip(xv, a.eps);
-                    split16((gv - mug) * sg, gh, gl);
-                    split16(gv * gv * sgq, gqh, gql);
+                __half h[4][2];
+                #pragma unroll
+                for (int q = 0; q < 4; ++q) h[q][0] = h[q][1] = z;
+                if (v0) {
+                    const float gv = safe_recip(xv.x, a.eps);
+                    split16((gv - k0.mug) * k0.sg, h[0][0], h[1][0]);
+                    split16(gv * gv * k0.sgq, h[2][0], h[3][0]);
                 }
-                a.planes[P_GH * plane + o] = gh;
-                a.planes[P_GL * plane + o] = gl;
-                a.planes[P_GQH * plane + o] = gqh;
-                a.planes[P_GQL * plane + o] = gql;
+                if (v1) {
+                    const float gv = safe_recip(xv.y, a.eps);
+                    split16((gv - k1.mug) * k1.sg, h[0][1], h[1][1]);
+                    split16(gv * gv * k1.sgq, h[2][1], h[3][1]);
+                }
+                const int pl[4] = {P_GH, P_GL, P_GQH, P_GQL};
+                #pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<__half2*>(&a.planes[pl[q] * plane + o]) = __halves2half2(h[q][0], h[q][1]);
             }
         }
     }
@@ -724,7 +750,7 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
         pa.planes = planes;
         KernelTimer timer(stream, GAFIME_KERNEL_GRAM_PREP);
         gram_scale_kernel<<<(unsigned)((f + 127) / 128), 128, 0, stream>>>(sa);
-        const int64_t prep_tiles = (fp / 32) * (ld / 32);
+        const int64_t prep_tiles = (fp / 64) * (ld / 32);
         const int prep_blocks = (int)std::min<int64_t>(prep_tiles, 32 * (int64_t)b.sm_count);
         gram_prep_kernel<<<prep_blocks, 256, 0, stream>>>(pa);
         e = cudaGetLastError();

@@ -129,7 +129,10 @@ cudaError_t merge_candidates(Cand* buf, Cand* tmp, int n_lists, int k_pad, int n
                              Cand** final_list, cudaStream_t stream) {
     (void)n_groups_unused;
     // group * k_pad <= 8192 entries (128 KB of shared memory)
-    int group = std::max(2, 8192 / k_pad);
+    // lists per CTA: as many as fit 8192 entries, but no more than the lists there are
+    int fit = std::max(2, 8192 / k_pad);
+    int group = 2;
+    while (group < fit && group < n_lists) group <<= 1;
     size_t smem = sizeof(Cand) * (size_t)group * k_pad;
     cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     Cand* src = buf;
