@@ -187,6 +187,9 @@ def measured_peaks():
 NCU_TRAFFIC_BYTES = {
     # profiles/pair_moments_config2.md: mul-group launch, 1.0298 GB read + 5.09 MB written
     ("config2", "pair_moments"): 1.0349e9,
+    # profiles/gram_tile_config2.md: 250k-row capture scaled to 1e6 rows, mean of the
+    # multiply (3.47 GB) and divide (5.52 GB) launches
+    ("config2", "gram_tc"): 4.5e9,
 }
 
 
