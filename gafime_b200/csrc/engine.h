@@ -97,8 +97,8 @@ cudaError_t launch_pair_moments(const float* d_x, int64_t ld, const float* d_yce
 // Tensor-core pair moments (gram.cu): the same S1/S2/S3 as launch_pair_moments for the
 // shard's 64-tiles, computed as tcgen05 Gram tiles over 128-blocks; writes one split
 // (splits = 1) into d_moments.  *host_err != 0 reports a bounded wait that gave up.
-// prep_mode: GRAM_PREP_OWN writes the operand planes this group needs, GRAM_PREP_BOTH
-// writes the planes of both groups (a divide group follows), GRAM_PREP_DONE reuses them.
+// prep_mode: GRAM_PREP_OWN computes the per-column scales this group needs, GRAM_PREP_BOTH
+// those of both groups (a divide group follows), GRAM_PREP_DONE reuses them.
 enum { GRAM_PREP_OWN = 0, GRAM_PREP_BOTH = 1, GRAM_PREP_DONE = 2 };
 bool gram_path_enabled(const Bucket& b);
 cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoord* d_tiles64,

@@ -7,28 +7,39 @@
 //     W = sum (a' ycen) b'    (ycen = y - mean y)
 // with g = identity (multiply; add / subtract reuse C) or g(b) = 1/safe(b) (divide).
 // They are computed by tcgen05.mma kind::f16 with fp32 accumulators in tensor memory
-// (TMEM columns 0-127: C, 128-255: Q, 256-383: W).  Operands are fp16 planes stored row-major
-// ([row][column], so a 16-row x 64-column TMA box is 16 runs of 128 B and the MMA reads
-// MN-major operands), prepared once per call by gram_prep_kernel with every column scaled by
-// a power of two so its largest magnitude is at most 2^14:
-//     XH = fp16(s a'),  XL = fp16(s a' - XH)          (2-term split, ~22 bits)
-//     QH/QL = 2-term split of s_q a^2
-//     WH/WL = 2-term split of s_w a' ycen
-//     GH/GL, GQH/GQL: the same for g(b) and g(b)^2 (divide only)
-// Each Gram is hi.hi + hi.lo + lo.hi (the lo.lo term is below fp32 rounding): nine MMAs per
-// 16-row step.  One fp16 term is not enough when a few rows dominate a sum (heavy tails,
-// near-zero divisors): their 2^-12 rounding would not average out.
+// (TMEM columns 0-127: C, 128-255: Q, 256-383: W).  Each fp16 operand is a 2-term split of
+// a per-column power-of-two-scaled value (|value| <= 2^14, ~22 significant bits):
+//     XH/XL = split(s_x a'),  QH/QL = split(s_q a^2),  WH/WL = split(s_x a' * s_y ycen)  (A)
+//     BH/BL, BQH/BQL: the same for the B block's b' and g(b)^2                          (B)
+// and each Gram is hi.hi + hi.lo + lo.hi (the lo.lo term is below fp32 rounding): nine MMAs
+// per 16-row step.  One fp16 term per operand is not enough when a few rows dominate a sum
+// (heavy tails, near-zero divisors): their 2^-12 rounding would not average out.
 //
-// Pipeline per CTA (one tile x one row chunk of <= 8192 rows, so each fp32 accumulation
-// stays short): warp 0 issues TMA copies (2-D tensor maps, 128-byte swizzle, no multicast)
-// of 10 operand tiles (two 64-column boxes each) per 16-row stage into a 5-stage ring; warp 1 issues the MMAs and
-// commits each stage back to its "empty" barrier; warps 2-5 drain TMEM (tcgen05.ld) into
-// fp32 partials [chunk][tile][C|Q|W][n][m] in HBM.  gram_reduce_kernel adds the chunks in
-// fp64 in a fixed order, undoes the scales and the centring, and writes the raw moments
-// S1 = sum a g(b), S2 = Q, S3 = sum a g(b) ycen that select.cu's epilogue scores.
+// One CTA = one tile x one chunk of <= 8192 rows (each fp32 accumulation stays short), 10
+// warps:
+//   warp 0      TMA: raw fp32 column tiles (128 columns x 16 rows, 64-byte swizzle, no
+//               multicast) of the A block and, off the diagonal, the B block, plus 16 scaled
+//               ycen values (plain bulk copy) -> 8-stage raw ring
+//   warp 1      TMEM allocation; one thread issues the nine MMAs of each step (A operands
+//               from tensor memory, B operands from shared memory) and commits the operand
+//               stage back to its "empty" barrier
+//   warps 2-9   two converter groups of 4 warps, taking alternate steps; one column of each
+//               block per thread, in the TMEM lane quarter of its warp: centre, scale and
+//               split the values, write the six A rows to tensor memory (tcgen05.st) and the
+//               four B rows to K-major fp16 tiles (32-byte swizzle) in shared memory.
+//               Diagonal tiles of the multiply group load and convert one block only.  After
+//               the last step group 0 drains TMEM (tcgen05.ld) into fp32 chunk partials.
+// Keeping A in tensor memory halves the shared-memory reads of the MMAs (shared-memory
+// bandwidth, not the tensor pipe, bounds a 128 x 128 tile with both operands there).  The
+// raw fp32 matrix is read once per tile and chunk (concurrent tiles of one chunk share it
+// through L2); no operand planes exist in HBM.
+// gram_reduce_kernel then adds the chunk partials in fp64 in a fixed order, undoes the scales
+// and the centring, and writes the raw moments S1 = sum a g(b), S2 = Q, S3 = sum a g(b) ycen
+// that select.cu's epilogue scores.
 //
-// Every mbarrier wait is bounded: on timeout the thread records an error code in err[0],
-// stops issuing work, drains what it issued, and the CTA frees its TMEM before returning.
+// Every mbarrier wait is bounded: on timeout the thread records an error code in err[0] and
+// stops; the MMA warp still commits the accumulator barrier, the producer drains its copies,
+// and the CTA frees its TMEM before returning.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp16.h>
@@ -38,6 +49,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -49,29 +61,37 @@ namespace gafime {
 namespace {
 
 constexpr int kGT = 128;                      // Gram tile edge (columns)
-constexpr int kGK = 16;                       // rows per pipeline stage (one MMA K step)
-constexpr int kGStages = 5;
-constexpr int kOpBytes = kGT * kGK * 2;       // one operand tile: 128 columns x 16 rows fp16
-constexpr int kNumA = 6, kNumB = 4;
-constexpr int kStageBytes = (kNumA + kNumB) * kOpBytes;
-constexpr int kGramThreads = 192;
+constexpr int kGK = 16;                       // rows per step (one MMA K step)
+constexpr int kRawStages = 8;
+constexpr int kOpStages = 2;                  // A operands in TMEM + B operands in shared memory
+constexpr int kRawBox = kGT * kGK * 4;        // one fp32 column tile: 128 columns x 16 rows
+constexpr int kRawStageBytes = 2 * kRawBox;   // A block + B block
+constexpr int kYsBytes = 64;                  // 16 scaled ycen values
+constexpr int kOpBytes = kGT * kGK * 2;       // one fp16 operand tile: 128 columns x 16 rows
+constexpr int kBStageBytes = 4 * kOpBytes;    // BH BL BQH BQL
+constexpr uint32_t kTmemA = 384;              // A operand stages after the C, Q, W accumulators
+constexpr uint32_t kTmemAStride = 64;         // XH XL QH QL WH WL: 8 columns each
+constexpr int kConvWarps = 4;                 // warps per converter group (one column per thread)
+constexpr int kGroups = 2;                    // converter groups, interleaved over the steps
+constexpr int kGramThreads = (2 + kGroups * kConvWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr long long kSpinLimit = 1LL << 24;
 constexpr int64_t kMaxChunkRows = 8192;
-
-enum Plane { P_XH = 0, P_XL, P_QH, P_QL, P_WH, P_WL, P_GH, P_GL, P_GQH, P_GQL, P_COUNT };
-
-struct GramMaps {
-    CUtensorMap m[P_COUNT];
-};
+constexpr size_t kGramSmem = (size_t)kRawStages * (kRawStageBytes + kYsBytes) + (size_t)kOpStages * kBStageBytes +
+                             1024 + 256;
+static_assert(kGramSmem <= 232448, "shared memory per CTA");
+static_assert(kTmemA + kOpStages * kTmemAStride <= kTmemCols, "tensor memory columns");
 
 struct GramArgs {
     const TileCoord* tiles;   // 128-blocks (bi, bj), bi <= bj
     int n_tiles;
     int64_t chunk_rows;       // multiple of kGK
     int64_t rows;             // padded rows (ld)
-    int a_plane[kNumA];       // XH, XL, QH, QL, WH, WL
-    int b_plane[kNumB];       // XH|GH, XL|GL, QH|GQH, QL|GQL
+    int64_t n, f;             // valid rows and columns
+    const float* ys;          // [ld] ycen * s_y (s_y: power of two, |ys| <= 1), zero beyond n
+    const double* cs;         // per-column scales and means (12 doubles per column)
+    int recip;                // B side is 1/safe(b)
+    float eps;
     float* partial;           // [chunk][tile][3][128 n][128 m]
     int* err;
 };
@@ -117,27 +137,76 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// Plain bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"((uint64_t)src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// MN-major operand tile, 128-byte swizzle: 64 columns (128 B) per swizzle row, 16 K rows;
-// the two 64-column halves of a 128-column tile are 2048 B apart (LBO) and the two 8-row K
-// groups 1024 B apart (SBO); descriptor version 1, layout code 2.
+// K-major operand tile with the 32-byte swizzle: 128 rows (columns of X) of 32 B (16 fp16
+// along K), 8-row groups 256 B apart (SBO), LBO unused (1), descriptor version 1, layout 6.
 __device__ __forceinline__ uint64_t umma_desc(uint32_t addr) {
-    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(2048 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(256 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)6 << 61);
 }
 
-// kind::f16 instruction descriptor: D f32, A/B f16, both MN-major, N = 128, M = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (1u << 15) | (1u << 16) |
-                            ((uint32_t)(kGT >> 3) << 17) | ((uint32_t)(kGT >> 4) << 24);
+// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N = 128, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kGT >> 3) << 17) |
+                            ((uint32_t)(kGT >> 4) << 24);
 
-__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void fence_async_smem() {
+    // make generic-proxy shared-memory writes visible to the tensor cores (async proxy)
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ float safe_recip(float v, float eps) {
+    float d = fabsf(v) < eps ? copysignf(eps, v) : v;
+    return __frcp_rn(d);
+}
+
+// 16 consecutive rows of one column -> hi and lo fp16 vectors (two 16-byte halves each)
+struct Split16 {
+    uint32_t hi[8], lo[8];
+};
+
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
+    __half2 h = __floats2half2_rn(a, b);
+    float2 hf = __half22float2(h);
+    __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);   // a - hi is exact in fp32
+    hi = *reinterpret_cast<uint32_t*>(&h);
+    lo = *reinterpret_cast<uint32_t*>(&l);
+}
+
+// Store a 16-row hi/lo pair of one column m into two K-major SW32 tiles: row m of the tile
+// is 32 B, its 16-byte halves (K 0-7, K 8-15) swapped when bit 2 of m is set.
+__device__ __forceinline__ void store_split(unsigned char* hi_tile, unsigned char* lo_tile, int m,
+                                            const Split16& s) {
+    const int sw = (m >> 2) & 1;
+    uint4* h0 = reinterpret_cast<uint4*>(hi_tile + m * 32 + 16 * (0 ^ sw));
+    uint4* h1 = reinterpret_cast<uint4*>(hi_tile + m * 32 + 16 * (1 ^ sw));
+    uint4* l0 = reinterpret_cast<uint4*>(lo_tile + m * 32 + 16 * (0 ^ sw));
+    uint4* l1 = reinterpret_cast<uint4*>(lo_tile + m * 32 + 16 * (1 ^ sw));
+    *h0 = make_uint4(s.hi[0], s.hi[1], s.hi[2], s.hi[3]);
+    *h1 = make_uint4(s.hi[4], s.hi[5], s.hi[6], s.hi[7]);
+    *l0 = make_uint4(s.lo[0], s.lo[1], s.lo[2], s.lo[3]);
+    *l1 = make_uint4(s.lo[4], s.lo[5], s.lo[6], s.lo[7]);
+}
+
+// A operand in tensor memory (lane = row m, 8 columns = 16 fp16 along K), B in shared memory
+__device__ __forceinline__ void umma_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(tmem_d), "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate)
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(kIdesc), "r"(accumulate)
         : "memory");
 }
 
@@ -163,29 +232,133 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int c = 0; c < 32; ++c) v[c] = __uint_as_float(r[c]);
 }
 
-// ---- the Gram kernel -------------------------------------------------------------
+// ---- the fused Gram kernel ---------------------------------------------------------
+
+// Bounded wait by lane 0 of a warp, then a warp barrier (which orders the other lanes'
+// later accesses after lane 0's acquire).  Warp-uniform result.
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int* err, int code, int lane) {
+    int ok = 1;
+    if (lane == 0) ok = mbar_wait(bar, parity, err, code) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    return ok != 0;
+}
+
+__device__ __forceinline__ void load16(const unsigned char* p, float (&v)[16]) {
+    #pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        float4 t = *reinterpret_cast<const float4*>(p + 16 * q);
+        v[4 * q + 0] = t.x;
+        v[4 * q + 1] = t.y;
+        v[4 * q + 2] = t.z;
+        v[4 * q + 3] = t.w;
+    }
+}
+
+// 2-term split of 16 values (rows of one column)
+__device__ __forceinline__ void split16v(const float (&v)[16], Split16& s) {
+    #pragma unroll
+    for (int r = 0; r < 16; r += 2) split_pair(v[r], v[r + 1], s.hi[r / 2], s.lo[r / 2]);
+}
+
+// The 16 rows of column m of a raw fp32 tile (64-byte swizzle: the 16-byte chunk q of
+// column m sits at position q ^ ((m >> 1) & 3)).
+__device__ __forceinline__ void load_raw(const unsigned char* tile, int m, float (&x)[16]) {
+    const int sw = (m >> 1) & 3;
+    #pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        float4 u = *reinterpret_cast<const float4*>(tile + m * 64 + 16 * (q ^ sw));
+        x[4 * q] = u.x;
+        x[4 * q + 1] = u.y;
+        x[4 * q + 2] = u.z;
+        x[4 * q + 3] = u.w;
+    }
+}
+
+// 8 consecutive 32-bit TMEM columns of this thread's lane (one K=16 fp16 row of an A tile)
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+
+// Per-column constants of one converter thread (all zero for columns beyond f).
+struct ConvCols {
+    float mus_a, sx_a, sq_a;   // A block: mean * s_x, s_x, s_q
+    float mus_b, sx_b, sq_b;   // B block: mean * s, s, s_q of b (multiply) or g(b) (divide)
+};
+
+// Operand rows of one column for one step: A planes (tensor memory) and B planes (shared)
+struct StepOps {
+    Split16 x, q, w;   // A: s_x a',  s_q a^2,  (s_x a') (s_y ycen)
+    Split16 b, bq;     // B: s b',    s_q g(b)^2
+};
+
+// Convert one step of one column (A block, and the B block when kB).  kMask zeroes rows at
+// or beyond `valid`.  fma(x, s, -mean*s) equals fl(x - mean) * s exactly (s is a power of
+// two).
+template <bool kMask, bool kB, bool kRecip>
+__device__ __forceinline__ void convert_step(const unsigned char* raw, const unsigned char* ysm, int m, int valid,
+                                             const ConvCols& k, float eps, StepOps& o) {
+    float x[16], v[16];
+    load_raw(raw, m, x);
+    #pragma unroll
+    for (int r = 0; r < 16; ++r) v[r] = (!kMask || r < valid) ? fmaf(x[r], k.sx_a, -k.mus_a) : 0.f;
+    split16v(v, o.x);
+    {
+        float ys[16];
+        load16(ysm, ys);
+        #pragma unroll
+        for (int r = 0; r < 16; ++r) v[r] *= ys[r];
+    }
+    split16v(v, o.w);
+    #pragma unroll
+    for (int r = 0; r < 16; ++r) v[r] = (!kMask || r < valid) ? x[r] * x[r] * k.sq_a : 0.f;
+    split16v(v, o.q);
+    if (kB) {
+        load_raw(raw + kRawBox, m, x);
+        if (kRecip) {
+            #pragma unroll
+            for (int r = 0; r < 16; ++r) x[r] = safe_recip(x[r], eps);
+        }
+        #pragma unroll
+        for (int r = 0; r < 16; ++r) v[r] = (!kMask || r < valid) ? fmaf(x[r], k.sx_b, -k.mus_b) : 0.f;
+        split16v(v, o.b);
+        #pragma unroll
+        for (int r = 0; r < 16; ++r) v[r] = (!kMask || r < valid) ? x[r] * x[r] * k.sq_b : 0.f;
+        split16v(v, o.bq);
+    }
+}
 
 __global__ void __launch_bounds__(kGramThreads, 1)
-gram_tile_kernel(const __grid_constant__ GramMaps maps, const GramArgs a) {
+gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
     extern __shared__ __align__(1024) unsigned char gsmem_raw[];
-    // 1024-byte alignment for the swizzled tiles
     unsigned char* smem = (unsigned char*)(((uintptr_t)gsmem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = (uint64_t*)(smem + kGStages * kStageBytes);   // full[S], empty[S], accum
-    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * kGStages + 1);
-    const uint32_t smem0 = smem_u32(smem);
-    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kGStages);
-    const uint32_t accum = smem_u32(bars + 2 * kGStages);
+    unsigned char* raw0 = smem;                                    // raw ring
+    unsigned char* bop0 = raw0 + kRawStages * kRawStageBytes;      // B operand ring
+    unsigned char* ys0 = bop0 + kOpStages * kBStageBytes;          // scaled ycen ring
+    uint64_t* bars = (uint64_t*)(ys0 + kRawStages * kYsBytes);
+    // raw_full[R], raw_empty[R], op_full[O], op_empty[O], accum
+    const uint32_t rfull0 = smem_u32(bars), rempty0 = smem_u32(bars + kRawStages);
+    const uint32_t ofull0 = smem_u32(bars + 2 * kRawStages), oempty0 = smem_u32(bars + 2 * kRawStages + kOpStages);
+    const uint32_t accum = smem_u32(bars + 2 * kRawStages + 2 * kOpStages);
+    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * kRawStages + 2 * kOpStages + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const TileCoord tc = a.tiles[blockIdx.x];
+    // the multiply group's diagonal tiles load and convert one block (A and B are the same)
+    const bool b_same = (tc.bi == tc.bj) && !a.recip;
     const int64_t r0 = (int64_t)blockIdx.y * a.chunk_rows;
     const int64_t r1 = min(r0 + a.chunk_rows, a.rows);
     const int nk = r1 > r0 ? (int)((r1 - r0) / kGK) : 0;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kGStages; ++s) {
-            mbar_init(full0 + 8 * s, 1);
-            mbar_init(empty0 + 8 * s, 1);
+        for (int s = 0; s < kRawStages; ++s) {
+            mbar_init(rfull0 + 8 * s, 1);
+            mbar_init(rempty0 + 8 * s, kConvWarps);
+        }
+        for (int s = 0; s < kOpStages; ++s) {
+            mbar_init(ofull0 + 8 * s, kConvWarps);
+            mbar_init(oempty0 + 8 * s, 1);
         }
         mbar_init(accum, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -204,82 +377,140 @@ gram_tile_kernel(const __grid_constant__ GramMaps maps, const GramArgs a) {
 
     if (warp == 0) {
         if (lane == 0) {
-            // producer: 10 operand tiles per stage
+            // producer: raw fp32 column tiles + 16 scaled ycen values per step
+            const uint32_t bytes = (b_same ? (uint32_t)kRawBox : (uint32_t)kRawStageBytes) + (uint32_t)(kGK * 4);
             int issued = 0;
             bool ok = true;
-            for (int k = 0; k < nk && ok; ++k) {
-                const int s = k % kGStages;
-                if (k >= kGStages) ok = mbar_wait(empty0 + 8 * s, ((k / kGStages) - 1) & 1, a.err, 1);
-                if (!ok) break;
-                const uint32_t full = full0 + 8 * s;
-                mbar_expect_tx(full, (uint32_t)kStageBytes);
-                const uint32_t st = smem0 + s * kStageBytes;
-                const int x = (int)(r0 + (int64_t)k * kGK);  // first row of the stage
-                #pragma unroll
-                for (int o = 0; o < kNumA; ++o)
-                    #pragma unroll
-                    for (int h = 0; h < 2; ++h)
-                        tma_load_2d(st + o * kOpBytes + h * (kOpBytes / 2), &maps.m[a.a_plane[o]], full,
-                                    tc.bi * kGT + h * 64, x);
-                #pragma unroll
-                for (int o = 0; o < kNumB; ++o)
-                    #pragma unroll
-                    for (int h = 0; h < 2; ++h)
-                        tma_load_2d(st + (kNumA + o) * kOpBytes + h * (kOpBytes / 2), &maps.m[a.b_plane[o]],
-                                    full, tc.bj * kGT + h * 64, x);
+            for (int k = 0; k < nk; ++k) {
+                const int s = k % kRawStages;
+                if (k >= kRawStages && !(ok = mbar_wait(rempty0 + 8 * s, ((k / kRawStages) - 1) & 1, a.err, 1)))
+                    break;
+                const uint32_t full = rfull0 + 8 * s;
+                mbar_expect_tx(full, bytes);
+                const uint32_t st = smem_u32(raw0 + s * kRawStageBytes);
+                const int64_t row = r0 + (int64_t)k * kGK;
+                tma_load_2d(st, &xmap, full, (int)row, tc.bi * kGT);
+                if (!b_same) tma_load_2d(st + kRawBox, &xmap, full, (int)row, tc.bj * kGT);
+                bulk_load(smem_u32(ys0 + s * kYsBytes), a.ys + row, (uint32_t)(kGK * 4), full);
                 ++issued;
             }
-            if (!ok) {
-                // drain: wait (bounded) for every stage that may still be filling
-                for (int k = max(0, issued - kGStages); k < issued; ++k)
-                    mbar_wait(full0 + 8 * (k % kGStages), (k / kGStages) & 1, a.err, 4);
-            }
+            if (!ok)
+                for (int k = max(0, issued - kRawStages); k < issued; ++k)
+                    mbar_wait(rfull0 + 8 * (k % kRawStages), (k / kRawStages) & 1, a.err, 4);
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            // MMA issuer
+            // MMA issuer: A operands from tensor memory, B operands from shared memory
             for (int k = 0; k < nk; ++k) {
-                const int s = k % kGStages;
-                if (!mbar_wait(full0 + 8 * s, (k / kGStages) & 1, a.err, 2)) break;
+                const int s = k % kOpStages;
+                if (!mbar_wait(ofull0 + 8 * s, (k / kOpStages) & 1, a.err, 2)) break;
                 tc_fence_after();
-                const uint32_t st = smem0 + s * kStageBytes;
-                const uint64_t aXH = umma_desc(st + 0 * kOpBytes), aXL = umma_desc(st + 1 * kOpBytes);
-                const uint64_t aQH = umma_desc(st + 2 * kOpBytes), aQL = umma_desc(st + 3 * kOpBytes);
-                const uint64_t aWH = umma_desc(st + 4 * kOpBytes), aWL = umma_desc(st + 5 * kOpBytes);
-                const uint64_t bH = umma_desc(st + 6 * kOpBytes), bL = umma_desc(st + 7 * kOpBytes);
-                const uint64_t bQH = umma_desc(st + 8 * kOpBytes), bQL = umma_desc(st + 9 * kOpBytes);
+                const uint32_t ta = tmem + kTmemA + (uint32_t)(s * kTmemAStride);
+                const uint32_t bst = smem_u32(bop0 + s * kBStageBytes);
+                const uint64_t bH = umma_desc(bst + 0 * kOpBytes), bL = umma_desc(bst + 1 * kOpBytes);
+                const uint64_t bQH = umma_desc(bst + 2 * kOpBytes), bQL = umma_desc(bst + 3 * kOpBytes);
                 const uint32_t acc = k > 0 ? 1u : 0u;
-                umma(tmem + 0, aXH, bH, acc);      // C: hi x hi
-                umma(tmem + 0, aXH, bL, 1u);       //    hi x lo
-                umma(tmem + 0, aXL, bH, 1u);       //    lo x hi
-                umma(tmem + 128, aQH, bQH, acc);   // Q
-                umma(tmem + 128, aQH, bQL, 1u);
-                umma(tmem + 128, aQL, bQH, 1u);
-                umma(tmem + 256, aWH, bH, acc);    // W
-                umma(tmem + 256, aWH, bL, 1u);
-                umma(tmem + 256, aWL, bH, 1u);
-                umma_commit(empty0 + 8 * s);  // stage free once these MMAs have read it
+                umma_ta(tmem + 0, ta + 0 * 8, bH, acc);      // C: XH.BH
+                umma_ta(tmem + 0, ta + 0 * 8, bL, 1u);       //    XH.BL
+                umma_ta(tmem + 0, ta + 1 * 8, bH, 1u);       //    XL.BH
+                umma_ta(tmem + 128, ta + 2 * 8, bQH, acc);   // Q: QH.BQH
+                umma_ta(tmem + 128, ta + 2 * 8, bQL, 1u);    //    QH.BQL
+                umma_ta(tmem + 128, ta + 3 * 8, bQH, 1u);    //    QL.BQH
+                umma_ta(tmem + 256, ta + 4 * 8, bH, acc);    // W: WH.BH
+                umma_ta(tmem + 256, ta + 4 * 8, bL, 1u);     //    WH.BL
+                umma_ta(tmem + 256, ta + 5 * 8, bH, 1u);     //    WL.BH
+                umma_commit(oempty0 + 8 * s);  // operand stage free once these MMAs have read it
             }
             umma_commit(accum);  // all issued MMAs complete (also on the error path)
         }
     } else {
-        // epilogue warps 2..5: TMEM lanes 32*(warp%4) .. +31 hold rows m of the tile.
-        // The outcome is made warp-uniform: tcgen05.ld below is a whole-warp instruction.
-        const bool ok = __all_sync(0xffffffffu, mbar_wait(accum, 0, a.err, 3));
-        tc_fence_after();
-        if (ok && nk > 0) {
-            const int q = warp & 3;
-            const int m = q * 32 + lane;
-            float* out = a.partial + ((int64_t)blockIdx.y * a.n_tiles + blockIdx.x) * 3 * kGT * kGT;
-            #pragma unroll 1
-            for (int g = 0; g < 3; ++g) {
+        // converter groups: group g (warps 2+4g .. 5+4g) converts the steps k = g mod kGroups.
+        // Thread = column m of the 128-column blocks, m in the TMEM lane quarter of its warp.
+        const int grp = (warp - 2) / kConvWarps;
+        const int quarter = warp & 3;
+        const int m = quarter * 32 + lane;
+        const uint32_t tlane = (uint32_t)(quarter * 32) << 16;
+        const int64_t col_a = (int64_t)tc.bi * kGT + m, col_b = (int64_t)tc.bj * kGT + m;
+        ConvCols kc{0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (col_a < a.f) {
+            const double* c = a.cs + col_a * 12;
+            kc.sx_a = (float)c[0];
+            kc.sq_a = (float)c[1];
+            kc.mus_a = (float)c[9] * kc.sx_a;
+        }
+        if (col_b < a.f) {
+            const double* c = a.cs + col_b * 12;
+            const int o = a.recip ? 3 : 0;
+            kc.sx_b = (float)c[o];
+            kc.sq_b = (float)c[o + 1];
+            kc.mus_b = (float)c[a.recip ? 5 : 9] * kc.sx_b;
+        }
+        for (int k = grp; k < nk; k += kGroups) {
+            const int rs = k % kRawStages, os = k % kOpStages;
+            if (!warp_wait(rfull0 + 8 * rs, (k / kRawStages) & 1, a.err, 5, lane)) break;
+            __syncwarp();
+            const int64_t left = a.n - (r0 + (int64_t)k * kGK);
+            const int valid = left <= 0 ? 0 : (left >= kGK ? kGK : (int)left);   // rows < n
+            const unsigned char* raw = raw0 + rs * kRawStageBytes;
+            const unsigned char* ysm = ys0 + rs * kYsBytes;
+            StepOps o;
+            if (valid == kGK) {
+                if (b_same) convert_step<false, false, false>(raw, ysm, m, valid, kc, a.eps, o);
+                else if (a.recip) convert_step<false, true, true>(raw, ysm, m, valid, kc, a.eps, o);
+                else convert_step<false, true, false>(raw, ysm, m, valid, kc, a.eps, o);
+            } else {
+                if (b_same) convert_step<true, false, false>(raw, ysm, m, valid, kc, a.eps, o);
+                else if (a.recip) convert_step<true, true, true>(raw, ysm, m, valid, kc, a.eps, o);
+                else convert_step<true, true, false>(raw, ysm, m, valid, kc, a.eps, o);
+            }
+            // the operand stage must be free: the MMAs of step k - kOpStages have completed
+            if (k >= kOpStages && !warp_wait(oempty0 + 8 * os, ((k / kOpStages) - 1) & 1, a.err, 6, lane)) break;
+            tc_fence_after();
+            const uint32_t ta = tmem + tlane + kTmemA + (uint32_t)(os * kTmemAStride);
+            tmem_st8(ta + 0 * 8, o.x.hi);
+            tmem_st8(ta + 1 * 8, o.x.lo);
+            tmem_st8(ta + 2 * 8, o.q.hi);
+            tmem_st8(ta + 3 * 8, o.q.lo);
+            tmem_st8(ta + 4 * 8, o.w.hi);
+            tmem_st8(ta + 5 * 8, o.w.lo);
+            unsigned char* sb = bop0 + os * kBStageBytes;
+            if (b_same) {
+                store_split(sb + 0 * kOpBytes, sb + 1 * kOpBytes, m, o.x);
+                store_split(sb + 2 * kOpBytes, sb + 3 * kOpBytes, m, o.q);
+            } else {
+                store_split(sb + 0 * kOpBytes, sb + 1 * kOpBytes, m, o.b);
+                store_split(sb + 2 * kOpBytes, sb + 3 * kOpBytes, m, o.bq);
+            }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            fence_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(ofull0 + 8 * os);
+                // The raw stage goes back to the producer only now: every value read from it
+                // has been consumed by the stores above (a release issued right after the
+                // shared loads let the next TMA copy overwrite the stage before those loads
+                // had completed).
+                mbar_arrive(rempty0 + 8 * rs);
+            }
+        }
+        if (grp == 0) {
+            // group 0 drains the accumulators: TMEM lanes 32*(warp%4) .. +31 are rows m
+            const bool done = warp_wait(accum, 0, a.err, 3, lane);
+            __syncwarp();
+            tc_fence_after();
+            if (done && nk > 0) {
+                float* out = a.partial + ((int64_t)blockIdx.y * a.n_tiles + blockIdx.x) * 3 * kGT * kGT;
                 #pragma unroll 1
-                for (int c0 = 0; c0 < kGT; c0 += 32) {
-                    float v[32];
-                    tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(g * kGT + c0), v);
-                    float* o = out + (int64_t)g * kGT * kGT + (int64_t)c0 * kGT + m;
-                    #pragma unroll
-                    for (int c = 0; c < 32; ++c) o[(int64_t)c * kGT] = v[c];
+                for (int gi = 0; gi < 3; ++gi) {
+                    #pragma unroll 1
+                    for (int c0 = 0; c0 < kGT; c0 += 32) {
+                        float tt[32];
+                        tmem_ld32(tmem + tlane + (uint32_t)(gi * kGT + c0), tt);
+                        float* op = out + (int64_t)gi * kGT * kGT + (int64_t)c0 * kGT + m;
+                        #pragma unroll
+                        for (int c = 0; c < 32; ++c) op[(int64_t)c * kGT] = tt[c];
+                    }
                 }
             }
         }
@@ -287,9 +518,9 @@ gram_tile_kernel(const __grid_constant__ GramMaps maps, const GramArgs a) {
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
-        // no MMA may still be writing TMEM when it is freed (bounded, returns at once
-        // when the accumulator barrier has already completed)
-        if (lane == 0) mbar_wait(accum, 0, a.err, 5);
+        // no MMA may still be writing TMEM when it is freed (bounded; returns at once when
+        // the accumulator barrier has completed)
+        if (lane == 0) mbar_wait(accum, 0, a.err, 7);
         __syncwarp();
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
@@ -297,18 +528,13 @@ gram_tile_kernel(const __grid_constant__ GramMaps maps, const GramArgs a) {
     }
 }
 
-// ---- operand preparation ------------------------------------------------------------
+// ---- per-column statistics and scales -------------------------------------------
 
 // Per column and row split: [0] min x, [1] max x, [2] sum g, [3] sum g^2, [4] sum g*ycen,
 // [5] min g, [6] max g
 struct GramColPart {
     double v[7];
 };
-
-__device__ __forceinline__ float safe_recip(float v, float eps) {
-    float d = fabsf(v) < eps ? copysignf(eps, v) : v;
-    return __frcp_rn(d);
-}
 
 __global__ void __launch_bounds__(256) gram_colstats_kernel(const float* __restrict__ x, int64_t ld, int64_t n,
                                                             const float* __restrict__ ycen, int recip,
@@ -354,15 +580,15 @@ __global__ void __launch_bounds__(256) gram_colstats_kernel(const float* __restr
 
 // Per-column scales and statistics of the operands:
 //   cs[c*12 + 0..4]: s_x, s_q, s_w, s_g, s_gq (powers of two)
-//   cs[c*12 + 5]: mean g rounded to fp32 (the value the planes subtract)
+//   cs[c*12 + 5]: mean g rounded to fp32 (the value the operand conversion subtracts)
 //   cs[c*12 + 6..8]: sum g, sum g^2, sum g*ycen
-//   cs[c*12 + 9]: mean x rounded to fp32 (the value the planes subtract)
+//   cs[c*12 + 9]: mean x rounded to fp32 (the value the operand conversion subtracts)
 struct GramScaleArgs {
     const GramColPart* part;
     int splits;
     int64_t f, n;
     const double* colstats;   // sum, sumsq, sum*ycen, mean per column
-    double ycen_absmax;
+    double s_y;               // power-of-two scale of ycen (|ycen * s_y| <= 1)
     int recip;
     double* cs;
 };
@@ -395,7 +621,7 @@ __global__ void gram_scale_kernel(GramScaleArgs a) {
     double* o = a.cs + c * 12;
     o[0] = pow2_scale(dev);
     o[1] = pow2_scale(fmax(mx * mx, mn * mn) * (1.0 + 1e-6));
-    o[2] = pow2_scale(dev * a.ycen_absmax * (1.0 + 1e-6));
+    o[2] = o[0] * a.s_y;   // W operand = (s_x a') * (s_y ycen)
     o[9] = mu;
     if (a.recip) {
         const double mug = (double)(float)(sg / (double)a.n);
@@ -412,117 +638,17 @@ __global__ void gram_scale_kernel(GramScaleArgs a) {
     o[8] = sgy;
 }
 
+__global__ void scale_rows_kernel(const float* __restrict__ v, int64_t n, float s, float* __restrict__ out) {
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x)
+        out[r] = v[r] * s;
+}
+
 __global__ void absmax_kernel(const float* __restrict__ v, int64_t n, unsigned* out_bits) {
     float m = 0.0f;
     for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x)
         m = fmaxf(m, fabsf(v[r]));
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((threadIdx.x & 31) == 0) atomicMax(out_bits, __float_as_uint(m));  // non-negative floats order as uints
-}
-
-__device__ __forceinline__ void split16(float v, __half& hi, __half& lo) {
-    hi = __float2half_rn(v);
-    lo = __float2half_rn(v - __half2float(hi));  // v - hi is exact in fp32
-}
-
-struct GramPrepArgs {
-    const float* x;           // column-major, ld rows per column
-    int64_t ld, n, f, fp;     // fp: row length of the planes (f rounded up to 64)
-    const float* ycen;
-    const double* cs;
-    float eps;
-    int write_x, write_g;     // which plane groups to write
-    __half* planes;           // plane p: [ld][fp] at planes + p * ld * fp
-};
-
-struct ColConst {
-    float sx, sq, sw, sg, sgq, mug, mu;
-    bool valid;
-};
-
-__device__ __forceinline__ ColConst col_const(const double* cs, int64_t c, int64_t f) {
-    ColConst k{0, 0, 0, 0, 0, 0, 0, c < f};
-    if (k.valid) {
-        const double* s = cs + c * 12;
-        k.sx = (float)s[0]; k.sq = (float)s[1]; k.sw = (float)s[2];
-        k.sg = (float)s[3]; k.sgq = (float)s[4]; k.mug = (float)s[5]; k.mu = (float)s[9];
-    }
-    return k;
-}
-
-// Column-major fp32 -> row-major fp16 planes through a 64-column x 32-row shared-memory
-// tile; each thread writes two adjacent columns (__half2, 128 B per warp store).  Rows at or
-// beyond n and columns at or beyond f are zero in every plane.
-__global__ void __launch_bounds__(256) gram_prep_kernel(GramPrepArgs a) {
-    __shared__ __align__(8) float xs[32][66];   // [row][column], even pitch for float2 reads
-    __shared__ float ys[32];
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-    const int64_t n_ct = a.fp / 64, total = n_ct * (a.ld / 32);
-    const int64_t plane = a.ld * a.fp;
-    for (int64_t t = blockIdx.x; t < total; t += gridDim.x) {
-        const int64_t c0 = (t % n_ct) * 64, r0 = (t / n_ct) * 32;
-        __syncthreads();
-        #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const int64_t c = c0 + ty + 8 * k, r = r0 + tx;
-            xs[tx][ty + 8 * k] = (c < a.f && r < a.n) ? a.x[c * a.ld + r] : 0.0f;
-        }
-        if (ty == 0) ys[tx] = a.ycen[r0 + tx];
-        __syncthreads();
-        const int64_t c = c0 + 2 * tx;
-        const ColConst k0 = col_const(a.cs, c, a.f), k1 = col_const(a.cs, c + 1, a.f);
-        #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const int rr = ty + 8 * k;
-            const int64_t r = r0 + rr;
-            const bool rv = r < a.n;
-            const float2 xv = *reinterpret_cast<const float2*>(&xs[rr][2 * tx]);
-            const float yv = ys[rr];
-            const int64_t o = r * a.fp + c;
-            const bool v0 = rv && k0.valid, v1 = rv && k1.valid;
-            const __half z = __float2half_rn(0.f);
-            if (a.write_x) {
-                __half h[6][2];
-                #pragma unroll
-                for (int q = 0; q < 6; ++q) h[q][0] = h[q][1] = z;
-                if (v0) {
-                    const float ap = xv.x - k0.mu;
-                    split16(ap * k0.sx, h[0][0], h[1][0]);
-                    split16(xv.x * xv.x * k0.sq, h[2][0], h[3][0]);
-                    split16(ap * yv * k0.sw, h[4][0], h[5][0]);
-                }
-                if (v1) {
-                    const float ap = xv.y - k1.mu;
-                    split16(ap * k1.sx, h[0][1], h[1][1]);
-                    split16(xv.y * xv.y * k1.sq, h[2][1], h[3][1]);
-                    split16(ap * yv * k1.sw, h[4][1], h[5][1]);
-                }
-                const int pl[6] = {P_XH, P_XL, P_QH, P_QL, P_WH, P_WL};
-                #pragma unroll
-                for (int q = 0; q < 6; ++q)
-                    *reinterpret_cast<__half2*>(&a.planes[pl[q] * plane + o]) = __halves2half2(h[q][0], h[q][1]);
-            }
-            if (a.write_g) {
-                __half h[4][2];
-                #pragma unroll
-                for (int q = 0; q < 4; ++q) h[q][0] = h[q][1] = z;
-                if (v0) {
-                    const float gv = safe_recip(xv.x, a.eps);
-                    split16((gv - k0.mug) * k0.sg, h[0][0], h[1][0]);
-                    split16(gv * gv * k0.sgq, h[2][0], h[3][0]);
-                }
-                if (v1) {
-                    const float gv = safe_recip(xv.y, a.eps);
-                    split16((gv - k1.mug) * k1.sg, h[0][1], h[1][1]);
-                    split16(gv * gv * k1.sgq, h[2][1], h[3][1]);
-                }
-                const int pl[4] = {P_GH, P_GL, P_GQH, P_GQL};
-                #pragma unroll
-                for (int q = 0; q < 4; ++q)
-                    *reinterpret_cast<__half2*>(&a.planes[pl[q] * plane + o]) = __halves2half2(h[q][0], h[q][1]);
-            }
-        }
-    }
 }
 
 // ---- reduce: chunks -> raw moments in the 64-tile layout of select.cu ----------------
@@ -569,7 +695,7 @@ __global__ void __launch_bounds__(256) gram_reduce_kernel(GramReduceArgs a) {
         }
         const double* ci = a.cs + i * 12;
         const double* cj = a.cs + j * 12;
-        const double mua = ci[9];                 // the mean the planes subtracted (fp32)
+        const double mua = ci[9];                 // the mean the operand conversion subtracted (fp32)
         const double Sa = a.colstats[i * 4 + 0], Ua = a.colstats[i * 4 + 2];
         double mub, Sb, Ub, sB, sQB;
         if (a.recip) {
@@ -609,15 +735,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-bool make_plane_map(CUtensorMap* map, const __half* base, int64_t ld, int64_t fp) {
+bool make_x_map(CUtensorMap* map, const float* base, int64_t ld, int64_t f) {
     auto enc = encode_fn();
     if (!enc) return false;
-    cuuint64_t dims[2] = {(cuuint64_t)fp, (cuuint64_t)ld};
-    cuuint64_t strides[1] = {(cuuint64_t)fp * sizeof(__half)};
-    cuuint32_t box[2] = {64, (cuuint32_t)kGK};
+    cuuint64_t dims[2] = {(cuuint64_t)ld, (cuuint64_t)f};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * sizeof(float)};
+    cuuint32_t box[2] = {(cuuint32_t)kGK, (cuuint32_t)kGT};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)base, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -653,7 +779,6 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
                                 double* d_moments, cudaStream_t stream, int* host_err, int prep_mode) {
     *host_err = 0;
     const int64_t f = b.f, ld = b.ld, n = b.n;
-    const int64_t fp = (f + 63) / 64 * 64;
     const int nb128 = (int)((f + kGT - 1) / kGT);
     // 128-tiles that cover this shard's 64-tiles
     std::vector<int> lut((size_t)nb128 * nb128, -1);
@@ -674,32 +799,28 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     chunk = (chunk + kRowPad - 1) / kRowPad * kRowPad;
     const int n_chunks = (int)((ld + chunk - 1) / chunk);
 
-    // scratch: planes | partial | lut | tiles128 | colparts | cs | err/absmax.  The plane
-    // region has room for the divide planes whenever this call or the next one needs them,
-    // so both moment groups of one scoring call see the same layout.
-    const bool g_planes = recip || prep_mode != GRAM_PREP_OWN;
-    const int n_planes = g_planes ? P_COUNT : P_GH;
-    size_t planes_bytes = (size_t)n_planes * fp * ld * sizeof(__half);
-    size_t off_part = (planes_bytes + 255) / 256 * 256;
+    // scratch: partial | lut | tiles128 | colparts | cs | err/absmax (same layout for both
+    // moment groups of one call, so the second group reuses the first one's statistics)
     size_t part_bytes = (size_t)n_chunks * nt * 3 * kGT * kGT * sizeof(float);
-    size_t off_lut = (off_part + part_bytes + 255) / 256 * 256;
+    size_t off_lut = (part_bytes + 255) / 256 * 256;
     size_t off_t128 = (off_lut + lut.size() * sizeof(int) + 255) / 256 * 256;
     int splits = (int)std::max<int64_t>(1, std::min<int64_t>((4 * (int64_t)b.sm_count + f - 1) / f,
                                                              (n + 4095) / 4096));
     splits = std::min(splits, 256);
     size_t off_colp = (off_t128 + t128.size() * sizeof(TileCoord) + 255) / 256 * 256;
     size_t off_cs = (off_colp + (size_t)f * splits * sizeof(GramColPart) + 255) / 256 * 256;
-    size_t off_err = (off_cs + (size_t)f * 12 * sizeof(double) + 255) / 256 * 256;
+    size_t off_ys = (off_cs + (size_t)f * 12 * sizeof(double) + 255) / 256 * 256;
+    size_t off_err = (off_ys + (size_t)ld * sizeof(float) + 255) / 256 * 256;
     size_t total = off_err + 256;
     cudaError_t e = ensure(b.gram, total);
     if (e != cudaSuccess) return e;
     char* base = (char*)b.gram.ptr;
-    __half* planes = (__half*)base;
-    float* partial = (float*)(base + off_part);
+    float* partial = (float*)base;
     int* d_lut = (int*)(base + off_lut);
     TileCoord* d_t128 = (TileCoord*)(base + off_t128);
     GramColPart* colp = (GramColPart*)(base + off_colp);
     double* d_cs = (double*)(base + off_cs);
+    float* d_ys = (float*)(base + off_ys);
     int* d_err = (int*)(base + off_err);
     unsigned* d_absmax = (unsigned*)(base + off_err + 64);
 
@@ -710,7 +831,7 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     if (e != cudaSuccess) return e;
 
     if (prep_mode != GRAM_PREP_DONE) {
-        // operand statistics, scales and planes (both groups' planes when asked)
+        // per-column ranges (and the divide side's sums) -> power-of-two scales
         const bool both = prep_mode == GRAM_PREP_BOTH;
         int64_t span = ((n + splits - 1) / splits + 255) / 256 * 256;
         {
@@ -727,58 +848,49 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
         if (e != cudaSuccess) return e;
         float yabs = 0.0f;
         memcpy(&yabs, &h_absmax, sizeof(float));
+        // s_y: the largest power of two with s_y * max|ycen| <= 1 (1 for a zero target)
+        double s_y = 1.0;
+        if (yabs > 0.0f && std::isfinite(yabs)) {
+            int ex;
+            frexp(1.0 / (double)yabs, &ex);
+            s_y = ldexp(1.0, ex - 1);
+        }
         GramScaleArgs sa;
         sa.part = colp;
         sa.splits = splits;
         sa.f = f;
         sa.n = n;
         sa.colstats = cs.d_col;
-        sa.ycen_absmax = (double)yabs;
+        sa.s_y = s_y;
         sa.recip = (recip || both) ? 1 : 0;
         sa.cs = d_cs;
-        GramPrepArgs pa;
-        pa.x = cs.d_x;
-        pa.ld = ld;
-        pa.n = n;
-        pa.f = f;
-        pa.fp = fp;
-        pa.ycen = cs.d_ycen;
-        pa.cs = d_cs;
-        pa.eps = eps;
-        pa.write_x = 1;
-        pa.write_g = (recip || both) ? 1 : 0;
-        pa.planes = planes;
         KernelTimer timer(stream, GAFIME_KERNEL_GRAM_PREP);
         gram_scale_kernel<<<(unsigned)((f + 127) / 128), 128, 0, stream>>>(sa);
-        const int64_t prep_tiles = (fp / 64) * (ld / 32);
-        const int prep_blocks = (int)std::min<int64_t>(prep_tiles, 32 * (int64_t)b.sm_count);
-        gram_prep_kernel<<<prep_blocks, 256, 0, stream>>>(pa);
+        scale_rows_kernel<<<2 * b.sm_count, 256, 0, stream>>>(cs.d_ycen, ld, (float)s_y, d_ys);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
 
-    GramMaps maps;
-    for (int p = 0; p < P_COUNT; ++p)
-        if (!make_plane_map(&maps.m[p], planes + (size_t)(p < n_planes ? p : 0) * fp * ld, ld, fp))
-            return cudaErrorInvalidValue;
+    CUtensorMap xmap;
+    if (!make_x_map(&xmap, cs.d_x, ld, f)) return cudaErrorInvalidValue;
     GramArgs ga;
     ga.tiles = d_t128;
     ga.n_tiles = nt;
     ga.chunk_rows = chunk;
     ga.rows = ld;
-    const int a_planes[kNumA] = {P_XH, P_XL, P_QH, P_QL, P_WH, P_WL};
-    const int b_planes[kNumB] = {recip ? P_GH : P_XH, recip ? P_GL : P_XL, recip ? P_GQH : P_QH,
-                                 recip ? P_GQL : P_QL};
-    for (int o = 0; o < kNumA; ++o) ga.a_plane[o] = a_planes[o];
-    for (int o = 0; o < kNumB; ++o) ga.b_plane[o] = b_planes[o];
+    ga.n = n;
+    ga.f = f;
+    ga.ys = d_ys;
+    ga.cs = d_cs;
+    ga.recip = recip ? 1 : 0;
+    ga.eps = eps;
     ga.partial = partial;
     ga.err = d_err;
-    const size_t smem = (size_t)kGStages * kStageBytes + 1024 + 256;
-    e = cudaFuncSetAttribute(gram_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    e = cudaFuncSetAttribute(gram_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGramSmem);
     if (e != cudaSuccess) return e;
     {
         KernelTimer timer(stream, GAFIME_KERNEL_GRAM_TC);
-        gram_tile_kernel<<<dim3((unsigned)nt, (unsigned)n_chunks), kGramThreads, smem, stream>>>(maps, ga);
+        gram_fused_kernel<<<dim3((unsigned)nt, (unsigned)n_chunks), kGramThreads, kGramSmem, stream>>>(xmap, ga);
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
