@@ -71,11 +71,13 @@ constexpr int kOpBytes = kGT * kGK * 2;       // one fp16 operand tile: 128 colu
 constexpr int kBStageBytes = 4 * kOpBytes;    // BH BL BQH BQL
 constexpr uint32_t kTmemA = 384;              // A operand stages after the C, Q, W accumulators
 constexpr uint32_t kTmemAStride = 64;         // XH XL QH QL WH WL: 8 columns each
-constexpr int kConvWarps = 4;                 // warps per converter group (one column per thread)
+constexpr int kConvWarps = 8;                 // warps per converter group (column x K half per thread)
 constexpr int kGroups = 2;                    // converter groups, interleaved over the steps
 constexpr int kGramThreads = (2 + kGroups * kConvWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr long long kSpinLimit = 1LL << 24;
+constexpr uint32_t kSuspendNs = 20000;           // try_wait suspend-time hint
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s: a wait this long is a fault
 constexpr int64_t kMaxChunkRows = 8192;
 constexpr size_t kGramSmem = (size_t)kRawStages * (kRawStageBytes + kYsBytes) + (size_t)kOpStages * kBStageBytes +
                              1024 + 256;
@@ -112,20 +114,33 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
 
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
+    // the suspend-time hint lets the thread sleep until the phase completes (or the hint
+    // expires) instead of spinning on the issue slots the converter warps need
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(kSuspendNs)
         : "memory");
     return ok != 0;
 }
 
-// Bounded wait: true when the phase completed, false (error recorded) on timeout.
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait: true when the phase completed, false (error recorded) after kWaitLimitNs of
+// wall time or kSpinLimit attempts, whichever comes first.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
-    for (long long i = 0; i < kSpinLimit; ++i)
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (long long i = 1; i < kSpinLimit; ++i) {
         if (mbar_try(bar, parity)) return true;
+        if ((i & 15) == 0 && global_ns() - t0 > kWaitLimitNs) break;
+    }
     atomicCAS(err, 0, code);
     return false;
 }
@@ -172,34 +187,6 @@ __device__ __forceinline__ float safe_recip(float v, float eps) {
     return __frcp_rn(d);
 }
 
-// 16 consecutive rows of one column -> hi and lo fp16 vectors (two 16-byte halves each)
-struct Split16 {
-    uint32_t hi[8], lo[8];
-};
-
-__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
-    __half2 h = __floats2half2_rn(a, b);
-    float2 hf = __half22float2(h);
-    __half2 l = __floats2half2_rn(a - hf.x, b - hf.y);   // a - hi is exact in fp32
-    hi = *reinterpret_cast<uint32_t*>(&h);
-    lo = *reinterpret_cast<uint32_t*>(&l);
-}
-
-// Store a 16-row hi/lo pair of one column m into two K-major SW32 tiles: row m of the tile
-// is 32 B, its 16-byte halves (K 0-7, K 8-15) swapped when bit 2 of m is set.
-__device__ __forceinline__ void store_split(unsigned char* hi_tile, unsigned char* lo_tile, int m,
-                                            const Split16& s) {
-    const int sw = (m >> 2) & 1;
-    uint4* h0 = reinterpret_cast<uint4*>(hi_tile + m * 32 + 16 * (0 ^ sw));
-    uint4* h1 = reinterpret_cast<uint4*>(hi_tile + m * 32 + 16 * (1 ^ sw));
-    uint4* l0 = reinterpret_cast<uint4*>(lo_tile + m * 32 + 16 * (0 ^ sw));
-    uint4* l1 = reinterpret_cast<uint4*>(lo_tile + m * 32 + 16 * (1 ^ sw));
-    *h0 = make_uint4(s.hi[0], s.hi[1], s.hi[2], s.hi[3]);
-    *h1 = make_uint4(s.hi[4], s.hi[5], s.hi[6], s.hi[7]);
-    *l0 = make_uint4(s.lo[0], s.lo[1], s.lo[2], s.lo[3]);
-    *l1 = make_uint4(s.lo[4], s.lo[5], s.lo[6], s.lo[7]);
-}
-
 // A operand in tensor memory (lane = row m, 8 columns = 16 fp16 along K), B in shared memory
 __device__ __forceinline__ void umma_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t accumulate) {
     asm volatile(
@@ -234,8 +221,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 // ---- the fused Gram kernel ---------------------------------------------------------
 
-// Bounded wait by lane 0 of a warp, then a warp barrier (which orders the other lanes'
-// later accesses after lane 0's acquire).  Warp-uniform result.
+// Bounded wait by lane 0 of a warp; the shuffle makes the outcome warp-uniform and orders
+// the other lanes' later accesses after lane 0's acquire.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int* err, int code, int lane) {
     int ok = 1;
     if (lane == 0) ok = mbar_wait(bar, parity, err, code) ? 1 : 0;
@@ -243,30 +230,31 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int* er
     return ok != 0;
 }
 
-__device__ __forceinline__ void load16(const unsigned char* p, float (&v)[16]) {
+// 8 consecutive rows (one K half) of one column as hi and lo fp16 pairs
+struct Split8 {
+    uint32_t hi[4], lo[4];
+};
+
+// 2-term split of 8 values: hi = fp16(v), lo = fp16(v - hi) (v - hi is exact in fp32, and
+// |v - hi| <= 2^-11 |v|, so hi + lo carries ~22 significant bits).
+__device__ __forceinline__ void split8(const float (&v)[8], Split8& s) {
     #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        float4 t = *reinterpret_cast<const float4*>(p + 16 * q);
-        v[4 * q + 0] = t.x;
-        v[4 * q + 1] = t.y;
-        v[4 * q + 2] = t.z;
-        v[4 * q + 3] = t.w;
+    for (int r = 0; r < 8; r += 2) {
+        __half2 h = __floats2half2_rn(v[r], v[r + 1]);
+        const float2 hf = __half22float2(h);
+        __half2 l = __floats2half2_rn(v[r] - hf.x, v[r + 1] - hf.y);
+        s.hi[r / 2] = *reinterpret_cast<uint32_t*>(&h);
+        s.lo[r / 2] = *reinterpret_cast<uint32_t*>(&l);
     }
 }
 
-// 2-term split of 16 values (rows of one column)
-__device__ __forceinline__ void split16v(const float (&v)[16], Split16& s) {
-    #pragma unroll
-    for (int r = 0; r < 16; r += 2) split_pair(v[r], v[r + 1], s.hi[r / 2], s.lo[r / 2]);
-}
-
-// The 16 rows of column m of a raw fp32 tile (64-byte swizzle: the 16-byte chunk q of
+// Rows 8h .. 8h+7 of column m of a raw fp32 tile (64-byte swizzle: the 16-byte chunk q of
 // column m sits at position q ^ ((m >> 1) & 3)).
-__device__ __forceinline__ void load_raw(const unsigned char* tile, int m, float (&x)[16]) {
+__device__ __forceinline__ void load_raw8(const unsigned char* tile, int m, int h, float (&x)[8]) {
     const int sw = (m >> 1) & 3;
     #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        float4 u = *reinterpret_cast<const float4*>(tile + m * 64 + 16 * (q ^ sw));
+    for (int q = 0; q < 2; ++q) {
+        float4 u = *reinterpret_cast<const float4*>(tile + m * 64 + 16 * ((2 * h + q) ^ sw));
         x[4 * q] = u.x;
         x[4 * q + 1] = u.y;
         x[4 * q + 2] = u.z;
@@ -274,10 +262,16 @@ __device__ __forceinline__ void load_raw(const unsigned char* tile, int m, float
     }
 }
 
-// 8 consecutive 32-bit TMEM columns of this thread's lane (one K=16 fp16 row of an A tile)
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
-                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+// K half h of row m of a K-major fp16 tile with the 32-byte swizzle (halves swapped when
+// bit 2 of m is set)
+__device__ __forceinline__ void store_half(unsigned char* tile, int m, int h, const uint32_t (&v)[4]) {
+    *reinterpret_cast<uint4*>(tile + m * 32 + 16 * (h ^ ((m >> 2) & 1))) = make_uint4(v[0], v[1], v[2], v[3]);
+}
+
+// 4 consecutive 32-bit TMEM columns of this thread's lane (one K half of an A row)
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&v)[4]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(v[0]), "r"(v[1]),
+                 "r"(v[2]), "r"(v[3])
                  : "memory");
 }
 
@@ -287,45 +281,108 @@ struct ConvCols {
     float mus_b, sx_b, sq_b;   // B block: mean * s, s, s_q of b (multiply) or g(b) (divide)
 };
 
-// Operand rows of one column for one step: A planes (tensor memory) and B planes (shared)
+// Operand rows of one column and K half for one step
 struct StepOps {
-    Split16 x, q, w;   // A: s_x a',  s_q a^2,  (s_x a') (s_y ycen)
-    Split16 b, bq;     // B: s b',    s_q g(b)^2
+    Split8 x, q, w;   // A: s_x a',  s_q a^2,  (s_x a') (s_y ycen)
+    Split8 b, bq;     // B: s b',    s_q g(b)^2
 };
 
-// Convert one step of one column (A block, and the B block when kB).  kMask zeroes rows at
-// or beyond `valid`.  fma(x, s, -mean*s) equals fl(x - mean) * s exactly (s is a power of
-// two).
+// Convert K half h of column m for one step (A block, and the B block when kB).  kMask
+// zeroes rows at or beyond `valid`.  fma(x, s, -mean*s) equals fl(x - mean) * s exactly (s
+// is a power of two).
 template <bool kMask, bool kB, bool kRecip>
-__device__ __forceinline__ void convert_step(const unsigned char* raw, const unsigned char* ysm, int m, int valid,
-                                             const ConvCols& k, float eps, StepOps& o) {
-    float x[16], v[16];
-    load_raw(raw, m, x);
+__device__ __forceinline__ void convert_step(const unsigned char* raw, const unsigned char* ysm, int m, int h,
+                                             int valid, const ConvCols& k, float eps, StepOps& o) {
+    float x[8], v[8];
+    load_raw8(raw, m, h, x);
     #pragma unroll
-    for (int r = 0; r < 16; ++r) v[r] = (!kMask || r < valid) ? fmaf(x[r], k.sx_a, -k.mus_a) : 0.f;
-    split16v(v, o.x);
+    for (int r = 0; r < 8; ++r) v[r] = (!kMask || 8 * h + r < valid) ? fmaf(x[r], k.sx_a, -k.mus_a) : 0.f;
+    split8(v, o.x);
     {
-        float ys[16];
-        load16(ysm, ys);
-        #pragma unroll
-        for (int r = 0; r < 16; ++r) v[r] *= ys[r];
+        const float4 y0 = *reinterpret_cast<const float4*>(ysm + 32 * h);
+        const float4 y1 = *reinterpret_cast<const float4*>(ysm + 32 * h + 16);
+        v[0] *= y0.x; v[1] *= y0.y; v[2] *= y0.z; v[3] *= y0.w;
+        v[4] *= y1.x; v[5] *= y1.y; v[6] *= y1.z; v[7] *= y1.w;
     }
-    split16v(v, o.w);
+    split8(v, o.w);
     #pragma unroll
-    for (int r = 0; r < 16; ++r) v[r] = (!kMask || r < valid) ? x[r] * x[r] * k.sq_a : 0.f;
-    split16v(v, o.q);
+    for (int r = 0; r < 8; ++r) v[r] = (!kMask || 8 * h + r < valid) ? x[r] * x[r] * k.sq_a : 0.f;
+    split8(v, o.q);
     if (kB) {
-        load_raw(raw + kRawBox, m, x);
+        load_raw8(raw + kRawBox, m, h, x);
         if (kRecip) {
             #pragma unroll
-            for (int r = 0; r < 16; ++r) x[r] = safe_recip(x[r], eps);
+            for (int r = 0; r < 8; ++r) x[r] = safe_recip(x[r], eps);
         }
         #pragma unroll
-        for (int r = 0; r < 16; ++r) v[r] = (!kMask || r < valid) ? fmaf(x[r], k.sx_b, -k.mus_b) : 0.f;
-        split16v(v, o.b);
+        for (int r = 0; r < 8; ++r) v[r] = (!kMask || 8 * h + r < valid) ? fmaf(x[r], k.sx_b, -k.mus_b) : 0.f;
+        split8(v, o.b);
         #pragma unroll
-        for (int r = 0; r < 16; ++r) v[r] = (!kMask || r < valid) ? x[r] * x[r] * k.sq_b : 0.f;
-        split16v(v, o.bq);
+        for (int r = 0; r < 8; ++r) v[r] = (!kMask || 8 * h + r < valid) ? x[r] * x[r] * k.sq_b : 0.f;
+        split8(v, o.bq);
+    }
+}
+
+// Shared-memory and tensor-memory addresses of one converter thread
+struct ConvCtx {
+    const unsigned char* raw0;   // raw ring
+    const unsigned char* ys0;    // scaled ycen ring
+    unsigned char* bop0;         // B operand ring
+    uint32_t rfull0, rempty0, ofull0, oempty0;
+    uint32_t tmem_a;             // tmem + lane quarter + kTmemA + 4h
+    int m, h, lane;
+    int nk, n_full;              // steps in the chunk; steps with all 16 rows below n
+    int64_t rows_left;           // n - first row of the chunk
+    float eps;
+    int* err;
+};
+
+// The steps k = grp, grp + kGroups, ... of one converter thread.  kB: convert the B block
+// (off the multiply group's diagonal); kRecip: the B operand is 1/safe(b).
+template <bool kB, bool kRecip>
+__device__ __forceinline__ void conv_loop(const ConvCtx& c, const ConvCols& kc, int grp) {
+    for (int k = grp; k < c.nk; k += kGroups) {
+        const int rs = k % kRawStages, os = k % kOpStages;
+        if (!warp_wait(c.rfull0 + 8 * rs, (k / kRawStages) & 1, c.err, 5, c.lane)) return;
+        const unsigned char* raw = c.raw0 + rs * kRawStageBytes;
+        const unsigned char* ysm = c.ys0 + rs * kYsBytes;
+        StepOps o;
+        if (k < c.n_full) {
+            convert_step<false, kB, kRecip>(raw, ysm, c.m, c.h, kGK, kc, c.eps, o);
+        } else {
+            const int64_t left = c.rows_left - (int64_t)k * kGK;
+            const int valid = left <= 0 ? 0 : (int)left;   // < kGK here
+            convert_step<true, kB, kRecip>(raw, ysm, c.m, c.h, valid, kc, c.eps, o);
+        }
+        // the operand stage must be free: the MMAs of step k - kOpStages have completed
+        if (k >= kOpStages && !warp_wait(c.oempty0 + 8 * os, ((k / kOpStages) - 1) & 1, c.err, 6, c.lane)) return;
+        tc_fence_after();
+        const uint32_t ta = c.tmem_a + (uint32_t)(os * kTmemAStride);
+        tmem_st4(ta + 0 * 8, o.x.hi);
+        tmem_st4(ta + 1 * 8, o.x.lo);
+        tmem_st4(ta + 2 * 8, o.q.hi);
+        tmem_st4(ta + 3 * 8, o.q.lo);
+        tmem_st4(ta + 4 * 8, o.w.hi);
+        tmem_st4(ta + 5 * 8, o.w.lo);
+        unsigned char* sb = c.bop0 + os * kBStageBytes;
+        const Split8& b0 = kB ? o.b : o.x;
+        const Split8& b1 = kB ? o.bq : o.q;
+        store_half(sb + 0 * kOpBytes, c.m, c.h, b0.hi);
+        store_half(sb + 1 * kOpBytes, c.m, c.h, b0.lo);
+        store_half(sb + 2 * kOpBytes, c.m, c.h, b1.hi);
+        store_half(sb + 3 * kOpBytes, c.m, c.h, b1.lo);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (c.lane == 0) {
+            mbar_arrive(c.ofull0 + 8 * os);
+            // The raw stage goes back to the producer only now: every value read from it
+            // has been consumed by the stores above (a release issued right after the
+            // shared loads let the next TMA copy overwrite the stage before those loads
+            // had completed).
+            mbar_arrive(c.rempty0 + 8 * rs);
+        }
     }
 }
 
@@ -424,10 +481,13 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
             umma_commit(accum);  // all issued MMAs complete (also on the error path)
         }
     } else {
-        // converter groups: group g (warps 2+4g .. 5+4g) converts the steps k = g mod kGroups.
-        // Thread = column m of the 128-column blocks, m in the TMEM lane quarter of its warp.
+        // converter groups: group g (warps 2+8g .. 9+8g) converts the steps k = g mod kGroups.
+        // Thread = column m of the 128-column blocks (m in the TMEM lane quarter of its warp)
+        // and K half h (rows 8h .. 8h+7 of the step).
+        const int cw = (warp - 2) % kConvWarps;
         const int grp = (warp - 2) / kConvWarps;
         const int quarter = warp & 3;
+        const int h = cw >> 2;
         const int m = quarter * 32 + lane;
         const uint32_t tlane = (uint32_t)(quarter * 32) << 16;
         const int64_t col_a = (int64_t)tc.bi * kGT + m, col_b = (int64_t)tc.bj * kGT + m;
@@ -445,72 +505,44 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
             kc.sq_b = (float)c[o + 1];
             kc.mus_b = (float)c[a.recip ? 5 : 9] * kc.sx_b;
         }
-        for (int k = grp; k < nk; k += kGroups) {
-            const int rs = k % kRawStages, os = k % kOpStages;
-            if (!warp_wait(rfull0 + 8 * rs, (k / kRawStages) & 1, a.err, 5, lane)) break;
-            __syncwarp();
-            const int64_t left = a.n - (r0 + (int64_t)k * kGK);
-            const int valid = left <= 0 ? 0 : (left >= kGK ? kGK : (int)left);   // rows < n
-            const unsigned char* raw = raw0 + rs * kRawStageBytes;
-            const unsigned char* ysm = ys0 + rs * kYsBytes;
-            StepOps o;
-            if (valid == kGK) {
-                if (b_same) convert_step<false, false, false>(raw, ysm, m, valid, kc, a.eps, o);
-                else if (a.recip) convert_step<false, true, true>(raw, ysm, m, valid, kc, a.eps, o);
-                else convert_step<false, true, false>(raw, ysm, m, valid, kc, a.eps, o);
-            } else {
-                if (b_same) convert_step<true, false, false>(raw, ysm, m, valid, kc, a.eps, o);
-                else if (a.recip) convert_step<true, true, true>(raw, ysm, m, valid, kc, a.eps, o);
-                else convert_step<true, true, false>(raw, ysm, m, valid, kc, a.eps, o);
-            }
-            // the operand stage must be free: the MMAs of step k - kOpStages have completed
-            if (k >= kOpStages && !warp_wait(oempty0 + 8 * os, ((k / kOpStages) - 1) & 1, a.err, 6, lane)) break;
-            tc_fence_after();
-            const uint32_t ta = tmem + tlane + kTmemA + (uint32_t)(os * kTmemAStride);
-            tmem_st8(ta + 0 * 8, o.x.hi);
-            tmem_st8(ta + 1 * 8, o.x.lo);
-            tmem_st8(ta + 2 * 8, o.q.hi);
-            tmem_st8(ta + 3 * 8, o.q.lo);
-            tmem_st8(ta + 4 * 8, o.w.hi);
-            tmem_st8(ta + 5 * 8, o.w.lo);
-            unsigned char* sb = bop0 + os * kBStageBytes;
-            if (b_same) {
-                store_split(sb + 0 * kOpBytes, sb + 1 * kOpBytes, m, o.x);
-                store_split(sb + 2 * kOpBytes, sb + 3 * kOpBytes, m, o.q);
-            } else {
-                store_split(sb + 0 * kOpBytes, sb + 1 * kOpBytes, m, o.b);
-                store_split(sb + 2 * kOpBytes, sb + 3 * kOpBytes, m, o.bq);
-            }
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-            fence_async_smem();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(ofull0 + 8 * os);
-                // The raw stage goes back to the producer only now: every value read from it
-                // has been consumed by the stores above (a release issued right after the
-                // shared loads let the next TMA copy overwrite the stage before those loads
-                // had completed).
-                mbar_arrive(rempty0 + 8 * rs);
-            }
+        ConvCtx cx;
+        cx.raw0 = raw0;
+        cx.ys0 = ys0;
+        cx.bop0 = bop0;
+        cx.rfull0 = rfull0;
+        cx.rempty0 = rempty0;
+        cx.ofull0 = ofull0;
+        cx.oempty0 = oempty0;
+        cx.tmem_a = tmem + tlane + kTmemA + 4 * h;
+        cx.m = m;
+        cx.h = h;
+        cx.lane = lane;
+        cx.nk = nk;
+        cx.rows_left = a.n - r0;
+        {
+            const int64_t full = cx.rows_left / kGK;   // steps whose 16 rows are all below n
+            cx.n_full = full <= 0 ? 0 : (full >= nk ? nk : (int)full);
         }
+        cx.eps = a.eps;
+        cx.err = a.err;
+        if (b_same) conv_loop<false, false>(cx, kc, grp);
+        else if (a.recip) conv_loop<true, true>(cx, kc, grp);
+        else conv_loop<true, false>(cx, kc, grp);
         if (grp == 0) {
-            // group 0 drains the accumulators: TMEM lanes 32*(warp%4) .. +31 are rows m
+            // group 0 drains the accumulators: TMEM lanes 32*(warp%4) .. +31 are rows m; the
+            // two warps of a lane quarter take alternate 32-column chunks
             const bool done = warp_wait(accum, 0, a.err, 3, lane);
-            __syncwarp();
             tc_fence_after();
             if (done && nk > 0) {
                 float* out = a.partial + ((int64_t)blockIdx.y * a.n_tiles + blockIdx.x) * 3 * kGT * kGT;
                 #pragma unroll 1
-                for (int gi = 0; gi < 3; ++gi) {
-                    #pragma unroll 1
-                    for (int c0 = 0; c0 < kGT; c0 += 32) {
-                        float tt[32];
-                        tmem_ld32(tmem + tlane + (uint32_t)(gi * kGT + c0), tt);
-                        float* op = out + (int64_t)gi * kGT * kGT + (int64_t)c0 * kGT + m;
-                        #pragma unroll
-                        for (int c = 0; c < 32; ++c) op[(int64_t)c * kGT] = tt[c];
-                    }
+                for (int idx = h; idx < 3 * kGT / 32; idx += 2) {
+                    const int c0 = idx * 32;   // column of the C | Q | W accumulators
+                    float tt[32];
+                    tmem_ld32(tmem + tlane + (uint32_t)c0, tt);
+                    float* op = out + (int64_t)c0 * kGT + m;
+                    #pragma unroll
+                    for (int c = 0; c < 32; ++c) op[(int64_t)c * kGT] = tt[c];
                 }
             }
         }
