@@ -108,20 +108,25 @@ bool valid_op(int op) { return op >= GAFIME_INTERACT_MULT && op <= GAFIME_INTERA
 
 // Column statistics for one call.  Mutual information centres on the fly from the
 // raw-column means, so it always asks for uncentred statistics.
-int prepare(Bucket& b, int center, int metric, ColumnStats& cs) {
+// pair_scoring: the caller scores pairs next, so on the tensor-core path (raw Pearson) the
+// column sums come from the Gram statistics pass instead of a pass of their own.
+int prepare(Bucket& b, int center, int metric, ColumnStats& cs, bool pair_scoring) {
     bool finite = true;
     int st = check_finite(b, &finite);  // computed at upload; a cached flag here
     if (st != GAFIME_SUCCESS) return st;
     if (!finite) return GAFIME_ERROR_INVALID_ARGS;
+    const bool centred = center != 0 && metric == GAFIME_METRIC_PEARSON;
+    const bool gram_sums = pair_scoring && metric == GAFIME_METRIC_PEARSON && !centred && gram_path_enabled(b);
     KernelTimer timer(b.stream, GAFIME_KERNEL_COLUMN_STATS);
-    return compute_column_stats(b, center != 0 && metric == GAFIME_METRIC_PEARSON, cs);
+    return compute_column_stats(b, centred, cs, !gram_sums);
 }
 
-// Queue moments + epilogue for the requested operators.  cands[o] receives
-// n_tiles lists of k_pad entries for operator o (nullptr: no selection).
+// Queue moments + epilogue for the requested operators.  cands[o] receives n_tiles *
+// sub_lists lists of k_pad entries for operator o (nullptr: no selection); mutual
+// information writes n_tiles lists.
 int score_ops(Bucket& b, const ColumnStats& cs, const Plan& plan, const TileCoord* d_tiles,
               const int* ops, int n_ops, int metric, int center, float div_eps, int mi_bins,
-              int k_pad, Cand* const* cands, double* all_scores) {
+              int k_pad, int sub_lists, Cand* const* cands, double* all_scores) {
     const int nt = (int)plan.tiles.size();
     if (nt == 0) return GAFIME_SUCCESS;
     cudaError_t e;
@@ -171,6 +176,7 @@ int score_ops(Bucket& b, const ColumnStats& cs, const Plan& plan, const TileCoor
         a.ystats = cs.d_y;
         a.op = ops[o];
         a.k_pad = k_pad;
+        a.sub_lists = sub_lists;
         a.cands = cands[o];
         a.all_scores = all_scores;
         KernelTimer timer(b.stream, GAFIME_KERNEL_EPILOGUE_TOPK);
@@ -221,14 +227,16 @@ extern "C" int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact
     const int nt = (int)plan.tiles.size();
     if (nt == 0) return GAFIME_SUCCESS;
     ColumnStats cs;
-    int st = prepare(b, center, metric, cs);
+    int st = prepare(b, center, metric, cs, true);
     if (st != GAFIME_SUCCESS) return st;
     TileCoord* d_tiles = nullptr;
     st = upload_tiles(b, plan, &d_tiles);
     if (st != GAFIME_SUCCESS) return st;
 
     const int k_pad = next_pow2(k);
-    size_t per_op = (size_t)nt * k_pad;
+    const int sub_lists = metric == GAFIME_METRIC_PEARSON ? epilogue_sub_lists(nt, k_pad, b.sm_count) : 1;
+    const int n_lists = nt * sub_lists;
+    size_t per_op = (size_t)n_lists * k_pad;
     cudaError_t e = ensure(b.cands, per_op * n_ops * sizeof(Cand));
     if (e == cudaSuccess) e = ensure(b.cands2, per_op * n_ops * sizeof(Cand));
     if (e != cudaSuccess) return status_from(e);
@@ -239,7 +247,7 @@ extern "C" int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact
         tmp[o] = (Cand*)b.cands2.ptr + per_op * o;
     }
     st = score_ops(b, cs, plan, d_tiles, interact_types, n_ops, metric, center, div_eps, mi_bins,
-                   k_pad, cands, nullptr);
+                   k_pad, sub_lists, cands, nullptr);
     if (st != GAFIME_SUCCESS) return st;
 
     std::vector<Cand> host((size_t)k_pad * n_ops);
@@ -247,7 +255,7 @@ extern "C" int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact
         Cand* fin = nullptr;
         {
             KernelTimer timer(b.stream, GAFIME_KERNEL_MERGE);
-            e = merge_candidates(cands[o], tmp[o], nt, k_pad, 0, &fin, b.stream);
+            e = merge_candidates(cands[o], tmp[o], n_lists, k_pad, 0, &fin, b.stream);
         }
         if (e != cudaSuccess) return status_from(e);
         e = cudaMemcpyAsync(host.data() + (size_t)k_pad * o, fin, sizeof(Cand) * k_pad,
@@ -289,7 +297,7 @@ extern "C" int gafime_allpairs_scores(ContiguousBucket bucket, int interact_type
     if (P == 0) return GAFIME_SUCCESS;
     Plan plan = make_plan(b, 0, 1);
     ColumnStats cs;
-    int st = prepare(b, center, metric, cs);
+    int st = prepare(b, center, metric, cs, true);
     if (st != GAFIME_SUCCESS) return st;
     TileCoord* d_tiles = nullptr;
     st = upload_tiles(b, plan, &d_tiles);
@@ -297,7 +305,7 @@ extern "C" int gafime_allpairs_scores(ContiguousBucket bucket, int interact_type
     cudaError_t e = ensure(b.scores, (size_t)P * sizeof(double));
     if (e != cudaSuccess) return status_from(e);
     Cand* none[1] = {nullptr};
-    st = score_ops(b, cs, plan, d_tiles, &interact_type, 1, metric, center, div_eps, mi_bins, 1,
+    st = score_ops(b, cs, plan, d_tiles, &interact_type, 1, metric, center, div_eps, mi_bins, 1, 1,
                    none, (double*)b.scores.ptr);
     if (st != GAFIME_SUCCESS) return st;
     e = cudaMemcpyAsync(out_scores, b.scores.ptr, (size_t)P * sizeof(double), cudaMemcpyDeviceToHost,
@@ -337,7 +345,7 @@ extern "C" int gafime_unary_scores(ContiguousBucket bucket, int metric, int mi_b
     Bucket& b = *(Bucket*)bucket;
     cudaSetDevice(b.device);
     ColumnStats cs;
-    int st = prepare(b, 0, GAFIME_METRIC_PEARSON, cs);
+    int st = prepare(b, 0, GAFIME_METRIC_PEARSON, cs, false);
     if (st != GAFIME_SUCCESS) return st;
     cudaError_t e = ensure(b.scores, (size_t)std::max<int64_t>(b.f, 1) * sizeof(double));
     if (e != cudaSuccess) return status_from(e);

@@ -172,11 +172,25 @@ __global__ void __launch_bounds__(256) col_partial_kernel(
     int64_t r0 = (int64_t)s * span;
     int64_t r1 = r0 + span < n ? r0 + span : n;
     double v[3] = {0.0, 0.0, 0.0};
-    for (int64_t r = r0 + threadIdx.x; r < r1; r += 256) {
-        double a = col[r];
-        v[0] += a;
-        v[1] += a * a;
-        if (ycen) v[2] += a * (double)ycen[r];
+    // rows r0 + tid, + 256, ... in order; each run of 8 issues its loads before any use
+    constexpr int kRun = 8;
+    for (int64_t base = r0 + threadIdx.x; base < r1; base += 256 * kRun) {
+        float xv[kRun], yv[kRun];
+        #pragma unroll
+        for (int i = 0; i < kRun; ++i) {
+            const int64_t r = base + 256 * i;
+            xv[i] = r < r1 ? __ldg(col + r) : 0.f;
+            yv[i] = (ycen && r < r1) ? __ldg(ycen + r) : 0.f;
+        }
+        #pragma unroll
+        for (int i = 0; i < kRun; ++i) {
+            if (base + 256 * i < r1) {
+                const double a = xv[i];
+                v[0] += a;
+                v[1] += a * a;
+                if (ycen) v[2] += a * (double)yv[i];
+            }
+        }
     }
     block_reduce_fixed<3>(v, red);
     if (threadIdx.x == 0) {
@@ -268,7 +282,7 @@ static cudaError_t column_sums(Bucket& b, const float* x, int64_t cols, const fl
     return cudaGetLastError();
 }
 
-int compute_column_stats(Bucket& b, bool centred, ColumnStats& out) {
+int compute_column_stats(Bucket& b, bool centred, ColumnStats& out, bool x_sums) {
     // stats buffer: [f*4] column stats, [4] y column sums, [4] ystats
     cudaError_t e = ensure(b.stats, (size_t)(b.f * 4 + 8) * sizeof(double));
     if (e == cudaSuccess) {
@@ -299,8 +313,10 @@ int compute_column_stats(Bucket& b, bool centred, ColumnStats& out) {
                                                    (float*)b.xcen.ptr);
         xs = (const float*)b.xcen.ptr;
     }
-    e = column_sums(b, xs, b.f, ycen, colstats);
-    if (e != cudaSuccess) return status_from(e);
+    if (x_sums) {
+        e = column_sums(b, xs, b.f, ycen, colstats);
+        if (e != cudaSuccess) return status_from(e);
+    }
     out.d_col = colstats;
     out.d_y = ystats;
     out.d_x = xs;

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 #include <vector>
 
@@ -68,7 +69,9 @@ struct ColumnStats {
     const float* d_ycen = nullptr;  // fl32(y - mean y), zero padded
     double h_y[4];
 };
-int compute_column_stats(Bucket& b, bool centred, ColumnStats& out);
+// x_sums = false leaves colstats to the caller (the tensor-core path computes the column
+// sums in its own pass over the columns, before anything reads them).
+int compute_column_stats(Bucket& b, bool centred, ColumnStats& out, bool x_sums = true);
 
 // Finite-input check over the features and y, run once per upload and cached.
 int check_finite(Bucket& b, bool* all_finite);
@@ -116,10 +119,13 @@ struct EpilogueArgs {
     const double* ystats;        // [4]
     int op;                      // GAFIME_INTERACT_*
     int k_pad;                   // power of two >= k, <= 4096
-    Cand* cands;                 // [n_tiles * k_pad] for this op
+    int sub_lists;               // candidate lists per tile (power of two, 4096 / sub_lists >= k_pad)
+    Cand* cands;                 // [n_tiles * sub_lists * k_pad] for this op
     double* all_scores;          // nullable, [P] triangle order
 };
 cudaError_t launch_epilogue_topk(const EpilogueArgs& a, cudaStream_t stream);
+// Candidate lists per tile for a top-k call: enough CTAs to fill the GPU.
+int epilogue_sub_lists(int n_tiles, int k_pad, int sm_count);
 
 // Merge n_lists sorted candidate lists of k_pad entries down to one (in place
 // ping-pong between buf and tmp); returns the buffer holding the final list.
@@ -141,16 +147,20 @@ cudaError_t launch_mi_unary(Bucket& b, int mi_bins, double* d_out, cudaStream_t 
 std::vector<TileCoord> shard_tiles(int64_t f, int shard_id, int n_shards);
 
 // Ranking used everywhere: |score| descending, NaN after every number, empty
-// slots last; ties by pair id ascending.
-__host__ __device__ inline double cand_rank(const Cand& c) {
-    if (c.pid == kNoPair) return -2.0;
-    double s = c.score;
-    if (s != s) return -1.0;
-    return s < 0 ? -s : s;
+// slots last; ties by pair id ascending.  cand_key orders like that rank as an unsigned
+// integer (|score| bits order like |score| for non-NaN doubles), so a comparison is two
+// integer compares.
+__host__ __device__ inline uint64_t cand_key(const Cand& c) {
+    if (c.pid == kNoPair) return 0;
+    uint64_t u;
+    memcpy(&u, &c.score, sizeof(u));
+    u &= 0x7FFFFFFFFFFFFFFFull;
+    if (u > 0x7FF0000000000000ull) return 1;  // NaN
+    return u + 2;
 }
 __host__ __device__ inline bool cand_before(const Cand& a, const Cand& b) {
-    double ra = cand_rank(a), rb = cand_rank(b);
-    if (ra != rb) return ra > rb;
+    const uint64_t ka = cand_key(a), kb = cand_key(b);
+    if (ka != kb) return ka > kb;
     return a.pid < b.pid;
 }
 

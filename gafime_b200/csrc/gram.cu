@@ -235,16 +235,46 @@ struct Split8 {
     uint32_t hi[4], lo[4];
 };
 
-// 2-term split of 8 values: hi = fp16(v), lo = fp16(v - hi) (v - hi is exact in fp32, and
-// |v - hi| <= 2^-11 |v|, so hi + lo carries ~22 significant bits).
-__device__ __forceinline__ void split8(const float (&v)[8], Split8& s) {
+// Packed fp32 pairs (two rows of one column) for the sm_100 f32x2 instructions; each lane
+// is rounded exactly like the scalar operation.
+__device__ __forceinline__ uint64_t pk(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 upk(uint64_t v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// 2-term split of 8 values (4 packed pairs): hi = fp16(v), lo = fp16(v - hi) (v - hi is
+// exact in fp32, and |v - hi| <= 2^-11 |v|, so hi + lo carries ~22 significant bits).
+__device__ __forceinline__ void split8(const uint64_t (&v)[4], Split8& s) {
     #pragma unroll
-    for (int r = 0; r < 8; r += 2) {
-        __half2 h = __floats2half2_rn(v[r], v[r + 1]);
+    for (int p = 0; p < 4; ++p) {
+        const float2 f = upk(v[p]);
+        __half2 h = __floats2half2_rn(f.x, f.y);
         const float2 hf = __half22float2(h);
-        __half2 l = __floats2half2_rn(v[r] - hf.x, v[r + 1] - hf.y);
-        s.hi[r / 2] = *reinterpret_cast<uint32_t*>(&h);
-        s.lo[r / 2] = *reinterpret_cast<uint32_t*>(&l);
+        const float2 d = upk(sub2(v[p], pk(hf.x, hf.y)));
+        __half2 l = __floats2half2_rn(d.x, d.y);
+        s.hi[p] = *reinterpret_cast<uint32_t*>(&h);
+        s.lo[p] = *reinterpret_cast<uint32_t*>(&l);
     }
 }
 
@@ -289,25 +319,38 @@ struct StepOps {
 
 // Convert K half h of column m for one step (A block, and the B block when kB).  kMask
 // zeroes rows at or beyond `valid`.  fma(x, s, -mean*s) equals fl(x - mean) * s exactly (s
-// is a power of two).
+// is a power of two).  Rows are processed in packed pairs (f32x2).
 template <bool kMask, bool kB, bool kRecip>
 __device__ __forceinline__ void convert_step(const unsigned char* raw, const unsigned char* ysm, int m, int h,
                                              int valid, const ConvCols& k, float eps, StepOps& o) {
-    float x[8], v[8];
+    float x[8];
+    uint64_t x2[4], v2[4], t2[4];
     load_raw8(raw, m, h, x);
     #pragma unroll
-    for (int r = 0; r < 8; ++r) v[r] = (!kMask || 8 * h + r < valid) ? fmaf(x[r], k.sx_a, -k.mus_a) : 0.f;
-    split8(v, o.x);
+    for (int p = 0; p < 4; ++p) x2[p] = pk(x[2 * p], x[2 * p + 1]);
+    const uint64_t sx = pk(k.sx_a, k.sx_a), nmu = pk(-k.mus_a, -k.mus_a), sq = pk(k.sq_a, k.sq_a);
+    #pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        v2[p] = fma2(x2[p], sx, nmu);              // C: s_x (a - mean)
+        t2[p] = mul2(mul2(x2[p], x2[p]), sq);      // Q: s_q a^2
+        if (kMask) {
+            const bool v0 = 8 * h + 2 * p < valid, v1 = 8 * h + 2 * p + 1 < valid;
+            const float2 c = upk(v2[p]), q = upk(t2[p]);
+            v2[p] = pk(v0 ? c.x : 0.f, v1 ? c.y : 0.f);
+            t2[p] = pk(v0 ? q.x : 0.f, v1 ? q.y : 0.f);
+        }
+    }
+    split8(v2, o.x);
+    split8(t2, o.q);
     {
         const float4 y0 = *reinterpret_cast<const float4*>(ysm + 32 * h);
         const float4 y1 = *reinterpret_cast<const float4*>(ysm + 32 * h + 16);
-        v[0] *= y0.x; v[1] *= y0.y; v[2] *= y0.z; v[3] *= y0.w;
-        v[4] *= y1.x; v[5] *= y1.y; v[6] *= y1.z; v[7] *= y1.w;
+        v2[0] = mul2(v2[0], pk(y0.x, y0.y));       // W: C * (s_y ycen)
+        v2[1] = mul2(v2[1], pk(y0.z, y0.w));
+        v2[2] = mul2(v2[2], pk(y1.x, y1.y));
+        v2[3] = mul2(v2[3], pk(y1.z, y1.w));
     }
-    split8(v, o.w);
-    #pragma unroll
-    for (int r = 0; r < 8; ++r) v[r] = (!kMask || 8 * h + r < valid) ? x[r] * x[r] * k.sq_a : 0.f;
-    split8(v, o.q);
+    split8(v2, o.w);
     if (kB) {
         load_raw8(raw + kRawBox, m, h, x);
         if (kRecip) {
@@ -315,11 +358,21 @@ __device__ __forceinline__ void convert_step(const unsigned char* raw, const uns
             for (int r = 0; r < 8; ++r) x[r] = safe_recip(x[r], eps);
         }
         #pragma unroll
-        for (int r = 0; r < 8; ++r) v[r] = (!kMask || 8 * h + r < valid) ? fmaf(x[r], k.sx_b, -k.mus_b) : 0.f;
-        split8(v, o.b);
+        for (int p = 0; p < 4; ++p) x2[p] = pk(x[2 * p], x[2 * p + 1]);
+        const uint64_t sxb = pk(k.sx_b, k.sx_b), nmub = pk(-k.mus_b, -k.mus_b), sqb = pk(k.sq_b, k.sq_b);
         #pragma unroll
-        for (int r = 0; r < 8; ++r) v[r] = (!kMask || 8 * h + r < valid) ? x[r] * x[r] * k.sq_b : 0.f;
-        split8(v, o.bq);
+        for (int p = 0; p < 4; ++p) {
+            v2[p] = fma2(x2[p], sxb, nmub);
+            t2[p] = mul2(mul2(x2[p], x2[p]), sqb);
+            if (kMask) {
+                const bool v0 = 8 * h + 2 * p < valid, v1 = 8 * h + 2 * p + 1 < valid;
+                const float2 c = upk(v2[p]), q = upk(t2[p]);
+                v2[p] = pk(v0 ? c.x : 0.f, v1 ? c.y : 0.f);
+                t2[p] = pk(v0 ? q.x : 0.f, v1 ? q.y : 0.f);
+            }
+        }
+        split8(v2, o.b);
+        split8(t2, o.bq);
     }
 }
 
@@ -563,50 +616,135 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
 // ---- per-column statistics and scales -------------------------------------------
 
 // Per column and row split: [0] min x, [1] max x, [2] sum g, [3] sum g^2, [4] sum g*ycen,
-// [5] min g, [6] max g
+// [5] min g, [6] max g, [7] sum x, [8] sum x^2, [9] sum x*ycen
 struct GramColPart {
-    double v[7];
+    double v[10];
 };
 
-__global__ void __launch_bounds__(256) gram_colstats_kernel(const float* __restrict__ x, int64_t ld, int64_t n,
-                                                            const float* __restrict__ ycen, int recip,
-                                                            float eps, int64_t span, GramColPart* part) {
-    __shared__ double red[7][256];
-    const int c = blockIdx.x, s = blockIdx.y, splits = gridDim.y;
-    const int64_t rb = (int64_t)s * span, re = min(rb + span, n);
-    double v[7] = {INFINITY, -INFINITY, 0.0, 0.0, 0.0, INFINITY, -INFINITY};
-    for (int64_t r = rb + threadIdx.x; r < re; r += 256) {
-        float xv = x[(int64_t)c * ld + r];
-        v[0] = fmin(v[0], (double)xv);
-        v[1] = fmax(v[1], (double)xv);
-        if (recip) {
-            double g = safe_recip(xv, eps);
-            v[2] += g;
-            v[3] += g * g;
-            v[4] += g * (double)ycen[r];
-            v[5] = fmin(v[5], g);
-            v[6] = fmax(v[6], g);
+constexpr int kStatCols = 4;        // columns per CTA of the statistics pass
+constexpr int kStatColsRecip = 2;   // ... when g = 1/safe(x) is accumulated too
+
+__device__ __forceinline__ double warp_sum(double v) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_min(float v) {
+    for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// One 2048-row pass of the statistics kernel for one thread (two float4 runs per column).
+// kMask: rows e of run u count only when e < valid_u (the rows left before n).
+template <int kCB, bool kRecip, bool kMask>
+__device__ __forceinline__ void stat_pass(const float4 (&xv)[kCB][2], const float4 (&yv)[2], int valid0, int valid1,
+                                          float eps, float (&mn)[kCB], float (&mx)[kCB], float (&gmn)[kCB],
+                                          float (&gmx)[kCB], double (&S)[kCB], double (&Q)[kCB], double (&W)[kCB],
+                                          double (&G)[kCB], double (&GQ)[kCB], double (&GW)[kCB]) {
+    #pragma unroll
+    for (int c = 0; c < kCB; ++c) {
+        float s1 = 0.f, q1 = 0.f, w1 = 0.f, g1 = 0.f, gq1 = 0.f, gw1 = 0.f;
+        #pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const float xs[4] = {xv[c][u].x, xv[c][u].y, xv[c][u].z, xv[c][u].w};
+            const float ys[4] = {yv[u].x, yv[u].y, yv[u].z, yv[u].w};
+            const int valid = u == 0 ? valid0 : valid1;
+            #pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const bool in = !kMask || e < valid;
+                const float v = xs[e];
+                s1 += v;
+                q1 = fmaf(v, v, q1);
+                w1 = fmaf(v, ys[e], w1);
+                mn[c] = fminf(mn[c], in ? v : INFINITY);
+                mx[c] = fmaxf(mx[c], in ? v : -INFINITY);
+                if (kRecip) {
+                    const float gv = in ? safe_recip(v, eps) : 0.f;
+                    g1 += gv;
+                    gq1 = fmaf(gv, gv, gq1);
+                    gw1 = fmaf(gv, ys[e], gw1);
+                    gmn[c] = fminf(gmn[c], in ? gv : INFINITY);
+                    gmx[c] = fmaxf(gmx[c], in ? gv : -INFINITY);
+                }
+            }
+        }
+        S[c] += s1;
+        Q[c] += q1;
+        W[c] += w1;
+        if (kRecip) {
+            G[c] += g1;
+            GQ[c] += gq1;
+            GW[c] += gw1;
         }
     }
-    for (int m = 0; m < 7; ++m) red[m][threadIdx.x] = v[m];
+}
+
+// One pass over the columns: the column sums the epilogue and the reconstruction need
+// (sum x, sum x^2, sum x*ycen) and the ranges that set the operand scales, plus the same
+// for g = 1/safe(x) when the divide group is scored (kRecip).  A CTA takes kCB columns and
+// a row span; each thread reads float4 runs of 4 rows (rows up to ld exist: the padding is
+// zero in x and ycen, which adds nothing to the sums, and is masked out of the ranges and
+// of g).  Each thread adds its 8 rows of a pass in fp32 and the passes in fp64, in a fixed
+// order, so the result does not depend on timing.
+template <int kCB, bool kRecip>
+__global__ void __launch_bounds__(256) gram_stats_kernel(const float* __restrict__ x, int64_t ld, int64_t n,
+                                                         int64_t f, const float* __restrict__ ycen, float eps,
+                                                         int64_t span, GramColPart* part) {
+    __shared__ double red[8][kCB][10];
+    const int64_t c0 = (int64_t)blockIdx.x * kCB;
+    const int s = blockIdx.y, splits = gridDim.y;
+    const int64_t rb = (int64_t)s * span, re = min(rb + span, ld);   // span: a multiple of 2048
+    float mn[kCB], mx[kCB], gmn[kCB], gmx[kCB];
+    double S[kCB], Q[kCB], W[kCB], G[kCB], GQ[kCB], GW[kCB];
+    #pragma unroll
+    for (int c = 0; c < kCB; ++c) {
+        mn[c] = gmn[c] = INFINITY;
+        mx[c] = gmx[c] = -INFINITY;
+        S[c] = Q[c] = W[c] = G[c] = GQ[c] = GW[c] = 0.0;
+    }
+    for (int64_t base = rb; base < re; base += 2048) {
+        float4 yv[2], xv[kCB][2];
+        #pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int64_t r = base + 1024 * u + 4 * threadIdx.x;
+            const bool ok = r < re;
+            yv[u] = ok ? __ldg(reinterpret_cast<const float4*>(ycen + r)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            #pragma unroll
+            for (int c = 0; c < kCB; ++c)
+                xv[c][u] = (ok && c0 + c < f) ? __ldg(reinterpret_cast<const float4*>(x + (c0 + c) * ld + r))
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (base + 2048 <= n) {
+            stat_pass<kCB, kRecip, false>(xv, yv, 0, 0, eps, mn, mx, gmn, gmx, S, Q, W, G, GQ, GW);
+        } else {
+            // rows from n on are padding: masked out of the ranges and of g
+            const int64_t left = n - (base + 4 * threadIdx.x);
+            const int v0 = left <= 0 ? 0 : (left >= 4 ? 4 : (int)left);
+            const int v1 = left <= 1024 ? 0 : (left >= 1028 ? 4 : (int)(left - 1024));
+            stat_pass<kCB, kRecip, true>(xv, yv, v0, v1, eps, mn, mx, gmn, gmx, S, Q, W, G, GQ, GW);
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    #pragma unroll
+    for (int c = 0; c < kCB; ++c) {
+        const double v[10] = {(double)warp_min(mn[c]), (double)warp_max(mx[c]), warp_sum(G[c]), warp_sum(GQ[c]),
+                              warp_sum(GW[c]), (double)warp_min(gmn[c]), (double)warp_max(gmx[c]), warp_sum(S[c]),
+                              warp_sum(Q[c]), warp_sum(W[c])};
+        if (lane == 0)
+            for (int m = 0; m < 10; ++m) red[warp][c][m] = v[m];
+    }
     __syncthreads();
-    for (int st = 128; st > 0; st >>= 1) {
-        if (threadIdx.x < st) {
-            int t = threadIdx.x;
-            red[0][t] = fmin(red[0][t], red[0][t + st]);
-            red[1][t] = fmax(red[1][t], red[1][t + st]);
-            red[2][t] += red[2][t + st];
-            red[3][t] += red[3][t + st];
-            red[4][t] += red[4][t + st];
-            red[5][t] = fmin(red[5][t], red[5][t + st]);
-            red[6][t] = fmax(red[6][t], red[6][t + st]);
+    if (threadIdx.x < kCB * 10) {
+        const int c = threadIdx.x / 10, m = threadIdx.x % 10;
+        double acc = red[0][c][m];
+        for (int w = 1; w < 8; ++w) {
+            const double t = red[w][c][m];
+            acc = (m == 0 || m == 5) ? fmin(acc, t) : (m == 1 || m == 6) ? fmax(acc, t) : acc + t;
         }
-        __syncthreads();
-    }
-    if (threadIdx.x == 0) {
-        GramColPart p;
-        for (int m = 0; m < 7; ++m) p.v[m] = red[m][0];
-        part[(int64_t)c * splits + s] = p;
+        if (c0 + c < f) part[(c0 + c) * splits + s].v[m] = acc;
     }
 }
 
@@ -615,12 +753,14 @@ __global__ void __launch_bounds__(256) gram_colstats_kernel(const float* __restr
 //   cs[c*12 + 5]: mean g rounded to fp32 (the value the operand conversion subtracts)
 //   cs[c*12 + 6..8]: sum g, sum g^2, sum g*ycen
 //   cs[c*12 + 9]: mean x rounded to fp32 (the value the operand conversion subtracts)
+// and the column statistics the epilogue reads: colstats[c*4 + {0,1,2,3}] =
+// {sum x, sum x^2, sum x*ycen, mean x}.
 struct GramScaleArgs {
     const GramColPart* part;
     int splits;
     int64_t f, n;
-    const double* colstats;   // sum, sumsq, sum*ycen, mean per column
-    double s_y;               // power-of-two scale of ycen (|ycen * s_y| <= 1)
+    double* colstats;
+    const unsigned* ycen_absmax;   // bits of max |ycen| (a non-negative float)
     int recip;
     double* cs;
 };
@@ -633,10 +773,20 @@ __device__ __forceinline__ double pow2_scale(double maxabs) {
     return ldexp(1.0, e - 1);
 }
 
+// s_y: the largest power of two with s_y * max|ycen| <= 1 (1 for a zero target)
+__device__ __forceinline__ double ycen_scale(const unsigned* bits) {
+    const float yabs = __uint_as_float(*bits);
+    if (!(yabs > 0.0f) || !isfinite(yabs)) return 1.0;
+    int e;
+    frexp(1.0 / (double)yabs, &e);
+    return ldexp(1.0, e - 1);
+}
+
 __global__ void gram_scale_kernel(GramScaleArgs a) {
     int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= a.f) return;
     double mn = INFINITY, mx = -INFINITY, sg = 0, sgg = 0, sgy = 0, gmn = INFINITY, gmx = -INFINITY;
+    double sx = 0, sxx = 0, sxy = 0;
     for (int s = 0; s < a.splits; ++s) {
         const GramColPart& p = a.part[c * a.splits + s];
         mn = fmin(mn, p.v[0]);
@@ -646,17 +796,26 @@ __global__ void gram_scale_kernel(GramScaleArgs a) {
         sgy += p.v[4];
         gmn = fmin(gmn, p.v[5]);
         gmx = fmax(gmx, p.v[6]);
+        sx += p.v[7];
+        sxx += p.v[8];
+        sxy += p.v[9];
     }
-    const double mu = (double)(float)a.colstats[c * 4 + 3];
+    const double n = (double)a.n;
+    double* col = a.colstats + c * 4;
+    col[0] = sx;
+    col[1] = sxx;
+    col[2] = sxy;
+    col[3] = sx / n;
+    const double mu = (double)(float)(sx / n);
     // the fp32 subtraction may round up by one ulp: a 2^-20 margin keeps |value| <= 2^14
     const double dev = fmax(fabs(mx - mu), fabs(mu - mn)) * (1.0 + 1e-6);
     double* o = a.cs + c * 12;
     o[0] = pow2_scale(dev);
     o[1] = pow2_scale(fmax(mx * mx, mn * mn) * (1.0 + 1e-6));
-    o[2] = o[0] * a.s_y;   // W operand = (s_x a') * (s_y ycen)
+    o[2] = o[0] * ycen_scale(a.ycen_absmax);   // W operand = (s_x a') * (s_y ycen)
     o[9] = mu;
     if (a.recip) {
-        const double mug = (double)(float)(sg / (double)a.n);
+        const double mug = (double)(float)(sg / n);
         const double gdev = fmax(fabs(gmx - mug), fabs(mug - gmn)) * (1.0 + 1e-6);
         o[3] = pow2_scale(gdev);
         o[4] = pow2_scale(fmax(gmx * gmx, gmn * gmn) * (1.0 + 1e-6));
@@ -670,7 +829,10 @@ __global__ void gram_scale_kernel(GramScaleArgs a) {
     o[8] = sgy;
 }
 
-__global__ void scale_rows_kernel(const float* __restrict__ v, int64_t n, float s, float* __restrict__ out) {
+// ys = ycen * s_y
+__global__ void scale_rows_kernel(const float* __restrict__ v, int64_t n, const unsigned* absmax_bits,
+                                  float* __restrict__ out) {
+    const float s = (float)ycen_scale(absmax_bits);
     for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x)
         out[r] = v[r] * s;
 }
@@ -836,8 +998,11 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     size_t part_bytes = (size_t)n_chunks * nt * 3 * kGT * kGT * sizeof(float);
     size_t off_lut = (part_bytes + 255) / 256 * 256;
     size_t off_t128 = (off_lut + lut.size() * sizeof(int) + 255) / 256 * 256;
-    int splits = (int)std::max<int64_t>(1, std::min<int64_t>((4 * (int64_t)b.sm_count + f - 1) / f,
-                                                             (n + 4095) / 4096));
+    // statistics pass: about 8 CTAs per SM, row spans of whole 2048-row passes
+    const int stat_cols = (recip || prep_mode == GRAM_PREP_BOTH) ? kStatColsRecip : kStatCols;
+    const int64_t col_groups = (f + stat_cols - 1) / stat_cols;
+    int splits = (int)std::max<int64_t>(1, std::min<int64_t>((8 * (int64_t)b.sm_count + col_groups - 1) / col_groups,
+                                                             (ld + 2047) / 2048));
     splits = std::min(splits, 256);
     size_t off_colp = (off_t128 + t128.size() * sizeof(TileCoord) + 255) / 256 * 256;
     size_t off_cs = (off_colp + (size_t)f * splits * sizeof(GramColPart) + 255) / 256 * 256;
@@ -863,42 +1028,32 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     if (e != cudaSuccess) return e;
 
     if (prep_mode != GRAM_PREP_DONE) {
-        // per-column ranges (and the divide side's sums) -> power-of-two scales
+        // one pass over the columns: column sums (the epilogue's statistics) and ranges (and
+        // the divide side's sums) -> power-of-two scales; no host round trip
         const bool both = prep_mode == GRAM_PREP_BOTH;
-        int64_t span = ((n + splits - 1) / splits + 255) / 256 * 256;
-        {
-            KernelTimer timer(stream, GAFIME_KERNEL_GRAM_PREP);
-            e = cudaMemsetAsync(d_absmax, 0, sizeof(unsigned), stream);
-            if (e != cudaSuccess) return e;
-            absmax_kernel<<<2 * b.sm_count, 256, 0, stream>>>(cs.d_ycen, ld, d_absmax);
-            gram_colstats_kernel<<<dim3((unsigned)f, (unsigned)splits), 256, 0, stream>>>(
-                cs.d_x, ld, n, cs.d_ycen, (recip || both) ? 1 : 0, eps, span, colp);
-        }
-        unsigned h_absmax = 0;
-        e = cudaMemcpyAsync(&h_absmax, d_absmax, sizeof(unsigned), cudaMemcpyDeviceToHost, stream);
-        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        const int64_t span = ((ld + splits - 1) / splits + 2047) / 2048 * 2048;
+        KernelTimer timer(stream, GAFIME_KERNEL_GRAM_PREP);
+        e = cudaMemsetAsync(d_absmax, 0, sizeof(unsigned), stream);
         if (e != cudaSuccess) return e;
-        float yabs = 0.0f;
-        memcpy(&yabs, &h_absmax, sizeof(float));
-        // s_y: the largest power of two with s_y * max|ycen| <= 1 (1 for a zero target)
-        double s_y = 1.0;
-        if (yabs > 0.0f && std::isfinite(yabs)) {
-            int ex;
-            frexp(1.0 / (double)yabs, &ex);
-            s_y = ldexp(1.0, ex - 1);
-        }
+        absmax_kernel<<<2 * b.sm_count, 256, 0, stream>>>(cs.d_ycen, ld, d_absmax);
+        if (recip || both)
+            gram_stats_kernel<kStatColsRecip, true><<<dim3((unsigned)((f + kStatColsRecip - 1) / kStatColsRecip),
+                                                          (unsigned)splits),
+                                                     256, 0, stream>>>(cs.d_x, ld, n, f, cs.d_ycen, eps, span, colp);
+        else
+            gram_stats_kernel<kStatCols, false><<<dim3((unsigned)((f + kStatCols - 1) / kStatCols), (unsigned)splits),
+                                                  256, 0, stream>>>(cs.d_x, ld, n, f, cs.d_ycen, eps, span, colp);
         GramScaleArgs sa;
         sa.part = colp;
         sa.splits = splits;
         sa.f = f;
         sa.n = n;
-        sa.colstats = cs.d_col;
-        sa.s_y = s_y;
+        sa.colstats = const_cast<double*>(cs.d_col);
+        sa.ycen_absmax = d_absmax;
         sa.recip = (recip || both) ? 1 : 0;
         sa.cs = d_cs;
-        KernelTimer timer(stream, GAFIME_KERNEL_GRAM_PREP);
         gram_scale_kernel<<<(unsigned)((f + 127) / 128), 128, 0, stream>>>(sa);
-        scale_rows_kernel<<<2 * b.sm_count, 256, 0, stream>>>(cs.d_ycen, ld, (float)s_y, d_ys);
+        scale_rows_kernel<<<2 * b.sm_count, 256, 0, stream>>>(cs.d_ycen, ld, d_absmax, d_ys);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }

@@ -171,6 +171,7 @@ extern "C" int gafime_allpairs_scores_noalloc(const float* d_x, int64_t ld, cons
     a.ystats = ystats;
     a.op = interact_type;
     a.k_pad = 1;
+    a.sub_lists = 1;
     a.cands = nullptr;  // scores only
     a.all_scores = d_scores_out;
     e = launch_epilogue_topk(a, s);

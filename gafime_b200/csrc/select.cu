@@ -38,14 +38,20 @@ __device__ __forceinline__ double pearson(double n, double sx, double sxx, doubl
     return cov / sqrt(d);
 }
 
+// Grid (n_tiles, sub_lists): CTA (t, s) scores the pairs e in [s*L, (s+1)*L) of tile t
+// (L = kTilePairs / sub_lists) and writes the k_pad best of them, sorted, as list
+// t * sub_lists + s.
 __global__ void __launch_bounds__(kEpiThreads) epilogue_topk_kernel(EpilogueArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    Cand* s = reinterpret_cast<Cand*>(smem_raw);  // [kTilePairs]
+    Cand* s = reinterpret_cast<Cand*>(smem_raw);  // [L]
     const int t = blockIdx.x;
+    const int L = kTilePairs / a.sub_lists;
+    const int e0 = blockIdx.y * L;
     const TileCoord tc = a.tiles[t];
     const double n = a.ystats[0], var_y = a.ystats[2];
     const int64_t f = a.f;
-    for (int e = threadIdx.x; e < kTilePairs; e += kEpiThreads) {
+    for (int q = threadIdx.x; q < L; q += kEpiThreads) {
+        const int e = e0 + q;
         int li = e / kTile, lj = e % kTile;
         int64_t i = (int64_t)tc.bi * kTile + li, j = (int64_t)tc.bj * kTile + lj;
         Cand c;
@@ -81,17 +87,19 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_topk_kernel(EpilogueArgs
             c.score = 0.0;
             c.pid = kNoPair;
         }
-        s[e] = c;
+        s[q] = c;
     }
     if (a.cands == nullptr) return;  // scores only (uniform across the block)
     __syncthreads();
-    bitonic_sort(s, kTilePairs);
-    Cand* out = a.cands + (int64_t)t * a.k_pad;
-    for (int e = threadIdx.x; e < a.k_pad; e += kEpiThreads) out[e] = s[e];
+    bitonic_sort(s, L);
+    Cand* out = a.cands + ((int64_t)t * a.sub_lists + blockIdx.y) * a.k_pad;
+    for (int q = threadIdx.x; q < a.k_pad; q += kEpiThreads) out[q] = s[q];
 }
 
-// Each CTA merges `group` consecutive sorted lists (k_pad entries each) into the
-// k_pad best entries.  Lists beyond n_lists are treated as empty.
+// Each CTA reduces `group` consecutive sorted lists (k_pad entries each; lists beyond
+// n_lists are empty) to their k_pad best entries, sorted.  Pairwise tree: for runs A and B
+// sorted best-first, better(A[i], B[k-1-i]) over i is a bitonic sequence holding the k best
+// of A and B, which log2(k) half-cleaner stages sort.
 __global__ void __launch_bounds__(1024) merge_kernel(const Cand* __restrict__ in, int n_lists,
                                                      int k_pad, int group, Cand* __restrict__ out) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -111,7 +119,27 @@ __global__ void __launch_bounds__(1024) merge_kernel(const Cand* __restrict__ in
         }
     }
     __syncthreads();
-    bitonic_sort(s, total);
+    for (int span = 1; span < group; span <<= 1) {
+        // runs a = 2*span*q keep the k best of runs a and a + span
+        const int pairs = group / (2 * span);
+        for (int e = threadIdx.x; e < pairs * k_pad; e += blockDim.x) {
+            const int q = e / k_pad, i = e % k_pad;
+            const int ra = 2 * span * q;
+            Cand* A = s + (int64_t)ra * k_pad;
+            const Cand& bv = s[(int64_t)(ra + span) * k_pad + (k_pad - 1 - i)];
+            if (cand_before(bv, A[i])) A[i] = bv;
+        }
+        __syncthreads();
+        for (int stride = k_pad >> 1; stride > 0; stride >>= 1) {
+            for (int e = threadIdx.x; e < pairs * (k_pad >> 1); e += blockDim.x) {
+                const int q = e / (k_pad >> 1), r = e % (k_pad >> 1);
+                Cand* A = s + (int64_t)(2 * span * q) * k_pad;
+                const int i = 2 * stride * (r / stride) + (r % stride);
+                cand_cswap(A, i, i + stride, true);
+            }
+            __syncthreads();
+        }
+    }
     for (int e = threadIdx.x; e < k_pad; e += blockDim.x) out[(int64_t)g * k_pad + e] = s[e];
 }
 
@@ -119,17 +147,29 @@ __global__ void __launch_bounds__(1024) merge_kernel(const Cand* __restrict__ in
 
 cudaError_t launch_epilogue_topk(const EpilogueArgs& a, cudaStream_t stream) {
     if (a.n_tiles <= 0) return cudaSuccess;
-    size_t smem = sizeof(Cand) * kTilePairs;
+    if (a.sub_lists < 1 || kTilePairs % a.sub_lists != 0 || (a.cands && kTilePairs / a.sub_lists < a.k_pad))
+        return cudaErrorInvalidValue;
+    size_t smem = sizeof(Cand) * (kTilePairs / a.sub_lists);
     cudaFuncSetAttribute(epilogue_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    epilogue_topk_kernel<<<a.n_tiles, kEpiThreads, smem, stream>>>(a);
+    epilogue_topk_kernel<<<dim3((unsigned)a.n_tiles, (unsigned)a.sub_lists), kEpiThreads, smem, stream>>>(a);
     return cudaGetLastError();
+}
+
+int epilogue_sub_lists(int n_tiles, int k_pad, int sm_count) {
+    // More lists per tile give the epilogue more CTAs; few enough lists that one merge CTA
+    // (8192 entries) can take them all keep the merge to one launch.  Each list stays at
+    // least k_pad long.
+    const int64_t cap = std::min<int64_t>(2 * (int64_t)sm_count, std::max<int64_t>(n_tiles, 8192 / k_pad));
+    int s = 1;
+    while (2 * s <= kTilePairs / k_pad && (int64_t)n_tiles * 2 * s <= cap) s <<= 1;
+    return s;
 }
 
 cudaError_t merge_candidates(Cand* buf, Cand* tmp, int n_lists, int k_pad, int n_groups_unused,
                              Cand** final_list, cudaStream_t stream) {
     (void)n_groups_unused;
-    // group * k_pad <= 8192 entries (128 KB of shared memory)
-    // lists per CTA: as many as fit 8192 entries, but no more than the lists there are
+    // lists per CTA: a power of two, group * k_pad <= 8192 entries (128 KB of shared memory),
+    // no more than the lists there are
     int fit = std::max(2, 8192 / k_pad);
     int group = 2;
     while (group < fit && group < n_lists) group <<= 1;
