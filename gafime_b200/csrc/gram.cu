@@ -7,28 +7,31 @@
 //     W = sum (a' ycen) b'    (ycen = y - mean y)
 // with g = identity (multiply; add / subtract reuse C) or g(b) = 1/safe(b) (divide).
 // They are computed by tcgen05.mma kind::f16 with fp32 accumulators in tensor memory
-// (TMEM columns 0-127: C, 128-255: Q, 256-383: W).  Each fp16 operand is a 2-term split of
-// a per-column power-of-two-scaled value (|value| <= 2^14, ~22 significant bits):
-//     XH/XL = split(s_x a'),  QH/QL = split(s_q a^2),  WH/WL = split(s_x a' * s_y ycen)  (A)
-//     BH/BL, BQH/BQL: the same for the B block's b' and g(b)^2                          (B)
-// and each Gram is hi.hi + hi.lo + lo.hi (the lo.lo term is below fp32 rounding): nine MMAs
-// per 16-row step.  One fp16 term per operand is not enough when a few rows dominate a sum
-// (heavy tails, near-zero divisors): their 2^-12 rounding would not average out.
+// (TMEM columns 0-127: C, 128-255: W, 256-383: Q).  Each fp16 operand is a 2-term split of a
+// per-column power-of-two-scaled value (|value| <= 2^14, ~22 significant bits):
+//     XH/XL = split(s_x a'),  QH/QL = split(s_q a^2)                                  (A)
+//     BH/BL = split(s b'),  WBH/WBL = split(s b' * s_y ycen),  BQH/BQL = split(s_q g(b)^2) (B)
+// and each Gram is hi.hi + hi.lo + lo.hi (the lo.lo term is below fp32 rounding).  C and W
+// share their A operand, so [BH|WBH] and [BL|WBL] are 256-row B operands of N = 256 MMAs:
+// six MMAs per 16-row step.  One fp16 term per operand is not enough when a few rows
+// dominate a sum (heavy tails, near-zero divisors): their 2^-12 rounding would not average
+// out.
 //
-// One CTA = one tile x one chunk of <= 8192 rows (each fp32 accumulation stays short), 10
+// One CTA = one tile x one chunk of <= 8192 rows (each fp32 accumulation stays short), 18
 // warps:
 //   warp 0      TMA: raw fp32 column tiles (128 columns x 16 rows, 64-byte swizzle, no
 //               multicast) of the A block and, off the diagonal, the B block, plus 16 scaled
-//               ycen values (plain bulk copy) -> 8-stage raw ring
-//   warp 1      TMEM allocation; one thread issues the nine MMAs of each step (A operands
+//               ycen values (plain bulk copy) -> 6-stage raw ring
+//   warp 1      TMEM allocation; one thread issues the six MMAs of each step (A operands
 //               from tensor memory, B operands from shared memory) and commits the operand
 //               stage back to its "empty" barrier
-//   warps 2-9   two converter groups of 4 warps, taking alternate steps; one column of each
-//               block per thread, in the TMEM lane quarter of its warp: centre, scale and
-//               split the values, write the six A rows to tensor memory (tcgen05.st) and the
-//               four B rows to K-major fp16 tiles (32-byte swizzle) in shared memory.
-//               Diagonal tiles of the multiply group load and convert one block only.  After
-//               the last step group 0 drains TMEM (tcgen05.ld) into fp32 chunk partials.
+//   warps 2-17  two converter groups of 8 warps, taking alternate steps; one column of each
+//               block and one 8-row K half per thread, in the TMEM lane quarter of its
+//               warp: centre, scale and split the values, write the four A rows to tensor
+//               memory (tcgen05.st) and the six B rows to K-major fp16 tiles (32-byte
+//               swizzle) in shared memory, 4-stage operand ring.  Diagonal tiles of the
+//               multiply group load and convert one block only.  After the last step group 0
+//               drains TMEM (tcgen05.ld) into fp32 chunk partials.
 // Keeping A in tensor memory halves the shared-memory reads of the MMAs (shared-memory
 // bandwidth, not the tensor pipe, bounds a 128 x 128 tile with both operands there).  The
 // raw fp32 matrix is read once per tile and chunk (concurrent tiles of one chunk share it
@@ -62,15 +65,19 @@ namespace {
 
 constexpr int kGT = 128;                      // Gram tile edge (columns)
 constexpr int kGK = 16;                       // rows per step (one MMA K step)
-constexpr int kRawStages = 8;
-constexpr int kOpStages = 2;                  // A operands in TMEM + B operands in shared memory
+constexpr int kRawStages = 6;
+constexpr int kOpStages = 4;                  // A operands in TMEM + B operands in shared memory
 constexpr int kRawBox = kGT * kGK * 4;        // one fp32 column tile: 128 columns x 16 rows
 constexpr int kRawStageBytes = 2 * kRawBox;   // A block + B block
 constexpr int kYsBytes = 64;                  // 16 scaled ycen values
 constexpr int kOpBytes = kGT * kGK * 2;       // one fp16 operand tile: 128 columns x 16 rows
-constexpr int kBStageBytes = 4 * kOpBytes;    // BH BL BQH BQL
-constexpr uint32_t kTmemA = 384;              // A operand stages after the C, Q, W accumulators
-constexpr uint32_t kTmemAStride = 64;         // XH XL QH QL WH WL: 8 columns each
+// B stage: [BH | WBH] [BL | WBL] (256-row N = 256 operands) BQH BQL
+constexpr int kBH = 0, kBL = 2 * kOpBytes, kBQH = 4 * kOpBytes, kBQL = 5 * kOpBytes;
+constexpr int kBStageBytes = 6 * kOpBytes;
+constexpr uint32_t kTmemCW = 0;               // [C | W] accumulators (256 columns)
+constexpr uint32_t kTmemQ = 256;              // Q accumulator (128 columns)
+constexpr uint32_t kTmemA = 384;              // A operand stages after the accumulators
+constexpr uint32_t kTmemAStride = 32;         // XH XL QH QL: 8 columns each
 constexpr int kConvWarps = 8;                 // warps per converter group (column x K half per thread)
 constexpr int kGroups = 2;                    // converter groups, interleaved over the steps
 constexpr int kGramThreads = (2 + kGroups * kConvWarps) * 32;
@@ -172,6 +179,9 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t addr) {
 // kind::f16 instruction descriptor: D f32, A/B f16, both K-major, N = 128, M = 128.
 constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(kGT >> 3) << 17) |
                             ((uint32_t)(kGT >> 4) << 24);
+// the same with N = 256: B = [b' rows | (s_y ycen) b' rows], D = [C | W]
+constexpr uint32_t kIdesc256 = (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(2 * kGT >> 3) << 17) |
+                               ((uint32_t)(kGT >> 4) << 24);
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
@@ -188,12 +198,13 @@ __device__ __forceinline__ float safe_recip(float v, float eps) {
 }
 
 // A operand in tensor memory (lane = row m, 8 columns = 16 fp16 along K), B in shared memory
-__device__ __forceinline__ void umma_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t accumulate) {
+__device__ __forceinline__ void umma_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                        uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
-        ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(kIdesc), "r"(accumulate)
+        ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
@@ -313,8 +324,8 @@ struct ConvCols {
 
 // Operand rows of one column and K half for one step
 struct StepOps {
-    Split8 x, q, w;   // A: s_x a',  s_q a^2,  (s_x a') (s_y ycen)
-    Split8 b, bq;     // B: s b',    s_q g(b)^2
+    Split8 x, q;        // A: s_x a',  s_q a^2
+    Split8 b, wb, bq;   // B: s b',    (s b') (s_y ycen),  s_q g(b)^2
 };
 
 // Convert K half h of column m for one step (A block, and the B block when kB).  kMask
@@ -342,15 +353,6 @@ __device__ __forceinline__ void convert_step(const unsigned char* raw, const uns
     }
     split8(v2, o.x);
     split8(t2, o.q);
-    {
-        const float4 y0 = *reinterpret_cast<const float4*>(ysm + 32 * h);
-        const float4 y1 = *reinterpret_cast<const float4*>(ysm + 32 * h + 16);
-        v2[0] = mul2(v2[0], pk(y0.x, y0.y));       // W: C * (s_y ycen)
-        v2[1] = mul2(v2[1], pk(y0.z, y0.w));
-        v2[2] = mul2(v2[2], pk(y1.x, y1.y));
-        v2[3] = mul2(v2[3], pk(y1.z, y1.w));
-    }
-    split8(v2, o.w);
     if (kB) {
         load_raw8(raw + kRawBox, m, h, x);
         if (kRecip) {
@@ -374,6 +376,17 @@ __device__ __forceinline__ void convert_step(const unsigned char* raw, const uns
         split8(v2, o.b);
         split8(t2, o.bq);
     }
+    {
+        // W's B operand: the B block's C operand times s_y ycen (the A block's on the
+        // multiply group's diagonal, where B = A)
+        const float4 y0 = *reinterpret_cast<const float4*>(ysm + 32 * h);
+        const float4 y1 = *reinterpret_cast<const float4*>(ysm + 32 * h + 16);
+        v2[0] = mul2(v2[0], pk(y0.x, y0.y));
+        v2[1] = mul2(v2[1], pk(y0.z, y0.w));
+        v2[2] = mul2(v2[2], pk(y1.x, y1.y));
+        v2[3] = mul2(v2[3], pk(y1.z, y1.w));
+    }
+    split8(v2, o.wb);
 }
 
 // Shared-memory and tensor-memory addresses of one converter thread
@@ -415,15 +428,15 @@ __device__ __forceinline__ void conv_loop(const ConvCtx& c, const ConvCols& kc, 
         tmem_st4(ta + 1 * 8, o.x.lo);
         tmem_st4(ta + 2 * 8, o.q.hi);
         tmem_st4(ta + 3 * 8, o.q.lo);
-        tmem_st4(ta + 4 * 8, o.w.hi);
-        tmem_st4(ta + 5 * 8, o.w.lo);
         unsigned char* sb = c.bop0 + os * kBStageBytes;
         const Split8& b0 = kB ? o.b : o.x;
         const Split8& b1 = kB ? o.bq : o.q;
-        store_half(sb + 0 * kOpBytes, c.m, c.h, b0.hi);
-        store_half(sb + 1 * kOpBytes, c.m, c.h, b0.lo);
-        store_half(sb + 2 * kOpBytes, c.m, c.h, b1.hi);
-        store_half(sb + 3 * kOpBytes, c.m, c.h, b1.lo);
+        store_half(sb + kBH, c.m, c.h, b0.hi);
+        store_half(sb + kBL, c.m, c.h, b0.lo);
+        store_half(sb + kBH + kOpBytes, c.m, c.h, o.wb.hi);
+        store_half(sb + kBL + kOpBytes, c.m, c.h, o.wb.lo);
+        store_half(sb + kBQH, c.m, c.h, b1.hi);
+        store_half(sb + kBQL, c.m, c.h, b1.lo);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         fence_async_smem();
         tc_fence_before();
@@ -517,18 +530,16 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
                 tc_fence_after();
                 const uint32_t ta = tmem + kTmemA + (uint32_t)(s * kTmemAStride);
                 const uint32_t bst = smem_u32(bop0 + s * kBStageBytes);
-                const uint64_t bH = umma_desc(bst + 0 * kOpBytes), bL = umma_desc(bst + 1 * kOpBytes);
-                const uint64_t bQH = umma_desc(bst + 2 * kOpBytes), bQL = umma_desc(bst + 3 * kOpBytes);
+                // [b' | ycen b'] tiles are 256 consecutive K-major rows: one N = 256 MMA
+                const uint64_t bH = umma_desc(bst + kBH), bL = umma_desc(bst + kBL);
+                const uint64_t bQH = umma_desc(bst + kBQH), bQL = umma_desc(bst + kBQL);
                 const uint32_t acc = k > 0 ? 1u : 0u;
-                umma_ta(tmem + 0, ta + 0 * 8, bH, acc);      // C: XH.BH
-                umma_ta(tmem + 0, ta + 0 * 8, bL, 1u);       //    XH.BL
-                umma_ta(tmem + 0, ta + 1 * 8, bH, 1u);       //    XL.BH
-                umma_ta(tmem + 128, ta + 2 * 8, bQH, acc);   // Q: QH.BQH
-                umma_ta(tmem + 128, ta + 2 * 8, bQL, 1u);    //    QH.BQL
-                umma_ta(tmem + 128, ta + 3 * 8, bQH, 1u);    //    QL.BQH
-                umma_ta(tmem + 256, ta + 4 * 8, bH, acc);    // W: WH.BH
-                umma_ta(tmem + 256, ta + 4 * 8, bL, 1u);     //    WH.BL
-                umma_ta(tmem + 256, ta + 5 * 8, bH, 1u);     //    WL.BH
+                umma_ta(tmem + kTmemCW, ta + 0 * 8, bH, kIdesc256, acc);   // [C|W]: XH.[BH|WBH]
+                umma_ta(tmem + kTmemCW, ta + 0 * 8, bL, kIdesc256, 1u);    //        XH.[BL|WBL]
+                umma_ta(tmem + kTmemCW, ta + 1 * 8, bH, kIdesc256, 1u);    //        XL.[BH|WBH]
+                umma_ta(tmem + kTmemQ, ta + 2 * 8, bQH, kIdesc, acc);      // Q:     QH.BQH
+                umma_ta(tmem + kTmemQ, ta + 2 * 8, bQL, kIdesc, 1u);       //        QH.BQL
+                umma_ta(tmem + kTmemQ, ta + 3 * 8, bQH, kIdesc, 1u);       //        QL.BQH
                 umma_commit(oempty0 + 8 * s);  // operand stage free once these MMAs have read it
             }
             umma_commit(accum);  // all issued MMAs complete (also on the error path)
@@ -590,9 +601,13 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
                 float* out = a.partial + ((int64_t)blockIdx.y * a.n_tiles + blockIdx.x) * 3 * kGT * kGT;
                 #pragma unroll 1
                 for (int idx = h; idx < 3 * kGT / 32; idx += 2) {
-                    const int c0 = idx * 32;   // column of the C | Q | W accumulators
+                    // partial gram gi = idx / 4 (C, Q, W); its TMEM columns: C at kTmemCW,
+                    // W at kTmemCW + 128, Q at kTmemQ
+                    const int gi = idx >> 2, cc = (idx & 3) * 32;
+                    const uint32_t tcol = (gi == 0 ? kTmemCW : gi == 1 ? kTmemQ : kTmemCW + kGT) + (uint32_t)cc;
+                    const int c0 = idx * 32;   // column of the partial's [C | Q | W] layout
                     float tt[32];
-                    tmem_ld32(tmem + tlane + (uint32_t)c0, tt);
+                    tmem_ld32(tmem + tlane + tcol, tt);
                     float* op = out + (int64_t)c0 * kGT + m;
                     #pragma unroll
                     for (int c = 0; c < 32; ++c) op[(int64_t)c * kGT] = tt[c];
