@@ -187,9 +187,9 @@ def measured_peaks():
 NCU_TRAFFIC_BYTES = {
     # profiles/pair_moments_config2.md: mul-group launch, 1.0298 GB read + 5.09 MB written
     ("config2", "pair_moments"): 1.0349e9,
-    # profiles/gram_tile_config2.md: 250k-row capture scaled to 1e6 rows, mean of the
-    # multiply (3.47 GB) and divide (5.52 GB) launches
-    ("config2", "gram_tc"): 4.5e9,
+    # profiles/gram_fused_config2.md: 250k-row capture (258 MB read: the fp32 matrix once;
+    # ~86 MB of chunk partials written) scaled by the rows processed to 1e6 rows
+    ("config2", "gram_tc"): 1.376e9,
 }
 
 
@@ -544,7 +544,8 @@ def run_ours(args):
         achieved = flops / (avg_ms / 1e3) / 1e12
         peak = peaks["bf16_tflops"]
         roof = {"bound": "tensor",
-                "kernel": ("gram_tile_kernel (tcgen05 kind::f16, 2-term fp16 splits, TMEM fp32)"
+                "kernel": ("gram_fused_kernel (TMA fp32 tiles, in-kernel 2-term fp16 split, A operands in "
+                           "TMEM, tcgen05 kind::f16, fp32 TMEM accumulators)"
                            if dom == "gram_tc" else "pair_moments_kernel (CUDA-core fp32, fp64 flush)"),
                 "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_source": f"bf16_tflops (burst) of {peak_kind} MEASURED_PEAKS.json",
