@@ -165,24 +165,28 @@ int score_ops(Bucket& b, const ColumnStats& cs, const Plan& plan, const TileCoor
             if (e != cudaSuccess) return status_from(e);
         }
     }
+    EpilogueArgs a;
     for (int o = 0; o < n_ops; ++o) {
-        EpilogueArgs a;
-        a.moments = mom[ops[o] == GAFIME_INTERACT_DIV ? 1 : 0];
-        a.splits = group_splits[ops[o] == GAFIME_INTERACT_DIV ? 1 : 0];
-        a.tiles = d_tiles;
-        a.n_tiles = nt;
-        a.f = b.f;
-        a.colstats = cs.d_col;
-        a.ystats = cs.d_y;
-        a.op = ops[o];
-        a.k_pad = k_pad;
-        a.sub_lists = sub_lists;
-        a.cands = cands[o];
-        a.all_scores = all_scores;
+        const int grp = ops[o] == GAFIME_INTERACT_DIV ? 1 : 0;
+        a.moments[o] = mom[grp];
+        a.splits[o] = group_splits[grp];
+        a.op[o] = ops[o];
+        a.cands[o] = cands[o];
+    }
+    a.n_ops = n_ops;
+    a.tiles = d_tiles;
+    a.n_tiles = nt;
+    a.f = b.f;
+    a.colstats = cs.d_col;
+    a.ystats = cs.d_y;
+    a.k_pad = k_pad;
+    a.sub_lists = sub_lists;
+    a.all_scores = all_scores;
+    {
         KernelTimer timer(b.stream, GAFIME_KERNEL_EPILOGUE_TOPK);
         e = launch_epilogue_topk(a, b.stream);
-        if (e != cudaSuccess) return status_from(e);
     }
+    if (e != cudaSuccess) return status_from(e);
     return GAFIME_SUCCESS;
 }
 
@@ -251,14 +255,14 @@ extern "C" int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact
     if (st != GAFIME_SUCCESS) return st;
 
     std::vector<Cand> host((size_t)k_pad * n_ops);
+    Cand* fin = nullptr;
+    {
+        KernelTimer timer(b.stream, GAFIME_KERNEL_MERGE);
+        e = merge_candidates(cands[0], tmp[0], n_lists, k_pad, n_ops, per_op, &fin, b.stream);
+    }
+    if (e != cudaSuccess) return status_from(e);
     for (int o = 0; o < n_ops; ++o) {
-        Cand* fin = nullptr;
-        {
-            KernelTimer timer(b.stream, GAFIME_KERNEL_MERGE);
-            e = merge_candidates(cands[o], tmp[o], n_lists, k_pad, 0, &fin, b.stream);
-        }
-        if (e != cudaSuccess) return status_from(e);
-        e = cudaMemcpyAsync(host.data() + (size_t)k_pad * o, fin, sizeof(Cand) * k_pad,
+        e = cudaMemcpyAsync(host.data() + (size_t)k_pad * o, fin + per_op * o, sizeof(Cand) * k_pad,
                             cudaMemcpyDeviceToHost, b.stream);
         if (e != cudaSuccess) return status_from(e);
     }

@@ -110,26 +110,31 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
 
 // Scoring epilogue + per-tile top-k (select.cu).
 struct EpilogueArgs {
-    const double* moments;       // from launch_pair_moments (mul or div group)
-    int splits;
+    // per operator (blockIdx.z): moments from the pair-moment kernels (mul or div group),
+    // their row splits, the GAFIME_INTERACT_* id, and the candidate lists
+    const double* moments[4];
+    int splits[4];
+    int op[4];
+    Cand* cands[4];              // [n_tiles * sub_lists * k_pad] per op (nullptr: scores only)
+    int n_ops;
     const TileCoord* tiles;
     int n_tiles;
     int64_t f;
     const double* colstats;      // [f*4]
     const double* ystats;        // [4]
-    int op;                      // GAFIME_INTERACT_*
     int k_pad;                   // power of two >= k, <= 4096
     int sub_lists;               // candidate lists per tile (power of two, 4096 / sub_lists >= k_pad)
-    Cand* cands;                 // [n_tiles * sub_lists * k_pad] for this op
-    double* all_scores;          // nullable, [P] triangle order
+    double* all_scores;          // nullable, [P] triangle order (n_ops = 1)
 };
 cudaError_t launch_epilogue_topk(const EpilogueArgs& a, cudaStream_t stream);
 // Candidate lists per tile for a top-k call: enough CTAs to fill the GPU.
 int epilogue_sub_lists(int n_tiles, int k_pad, int sm_count);
 
-// Merge n_lists sorted candidate lists of k_pad entries down to one (in place
-// ping-pong between buf and tmp); returns the buffer holding the final list.
-cudaError_t merge_candidates(Cand* buf, Cand* tmp, int n_lists, int k_pad, int n_groups,
+// Merge n_lists sorted candidate lists of k_pad entries down to one, for n_ops operators at
+// once (operator o's lists start op_stride entries after operator o-1's, in buf and tmp);
+// ping-pong between buf and tmp.  *final_list holds operator 0's result; operator o's is
+// op_stride entries further.
+cudaError_t merge_candidates(Cand* buf, Cand* tmp, int n_lists, int k_pad, int n_ops, size_t op_stride,
                              Cand** final_list, cudaStream_t stream);
 
 // Mutual-information scoring (mi.cu): centred product, equal-width bins.

@@ -628,6 +628,410 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
     }
 }
 
+// ---- the CTA-pair Gram kernel (cta_group::2) ----------------------------------------
+//
+// A cluster of two CTAs computes a 256 x 128 block of pairs: CTA r holds the A operands of
+// its own 128-column block I_r in its tensor memory (rows r*128 .. r*128+127 of the
+// M = 256 MMA), and half of every B operand in its shared memory (the MMA reads the two
+// halves from the two CTAs):
+//   N = 256 [C | W] operand: CTA 0 holds s b' (the C half), CTA 1 holds s b' * s_y ycen
+//   N = 128 Q operand:       CTA r holds s_q g(b)^2 of B columns r*64 .. r*64+63
+// so each SM converts half of the B work of the single-CTA kernel and its tensor cores
+// read half the B bytes from shared memory.  CTA 0's MMA thread issues the cta_group::2
+// MMAs for the pair; both CTAs' converters arrive on CTA 0's "operand full" barrier (CTA 1
+// remotely), and tcgen05.commit multicasts "operand free" and "accumulators done" to both.
+
+struct PairCoord {
+    int i0, i1, j;   // A blocks of CTA 0 and CTA 1, B block
+    int t0, t1;      // partial slots of tiles (i0, j), (i1, j); -1: not needed
+};
+
+struct PairArgs {
+    const PairCoord* pairs;
+    int n_slots;              // partial slots per chunk
+    int64_t chunk_rows, rows, n, f;
+    const float* ys;
+    const double* cs;
+    int recip;
+    float eps;
+    float* partial;           // [chunk][slot][3][128 n][128 m]
+    int* err;
+};
+
+constexpr int kPBStageBytes = 2 * kOpBytes + kOpBytes;   // N256 half hi+lo (4 KB each), Q half hi+lo (2 KB each)
+constexpr int kPB_H = 0, kPB_L = kOpBytes, kPB_QH = 2 * kOpBytes, kPB_QL = 2 * kOpBytes + kOpBytes / 2;
+constexpr int kPRawStages = 8;
+constexpr size_t kPairSmem = (size_t)kPRawStages * (kRawStageBytes + kYsBytes) + (size_t)kOpStages * kPBStageBytes +
+                             1024 + 256;
+static_assert(kPairSmem <= 232448, "shared memory per CTA");
+// kind::f16 instruction descriptors with M = 256 (cta_group::2)
+constexpr uint32_t kIdescP256 = (1u << 4) | ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+constexpr uint32_t kIdescP128 = (1u << 4) | ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+
+__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// arrive on both CTAs' copy of a barrier once every tcgen05 op issued so far has completed
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+    asm volatile(
+        "{\n\t.reg .b16 m;\n\t"
+        "mov.b16 m, 3;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}"
+        ::"r"(bar)
+        : "memory");
+}
+
+// arrive on the barrier at the same shared-memory offset in CTA `rank` of the cluster
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar, uint32_t rank) {
+    asm volatile(
+        "{\n\t.reg .b32 ra;\n\t"
+        "mapa.shared::cluster.u32 ra, %0, %1;\n\t"
+        "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n\t}"
+        ::"r"(bar), "r"(rank)
+        : "memory");
+}
+
+// Bounded wait with cluster-scope acquire (arrivals come from both CTAs of the pair)
+__device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(kSuspendNs)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int* err, int code) {
+    if (mbar_try_cluster(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (long long i = 1; i < kSpinLimit; ++i) {
+        if (mbar_try_cluster(bar, parity)) return true;
+        if ((i & 15) == 0 && global_ns() - t0 > kWaitLimitNs) break;
+    }
+    atomicCAS(err, 0, code);
+    return false;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+struct PairOps {
+    Split8 x, q;    // A: s_x a', s_q a^2
+    Split8 bn;      // B, N = 256 half: s b' (CTA 0) or s b' * s_y ycen (CTA 1)
+    Split8 bq;      // B, Q half: s_q g(b)^2 (threads of the CTA's 64 columns)
+};
+
+// One step of one converter thread of a CTA pair: column m, K half h.  kSame: the B block
+// is the A block (multiply group, I_r == J); kRecip: B operand 1/safe(b); kQ: this thread's
+// column is in the CTA's Q half.
+template <bool kMask, bool kSame, bool kRecip>
+__device__ __forceinline__ void convert_pair_step(const unsigned char* raw, const unsigned char* ysm, int m, int h,
+                                                  int valid, int rank, bool q_half, const ConvCols& k, float eps,
+                                                  PairOps& o) {
+    float x[8];
+    uint64_t x2[4], v2[4], t2[4];
+    load_raw8(raw, m, h, x);
+    #pragma unroll
+    for (int p = 0; p < 4; ++p) x2[p] = pk(x[2 * p], x[2 * p + 1]);
+    {
+        const uint64_t sx = pk(k.sx_a, k.sx_a), nmu = pk(-k.mus_a, -k.mus_a), sq = pk(k.sq_a, k.sq_a);
+        #pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            v2[p] = fma2(x2[p], sx, nmu);
+            t2[p] = mul2(mul2(x2[p], x2[p]), sq);
+            if (kMask) {
+                const bool v0 = 8 * h + 2 * p < valid, v1 = 8 * h + 2 * p + 1 < valid;
+                const float2 c = upk(v2[p]), q = upk(t2[p]);
+                v2[p] = pk(v0 ? c.x : 0.f, v1 ? c.y : 0.f);
+                t2[p] = pk(v0 ? q.x : 0.f, v1 ? q.y : 0.f);
+            }
+        }
+        split8(v2, o.x);
+        split8(t2, o.q);
+    }
+    if (!kSame) {
+        load_raw8(raw + kRawBox, m, h, x);
+        if (kRecip) {
+            #pragma unroll
+            for (int r = 0; r < 8; ++r) x[r] = safe_recip(x[r], eps);
+        }
+        #pragma unroll
+        for (int p = 0; p < 4; ++p) x2[p] = pk(x[2 * p], x[2 * p + 1]);
+        const uint64_t sxb = pk(k.sx_b, k.sx_b), nmub = pk(-k.mus_b, -k.mus_b), sqb = pk(k.sq_b, k.sq_b);
+        #pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            v2[p] = fma2(x2[p], sxb, nmub);
+            t2[p] = mul2(mul2(x2[p], x2[p]), sqb);
+            if (kMask) {
+                const bool v0 = 8 * h + 2 * p < valid, v1 = 8 * h + 2 * p + 1 < valid;
+                const float2 c = upk(v2[p]), q = upk(t2[p]);
+                v2[p] = pk(v0 ? c.x : 0.f, v1 ? c.y : 0.f);
+                t2[p] = pk(v0 ? q.x : 0.f, v1 ? q.y : 0.f);
+            }
+        }
+        if (q_half) split8(t2, o.bq);
+    } else if (q_half) {
+        o.bq = o.q;
+    }
+    if (rank == 1) {
+        const float4 y0 = *reinterpret_cast<const float4*>(ysm + 32 * h);
+        const float4 y1 = *reinterpret_cast<const float4*>(ysm + 32 * h + 16);
+        v2[0] = mul2(v2[0], pk(y0.x, y0.y));
+        v2[1] = mul2(v2[1], pk(y0.z, y0.w));
+        v2[2] = mul2(v2[2], pk(y1.x, y1.y));
+        v2[3] = mul2(v2[3], pk(y1.z, y1.w));
+        split8(v2, o.bn);
+    } else if (!kSame) {
+        split8(v2, o.bn);
+    } else {
+        o.bn = o.x;
+    }
+}
+
+struct PairCtx {
+    const unsigned char* raw0;
+    const unsigned char* ys0;
+    unsigned char* bop0;
+    uint32_t rfull0, rempty0, ofull0, oempty0;
+    uint32_t tmem_a;   // tmem + lane quarter + kTmemA + 4h
+    int m, h, lane, rank;
+    bool q_half;
+    int nk, n_full;
+    int64_t rows_left;
+    float eps;
+    int* err;
+};
+
+template <bool kSame, bool kRecip>
+__device__ __forceinline__ void pair_conv_loop(const PairCtx& c, const ConvCols& kc, int grp) {
+    for (int k = grp; k < c.nk; k += kGroups) {
+        const int rs = k % kPRawStages, os = k % kOpStages;
+        if (!warp_wait(c.rfull0 + 8 * rs, (k / kPRawStages) & 1, c.err, 5, c.lane)) return;
+        const unsigned char* raw = c.raw0 + rs * kRawStageBytes;
+        const unsigned char* ysm = c.ys0 + rs * kYsBytes;
+        PairOps o;
+        if (k < c.n_full) {
+            convert_pair_step<false, kSame, kRecip>(raw, ysm, c.m, c.h, kGK, c.rank, c.q_half, kc, c.eps, o);
+        } else {
+            const int64_t left = c.rows_left - (int64_t)k * kGK;
+            const int valid = left <= 0 ? 0 : (int)left;
+            convert_pair_step<true, kSame, kRecip>(raw, ysm, c.m, c.h, valid, c.rank, c.q_half, kc, c.eps, o);
+        }
+        // this CTA's operand stage is free once the pair's MMAs of step k - kOpStages completed
+        if (k >= kOpStages && !warp_wait(c.oempty0 + 8 * os, ((k / kOpStages) - 1) & 1, c.err, 6, c.lane)) return;
+        tc_fence_after();
+        const uint32_t ta = c.tmem_a + (uint32_t)(os * kTmemAStride);
+        tmem_st4(ta + 0 * 8, o.x.hi);
+        tmem_st4(ta + 1 * 8, o.x.lo);
+        tmem_st4(ta + 2 * 8, o.q.hi);
+        tmem_st4(ta + 3 * 8, o.q.lo);
+        unsigned char* sb = c.bop0 + os * kPBStageBytes;
+        store_half(sb + kPB_H, c.m, c.h, o.bn.hi);
+        store_half(sb + kPB_L, c.m, c.h, o.bn.lo);
+        if (c.q_half) {
+            const int mq = c.m - 64 * c.rank;   // row of the CTA's 64-row Q half
+            store_half(sb + kPB_QH, mq, c.h, o.bq.hi);
+            store_half(sb + kPB_QL, mq, c.h, o.bq.lo);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        fence_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (c.lane == 0) {
+            // CTA 0's barrier counts both CTAs' converter warps
+            if (c.rank == 0) mbar_arrive(c.ofull0 + 8 * os);
+            else mbar_arrive_cluster(c.ofull0 + 8 * os, 0);
+            // the raw stage is released after the stores that consume it
+            mbar_arrive(c.rempty0 + 8 * rs);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kGramThreads, 1)
+gram_pair_kernel(const __grid_constant__ CUtensorMap xmap, const PairArgs a) {
+    extern __shared__ __align__(1024) unsigned char gsmem_raw[];
+    unsigned char* smem = (unsigned char*)(((uintptr_t)gsmem_raw + 1023) & ~(uintptr_t)1023);
+    unsigned char* raw0 = smem;
+    unsigned char* bop0 = raw0 + kPRawStages * kRawStageBytes;
+    unsigned char* ys0 = bop0 + kOpStages * kPBStageBytes;
+    uint64_t* bars = (uint64_t*)(ys0 + kPRawStages * kYsBytes);
+    const uint32_t rfull0 = smem_u32(bars), rempty0 = smem_u32(bars + kPRawStages);
+    const uint32_t ofull0 = smem_u32(bars + 2 * kPRawStages), oempty0 = smem_u32(bars + 2 * kPRawStages + kOpStages);
+    const uint32_t accum = smem_u32(bars + 2 * kPRawStages + 2 * kOpStages);
+    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * kPRawStages + 2 * kOpStages + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rank = (int)(blockIdx.x & 1);   // cluster dims (2, 1, 1)
+    const PairCoord pc = a.pairs[blockIdx.x >> 1];
+    const int blk_a = rank ? pc.i1 : pc.i0;
+    const int slot = rank ? pc.t1 : pc.t0;
+    const bool same = (blk_a == pc.j) && !a.recip;
+    const int64_t r0 = (int64_t)blockIdx.y * a.chunk_rows;
+    const int64_t r1 = min(r0 + a.chunk_rows, a.rows);
+    const int nk = r1 > r0 ? (int)((r1 - r0) / kGK) : 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPRawStages; ++s) {
+            mbar_init(rfull0 + 8 * s, 1);
+            mbar_init(rempty0 + 8 * s, kConvWarps);
+        }
+        for (int s = 0; s < kOpStages; ++s) {
+            mbar_init(ofull0 + 8 * s, 2 * kConvWarps);   // used in CTA 0: both CTAs' warps
+            mbar_init(oempty0 + 8 * s, 1);
+        }
+        mbar_init(accum, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    // both CTAs' barriers are initialised before any remote arrive
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint32_t bytes = (same ? (uint32_t)kRawBox : (uint32_t)kRawStageBytes) + (uint32_t)(kGK * 4);
+            int issued = 0;
+            bool ok = true;
+            for (int k = 0; k < nk; ++k) {
+                const int s = k % kPRawStages;
+                if (k >= kPRawStages && !(ok = mbar_wait(rempty0 + 8 * s, ((k / kPRawStages) - 1) & 1, a.err, 1)))
+                    break;
+                const uint32_t full = rfull0 + 8 * s;
+                mbar_expect_tx(full, bytes);
+                const uint32_t st = smem_u32(raw0 + s * kRawStageBytes);
+                const int64_t row = r0 + (int64_t)k * kGK;
+                tma_load_2d(st, &xmap, full, (int)row, blk_a * kGT);
+                if (!same) tma_load_2d(st + kRawBox, &xmap, full, (int)row, pc.j * kGT);
+                bulk_load(smem_u32(ys0 + s * kYsBytes), a.ys + row, (uint32_t)(kGK * 4), full);
+                ++issued;
+            }
+            if (!ok)
+                for (int k = max(0, issued - kPRawStages); k < issued; ++k)
+                    mbar_wait(rfull0 + 8 * (k % kPRawStages), (k / kPRawStages) & 1, a.err, 4);
+        }
+    } else if (warp == 1) {
+        if (rank == 0 && lane == 0) {
+            for (int k = 0; k < nk; ++k) {
+                const int s = k % kOpStages;
+                if (!mbar_wait_cluster(ofull0 + 8 * s, (k / kOpStages) & 1, a.err, 2)) break;
+                tc_fence_after();
+                const uint32_t ta = tmem + kTmemA + (uint32_t)(s * kTmemAStride);
+                const uint32_t bst = smem_u32(bop0 + s * kPBStageBytes);
+                const uint64_t bH = umma_desc(bst + kPB_H), bL = umma_desc(bst + kPB_L);
+                const uint64_t bQH = umma_desc(bst + kPB_QH), bQL = umma_desc(bst + kPB_QL);
+                const uint32_t acc = k > 0 ? 1u : 0u;
+                umma_pair(tmem + kTmemCW, ta + 0 * 8, bH, kIdescP256, acc);
+                umma_pair(tmem + kTmemCW, ta + 0 * 8, bL, kIdescP256, 1u);
+                umma_pair(tmem + kTmemCW, ta + 1 * 8, bH, kIdescP256, 1u);
+                umma_pair(tmem + kTmemQ, ta + 2 * 8, bQH, kIdescP128, acc);
+                umma_pair(tmem + kTmemQ, ta + 2 * 8, bQL, kIdescP128, 1u);
+                umma_pair(tmem + kTmemQ, ta + 3 * 8, bQH, kIdescP128, 1u);
+                umma_commit_pair(oempty0 + 8 * s);
+            }
+            umma_commit_pair(accum);
+        }
+    } else {
+        const int cw = (warp - 2) % kConvWarps;
+        const int grp = (warp - 2) / kConvWarps;
+        const int quarter = warp & 3;
+        const int h = cw >> 2;
+        const int m = quarter * 32 + lane;
+        const uint32_t tlane = (uint32_t)(quarter * 32) << 16;
+        const int64_t col_a = (int64_t)blk_a * kGT + m, col_b = (int64_t)pc.j * kGT + m;
+        ConvCols kc{0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (col_a < a.f) {
+            const double* c = a.cs + col_a * 12;
+            kc.sx_a = (float)c[0];
+            kc.sq_a = (float)c[1];
+            kc.mus_a = (float)c[9] * kc.sx_a;
+        }
+        if (col_b < a.f) {
+            const double* c = a.cs + col_b * 12;
+            const int o = a.recip ? 3 : 0;
+            kc.sx_b = (float)c[o];
+            kc.sq_b = (float)c[o + 1];
+            kc.mus_b = (float)c[a.recip ? 5 : 9] * kc.sx_b;
+        }
+        PairCtx cx;
+        cx.raw0 = raw0;
+        cx.ys0 = ys0;
+        cx.bop0 = bop0;
+        cx.rfull0 = rfull0;
+        cx.rempty0 = rempty0;
+        cx.ofull0 = ofull0;
+        cx.oempty0 = oempty0;
+        cx.tmem_a = tmem + tlane + kTmemA + 4 * h;
+        cx.m = m;
+        cx.h = h;
+        cx.lane = lane;
+        cx.rank = rank;
+        cx.q_half = (m >> 6) == rank;
+        cx.nk = nk;
+        cx.rows_left = a.n - r0;
+        {
+            const int64_t full = cx.rows_left / kGK;
+            cx.n_full = full <= 0 ? 0 : (full >= nk ? nk : (int)full);
+        }
+        cx.eps = a.eps;
+        cx.err = a.err;
+        if (same) pair_conv_loop<true, false>(cx, kc, grp);
+        else if (a.recip) pair_conv_loop<false, true>(cx, kc, grp);
+        else pair_conv_loop<false, false>(cx, kc, grp);
+        if (grp == 0) {
+            const bool done = warp_wait(accum, 0, a.err, 3, lane);
+            tc_fence_after();
+            if (done && nk > 0 && slot >= 0) {
+                float* out = a.partial + ((int64_t)blockIdx.y * a.n_slots + slot) * 3 * kGT * kGT;
+                #pragma unroll 1
+                for (int idx = h; idx < 3 * kGT / 32; idx += 2) {
+                    const int gi = idx >> 2, cc = (idx & 3) * 32;
+                    const uint32_t tcol = (gi == 0 ? kTmemCW : gi == 1 ? kTmemQ : kTmemCW + kGT) + (uint32_t)cc;
+                    const int c0 = idx * 32;
+                    float tt[32];
+                    tmem_ld32(tmem + tlane + tcol, tt);
+                    float* op = out + (int64_t)c0 * kGT + m;
+                    #pragma unroll
+                    for (int c = 0; c < 32; ++c) op[(int64_t)c * kGT] = tt[c];
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        // every MMA of the pair (which reads both CTAs' shared memory and writes both TMEMs)
+        // has completed before either CTA frees TMEM or exits
+        if (lane == 0) mbar_wait(accum, 0, a.err, 7);
+        __syncwarp();
+    }
+    __syncthreads();
+    cluster_sync_all();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
 // ---- per-column statistics and scales -------------------------------------------
 
 // Per column and row split: [0] min x, [1] max x, [2] sum g, [3] sum g^2, [4] sum g*ycen,
@@ -971,6 +1375,19 @@ int64_t max_chunk_rows() {
 
 }  // namespace
 
+// CTA-pair Gram kernel (cta_group::2) when GAFIME_GRAM_PAIRS=1.  Off by default: it
+// halves each SM's B-operand conversion and shared-memory traffic, but the two CTAs of a
+// pair wait on each other every step, and on the measured workloads (1e6 x 256 and
+// 2e6 x 2048) it is 3-35 % slower than the single-CTA kernel.
+bool gram_pairs_enabled() {
+    static int env = -1;
+    if (env < 0) {
+        const char* v = getenv("GAFIME_GRAM_PAIRS");
+        env = (v && std::string(v) == "1") ? 1 : 0;
+    }
+    return env != 0;
+}
+
 bool gram_path_enabled(const Bucket& b) {
     static int env = -1;
     if (env < 0) {
@@ -1001,8 +1418,30 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     }
     const int nt = (int)t128.size();
     if (nt == 0) return cudaSuccess;
+    // CTA pairs (cta_group::2): the 128-tiles of one B block J, two A blocks per pair; an odd
+    // one out is paired with itself and its second result discarded
+    const bool pairs_on = gram_pairs_enabled();
+    std::vector<PairCoord> pairs;
+    if (pairs_on) {
+        std::vector<std::vector<std::pair<int, int>>> by_j(nb128);
+        for (int s = 0; s < nt; ++s) by_j[t128[s].bj].push_back({t128[s].bi, s});
+        for (int J = 0; J < nb128; ++J) {
+            auto& v = by_j[J];
+            std::sort(v.begin(), v.end());
+            for (size_t q = 0; q < v.size(); q += 2) {
+                PairCoord pc;
+                pc.j = J;
+                pc.i0 = v[q].first;
+                pc.t0 = v[q].second;
+                pc.i1 = q + 1 < v.size() ? v[q + 1].first : v[q].first;
+                pc.t1 = q + 1 < v.size() ? v[q + 1].second : -1;
+                pairs.push_back(pc);
+            }
+        }
+    }
+    const int ctas_per_chunk = pairs_on ? 2 * (int)pairs.size() : nt;
     // row chunks: <= max_chunk_rows() rows, enough CTAs for every SM
-    int64_t want = std::max<int64_t>(1, (4 * (int64_t)b.sm_count + nt - 1) / nt);
+    int64_t want = std::max<int64_t>(1, (4 * (int64_t)b.sm_count + ctas_per_chunk - 1) / ctas_per_chunk);
     int64_t chunk = (ld + want - 1) / want;
     chunk = std::min<int64_t>(max_chunk_rows(), std::max<int64_t>(1024, chunk));
     chunk = (chunk + kRowPad - 1) / kRowPad * kRowPad;
@@ -1019,7 +1458,8 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     int splits = (int)std::max<int64_t>(1, std::min<int64_t>((8 * (int64_t)b.sm_count + col_groups - 1) / col_groups,
                                                              (ld + 2047) / 2048));
     splits = std::min(splits, 256);
-    size_t off_colp = (off_t128 + t128.size() * sizeof(TileCoord) + 255) / 256 * 256;
+    size_t off_pairs = (off_t128 + t128.size() * sizeof(TileCoord) + 255) / 256 * 256;
+    size_t off_colp = (off_pairs + t128.size() * sizeof(PairCoord) + 255) / 256 * 256;
     size_t off_cs = (off_colp + (size_t)f * splits * sizeof(GramColPart) + 255) / 256 * 256;
     size_t off_ys = (off_cs + (size_t)f * 12 * sizeof(double) + 255) / 256 * 256;
     size_t off_err = (off_ys + (size_t)ld * sizeof(float) + 255) / 256 * 256;
@@ -1030,6 +1470,7 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     float* partial = (float*)base;
     int* d_lut = (int*)(base + off_lut);
     TileCoord* d_t128 = (TileCoord*)(base + off_t128);
+    PairCoord* d_pairs = (PairCoord*)(base + off_pairs);
     GramColPart* colp = (GramColPart*)(base + off_colp);
     double* d_cs = (double*)(base + off_cs);
     float* d_ys = (float*)(base + off_ys);
@@ -1039,6 +1480,8 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     e = cudaMemcpyAsync(d_lut, lut.data(), lut.size() * sizeof(int), cudaMemcpyHostToDevice, stream);
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(d_t128, t128.data(), t128.size() * sizeof(TileCoord), cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess && pairs_on)
+        e = cudaMemcpyAsync(d_pairs, pairs.data(), pairs.size() * sizeof(PairCoord), cudaMemcpyHostToDevice, stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(d_err, 0, 128, stream);
     if (e != cudaSuccess) return e;
 
@@ -1088,13 +1531,43 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     ga.eps = eps;
     ga.partial = partial;
     ga.err = d_err;
-    e = cudaFuncSetAttribute(gram_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGramSmem);
-    if (e != cudaSuccess) return e;
-    {
+    if (pairs_on) {
+        PairArgs pa;
+        pa.pairs = d_pairs;
+        pa.n_slots = nt;
+        pa.chunk_rows = chunk;
+        pa.rows = ld;
+        pa.n = n;
+        pa.f = f;
+        pa.ys = d_ys;
+        pa.cs = d_cs;
+        pa.recip = recip ? 1 : 0;
+        pa.eps = eps;
+        pa.partial = partial;
+        pa.err = d_err;
+        e = cudaFuncSetAttribute(gram_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem);
+        if (e != cudaSuccess) return e;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(2 * pairs.size()), (unsigned)n_chunks);
+        cfg.blockDim = dim3(kGramThreads);
+        cfg.dynamicSmemBytes = kPairSmem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        KernelTimer timer(stream, GAFIME_KERNEL_GRAM_TC);
+        e = cudaLaunchKernelEx(&cfg, gram_pair_kernel, xmap, pa);
+    } else {
+        e = cudaFuncSetAttribute(gram_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGramSmem);
+        if (e != cudaSuccess) return e;
         KernelTimer timer(stream, GAFIME_KERNEL_GRAM_TC);
         gram_fused_kernel<<<dim3((unsigned)nt, (unsigned)n_chunks), kGramThreads, kGramSmem, stream>>>(xmap, ga);
+        e = cudaGetLastError();
     }
-    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
 
     GramReduceArgs ra;

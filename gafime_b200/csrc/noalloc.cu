@@ -162,17 +162,18 @@ extern "C" int gafime_allpairs_scores_noalloc(const float* d_x, int64_t ld, cons
                             interact_type == GAFIME_INTERACT_DIV, div_eps, moments, s);
     if (e != cudaSuccess) return status_from(e);
     EpilogueArgs a;
-    a.moments = moments;
-    a.splits = splits;
+    a.moments[0] = moments;
+    a.splits[0] = splits;
+    a.op[0] = interact_type;
+    a.cands[0] = nullptr;  // scores only
+    a.n_ops = 1;
     a.tiles = tiles;
     a.n_tiles = nt;
     a.f = f;
     a.colstats = colstats;
     a.ystats = ystats;
-    a.op = interact_type;
     a.k_pad = 1;
     a.sub_lists = 1;
-    a.cands = nullptr;  // scores only
     a.all_scores = d_scores_out;
     e = launch_epilogue_topk(a, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);

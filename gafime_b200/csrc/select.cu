@@ -38,13 +38,17 @@ __device__ __forceinline__ double pearson(double n, double sx, double sxx, doubl
     return cov / sqrt(d);
 }
 
-// Grid (n_tiles, sub_lists): CTA (t, s) scores the pairs e in [s*L, (s+1)*L) of tile t
-// (L = kTilePairs / sub_lists) and writes the k_pad best of them, sorted, as list
-// t * sub_lists + s.
+// Grid (n_tiles, sub_lists, n_ops): CTA (t, s, o) scores operator o on the pairs e in
+// [s*L, (s+1)*L) of tile t (L = kTilePairs / sub_lists) and writes the k_pad best of them,
+// sorted, as list t * sub_lists + s of that operator.
 __global__ void __launch_bounds__(kEpiThreads) epilogue_topk_kernel(EpilogueArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Cand* s = reinterpret_cast<Cand*>(smem_raw);  // [L]
     const int t = blockIdx.x;
+    const int oi = blockIdx.z;
+    const int op = a.op[oi], splits = a.splits[oi];
+    const double* moments = a.moments[oi];
+    Cand* cands = a.cands[oi];
     const int L = kTilePairs / a.sub_lists;
     const int e0 = blockIdx.y * L;
     const TileCoord tc = a.tiles[t];
@@ -58,15 +62,15 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_topk_kernel(EpilogueArgs
         c.pad = 0;
         if (i < j && j < f) {
             double S1 = 0.0, S2 = 0.0, S3 = 0.0;
-            for (int sp = 0; sp < a.splits; ++sp) {
-                const double* m = a.moments + ((int64_t)sp * a.n_tiles + t) * 3 * kTilePairs;
+            for (int sp = 0; sp < splits; ++sp) {
+                const double* m = moments + ((int64_t)sp * a.n_tiles + t) * 3 * kTilePairs;
                 S1 += m[e];
                 S2 += m[kTilePairs + e];
                 S3 += m[2 * kTilePairs + e];
             }
             double sx, sxx, cov;
-            if (a.op == GAFIME_INTERACT_ADD || a.op == GAFIME_INTERACT_SUB) {
-                double sg = a.op == GAFIME_INTERACT_ADD ? 1.0 : -1.0;
+            if (op == GAFIME_INTERACT_ADD || op == GAFIME_INTERACT_SUB) {
+                double sg = op == GAFIME_INTERACT_ADD ? 1.0 : -1.0;
                 const double* ci = a.colstats + i * 4;
                 const double* cj = a.colstats + j * 4;
                 sx = ci[0] + sg * cj[0];
@@ -89,22 +93,25 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_topk_kernel(EpilogueArgs
         }
         s[q] = c;
     }
-    if (a.cands == nullptr) return;  // scores only (uniform across the block)
+    if (cands == nullptr) return;  // scores only (uniform across the block)
     __syncthreads();
     bitonic_sort(s, L);
-    Cand* out = a.cands + ((int64_t)t * a.sub_lists + blockIdx.y) * a.k_pad;
+    Cand* out = cands + ((int64_t)t * a.sub_lists + blockIdx.y) * a.k_pad;
     for (int q = threadIdx.x; q < a.k_pad; q += kEpiThreads) out[q] = s[q];
 }
 
 // Each CTA reduces `group` consecutive sorted lists (k_pad entries each; lists beyond
-// n_lists are empty) to their k_pad best entries, sorted.  Pairwise tree: for runs A and B
+// n_lists are empty) of operator blockIdx.y to their k_pad best entries, sorted.  Pairwise tree: for runs A and B
 // sorted best-first, better(A[i], B[k-1-i]) over i is a bitonic sequence holding the k best
 // of A and B, which log2(k) half-cleaner stages sort.
 __global__ void __launch_bounds__(1024) merge_kernel(const Cand* __restrict__ in, int n_lists,
-                                                     int k_pad, int group, Cand* __restrict__ out) {
+                                                     int k_pad, int group, int64_t op_stride,
+                                                     Cand* __restrict__ out) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Cand* s = reinterpret_cast<Cand*>(smem_raw);
     const int g = blockIdx.x;
+    in += blockIdx.y * op_stride;
+    out += blockIdx.y * op_stride;
     const int total = group * k_pad;
     for (int e = threadIdx.x; e < total; e += blockDim.x) {
         int l = g * group + e / k_pad;
@@ -147,11 +154,13 @@ __global__ void __launch_bounds__(1024) merge_kernel(const Cand* __restrict__ in
 
 cudaError_t launch_epilogue_topk(const EpilogueArgs& a, cudaStream_t stream) {
     if (a.n_tiles <= 0) return cudaSuccess;
-    if (a.sub_lists < 1 || kTilePairs % a.sub_lists != 0 || (a.cands && kTilePairs / a.sub_lists < a.k_pad))
-        return cudaErrorInvalidValue;
+    if (a.n_ops < 1 || a.n_ops > 4 || a.sub_lists < 1 || kTilePairs % a.sub_lists != 0) return cudaErrorInvalidValue;
+    for (int o = 0; o < a.n_ops; ++o)
+        if (a.cands[o] && kTilePairs / a.sub_lists < a.k_pad) return cudaErrorInvalidValue;
     size_t smem = sizeof(Cand) * (kTilePairs / a.sub_lists);
     cudaFuncSetAttribute(epilogue_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    epilogue_topk_kernel<<<dim3((unsigned)a.n_tiles, (unsigned)a.sub_lists), kEpiThreads, smem, stream>>>(a);
+    epilogue_topk_kernel<<<dim3((unsigned)a.n_tiles, (unsigned)a.sub_lists, (unsigned)a.n_ops), kEpiThreads, smem,
+                           stream>>>(a);
     return cudaGetLastError();
 }
 
@@ -165,9 +174,8 @@ int epilogue_sub_lists(int n_tiles, int k_pad, int sm_count) {
     return s;
 }
 
-cudaError_t merge_candidates(Cand* buf, Cand* tmp, int n_lists, int k_pad, int n_groups_unused,
+cudaError_t merge_candidates(Cand* buf, Cand* tmp, int n_lists, int k_pad, int n_ops, size_t op_stride,
                              Cand** final_list, cudaStream_t stream) {
-    (void)n_groups_unused;
     // lists per CTA: a power of two, group * k_pad <= 8192 entries (128 KB of shared memory),
     // no more than the lists there are
     int fit = std::max(2, 8192 / k_pad);
@@ -179,7 +187,8 @@ cudaError_t merge_candidates(Cand* buf, Cand* tmp, int n_lists, int k_pad, int n
     Cand* dst = tmp;
     while (n_lists > 1) {
         int out_lists = (n_lists + group - 1) / group;
-        merge_kernel<<<out_lists, 1024, smem, stream>>>(src, n_lists, k_pad, group, dst);
+        merge_kernel<<<dim3((unsigned)out_lists, (unsigned)n_ops), 1024, smem, stream>>>(src, n_lists, k_pad, group,
+                                                                                    (int64_t)op_stride, dst);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         std::swap(src, dst);

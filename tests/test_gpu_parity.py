@@ -262,3 +262,27 @@ def test_tensor_core_moments_match_cuda_core_kernel(native, tmp_path):
     with bucket_for(native, X, y) as b:
         for op in OPS:
             assert_pearson_close(b.scores(op, div_eps=1e-6), ref[op])
+
+
+def test_cta_pair_gram_kernel_matches_cuda_core_kernel(native, tmp_path):
+    """The opt-in CTA-pair (cta_group::2) Gram kernel (GAFIME_GRAM_PAIRS=1, a separate
+    process) scores like the CUDA-core kernel, including an odd tile count per B block (the
+    self-paired CTA) and a ragged last block."""
+    import os
+    import subprocess
+    import sys
+    rng = np.random.default_rng(23)
+    n, f = 50_000, 300
+    X = np.hstack([rng.standard_normal((n, 150)), rng.lognormal(0, 1, (n, 150))]).astype(np.float32)
+    y = (X[:, 11] * X[:, 200] + rng.standard_normal(n) > 1.0).astype(np.float32)
+    src = tmp_path / "in.npz"
+    np.savez(src, X=X, y=y)
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    outs = {}
+    for name, extra in (("pairs", {"GAFIME_GRAM_PAIRS": "1"}), ("cuda_core", {"GAFIME_PAIR_MOMENTS": "cuda-core"})):
+        dst = tmp_path / f"{name}.npz"
+        subprocess.run([sys.executable, "-c", _CUDA_CORE_SCRIPT, repo, str(src), str(dst)],
+                       env=dict(os.environ, **extra), check=True, timeout=600)
+        outs[name] = np.load(dst)
+    for op in OPS:
+        assert_pearson_close(outs["pairs"][op], outs["cuda_core"][op])
