@@ -41,7 +41,7 @@ EXPORTED = (
     "gafime_contiguous_bucket_info", "gafime_allpairs_topk", "gafime_allpairs_scores",
     "gafime_topk_merge", "gafime_profile_enable", "gafime_profile_read",
     "gafime_contiguous_bucket_stream", "gafime_allpairs_scores_noalloc", "gafime_unary_scores",
-    "gafime_shard_tiles",
+    "gafime_shard_tiles", "gafime_feature_interaction_cuda",
 )
 
 # kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
@@ -86,6 +86,8 @@ def _bind(lib: ctypes.CDLL) -> None:
         "gafime_allpairs_scores_noalloc": ([_vp, _i64, _vp, _i, _i, _i, _f, _vp, _vp], _i),
         "gafime_unary_scores": ([_vp, _i, _i, _vp], _i),
         "gafime_shard_tiles": ([_i, _i, _i, _vp, _i, _ip], _i),
+        "gafime_feature_interaction_cuda": ([_vp, _vp, _vp, _vp, _vp, ctypes.c_int32, ctypes.c_int32,
+                                             ctypes.c_int32], _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)
@@ -276,6 +278,23 @@ def profile_read(kernel: str = "all") -> Tuple[float, int]:
 
 
 TILE = 64
+
+
+def feature_interaction(X: np.ndarray, means: np.ndarray, combos) -> np.ndarray:
+    """Interaction columns through gafime_feature_interaction_cuda: X row-major (n, F),
+    combos a sequence of feature-id sequences -> (n, len(combos)) fp32."""
+    lib = load()
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    means = np.ascontiguousarray(means, dtype=np.float32)
+    idx = np.array([f for c in combos for f in c], dtype=np.int32)
+    off = np.zeros(len(combos) + 1, dtype=np.int32)
+    off[1:] = np.cumsum([len(c) for c in combos])
+    if idx.size == 0:
+        idx = np.zeros(1, dtype=np.int32)
+    out = np.empty((X.shape[0], len(combos)), dtype=np.float32)
+    check("gafime_feature_interaction_cuda", lib.gafime_feature_interaction_cuda(
+        _ptr(X), _ptr(means), _ptr(out), _ptr(idx), _ptr(off), X.shape[0], X.shape[1], len(combos)))
+    return out
 
 
 def shard_tiles(n_features: int, shard_id: int, n_shards: int) -> np.ndarray:

@@ -119,6 +119,17 @@ int gafime_contiguous_bucket_free(ContiguousBucket bucket);
 int gafime_contiguous_bucket_info(ContiguousBucket bucket, int* n_samples_out,
                                   int* n_features_out);
 
+/* interfaces.h:392-401 (legacy interaction materialiser; the reference's CUDA
+ * kernel is src/cuda/kernels.cu:1646-1676).  X row-major [n_samples][n_features] fp32,
+ * output row-major [n_samples][n_combos]: for a one-feature combo the raw value, otherwise
+ * the fp32 product of (X - means) over the combo's features in order; feature ids outside
+ * [0, n_features) are skipped (an empty combo gives 1).  combo c spans
+ * combo_indices[combo_offsets[c] .. combo_offsets[c+1]).  Synchronous; host buffers.
+ * GAFIME_ERROR_INVALID_ARGS for NULL pointers, non-positive sizes or decreasing offsets. */
+int gafime_feature_interaction_cuda(const float* X, const float* means, float* output,
+                                    const int32_t* combo_indices, const int32_t* combo_offsets,
+                                    int32_t n_samples, int32_t n_features, int32_t n_combos);
+
 /* ------------------------------------------------------- NEW: all pairs ---- */
 
 /*

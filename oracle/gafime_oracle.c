@@ -30,7 +30,15 @@
  *     (gafime_core.cpp:486-497), mutual information with equal-width min/max
  *     bins on both axes (gafime_core.cpp:200-226, 267-333).
  *
- * Data layout: X is column-major fp32, column f at X + f * ld, n rows.
+ *  4. The interaction materialiser (legacy ABI gafime_feature_interaction_cuda,
+ *     src/cuda/kernels.cu:1646-1676): out[i, c] = X[i, f] for a one-feature combo,
+ *     otherwise the fp32 product over the combo's features of (X[i, f] - means[f]) in
+ *     combo order; feature ids outside [0, F) are skipped, so an empty combo (or one whose
+ *     features are all invalid) yields 1.  cpu_backend.cpp:316-370 agrees on every combo
+ *     whose features are valid (it writes 0 for the degenerate ones).
+ *
+ * Data layout: X is column-major fp32, column f at X + f * ld, n rows (the materialiser
+ * takes the reference's row-major X, row i at X + i * F).
  */
 #include <math.h>
 #include <stdint.h>
@@ -258,4 +266,24 @@ int gafime_oracle_centred_scores(const float* X, int64_t ld, const float* y, int
     }
     free(means); free(yc); free(yd); free(y_bins);
     return status;
+}
+
+/* Interaction materialiser, src/cuda/kernels.cu:1646-1676 (row-major X and out). */
+void gafime_oracle_feature_interaction(const float* X, const float* means, float* out,
+                                       const int32_t* idx, const int32_t* off, int32_t n,
+                                       int32_t f, int32_t n_combos) {
+    for (int32_t i = 0; i < n; ++i) {
+        for (int32_t c = 0; c < n_combos; ++c) {
+            const int32_t start = off[c], end = off[c + 1], size = end - start;
+            float prod = 1.0f;
+            for (int32_t j = start; j < end; ++j) {
+                const int32_t feat = idx[j];
+                if (feat < 0 || feat >= f) continue;
+                const float v = X[(int64_t)i * f + feat];
+                if (size == 1) prod = v;
+                else prod *= (v - means[feat]);
+            }
+            out[(int64_t)i * n_combos + c] = prod;
+        }
+    }
 }

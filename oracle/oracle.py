@@ -59,6 +59,9 @@ def lib() -> ctypes.CDLL:
         _LIB.gafime_oracle_pair_moments.argtypes = [
             _f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, _f64p]
         _LIB.gafime_oracle_pair_moments.restype = None
+        _LIB.gafime_oracle_feature_interaction.argtypes = [
+            _f32p, _f32p, _f32p, _i32p, _i32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
+        _LIB.gafime_oracle_feature_interaction.restype = None
     return _LIB
 
 
@@ -119,3 +122,18 @@ def topk(scores: np.ndarray, pi: np.ndarray, pj: np.ndarray, k: int, absolute: b
     hi = np.maximum(pi, pj)
     order = np.lexsort((hi, lo, -s))
     return order[:k]
+
+
+def feature_interaction(X: np.ndarray, means: np.ndarray, combos) -> np.ndarray:
+    """Interaction columns of the legacy materialiser (src/cuda/kernels.cu:1646-1676):
+    X row-major (n, F) fp32, combos a list of feature-id sequences -> (n, len(combos))."""
+    X = np.ascontiguousarray(X, dtype=np.float32)
+    means = np.ascontiguousarray(means, dtype=np.float32)
+    idx = np.array([f for c in combos for f in c], dtype=np.int32)
+    off = np.zeros(len(combos) + 1, dtype=np.int32)
+    off[1:] = np.cumsum([len(c) for c in combos])
+    if idx.size == 0:
+        idx = np.zeros(1, dtype=np.int32)
+    out = np.empty((X.shape[0], len(combos)), dtype=np.float32)
+    lib().gafime_oracle_feature_interaction(X, means, out, idx, off, X.shape[0], X.shape[1], len(combos))
+    return out

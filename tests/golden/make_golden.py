@@ -14,7 +14,9 @@ Every expected value in the fixtures comes from the reference itself:
   ``backend='python'`` for the end-to-end top-k;
 * the reference's numpy metrics (gafime/metrics/cpu_metrics.py) for the numpy twin;
 * ``gafime_fused_interaction_perpair_cpu`` (src/cpu/cpu_backend.cpp:229-310) for the
-  raw-operator 12-float statistics of all four operators.
+  raw-operator 12-float statistics of all four operators;
+* ``gafime_feature_interaction_cpu`` (src/cpu/cpu_backend.cpp:316-370) for the interaction
+  materialiser on combos of 1-4 valid features.
 
 Inputs are stored beside the outputs, so the tests never depend on the random
 generator.  The fixtures are small (a few hundred KB in total).
@@ -210,6 +212,23 @@ def main():
         plans[f"unary_{seed}"] = np.array(u, dtype=np.int32).reshape(-1)
         plans[f"pairs_{seed}"] = np.array(h, dtype=np.int32)
     np.savez_compressed(os.path.join(HERE, "planning.npz"), **plans)
+    # --- interaction materialiser (legacy ABI), valid combos of 1-4 features ----------
+    rng = np.random.default_rng(5)
+    Xi = rng.standard_normal((300, 9)).astype(np.float32)
+    Xi[:, 4] = rng.lognormal(0.0, 1.0, 300).astype(np.float32)
+    mi = Xi.mean(axis=0).astype(np.float32)
+    combos = [[0], [3], [1, 2], [4, 8], [8, 4], [2, 5, 7], [0, 1, 2, 3], [6, 6]]
+    idx = np.array([f for c in combos for f in c], dtype=np.int32)
+    off = np.zeros(len(combos) + 1, dtype=np.int32)
+    off[1:] = np.cumsum([len(c) for c in combos])
+    outi = np.zeros((300, len(combos)), dtype=np.float32)
+    fi = cpu.gafime_feature_interaction_cpu
+    fi.restype = ctypes.c_int
+    rc = fi(ctypes.c_void_p(Xi.ctypes.data), ctypes.c_void_p(mi.ctypes.data), ctypes.c_void_p(outi.ctypes.data),
+            ctypes.c_void_p(idx.ctypes.data), ctypes.c_void_p(off.ctypes.data), ctypes.c_int32(300),
+            ctypes.c_int32(9), ctypes.c_int32(len(combos)))
+    assert rc == 0, rc
+    np.savez_compressed(os.path.join(HERE, "interaction.npz"), X=Xi, means=mi, idx=idx, off=off, out=outi)
     print("wrote fixtures to", HERE)
 
 

@@ -286,3 +286,33 @@ def test_cta_pair_gram_kernel_matches_cuda_core_kernel(native, tmp_path):
         outs[name] = np.load(dst)
     for op in OPS:
         assert_pearson_close(outs["pairs"][op], outs["cuda_core"][op])
+
+
+def test_interaction_materialiser_matches_oracle(native, golden, oracle):
+    """gafime_feature_interaction_cuda equals the oracle (and through it the reference CPU
+    materialiser) bit for bit, including invalid feature ids and empty combos."""
+    g = golden("interaction.npz")
+    off = g["off"]
+    combos = [g["idx"][off[c]:off[c + 1]].tolist() for c in range(len(off) - 1)]
+    np.testing.assert_array_equal(native.feature_interaction(g["X"], g["means"], combos), g["out"])
+    rng = np.random.default_rng(8)
+    X = rng.standard_normal((5000, 40)).astype(np.float32)
+    m = X.mean(axis=0).astype(np.float32)
+    combos = [[int(a)] for a in range(40)] + [[int(a), int(b)] for a, b in rng.integers(0, 40, (300, 2))]
+    combos += [[1, 2, 3], [4, 50, 6], [], [-1], [7, 7, 7, 7]]
+    np.testing.assert_array_equal(native.feature_interaction(X, m, combos), oracle.feature_interaction(X, m, combos))
+
+
+def test_interaction_materialiser_rejects_bad_arguments(native):
+    import ctypes
+    lib = native.load()
+    X = np.zeros((4, 3), np.float32)
+    m = np.zeros(3, np.float32)
+    out = np.zeros((4, 2), np.float32)
+    idx = np.array([0, 1], np.int32)
+    bad_off = np.array([0, 2, 1], np.int32)   # decreasing
+    rc = lib.gafime_feature_interaction_cuda(X.ctypes.data, m.ctypes.data, out.ctypes.data, idx.ctypes.data,
+                                             bad_off.ctypes.data, 4, 3, 2)
+    assert rc == -1
+    assert lib.gafime_feature_interaction_cuda(None, m.ctypes.data, out.ctypes.data, idx.ctypes.data,
+                                               bad_off.ctypes.data, 4, 3, 2) == -1

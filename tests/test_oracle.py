@@ -76,3 +76,23 @@ def test_topk_tie_order_is_pair_ascending(oracle):
     pi = np.array([3, 0, 1, 0], dtype=np.int32)
     pj = np.array([4, 2, 2, 1], dtype=np.int32)
     assert oracle.topk(s, pi, pj, 3).tolist() == [3, 1, 0]
+
+
+def test_interaction_materialiser_matches_reference_cpu(golden, oracle):
+    """The oracle's restatement of the materialiser equals gafime_feature_interaction_cpu
+    (cpu_backend.cpp:316-370) bit for bit on combos of valid features."""
+    g = golden("interaction.npz")
+    off = g["off"]
+    combos = [g["idx"][off[c]:off[c + 1]].tolist() for c in range(len(off) - 1)]
+    np.testing.assert_array_equal(oracle.feature_interaction(g["X"], g["means"], combos), g["out"])
+
+
+def test_interaction_materialiser_degenerate_combos(oracle):
+    """Invalid feature ids are skipped and an empty combo gives 1 (kernels.cu:1646-1676)."""
+    X = np.arange(12, dtype=np.float32).reshape(4, 3)
+    m = X.mean(axis=0).astype(np.float32)
+    out = oracle.feature_interaction(X, m, [[0], [1, 2], [], [5], [0, 7, 2]])
+    np.testing.assert_array_equal(out[:, 0], X[:, 0])
+    np.testing.assert_array_equal(out[:, 1], (X[:, 1] - m[1]) * (X[:, 2] - m[2]))
+    assert np.all(out[:, 2] == 1.0) and np.all(out[:, 3] == 1.0)
+    np.testing.assert_array_equal(out[:, 4], out[:, 1] * 0 + (X[:, 0] - m[0]) * (X[:, 2] - m[2]))
