@@ -73,3 +73,22 @@ def test_host_topk_merge_orders_by_abs_score_then_pair(lib):
     assert s.tolist() == [0.9, -0.5, 0.5]
     i, j, s = _native.merge_topk(ci, cj, cs, 10)
     assert len(i) == 4  # the empty slot (-1, -1) is dropped
+
+
+def test_reference_backend_ctypes_setup_binds_this_library(lib):
+    """The reference's own NativeCudaBackend._setup_functions (native_cuda_backend.py:97-157)
+    binds every symbol it needs from this library unchanged (run where the reference
+    sources are present; the setup only sets ctypes signatures)."""
+    import importlib
+    import sys
+    ref = "/root/reference"
+    if not os.path.isdir(os.path.join(ref, "gafime")):
+        pytest.skip("reference sources not present")
+    sys.path.insert(0, ref)
+    try:
+        mod = importlib.import_module("gafime.backends.native_cuda_backend")
+    finally:
+        sys.path.remove(ref)
+    backend = object.__new__(mod.NativeCudaBackend)
+    backend.lib = lib
+    backend._setup_functions()   # raises AttributeError if a bound symbol is missing
