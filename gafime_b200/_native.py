@@ -42,6 +42,9 @@ EXPORTED = (
     "gafime_topk_merge", "gafime_profile_enable", "gafime_profile_read",
     "gafime_contiguous_bucket_stream", "gafime_allpairs_scores_noalloc", "gafime_unary_scores",
     "gafime_shard_tiles", "gafime_feature_interaction_cuda",
+    "gafime_bucket_alloc", "gafime_bucket_upload_feature", "gafime_bucket_upload_target",
+    "gafime_bucket_upload_mask", "gafime_bucket_compute", "gafime_bucket_free",
+    "gafime_bucket_compute_batch", "gafime_interleaved_compute", "gafime_fused_interaction",
 )
 
 # kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
@@ -88,6 +91,15 @@ def _bind(lib: ctypes.CDLL) -> None:
         "gafime_shard_tiles": ([_i, _i, _i, _vp, _i, _ip], _i),
         "gafime_feature_interaction_cuda": ([_vp, _vp, _vp, _vp, _vp, ctypes.c_int32, ctypes.c_int32,
                                              ctypes.c_int32], _i),
+        "gafime_bucket_alloc": ([_i, _i, ctypes.POINTER(_vp)], _i),
+        "gafime_bucket_upload_feature": ([_vp, _i, _vp], _i),
+        "gafime_bucket_upload_target": ([_vp, _vp], _i),
+        "gafime_bucket_upload_mask": ([_vp, _vp], _i),
+        "gafime_bucket_compute": ([_vp, _vp, _vp, _i, _vp, _i, _vp], _i),
+        "gafime_bucket_free": ([_vp], _i),
+        "gafime_bucket_compute_batch": ([_vp, _vp, _vp, _vp, _i, _i, _vp], _i),
+        "gafime_interleaved_compute": ([_vp, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
+        "gafime_fused_interaction": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp], _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

@@ -14,6 +14,7 @@
 
 #include <algorithm>
 #include <new>
+#include <vector>
 
 #include "engine.h"
 
@@ -538,3 +539,301 @@ int gafime_contiguous_bucket_info(ContiguousBucket bucket, int* n_samples_out, i
 }
 
 }  // extern "C"
+
+// ============================================================ GafimeBucket ABI ==
+//
+// The reference's small-bucket API (interfaces.h:176-382; GafimeBucketImpl and kernels in
+// src/cuda/kernels.cu:589-1400), used by StaticBucket / FusedKernelWrapper
+// (gafime/backends/fused_kernel.py:318-848): at most 5 feature columns, arity-2..5 chains
+// x = combine(...combine(combine(op0(f0), op1(f1), t0), op2(f2), t1)..., t_{a-2}) in fp32
+// (the per-pair-type form of cpu_backend.cpp:229-310), 12 stats split by fold.  Here the
+// bucket is the contiguous bucket with F <= 5 (same column-major layout, y in column F);
+// sums are fp64 in a fixed order and cast to float at the end, like the CPU reference.
+
+namespace gafime {
+namespace {
+
+constexpr int kMaxChain = 5;       // GAFIME_MAX_FEATURES of the reference
+constexpr int kMaxBatch = 1024;    // GAFIME_MAX_BATCH_SIZE of the reference
+
+struct ChainDesc {
+    int arity;
+    int feat[kMaxChain];
+    int op[kMaxChain];
+    int inter[kMaxChain - 1];
+};
+
+__device__ __forceinline__ float chain_value(const float* __restrict__ data, int64_t ld, int64_t r,
+                                             const ChainDesc& d) {
+    float x = combine_op(apply_op(data[(int64_t)d.feat[0] * ld + r], d.op[0]),
+                         apply_op(data[(int64_t)d.feat[1] * ld + r], d.op[1]), d.inter[0]);
+    #pragma unroll
+    for (int k = 2; k < kMaxChain; ++k)
+        if (k < d.arity) x = combine_op(x, apply_op(data[(int64_t)d.feat[k] * ld + r], d.op[k]), d.inter[k - 1]);
+    return x;
+}
+
+// Fixed-order reduction of NV doubles per thread over the block (256 threads): warp
+// shuffles, then warps in order.  Result valid in thread 0.
+template <int NV>
+__device__ __forceinline__ void block_reduce_warps(double (&v)[NV], double* smem /*[8*NV]*/) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    #pragma unroll
+    for (int m = 0; m < NV; ++m)
+        for (int o = 16; o > 0; o >>= 1) v[m] += __shfl_down_sync(0xffffffffu, v[m], o);
+    if (lane == 0)
+        #pragma unroll
+        for (int m = 0; m < NV; ++m) smem[warp * NV + m] = v[m];
+    __syncthreads();
+    if (threadIdx.x == 0)
+        #pragma unroll
+        for (int m = 0; m < NV; ++m) {
+            double s = smem[m];
+            for (int w = 1; w < 8; ++w) s += smem[w * NV + m];
+            v[m] = s;
+        }
+}
+
+// Grid (blocks, items): kSlots chains per item evaluated on the same rows.  A row is
+// skipped when y or any slot's x is NaN (with two slots this is the interleaved kernel's
+// rule, kernels.cu:1217-1218).
+template <int kSlots>
+__global__ void __launch_bounds__(256) chain_stats_kernel(const float* __restrict__ data,
+                                                          const uint8_t* __restrict__ mask, int64_t n,
+                                                          int64_t ld, int64_t ycol,
+                                                          const ChainDesc* __restrict__ descs, int val_fold_id,
+                                                          double* __restrict__ partial) {
+    __shared__ double red[8 * 12 * kSlots];
+    ChainDesc d[kSlots];
+    #pragma unroll
+    for (int s = 0; s < kSlots; ++s) d[s] = descs[blockIdx.y * kSlots + s];
+    double acc[12 * kSlots];
+    #pragma unroll
+    for (int m = 0; m < 12 * kSlots; ++m) acc[m] = 0.0;
+    const float* y = data + ycol * ld;
+    for (int64_t r = (int64_t)blockIdx.x * 256 + threadIdx.x; r < n; r += (int64_t)gridDim.x * 256) {
+        float x[kSlots];
+        bool skip = false;
+        #pragma unroll
+        for (int s = 0; s < kSlots; ++s) {
+            x[s] = chain_value(data, ld, r, d[s]);
+            skip |= isnan(x[s]);
+        }
+        const float yv = y[r];
+        if (skip || isnan(yv)) continue;
+        const int o = (mask[r] == val_fold_id) ? 6 : 0;
+        const double yd = yv;
+        #pragma unroll
+        for (int s = 0; s < kSlots; ++s) {
+            const double xd = x[s];
+            #pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (o == 6 * h) {
+                    double* a = acc + 12 * s + 6 * h;
+                    a[0] += 1.0;
+                    a[1] += xd;
+                    a[2] += yd;
+                    a[3] += xd * xd;
+                    a[4] += yd * yd;
+                    a[5] += xd * yd;
+                }
+            }
+        }
+    }
+    block_reduce_warps<12 * kSlots>(acc, red);
+    if (threadIdx.x == 0) {
+        double* out = partial + ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * 12 * kSlots;
+        #pragma unroll
+        for (int m = 0; m < 12 * kSlots; ++m) out[m] = acc[m];
+    }
+}
+
+// out[item][m] = sum over the blocks of partial[item][block][m], in block order
+__global__ void sum_item_partials_kernel(const double* __restrict__ partial, int blocks, int width,
+                                         double* __restrict__ out) {
+    const int item = blockIdx.x, m = threadIdx.x;
+    if (m >= width) return;
+    double s = 0.0;
+    for (int b = 0; b < blocks; ++b) s += partial[((int64_t)item * blocks + b) * width + m];
+    out[(int64_t)item * width + m] = s;
+}
+
+bool valid_unary(int op) { return op >= GAFIME_OP_IDENTITY && op <= GAFIME_OP_ROLLING_STD; }
+bool valid_combiner(int t) { return t >= GAFIME_INTERACT_MULT && t <= GAFIME_INTERACT_MIN; }
+
+// Run `items` chain groups of kSlots chains and write items x (12 * kSlots) float stats.
+template <int kSlots>
+int run_chains(Bucket& b, const ChainDesc* h_descs, int items, int val_fold_id, float* h_stats) {
+    const int width = 12 * kSlots;
+    int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((b.n + 255) / 256, (4 * (int64_t)b.sm_count + items - 1) / items));
+    blocks = std::min(blocks, 1024);
+    const size_t desc_bytes = (size_t)items * kSlots * sizeof(ChainDesc);
+    const size_t part_bytes = (size_t)items * blocks * width * sizeof(double);
+    const size_t off_part = (desc_bytes + 255) / 256 * 256;
+    const size_t off_out = (off_part + part_bytes + 255) / 256 * 256;
+    const size_t out_bytes = (size_t)items * width * sizeof(double);
+    cudaError_t e = ensure(b.stats_part, off_out + out_bytes);
+    if (e != cudaSuccess) return status_from(e);
+    char* base = (char*)b.stats_part.ptr;
+    ChainDesc* d_descs = (ChainDesc*)base;
+    double* d_part = (double*)(base + off_part);
+    double* d_out = (double*)(base + off_out);
+    std::vector<double> host((size_t)items * width);
+    e = cudaMemcpyAsync(d_descs, h_descs, desc_bytes, cudaMemcpyHostToDevice, b.stream);
+    if (e == cudaSuccess) {
+        KernelTimer timer(b.stream, GAFIME_KERNEL_LEGACY_PAIR);
+        chain_stats_kernel<kSlots><<<dim3((unsigned)blocks, (unsigned)items), 256, 0, b.stream>>>(
+            b.d_data, b.d_mask, b.n, b.ld, b.f, d_descs, val_fold_id, d_part);
+        sum_item_partials_kernel<<<items, 32, 0, b.stream>>>(d_part, blocks, width, d_out);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(host.data(), d_out, out_bytes, cudaMemcpyDeviceToHost, b.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b.stream);
+    if (e != cudaSuccess) return status_from(e);
+    for (size_t m = 0; m < host.size(); ++m) h_stats[m] = (float)host[m];
+    return GAFIME_SUCCESS;
+}
+
+int upload_column(Bucket* b, int64_t col, const void* h, size_t bytes) {
+    cudaSetDevice(b->device);
+    cudaError_t e = cudaMemcpyAsync(b->d_data + col * b->ld, h, bytes, cudaMemcpyHostToDevice, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    b->finite_state = -1;
+    return e == cudaSuccess ? GAFIME_SUCCESS : GAFIME_ERROR_KERNEL_FAILED;
+}
+
+}  // namespace
+}  // namespace gafime
+
+extern "C" int gafime_bucket_alloc(int n_samples, int n_features, GafimeBucket* bucket_out) {
+    if (n_samples <= 0 || n_features <= 0 || n_features > kMaxChain || !bucket_out) return GAFIME_ERROR_INVALID_ARGS;
+    return gafime_contiguous_bucket_alloc(n_samples, n_features, (ContiguousBucket*)bucket_out);
+}
+
+extern "C" int gafime_bucket_upload_feature(GafimeBucket bucket, int feature_idx, const float* h_data) {
+    if (!bucket || !h_data) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket* b = (Bucket*)bucket;
+    if (feature_idx < 0 || feature_idx >= b->f) return GAFIME_ERROR_INVALID_ARGS;
+    return upload_column(b, feature_idx, h_data, (size_t)b->n * sizeof(float));
+}
+
+extern "C" int gafime_bucket_upload_target(GafimeBucket bucket, const float* h_target) {
+    if (!bucket || !h_target) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket* b = (Bucket*)bucket;
+    return upload_column(b, b->f, h_target, (size_t)b->n * sizeof(float));
+}
+
+extern "C" int gafime_bucket_upload_mask(GafimeBucket bucket, const uint8_t* h_mask) {
+    if (!bucket || !h_mask) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket* b = (Bucket*)bucket;
+    cudaSetDevice(b->device);
+    cudaError_t e = cudaMemcpyAsync(b->d_mask, h_mask, (size_t)b->n, cudaMemcpyHostToDevice, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    return e == cudaSuccess ? GAFIME_SUCCESS : GAFIME_ERROR_KERNEL_FAILED;
+}
+
+extern "C" int gafime_bucket_compute(GafimeBucket bucket, const int* feature_indices, const int* ops, int arity,
+                                     const int* interaction_types, int val_fold_id, float* h_stats) {
+    if (!bucket || !feature_indices || !ops || !interaction_types || !h_stats) return GAFIME_ERROR_INVALID_ARGS;
+    if (arity < 2 || arity > kMaxChain) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket* b = (Bucket*)bucket;
+    ChainDesc d{};
+    d.arity = arity;
+    for (int k = 0; k < arity; ++k) {
+        if (feature_indices[k] < 0 || feature_indices[k] >= b->f || !valid_unary(ops[k])) return GAFIME_ERROR_INVALID_ARGS;
+        d.feat[k] = feature_indices[k];
+        d.op[k] = ops[k];
+        if (k > 0) {
+            if (!valid_combiner(interaction_types[k - 1])) return GAFIME_ERROR_INVALID_ARGS;
+            d.inter[k - 1] = interaction_types[k - 1];
+        }
+    }
+    cudaSetDevice(b->device);
+    return run_chains<1>(*b, &d, 1, val_fold_id, h_stats);
+}
+
+extern "C" int gafime_bucket_compute_batch(GafimeBucket bucket, const int* batch_indices, const int* batch_ops,
+                                           const int* batch_interact, int batch_size, int val_fold_id,
+                                           float* h_stats_batch) {
+    if (!bucket || !batch_indices || !batch_ops || !batch_interact || !h_stats_batch) return GAFIME_ERROR_INVALID_ARGS;
+    if (batch_size <= 0 || batch_size > kMaxBatch) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket* b = (Bucket*)bucket;
+    std::vector<ChainDesc> d((size_t)batch_size);
+    for (int q = 0; q < batch_size; ++q) {
+        ChainDesc& c = d[q];
+        c = ChainDesc{};
+        c.arity = 2;
+        for (int k = 0; k < 2; ++k) {
+            const int fi = batch_indices[2 * q + k], op = batch_ops[2 * q + k];
+            if (fi < 0 || fi >= b->f || !valid_unary(op)) return GAFIME_ERROR_INVALID_ARGS;
+            c.feat[k] = fi;
+            c.op[k] = op;
+        }
+        if (!valid_combiner(batch_interact[q])) return GAFIME_ERROR_INVALID_ARGS;
+        c.inter[0] = batch_interact[q];
+    }
+    cudaSetDevice(b->device);
+    return run_chains<1>(*b, d.data(), batch_size, val_fold_id, h_stats_batch);
+}
+
+extern "C" int gafime_interleaved_compute(GafimeBucket bucket, const int* feature_indices_A, const int* ops_A,
+                                          int arity_A, int interact_A, const int* feature_indices_B,
+                                          const int* ops_B, int arity_B, int interact_B, int window_size,
+                                          int val_fold_id, float* h_stats_A, float* h_stats_B) {
+    (void)window_size;   // rolling operators evaluate to NaN on the device, as in the reference
+    if (!bucket || !feature_indices_A || !ops_A || !feature_indices_B || !ops_B || !h_stats_A || !h_stats_B)
+        return GAFIME_ERROR_INVALID_ARGS;
+    if (arity_A != 2 || arity_B != 2) return GAFIME_ERROR_INVALID_ARGS;   // kernels.cu:1348-1351
+    Bucket* b = (Bucket*)bucket;
+    ChainDesc d[2] = {};
+    const int* fi[2] = {feature_indices_A, feature_indices_B};
+    const int* op[2] = {ops_A, ops_B};
+    const int it[2] = {interact_A, interact_B};
+    for (int s = 0; s < 2; ++s) {
+        d[s].arity = 2;
+        for (int k = 0; k < 2; ++k) {
+            if (fi[s][k] < 0 || fi[s][k] >= b->f || !valid_unary(op[s][k])) return GAFIME_ERROR_INVALID_ARGS;
+            d[s].feat[k] = fi[s][k];
+            d[s].op[k] = op[s][k];
+        }
+        if (!valid_combiner(it[s])) return GAFIME_ERROR_INVALID_ARGS;
+        d[s].inter[0] = it[s];
+    }
+    cudaSetDevice(b->device);
+    float both[24];
+    const int st = run_chains<2>(*b, d, 1, val_fold_id, both);
+    if (st != GAFIME_SUCCESS) return st;
+    for (int m = 0; m < 12; ++m) {
+        h_stats_A[m] = both[m];
+        h_stats_B[m] = both[12 + m];
+    }
+    return GAFIME_SUCCESS;
+}
+
+extern "C" int gafime_bucket_free(GafimeBucket bucket) { return gafime_contiguous_bucket_free((ContiguousBucket)bucket); }
+
+// Legacy one-shot form (interfaces.h:372-382): a temporary bucket per call, one interaction
+// type for every step of the chain (gafime_fused_interaction_cpu, cpu_backend.cpp:127-213).
+extern "C" int gafime_fused_interaction(const float** h_inputs, const float* h_target, const uint8_t* h_mask,
+                                        const int* h_ops, int arity, int interaction_type, int val_fold_id,
+                                        int n_samples, float* h_stats) {
+    if (!h_inputs || !h_target || !h_mask || !h_ops || !h_stats) return GAFIME_ERROR_INVALID_ARGS;
+    if (arity < 2 || arity > kMaxChain || n_samples <= 0) return GAFIME_ERROR_INVALID_ARGS;
+    for (int k = 0; k < arity; ++k)
+        if (!h_inputs[k] || !valid_unary(h_ops[k])) return GAFIME_ERROR_INVALID_ARGS;
+    if (!valid_combiner(interaction_type)) return GAFIME_ERROR_INVALID_ARGS;
+    GafimeBucket b = nullptr;
+    int st = gafime_bucket_alloc(n_samples, arity, &b);
+    if (st != GAFIME_SUCCESS) return st;
+    for (int k = 0; k < arity && st == GAFIME_SUCCESS; ++k) st = gafime_bucket_upload_feature(b, k, h_inputs[k]);
+    if (st == GAFIME_SUCCESS) st = gafime_bucket_upload_target(b, h_target);
+    if (st == GAFIME_SUCCESS) st = gafime_bucket_upload_mask(b, h_mask);
+    if (st == GAFIME_SUCCESS) {
+        int fi[kMaxChain], types[kMaxChain - 1];
+        for (int k = 0; k < arity; ++k) fi[k] = k;
+        for (int k = 0; k + 1 < arity; ++k) types[k] = interaction_type;
+        st = gafime_bucket_compute(b, fi, h_ops, arity, types, val_fold_id, h_stats);
+    }
+    gafime_bucket_free(b);
+    return st;
+}

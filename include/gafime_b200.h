@@ -130,6 +130,46 @@ int gafime_feature_interaction_cuda(const float* X, const float* means, float* o
                                     const int32_t* combo_indices, const int32_t* combo_offsets,
                                     int32_t n_samples, int32_t n_features, int32_t n_combos);
 
+/* ------------------------------------------- small bucket (GafimeBucket) ---- */
+/* interfaces.h:176-382.  At most GAFIME_MAX_FEATURES columns; arity-2..5 chains
+ * x = t_{a-2}(...t_1(t_0(op_0(f_0), op_1(f_1)), op_2(f_2))..., op_{a-1}(f_{a-1})) in fp32
+ * (the per-pair-type form of cpu_backend.cpp:229-310), 12 stats split by the fold mask,
+ * NaN rows skipped, fp64 sums cast to float.  Used by the reference's StaticBucket and
+ * FusedKernelWrapper (gafime/backends/fused_kernel.py:318-848). */
+typedef void* GafimeBucket;  /* interfaces.h:185 */
+#define GAFIME_MAX_FEATURES 5
+#define GAFIME_MAX_BATCH_SIZE 1024
+
+/* interfaces.h:203-207 */
+int gafime_bucket_alloc(int n_samples, int n_features, GafimeBucket* bucket_out);
+/* interfaces.h:220-224; feature_idx in [0, n_features) */
+int gafime_bucket_upload_feature(GafimeBucket bucket, int feature_idx, const float* h_data);
+/* interfaces.h:233-236 */
+int gafime_bucket_upload_target(GafimeBucket bucket, const float* h_target);
+/* interfaces.h:245-248 */
+int gafime_bucket_upload_mask(GafimeBucket bucket, const uint8_t* h_mask);
+/* interfaces.h:266-274: feature_indices[arity], ops[arity], interaction_types[arity-1] */
+int gafime_bucket_compute(GafimeBucket bucket, const int* feature_indices, const int* ops, int arity,
+                          const int* interaction_types, int val_fold_id, float* h_stats);
+/* interfaces.h:284 */
+int gafime_bucket_free(GafimeBucket bucket);
+/* interfaces.h:310-318: batch_size pairs, h_stats_batch[batch_size * 12] */
+int gafime_bucket_compute_batch(GafimeBucket bucket, const int* batch_indices, const int* batch_ops,
+                                const int* batch_interact, int batch_size, int val_fold_id,
+                                float* h_stats_batch);
+/* interfaces.h:347-361: two arity-2 interactions over the same rows; a row whose y or
+ * either slot's x is NaN counts for neither slot (kernels.cu:1217-1218); rolling
+ * operators evaluate to NaN (kernels.cu:298-306), window_size is accepted and unused. */
+int gafime_interleaved_compute(GafimeBucket bucket, const int* feature_indices_A, const int* ops_A,
+                               int arity_A, int interact_A, const int* feature_indices_B, const int* ops_B,
+                               int arity_B, int interact_B, int window_size, int val_fold_id,
+                               float* h_stats_A, float* h_stats_B);
+/* interfaces.h:372-382: one-shot form with one interaction type for every chain step
+ * (gafime_fused_interaction_cpu, cpu_backend.cpp:127-213). */
+int gafime_fused_interaction(const float** h_inputs, const float* h_target, const uint8_t* h_mask,
+                             const int* h_ops, int arity, int interaction_type, int val_fold_id,
+                             int n_samples, float* h_stats);
+
 /* ------------------------------------------------------- NEW: all pairs ---- */
 
 /*

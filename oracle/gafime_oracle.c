@@ -30,7 +30,13 @@
  *     (gafime_core.cpp:486-497), mutual information with equal-width min/max
  *     bins on both axes (gafime_core.cpp:200-226, 267-333).
  *
- *  4. The interaction materialiser (legacy ABI gafime_feature_interaction_cuda,
+ *  4. Chains of the small-bucket ABI (gafime_bucket_compute / gafime_fused_interaction):
+ *     per-feature unary operators of cpu_backend.cpp:30-77, left-to-right combination
+ *     with per-step interaction types (combine_cpu, cpu_backend.cpp:85-103, literal
+ *     divide epsilon 1e-8f), NaN rows skipped, 12 fp64 sums split by the fold mask
+ *     (cpu_backend.cpp:229-295), returned in fp64.
+ *
+ *  5. The interaction materialiser (legacy ABI gafime_feature_interaction_cuda,
  *     src/cuda/kernels.cu:1646-1676): out[i, c] = X[i, f] for a one-feature combo,
  *     otherwise the fp32 product over the combo's features of (X[i, f] - means[f]) in
  *     combo order; feature ids outside [0, F) are skipped, so an empty combo (or one whose
@@ -285,5 +291,61 @@ void gafime_oracle_feature_interaction(const float* X, const float* means, float
             }
             out[(int64_t)i * n_combos + c] = prod;
         }
+    }
+}
+
+/* Unary operators, cpu_backend.cpp:30-77. */
+static inline float or_unary(float x, int op) {
+    switch (op) {
+        case 1: return logf(fabsf(x) + 1e-8f);
+        case 2: return expf(fminf(fmaxf(x, -20.0f), 20.0f));
+        case 3: return sqrtf(fabsf(x));
+        case 4: {
+            float c = fminf(fmaxf(x, -10.0f), 10.0f);
+            float e2 = expf(2.0f * c);
+            return (e2 - 1.0f) / (e2 + 1.0f);
+        }
+        case 5: {
+            float c = fminf(fmaxf(x, -20.0f), 20.0f);
+            return 1.0f / (1.0f + expf(-c));
+        }
+        case 6: return x * x;
+        case 7: return -x;
+        case 8: return fabsf(x);
+        case 9: return 1.0f / (fabsf(x) < 1e-8f ? copysignf(1e-8f, x) : x);
+        case 10: return x * x * x;
+        case 11:
+        case 12: return NAN;
+        default: return x;
+    }
+}
+
+/* combine_cpu with MAX / MIN, cpu_backend.cpp:85-103. */
+static inline float or_combine_chain(float a, float b, int t) {
+    switch (t) {
+        case 4: return fmaxf(a, b);
+        case 5: return fminf(a, b);
+        default: return or_combine(a, b, t, 1e-8f);
+    }
+}
+
+/* Chain statistics, cpu_backend.cpp:229-295: out = {train n, sx, sy, sxx, syy, sxy, the same
+ * for rows whose mask equals val_fold_id}. */
+void gafime_oracle_chain_stats(const float* const* cols, const float* y, const uint8_t* mask, int64_t n,
+                               const int* ops, int arity, const int* inter, int val_fold_id, double* out) {
+    for (int m = 0; m < 12; ++m) out[m] = 0.0;
+    for (int64_t r = 0; r < n; ++r) {
+        float x = or_combine_chain(or_unary(cols[0][r], ops[0]), or_unary(cols[1][r], ops[1]), inter[0]);
+        for (int k = 2; k < arity; ++k) x = or_combine_chain(x, or_unary(cols[k][r], ops[k]), inter[k - 1]);
+        const float yv = y[r];
+        if (isnan(x) || isnan(yv)) continue;
+        const double xd = x, yd = yv;
+        double* o = out + (mask[r] == val_fold_id ? 6 : 0);
+        o[0] += 1.0;
+        o[1] += xd;
+        o[2] += yd;
+        o[3] += xd * xd;
+        o[4] += yd * yd;
+        o[5] += xd * yd;
     }
 }

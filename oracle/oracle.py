@@ -32,6 +32,7 @@ OP_IDS = {"multiply": 0, "add": 1, "subtract": 2, "divide": 3}
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
 _i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 
 
 def build() -> str:
@@ -62,6 +63,9 @@ def lib() -> ctypes.CDLL:
         _LIB.gafime_oracle_feature_interaction.argtypes = [
             _f32p, _f32p, _f32p, _i32p, _i32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
         _LIB.gafime_oracle_feature_interaction.restype = None
+        _LIB.gafime_oracle_chain_stats.argtypes = [
+            ctypes.c_void_p, _f32p, _u8p, ctypes.c_int64, _i32p, ctypes.c_int, _i32p, ctypes.c_int, _f64p]
+        _LIB.gafime_oracle_chain_stats.restype = None
     return _LIB
 
 
@@ -136,4 +140,17 @@ def feature_interaction(X: np.ndarray, means: np.ndarray, combos) -> np.ndarray:
         idx = np.zeros(1, dtype=np.int32)
     out = np.empty((X.shape[0], len(combos)), dtype=np.float32)
     lib().gafime_oracle_feature_interaction(X, means, out, idx, off, X.shape[0], X.shape[1], len(combos))
+    return out
+
+
+def chain_stats(cols, y: np.ndarray, mask: np.ndarray, ops, inter, val_fold_id: int) -> np.ndarray:
+    """12 fp64 stats of the small-bucket chain (cpu_backend.cpp:229-295 with unary operators):
+    cols a list of 2-5 fp32 columns, ops one unary id per column, inter arity-1 combiner ids."""
+    cols = [np.ascontiguousarray(c, dtype=np.float32) for c in cols]
+    ptrs = (ctypes.c_void_p * len(cols))(*[c.ctypes.data for c in cols])
+    out = np.zeros(12)
+    lib().gafime_oracle_chain_stats(ptrs, np.ascontiguousarray(y, dtype=np.float32),
+                                    np.ascontiguousarray(mask, dtype=np.uint8), len(y),
+                                    np.asarray(ops, dtype=np.int32), len(cols),
+                                    np.asarray(list(inter) + [0], dtype=np.int32), int(val_fold_id), out)
     return out

@@ -16,7 +16,9 @@ Every expected value in the fixtures comes from the reference itself:
 * ``gafime_fused_interaction_perpair_cpu`` (src/cpu/cpu_backend.cpp:229-310) for the
   raw-operator 12-float statistics of all four operators;
 * ``gafime_feature_interaction_cpu`` (src/cpu/cpu_backend.cpp:316-370) for the interaction
-  materialiser on combos of 1-4 valid features.
+  materialiser on combos of 1-4 valid features;
+* ``gafime_fused_interaction_perpair_cpu`` with unary operators and arity 2-5 chains, and
+  ``gafime_fused_interaction_cpu`` (cpu_backend.cpp:127-213), for the small-bucket ABI.
 
 Inputs are stored beside the outputs, so the tests never depend on the random
 generator.  The fixtures are small (a few hundred KB in total).
@@ -229,6 +231,60 @@ def main():
             ctypes.c_int32(9), ctypes.c_int32(len(combos)))
     assert rc == 0, rc
     np.savez_compressed(os.path.join(HERE, "interaction.npz"), X=Xi, means=mi, idx=idx, off=off, out=outi)
+    # --- small-bucket chains: unary operators, per-step combiners, folds --------------
+    rng = np.random.default_rng(9)
+    nc = 2000
+    Xc = rng.standard_normal((nc, 5)).astype(np.float32)
+    Xc[:, 3] = rng.lognormal(0.0, 0.7, nc).astype(np.float32)
+    yc = (rng.random(nc) < 0.4).astype(np.float32)
+    maskc = rng.integers(0, 5, nc).astype(np.uint8)
+    chains = [([0, 1], [0, 0], [0]), ([0, 1], [1, 2], [1]), ([2, 3, 4], [3, 6, 7], [0, 2]),
+              ([0, 1, 2, 3], [4, 5, 8, 9], [3, 4, 5]), ([4, 3, 2, 1, 0], [10, 0, 1, 2, 3], [0, 1, 2, 3]),
+              ([1, 4], [11, 0], [0]), ([3, 3], [9, 6], [3])]
+    cols = [np.ascontiguousarray(Xc[:, c]) for c in range(5)]
+    fn = cpu.gafime_fused_interaction_perpair_cpu
+    chain_stats = np.zeros((len(chains), 12), dtype=np.float32)
+    for q, (feats, ops_, inter) in enumerate(chains):
+        ptrs = (ctypes.c_void_p * len(feats))(*[cols[c].ctypes.data for c in feats])
+        opsa = np.array(ops_, dtype=np.int32)
+        inta = np.array(inter, dtype=np.int32)
+        st = np.zeros(12, dtype=np.float32)
+        rc = fn(ptrs, yc.ctypes.data, maskc.ctypes.data, opsa.ctypes.data, len(feats), inta.ctypes.data, 2, nc,
+                st.ctypes.data)
+        assert rc == 0, rc
+        chain_stats[q] = st
+    ff = cpu.gafime_fused_interaction_cpu
+    ff.restype = ctypes.c_int
+    fused_cases = [([0, 1, 2], [0, 6, 1], 1), ([3, 4], [9, 0], 3), ([0, 1, 2, 3, 4], [0, 0, 0, 0, 0], 0)]
+    fused_stats = np.zeros((len(fused_cases), 12), dtype=np.float32)
+    for q, (feats, ops_, t) in enumerate(fused_cases):
+        ptrs = (ctypes.c_void_p * len(feats))(*[cols[c].ctypes.data for c in feats])
+        opsa = np.array(ops_, dtype=np.int32)
+        st = np.zeros(12, dtype=np.float32)
+        rc = ff(ptrs, ctypes.c_void_p(yc.ctypes.data), ctypes.c_void_p(maskc.ctypes.data),
+                ctypes.c_void_p(opsa.ctypes.data), ctypes.c_int(len(feats)), ctypes.c_int(t), ctypes.c_int(2),
+                ctypes.c_int(nc), ctypes.c_void_p(st.ctypes.data))
+        assert rc == 0, rc
+        fused_stats[q] = st
+
+    def pack(cases, width):
+        feats = np.full((len(cases), 5), -1, dtype=np.int32)
+        ops_ = np.zeros((len(cases), 5), dtype=np.int32)
+        inter = np.zeros((len(cases), 4), dtype=np.int32)
+        for q, c in enumerate(cases):
+            feats[q, :len(c[0])] = c[0]
+            ops_[q, :len(c[1])] = c[1]
+            if width:
+                inter[q, :len(c[2])] = c[2]
+            else:
+                inter[q, :] = c[2]
+        return feats, ops_, inter
+
+    cf, co, ci = pack(chains, 1)
+    ff_, fo, fi = pack(fused_cases, 0)
+    np.savez_compressed(os.path.join(HERE, "chains.npz"), X=Xc, y=yc, mask=maskc, val_fold=np.array(2),
+                        chain_feats=cf, chain_ops=co, chain_inter=ci, chain_stats=chain_stats,
+                        fused_feats=ff_, fused_ops=fo, fused_type=fi[:, 0], fused_stats=fused_stats)
     print("wrote fixtures to", HERE)
 
 

@@ -92,3 +92,22 @@ def test_reference_backend_ctypes_setup_binds_this_library(lib):
     backend = object.__new__(mod.NativeCudaBackend)
     backend.lib = lib
     backend._setup_functions()   # raises AttributeError if a bound symbol is missing
+
+
+def test_reference_fused_kernel_wrappers_bind_this_library(lib):
+    """The reference's StaticBucket and FusedKernelWrapper ctypes setups
+    (gafime/backends/fused_kernel.py:375-393, 532-602) bind every symbol they need."""
+    import importlib
+    import sys
+    ref = "/root/reference"
+    if not os.path.isdir(os.path.join(ref, "gafime")):
+        pytest.skip("reference sources not present")
+    sys.path.insert(0, ref)
+    try:
+        mod = importlib.import_module("gafime.backends.fused_kernel")
+    finally:
+        sys.path.remove(ref)
+    for cls in (mod.StaticBucket, mod.FusedKernelWrapper):
+        obj = object.__new__(cls)
+        obj.lib = lib
+        obj._setup_functions()

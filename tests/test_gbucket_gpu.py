@@ -1,0 +1,148 @@
+"""The small-bucket ABI (gafime_bucket_*, gafime_interleaved_compute, gafime_fused_interaction)
+against the reference CPU library's outputs (tests/golden/chains.npz) and the oracle.
+
+Tolerance: the 12 stats are fp64 sums cast to float, like the reference; transcendental
+unary operators may differ from the CPU's libm by an ulp per element, so the stats are
+compared at 1e-5 relative (1e-3 absolute for sums near zero)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-5, 1e-3
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from gafime_b200 import _native
+    return _native.load()
+
+
+def _p(a):
+    return ctypes.c_void_p(a.ctypes.data)
+
+
+class Small:
+    def __init__(self, lib, X, y, mask):
+        self.lib = lib
+        self.h = ctypes.c_void_p()
+        assert lib.gafime_bucket_alloc(X.shape[0], X.shape[1], ctypes.byref(self.h)) == 0
+        self.cols = [np.ascontiguousarray(X[:, c], dtype=np.float32) for c in range(X.shape[1])]
+        for c, col in enumerate(self.cols):
+            assert lib.gafime_bucket_upload_feature(self.h, c, _p(col)) == 0
+        self.y = np.ascontiguousarray(y, dtype=np.float32)
+        self.mask = np.ascontiguousarray(mask, dtype=np.uint8)
+        assert lib.gafime_bucket_upload_target(self.h, _p(self.y)) == 0
+        assert lib.gafime_bucket_upload_mask(self.h, _p(self.mask)) == 0
+
+    def compute(self, feats, ops, inter, vf):
+        st = np.zeros(12, np.float32)
+        f = np.array(feats, np.int32)
+        o = np.array(ops, np.int32)
+        t = np.array(list(inter) + [0], np.int32)
+        rc = self.lib.gafime_bucket_compute(self.h, _p(f), _p(o), len(feats), _p(t), vf, _p(st))
+        return rc, st
+
+    def free(self):
+        assert self.lib.gafime_bucket_free(self.h) == 0
+
+
+def _cases(g, prefix):
+    feats, ops = g[f"{prefix}_feats"], g[f"{prefix}_ops"]
+    for q in range(feats.shape[0]):
+        a = int((feats[q] >= 0).sum())
+        yield q, feats[q, :a].tolist(), ops[q, :a].tolist()
+
+
+def test_bucket_compute_matches_reference_cpu(lib, golden):
+    g = golden("chains.npz")
+    vf = int(g["val_fold"])
+    b = Small(lib, g["X"], g["y"], g["mask"])
+    try:
+        for q, feats, ops in _cases(g, "chain"):
+            rc, st = b.compute(feats, ops, g["chain_inter"][q, :len(feats) - 1].tolist(), vf)
+            assert rc == 0
+            np.testing.assert_allclose(st, g["chain_stats"][q], rtol=RTOL, atol=ATOL, err_msg=str((feats, ops)))
+    finally:
+        b.free()
+
+
+def test_fused_interaction_matches_reference_cpu(lib, golden):
+    g = golden("chains.npz")
+    vf = int(g["val_fold"])
+    X = g["X"]
+    y = np.ascontiguousarray(g["y"], dtype=np.float32)
+    mask = np.ascontiguousarray(g["mask"], dtype=np.uint8)
+    for q, feats, ops in _cases(g, "fused"):
+        cols = [np.ascontiguousarray(X[:, c], dtype=np.float32) for c in feats]
+        ptrs = (ctypes.c_void_p * len(cols))(*[c.ctypes.data for c in cols])
+        o = np.array(ops, np.int32)
+        st = np.zeros(12, np.float32)
+        rc = lib.gafime_fused_interaction(ptrs, _p(y), _p(mask), _p(o), len(feats), int(g["fused_type"][q]), vf,
+                                          len(y), _p(st))
+        assert rc == 0
+        np.testing.assert_allclose(st, g["fused_stats"][q], rtol=RTOL, atol=ATOL)
+
+
+def test_batch_and_interleaved_agree_with_single_calls(lib, oracle):
+    rng = np.random.default_rng(4)
+    n = 30_000
+    X = rng.standard_normal((n, 5)).astype(np.float32)
+    y = rng.standard_normal(n).astype(np.float32)
+    mask = rng.integers(0, 3, n).astype(np.uint8)
+    b = Small(lib, X, y, mask)
+    try:
+        N = 200
+        idx = rng.integers(0, 5, (N, 2)).astype(np.int32)
+        ops = rng.integers(0, 11, (N, 2)).astype(np.int32)
+        inter = rng.integers(0, 6, N).astype(np.int32)
+        st = np.zeros((N, 12), np.float32)
+        rc = lib.gafime_bucket_compute_batch(b.h, _p(idx), _p(ops), _p(inter), N, 1, _p(st))
+        assert rc == 0
+        for q in range(0, N, 17):
+            rc, one = b.compute(idx[q].tolist(), ops[q].tolist(), [int(inter[q])], 1)
+            assert rc == 0
+            np.testing.assert_allclose(st[q], one, rtol=1e-6, atol=1e-4)
+            ref = oracle.chain_stats([X[:, c] for c in idx[q]], y, mask, ops[q], [inter[q]], 1)
+            np.testing.assert_allclose(st[q], ref.astype(np.float32), rtol=RTOL, atol=ATOL)
+        # interleaved: two slots over the same rows
+        fa, oa = np.array([0, 1], np.int32), np.array([1, 2], np.int32)
+        fb, ob = np.array([2, 3], np.int32), np.array([6, 0], np.int32)
+        sa, sb = np.zeros(12, np.float32), np.zeros(12, np.float32)
+        assert lib.gafime_interleaved_compute(b.h, _p(fa), _p(oa), 2, 1, _p(fb), _p(ob), 2, 0, 0, 1, _p(sa),
+                                              _p(sb)) == 0
+        np.testing.assert_allclose(sa, b.compute([0, 1], [1, 2], [1], 1)[1], rtol=1e-6, atol=1e-4)
+        np.testing.assert_allclose(sb, b.compute([2, 3], [6, 0], [0], 1)[1], rtol=1e-6, atol=1e-4)
+        # a rolling operator in slot B makes every row NaN there, and the row counts for neither slot
+        ob_roll = np.array([11, 0], np.int32)
+        assert lib.gafime_interleaved_compute(b.h, _p(fa), _p(oa), 2, 1, _p(fb), _p(ob_roll), 2, 0, 5, 1, _p(sa),
+                                              _p(sb)) == 0
+        assert np.all(sa == 0) and np.all(sb == 0)
+    finally:
+        b.free()
+
+
+def test_small_bucket_argument_errors(lib):
+    h = ctypes.c_void_p()
+    assert lib.gafime_bucket_alloc(100, 6, ctypes.byref(h)) == -1     # more than 5 features
+    assert lib.gafime_bucket_alloc(0, 3, ctypes.byref(h)) == -1
+    assert lib.gafime_bucket_free(None) == 0
+    X = np.ones((64, 3), np.float32)
+    b = Small(lib, X, np.ones(64, np.float32), np.zeros(64, np.uint8))
+    try:
+        assert b.compute([0], [0], [], 255)[0] == -1                    # arity 1
+        assert b.compute([0, 3], [0, 0], [0], 255)[0] == -1             # feature out of range
+        assert b.compute([0, 1], [0, 13], [0], 255)[0] == -1            # unknown unary op
+        assert b.compute([0, 1], [0, 0], [6], 255)[0] == -1             # unknown combiner
+        col = np.ones(64, np.float32)
+        assert lib.gafime_bucket_upload_feature(b.h, 3, _p(col)) == -1
+        idx = np.zeros(2, np.int32)
+        st = np.zeros(12 * 1025, np.float32)
+        assert lib.gafime_bucket_compute_batch(b.h, _p(idx), _p(idx), _p(idx), 1025, 0, _p(st)) == -1
+        f3 = np.array([0, 1, 2], np.int32)
+        assert lib.gafime_interleaved_compute(b.h, _p(f3), _p(f3), 3, 0, _p(f3), _p(f3), 2, 0, 0, 0, _p(st),
+                                              _p(st)) == -1
+    finally:
+        b.free()

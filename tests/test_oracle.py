@@ -96,3 +96,25 @@ def test_interaction_materialiser_degenerate_combos(oracle):
     np.testing.assert_array_equal(out[:, 1], (X[:, 1] - m[1]) * (X[:, 2] - m[2]))
     assert np.all(out[:, 2] == 1.0) and np.all(out[:, 3] == 1.0)
     np.testing.assert_array_equal(out[:, 4], out[:, 1] * 0 + (X[:, 0] - m[0]) * (X[:, 2] - m[2]))
+
+
+def _chain_cases(g, prefix):
+    feats, ops = g[f"{prefix}_feats"], g[f"{prefix}_ops"]
+    for q in range(feats.shape[0]):
+        a = int((feats[q] >= 0).sum())
+        yield q, feats[q, :a].tolist(), ops[q, :a].tolist()
+
+
+def test_chain_stats_match_reference_cpu(golden, oracle):
+    """Small-bucket chains (unary operators, per-step combiners, folds, arity 2-5) equal
+    gafime_fused_interaction_perpair_cpu after the reference's float cast."""
+    g = golden("chains.npz")
+    X, y, mask, vf = g["X"], g["y"], g["mask"], int(g["val_fold"])
+    for q, feats, ops in _chain_cases(g, "chain"):
+        inter = g["chain_inter"][q, :len(feats) - 1].tolist()
+        st = oracle.chain_stats([X[:, c] for c in feats], y, mask, ops, inter, vf)
+        np.testing.assert_array_equal(st.astype(np.float32), g["chain_stats"][q])
+    for q, feats, ops in _chain_cases(g, "fused"):
+        inter = [int(g["fused_type"][q])] * (len(feats) - 1)
+        st = oracle.chain_stats([X[:, c] for c in feats], y, mask, ops, inter, vf)
+        np.testing.assert_array_equal(st.astype(np.float32), g["fused_stats"][q])
