@@ -45,6 +45,8 @@ EXPORTED = (
     "gafime_bucket_alloc", "gafime_bucket_upload_feature", "gafime_bucket_upload_target",
     "gafime_bucket_upload_mask", "gafime_bucket_compute", "gafime_bucket_free",
     "gafime_bucket_compute_batch", "gafime_interleaved_compute", "gafime_fused_interaction",
+    "gafime_pipeline_init", "gafime_pipeline_submit", "gafime_pipeline_poll", "gafime_pipeline_wait",
+    "gafime_pipeline_pending", "gafime_pipeline_flush", "gafime_pipeline_free",
 )
 
 # kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
@@ -100,6 +102,13 @@ def _bind(lib: ctypes.CDLL) -> None:
         "gafime_bucket_compute_batch": ([_vp, _vp, _vp, _vp, _i, _i, _vp], _i),
         "gafime_interleaved_compute": ([_vp, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _vp, _vp], _i),
         "gafime_fused_interaction": ([_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp], _i),
+        "gafime_pipeline_init": ([_vp, _i, ctypes.POINTER(_vp)], _i),
+        "gafime_pipeline_submit": ([_vp, _vp, _vp, _vp, _i, _ip], _i),
+        "gafime_pipeline_poll": ([_vp, _vp, _ip], _i),
+        "gafime_pipeline_wait": ([_vp, _vp, _ip], _i),
+        "gafime_pipeline_pending": ([_vp], _i),
+        "gafime_pipeline_flush": ([_vp, _vp, _ip], _i),
+        "gafime_pipeline_free": ([_vp], _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

@@ -661,12 +661,28 @@ __global__ void sum_item_partials_kernel(const double* __restrict__ partial, int
 bool valid_unary(int op) { return op >= GAFIME_OP_IDENTITY && op <= GAFIME_OP_ROLLING_STD; }
 bool valid_combiner(int t) { return t >= GAFIME_INTERACT_MULT && t <= GAFIME_INTERACT_MIN; }
 
+// Row blocks per item of the chain kernel: about four CTAs per SM over all items.
+int chain_blocks(const Bucket& b, int items) {
+    int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((b.n + 255) / 256, (4 * (int64_t)b.sm_count + items - 1) / items));
+    return std::min(blocks, 1024);
+}
+
+// Queue the chain kernel and the per-item sums on `stream`: d_out[items][12 * kSlots].
+template <int kSlots>
+cudaError_t launch_chains(const Bucket& b, const ChainDesc* d_descs, int items, int val_fold_id, double* d_part,
+                          double* d_out, cudaStream_t stream) {
+    const int blocks = chain_blocks(b, items);
+    chain_stats_kernel<kSlots><<<dim3((unsigned)blocks, (unsigned)items), 256, 0, stream>>>(
+        b.d_data, b.d_mask, b.n, b.ld, b.f, d_descs, val_fold_id, d_part);
+    sum_item_partials_kernel<<<items, 32, 0, stream>>>(d_part, blocks, 12 * kSlots, d_out);
+    return cudaGetLastError();
+}
+
 // Run `items` chain groups of kSlots chains and write items x (12 * kSlots) float stats.
 template <int kSlots>
 int run_chains(Bucket& b, const ChainDesc* h_descs, int items, int val_fold_id, float* h_stats) {
     const int width = 12 * kSlots;
-    int blocks = (int)std::max<int64_t>(1, std::min<int64_t>((b.n + 255) / 256, (4 * (int64_t)b.sm_count + items - 1) / items));
-    blocks = std::min(blocks, 1024);
+    const int blocks = chain_blocks(b, items);
     const size_t desc_bytes = (size_t)items * kSlots * sizeof(ChainDesc);
     const size_t part_bytes = (size_t)items * blocks * width * sizeof(double);
     const size_t off_part = (desc_bytes + 255) / 256 * 256;
@@ -682,10 +698,7 @@ int run_chains(Bucket& b, const ChainDesc* h_descs, int items, int val_fold_id, 
     e = cudaMemcpyAsync(d_descs, h_descs, desc_bytes, cudaMemcpyHostToDevice, b.stream);
     if (e == cudaSuccess) {
         KernelTimer timer(b.stream, GAFIME_KERNEL_LEGACY_PAIR);
-        chain_stats_kernel<kSlots><<<dim3((unsigned)blocks, (unsigned)items), 256, 0, b.stream>>>(
-            b.d_data, b.d_mask, b.n, b.ld, b.f, d_descs, val_fold_id, d_part);
-        sum_item_partials_kernel<<<items, 32, 0, b.stream>>>(d_part, blocks, width, d_out);
-        e = cudaGetLastError();
+        e = launch_chains<kSlots>(b, d_descs, items, val_fold_id, d_part, d_out, b.stream);
     }
     if (e == cudaSuccess) e = cudaMemcpyAsync(host.data(), d_out, out_bytes, cudaMemcpyDeviceToHost, b.stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b.stream);
@@ -702,6 +715,29 @@ int upload_column(Bucket* b, int64_t col, const void* h, size_t bytes) {
     return e == cudaSuccess ? GAFIME_SUCCESS : GAFIME_ERROR_KERNEL_FAILED;
 }
 
+}  // namespace
+}  // namespace gafime
+
+namespace gafime {
+namespace {
+// Arity-2 descriptors of a batch (indices / ops [2 per item], one combiner per item);
+// false when an id is out of range.
+bool batch_descs(const Bucket& b, const int* idx, const int* ops, const int* inter, int n, ChainDesc* d) {
+    for (int q = 0; q < n; ++q) {
+        ChainDesc& c = d[q];
+        c = ChainDesc{};
+        c.arity = 2;
+        for (int k = 0; k < 2; ++k) {
+            const int fi = idx[2 * q + k], op = ops[2 * q + k];
+            if (fi < 0 || fi >= b.f || !valid_unary(op)) return false;
+            c.feat[k] = fi;
+            c.op[k] = op;
+        }
+        if (!valid_combiner(inter[q])) return false;
+        c.inter[0] = inter[q];
+    }
+    return true;
+}
 }  // namespace
 }  // namespace gafime
 
@@ -759,19 +795,8 @@ extern "C" int gafime_bucket_compute_batch(GafimeBucket bucket, const int* batch
     if (batch_size <= 0 || batch_size > kMaxBatch) return GAFIME_ERROR_INVALID_ARGS;
     Bucket* b = (Bucket*)bucket;
     std::vector<ChainDesc> d((size_t)batch_size);
-    for (int q = 0; q < batch_size; ++q) {
-        ChainDesc& c = d[q];
-        c = ChainDesc{};
-        c.arity = 2;
-        for (int k = 0; k < 2; ++k) {
-            const int fi = batch_indices[2 * q + k], op = batch_ops[2 * q + k];
-            if (fi < 0 || fi >= b->f || !valid_unary(op)) return GAFIME_ERROR_INVALID_ARGS;
-            c.feat[k] = fi;
-            c.op[k] = op;
-        }
-        if (!valid_combiner(batch_interact[q])) return GAFIME_ERROR_INVALID_ARGS;
-        c.inter[0] = batch_interact[q];
-    }
+    if (!batch_descs(*b, batch_indices, batch_ops, batch_interact, batch_size, d.data()))
+        return GAFIME_ERROR_INVALID_ARGS;
     cudaSetDevice(b->device);
     return run_chains<1>(*b, d.data(), batch_size, val_fold_id, h_stats_batch);
 }
@@ -836,4 +861,171 @@ extern "C" int gafime_fused_interaction(const float** h_inputs, const float* h_t
     }
     gafime_bucket_free(b);
     return st;
+}
+
+// ============================================================ async pipeline ==
+//
+// The reference's 4-slot ring (interfaces.h:433-504, kernels.cu:1755-2140): submit queues a
+// batch of arity-2 interactions on its slot's stream and returns at once (PIPELINE_FULL when
+// four batches are in flight); poll / wait hand back the oldest batch first; flush drains
+// every pending batch in submission order.  Each slot owns pinned staging and device
+// buffers sized for the largest batch, so submit allocates nothing.
+
+namespace gafime {
+namespace {
+
+constexpr int kPipeSlots = 4;      // PIPELINE_SLOTS
+constexpr int kPipeMaxBatch = 1024; // PIPELINE_MAX_BATCH
+
+struct PipeSlot {
+    cudaStream_t stream = nullptr;
+    cudaEvent_t done = nullptr;
+    ChainDesc* h_desc = nullptr;   // pinned [kPipeMaxBatch]
+    double* h_out = nullptr;       // pinned [kPipeMaxBatch * 12]
+    ChainDesc* d_desc = nullptr;
+    double* d_part = nullptr;      // [kPipeMaxBatch * max blocks * 12]
+    double* d_out = nullptr;       // [kPipeMaxBatch * 12]
+    int batch = 0;
+    bool busy = false;
+};
+
+struct Pipeline {
+    Bucket* b = nullptr;
+    int val_fold = 0;
+    PipeSlot slots[kPipeSlots];
+    int read = 0, write = 0, pending = 0;
+};
+
+void pipe_release(Pipeline* p) {
+    for (PipeSlot& s : p->slots) {
+        if (s.done) cudaEventSynchronize(s.done);
+        if (s.stream) cudaStreamDestroy(s.stream);
+        if (s.done) cudaEventDestroy(s.done);
+        if (s.h_desc) cudaFreeHost(s.h_desc);
+        if (s.h_out) cudaFreeHost(s.h_out);
+        if (s.d_desc) cudaFree(s.d_desc);
+        if (s.d_part) cudaFree(s.d_part);
+        if (s.d_out) cudaFree(s.d_out);
+    }
+    delete p;
+}
+
+// hand the oldest batch back (its event has completed)
+void pipe_pop(Pipeline* p, float* h_stats_out, int* batch_size_out) {
+    PipeSlot& s = p->slots[p->read];
+    if (h_stats_out)
+        for (int m = 0; m < s.batch * 12; ++m) h_stats_out[m] = (float)s.h_out[m];
+    if (batch_size_out) *batch_size_out = s.batch;
+    s.batch = 0;
+    s.busy = false;
+    p->read = (p->read + 1) % kPipeSlots;
+    --p->pending;
+}
+
+}  // namespace
+}  // namespace gafime
+
+extern "C" int gafime_pipeline_init(GafimeBucket bucket, int val_fold_id, GafimePipeline* pipeline_out) {
+    if (!bucket || !pipeline_out) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket* b = (Bucket*)bucket;
+    cudaSetDevice(b->device);
+    Pipeline* p = new (std::nothrow) Pipeline();
+    if (!p) return GAFIME_ERROR_OUT_OF_MEMORY;
+    p->b = b;
+    p->val_fold = val_fold_id;
+    int max_part = 0;
+    for (int items = 1; items <= kPipeMaxBatch; ++items) max_part = std::max(max_part, items * chain_blocks(*b, items));
+    cudaError_t e = cudaSuccess;
+    for (PipeSlot& s : p->slots) {
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaMallocHost(&s.h_desc, kPipeMaxBatch * sizeof(ChainDesc));
+        if (e == cudaSuccess) e = cudaMallocHost(&s.h_out, kPipeMaxBatch * 12 * sizeof(double));
+        if (e == cudaSuccess) e = cudaMalloc(&s.d_desc, kPipeMaxBatch * sizeof(ChainDesc));
+        if (e == cudaSuccess) e = cudaMalloc(&s.d_part, (size_t)max_part * 12 * sizeof(double));
+        if (e == cudaSuccess) e = cudaMalloc(&s.d_out, kPipeMaxBatch * 12 * sizeof(double));
+    }
+    if (e != cudaSuccess) {
+        pipe_release(p);
+        cudaGetLastError();
+        return e == cudaErrorMemoryAllocation ? GAFIME_ERROR_OUT_OF_MEMORY : GAFIME_ERROR_KERNEL_FAILED;
+    }
+    *pipeline_out = p;
+    return GAFIME_SUCCESS;
+}
+
+extern "C" int gafime_pipeline_submit(GafimePipeline pipeline, const int* h_indices, const int* h_ops,
+                                      const int* h_interact, int batch_size, int* slot_id_out) {
+    if (!pipeline || !h_indices || !h_ops || !h_interact) return GAFIME_ERROR_INVALID_ARGS;
+    if (batch_size <= 0 || batch_size > kPipeMaxBatch) return GAFIME_ERROR_INVALID_ARGS;
+    Pipeline* p = (Pipeline*)pipeline;
+    if (p->pending >= kPipeSlots) {
+        if (slot_id_out) *slot_id_out = -1;
+        return GAFIME_ERROR_PIPELINE_FULL;
+    }
+    const int id = p->write;
+    PipeSlot& s = p->slots[id];
+    if (!batch_descs(*p->b, h_indices, h_ops, h_interact, batch_size, s.h_desc)) return GAFIME_ERROR_INVALID_ARGS;
+    cudaSetDevice(p->b->device);
+    cudaError_t e = cudaMemcpyAsync(s.d_desc, s.h_desc, (size_t)batch_size * sizeof(ChainDesc), cudaMemcpyHostToDevice,
+                                    s.stream);
+    if (e == cudaSuccess) e = launch_chains<1>(*p->b, s.d_desc, batch_size, p->val_fold, s.d_part, s.d_out, s.stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(s.h_out, s.d_out, (size_t)batch_size * 12 * sizeof(double), cudaMemcpyDeviceToHost, s.stream);
+    if (e == cudaSuccess) e = cudaEventRecord(s.done, s.stream);
+    if (e != cudaSuccess) return GAFIME_ERROR_KERNEL_FAILED;
+    s.batch = batch_size;
+    s.busy = true;
+    p->write = (p->write + 1) % kPipeSlots;
+    ++p->pending;
+    if (slot_id_out) *slot_id_out = id;
+    return GAFIME_SUCCESS;
+}
+
+extern "C" int gafime_pipeline_poll(GafimePipeline pipeline, float* h_stats_out, int* batch_size_out) {
+    if (!pipeline) return GAFIME_ERROR_INVALID_ARGS;
+    Pipeline* p = (Pipeline*)pipeline;
+    if (p->pending == 0) return GAFIME_ERROR_NO_RESULT;
+    const cudaError_t e = cudaEventQuery(p->slots[p->read].done);
+    if (e == cudaErrorNotReady) return GAFIME_ERROR_NO_RESULT;
+    if (e != cudaSuccess) return GAFIME_ERROR_KERNEL_FAILED;
+    pipe_pop(p, h_stats_out, batch_size_out);
+    return GAFIME_SUCCESS;
+}
+
+extern "C" int gafime_pipeline_wait(GafimePipeline pipeline, float* h_stats_out, int* batch_size_out) {
+    if (!pipeline) return GAFIME_ERROR_INVALID_ARGS;
+    Pipeline* p = (Pipeline*)pipeline;
+    if (p->pending == 0) return GAFIME_ERROR_NO_RESULT;
+    if (cudaEventSynchronize(p->slots[p->read].done) != cudaSuccess) return GAFIME_ERROR_KERNEL_FAILED;
+    pipe_pop(p, h_stats_out, batch_size_out);
+    return GAFIME_SUCCESS;
+}
+
+extern "C" int gafime_pipeline_pending(GafimePipeline pipeline) {
+    return pipeline ? ((Pipeline*)pipeline)->pending : 0;
+}
+
+extern "C" int gafime_pipeline_flush(GafimePipeline pipeline, float* h_all_stats_out, int* total_batch_size_out) {
+    if (!pipeline) return GAFIME_ERROR_INVALID_ARGS;
+    Pipeline* p = (Pipeline*)pipeline;
+    int total = 0;
+    float* w = h_all_stats_out;
+    while (p->pending > 0) {
+        int n = 0;
+        const int st = gafime_pipeline_wait(pipeline, w, &n);
+        if (st != GAFIME_SUCCESS) return st;
+        total += n;
+        if (w) w += (size_t)n * 12;
+    }
+    if (total_batch_size_out) *total_batch_size_out = total;
+    return GAFIME_SUCCESS;
+}
+
+extern "C" int gafime_pipeline_free(GafimePipeline pipeline) {
+    if (!pipeline) return GAFIME_SUCCESS;
+    Pipeline* p = (Pipeline*)pipeline;
+    cudaSetDevice(p->b->device);
+    pipe_release(p);
+    return GAFIME_SUCCESS;
 }

@@ -170,6 +170,24 @@ int gafime_fused_interaction(const float** h_inputs, const float* h_target, cons
                              const int* h_ops, int arity, int interaction_type, int val_fold_id,
                              int n_samples, float* h_stats);
 
+/* ------------------------------------------------------- async pipeline ---- */
+/* interfaces.h:433-504.  A 4-slot ring of arity-2 batches on a GafimeBucket: submit
+ * returns at once (GAFIME_ERROR_PIPELINE_FULL with *slot_id_out = -1 when four batches
+ * are in flight); poll (GAFIME_ERROR_NO_RESULT while the oldest batch runs) and wait
+ * return the oldest batch's [batch_size * 12] stats; flush drains all in submission
+ * order; pending returns 0-4 (0 for NULL). */
+typedef void* GafimePipeline;  /* interfaces.h:41 */
+#define PIPELINE_SLOTS 4
+#define PIPELINE_MAX_BATCH 1024
+int gafime_pipeline_init(GafimeBucket bucket, int val_fold_id, GafimePipeline* pipeline_out);
+int gafime_pipeline_submit(GafimePipeline pipeline, const int* h_indices, const int* h_ops,
+                           const int* h_interact, int batch_size, int* slot_id_out);
+int gafime_pipeline_poll(GafimePipeline pipeline, float* h_stats_out, int* batch_size_out);
+int gafime_pipeline_wait(GafimePipeline pipeline, float* h_stats_out, int* batch_size_out);
+int gafime_pipeline_pending(GafimePipeline pipeline);
+int gafime_pipeline_flush(GafimePipeline pipeline, float* h_all_stats_out, int* total_batch_size_out);
+int gafime_pipeline_free(GafimePipeline pipeline);
+
 /* ------------------------------------------------------- NEW: all pairs ---- */
 
 /*

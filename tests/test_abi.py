@@ -111,3 +111,10 @@ def test_reference_fused_kernel_wrappers_bind_this_library(lib):
         obj = object.__new__(cls)
         obj.lib = lib
         obj._setup_functions()
+
+
+def test_pipeline_null_handles(lib):
+    assert lib.gafime_pipeline_pending(None) == 0
+    assert lib.gafime_pipeline_free(None) == 0
+    assert lib.gafime_pipeline_poll(None, None, None) == -1
+    assert lib.gafime_pipeline_init(None, 0, None) == -1

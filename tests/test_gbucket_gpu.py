@@ -146,3 +146,66 @@ def test_small_bucket_argument_errors(lib):
                                               _p(st)) == -1
     finally:
         b.free()
+
+
+def test_async_pipeline_fifo_backpressure_and_results(lib):
+    import time
+    rng = np.random.default_rng(12)
+    n = 20_000
+    X = rng.standard_normal((n, 4)).astype(np.float32)
+    y = rng.standard_normal(n).astype(np.float32)
+    mask = rng.integers(0, 4, n).astype(np.uint8)
+    b = Small(lib, X, y, mask)
+    pipe = ctypes.c_void_p()
+    assert lib.gafime_pipeline_init(b.h, 3, ctypes.byref(pipe)) == 0
+    try:
+        batches = []
+        for s in range(5):
+            N = 50 + 30 * s
+            idx = rng.integers(0, 4, (N, 2)).astype(np.int32)
+            ops = rng.integers(0, 11, (N, 2)).astype(np.int32)
+            inter = rng.integers(0, 6, N).astype(np.int32)
+            batches.append((idx, ops, inter))
+        slot = ctypes.c_int(-2)
+        for s in range(4):
+            idx, ops, inter = batches[s]
+            assert lib.gafime_pipeline_submit(pipe, _p(idx), _p(ops), _p(inter), len(inter), ctypes.byref(slot)) == 0
+            assert slot.value == s
+        assert lib.gafime_pipeline_pending(pipe) == 4
+        idx, ops, inter = batches[4]
+        assert lib.gafime_pipeline_submit(pipe, _p(idx), _p(ops), _p(inter), len(inter), ctypes.byref(slot)) == -5
+        assert slot.value == -1
+        # poll returns the oldest batch first (bounded wait for it to finish)
+        out = np.zeros(1024 * 12, np.float32)
+        got = ctypes.c_int(0)
+        t0 = time.time()
+        while True:
+            rc = lib.gafime_pipeline_poll(pipe, _p(out), ctypes.byref(got))
+            if rc == 0:
+                break
+            assert rc == -6 and time.time() - t0 < 30
+            time.sleep(0.001)
+        results = [out[:got.value * 12].reshape(-1, 12).copy()]
+        assert got.value == len(batches[0][2])
+        assert lib.gafime_pipeline_submit(pipe, _p(idx), _p(ops), _p(inter), len(inter), ctypes.byref(slot)) == 0
+        assert lib.gafime_pipeline_wait(pipe, _p(out), ctypes.byref(got)) == 0
+        results.append(out[:got.value * 12].reshape(-1, 12).copy())
+        allout = np.zeros(5 * 1024 * 12, np.float32)
+        total = ctypes.c_int(0)
+        assert lib.gafime_pipeline_flush(pipe, _p(allout), ctypes.byref(total)) == 0
+        assert lib.gafime_pipeline_pending(pipe) == 0
+        assert lib.gafime_pipeline_poll(pipe, _p(out), ctypes.byref(got)) == -6
+        rest = allout[:total.value * 12].reshape(-1, 12)
+        sizes = [len(bt[2]) for bt in batches[2:]]
+        assert total.value == sum(sizes)
+        off = 0
+        for sz in sizes:
+            results.append(rest[off:off + sz])
+            off += sz
+        for (idx, ops, inter), res in zip(batches, results):
+            ref = np.zeros((len(inter), 12), np.float32)
+            assert lib.gafime_bucket_compute_batch(b.h, _p(idx), _p(ops), _p(inter), len(inter), 3, _p(ref)) == 0
+            np.testing.assert_allclose(res, ref, rtol=1e-6, atol=1e-4)
+    finally:
+        assert lib.gafime_pipeline_free(pipe) == 0
+        b.free()
