@@ -46,7 +46,7 @@ EXPORTED = (
     "gafime_bucket_upload_mask", "gafime_bucket_compute", "gafime_bucket_free",
     "gafime_bucket_compute_batch", "gafime_interleaved_compute", "gafime_fused_interaction",
     "gafime_pipeline_init", "gafime_pipeline_submit", "gafime_pipeline_poll", "gafime_pipeline_wait",
-    "gafime_pipeline_pending", "gafime_pipeline_flush", "gafime_pipeline_free",
+    "gafime_pipeline_pending", "gafime_pipeline_flush", "gafime_pipeline_free", "gafime_pearson_cuda",
 )
 
 # kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
@@ -109,6 +109,7 @@ def _bind(lib: ctypes.CDLL) -> None:
         "gafime_pipeline_pending": ([_vp], _i),
         "gafime_pipeline_flush": ([_vp, _vp, _ip], _i),
         "gafime_pipeline_free": ([_vp], _i),
+        "gafime_pearson_cuda": ([_vp, _vp, ctypes.c_int32, _vp], _i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

@@ -11,7 +11,10 @@
 // mutual-information route (native_cuda_backend.py:420-468).  Synchronous, host buffers in
 // and out, like the reference.
 #include <cuda_runtime.h>
+#include <math.h>
 #include <stdint.h>
+
+#include <algorithm>
 
 #include "engine.h"
 
@@ -86,6 +89,85 @@ extern "C" int gafime_feature_interaction_cuda(const float* X, const float* mean
     cudaFree(d_out);
     cudaFree(d_idx);
     cudaFree(d_off);
+    if (e == cudaSuccess) return GAFIME_SUCCESS;
+    return oom ? GAFIME_ERROR_OUT_OF_MEMORY : GAFIME_ERROR_KERNEL_FAILED;
+}
+
+// ---- gafime_pearson_cuda ----------------------------------------------------------
+//
+// Declared by the reference (interfaces.h:420-425) without a GPU implementation; the
+// arithmetic follows its CPU twin gafime_pearson_cpu (cpu_backend.cpp:374-411): fp64
+// sums, r = (Sxy - Sx*my) / sqrt((Sxx - Sx*mx)(Syy - Sy*my)), 0 when a variance is <= 0,
+// cast to float.  Sums here are reduced in a fixed order (deterministic).
+
+namespace gafime {
+namespace {
+
+constexpr int kPearsonBlocks = 256;
+
+__global__ void __launch_bounds__(256) pearson_sums_kernel(const float* __restrict__ x, const float* __restrict__ y,
+                                                           int32_t n, double* __restrict__ part /*[blocks][5]*/) {
+    __shared__ double red[8][5];
+    double s[5] = {0.0, 0.0, 0.0, 0.0, 0.0};
+    for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
+        const double xi = x[i], yi = y[i];
+        s[0] += xi;
+        s[1] += yi;
+        s[2] += xi * xi;
+        s[3] += yi * yi;
+        s[4] += xi * yi;
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    #pragma unroll
+    for (int m = 0; m < 5; ++m)
+        for (int o = 16; o > 0; o >>= 1) s[m] += __shfl_down_sync(0xffffffffu, s[m], o);
+    if (lane == 0)
+        #pragma unroll
+        for (int m = 0; m < 5; ++m) red[warp][m] = s[m];
+    __syncthreads();
+    if (threadIdx.x < 5) {
+        double t = red[0][threadIdx.x];
+        for (int w = 1; w < 8; ++w) t += red[w][threadIdx.x];
+        part[blockIdx.x * 5 + threadIdx.x] = t;
+    }
+}
+
+__global__ void pearson_finish_kernel(const double* __restrict__ part, int blocks, int32_t n, float* out) {
+    double s[5] = {0.0, 0.0, 0.0, 0.0, 0.0};
+    for (int b = 0; b < blocks; ++b)
+        for (int m = 0; m < 5; ++m) s[m] += part[b * 5 + m];
+    const double mx = s[0] / n, my = s[1] / n;
+    const double vx = s[2] - s[0] * mx, vy = s[3] - s[1] * my, cov = s[4] - s[0] * my;
+    *out = (vx <= 0.0 || vy <= 0.0) ? 0.0f : (float)(cov / sqrt(vx * vy));
+}
+
+}  // namespace
+}  // namespace gafime
+
+extern "C" int gafime_pearson_cuda(const float* x, const float* y, int32_t n, float* result_out) {
+    if (!x || !y || !result_out || n <= 0) return GAFIME_ERROR_INVALID_ARGS;
+    int dev_count = 0;
+    if (cudaGetDeviceCount(&dev_count) != cudaSuccess || dev_count == 0) return GAFIME_ERROR_CUDA_NOT_AVAILABLE;
+    const int blocks = (int)std::min<int64_t>(kPearsonBlocks, ((int64_t)n + 255) / 256);
+    float *d_x = nullptr, *d_y = nullptr, *d_r = nullptr;
+    double* d_part = nullptr;
+    cudaError_t e = cudaMalloc(&d_x, (size_t)n * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&d_y, (size_t)n * sizeof(float));
+    if (e == cudaSuccess) e = cudaMalloc(&d_part, (size_t)blocks * 5 * sizeof(double));
+    if (e == cudaSuccess) e = cudaMalloc(&d_r, sizeof(float));
+    if (e == cudaSuccess) e = cudaMemcpy(d_x, x, (size_t)n * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(d_y, y, (size_t)n * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        pearson_sums_kernel<<<blocks, 256>>>(d_x, d_y, n, d_part);
+        pearson_finish_kernel<<<1, 1>>>(d_part, blocks, n, d_r);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(result_out, d_r, sizeof(float), cudaMemcpyDeviceToHost);
+    const bool oom = e == cudaErrorMemoryAllocation;
+    cudaFree(d_x);
+    cudaFree(d_y);
+    cudaFree(d_part);
+    cudaFree(d_r);
     if (e == cudaSuccess) return GAFIME_SUCCESS;
     return oom ? GAFIME_ERROR_OUT_OF_MEMORY : GAFIME_ERROR_KERNEL_FAILED;
 }

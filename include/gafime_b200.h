@@ -130,6 +130,11 @@ int gafime_feature_interaction_cuda(const float* X, const float* means, float* o
                                     const int32_t* combo_indices, const int32_t* combo_offsets,
                                     int32_t n_samples, int32_t n_features, int32_t n_combos);
 
+/* interfaces.h:420-425 (declared there without a GPU implementation): Pearson r of two
+ * host vectors, arithmetic of gafime_pearson_cpu (cpu_backend.cpp:374-411), fp64 sums,
+ * 0 when a variance is <= 0, result cast to float. */
+int gafime_pearson_cuda(const float* x, const float* y, int32_t n, float* result_out);
+
 /* ------------------------------------------- small bucket (GafimeBucket) ---- */
 /* interfaces.h:176-382.  At most GAFIME_MAX_FEATURES columns; arity-2..5 chains
  * x = t_{a-2}(...t_1(t_0(op_0(f_0), op_1(f_1)), op_2(f_2))..., op_{a-1}(f_{a-1})) in fp32

@@ -209,3 +209,24 @@ def test_async_pipeline_fifo_backpressure_and_results(lib):
     finally:
         assert lib.gafime_pipeline_free(pipe) == 0
         b.free()
+
+
+def test_pearson_cuda_matches_cpu_formula(lib):
+    """gafime_pearson_cuda (declared by the reference without a GPU body) follows
+    gafime_pearson_cpu's arithmetic: fp64 sums, r cast to float."""
+    rng = np.random.default_rng(2)
+    for n in (1, 7, 1000, 300_001):
+        x = rng.standard_normal(n).astype(np.float32)
+        y = (0.3 * x + rng.standard_normal(n)).astype(np.float32)
+        r = np.zeros(1, np.float32)
+        assert lib.gafime_pearson_cuda(_p(x), _p(y), n, _p(r)) == 0
+        xd, yd = x.astype(np.float64), y.astype(np.float64)
+        sx, sy = xd.sum(), yd.sum()
+        vx, vy = (xd * xd).sum() - sx * (sx / n), (yd * yd).sum() - sy * (sy / n)
+        cov = (xd * yd).sum() - sx * (sy / n)
+        want = 0.0 if (vx <= 0 or vy <= 0) else cov / np.sqrt(vx * vy)
+        np.testing.assert_allclose(r[0], np.float32(want), rtol=1e-6, atol=1e-7)
+    const = np.ones(10, np.float32)
+    r = np.zeros(1, np.float32)
+    assert lib.gafime_pearson_cuda(_p(const), _p(const), 10, _p(r)) == 0 and r[0] == 0.0
+    assert lib.gafime_pearson_cuda(_p(const), _p(const), 0, _p(r)) == -1
