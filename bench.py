@@ -565,6 +565,9 @@ def run_ours(args):
                 "frac": achieved / peak, "peak_source": f"hbm_gbs of {peak_kind} MEASURED_PEAKS.json",
                 "avg_launch_ms": avg_ms, "launches": d["launches"],
                 "algorithmic": f"13 B per pair-row x {my_pairs:.0f} pairs x {n} rows per launch",
+                "note": ("effective bytes of the per-pair formulation: the tiled kernel reads each "
+                         "column block once per 16 x 16 pair block, so it can exceed 1.0; its binding "
+                         "unit is the shared-memory (LSU) pipe"),
                 "traffic": NCU_TRAFFIC_BYTES.get((args.workload, dom))}
 
     cpu = None

@@ -52,7 +52,8 @@ EXPORTED = (
 # kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
 KERNEL_IDS = {"column_stats": 1, "pair_moments": 2, "epilogue_topk": 3, "merge": 4,
               "mi_pass1": 5, "mi_pass2": 6, "mi_finish": 7, "legacy_pair": 8,
-              "finite_check": 9, "gram_tc": 10, "gram_prep": 11, "gram_reduce": 12}
+              "finite_check": 9, "gram_tc": 10, "gram_prep": 11, "gram_reduce": 12,
+              "mi_class_copy": 13}
 
 
 class GafimeError(RuntimeError):

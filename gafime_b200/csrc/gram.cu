@@ -192,9 +192,15 @@ __device__ __forceinline__ void fence_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// 1 / safe(v) with the hardware reciprocal (max error 1 ulp; the operand split keeps 22
+// bits of it).  The statistics pass and the operand converters both use this function, so
+// the centring means are those of the values the tensor cores multiply.  Subnormals flush
+// to zero: a result for |v| >= 2^126, an input only when eps < 2^-126.
 __device__ __forceinline__ float safe_recip(float v, float eps) {
     float d = fabsf(v) < eps ? copysignf(eps, v) : v;
-    return __frcp_rn(d);
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+    return r;
 }
 
 // A operand in tensor memory (lane = row m, 8 columns = 16 fp16 along K), B in shared memory

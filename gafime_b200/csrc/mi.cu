@@ -12,10 +12,14 @@
 // Device plan (per call):
 //   y codes : y-bin of every row, remapped to the U bins that occur (exact: bins no row
 //             falls in contribute nothing);
+//   class copy: the feature columns are copied with their rows grouped by y code, so every
+//             row split below holds rows of one y class only and a pair's histogram for it
+//             is one row of `bins` counters (the joint histogram is order-free);
 //   pass 1  : per-pair min / max of x over row splits, merged with 64-bit integer
 //             atomics on an order-preserving key (deterministic);
-//   pass 2  : each thread owns one pair and a private 16-bit joint histogram
-//             (bins x U) in shared memory; split results merge with integer atomics;
+//   pass 2  : each thread owns one pair and a private 16-bit x histogram for the split's
+//             class in shared memory; split results merge into the joint histogram with
+//             integer atomics;
 //   finish  : MI per pair in fp64 in the reference's summation order, then the same
 //             bitonic top-k as the Pearson epilogue.
 #include <cuda_runtime.h>
@@ -23,6 +27,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <vector>
 
 #include "engine.h"
 #include "select.cuh"
@@ -31,7 +36,7 @@ namespace gafime {
 
 namespace {
 
-constexpr int kMiRows = 128;                 // rows per shared-memory chunk
+constexpr int kMiRows = 64;                  // rows per shared-memory chunk
 constexpr int64_t kMiMaxSplitRows = 32768;   // 16-bit counters cannot overflow
 
 __device__ __forceinline__ long long dkey(double v) {
@@ -59,18 +64,23 @@ __device__ __forceinline__ double combine_d(double a, double b, int op, double e
     }
 }
 
+// Rows [r0, r1) of the class-grouped copy, all of y class u
+struct MiSplit {
+    int64_t r0, r1;
+    int u, pad;
+};
+
 struct MiArgs {
-    const float* x;
-    int64_t ld, n, f;
+    const float* xs;          // class-grouped copy of the feature columns, [f][lds]
+    int64_t lds, f;
     const double* colstats;   // mean at [c*4 + 3]
     const TileCoord* tiles;
     int n_tiles;
     int op;
     float eps;
-    int64_t rows_per_split;
+    const MiSplit* splits;
     long long* mm;            // [n_tiles][4096][2] keys: min, max
-    const uint8_t* ycode;     // [n] compact y-bin codes
-    int bins, U, hstride;     // hstride: 16-bit slots per pair in shared memory
+    int bins, U, hwords;      // hwords: 32-bit words per thread histogram (two 16-bit counters each)
     unsigned* hist;           // [n_tiles][4096][bins * U]
 };
 
@@ -82,8 +92,7 @@ __global__ void __launch_bounds__(TS * TS) mi_pass_kernel(MiArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     V* As = reinterpret_cast<V*>(smem_raw);                  // [kMiRows][TS + 1]
     V* Bs = As + kMiRows * (TS + 1);                         // [kMiRows][TS + 1]
-    uint8_t* ys = reinterpret_cast<uint8_t*>(Bs + kMiRows * (TS + 1));  // [kMiRows]
-    uint16_t* hs = reinterpret_cast<uint16_t*>(ys + kMiRows);           // [TS*TS][hstride]
+    uint16_t* hs = reinterpret_cast<uint16_t*>(Bs + kMiRows * (TS + 1));  // [warps][hwords][32 lanes][2]
 
     const int t = blockIdx.x / (SUBS * SUBS), sub = blockIdx.x % (SUBS * SUBS);
     const int si = sub / SUBS, sj = sub % SUBS;
@@ -98,15 +107,18 @@ __global__ void __launch_bounds__(TS * TS) mi_pass_kernel(MiArgs a) {
     const int e = (si * TS + li) * 64 + (sj * TS + lj);
     long long* mm = a.mm + ((int64_t)t * kTilePairs + e) * 2;
 
-    const int64_t r0 = (int64_t)blockIdx.y * a.rows_per_split;
-    const int64_t r1 = std::min<int64_t>(r0 + a.rows_per_split, a.n);
+    const MiSplit sp = a.splits[blockIdx.y];
+    const int64_t r0 = sp.r0, r1 = sp.r1;
 
     double mn = INFINITY, mx = -INFINITY;
     double xmin = 0.0, scale = 0.0;
     bool live = valid;
-    uint16_t* h = hs + tid * a.hstride;
+    // Each thread's private 16-bit histogram is interleaved with its warp's: counter c of
+    // lane l sits in word (c / 2) * 32 + l, so every lane only touches its own bank.
+    uint16_t* h = hs + (tid >> 5) * (a.hwords * 64) + ((tid & 31) << 1);
+    auto hidx = [](int c) { return ((c >> 1) << 6) + (c & 1); };
     if (PASS == 2) {
-        for (int c = 0; c < a.hstride; ++c) h[c] = 0;
+        for (int c = 0; c < 2 * a.hwords; ++c) h[hidx(c)] = 0;
         if (valid) {
             xmin = dval(mm[0]);
             double xmax = dval(mm[1]);
@@ -124,19 +136,17 @@ __global__ void __launch_bounds__(TS * TS) mi_pass_kernel(MiArgs a) {
             if (row < rows) {
                 int64_t ca = i0 + col, cb = j0 + col;
                 if (ca < a.f) {
-                    float raw = a.x[ca * a.ld + rb + row];
+                    float raw = a.xs[ca * a.lds + rb + row];
                     if (CENTRED) va = (V)((double)raw - a.colstats[ca * 4 + 3]); else va = (V)raw;
                 }
                 if (cb < a.f) {
-                    float raw = a.x[cb * a.ld + rb + row];
+                    float raw = a.xs[cb * a.lds + rb + row];
                     if (CENTRED) vb = (V)((double)raw - a.colstats[cb * 4 + 3]); else vb = (V)raw;
                 }
             }
             As[row * (TS + 1) + col] = va;
             Bs[row * (TS + 1) + col] = vb;
         }
-        if (PASS == 2)
-            for (int q = tid; q < rows; q += TS * TS) ys[q] = a.ycode[rb + q];
         __syncthreads();
         if (!live) continue;
         // pass 2: four rows per iteration, their products and bins are independent chains
@@ -172,11 +182,10 @@ __global__ void __launch_bounds__(TS * TS) mi_pass_kernel(MiArgs a) {
                 #pragma unroll
                 for (int u = 0; u < kU; ++u) {
                     int xb = (int)((xv[u] - xmin) * scale);
-                    xb = xb < 0 ? 0 : (xb >= a.bins ? a.bins - 1 : xb);
-                    slot[u] = xb * a.U + ys[r + u];
+                    slot[u] = xb < 0 ? 0 : (xb >= a.bins ? a.bins - 1 : xb);
                 }
                 #pragma unroll
-                for (int u = 0; u < kU; ++u) h[slot[u]] += 1;
+                for (int u = 0; u < kU; ++u) h[hidx(slot[u])] += 1;
             }
         }
         for (; r < rows; ++r) {
@@ -191,7 +200,7 @@ __global__ void __launch_bounds__(TS * TS) mi_pass_kernel(MiArgs a) {
             } else {
                 int xb = (int)((xv - xmin) * scale);
                 xb = xb < 0 ? 0 : (xb >= a.bins ? a.bins - 1 : xb);
-                h[xb * a.U + ys[r]] += 1;
+                h[hidx(xb)] += 1;
             }
         }
         if (PASS == 1) {
@@ -209,9 +218,38 @@ __global__ void __launch_bounds__(TS * TS) mi_pass_kernel(MiArgs a) {
             atomicMax(&mm[1], dkey(mx));
         }
     } else if (live) {
-        unsigned* g = a.hist + ((int64_t)t * kTilePairs + e) * (a.bins * a.U);
-        for (int c = 0; c < a.bins * a.U; ++c)
-            if (h[c]) atomicAdd(&g[c], (unsigned)h[c]);
+        unsigned* g = a.hist + ((int64_t)t * kTilePairs + e) * (a.bins * a.U) + sp.u;
+        for (int c = 0; c < a.bins; ++c)
+            if (h[hidx(c)]) atomicAdd(&g[c * a.U], (unsigned)h[hidx(c)]);
+    }
+}
+
+// Copy the feature columns with their rows grouped by y code: row r goes to the next free
+// slot of its class (cursor[u] starts at the class's first row).  Rows of one class land in
+// arbitrary order, which nothing downstream depends on (histograms and min / max are
+// order-free).  Each warp claims one contiguous run per class it holds, so the stores of a
+// warp fall into at most a few runs per column.
+__global__ void __launch_bounds__(256) class_scatter_kernel(const float* __restrict__ x, int64_t ld,
+                                                            int64_t f, int64_t n,
+                                                            const uint8_t* __restrict__ ycode,
+                                                            unsigned long long* cursor, float* xs,
+                                                            int64_t lds) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t base = warp * 32; base < n; base += warps * 32) {
+        const int64_t r = base + lane;
+        const bool in = r < n;
+        const unsigned active = __ballot_sync(0xffffffffu, in);
+        if (!in) continue;
+        const int code = ycode[r];
+        const unsigned same = __match_any_sync(active, code);
+        const int leader = __ffs(same) - 1;
+        unsigned long long first = 0;
+        if (lane == leader) first = atomicAdd(&cursor[code], (unsigned long long)__popc(same));
+        first = __shfl_sync(same, first, leader);
+        const int64_t dest = (int64_t)first + __popc(same & ((1u << lane) - 1u));
+        for (int64_t c = 0; c < f; ++c) xs[c * lds + dest] = x[c * ld + r];
     }
 }
 
@@ -345,9 +383,8 @@ __global__ void __launch_bounds__(256) mi_finish_kernel(MiFinishArgs a) {
 template <int TS, int PASS, bool CENTRED>
 cudaError_t launch_pass(const MiArgs& a, int splits, cudaStream_t stream) {
     using V = typename std::conditional<CENTRED, double, float>::type;
-    size_t smem = 2 * sizeof(V) * kMiRows * (TS + 1) + kMiRows;
-    smem = (smem + 15) / 16 * 16;
-    if (PASS == 2) smem += (size_t)TS * TS * a.hstride * sizeof(uint16_t);
+    size_t smem = 2 * sizeof(V) * kMiRows * (TS + 1);
+    if (PASS == 2) smem += (size_t)((TS * TS + 31) / 32) * a.hwords * 64 * sizeof(uint16_t);
     auto kern = mi_pass_kernel<TS, PASS, CENTRED>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -380,6 +417,7 @@ struct YBins {
     int* map;           // [256] compact code per bin, 255 when unused
     uint8_t* ycode;     // [n] compact code per row
     int U = 1, ready = 0;
+    unsigned hcounts[256];  // host copy of counts
 };
 
 cudaError_t prepare_ybins(Bucket& b, int bins, YBins& yb, cudaStream_t stream) {
@@ -404,6 +442,8 @@ cudaError_t prepare_ybins(Bucket& b, int bins, YBins& yb, cudaStream_t stream) {
     ymap_kernel<<<1, 1, 0, stream>>>(yb.counts, yb.ymm, bins, yb.map, meta);
     int hmeta[2] = {0, 0};
     e = cudaMemcpyAsync(hmeta, meta, sizeof(hmeta), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(yb.hcounts, yb.counts, sizeof(yb.hcounts), cudaMemcpyDeviceToHost, stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
     if (e != cudaSuccess) return e;
     yb.U = std::max(1, hmeta[0]);
@@ -420,80 +460,116 @@ cudaError_t launch_mi_scores(Bucket& b, const ColumnStats& cs, bool centred, int
     cudaError_t e = prepare_ybins(b, bins, yb, stream);
     if (e != cudaSuccess) return e;
     const int U = yb.U, ready = yb.ready;
-    if (bins * U > 768) return cudaErrorInvalidValue;  // joint histogram too large for shared memory
-    // per-pair min/max keys and the joint histograms live in their own buffers
-    size_t mm_bytes = (size_t)n_tiles * kTilePairs * 2 * sizeof(long long);
-    size_t hist_bytes = (size_t)n_tiles * kTilePairs * bins * U * sizeof(unsigned);
-    e = ensure(b.mi_mm, mm_bytes);
-    if (e == cudaSuccess) e = ensure(b.mi_hist, hist_bytes);
+    long long* mm = nullptr;
+    unsigned* hist = nullptr;
+    // tiles per batch: the joint histograms of one batch stay under 2 GiB
+    const size_t tile_bytes = (size_t)kTilePairs * (bins * U * sizeof(unsigned) + 2 * sizeof(long long));
+    const int batch = (int)std::max<size_t>(1, std::min<size_t>((size_t)n_tiles, ((size_t)2 << 30) / tile_bytes));
+    e = ensure(b.mi_mm, (size_t)batch * kTilePairs * 2 * sizeof(long long));
+    if (e == cudaSuccess) e = ensure(b.mi_hist, (size_t)batch * kTilePairs * bins * U * sizeof(unsigned));
     if (e != cudaSuccess) return e;
-    long long* mm = (long long*)b.mi_mm.ptr;
-    unsigned* hist = (unsigned*)b.mi_hist.ptr;
-    unsigned* counts = yb.counts;
-    int* map = yb.map;
-    uint8_t* ycode = yb.ycode;
-    const double* means = cs.d_col;
-    mm_init_kernel<<<2 * b.sm_count, 256, 0, stream>>>(mm, (int64_t)n_tiles * kTilePairs);
-    e = cudaMemsetAsync(hist, 0, hist_bytes, stream);
-    if (e != cudaSuccess) return e;
+    mm = (long long*)b.mi_mm.ptr;
+    hist = (unsigned*)b.mi_hist.ptr;
 
     MiArgs a;
-    a.x = b.d_data;
-    a.ld = b.ld;
-    a.n = b.n;
     a.f = b.f;
-    a.colstats = means;
-    a.tiles = d_tiles;
-    a.n_tiles = n_tiles;
+    a.colstats = cs.d_col;
     a.op = op;
     a.eps = div_eps;
     a.mm = mm;
-    a.ycode = ycode;
     a.bins = bins;
     a.U = U;
-    a.hstride = ((bins * U + 1) / 2) * 2;
-    if (((a.hstride / 2) & 1) == 0) a.hstride += 2;  // odd word stride: spreads banks
+    a.hwords = (bins + 1) / 2;
     a.hist = hist;
+    int n_splits = 0;
     if (ready) {
+        // rows per split: at most 32768 (16-bit counters), fewer while the grid would hold
+        // under 4 CTAs per SM
         int64_t per = std::min<int64_t>(kMiMaxSplitRows, (b.n + 1) / 2 + kMiRows);
         per = std::max<int64_t>(kMiRows, (per + kMiRows - 1) / kMiRows * kMiRows);
-        int splits = (int)((b.n + per - 1) / per);
-        // aim for >= 4 resident CTAs per SM across the grid
-        int64_t ctas = (int64_t)n_tiles * 16 * splits;
-        while (ctas < 4 * b.sm_count && per > 4 * kMiRows) {
+        auto count_splits = [&](int64_t p) {
+            int64_t s = 0;
+            for (int u = 0, c = 0; c < bins; ++c)
+                if (yb.hcounts[c]) { s += ((int64_t)yb.hcounts[c] + p - 1) / p; ++u; }
+            return s;
+        };
+        const int64_t ctas_per_split = (int64_t)std::min(batch, n_tiles) * 16;
+        while (count_splits(per) * ctas_per_split < 4 * b.sm_count && per > 4 * kMiRows)
             per = std::max<int64_t>(kMiRows, (per / 2 + kMiRows - 1) / kMiRows * kMiRows);
-            splits = (int)((b.n + per - 1) / per);
-            ctas = (int64_t)n_tiles * 16 * splits;
+        std::vector<MiSplit> host;
+        std::vector<unsigned long long> first;
+        int64_t off = 0;
+        for (int c = 0; c < bins; ++c) {
+            if (!yb.hcounts[c]) continue;
+            const int u = (int)first.size();
+            first.push_back((unsigned long long)off);
+            for (int64_t r = off; r < off + yb.hcounts[c]; r += per)
+                host.push_back(MiSplit{r, std::min<int64_t>(r + per, off + yb.hcounts[c]), u, 0});
+            off += yb.hcounts[c];
         }
-        a.rows_per_split = per;
-        const bool small = bins * U <= 192;
-        if (centred)
-            e = small ? run_passes<16, true>(a, splits, stream) : run_passes<8, true>(a, splits, stream);
-        else
-            e = small ? run_passes<16, false>(a, splits, stream) : run_passes<8, false>(a, splits, stream);
+        if (host.size() > 65535 || (int)first.size() != U || off != b.n) return cudaErrorInvalidValue;
+        n_splits = (int)host.size();
+        // cursor[256] | splits[n_splits]
+        e = ensure(b.mi_split, 256 * sizeof(unsigned long long) + host.size() * sizeof(MiSplit));
         if (e != cudaSuccess) return e;
+        unsigned long long* cursor = (unsigned long long*)b.mi_split.ptr;
+        MiSplit* d_splits = (MiSplit*)(cursor + 256);
+        const int64_t lds = (b.n + 31) / 32 * 32;
+        e = ensure(b.mi_xs, (size_t)b.f * lds * sizeof(float));
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(cursor, first.data(), first.size() * sizeof(unsigned long long),
+                                cudaMemcpyHostToDevice, stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(d_splits, host.data(), host.size() * sizeof(MiSplit), cudaMemcpyHostToDevice,
+                                stream);
+        if (e != cudaSuccess) return e;
+        {
+            KernelTimer timer(stream, GAFIME_KERNEL_MI_CLASS_COPY);
+            class_scatter_kernel<<<4 * b.sm_count, 256, 0, stream>>>(b.d_data, b.ld, b.f, b.n, yb.ycode, cursor,
+                                                                     (float*)b.mi_xs.ptr, lds);
+        }
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        a.xs = (const float*)b.mi_xs.ptr;
+        a.lds = lds;
+        a.splits = d_splits;
     }
 
     MiFinishArgs fa;
-    fa.tiles = d_tiles;
-    fa.n_tiles = n_tiles;
     fa.f = b.f;
     fa.n = b.n;
     fa.mm = mm;
     fa.hist = hist;
-    fa.ycounts = counts;
-    fa.map = map;
+    fa.ycounts = yb.counts;
+    fa.map = yb.map;
     fa.bins = bins;
     fa.U = U;
     fa.ready = ready;
     fa.k_pad = k_pad;
-    fa.cands = cands;
     fa.all_scores = all_scores;
-    size_t smem = sizeof(Cand) * kTilePairs;
-    cudaFuncSetAttribute(mi_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    KernelTimer timer(stream, GAFIME_KERNEL_MI_FINISH);
-    mi_finish_kernel<<<n_tiles, 256, smem, stream>>>(fa);
-    return cudaGetLastError();
+    const size_t fsmem = sizeof(Cand) * kTilePairs;
+    e = cudaFuncSetAttribute(mi_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fsmem);
+    if (e != cudaSuccess) return e;
+    for (int t0 = 0; t0 < n_tiles; t0 += batch) {
+        const int nt = std::min(batch, n_tiles - t0);
+        mm_init_kernel<<<2 * b.sm_count, 256, 0, stream>>>(mm, (int64_t)nt * kTilePairs);
+        e = cudaMemsetAsync(hist, 0, (size_t)nt * kTilePairs * bins * U * sizeof(unsigned), stream);
+        if (e != cudaSuccess) return e;
+        if (ready) {
+            a.tiles = d_tiles + t0;
+            a.n_tiles = nt;
+            e = centred ? run_passes<16, true>(a, n_splits, stream) : run_passes<16, false>(a, n_splits, stream);
+            if (e != cudaSuccess) return e;
+        }
+        fa.tiles = d_tiles + t0;
+        fa.n_tiles = nt;
+        fa.cands = cands ? cands + (int64_t)t0 * k_pad : nullptr;
+        KernelTimer timer(stream, GAFIME_KERNEL_MI_FINISH);
+        mi_finish_kernel<<<nt, 256, fsmem, stream>>>(fa);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 // ---- unary mutual information (one raw column against y) -------------------
@@ -527,14 +603,20 @@ __global__ void __launch_bounds__(256) unary_mm_kernel(const float* __restrict__
     }
 }
 
+// kShared: count in a shared-memory copy of the column's joint histogram, else straight
+// into global memory (joint histograms over 48K counters)
+template <bool kShared>
 __global__ void __launch_bounds__(256) unary_hist_kernel(const float* __restrict__ x, int64_t ld,
                                                          int64_t n, int64_t rps, const long long* mm,
                                                          const uint8_t* ycode, int bins, int U,
                                                          unsigned* hist) {
-    extern __shared__ unsigned h[];  // [bins * U]
+    extern __shared__ unsigned hsh[];  // [bins * U]
     const int c = blockIdx.x;
-    for (int q = threadIdx.x; q < bins * U; q += 256) h[q] = 0;
-    __syncthreads();
+    unsigned* h = kShared ? hsh : hist + (int64_t)c * bins * U;
+    if (kShared) {
+        for (int q = threadIdx.x; q < bins * U; q += 256) h[q] = 0;
+        __syncthreads();
+    }
     const double xmin = dval(mm[2 * c]), xmax = dval(mm[2 * c + 1]);
     if (xmax != xmin) {
         const double scale = (double)bins / (xmax - xmin);
@@ -545,6 +627,7 @@ __global__ void __launch_bounds__(256) unary_hist_kernel(const float* __restrict
             atomicAdd(&h[xb * U + ycode[r]], 1u);
         }
     }
+    if (!kShared) return;
     __syncthreads();
     for (int q = threadIdx.x; q < bins * U; q += 256)
         if (h[q]) atomicAdd(&hist[(int64_t)c * bins * U + q], h[q]);
@@ -599,10 +682,17 @@ cudaError_t launch_mi_unary(Bucket& b, int mi_bins, double* d_out, cudaStream_t 
         int64_t rps = (b.n + splits - 1) / splits;
         dim3 grid((unsigned)b.f, (unsigned)splits);
         unary_mm_kernel<<<grid, 256, 0, stream>>>(b.d_data, b.ld, b.n, rps, mm);
-        size_t smem = (size_t)bins * U * sizeof(unsigned);
-        cudaFuncSetAttribute(unary_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        unary_hist_kernel<<<grid, 256, smem, stream>>>(b.d_data, b.ld, b.n, rps, mm, yb.ycode, bins, U,
-                                                       hist);
+        const size_t smem = (size_t)bins * U * sizeof(unsigned);
+        if (smem <= 192 * 1024) {
+            e = cudaFuncSetAttribute(unary_hist_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem);
+            if (e != cudaSuccess) return e;
+            unary_hist_kernel<true><<<grid, 256, smem, stream>>>(b.d_data, b.ld, b.n, rps, mm, yb.ycode, bins,
+                                                                 U, hist);
+        } else {
+            unary_hist_kernel<false><<<grid, 256, 0, stream>>>(b.d_data, b.ld, b.n, rps, mm, yb.ycode, bins, U,
+                                                               hist);
+        }
     }
     unary_finish_kernel<<<(unsigned)((b.f + 127) / 128), 128, 0, stream>>>(
         b.f, b.n, mm, hist, yb.counts, yb.map, bins, U, yb.ready, d_out);

@@ -281,6 +281,7 @@ int gafime_topk_merge(const int32_t* cand_i, const int32_t* cand_j, const double
 #define GAFIME_KERNEL_GRAM_TC 10
 #define GAFIME_KERNEL_GRAM_PREP 11
 #define GAFIME_KERNEL_GRAM_REDUCE 12
+#define GAFIME_KERNEL_MI_CLASS_COPY 13
 
 /* NEW.  enable = 1: drop any previous records, then bracket every engine kernel
  * launch with CUDA events on its stream.  enable = 0: stop recording (the records

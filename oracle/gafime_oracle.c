@@ -274,6 +274,94 @@ int gafime_oracle_centred_scores(const float* X, int64_t ld, const float* y, int
     return status;
 }
 
+/* Mutual information of x = a op b for pairs (i, j), binned as gafime_core does
+ * (y bins: build_bins, gafime_core.cpp:200-226; x bins and MI:
+ * mutual_info_from_vector, gafime_core.cpp:267-333).
+ *   center = 0: x = fl32(a op b), the kernel-API interaction (cpu_backend.cpp:87-103);
+ *   center = 1: x = (a - mean_a) op (b - mean_b) in fp64 with fp64 column means in serial
+ *               row order (gafime_core.cpp:134-150); for multiply this is the reference's
+ *               centred product (gafime_core.cpp:571-577), the other operators extend it
+ *               with the same divide rule as combine_cpu (copysign clamp at eps). */
+int gafime_oracle_pair_mi(const float* X, int64_t ld, const float* y, int64_t n, int64_t f_count,
+                          const int32_t* pi, const int32_t* pj, int64_t n_pairs, int op, float eps,
+                          int center, int mi_bins, double* out_mi) {
+    double* means = (double*)malloc((size_t)(f_count > 0 ? f_count : 1) * sizeof(double));
+    double* yd = (double*)malloc((size_t)(n > 0 ? n : 1) * sizeof(double));
+    int32_t* y_bins = (int32_t*)malloc((size_t)(n > 0 ? n : 1) * sizeof(int32_t));
+    if (!means || !yd || !y_bins) {
+        free(means); free(yd); free(y_bins);
+        return -3;
+    }
+    if (center) gafime_oracle_column_means(X, ld, n, f_count, means);
+    for (int64_t r = 0; r < n; ++r) yd[r] = (double)y[r];
+    const int ready = or_build_bins(yd, n, mi_bins, y_bins);
+    int status = 0;
+#pragma omp parallel
+    {
+        double* inter = (double*)malloc((size_t)(n > 0 ? n : 1) * sizeof(double));
+        size_t nb = mi_bins >= 2 ? (size_t)mi_bins : 2;
+        double* joint = (double*)malloc(nb * nb * sizeof(double));
+        double* p_x = (double*)malloc(nb * sizeof(double));
+        double* p_y = (double*)malloc(nb * sizeof(double));
+        if (!inter || !joint || !p_x || !p_y) {
+#pragma omp atomic write
+            status = -3;
+        } else {
+#pragma omp for schedule(dynamic, 8)
+            for (int64_t p = 0; p < n_pairs; ++p) {
+                const float* ca = X + (int64_t)pi[p] * ld;
+                const float* cb = X + (int64_t)pj[p] * ld;
+                for (int64_t r = 0; r < n; ++r) {
+                    if (center) {
+                        double a = (double)ca[r] - means[pi[p]], b = (double)cb[r] - means[pj[p]];
+                        double v;
+                        switch (op) {
+                            case OR_ADD: v = a + b; break;
+                            case OR_SUB: v = a - b; break;
+                            case OR_DIV: v = a / (fabs(b) < (double)eps ? copysign((double)eps, b) : b); break;
+                            default: v = a * b;
+                        }
+                        inter[r] = v;
+                    } else {
+                        inter[r] = (double)or_combine(ca[r], cb[r], op, eps);
+                    }
+                }
+                out_mi[p] = ready ? or_mutual_info(inter, n, mi_bins, y_bins, joint, p_x, p_y) : 0.0;
+            }
+        }
+        free(inter); free(joint); free(p_x); free(p_y);
+    }
+    free(means); free(yd); free(y_bins);
+    return status;
+}
+
+/* Mutual information of each raw column against y: a one-feature combo of
+ * gafime_core.score_combos scores the column's own values (gafime_core.cpp:558-568),
+ * binned by mutual_info_from_vector (gafime_core.cpp:267-333). */
+int gafime_oracle_unary_mi(const float* X, int64_t ld, const float* y, int64_t n, int64_t f_count,
+                           int mi_bins, double* out_mi) {
+    double* yd = (double*)malloc((size_t)(n > 0 ? n : 1) * sizeof(double));
+    double* xd = (double*)malloc((size_t)(n > 0 ? n : 1) * sizeof(double));
+    int32_t* y_bins = (int32_t*)malloc((size_t)(n > 0 ? n : 1) * sizeof(int32_t));
+    size_t nb = mi_bins >= 2 ? (size_t)mi_bins : 2;
+    double* joint = (double*)malloc(nb * nb * sizeof(double));
+    double* p_x = (double*)malloc(nb * sizeof(double));
+    double* p_y = (double*)malloc(nb * sizeof(double));
+    int status = 0;
+    if (!yd || !xd || !y_bins || !joint || !p_x || !p_y) {
+        status = -3;
+    } else {
+        for (int64_t r = 0; r < n; ++r) yd[r] = (double)y[r];
+        const int ready = or_build_bins(yd, n, mi_bins, y_bins);
+        for (int64_t c = 0; c < f_count; ++c) {
+            for (int64_t r = 0; r < n; ++r) xd[r] = (double)X[c * ld + r];
+            out_mi[c] = ready ? or_mutual_info(xd, n, mi_bins, y_bins, joint, p_x, p_y) : 0.0;
+        }
+    }
+    free(yd); free(xd); free(y_bins); free(joint); free(p_x); free(p_y);
+    return status;
+}
+
 /* Interaction materialiser, src/cuda/kernels.cu:1646-1676 (row-major X and out). */
 void gafime_oracle_feature_interaction(const float* X, const float* means, float* out,
                                        const int32_t* idx, const int32_t* off, int32_t n,

@@ -57,6 +57,13 @@ def lib() -> ctypes.CDLL:
             _f32p, ctypes.c_int64, _f32p, ctypes.c_int64, ctypes.c_int64, _i32p, _i32p,
             ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
         _LIB.gafime_oracle_centred_scores.restype = ctypes.c_int
+        _LIB.gafime_oracle_pair_mi.argtypes = [
+            _f32p, ctypes.c_int64, _f32p, ctypes.c_int64, ctypes.c_int64, _i32p, _i32p,
+            ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int, _f64p]
+        _LIB.gafime_oracle_pair_mi.restype = ctypes.c_int
+        _LIB.gafime_oracle_unary_mi.argtypes = [
+            _f32p, ctypes.c_int64, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, _f64p]
+        _LIB.gafime_oracle_unary_mi.restype = ctypes.c_int
         _LIB.gafime_oracle_pair_moments.argtypes = [
             _f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, _f64p]
         _LIB.gafime_oracle_pair_moments.restype = None
@@ -117,6 +124,35 @@ def centred_scores(X: np.ndarray, y: np.ndarray, pi=None, pj=None, pearson: bool
     if rc != 0:
         raise MemoryError("oracle allocation failed")
     return out_p, out_m
+
+
+def pair_mi(X: np.ndarray, y: np.ndarray, op: str = "multiply", center: bool = True,
+            mi_bins: int = 16, div_eps: float = 1e-8, pi=None, pj=None) -> np.ndarray:
+    """Binned mutual information of x = X[:, i] op X[:, j] (centred in fp64, or the fp32
+    kernel-API interaction when center is False) against y for each pair."""
+    flat, ld, n, f = _colmajor(X)
+    if pi is None:
+        pi, pj = all_pairs(f)
+    pi = np.ascontiguousarray(pi, dtype=np.int32)
+    pj = np.ascontiguousarray(pj, dtype=np.int32)
+    yv = np.ascontiguousarray(y, dtype=np.float32)
+    out = np.empty(len(pi), dtype=np.float64)
+    rc = lib().gafime_oracle_pair_mi(flat, ld, yv, n, f, pi, pj, len(pi), OP_IDS[op],
+                                     np.float32(div_eps), int(center), int(mi_bins), out)
+    if rc != 0:
+        raise MemoryError("oracle allocation failed")
+    return out
+
+
+def unary_mi(X: np.ndarray, y: np.ndarray, mi_bins: int = 16) -> np.ndarray:
+    """Binned mutual information of every raw column against y."""
+    flat, ld, n, f = _colmajor(X)
+    out = np.empty(f, dtype=np.float64)
+    rc = lib().gafime_oracle_unary_mi(flat, ld, np.ascontiguousarray(y, dtype=np.float32), n, f,
+                                      int(mi_bins), out)
+    if rc != 0:
+        raise MemoryError("oracle allocation failed")
+    return out
 
 
 def topk(scores: np.ndarray, pi: np.ndarray, pj: np.ndarray, k: int, absolute: bool = True):

@@ -285,6 +285,39 @@ def main():
     np.savez_compressed(os.path.join(HERE, "chains.npz"), X=Xc, y=yc, mask=maskc, val_fold=np.array(2),
                         chain_feats=cf, chain_ops=co, chain_inter=ci, chain_stats=chain_stats,
                         fused_feats=ff_, fused_ops=fo, fused_type=fi[:, 0], fused_stats=fused_stats)
+    # --- raw-operator interactions scored by the reference's numpy MI -------------------
+    # x = fl32(a op b) as combine_cpu forms it (cpu_backend.cpp:87-103, divide clamp at
+    # 1e-8 with copysign), scored by gafime/metrics/cpu_metrics.py:46-61 against a 3-class
+    # and a continuous target.
+    from gafime.metrics import cpu_metrics
+    rng = np.random.default_rng(11)
+    Xr = np.hstack([rng.standard_normal((3000, 6)), rng.lognormal(0, 0.7, (3000, 6))]).astype(np.float32)
+    y3 = (rng.integers(0, 3, 3000)).astype(np.float32)
+    yc = (Xr[:, 1].astype(np.float64) * Xr[:, 7] + rng.standard_normal(3000)).astype(np.float32)
+    pi, pj = np.triu_indices(Xr.shape[1], k=1)
+    eps = np.float32(1e-8)
+    raw_mi = np.zeros((2, 4, len(pi)))
+    for t, yv in enumerate((y3, yc)):
+        for o in range(4):
+            for p, (a, b) in enumerate(zip(pi, pj)):
+                xa, xb = Xr[:, a], Xr[:, b]
+                if o == 0:
+                    v = xa * xb
+                elif o == 1:
+                    v = xa + xb
+                elif o == 2:
+                    v = xa - xb
+                else:
+                    v = xa / np.where(np.abs(xb) < eps, np.copysign(eps, xb), xb)
+                raw_mi[t, o, p] = cpu_metrics.mutual_info(v.astype(np.float64), yv.astype(np.float64), bins=16)
+    # one-feature combos: gafime_core scores the raw column (gafime_core.cpp:558-568)
+    uidx, uoff = core.pack_combos([(int(c),) for c in range(Xr.shape[1])])
+    unary_mi = np.stack([np.asarray(core.score_combos(np.ascontiguousarray(Xr, dtype=np.float64),
+                                                      np.ascontiguousarray(yv, dtype=np.float64),
+                                                      uidx, uoff, ["mutual_info"], 16))[:, 0]
+                         for yv in (y3, yc)])
+    np.savez_compressed(os.path.join(HERE, "raw_mi.npz"), X=Xr, y3=y3, yc=yc, bins=np.array(16), mi=raw_mi,
+                        unary_mi=unary_mi)
     print("wrote fixtures to", HERE)
 
 

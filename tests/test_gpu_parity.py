@@ -80,6 +80,71 @@ def test_mi_3class_matches_gafime_core(native, golden, bins, key, col):
     assert_topk_equivalent(top[0], top[1], want, pi, pj, 10, rtol=0, atol=1e-5)
 
 
+@pytest.mark.parametrize("target", ["y3", "yc"])
+@pytest.mark.parametrize("center", [False, True])
+@pytest.mark.parametrize("op", OPS)
+def test_mi_all_ops_match_oracle(native, golden, oracle, op, center, target):
+    """MI of every operator, raw (fp32 interaction) and centred (fp64), 3-class and
+    continuous targets: 1e-5 absolute against the oracle; the raw interactions also
+    against the reference's numpy MI of the same fp32 columns."""
+    g = golden("raw_mi.npz")
+    X, y = g["X"], g[target]
+    want = oracle.pair_mi(X, y, op, center=center, mi_bins=16, div_eps=1e-8)
+    with bucket_for(native, X, y) as b:
+        got = b.scores(op, metric="mutual_info", center=center, div_eps=1e-8, mi_bins=16)
+        top = b.topk([op], 10, metric="mutual_info", center=center, div_eps=1e-8, mi_bins=16)[op]
+    np.testing.assert_allclose(got, want, rtol=0, atol=1e-5)
+    if not center:
+        np.testing.assert_allclose(got, g["mi"][0 if target == "y3" else 1, OPS.index(op)], rtol=0, atol=1e-5)
+    pi, pj = np.triu_indices(X.shape[1], k=1)
+    assert_topk_equivalent(top[0], top[1], want, pi, pj, 10, rtol=0, atol=1e-5)
+
+
+@pytest.mark.parametrize("bins,n,f", [(64, 4000, 70), (255, 6000, 130)])
+def test_mi_many_target_bins(native, oracle, bins, n, f):
+    """A continuous target fills most of its bins: joint histograms of bins x U counters
+    well past what fits in shared memory (U ~ bins), and at 255 bins more than one batch
+    of tiles."""
+    rng = np.random.default_rng(bins)
+    X = rng.standard_normal((n, f)).astype(np.float32)
+    y = (X[:, 2].astype(np.float64) * X[:, 5] + 0.5 * rng.standard_normal(n)).astype(np.float32)
+    want = oracle.pair_mi(X, y, "multiply", center=True, mi_bins=bins)
+    with bucket_for(native, X, y) as b:
+        got = b.scores("multiply", metric="mutual_info", center=True, mi_bins=bins)
+    np.testing.assert_allclose(got, want, rtol=0, atol=1e-5)
+
+
+@pytest.mark.parametrize("target", ["y3", "yc"])
+def test_unary_mi_matches_gafime_core(native, golden, oracle, target):
+    g = golden("raw_mi.npz")
+    with bucket_for(native, g["X"], g[target]) as b:
+        got = b.unary_scores("mutual_info", mi_bins=16)
+    np.testing.assert_allclose(got, g["unary_mi"][0 if target == "y3" else 1], rtol=0, atol=1e-5)
+
+
+def test_unary_mi_joint_histogram_past_shared_memory(native, oracle):
+    """255 x 255 bins of a uniform target: the joint histogram (260 KB) is counted in
+    global memory."""
+    rng = np.random.default_rng(3)
+    X = rng.standard_normal((60000, 5)).astype(np.float32)
+    y = rng.random(60000).astype(np.float32)
+    with bucket_for(native, X, y) as b:
+        got = b.unary_scores("mutual_info", mi_bins=255)
+    np.testing.assert_allclose(got, oracle.unary_mi(X, y, mi_bins=255), rtol=0, atol=1e-5)
+
+
+@pytest.mark.parametrize("n,f", [(33, 5), (257, 64), (1000, 70), (1, 3), (2, 2), (70001, 6)])
+def test_mi_ragged_shapes(native, oracle, n, f):
+    rng = np.random.default_rng(n + 7 * f)
+    X = rng.standard_normal((n, f)).astype(np.float32)
+    y = (rng.random(n) < 0.3).astype(np.float32)
+    with bucket_for(native, X, y) as b:
+        for op, center in (("multiply", True), ("add", False), ("divide", False)):
+            want = oracle.pair_mi(X, y, op, center=center, mi_bins=16, div_eps=1e-6)
+            got = b.scores(op, metric="mutual_info", center=center, div_eps=1e-6, mi_bins=16)
+            np.testing.assert_allclose(got, want, rtol=0, atol=1e-5)
+
+
 @pytest.mark.parametrize("op", OPS)
 def test_raw_ops_match_oracle_and_reference_stats(native, golden, oracle, op):
     g = golden("raw_ops.npz")

@@ -118,3 +118,29 @@ def test_chain_stats_match_reference_cpu(golden, oracle):
         inter = [int(g["fused_type"][q])] * (len(feats) - 1)
         st = oracle.chain_stats([X[:, c] for c in feats], y, mask, ops, inter, vf)
         np.testing.assert_array_equal(st.astype(np.float32), g["fused_stats"][q])
+
+
+def test_pair_mi_centred_multiply_equals_gafime_core(golden, oracle):
+    g = golden("mi_3class.npz")
+    for bins, key, col in ((32, "core_b32", 1), (16, "core_b16", 0)):
+        m = oracle.pair_mi(g["X"], g["y"], "multiply", center=True, mi_bins=bins)
+        np.testing.assert_array_equal(m, g[key][:, col])
+
+
+@pytest.mark.parametrize("target", ["y3", "yc"])
+@pytest.mark.parametrize("op_id,op", list(enumerate(OPS)))
+def test_pair_mi_raw_ops_match_reference_numpy_mi(golden, oracle, target, op_id, op):
+    """fp32 interactions binned with gafime_core's rule vs the reference's numpy metric
+    (np.histogram2d): the bin rules agree except for values within rounding of an
+    interior edge, which this data does not hold."""
+    g = golden("raw_mi.npz")
+    t = 0 if target == "y3" else 1
+    m = oracle.pair_mi(g["X"], g[target], op, center=False, mi_bins=int(g["bins"]), div_eps=1e-8)
+    np.testing.assert_allclose(m, g["mi"][t, op_id], rtol=0, atol=1e-12)
+
+
+@pytest.mark.parametrize("target", ["y3", "yc"])
+def test_unary_mi_matches_gafime_core(golden, oracle, target):
+    g = golden("raw_mi.npz")
+    m = oracle.unary_mi(g["X"], g[target], mi_bins=int(g["bins"]))
+    np.testing.assert_array_equal(m, g["unary_mi"][0 if target == "y3" else 1])
