@@ -47,6 +47,7 @@ EXPORTED = (
     "gafime_bucket_compute_batch", "gafime_interleaved_compute", "gafime_fused_interaction",
     "gafime_pipeline_init", "gafime_pipeline_submit", "gafime_pipeline_poll", "gafime_pipeline_wait",
     "gafime_pipeline_pending", "gafime_pipeline_flush", "gafime_pipeline_free", "gafime_pearson_cuda",
+    "gafime_contiguous_bucket_upload_target", "gafime_contiguous_bucket_gather",
 )
 
 # kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
@@ -89,6 +90,8 @@ def _bind(lib: ctypes.CDLL) -> None:
         "gafime_profile_enable": ([_i], _i),
         "gafime_profile_read": ([_i, ctypes.POINTER(ctypes.c_double), _ip], _i),
         "gafime_contiguous_bucket_stream": ([_vp, ctypes.POINTER(_vp)], _i),
+        "gafime_contiguous_bucket_upload_target": ([_vp, _vp], _i),
+        "gafime_contiguous_bucket_gather": ([_vp, _vp, _vp, ctypes.c_int32, _vp, _i64], _i),
         "gafime_allpairs_scores_noalloc": ([_vp, _i64, _vp, _i, _i, _i, _f, _vp, _vp], _i),
         "gafime_unary_scores": ([_vp, _i, _i, _vp], _i),
         "gafime_shard_tiles": ([_i, _i, _i, _vp, _i, _ip], _i),
@@ -177,6 +180,7 @@ class Bucket:
         self.lib = load()
         if device is not None:
             select_device(device)
+        self.device = device
         self.n = int(n_samples)
         self.f = int(n_features)
         h = ctypes.c_void_p(0)
@@ -196,6 +200,30 @@ class Bucket:
 
     def upload(self, X: np.ndarray, y: np.ndarray, mask: Optional[np.ndarray] = None) -> None:
         self.upload_packed(pack_columns(X, y), mask)
+
+    def set_target(self, y: np.ndarray) -> None:
+        """Replace only the target (n floats); the features stay resident."""
+        yv = np.ascontiguousarray(y, dtype=np.float32)
+        if yv.shape != (self.n,):
+            raise ValueError(f"target must hold {self.n} values")
+        check("gafime_contiguous_bucket_upload_target",
+              self.lib.gafime_contiguous_bucket_upload_target(self.handle, _ptr(yv)))
+
+    @classmethod
+    def gather(cls, src: "Bucket", cols: Sequence[int], rows: Optional[np.ndarray] = None) -> "Bucket":
+        """A new bucket of src's columns `cols` and rows `rows` (all rows when None), filled
+        on the device from src's resident data."""
+        c = np.ascontiguousarray(cols, dtype=np.int32)
+        r = None if rows is None else np.ascontiguousarray(rows, dtype=np.int64)
+        n = src.n if r is None else len(r)
+        dst = cls(n, len(c), device=src.device)
+        try:
+            check("gafime_contiguous_bucket_gather", dst.lib.gafime_contiguous_bucket_gather(
+                dst.handle, src.handle, _ptr(c), len(c), None if r is None else _ptr(r), n))
+        except Exception:
+            dst.free()
+            raise
+        return dst
 
     # -- scoring ------------------------------------------------------------------
     def compute_pair(self, a: int, b: int, op_a: int = 0, op_b: int = 0, interact: int = 0,

@@ -4,6 +4,10 @@ Mirrors NativeCudaBackend (gafime/backends/native_cuda_backend.py:24-468) but re
 per-pair loop (one launch + sync per pair, :368-379) with one all-pairs call over the
 features the combo list touches, and scores unaries on the GPU too (the reference used
 numpy for them, :383-404).  There is no CPU fallback: a failure raises.
+
+The matrix is uploaded once per array (the reference re-uploads matrix and target for
+every call, :339-352).  Column subsets and bootstrap resamples are gathered from it on the
+device, and a new target (permutation tests) replaces only the target column.
 """
 from __future__ import annotations
 
@@ -36,8 +40,8 @@ class NativeCudaBackend(Backend):
         self._memory_mb = info["memory_mb"]
         self._cc = info["compute_capability"]
         self.device_label = f"cuda:{self.device_id}"
-        # one resident bucket, reused while the same arrays and columns are scored
-        self._cache: Optional[Tuple[object, object, Tuple[int, ...], _native.Bucket]] = None
+        # the matrix last scored, resident on the device with its column-subset buckets
+        self._cache: Optional[_Resident] = None
 
     @classmethod
     def from_config(cls, config: EngineConfig) -> "NativeCudaBackend":
@@ -60,20 +64,17 @@ class NativeCudaBackend(Backend):
         return True, warnings
 
     # -- buckets ------------------------------------------------------------------
-    def _bucket(self, X: np.ndarray, y: np.ndarray, cols: Tuple[int, ...]) -> _native.Bucket:
-        c = self._cache
-        if c is not None and c[0] is X and c[1] is y and c[2] == cols:
-            return c[3]
+    def _resident(self, X: np.ndarray, y: np.ndarray) -> "_Resident":
+        r = self._cache
+        if r is not None and r.X is X:
+            return r
         self.release()
-        sub = X[:, list(cols)] if len(cols) != X.shape[1] or list(cols) != list(range(X.shape[1])) else X
-        b = _native.Bucket(X.shape[0], len(cols), device=self.device_id)
-        b.upload(np.asarray(sub, dtype=np.float32), np.asarray(y, dtype=np.float32))
-        self._cache = (X, y, cols, b)
-        return b
+        self._cache = _Resident(X, y, self.device_id)
+        return self._cache
 
     def release(self) -> None:
         if self._cache is not None:
-            self._cache[3].free()
+            self._cache.free()
             self._cache = None
 
     def __del__(self):
@@ -85,6 +86,22 @@ class NativeCudaBackend(Backend):
     # -- scoring ------------------------------------------------------------------
     def score_combos(self, X, y, combos: Iterable[Tuple[int, ...]], metric_suite: MetricSuite
                      ) -> Dict[Tuple[int, ...], Dict[str, float]]:
+        X = np.asarray(X)
+        y = np.asarray(y)
+        res = self._resident(X, y)
+        return self._score(lambda cols: (res.bucket(cols, y), False), combos, metric_suite)
+
+    def score_resampled(self, X, y, rows, combos: Iterable[Tuple[int, ...]], metric_suite: MetricSuite
+                        ) -> Dict[Tuple[int, ...], Dict[str, float]]:
+        """score_combos(X[rows], y[rows], ...) with the rows gathered on the device from the
+        resident matrix (bootstrap stability)."""
+        X = np.asarray(X)
+        y = np.asarray(y)
+        res = self._resident(X, y)
+        rows = np.asarray(rows, dtype=np.int64)
+        return self._score(lambda cols: (res.gather(cols, y, rows), True), combos, metric_suite)
+
+    def _score(self, bucket_for, combos, metric_suite: MetricSuite):
         combos_list = list(combos)
         if not combos_list:
             return {}
@@ -93,67 +110,71 @@ class NativeCudaBackend(Backend):
                 raise NotImplementedError(f"metric {m!r} is not on the GPU scoring path")
         if any(len(c) > 2 for c in combos_list):
             raise NotImplementedError("combos of more than two features are not on the GPU path")
-        X = np.asarray(X)
-        y = np.asarray(y)
         out: Dict[Tuple[int, ...], Dict[str, float]] = {c: {} for c in combos_list}
         unaries = [c for c in combos_list if len(c) == 1]
         pairs = [c for c in combos_list if len(c) == 2]
         if unaries:
             cols = tuple(sorted({c[0] for c in unaries}))
             pos = {f: i for i, f in enumerate(cols)}
-            b = self._bucket(X, y, cols)
-            cache = {}
-            for m in metric_suite.metric_names:
-                base = "pearson" if m in ("pearson", "r2") else "mutual_info"
-                if base not in cache:
-                    cache[base] = b.unary_scores(base, metric_suite.mi_bins)
-                v = cache[base]
-                for c in unaries:
-                    s = float(v[pos[c[0]]])
-                    out[c][m] = s * s if m == "r2" else s
+            b, temp = bucket_for(cols)
+            try:
+                cache = {}
+                for m in metric_suite.metric_names:
+                    base = "pearson" if m in ("pearson", "r2") else "mutual_info"
+                    if base not in cache:
+                        cache[base] = b.unary_scores(base, metric_suite.mi_bins)
+                    v = cache[base]
+                    for c in unaries:
+                        s = float(v[pos[c[0]]])
+                        out[c][m] = s * s if m == "r2" else s
+            finally:
+                if temp:
+                    b.free()
         if pairs:
             cols = tuple(sorted({i for c in pairs for i in c}))
             pos = {f: i for i, f in enumerate(cols)}
-            b = self._bucket(X, y, cols)
             f = len(cols)
             need_reverse = self.operator == "divide" and any(pos[a] > pos[c] for a, c in pairs)
-            cache = {}
-            for m in metric_suite.metric_names:
-                base = "pearson" if m in ("pearson", "r2") else "mutual_info"
-                if base not in cache:
-                    cache[base] = b.scores(self.operator, metric=base, center=self.center,
-                                           div_eps=self.div_eps, mi_bins=metric_suite.mi_bins)
-                v = cache[base]
-                rev = None
-                if need_reverse:
-                    rev = self._reverse_divide_scores(X, y, cols, base, metric_suite.mi_bins)
-                for a, c in pairs:
-                    i, j = pos[a], pos[c]
-                    if i < j:
-                        s = float(v[_tri(i, j, f)])
-                    elif self.operator == "divide":
-                        # x_a / x_c with a after c: from the column-reversed bucket
-                        s = float(rev[_tri(f - 1 - i, f - 1 - j, f)])
-                    else:
-                        s = float(v[_tri(j, i, f)])
-                        if self.operator == "subtract" and base == "pearson":
-                            s = -s  # x_a - x_c = -(x_c - x_a)
-                    out[(a, c)][m] = s * s if m == "r2" else s
+            b, temp = bucket_for(cols)
+            rb, rtemp = bucket_for(tuple(reversed(cols))) if need_reverse else (None, False)
+            try:
+                cache = {}
+                for m in metric_suite.metric_names:
+                    base = "pearson" if m in ("pearson", "r2") else "mutual_info"
+                    if base not in cache:
+                        cache[base] = b.scores(self.operator, metric=base, center=self.center,
+                                               div_eps=self.div_eps, mi_bins=metric_suite.mi_bins)
+                        if need_reverse:
+                            # x_a / x_c with a after c: from the column-reversed bucket
+                            cache[base + "/rev"] = rb.scores("divide", metric=base, center=self.center,
+                                                             div_eps=self.div_eps,
+                                                             mi_bins=metric_suite.mi_bins)
+                    v = cache[base]
+                    rev = cache.get(base + "/rev")
+                    for a, c in pairs:
+                        i, j = pos[a], pos[c]
+                        if i < j:
+                            s = float(v[_tri(i, j, f)])
+                        elif self.operator == "divide":
+                            s = float(rev[_tri(f - 1 - i, f - 1 - j, f)])
+                        else:
+                            s = float(v[_tri(j, i, f)])
+                            if self.operator == "subtract" and base == "pearson":
+                                s = -s  # x_a - x_c = -(x_c - x_a)
+                        out[(a, c)][m] = s * s if m == "r2" else s
+            finally:
+                if temp:
+                    b.free()
+                if rtemp:
+                    rb.free()
         return out
-
-    def _reverse_divide_scores(self, X, y, cols, base, bins):
-        rcols = tuple(reversed(cols))
-        sub = np.asarray(X[:, list(rcols)], dtype=np.float32)
-        with _native.Bucket(X.shape[0], len(rcols), device=self.device_id) as b:
-            b.upload(sub, np.asarray(y, dtype=np.float32))
-            return b.scores("divide", metric=base, center=self.center, div_eps=self.div_eps,
-                            mi_bins=bins)
 
     def top_pairs(self, X, y, k: int, metric: str = "pearson", mi_bins: int = 16,
                   ops: Sequence[str] = ()) -> Dict[str, Tuple[np.ndarray, np.ndarray, np.ndarray]]:
         """The k best pairs i<j of all columns per operator, without materialising every score."""
-        cols = tuple(range(np.shape(X)[1]))
-        b = self._bucket(np.asarray(X), np.asarray(y), cols)
+        X = np.asarray(X)
+        y = np.asarray(y)
+        b = self._resident(X, y).bucket(tuple(range(X.shape[1])), y)
         return b.topk(list(ops) or [self.operator], k, metric=metric, center=self.center,
                       div_eps=self.div_eps, mi_bins=mi_bins)
 
@@ -161,3 +182,57 @@ class NativeCudaBackend(Backend):
 def _tri(i: int, j: int, f: int) -> int:
     """Row-major upper-triangle index of pair (i, j), i < j."""
     return i * f - i * (i + 1) // 2 + (j - i - 1)
+
+
+class _Resident:
+    """One host matrix uploaded once (all columns + the target it came with), and buckets
+    of column subsets gathered from it on the device.  Each bucket remembers which target
+    array it holds; a different one replaces only the target column."""
+
+    max_subsets = 4
+
+    def __init__(self, X: np.ndarray, y: np.ndarray, device: int) -> None:
+        self.X = X
+        n, f = X.shape
+        self.all_cols = tuple(range(f))
+        self.full = _native.Bucket(n, f, device=device)
+        try:
+            self.full.upload(X, y)
+        except Exception:
+            self.full.free()
+            raise
+        self.y_of = {id(self.full): y}
+        self.subsets: Dict[Tuple[int, ...], _native.Bucket] = {}
+
+    def _with_target(self, b: _native.Bucket, y: np.ndarray) -> _native.Bucket:
+        if self.y_of.get(id(b)) is not y:
+            b.set_target(y)
+            self.y_of[id(b)] = y
+        return b
+
+    def bucket(self, cols: Tuple[int, ...], y: np.ndarray) -> _native.Bucket:
+        if cols == self.all_cols:
+            return self._with_target(self.full, y)
+        b = self.subsets.pop(cols, None)
+        if b is None:
+            self._with_target(self.full, y)
+            b = _native.Bucket.gather(self.full, cols)
+            self.y_of[id(b)] = y
+            while len(self.subsets) >= self.max_subsets:
+                old = self.subsets.pop(next(iter(self.subsets)))
+                self.y_of.pop(id(old), None)
+                old.free()
+        self.subsets[cols] = b  # most recently used last
+        return self._with_target(b, y)
+
+    def gather(self, cols: Tuple[int, ...], y: np.ndarray, rows: np.ndarray) -> _native.Bucket:
+        """A temporary bucket of rows `rows` of columns `cols` (and of the target y)."""
+        self._with_target(self.full, y)
+        return _native.Bucket.gather(self.full, cols, rows)
+
+    def free(self) -> None:
+        for b in self.subsets.values():
+            b.free()
+        self.subsets.clear()
+        self.full.free()
+        self.y_of.clear()

@@ -356,6 +356,26 @@ int check_finite(Bucket& b, bool* all_finite) {
     return GAFIME_SUCCESS;
 }
 
+// Rows [0, n) of dst's column c are src column scol[c] at rows rows[r] (identity when rows is
+// null); pad rows of dst stay zero.  blockIdx.y strides over dst's columns (features, then
+// the target), blockIdx.x over rows.
+__global__ void gather_rows_kernel(const float* __restrict__ src, int64_t src_ld, const int32_t* __restrict__ scol,
+                                   int64_t n_cols, const int64_t* __restrict__ rows, int64_t n,
+                                   float* __restrict__ dst, int64_t dst_ld) {
+    for (int64_t c = blockIdx.y; c < n_cols; c += gridDim.y) {
+        const float* s = src + (int64_t)scol[c] * src_ld;
+        float* d = dst + c * dst_ld;
+        for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x)
+            d[r] = s[rows ? rows[r] : r];
+    }
+}
+
+__global__ void gather_mask_kernel(const uint8_t* __restrict__ src, const int64_t* __restrict__ rows, int64_t n,
+                                   uint8_t* __restrict__ dst) {
+    for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x)
+        dst[r] = src[rows ? rows[r] : r];
+}
+
 }  // namespace gafime
 
 using namespace gafime;
@@ -477,6 +497,83 @@ int gafime_contiguous_bucket_upload(ContiguousBucket bucket, const float* h_data
     return check_finite(*b, &finite);
 }
 
+int gafime_contiguous_bucket_upload_target(ContiguousBucket bucket, const float* h_y) {
+    if (!bucket || !h_y) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket* b = (Bucket*)bucket;
+    cudaSetDevice(b->device);
+    float* y = b->d_data + b->f * b->ld;
+    cudaError_t e = cudaMemcpyAsync(y, h_y, (size_t)b->n * sizeof(float), cudaMemcpyHostToDevice, b->stream);
+    if (e != cudaSuccess) return status_from(e);
+    // features already known finite: only the new target needs the check
+    const int features_finite = b->finite_state;
+    b->finite_state = -1;
+    if (features_finite != 1) {
+        bool finite = true;
+        return check_finite(*b, &finite);
+    }
+    e = ensure(b->flags, 64);
+    if (e != cudaSuccess) return status_from(e);
+    int* flag = (int*)b->flags.ptr;
+    int h = 0;
+    e = cudaMemsetAsync(flag, 0, sizeof(int), b->stream);
+    if (e == cudaSuccess) {
+        KernelTimer timer(b->stream, GAFIME_KERNEL_FINITE_CHECK);
+        finite4_kernel<<<b->sm_count, 256, 0, b->stream>>>((const float4*)y, b->ld / 4, flag);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    if (e != cudaSuccess) return status_from(e);
+    b->finite_state = h == 0 ? 1 : 0;
+    return GAFIME_SUCCESS;
+}
+
+int gafime_contiguous_bucket_gather(ContiguousBucket dst, ContiguousBucket src, const int32_t* cols,
+                                    int32_t n_cols, const int64_t* rows, int64_t n_rows) {
+    if (!dst || !src || dst == src || !cols) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket* d = (Bucket*)dst;
+    Bucket* s = (Bucket*)src;
+    if (d->device != s->device || n_cols != d->f || n_rows != d->n || (!rows && n_rows != s->n))
+        return GAFIME_ERROR_INVALID_ARGS;
+    for (int32_t c = 0; c < n_cols; ++c)
+        if (cols[c] < 0 || cols[c] >= s->f) return GAFIME_ERROR_INVALID_ARGS;
+    if (rows)
+        for (int64_t r = 0; r < n_rows; ++r)
+            if (rows[r] < 0 || rows[r] >= s->n) return GAFIME_ERROR_INVALID_ARGS;
+    cudaSetDevice(d->device);
+    // source columns (the target last) and row indices, staged in dst's scratch
+    const size_t col_bytes = ((size_t)(n_cols + 1) * sizeof(int32_t) + 255) / 256 * 256;
+    const size_t row_bytes = rows ? (size_t)n_rows * sizeof(int64_t) : 0;
+    cudaError_t e = ensure(d->gather, col_bytes + row_bytes);
+    if (e != cudaSuccess) return status_from(e);
+    std::vector<int32_t> scol(cols, cols + n_cols);
+    scol.push_back((int32_t)s->f);
+    int32_t* d_cols = (int32_t*)d->gather.ptr;
+    int64_t* d_rows = rows ? (int64_t*)((char*)d->gather.ptr + col_bytes) : nullptr;
+    // the source bucket's queued work (its upload) must finish before dst's stream reads it
+    e = cudaStreamSynchronize(s->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(d_cols, scol.data(), scol.size() * sizeof(int32_t), cudaMemcpyHostToDevice, d->stream);
+    if (e == cudaSuccess && rows)
+        e = cudaMemcpyAsync(d_rows, rows, row_bytes, cudaMemcpyHostToDevice, d->stream);
+    if (e != cudaSuccess) return status_from(e);
+    // about 4 CTAs per SM: one grid row per destination column, enough row blocks to fill
+    const int64_t cols_total = (int64_t)n_cols + 1, gy = std::min<int64_t>(cols_total, 65535);
+    const int64_t gx = std::max<int64_t>(1, std::min<int64_t>((n_rows + 255) / 256, (4 * d->sm_count + gy - 1) / gy));
+    dim3 grid((unsigned)gx, (unsigned)gy);
+    gather_rows_kernel<<<grid, 256, 0, d->stream>>>(s->d_data, s->ld, d_cols, cols_total, d_rows, n_rows, d->d_data,
+                                                    d->ld);
+    gather_mask_kernel<<<(unsigned)std::min<int64_t>((n_rows + 255) / 256, 4 * d->sm_count), 256, 0, d->stream>>>(
+        s->d_mask, d_rows, n_rows, d->d_mask);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+    if (e != cudaSuccess) return status_from(e);
+    // rows of finite data are finite; anything else is checked like an upload
+    d->finite_state = s->finite_state == 1 ? 1 : -1;
+    bool finite = true;
+    return check_finite(*d, &finite);
+}
+
 int gafime_contiguous_bucket_compute(ContiguousBucket bucket, int feature_a_idx, int feature_b_idx,
                                      int op_a, int op_b, int interact_type, int val_fold_id,
                                      float* h_stats_out) {
@@ -513,7 +610,7 @@ int gafime_contiguous_bucket_free(ContiguousBucket bucket) {
     cudaSetDevice(b->device);
     if (b->stream) cudaStreamSynchronize(b->stream);
     DeviceBuf* bufs[] = {&b->stats_part, &b->stats, &b->ycen, &b->xcen, &b->moments, &b->cands,
-                         &b->cands2, &b->scores, &b->flags, &b->tiles, &b->mi, &b->mi_hist, &b->mi_mm, &b->mi_xs, &b->mi_split,
+                         &b->cands2, &b->scores, &b->flags, &b->tiles, &b->mi, &b->mi_hist, &b->mi_mm, &b->mi_xs, &b->mi_split, &b->gather,
                          &b->gram};
     for (DeviceBuf* d : bufs) release(*d);
     if (b->d_data) cudaFree(b->d_data);

@@ -17,7 +17,7 @@
 //             is one row of `bins` counters (the joint histogram is order-free);
 //   pass 1  : per-pair min / max of x over row splits, merged with 64-bit integer
 //             atomics on an order-preserving key (deterministic);
-//   pass 2  : each thread owns one pair and a private 16-bit x histogram for the split's
+//   pass 2  : each thread owns one pair and a private x histogram for the split's
 //             class in shared memory; split results merge into the joint histogram with
 //             integer atomics;
 //   finish  : MI per pair in fp64 in the reference's summation order, then the same
@@ -37,7 +37,7 @@ namespace gafime {
 namespace {
 
 constexpr int kMiRows = 64;                  // rows per shared-memory chunk
-constexpr int64_t kMiMaxSplitRows = 32768;   // 16-bit counters cannot overflow
+constexpr int64_t kMiMaxSplitRows = 32768;   // rows per split at most
 
 __device__ __forceinline__ long long dkey(double v) {
     long long b = __double_as_longlong(v);
@@ -45,23 +45,6 @@ __device__ __forceinline__ long long dkey(double v) {
 }
 __device__ __forceinline__ double dval(long long k) {
     return __longlong_as_double(k >= 0 ? k : (k ^ 0x7FFFFFFFFFFFFFFFLL));
-}
-
-__device__ __forceinline__ float combine_f(float a, float b, int op, float eps) {
-    switch (op) {
-        case GAFIME_INTERACT_ADD: return a + b;
-        case GAFIME_INTERACT_SUB: return a - b;
-        case GAFIME_INTERACT_DIV: return a / (fabsf(b) < eps ? copysignf(eps, b) : b);
-        default: return __fmul_rn(a, b);
-    }
-}
-__device__ __forceinline__ double combine_d(double a, double b, int op, double eps) {
-    switch (op) {
-        case GAFIME_INTERACT_ADD: return a + b;
-        case GAFIME_INTERACT_SUB: return a - b;
-        case GAFIME_INTERACT_DIV: return a / (fabs(b) < eps ? copysign(eps, b) : b);
-        default: return __dmul_rn(a, b);
-    }
 }
 
 // Rows [r0, r1) of the class-grouped copy, all of y class u
@@ -80,19 +63,54 @@ struct MiArgs {
     float eps;
     const MiSplit* splits;
     long long* mm;            // [n_tiles][4096][2] keys: min, max
-    int bins, U, hwords;      // hwords: 32-bit words per thread histogram (two 16-bit counters each)
+    int bins, U;
     unsigned* hist;           // [n_tiles][4096][bins * U]
 };
 
-// One CTA: one TS x TS block of pairs inside a 64 x 64 tile, one row split.
-template <int TS, int PASS, bool CENTRED>
+// Column stride of the staged operand blocks: four rows load as one 16-byte vector, and
+// the 16 columns a warp reads start in distinct bank groups.
+template <typename V>
+struct Stage {
+    static constexpr int kStride = sizeof(V) == 8 ? kMiRows + 2 : kMiRows + 4;
+};
+
+template <int OP>
+__device__ __forceinline__ double combine_t(double a, double b, double eps) {
+    if (OP == GAFIME_INTERACT_ADD) return a + b;
+    if (OP == GAFIME_INTERACT_SUB) return a - b;
+    if (OP == GAFIME_INTERACT_DIV) return a / (fabs(b) < eps ? copysign(eps, b) : b);
+    return __dmul_rn(a, b);
+}
+template <int OP>
+__device__ __forceinline__ float combine_t(float a, float b, float eps) {
+    if (OP == GAFIME_INTERACT_ADD) return a + b;
+    if (OP == GAFIME_INTERACT_SUB) return a - b;
+    if (OP == GAFIME_INTERACT_DIV) return a / (fabsf(b) < eps ? copysignf(eps, b) : b);
+    return __fmul_rn(a, b);
+}
+
+// Four consecutive staged rows of one column
+__device__ __forceinline__ void load4(const double* p, double v[4]) {
+    const double2 a = *reinterpret_cast<const double2*>(p);
+    const double2 b = *reinterpret_cast<const double2*>(p + 2);
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+__device__ __forceinline__ void load4(const float* p, float v[4]) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+}
+
+// One CTA: one TS x TS block of pairs inside a 64 x 64 tile, one row split.  The
+// interaction operator is a template argument so the row loop holds no branch on it.
+template <int TS, int PASS, bool CENTRED, int OP>
 __global__ void __launch_bounds__(TS * TS) mi_pass_kernel(MiArgs a) {
     using V = typename std::conditional<CENTRED, double, float>::type;
     constexpr int SUBS = 64 / TS;
+    constexpr int kS = Stage<V>::kStride;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    V* As = reinterpret_cast<V*>(smem_raw);                  // [kMiRows][TS + 1]
-    V* Bs = As + kMiRows * (TS + 1);                         // [kMiRows][TS + 1]
-    uint16_t* hs = reinterpret_cast<uint16_t*>(Bs + kMiRows * (TS + 1));  // [warps][hwords][32 lanes][2]
+    V* As = reinterpret_cast<V*>(smem_raw);                  // [TS][kS]: column-major rows
+    V* Bs = As + TS * kS;                                    // [TS][kS]
+    unsigned* hs = reinterpret_cast<unsigned*>(Bs + TS * kS);  // [warps][bins][32 lanes]
 
     const int t = blockIdx.x / (SUBS * SUBS), sub = blockIdx.x % (SUBS * SUBS);
     const int si = sub / SUBS, sj = sub % SUBS;
@@ -101,7 +119,11 @@ __global__ void __launch_bounds__(TS * TS) mi_pass_kernel(MiArgs a) {
     const int64_t i0 = (int64_t)tc.bi * 64 + si * TS, j0 = (int64_t)tc.bj * 64 + sj * TS;
     if (i0 >= a.f || j0 >= a.f) return;
     const int tid = threadIdx.x;
-    const int li = tid / TS, lj = tid % TS;
+    // a warp holds 4 x 8 pairs: its operand loads touch 4 A columns and 8 B columns, one
+    // wavefront each per four rows
+    constexpr int kWarpsPerBand = TS / 8;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int li = (warp / kWarpsPerBand) * 4 + (lane >> 3), lj = (warp % kWarpsPerBand) * 8 + (lane & 7);
     const int64_t i = i0 + li, j = j0 + lj;
     const bool valid = (i < j) && (j < a.f);
     const int e = (si * TS + li) * 64 + (sj * TS + lj);
@@ -110,15 +132,18 @@ __global__ void __launch_bounds__(TS * TS) mi_pass_kernel(MiArgs a) {
     const MiSplit sp = a.splits[blockIdx.y];
     const int64_t r0 = sp.r0, r1 = sp.r1;
 
-    double mn = INFINITY, mx = -INFINITY;
+    double mn[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
+    double mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     double xmin = 0.0, scale = 0.0;
     bool live = valid;
-    // Each thread's private 16-bit histogram is interleaved with its warp's: counter c of
-    // lane l sits in word (c / 2) * 32 + l, so every lane only touches its own bank.
-    uint16_t* h = hs + (tid >> 5) * (a.hwords * 64) + ((tid & 31) << 1);
-    auto hidx = [](int c) { return ((c >> 1) << 6) + (c & 1); };
+    // Each thread's private x histogram: counter c of lane l at word c * 32 + l of its warp's
+    // block, so the lanes of a warp always hit 32 distinct banks.  Counts go in with shared
+    // atomics whose result nobody waits for: consecutive rows of a thread never stall on a
+    // load-add-store round trip through the same counter.
+    unsigned* h = hs + (tid >> 5) * (a.bins * 32) + (tid & 31);
+    const int top = a.bins - 1;
     if (PASS == 2) {
-        for (int c = 0; c < 2 * a.hwords; ++c) h[hidx(c)] = 0;
+        for (int c = 0; c < a.bins; ++c) h[c * 32] = 0;
         if (valid) {
             xmin = dval(mm[0]);
             double xmax = dval(mm[1]);
@@ -126,6 +151,9 @@ __global__ void __launch_bounds__(TS * TS) mi_pass_kernel(MiArgs a) {
             scale = (double)a.bins / (xmax - xmin);
         }
     }
+    const V* ap = As + li * kS;
+    const V* bp = Bs + lj * kS;
+    const V eps = (V)a.eps;
 
     for (int64_t rb = r0; rb < r1; rb += kMiRows) {
         const int rows = (int)std::min<int64_t>(kMiRows, r1 - rb);
@@ -144,83 +172,60 @@ __global__ void __launch_bounds__(TS * TS) mi_pass_kernel(MiArgs a) {
                     if (CENTRED) vb = (V)((double)raw - a.colstats[cb * 4 + 3]); else vb = (V)raw;
                 }
             }
-            As[row * (TS + 1) + col] = va;
-            Bs[row * (TS + 1) + col] = vb;
+            As[col * kS + row] = va;
+            Bs[col * kS + row] = vb;
         }
         __syncthreads();
         if (!live) continue;
-        // pass 2: four rows per iteration, their products and bins are independent chains
-        // and only the histogram updates (which may hit the same counter) stay in row order;
-        // pass 1 keeps one row per iteration (measured faster: fewer registers)
-        constexpr int kU = PASS == 2 ? 4 : 1;
-        double mn2[kU], mx2[kU];
-        #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            mn2[u] = INFINITY;
-            mx2[u] = -INFINITY;
-        }
+        // four rows per iteration: products and bins are independent chains; only the
+        // histogram updates (which may hit the same counter) stay in row order
         int r = 0;
-        for (; r + kU <= rows; r += kU) {
-            double xv[kU];
+        for (; r + 4 <= rows; r += 4) {
+            V av[4], bv[4];
+            load4(ap + r, av);
+            load4(bp + r, bv);
+            double xv[4];
             #pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                if (CENTRED)
-                    xv[u] = combine_d((double)As[(r + u) * (TS + 1) + li], (double)Bs[(r + u) * (TS + 1) + lj], a.op,
-                                      (double)a.eps);
-                else
-                    xv[u] = (double)combine_f((float)As[(r + u) * (TS + 1) + li], (float)Bs[(r + u) * (TS + 1) + lj],
-                                              a.op, a.eps);
-            }
+            for (int u = 0; u < 4; ++u) xv[u] = (double)combine_t<OP>(av[u], bv[u], eps);
             if (PASS == 1) {
                 #pragma unroll
-                for (int u = 0; u < kU; ++u) {
-                    mn2[u] = xv[u] < mn2[u] ? xv[u] : mn2[u];
-                    mx2[u] = xv[u] > mx2[u] ? xv[u] : mx2[u];
+                for (int u = 0; u < 4; ++u) {
+                    mn[u] = xv[u] < mn[u] ? xv[u] : mn[u];
+                    mx[u] = xv[u] > mx[u] ? xv[u] : mx[u];
                 }
             } else {
-                int slot[kU];
+                // xv >= xmin holds exactly (xmin is the minimum of these same values), so the
+                // bin index is never negative; xv = xmax can land on bins and is clamped
                 #pragma unroll
-                for (int u = 0; u < kU; ++u) {
-                    int xb = (int)((xv[u] - xmin) * scale);
-                    slot[u] = xb < 0 ? 0 : (xb >= a.bins ? a.bins - 1 : xb);
+                for (int u = 0; u < 4; ++u) {
+                    const int xb = (int)((xv[u] - xmin) * scale);
+                    atomicAdd(&h[(xb < top ? xb : top) * 32], 1u);
                 }
-                #pragma unroll
-                for (int u = 0; u < kU; ++u) h[hidx(slot[u])] += 1;
             }
         }
         for (; r < rows; ++r) {
-            double xv;
-            if (CENTRED)
-                xv = combine_d((double)As[r * (TS + 1) + li], (double)Bs[r * (TS + 1) + lj], a.op, (double)a.eps);
-            else
-                xv = (double)combine_f((float)As[r * (TS + 1) + li], (float)Bs[r * (TS + 1) + lj], a.op, a.eps);
+            const double xv = (double)combine_t<OP>(ap[r], bp[r], eps);
             if (PASS == 1) {
-                mn2[0] = xv < mn2[0] ? xv : mn2[0];
-                mx2[0] = xv > mx2[0] ? xv : mx2[0];
+                mn[0] = xv < mn[0] ? xv : mn[0];
+                mx[0] = xv > mx[0] ? xv : mx[0];
             } else {
-                int xb = (int)((xv - xmin) * scale);
-                xb = xb < 0 ? 0 : (xb >= a.bins ? a.bins - 1 : xb);
-                h[hidx(xb)] += 1;
-            }
-        }
-        if (PASS == 1) {
-            #pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                mn = mn2[u] < mn ? mn2[u] : mn;
-                mx = mx2[u] > mx ? mx2[u] : mx;
+                const int xb = (int)((xv - xmin) * scale);
+                atomicAdd(&h[(xb < top ? xb : top) * 32], 1u);
             }
         }
     }
     if (!valid) return;
     if (PASS == 1) {
         if (r1 > r0) {
-            atomicMin(&mm[0], dkey(mn));
-            atomicMax(&mm[1], dkey(mx));
+            const double lo = fmin(fmin(mn[0], mn[1]), fmin(mn[2], mn[3]));
+            const double hi = fmax(fmax(mx[0], mx[1]), fmax(mx[2], mx[3]));
+            atomicMin(&mm[0], dkey(lo));
+            atomicMax(&mm[1], dkey(hi));
         }
     } else if (live) {
         unsigned* g = a.hist + ((int64_t)t * kTilePairs + e) * (a.bins * a.U) + sp.u;
         for (int c = 0; c < a.bins; ++c)
-            if (h[hidx(c)]) atomicAdd(&g[c * a.U], (unsigned)h[hidx(c)]);
+            if (h[c * 32]) atomicAdd(&g[c * a.U], h[c * 32]);
     }
 }
 
@@ -380,12 +385,12 @@ __global__ void __launch_bounds__(256) mi_finish_kernel(MiFinishArgs a) {
     for (int e = threadIdx.x; e < a.k_pad; e += blockDim.x) out[e] = s[e];
 }
 
-template <int TS, int PASS, bool CENTRED>
+template <int TS, int PASS, bool CENTRED, int OP>
 cudaError_t launch_pass(const MiArgs& a, int splits, cudaStream_t stream) {
     using V = typename std::conditional<CENTRED, double, float>::type;
-    size_t smem = 2 * sizeof(V) * kMiRows * (TS + 1);
-    if (PASS == 2) smem += (size_t)((TS * TS + 31) / 32) * a.hwords * 64 * sizeof(uint16_t);
-    auto kern = mi_pass_kernel<TS, PASS, CENTRED>;
+    size_t smem = 2 * sizeof(V) * TS * Stage<V>::kStride;
+    if (PASS == 2) smem += (size_t)((TS * TS + 31) / 32) * a.bins * 32 * sizeof(unsigned);
+    auto kern = mi_pass_kernel<TS, PASS, CENTRED, OP>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)(a.n_tiles * (64 / TS) * (64 / TS)), (unsigned)splits);
@@ -393,18 +398,28 @@ cudaError_t launch_pass(const MiArgs& a, int splits, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
-template <int TS, bool CENTRED>
-cudaError_t run_passes(const MiArgs& a, int splits, cudaStream_t stream) {
+template <int TS, bool CENTRED, int OP>
+cudaError_t run_passes_op(const MiArgs& a, int splits, cudaStream_t stream) {
     cudaError_t e;
     {
         KernelTimer timer(stream, GAFIME_KERNEL_MI_PASS1);
-        e = launch_pass<TS, 1, CENTRED>(a, splits, stream);
+        e = launch_pass<TS, 1, CENTRED, OP>(a, splits, stream);
     }
     if (e == cudaSuccess) {
         KernelTimer timer(stream, GAFIME_KERNEL_MI_PASS2);
-        e = launch_pass<TS, 2, CENTRED>(a, splits, stream);
+        e = launch_pass<TS, 2, CENTRED, OP>(a, splits, stream);
     }
     return e;
+}
+
+template <int TS, bool CENTRED>
+cudaError_t run_passes(const MiArgs& a, int splits, cudaStream_t stream) {
+    switch (a.op) {
+        case GAFIME_INTERACT_ADD: return run_passes_op<TS, CENTRED, GAFIME_INTERACT_ADD>(a, splits, stream);
+        case GAFIME_INTERACT_SUB: return run_passes_op<TS, CENTRED, GAFIME_INTERACT_SUB>(a, splits, stream);
+        case GAFIME_INTERACT_DIV: return run_passes_op<TS, CENTRED, GAFIME_INTERACT_DIV>(a, splits, stream);
+        default: return run_passes_op<TS, CENTRED, GAFIME_INTERACT_MULT>(a, splits, stream);
+    }
 }
 
 }  // namespace
@@ -479,11 +494,10 @@ cudaError_t launch_mi_scores(Bucket& b, const ColumnStats& cs, bool centred, int
     a.mm = mm;
     a.bins = bins;
     a.U = U;
-    a.hwords = (bins + 1) / 2;
     a.hist = hist;
     int n_splits = 0;
     if (ready) {
-        // rows per split: at most 32768 (16-bit counters), fewer while the grid would hold
+        // rows per split: at most 32768, fewer while the grid would hold
         // under 4 CTAs per SM
         int64_t per = std::min<int64_t>(kMiMaxSplitRows, (b.n + 1) / 2 + kMiRows);
         per = std::max<int64_t>(kMiRows, (per + kMiRows - 1) / kMiRows * kMiRows);
@@ -558,7 +572,12 @@ cudaError_t launch_mi_scores(Bucket& b, const ColumnStats& cs, bool centred, int
         if (ready) {
             a.tiles = d_tiles + t0;
             a.n_tiles = nt;
-            e = centred ? run_passes<16, true>(a, n_splits, stream) : run_passes<16, false>(a, n_splits, stream);
+            // 16 x 16 pairs per CTA while their histograms fit in shared memory (bins <= 192),
+            // else 8 x 8
+            if (bins <= 192)
+                e = centred ? run_passes<16, true>(a, n_splits, stream) : run_passes<16, false>(a, n_splits, stream);
+            else
+                e = centred ? run_passes<8, true>(a, n_splits, stream) : run_passes<8, false>(a, n_splits, stream);
             if (e != cudaSuccess) return e;
         }
         fa.tiles = d_tiles + t0;

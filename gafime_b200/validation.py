@@ -1,6 +1,7 @@
 """Bootstrap stability and permutation p-values (gafime/validation/stability.py:17-50,
 gafime/validation/permutation.py:17-54).  Both re-score through the backend, so every
-repeat runs on the GPU."""
+repeat runs on the GPU: a bootstrap gathers its rows on the device and a permutation
+uploads only the permuted target."""
 from __future__ import annotations
 
 from typing import Dict, List, Optional, Tuple
@@ -22,9 +23,14 @@ class StabilityAnalyzer:
         combos = list(combos)
         names = self.metric_suite.metric_names
         seen = {c: {m: [] for m in names} for c in combos}
+        resampled = getattr(self.backend, "score_resampled", None)
         for _ in range(repeats):
             idx = self.backend.sample_indices(X.shape[0], rng)
-            scores = self.backend.score_combos(X[idx], y[idx], combos, self.metric_suite)
+            if resampled is not None:
+                # the same rows, gathered on the device from the resident matrix
+                scores = resampled(X, y, idx, combos, self.metric_suite)
+            else:
+                scores = self.backend.score_combos(X[idx], y[idx], combos, self.metric_suite)
             for c, ms in scores.items():
                 for m, v in ms.items():
                     seen[c][m].append(v)

@@ -296,6 +296,23 @@ int gafime_profile_read(int kernel_id, double* total_ms, int* launches);
  * caller can order its own work or events against it. */
 int gafime_contiguous_bucket_stream(ContiguousBucket bucket, void** stream_out);
 
+/* NEW.  Replace only the target of an uploaded bucket with n_samples floats from the host
+ * (the features stay resident).  Permutation tests re-score the same matrix against
+ * permuted targets; the reference re-uploads matrix and target per call
+ * (gafime/backends/native_cuda_backend.py:344-352).  Checks the new target for non-finite
+ * values like an upload does. */
+int gafime_contiguous_bucket_upload_target(ContiguousBucket bucket, const float* h_y);
+
+/* NEW.  Fill dst from a resident bucket on the same device, without a host copy of the
+ * matrix: feature c of dst is feature cols[c] of src, and row r of dst (features, target
+ * and fold mask) is row rows[r] of src (rows == NULL: every row, n_rows == src's rows).
+ * dst must have been allocated with n_rows samples and n_cols features.  Column subsets and
+ * bootstrap resamples of the engine (gafime/validation/stability.py:35-42 indexes X[idx],
+ * y[idx] on the host) come from the matrix uploaded once.  GAFIME_ERROR_INVALID_ARGS for an
+ * index out of range or a size mismatch. */
+int gafime_contiguous_bucket_gather(ContiguousBucket dst, ContiguousBucket src, const int32_t* cols,
+                                    int32_t n_cols, const int64_t* rows, int64_t n_rows);
+
 /* ------------------------------------------- NEW: no device allocation ---- */
 
 /* Largest problem gafime_allpairs_scores_noalloc accepts. */

@@ -87,3 +87,30 @@ def test_mutual_info_metric_through_the_engine(golden):
     pi, pj = np.triu_indices(12, k=1)
     for p, (a, b) in enumerate(zip(pi, pj)):
         assert abs(pairs[(int(a), int(b))] - g["core_b32"][p, 1]) <= 1e-5
+
+
+def test_engine_uploads_the_matrix_once(golden, monkeypatch):
+    """Unary and pair scoring, 3 bootstraps and 10 permutations: one host-to-device copy
+    of the matrix; bootstraps gather rows on the device, permutations replace the target."""
+    from gafime_b200 import EngineConfig, GafimeEngine, _native
+    from gafime_b200.config import ComputeBudget
+    calls = {"upload": 0, "target": 0, "gather": 0}
+    up, tgt, gat = _native.Bucket.upload_packed, _native.Bucket.set_target, _native.Bucket.gather.__func__
+
+    def count(name, fn):
+        def wrapped(*a, **k):
+            calls[name] += 1
+            return fn(*a, **k)
+        return wrapped
+    monkeypatch.setattr(_native.Bucket, "upload_packed", count("upload", up))
+    monkeypatch.setattr(_native.Bucket, "set_target", count("target", tgt))
+    monkeypatch.setattr(_native.Bucket, "gather", classmethod(count("gather", gat)))
+    g = golden("engine_report.npz")
+    cfg = EngineConfig(metric_names=("pearson",),
+                       budget=ComputeBudget(max_comb_size=2, top_features_for_higher_k=8),
+                       num_repeats=3, permutation_tests=10)
+    rep = GafimeEngine(cfg).analyze(g["X"], g["y"])
+    assert calls["upload"] == 1
+    assert calls["gather"] >= 3 * 2 + 1
+    assert calls["target"] >= 10
+    assert len(rep.permutations) == len(rep.interactions)

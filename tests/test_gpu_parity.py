@@ -381,3 +381,54 @@ def test_interaction_materialiser_rejects_bad_arguments(native):
     assert rc == -1
     assert lib.gafime_feature_interaction_cuda(None, m.ctypes.data, out.ctypes.data, idx.ctypes.data,
                                                bad_off.ctypes.data, 4, 3, 2) == -1
+
+
+def test_gather_equals_upload_of_the_host_gather(native):
+    """A bucket gathered on the device (column subset, bootstrap rows with repeats) scores
+    bit-identically to one uploaded from the same rows and columns gathered on the host."""
+    rng = np.random.default_rng(21)
+    n, f = 5000, 40
+    X = np.hstack([rng.standard_normal((n, 30)), rng.lognormal(0, 1, (n, 10))]).astype(np.float32)
+    y = (X[:, 3] * X[:, 31] + rng.standard_normal(n) > 0).astype(np.float32)
+    cols = [31, 3, 17, 0, 39, 8]
+    rows = rng.integers(0, n, size=n + 123)
+    with bucket_for(native, X, y) as full:
+        for r in (None, rows):
+            g = native.Bucket.gather(full, cols, r)
+            try:
+                Xh = X[:, cols] if r is None else X[r][:, cols]
+                yh = y if r is None else y[r]
+                with bucket_for(native, np.ascontiguousarray(Xh), yh) as h:
+                    for op in OPS:
+                        np.testing.assert_array_equal(g.scores(op, center=True, div_eps=1e-6),
+                                                      h.scores(op, center=True, div_eps=1e-6))
+                    np.testing.assert_array_equal(g.scores("multiply", metric="mutual_info", center=True),
+                                                  h.scores("multiply", metric="mutual_info", center=True))
+                    np.testing.assert_array_equal(g.unary_scores(), h.unary_scores())
+            finally:
+                g.free()
+        with pytest.raises(native.GafimeError) as e:
+            native.Bucket.gather(full, [0, f], None)
+        assert e.value.code == -1
+        with pytest.raises(native.GafimeError):
+            native.Bucket.gather(full, [0, 1], np.array([0, n]))
+
+
+def test_set_target_equals_fresh_upload(native):
+    rng = np.random.default_rng(22)
+    X = rng.standard_normal((3000, 20)).astype(np.float32)
+    y1 = (rng.random(3000) < 0.5).astype(np.float32)
+    y2 = (X[:, 2] * X[:, 9] > 0).astype(np.float32)
+    with bucket_for(native, X, y1) as b, bucket_for(native, X, y2) as ref:
+        b.scores("multiply", center=True)
+        b.set_target(y2)
+        np.testing.assert_array_equal(b.scores("multiply", center=True), ref.scores("multiply", center=True))
+        np.testing.assert_array_equal(b.topk(OPS, 7)["add"][2], ref.topk(OPS, 7)["add"][2])
+        bad = y2.copy()
+        bad[7] = np.inf
+        b.set_target(bad)
+        with pytest.raises(native.GafimeError) as e:
+            b.scores("multiply")
+        assert e.value.code == -1
+        b.set_target(y2)
+        np.testing.assert_array_equal(b.scores("multiply"), ref.scores("multiply"))
