@@ -47,7 +47,7 @@ EXPORTED = (
     "gafime_bucket_compute_batch", "gafime_interleaved_compute", "gafime_fused_interaction",
     "gafime_pipeline_init", "gafime_pipeline_submit", "gafime_pipeline_poll", "gafime_pipeline_wait",
     "gafime_pipeline_pending", "gafime_pipeline_flush", "gafime_pipeline_free", "gafime_pearson_cuda",
-    "gafime_contiguous_bucket_upload_target", "gafime_contiguous_bucket_gather",
+    "gafime_contiguous_bucket_upload_target", "gafime_contiguous_bucket_gather", "gafime_spearman_scores",
 )
 
 # kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
@@ -92,6 +92,7 @@ def _bind(lib: ctypes.CDLL) -> None:
         "gafime_contiguous_bucket_stream": ([_vp, ctypes.POINTER(_vp)], _i),
         "gafime_contiguous_bucket_upload_target": ([_vp, _vp], _i),
         "gafime_contiguous_bucket_gather": ([_vp, _vp, _vp, ctypes.c_int32, _vp, _i64], _i),
+        "gafime_spearman_scores": ([_vp, _vp, _vp, _i64, _i, _i, _f, _vp], _i),
         "gafime_allpairs_scores_noalloc": ([_vp, _i64, _vp, _i, _i, _i, _f, _vp, _vp], _i),
         "gafime_unary_scores": ([_vp, _i, _i, _vp], _i),
         "gafime_shard_tiles": ([_i, _i, _i, _vp, _i, _ip], _i),
@@ -263,6 +264,19 @@ class Bucket:
             check("gafime_allpairs_scores", self.lib.gafime_allpairs_scores(
                 self.handle, INTERACT[op], METRIC[metric], int(bool(center)), float(div_eps),
                 int(mi_bins), _ptr(out)))
+        return out
+
+    def spearman(self, combos: Sequence[Tuple[int, ...]], op: str = "multiply", center: bool = True,
+                 div_eps: float = 1e-8) -> np.ndarray:
+        """Spearman rank correlation of each combo (one feature: the raw column; two: the
+        interaction) against the target."""
+        a = np.array([c[0] for c in combos], dtype=np.int32)
+        b = np.array([c[1] if len(c) > 1 else -1 for c in combos], dtype=np.int32)
+        out = np.empty(len(combos), dtype=np.float64)
+        if len(combos):
+            check("gafime_spearman_scores", self.lib.gafime_spearman_scores(
+                self.handle, _ptr(a), _ptr(b), len(combos), INTERACT[op], int(bool(center)),
+                float(div_eps), _ptr(out)))
         return out
 
     def unary_scores(self, metric: str = "pearson", mi_bins: int = 16) -> np.ndarray:

@@ -120,9 +120,10 @@ class NativeCudaBackend(Backend):
             try:
                 cache = {}
                 for m in metric_suite.metric_names:
-                    base = "pearson" if m in ("pearson", "r2") else "mutual_info"
+                    base = _BASE[m]
                     if base not in cache:
-                        cache[base] = b.unary_scores(base, metric_suite.mi_bins)
+                        cache[base] = (b.spearman([(i,) for i in range(len(cols))]) if base == "spearman"
+                                       else b.unary_scores(base, metric_suite.mi_bins))
                     v = cache[base]
                     for c in unaries:
                         s = float(v[pos[c[0]]])
@@ -140,7 +141,15 @@ class NativeCudaBackend(Backend):
             try:
                 cache = {}
                 for m in metric_suite.metric_names:
-                    base = "pearson" if m in ("pearson", "r2") else "mutual_info"
+                    base = _BASE[m]
+                    if base == "spearman":
+                        # ranks of x_a op x_c in the combo's own orientation
+                        if base not in cache:
+                            cache[base] = b.spearman([(pos[a], pos[c]) for a, c in pairs], self.operator,
+                                                     center=self.center, div_eps=self.div_eps)
+                        for p, (a, c) in enumerate(pairs):
+                            out[(a, c)][m] = float(cache[base][p])
+                        continue
                     if base not in cache:
                         cache[base] = b.scores(self.operator, metric=base, center=self.center,
                                                div_eps=self.div_eps, mi_bins=metric_suite.mi_bins)
@@ -177,6 +186,9 @@ class NativeCudaBackend(Backend):
         b = self._resident(X, y).bucket(tuple(range(X.shape[1])), y)
         return b.topk(list(ops) or [self.operator], k, metric=metric, center=self.center,
                       div_eps=self.div_eps, mi_bins=mi_bins)
+
+
+_BASE = {"pearson": "pearson", "r2": "pearson", "mutual_info": "mutual_info", "spearman": "spearman"}
 
 
 def _tri(i: int, j: int, f: int) -> int:

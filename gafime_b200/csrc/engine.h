@@ -52,7 +52,7 @@ struct Bucket {
     int sm_count = 148;
     // scratch
     DeviceBuf stats_part, stats, ycen, xcen, moments, cands, cands2, scores, flags, tiles, mi,
-        mi_hist, mi_mm, mi_xs, mi_split, gather, gram;
+        mi_hist, mi_mm, mi_xs, mi_split, gather, rank, gram;
 };
 
 // Grow a scratch buffer to at least `bytes`; returns cudaSuccess or an error.

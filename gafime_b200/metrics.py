@@ -2,14 +2,15 @@
 
 Scores are computed on the GPU by the backend; the suite only carries which metrics
 are wanted and the MI bin count.  ``r2`` is derived as Pearson r squared
-(gafime_core.cpp:591-594); ``spearman`` (a per-pair sort) is not on the GPU path.
+(gafime_core.cpp:591-594); ``spearman`` sorts each combo's values on the device
+(gafime_core.cpp:595-607).
 """
 from __future__ import annotations
 
 from typing import Iterable, Tuple
 
 SUPPORTED_METRICS = ("pearson", "spearman", "mutual_info", "r2")
-GPU_METRICS = ("pearson", "mutual_info", "r2")
+GPU_METRICS = ("pearson", "spearman", "mutual_info", "r2")
 
 
 class MetricSuite:

@@ -296,6 +296,18 @@ int gafime_profile_read(int kernel_id, double* total_ms, int* launches);
  * caller can order its own work or events against it. */
 int gafime_contiguous_bucket_stream(ContiguousBucket bucket, void** stream_out);
 
+/* NEW.  Spearman rank correlation of each combo against the target, as gafime_core's
+ * "spearman" metric computes it (gafime_core.cpp:156-177 average-tie ranks,
+ * 503-517 target ranks, 595-607 Pearson of the ranks).  Combo c is feature feat_a[c] alone
+ * when feat_b[c] < 0 (the raw column, gafime_core.cpp:558-568), else the pair
+ * x = (a - mean_a) op (b - mean_b) in fp64 (center = 1; gafime_core.cpp:571-577 for
+ * multiply) or fl32(a op b) (center = 0; cpu_backend.cpp:87-103).  interact_type as
+ * gafime_allpairs_topk; out_scores receives n_combos values.  One device-wide sort per
+ * combo (the reference sorts per combo on the host: gafime_core.cpp:596). */
+int gafime_spearman_scores(ContiguousBucket bucket, const int32_t* feat_a, const int32_t* feat_b,
+                           int64_t n_combos, int interact_type, int center, float div_eps,
+                           double* out_scores);
+
 /* NEW.  Replace only the target of an uploaded bucket with n_samples floats from the host
  * (the features stay resident).  Permutation tests re-score the same matrix against
  * permuted targets; the reference re-uploads matrix and target per call

@@ -43,6 +43,10 @@
  *     features are all invalid) yields 1.  cpu_backend.cpp:316-370 agrees on every combo
  *     whose features are valid (it writes 0 for the degenerate ones).
  *
+ *  6. Mutual information of any operator (raw fp32 or centred fp64 interaction) and of raw
+ *     columns, and Spearman rank correlation (rankdata with average ties and the Pearson of
+ *     ranks, gafime_core.cpp:156-177,503-517,595-607), for unaries and pairs.
+ *
  * Data layout: X is column-major fp32, column f at X + f * ld, n rows (the materialiser
  * takes the reference's row-major X, row i at X + i * F).
  */
@@ -359,6 +363,105 @@ int gafime_oracle_unary_mi(const float* X, int64_t ld, const float* y, int64_t n
         }
     }
     free(yd); free(xd); free(y_bins); free(joint); free(p_x); free(p_y);
+    return status;
+}
+
+/* rankdata, gafime_core.cpp:156-177: stable ascending order, a run of equal values gets
+ * the average 0-based rank 0.5 * (first + last).  Sorting (value, index) pairs gives the
+ * stable order. */
+typedef struct {
+    double v;
+    int64_t i;
+} OrRankItem;
+
+static int or_rank_cmp(const void* pa, const void* pb) {
+    const OrRankItem* a = (const OrRankItem*)pa;
+    const OrRankItem* b = (const OrRankItem*)pb;
+    if (a->v < b->v) return -1;
+    if (a->v > b->v) return 1;
+    return (a->i > b->i) - (a->i < b->i);
+}
+
+static void or_rankdata(const double* v, int64_t n, OrRankItem* items, double* out) {
+    for (int64_t i = 0; i < n; ++i) {
+        items[i].v = v[i];
+        items[i].i = i;
+    }
+    qsort(items, (size_t)n, sizeof(OrRankItem), or_rank_cmp);
+    int64_t i = 0;
+    while (i < n) {
+        int64_t j = i + 1;
+        while (j < n && items[j].v == items[i].v) ++j;
+        double avg = 0.5 * (double)(i + j - 1);
+        for (int64_t k = i; k < j; ++k) out[items[k].i] = avg;
+        i = j;
+    }
+}
+
+/* Spearman of each combo against y as gafime_core.score_combos computes it
+ * (gafime_core.cpp:503-517 target ranks, 595-607 the metric).  Combo c is column a[c]
+ * alone when b[c] < 0, else x = (a - mean_a) op (b - mean_b) in fp64 (center = 1) or
+ * fl32(a op b) (center = 0), with the operators and divide rule of gafime_oracle_pair_mi. */
+int gafime_oracle_spearman(const float* X, int64_t ld, const float* y, int64_t n, int64_t f_count,
+                           const int32_t* ca_idx, const int32_t* cb_idx, int64_t n_combos, int op,
+                           float eps, int center, double* out) {
+    size_t nn = (size_t)(n > 0 ? n : 1);
+    double* means = (double*)malloc((size_t)(f_count > 0 ? f_count : 1) * sizeof(double));
+    double* yd = (double*)malloc(nn * sizeof(double));
+    double* yr = (double*)malloc(nn * sizeof(double));
+    double* ycr = (double*)malloc(nn * sizeof(double));
+    OrRankItem* items = (OrRankItem*)malloc(nn * sizeof(OrRankItem));
+    double* xv = (double*)malloc(nn * sizeof(double));
+    double* xr = (double*)malloc(nn * sizeof(double));
+    int status = 0;
+    if (!means || !yd || !yr || !ycr || !items || !xv || !xr) {
+        status = -3;
+        goto done;
+    }
+    gafime_oracle_column_means(X, ld, n, f_count, means);
+    for (int64_t r = 0; r < n; ++r) yd[r] = (double)y[r];
+    or_rankdata(yd, n, items, yr);
+    {
+        double sum_r = 0.0, sum_r2 = 0.0;
+        for (int64_t r = 0; r < n; ++r) {
+            sum_r += yr[r];
+            sum_r2 += yr[r] * yr[r];
+        }
+        double mean_r = n == 0 ? 0.0 : sum_r / (double)n;
+        for (int64_t r = 0; r < n; ++r) ycr[r] = yr[r] - mean_r;
+        double var_y_rank = sum_r2 - (sum_r * mean_r);
+        for (int64_t c = 0; c < n_combos; ++c) {
+            const float* pa = X + (int64_t)ca_idx[c] * ld;
+            const float* pb = cb_idx[c] >= 0 ? X + (int64_t)cb_idx[c] * ld : NULL;
+            for (int64_t r = 0; r < n; ++r) {
+                if (!pb) {
+                    xv[r] = (double)pa[r];
+                } else if (center) {
+                    double a = (double)pa[r] - means[ca_idx[c]], b = (double)pb[r] - means[cb_idx[c]];
+                    double v;
+                    switch (op) {
+                        case OR_ADD: v = a + b; break;
+                        case OR_SUB: v = a - b; break;
+                        case OR_DIV: v = a / (fabs(b) < (double)eps ? copysign((double)eps, b) : b); break;
+                        default: v = 1.0; v *= a; v *= b;
+                    }
+                    xv[r] = v;
+                } else {
+                    xv[r] = (double)or_combine(pa[r], pb[r], op, eps);
+                }
+            }
+            or_rankdata(xv, n, items, xr);
+            double s1 = 0.0, s2 = 0.0, s3 = 0.0;
+            for (int64_t r = 0; r < n; ++r) {
+                s1 += xr[r];
+                s2 += xr[r] * xr[r];
+                s3 += xr[r] * ycr[r];
+            }
+            out[c] = or_pearson_from_sums(s1, s2, s3, var_y_rank, n);
+        }
+    }
+done:
+    free(means); free(yd); free(yr); free(ycr); free(items); free(xv); free(xr);
     return status;
 }
 

@@ -64,6 +64,10 @@ def lib() -> ctypes.CDLL:
         _LIB.gafime_oracle_unary_mi.argtypes = [
             _f32p, ctypes.c_int64, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, _f64p]
         _LIB.gafime_oracle_unary_mi.restype = ctypes.c_int
+        _LIB.gafime_oracle_spearman.argtypes = [
+            _f32p, ctypes.c_int64, _f32p, ctypes.c_int64, ctypes.c_int64, _i32p, _i32p,
+            ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_int, _f64p]
+        _LIB.gafime_oracle_spearman.restype = ctypes.c_int
         _LIB.gafime_oracle_pair_moments.argtypes = [
             _f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, _f64p]
         _LIB.gafime_oracle_pair_moments.restype = None
@@ -150,6 +154,21 @@ def unary_mi(X: np.ndarray, y: np.ndarray, mi_bins: int = 16) -> np.ndarray:
     out = np.empty(f, dtype=np.float64)
     rc = lib().gafime_oracle_unary_mi(flat, ld, np.ascontiguousarray(y, dtype=np.float32), n, f,
                                       int(mi_bins), out)
+    if rc != 0:
+        raise MemoryError("oracle allocation failed")
+    return out
+
+
+def spearman(X: np.ndarray, y: np.ndarray, combos, op: str = "multiply", center: bool = True,
+             div_eps: float = 1e-8) -> np.ndarray:
+    """Spearman rank correlation of each combo (one feature: the raw column; two: the
+    interaction) against y, as gafime_core computes it."""
+    flat, ld, n, f = _colmajor(X)
+    a = np.array([c[0] for c in combos], dtype=np.int32)
+    b = np.array([c[1] if len(c) > 1 else -1 for c in combos], dtype=np.int32)
+    out = np.empty(len(combos), dtype=np.float64)
+    rc = lib().gafime_oracle_spearman(flat, ld, np.ascontiguousarray(y, dtype=np.float32), n, f, a, b,
+                                      len(combos), OP_IDS[op], np.float32(div_eps), int(center), out)
     if rc != 0:
         raise MemoryError("oracle allocation failed")
     return out

@@ -206,6 +206,19 @@ def main():
                                 combos=np.array(combos, dtype=np.int32), pearson=np.array(vals),
                                 stability=np.array(stab), p_values=np.array(pv),
                                 decision=np.array(rep.decision.signal_detected))
+    # default metrics (pearson, spearman, mutual_info, r2) through the same engine
+    cfg = EngineConfig(backend="core", budget=ComputeBudget(max_comb_size=2, top_features_for_higher_k=8),
+                       num_repeats=3, permutation_tests=10)
+    rep = GafimeEngine(cfg).analyze(Xg, yg)
+    names = list(cfg.metric_names)
+    np.savez_compressed(
+        os.path.join(HERE, "engine_default_metrics.npz"), metric_names=np.array(names),
+        combos=np.array([list(r.combo) + [-1] * (2 - len(r.combo)) for r in rep.interactions], dtype=np.int32),
+        metrics=np.array([[r.metrics[m] for m in names] for r in rep.interactions]),
+        stab_mean=np.array([[r.metrics_mean[m] for m in names] for r in rep.stability]),
+        stab_std=np.array([[r.metrics_std[m] for m in names] for r in rep.stability]),
+        p_values=np.array([[r.p_values[m] for m in names] for r in rep.permutations]),
+        decision=np.array(rep.decision.signal_detected))
     plans = {}
     for seed in (0, 7, 11):
         r = np.random.default_rng(seed)
@@ -318,6 +331,24 @@ def main():
                          for yv in (y3, yc)])
     np.savez_compressed(os.path.join(HERE, "raw_mi.npz"), X=Xr, y3=y3, yc=yc, bins=np.array(16), mi=raw_mi,
                         unary_mi=unary_mi)
+    # --- Spearman (gafime_core.cpp:595-607) with tied values --------------------------
+    rng = np.random.default_rng(12)
+    ns = 1500
+    Xs = np.column_stack([rng.standard_normal((ns, 4)), rng.integers(0, 5, (ns, 2)),
+                          rng.lognormal(0, 1, ns), rng.integers(0, 2, ns)]).astype(np.float32)
+    ys3 = rng.integers(0, 3, ns).astype(np.float32)
+    ysc = (Xs[:, 0].astype(np.float64) * Xs[:, 4] + rng.standard_normal(ns)).astype(np.float32)
+    fs = Xs.shape[1]
+    scombos = [(int(c),) for c in range(fs)] + [(int(a), int(b)) for a, b in zip(*np.triu_indices(fs, k=1))]
+    sidx, soff = core.pack_combos(scombos)
+    spear = np.stack([np.asarray(core.score_combos(np.ascontiguousarray(Xs, dtype=np.float64),
+                                                   np.ascontiguousarray(yv, dtype=np.float64),
+                                                   sidx, soff, ["spearman"], 16))[:, 0]
+                      for yv in (ys3, ysc)])
+    width = np.array([len(c) for c in scombos])
+    pad = np.array([list(c) + [-1] * (2 - len(c)) for c in scombos], dtype=np.int32)
+    np.savez_compressed(os.path.join(HERE, "spearman.npz"), X=Xs, y3=ys3, yc=ysc, combos=pad, width=width,
+                        spearman=spear)
     print("wrote fixtures to", HERE)
 
 

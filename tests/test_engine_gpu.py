@@ -114,3 +114,32 @@ def test_engine_uploads_the_matrix_once(golden, monkeypatch):
     assert calls["gather"] >= 3 * 2 + 1
     assert calls["target"] >= 10
     assert len(rep.permutations) == len(rep.interactions)
+
+
+def test_engine_default_metrics_match_reference_engine(golden):
+    """EngineConfig's default metrics (pearson, spearman, mutual_info, r2): interactions,
+    bootstrap means / stds, permutation p-values and the decision of the reference engine."""
+    from gafime_b200 import EngineConfig, GafimeEngine
+    from gafime_b200.config import ComputeBudget
+    g = golden("engine_default_metrics.npz")
+    ref = golden("engine_report.npz")
+    cfg = EngineConfig(budget=ComputeBudget(max_comb_size=2, top_features_for_higher_k=8),
+                       num_repeats=3, permutation_tests=10)
+    assert list(cfg.metric_names) == g["metric_names"].tolist()
+    rep = GafimeEngine(cfg).analyze(ref["X"], ref["y"])
+    names = list(cfg.metric_names)
+    combos = [list(r.combo) + [-1] * (2 - len(r.combo)) for r in rep.interactions]
+    assert combos == g["combos"].tolist()
+    tol = {"pearson": (1e-4, 1e-6), "spearman": (0, 1e-10), "mutual_info": (0, 1e-5), "r2": (2e-4, 1e-6)}
+    got = np.array([[r.metrics[m] for m in names] for r in rep.interactions])
+    mean = np.array([[r.metrics_mean[m] for m in names] for r in rep.stability])
+    std = np.array([[r.metrics_std[m] for m in names] for r in rep.stability])
+    for k, m in enumerate(names):
+        rt, at = tol[m]
+        np.testing.assert_allclose(got[:, k], g["metrics"][:, k], rtol=rt, atol=at, err_msg=m)
+        np.testing.assert_allclose(mean[:, k], g["stab_mean"][:, k], rtol=rt, atol=at, err_msg=m)
+        np.testing.assert_allclose(std[:, k], g["stab_std"][:, k], rtol=max(rt, 1e-3), atol=max(at, 1e-6),
+                                   err_msg=m)
+    pv = np.array([[r.p_values[m] for m in names] for r in rep.permutations])
+    np.testing.assert_array_equal(pv, g["p_values"])
+    assert rep.decision.signal_detected == bool(g["decision"])

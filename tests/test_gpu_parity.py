@@ -432,3 +432,41 @@ def test_set_target_equals_fresh_upload(native):
         assert e.value.code == -1
         b.set_target(y2)
         np.testing.assert_array_equal(b.scores("multiply"), ref.scores("multiply"))
+
+
+@pytest.mark.parametrize("target", ["y3", "yc"])
+def test_spearman_matches_gafime_core(native, golden, target):
+    """Unaries and centred products with tied values (discrete and binary columns, 3-class
+    target): ranks are exact, the sums differ from gafime_core's only in summation order."""
+    g = golden("spearman.npz")
+    combos = [tuple(int(v) for v in c if v >= 0) for c in g["combos"]]
+    with bucket_for(native, g["X"], g[target]) as b:
+        got = b.spearman(combos)
+    np.testing.assert_allclose(got, g["spearman"][0 if target == "y3" else 1], rtol=0, atol=1e-12)
+
+
+@pytest.mark.parametrize("center", [True, False])
+@pytest.mark.parametrize("op", OPS)
+def test_spearman_operators_match_oracle(native, golden, oracle, op, center):
+    g = golden("spearman.npz")
+    X, y = g["X"], g["yc"]
+    f = X.shape[1]
+    combos = [(a, c) for a in range(f) for c in range(f) if a != c][::3] + [(2,), (5,)]
+    want = oracle.spearman(X, y, combos, op, center=center, div_eps=1e-6)
+    with bucket_for(native, X, y) as b:
+        got = b.spearman(combos, op, center=center, div_eps=1e-6)
+    np.testing.assert_allclose(got, want, rtol=0, atol=1e-12)
+
+
+def test_spearman_large_with_long_tie_runs(native, oracle):
+    """300k rows: a binary and a 3-valued column make tie runs of ~100k rows."""
+    rng = np.random.default_rng(31)
+    n = 300_000
+    X = np.column_stack([rng.standard_normal(n), rng.integers(0, 2, n), rng.integers(0, 3, n),
+                         rng.lognormal(0, 1, n)]).astype(np.float32)
+    y = (X[:, 0] * X[:, 2] + rng.standard_normal(n)).astype(np.float32)
+    combos = [(0,), (1,), (2,), (0, 1), (1, 2), (0, 3), (2, 3)]
+    want = oracle.spearman(X, y, combos)
+    with bucket_for(native, X, y) as b:
+        got = b.spearman(combos)
+    np.testing.assert_allclose(got, want, rtol=0, atol=1e-12)

@@ -144,3 +144,13 @@ def test_unary_mi_matches_gafime_core(golden, oracle, target):
     g = golden("raw_mi.npz")
     m = oracle.unary_mi(g["X"], g[target], mi_bins=int(g["bins"]))
     np.testing.assert_array_equal(m, g["unary_mi"][0 if target == "y3" else 1])
+
+
+@pytest.mark.parametrize("target", ["y3", "yc"])
+def test_spearman_matches_gafime_core(golden, oracle, target):
+    """Average-tie ranks (discrete and binary columns, a 3-class target) and the Pearson of
+    ranks: the same arithmetic in the same order as gafime_core, so equal to rounding."""
+    g = golden("spearman.npz")
+    combos = [tuple(int(v) for v in c if v >= 0) for c in g["combos"]]
+    got = oracle.spearman(g["X"], g[target], combos)
+    np.testing.assert_allclose(got, g["spearman"][0 if target == "y3" else 1], rtol=0, atol=1e-13)
