@@ -89,6 +89,13 @@ __device__ __forceinline__ float combine_t(float a, float b, float eps) {
     return __fmul_rn(a, b);
 }
 
+// A staged value the fp32 pre-filter of pass 1 cannot bound: nonzero with magnitude outside
+// [2^-60, 2^60] (its fp32 copy or a product of two could leave the normal fp32 range)
+__device__ __forceinline__ int out_of_filter_range(double v) {
+    const double m = fabs(v);
+    return m != 0.0 && (m < 0x1p-60 || m > 0x1p60);
+}
+
 // Four consecutive staged rows of one column
 __device__ __forceinline__ void load4(const double* p, double v[4]) {
     const double2 a = *reinterpret_cast<const double2*>(p);
@@ -111,6 +118,13 @@ __global__ void __launch_bounds__(TS * TS) mi_pass_kernel(MiArgs a) {
     V* As = reinterpret_cast<V*>(smem_raw);                  // [TS][kS]: column-major rows
     V* Bs = As + TS * kS;                                    // [TS][kS]
     unsigned* hs = reinterpret_cast<unsigned*>(Bs + TS * kS);  // [warps][bins][32 lanes]
+    // Pass 1 of the centred product also stages fp32 copies of the operands: the min / max
+    // scan runs on fp32 products and falls back to the exact fp64 products only for rows
+    // that could move the current minimum or maximum (see the bound below).
+    constexpr bool kFilter = PASS == 1 && CENTRED && OP == GAFIME_INTERACT_MULT;
+    constexpr int kSf = kMiRows + 4;
+    float* Af = reinterpret_cast<float*>(Bs + TS * kS);       // [TS][kSf] (kFilter only)
+    float* Bf = Af + TS * kSf;
 
     const int t = blockIdx.x / (SUBS * SUBS), sub = blockIdx.x % (SUBS * SUBS);
     const int si = sub / SUBS, sj = sub % SUBS;
@@ -155,28 +169,100 @@ __global__ void __launch_bounds__(TS * TS) mi_pass_kernel(MiArgs a) {
     const V* bp = Bs + lj * kS;
     const V eps = (V)a.eps;
 
+    // The raw values of the next chunk are loaded into registers while this chunk is
+    // computed, so the global-load latency hides behind the row loop.
+    constexpr int kPer = kMiRows / TS;  // staged values per thread and operand
+    float pa[kPer], pb[kPer];
+    auto fetch = [&](int64_t rb) {
+        const int rows = (int)std::min<int64_t>(kMiRows, r1 - rb);
+        #pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int q = tid + u * TS * TS, col = q / kMiRows, row = q % kMiRows;
+            const int64_t ca = i0 + col, cb = j0 + col;
+            pa[u] = (row < rows && ca < a.f) ? a.xs[ca * a.lds + rb + row] : 0.f;
+            pb[u] = (row < rows && cb < a.f) ? a.xs[cb * a.lds + rb + row] : 0.f;
+        }
+    };
+    if (r0 < r1) fetch(r0);
     for (int64_t rb = r0; rb < r1; rb += kMiRows) {
         const int rows = (int)std::min<int64_t>(kMiRows, r1 - rb);
+        int unsafe = 0;
         __syncthreads();
-        for (int q = tid; q < TS * kMiRows; q += TS * TS) {
-            int col = q / kMiRows, row = q % kMiRows;
-            V va = 0, vb = 0;
-            if (row < rows) {
-                int64_t ca = i0 + col, cb = j0 + col;
-                if (ca < a.f) {
-                    float raw = a.xs[ca * a.lds + rb + row];
-                    if (CENTRED) va = (V)((double)raw - a.colstats[ca * 4 + 3]); else va = (V)raw;
-                }
-                if (cb < a.f) {
-                    float raw = a.xs[cb * a.lds + rb + row];
-                    if (CENTRED) vb = (V)((double)raw - a.colstats[cb * 4 + 3]); else vb = (V)raw;
-                }
+        #pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int q = tid + u * TS * TS, col = q / kMiRows, row = q % kMiRows;
+            const int64_t ca = i0 + col, cb = j0 + col;
+            V va, vb;
+            if (CENTRED) {
+                va = ca < a.f ? (V)((double)pa[u] - a.colstats[ca * 4 + 3]) : (V)0;
+                vb = cb < a.f ? (V)((double)pb[u] - a.colstats[cb * 4 + 3]) : (V)0;
+            } else {
+                va = (V)pa[u];
+                vb = (V)pb[u];
             }
             As[col * kS + row] = va;
             Bs[col * kS + row] = vb;
+            if (kFilter) {
+                Af[col * kSf + row] = (float)va;
+                Bf[col * kSf + row] = (float)vb;
+                unsafe |= out_of_filter_range((double)va) | out_of_filter_range((double)vb);
+            }
         }
-        __syncthreads();
+        const bool exact_chunk = kFilter ? __syncthreads_or(unsafe) != 0 : true;
+        if (!kFilter) __syncthreads();
+        if (rb + kMiRows < r1) fetch(rb + kMiRows);
         if (!live) continue;
+        if (kFilter) {
+            // Every staged |value| is 0 or in [2^-60, 2^60], so a32 = a(1+e1), b32 = b(1+e2)
+            // and p32 = a32 b32 (1+e3), |e| <= 2^-24, with no underflow or overflow: p32 is
+            // within 2^-22 |p| of the exact product p.  A row with p > max has
+            // p32 >= max - 2^-22 |max| (either sign), hence p32 >= thr_hi below (margin 2^-20,
+            // rounded down), so rows below both thresholds cannot move the min or the max.
+            const float* afp = Af + li * kSf;
+            const float* bfp = Bf + lj * kSf;
+            float thr_hi = __double2float_rd(mx[0] - fabs(mx[0]) * 0x1p-20);
+            float thr_lo = __double2float_ru(mn[0] + fabs(mn[0]) * 0x1p-20);
+            int r = 0;
+            for (; r + 8 <= rows; r += 8) {
+                // eight rows: the extremes of their fp32 products against the thresholds
+                // (no product is NaN in a chunk inside the bound's range)
+                float fa[8], fb[8];
+                load4(afp + r, fa);
+                load4(afp + r + 4, fa + 4);
+                load4(bfp + r, fb);
+                load4(bfp + r + 4, fb + 4);
+                float p[8];
+                #pragma unroll
+                for (int u = 0; u < 8; ++u) p[u] = __fmul_rn(fa[u], fb[u]);
+                const float hi = fmaxf(fmaxf(fmaxf(p[0], p[1]), fmaxf(p[2], p[3])),
+                                       fmaxf(fmaxf(p[4], p[5]), fmaxf(p[6], p[7])));
+                const float lo = fminf(fminf(fminf(p[0], p[1]), fminf(p[2], p[3])),
+                                       fminf(fminf(p[4], p[5]), fminf(p[6], p[7])));
+                // a chunk outside the bound's range: every row exact
+                if (exact_chunk || !(hi < thr_hi) || !(lo > thr_lo)) {
+                    #pragma unroll
+                    for (int h = 0; h < 8; h += 4) {
+                        V av[4], bv[4];
+                        load4(ap + r + h, av);
+                        load4(bp + r + h, bv);
+                        #pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const double xv = (double)combine_t<OP>(av[u], bv[u], eps);
+                            mn[0] = xv < mn[0] ? xv : mn[0];
+                            mx[0] = xv > mx[0] ? xv : mx[0];
+                        }
+                    }
+                    thr_hi = __double2float_rd(mx[0] - fabs(mx[0]) * 0x1p-20);
+                    thr_lo = __double2float_ru(mn[0] + fabs(mn[0]) * 0x1p-20);
+                }
+            }
+            for (; r < rows; ++r) {
+                const double xv = (double)combine_t<OP>(ap[r], bp[r], eps);
+                mn[0] = xv < mn[0] ? xv : mn[0];
+                mx[0] = xv > mx[0] ? xv : mx[0];
+            }
+            continue;
+        }
         // four rows per iteration: products and bins are independent chains; only the
         // histogram updates (which may hit the same counter) stay in row order
         int r = 0;
@@ -389,6 +475,7 @@ template <int TS, int PASS, bool CENTRED, int OP>
 cudaError_t launch_pass(const MiArgs& a, int splits, cudaStream_t stream) {
     using V = typename std::conditional<CENTRED, double, float>::type;
     size_t smem = 2 * sizeof(V) * TS * Stage<V>::kStride;
+    if (PASS == 1 && CENTRED && OP == GAFIME_INTERACT_MULT) smem += 2 * sizeof(float) * TS * (kMiRows + 4);
     if (PASS == 2) smem += (size_t)((TS * TS + 31) / 32) * a.bins * 32 * sizeof(unsigned);
     auto kern = mi_pass_kernel<TS, PASS, CENTRED, OP>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -470,3 +470,20 @@ def test_spearman_large_with_long_tie_runs(native, oracle):
     with bucket_for(native, X, y) as b:
         got = b.spearman(combos)
     np.testing.assert_allclose(got, want, rtol=0, atol=1e-12)
+
+
+def test_mi_min_max_filter_edge_columns(native, oracle):
+    """Pass 1 scans fp32 products and recomputes fp64 ones only near the running min / max:
+    sorted columns (a new extreme every row), tiny and huge columns (outside the range the
+    fp32 bound covers, so those chunks run exact), a ramp and rounded (tied) values."""
+    rng = np.random.default_rng(41)
+    n = 20000
+    X = np.column_stack([rng.standard_normal(n), np.sort(rng.standard_normal(n)),
+                         rng.standard_normal(n) * 1e-20, rng.standard_normal(n) * 1e20,
+                         np.linspace(-1, 1, n), -np.sort(rng.lognormal(0, 1, n)),
+                         np.round(rng.standard_normal(n), 1)]).astype(np.float32)
+    y = rng.integers(0, 3, n).astype(np.float32)
+    want = oracle.pair_mi(X, y, "multiply", center=True, mi_bins=16)
+    with bucket_for(native, X, y) as b:
+        got = b.scores("multiply", metric="mutual_info", center=True, mi_bins=16)
+    np.testing.assert_allclose(got, want, rtol=0, atol=1e-5)
