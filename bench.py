@@ -459,6 +459,9 @@ def run_ours(args):
     def step():
         res = bucket.topk(ops, k, metric=w["metric"], center=w["center"], div_eps=w["eps"],
                           mi_bins=w["bins"], shard_id=rank, n_shards=world)
+        return gather_merge(res)
+
+    def gather_merge(res):
         if world == 1:
             return res
         # all-gather every shard's candidates over NCCL, then the deterministic merge
@@ -516,9 +519,12 @@ def run_ours(args):
     result = step()
 
     # e2e: the same step through the C ABI from pinned host buffers, upload included
+    # (gafime_allpairs_topk_host: the copy of each column block overlapped with the scoring
+    # of the tiles it completes)
     def e2e_step():
-        bucket.upload_packed(packed, mask)
-        return step()
+        res = bucket.topk_from_host(packed, ops, k, metric=w["metric"], center=w["center"], div_eps=w["eps"],
+                                    mi_bins=w["bins"], shard_id=rank, n_shards=world, mask=mask)
+        return gather_merge(res)
 
     for _ in range(max(1, args.warmup // 2)):
         e2e_step()

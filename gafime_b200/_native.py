@@ -48,6 +48,7 @@ EXPORTED = (
     "gafime_pipeline_init", "gafime_pipeline_submit", "gafime_pipeline_poll", "gafime_pipeline_wait",
     "gafime_pipeline_pending", "gafime_pipeline_flush", "gafime_pipeline_free", "gafime_pearson_cuda",
     "gafime_contiguous_bucket_upload_target", "gafime_contiguous_bucket_gather", "gafime_spearman_scores",
+    "gafime_allpairs_topk_host",
 )
 
 # kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
@@ -93,6 +94,8 @@ def _bind(lib: ctypes.CDLL) -> None:
         "gafime_contiguous_bucket_upload_target": ([_vp, _vp], _i),
         "gafime_contiguous_bucket_gather": ([_vp, _vp, _vp, ctypes.c_int32, _vp, _i64], _i),
         "gafime_spearman_scores": ([_vp, _vp, _vp, _i64, _i, _i, _f, _vp], _i),
+        "gafime_allpairs_topk_host": ([_vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _i, _i, _vp, _vp, _vp, _vp],
+                                      _i),
         "gafime_allpairs_scores_noalloc": ([_vp, _i64, _vp, _i, _i, _i, _f, _vp, _vp], _i),
         "gafime_unary_scores": ([_vp, _i, _i, _vp], _i),
         "gafime_shard_tiles": ([_i, _i, _i, _vp, _i, _ip], _i),
@@ -247,6 +250,32 @@ class Bucket:
         check("gafime_allpairs_topk", self.lib.gafime_allpairs_topk(
             self.handle, _ptr(ids), n_ops, METRIC[metric], int(bool(center)), float(div_eps),
             int(mi_bins), int(k), int(shard_id), int(n_shards), _ptr(oi), _ptr(oj), _ptr(os_),
+            _ptr(cnt)))
+        out = {}
+        for o, name in enumerate(ops):
+            c = int(cnt[o])
+            sl = slice(o * k, o * k + c)
+            out[name] = (oi[sl].copy(), oj[sl].copy(), os_[sl].copy())
+        return out
+
+    def topk_from_host(self, packed: np.ndarray, ops: Sequence[str], k: int, metric: str = "pearson",
+                       center: bool = False, div_eps: float = 1e-8, mi_bins: int = 16, shard_id: int = 0,
+                       n_shards: int = 1, mask: Optional[np.ndarray] = None
+                       ) -> Dict[str, Tuple[np.ndarray, np.ndarray, np.ndarray]]:
+        """upload_packed(packed) + topk(...) in one call, the copy overlapped with the
+        scoring (packed: (F+1) x n float32, ideally pinned)."""
+        if packed.dtype != np.float32 or not packed.flags.c_contiguous or packed.size != (self.f + 1) * self.n:
+            raise ValueError("packed must be a C-contiguous float32 array of (F+1)*n values")
+        m = self._mask if mask is None else np.ascontiguousarray(mask, dtype=np.uint8)
+        ids = np.array([INTERACT[o] for o in ops], dtype=np.int32)
+        n_ops = len(ids)
+        oi = np.empty(n_ops * k, dtype=np.int32)
+        oj = np.empty(n_ops * k, dtype=np.int32)
+        os_ = np.empty(n_ops * k, dtype=np.float64)
+        cnt = np.zeros(n_ops, dtype=np.int32)
+        check("gafime_allpairs_topk_host", self.lib.gafime_allpairs_topk_host(
+            self.handle, _ptr(packed), _ptr(m), _ptr(ids), n_ops, METRIC[metric], int(bool(center)),
+            float(div_eps), int(mi_bins), int(k), int(shard_id), int(n_shards), _ptr(oi), _ptr(oj), _ptr(os_),
             _ptr(cnt)))
         out = {}
         for o, name in enumerate(ops):

@@ -121,6 +121,37 @@ int prepare(Bucket& b, int center, int metric, ColumnStats& cs, bool pair_scorin
     return compute_column_stats(b, centred, cs, !gram_sums);
 }
 
+// Pearson per pair of every operator from the moments of its group (0: multiply / add /
+// subtract, 1: divide) and the per-list top-k (or every score into all_scores).
+int queue_epilogue(Bucket& b, const ColumnStats& cs, const TileCoord* d_tiles, int nt, const int* ops, int n_ops,
+                   const double* mom_mul, int splits_mul, const double* mom_div, int splits_div, int k_pad,
+                   int sub_lists, Cand* const* cands, double* all_scores) {
+    EpilogueArgs a;
+    memset(&a, 0, sizeof(a));
+    for (int o = 0; o < n_ops; ++o) {
+        const bool div = ops[o] == GAFIME_INTERACT_DIV;
+        a.moments[o] = div ? mom_div : mom_mul;
+        a.splits[o] = div ? splits_div : splits_mul;
+        a.op[o] = ops[o];
+        a.cands[o] = cands[o];
+    }
+    a.n_ops = n_ops;
+    a.tiles = d_tiles;
+    a.n_tiles = nt;
+    a.f = b.f;
+    a.colstats = cs.d_col;
+    a.ystats = cs.d_y;
+    a.k_pad = k_pad;
+    a.sub_lists = sub_lists;
+    a.all_scores = all_scores;
+    cudaError_t e;
+    {
+        KernelTimer timer(b.stream, GAFIME_KERNEL_EPILOGUE_TOPK);
+        e = launch_epilogue_topk(a, b.stream);
+    }
+    return status_from(e);
+}
+
 // Queue moments + epilogue for the requested operators.  cands[o] receives n_tiles *
 // sub_lists lists of k_pad entries for operator o (nullptr: no selection); mutual
 // information writes n_tiles lists.
@@ -165,30 +196,12 @@ int score_ops(Bucket& b, const ColumnStats& cs, const Plan& plan, const TileCoor
             if (e != cudaSuccess) return status_from(e);
         }
     }
-    EpilogueArgs a;
-    for (int o = 0; o < n_ops; ++o) {
-        const int grp = ops[o] == GAFIME_INTERACT_DIV ? 1 : 0;
-        a.moments[o] = mom[grp];
-        a.splits[o] = group_splits[grp];
-        a.op[o] = ops[o];
-        a.cands[o] = cands[o];
-    }
-    a.n_ops = n_ops;
-    a.tiles = d_tiles;
-    a.n_tiles = nt;
-    a.f = b.f;
-    a.colstats = cs.d_col;
-    a.ystats = cs.d_y;
-    a.k_pad = k_pad;
-    a.sub_lists = sub_lists;
-    a.all_scores = all_scores;
-    {
-        KernelTimer timer(b.stream, GAFIME_KERNEL_EPILOGUE_TOPK);
-        e = launch_epilogue_topk(a, b.stream);
-    }
-    if (e != cudaSuccess) return status_from(e);
-    return GAFIME_SUCCESS;
+    return queue_epilogue(b, cs, d_tiles, nt, ops, n_ops, mom[0], group_splits[0], mom[1], group_splits[1], k_pad,
+                          sub_lists, cands, all_scores);
 }
+
+int merge_and_copy(Bucket& b, Cand* const* cands, Cand* const* tmp, int n_lists, int k, int k_pad, int n_ops,
+                   size_t per_op, int32_t* out_i, int32_t* out_j, double* out_score, int* out_count);
 
 int upload_tiles(Bucket& b, const Plan& plan, TileCoord** d_tiles) {
     size_t bytes = std::max<size_t>(1, plan.tiles.size()) * sizeof(TileCoord);
@@ -254,8 +267,19 @@ extern "C" int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact
                    k_pad, sub_lists, cands, nullptr);
     if (st != GAFIME_SUCCESS) return st;
 
+    return merge_and_copy(b, cands, tmp, n_lists, k, k_pad, n_ops, per_op, out_i, out_j, out_score, out_count);
+}
+
+namespace gafime {
+namespace {
+
+// Merge the per-list candidates of every operator, copy the k best to the host and write
+// them in the output layout of gafime_allpairs_topk.
+int merge_and_copy(Bucket& b, Cand* const* cands, Cand* const* tmp, int n_lists, int k, int k_pad, int n_ops,
+                   size_t per_op, int32_t* out_i, int32_t* out_j, double* out_score, int* out_count) {
     std::vector<Cand> host((size_t)k_pad * n_ops);
     Cand* fin = nullptr;
+    cudaError_t e;
     {
         KernelTimer timer(b.stream, GAFIME_KERNEL_MERGE);
         e = merge_candidates(cands[0], tmp[0], n_lists, k_pad, n_ops, per_op, &fin, b.stream);
@@ -287,6 +311,9 @@ extern "C" int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact
     }
     return GAFIME_SUCCESS;
 }
+
+}  // namespace
+}  // namespace gafime
 
 extern "C" int gafime_allpairs_scores(ContiguousBucket bucket, int interact_type, int metric,
                                       int center, float div_eps, int mi_bins, double* out_scores) {
@@ -379,4 +406,173 @@ extern "C" int gafime_shard_tiles(int n_features, int shard_id, int n_shards, in
         out_tiles[2 * q + 1] = t[q].bj;
     }
     return GAFIME_SUCCESS;
+}
+
+// ---- streamed ingest: the host copy overlapped with scoring -------------------------------
+
+namespace gafime {
+namespace {
+
+// 128-column block whose arrival completes a 64-tile (the later of its two blocks)
+int arrival_block(const TileCoord& t) { return std::max(t.bi, t.bj) / 2; }
+
+cudaError_t ensure_copy_stream(Bucket& b, size_t n_events) {
+    cudaError_t e = cudaSuccess;
+    if (!b.copy_stream) e = cudaStreamCreateWithFlags(&b.copy_stream, cudaStreamNonBlocking);
+    while (e == cudaSuccess && b.arrived.size() < n_events) {
+        cudaEvent_t ev;
+        e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+        if (e == cudaSuccess) b.arrived.push_back(ev);
+    }
+    return e;
+}
+
+// Upload + top-k with the copy of column block J overlapped with the scoring of the tiles
+// that block J completes.  Same results as gafime_contiguous_bucket_upload followed by
+// gafime_allpairs_topk (the per-column statistics and every tile's moments are computed by
+// the same kernels on the same data; only the launch order differs).
+int streamed_topk(Bucket& b, const float* h_data, const uint8_t* h_mask, const int* ops, int n_ops, float div_eps,
+                  int k, int shard_id, int n_shards, int32_t* out_i, int32_t* out_j, double* out_score,
+                  int* out_count) {
+    const int64_t f = b.f, n = b.n, ld = b.ld;
+    constexpr int64_t kBlock = 2 * kTile;  // the 128-column block of the tensor-core Gram tile
+    const int nb = (int)((f + kBlock - 1) / kBlock);
+    cudaError_t e = ensure_copy_stream(b, (size_t)nb + 1);
+    if (e != cudaSuccess) return status_from(e);
+    // the target and the fold mask first, then the column blocks in order
+    float* y = b.d_data + f * ld;
+    e = cudaMemcpyAsync(y, h_data + f * n, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, b.copy_stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(b.d_mask, h_mask, (size_t)n, cudaMemcpyHostToDevice, b.copy_stream);
+    if (e == cudaSuccess) e = cudaEventRecord(b.arrived[(size_t)nb], b.copy_stream);
+    for (int J = 0; J < nb && e == cudaSuccess; ++J) {
+        const int64_t c0 = (int64_t)J * kBlock, c1 = std::min<int64_t>(f, c0 + kBlock);
+        e = cudaMemcpy2DAsync(b.d_data + c0 * ld, (size_t)ld * sizeof(float), h_data + c0 * n,
+                              (size_t)n * sizeof(float), (size_t)n * sizeof(float), (size_t)(c1 - c0),
+                              cudaMemcpyHostToDevice, b.copy_stream);
+        if (e == cudaSuccess) e = cudaEventRecord(b.arrived[(size_t)J], b.copy_stream);
+    }
+    if (e != cudaSuccess) return status_from(e);
+    b.finite_state = -1;
+
+    // tiles of this shard ordered by the block that completes them
+    Plan plan = make_plan(b, shard_id, n_shards);
+    std::stable_sort(plan.tiles.begin(), plan.tiles.end(),
+                     [](const TileCoord& x, const TileCoord& z) { return arrival_block(x) < arrival_block(z); });
+    const int nt = (int)plan.tiles.size();
+    if (nt == 0) {
+        // nothing to score on this shard: the upload alone, checked as an upload is
+        e = cudaStreamSynchronize(b.copy_stream);
+        if (e != cudaSuccess) return status_from(e);
+        bool finite = true;
+        return check_finite(b, &finite);
+    }
+    // the row chunks the whole tile set would get (same partial sums as an unstreamed call)
+    const int64_t chunk = gram_chunk_rows(b, gram_tiles128(plan.tiles));
+    TileCoord* d_tiles = nullptr;
+    int st = upload_tiles(b, plan, &d_tiles);
+    if (st != GAFIME_SUCCESS) return st;
+    e = ensure(b.flags, 64);
+    if (e != cudaSuccess) return status_from(e);
+    int* flag = (int*)b.flags.ptr;
+    e = cudaMemsetAsync(flag, 0, sizeof(int), b.stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(b.stream, b.arrived[(size_t)nb], 0);
+    if (e == cudaSuccess) e = launch_finite_check(y, ld, flag, b.sm_count, b.stream);
+    if (e != cudaSuccess) return status_from(e);
+    ColumnStats cs;
+    {
+        KernelTimer timer(b.stream, GAFIME_KERNEL_COLUMN_STATS);
+        st = compute_column_stats(b, false, cs, false);  // the target's statistics; columns below
+    }
+    if (st != GAFIME_SUCCESS) return st;
+    e = gram_prep_target(b, cs, b.stream);
+    if (e != cudaSuccess) return status_from(e);
+
+    bool need[2] = {false, false};
+    for (int o = 0; o < n_ops; ++o) need[ops[o] == GAFIME_INTERACT_DIV ? 1 : 0] = true;
+    const size_t per_tile = (size_t)3 * kTilePairs;
+    e = ensure(b.moments, 2 * std::max(1, nt) * per_tile * sizeof(double));
+    if (e != cudaSuccess) return status_from(e);
+    double* mom[2] = {(double*)b.moments.ptr, (double*)b.moments.ptr + std::max(1, nt) * per_tile};
+    int t0 = 0;
+    for (int J = 0; J < nb; ++J) {
+        const int64_t c0 = (int64_t)J * kBlock, c1 = std::min<int64_t>(f, c0 + kBlock);
+        e = cudaStreamWaitEvent(b.stream, b.arrived[(size_t)J], 0);
+        if (e == cudaSuccess) e = launch_finite_check(b.d_data + c0 * ld, (c1 - c0) * ld, flag, b.sm_count, b.stream);
+        if (e == cudaSuccess) e = gram_prep_columns(b, cs, need[1], div_eps, c0, c1, b.stream);
+        if (e != cudaSuccess) return status_from(e);
+        int t1 = t0;
+        while (t1 < nt && arrival_block(plan.tiles[(size_t)t1]) == J) ++t1;
+        if (t1 == t0) continue;
+        const std::vector<TileCoord> sub(plan.tiles.begin() + t0, plan.tiles.begin() + t1);
+        for (int g2 = 0; g2 < 2; ++g2) {
+            if (!need[g2]) continue;
+            int gerr = 0;
+            e = launch_gram_moments(b, cs, d_tiles + t0, sub, g2 == 1, div_eps, mom[g2] + (size_t)t0 * per_tile,
+                                    b.stream, &gerr, GRAM_PREP_DONE, chunk);
+            if (e != cudaSuccess) return status_from(e);
+            if (gerr) return GAFIME_ERROR_KERNEL_FAILED;
+        }
+        t0 = t1;
+    }
+    e = cudaStreamSynchronize(b.copy_stream);
+    if (e != cudaSuccess) return status_from(e);
+
+    const int k_pad = next_pow2(k);
+    const int sub_lists = epilogue_sub_lists(nt, k_pad, b.sm_count);
+    const int n_lists = nt * sub_lists;
+    const size_t per_op = (size_t)n_lists * k_pad;
+    e = ensure(b.cands, per_op * n_ops * sizeof(Cand));
+    if (e == cudaSuccess) e = ensure(b.cands2, per_op * n_ops * sizeof(Cand));
+    if (e != cudaSuccess) return status_from(e);
+    Cand* cands[4];
+    Cand* tmp[4];
+    for (int o = 0; o < n_ops; ++o) {
+        cands[o] = (Cand*)b.cands.ptr + per_op * o;
+        tmp[o] = (Cand*)b.cands2.ptr + per_op * o;
+    }
+    st = queue_epilogue(b, cs, d_tiles, nt, ops, n_ops, mom[0], 1, mom[1], 1, k_pad, sub_lists, cands, nullptr);
+    if (st != GAFIME_SUCCESS) return st;
+    st = merge_and_copy(b, cands, tmp, n_lists, k, k_pad, n_ops, per_op, out_i, out_j, out_score, out_count);
+    if (st != GAFIME_SUCCESS) return st;
+    // the ingest check of an upload: results over non-finite data are discarded
+    int h = 0;
+    e = cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, b.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b.stream);
+    if (e != cudaSuccess) return status_from(e);
+    b.finite_state = h == 0 ? 1 : 0;
+    if (h != 0) {
+        for (int o = 0; o < n_ops; ++o) out_count[o] = 0;
+        return GAFIME_ERROR_INVALID_ARGS;
+    }
+    return GAFIME_SUCCESS;
+}
+
+}  // namespace
+}  // namespace gafime
+
+extern "C" int gafime_allpairs_topk_host(ContiguousBucket bucket, const float* h_data, const uint8_t* h_mask,
+                                         const int* interact_types, int n_ops, int metric, int center,
+                                         float div_eps, int mi_bins, int k, int shard_id, int n_shards,
+                                         int32_t* out_i, int32_t* out_j, double* out_score, int* out_count) {
+    if (!bucket || !h_data || !h_mask || !interact_types || n_ops < 1 || n_ops > 4 || k < 1 ||
+        k > GAFIME_ALLPAIRS_MAX_K || n_shards < 1 || shard_id < 0 || shard_id >= n_shards || !out_i || !out_j ||
+        !out_score || !out_count)
+        return GAFIME_ERROR_INVALID_ARGS;
+    if (metric != GAFIME_METRIC_PEARSON && metric != GAFIME_METRIC_MUTUAL_INFO) return GAFIME_ERROR_INVALID_ARGS;
+    if (metric == GAFIME_METRIC_MUTUAL_INFO && (mi_bins < 2 || mi_bins > 255)) return GAFIME_ERROR_INVALID_ARGS;
+    if (!(div_eps > 0.0f)) return GAFIME_ERROR_INVALID_ARGS;
+    for (int o = 0; o < n_ops; ++o)
+        if (!valid_op(interact_types[o])) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket& b = *(Bucket*)bucket;
+    if (b.f >= 65536) return GAFIME_ERROR_INVALID_ARGS;
+    cudaSetDevice(b.device);
+    for (int o = 0; o < n_ops; ++o) out_count[o] = 0;
+    // the tensor-core Pearson path streams; the others score after a plain upload
+    if (metric == GAFIME_METRIC_PEARSON && center == 0 && gram_path_enabled(b) && b.f >= 2)
+        return streamed_topk(b, h_data, h_mask, interact_types, n_ops, div_eps, k, shard_id, n_shards, out_i,
+                             out_j, out_score, out_count);
+    int st = gafime_contiguous_bucket_upload(bucket, h_data, h_mask);
+    if (st != GAFIME_SUCCESS) return st;
+    return gafime_allpairs_topk(bucket, interact_types, n_ops, metric, center, div_eps, mi_bins, k, shard_id,
+                                n_shards, out_i, out_j, out_score, out_count);
 }

@@ -335,6 +335,11 @@ __global__ void finite4_kernel(const float4* __restrict__ x, int64_t n4, int* __
     if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(flag, 1);
 }
 
+cudaError_t launch_finite_check(const float* x, int64_t n_floats, int* flag, int blocks, cudaStream_t stream) {
+    finite4_kernel<<<blocks, 256, 0, stream>>>((const float4*)x, n_floats / 4, flag);
+    return cudaGetLastError();
+}
+
 // Checks the bucket's features and target once per upload (the result is kept until the
 // next upload replaces the data).
 int check_finite(Bucket& b, bool* all_finite) {
@@ -610,12 +615,17 @@ int gafime_contiguous_bucket_free(ContiguousBucket bucket) {
     cudaSetDevice(b->device);
     if (b->stream) cudaStreamSynchronize(b->stream);
     DeviceBuf* bufs[] = {&b->stats_part, &b->stats, &b->ycen, &b->xcen, &b->moments, &b->cands,
-                         &b->cands2, &b->scores, &b->flags, &b->tiles, &b->mi, &b->mi_hist, &b->mi_mm, &b->mi_xs, &b->mi_split, &b->gather, &b->rank,
+                         &b->cands2, &b->scores, &b->flags, &b->tiles, &b->mi, &b->mi_hist, &b->mi_mm, &b->mi_xs, &b->mi_split, &b->gather, &b->rank, &b->gram_cols,
                          &b->gram};
     for (DeviceBuf* d : bufs) release(*d);
     if (b->d_data) cudaFree(b->d_data);
     if (b->d_mask) cudaFree(b->d_mask);
     if (b->h_pinned) cudaFreeHost(b->h_pinned);
+    for (cudaEvent_t ev : b->arrived) cudaEventDestroy(ev);
+    if (b->copy_stream) {
+        cudaStreamSynchronize(b->copy_stream);
+        cudaStreamDestroy(b->copy_stream);
+    }
     if (b->stream) cudaStreamDestroy(b->stream);
     delete b;
     return GAFIME_SUCCESS;

@@ -47,12 +47,14 @@ struct Bucket {
     float* d_data = nullptr;   // (f + 1) * ld floats: features then target
     uint8_t* d_mask = nullptr; // n bytes
     cudaStream_t stream = nullptr;
+    cudaStream_t copy_stream = nullptr;       // host-to-device copies of a streamed call
+    std::vector<cudaEvent_t> arrived;         // one per column block (+ the target) of it
     double* h_pinned = nullptr;  // small pinned staging for stats
     int finite_state = -1;       // -1 unknown, 0 some value is NaN/inf, 1 all finite (per upload)
     int sm_count = 148;
     // scratch
     DeviceBuf stats_part, stats, ycen, xcen, moments, cands, cands2, scores, flags, tiles, mi,
-        mi_hist, mi_mm, mi_xs, mi_split, gather, rank, gram;
+        mi_hist, mi_mm, mi_xs, mi_split, gather, rank, gram, gram_cols;
 };
 
 // Grow a scratch buffer to at least `bytes`; returns cudaSuccess or an error.
@@ -75,6 +77,8 @@ int compute_column_stats(Bucket& b, bool centred, ColumnStats& out, bool x_sums 
 
 // Finite-input check over the features and y, run once per upload and cached.
 int check_finite(Bucket& b, bool* all_finite);
+// flag |= 1 when any of n_floats (a multiple of 4, 16-byte aligned) is NaN or infinite
+cudaError_t launch_finite_check(const float* x, int64_t n_floats, int* flag, int blocks, cudaStream_t stream);
 
 // Column-statistics kernels of bucket.cu, declared for other translation units.
 __global__ void col_partial_kernel(const float* __restrict__ x, int64_t ld, int64_t n,
@@ -104,9 +108,21 @@ cudaError_t launch_pair_moments(const float* d_x, int64_t ld, const float* d_yce
 // those of both groups (a divide group follows), GRAM_PREP_DONE reuses them.
 enum { GRAM_PREP_OWN = 0, GRAM_PREP_BOTH = 1, GRAM_PREP_DONE = 2 };
 bool gram_path_enabled(const Bucket& b);
+// Per-column preparation of the Gram path, split so a streamed call can prepare column
+// blocks as they arrive: the scaled target once (after the target statistics), then the
+// statistics and operand scales of columns [c0, c1) (recip: the divide side's too).
+cudaError_t gram_prep_target(Bucket& b, const ColumnStats& cs, cudaStream_t stream);
+cudaError_t gram_prep_columns(Bucket& b, const ColumnStats& cs, bool recip, float eps, int64_t c0, int64_t c1,
+                              cudaStream_t stream);
+// chunk_rows > 0 fixes the row chunk of the tiles (a streamed call launches its tiles in
+// several sets and keeps the chunking the whole set would get: gram_chunk_rows of the
+// whole set's 128-tile count, gram_tiles128).
 cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoord* d_tiles64,
                                 const std::vector<TileCoord>& tiles64, bool recip, float eps,
-                                double* d_moments, cudaStream_t stream, int* host_err, int prep_mode);
+                                double* d_moments, cudaStream_t stream, int* host_err, int prep_mode,
+                                int64_t chunk_rows = 0);
+int64_t gram_chunk_rows(const Bucket& b, int ctas_per_chunk);
+int gram_tiles128(const std::vector<TileCoord>& tiles64);
 
 // Scoring epilogue + per-tile top-k (select.cu).
 struct EpilogueArgs {

@@ -1048,6 +1048,7 @@ struct GramColPart {
 
 constexpr int kStatCols = 4;        // columns per CTA of the statistics pass
 constexpr int kStatColsRecip = 2;   // ... when g = 1/safe(x) is accumulated too
+constexpr int kMaxStatSplits = 64;  // row spans per column of the statistics pass
 
 __device__ __forceinline__ double warp_sum(double v) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -1116,10 +1117,11 @@ __device__ __forceinline__ void stat_pass(const float4 (&xv)[kCB][2], const floa
 // order, so the result does not depend on timing.
 template <int kCB, bool kRecip>
 __global__ void __launch_bounds__(256) gram_stats_kernel(const float* __restrict__ x, int64_t ld, int64_t n,
-                                                         int64_t f, const float* __restrict__ ycen, float eps,
-                                                         int64_t span, GramColPart* part) {
+                                                         int64_t c_base, int64_t f, const float* __restrict__ ycen,
+                                                         float eps, int64_t span, GramColPart* part) {
+    // columns c_base + blockIdx.x * kCB + (0 .. kCB-1), those below f
     __shared__ double red[8][kCB][10];
-    const int64_t c0 = (int64_t)blockIdx.x * kCB;
+    const int64_t c0 = c_base + (int64_t)blockIdx.x * kCB;
     const int s = blockIdx.y, splits = gridDim.y;
     const int64_t rb = (int64_t)s * span, re = min(rb + span, ld);   // span: a multiple of 2048
     float mn[kCB], mx[kCB], gmn[kCB], gmx[kCB];
@@ -1183,7 +1185,7 @@ __global__ void __launch_bounds__(256) gram_stats_kernel(const float* __restrict
 struct GramScaleArgs {
     const GramColPart* part;
     int splits;
-    int64_t f, n;
+    int64_t c_base, f, n;     // columns c_base .. f-1
     double* colstats;
     const unsigned* ycen_absmax;   // bits of max |ycen| (a non-negative float)
     int recip;
@@ -1208,7 +1210,7 @@ __device__ __forceinline__ double ycen_scale(const unsigned* bits) {
 }
 
 __global__ void gram_scale_kernel(GramScaleArgs a) {
-    int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t c = a.c_base + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= a.f) return;
     double mn = INFINITY, mx = -INFINITY, sg = 0, sgg = 0, sgy = 0, gmn = INFINITY, gmx = -INFINITY;
     double sx = 0, sxx = 0, sxy = 0;
@@ -1406,9 +1408,104 @@ bool gram_path_enabled(const Bucket& b) {
     return major == 10 && encode_fn() != nullptr;
 }
 
+// Per-column state of one scoring call on the Gram path (statistics partials, operand
+// scales and means, the scaled target, the error flag), independent of the tile set.
+struct GramCols {
+    GramColPart* colp;   // [f][kMaxStatSplits]
+    double* cs;          // [f][12]
+    float* ys;           // [ld]
+    int* err;
+    unsigned* absmax;
+};
+
+cudaError_t gram_cols(Bucket& b, GramCols& g) {
+    const int64_t f = b.f, ld = b.ld;
+    const size_t off_cs = ((size_t)f * kMaxStatSplits * sizeof(GramColPart) + 255) / 256 * 256;
+    const size_t off_ys = (off_cs + (size_t)f * 12 * sizeof(double) + 255) / 256 * 256;
+    const size_t off_err = (off_ys + (size_t)ld * sizeof(float) + 255) / 256 * 256;
+    cudaError_t e = ensure(b.gram_cols, off_err + 256);
+    if (e != cudaSuccess) return e;
+    char* base = (char*)b.gram_cols.ptr;
+    g.colp = (GramColPart*)base;
+    g.cs = (double*)(base + off_cs);
+    g.ys = (float*)(base + off_ys);
+    g.err = (int*)(base + off_err);
+    g.absmax = (unsigned*)(base + off_err + 64);
+    return cudaSuccess;
+}
+
+cudaError_t gram_prep_target(Bucket& b, const ColumnStats& cs, cudaStream_t stream) {
+    GramCols g;
+    cudaError_t e = gram_cols(b, g);
+    if (e != cudaSuccess) return e;
+    KernelTimer timer(stream, GAFIME_KERNEL_GRAM_PREP);
+    e = cudaMemsetAsync(g.absmax, 0, sizeof(unsigned), stream);
+    if (e != cudaSuccess) return e;
+    absmax_kernel<<<2 * b.sm_count, 256, 0, stream>>>(cs.d_ycen, b.ld, g.absmax);
+    scale_rows_kernel<<<2 * b.sm_count, 256, 0, stream>>>(cs.d_ycen, b.ld, g.absmax, g.ys);
+    return cudaGetLastError();
+}
+
+cudaError_t gram_prep_columns(Bucket& b, const ColumnStats& cs, bool recip, float eps, int64_t c0, int64_t c1,
+                              cudaStream_t stream) {
+    // one pass over columns [c0, c1): column sums (the epilogue's statistics) and ranges (and
+    // the divide side's sums) -> power-of-two scales; no host round trip.  About 8 CTAs
+    // per SM, row spans of whole 2048-row passes.
+    if (c1 <= c0) return cudaSuccess;
+    GramCols g;
+    cudaError_t e = gram_cols(b, g);
+    if (e != cudaSuccess) return e;
+    const int64_t ld = b.ld, n = b.n;
+    // the row spans follow from the whole matrix's column count, so a column's sums are the
+    // same whichever range it is prepared in
+    const int stat_cols = recip ? kStatColsRecip : kStatCols;
+    const int64_t col_groups = (c1 - c0 + stat_cols - 1) / stat_cols;
+    const int64_t all_groups = (b.f + stat_cols - 1) / stat_cols;
+    int splits = (int)std::max<int64_t>(1, std::min<int64_t>((8 * (int64_t)b.sm_count + all_groups - 1) / all_groups,
+                                                             (ld + 2047) / 2048));
+    splits = std::min(splits, kMaxStatSplits);
+    const int64_t span = ((ld + splits - 1) / splits + 2047) / 2048 * 2048;
+    KernelTimer timer(stream, GAFIME_KERNEL_GRAM_PREP);
+    if (recip)
+        gram_stats_kernel<kStatColsRecip, true><<<dim3((unsigned)col_groups, (unsigned)splits), 256, 0, stream>>>(
+            cs.d_x, ld, n, c0, c1, cs.d_ycen, eps, span, g.colp);
+    else
+        gram_stats_kernel<kStatCols, false><<<dim3((unsigned)col_groups, (unsigned)splits), 256, 0, stream>>>(
+            cs.d_x, ld, n, c0, c1, cs.d_ycen, eps, span, g.colp);
+    GramScaleArgs sa;
+    sa.part = g.colp;
+    sa.splits = splits;
+    sa.c_base = c0;
+    sa.f = c1;
+    sa.n = n;
+    sa.colstats = const_cast<double*>(cs.d_col);
+    sa.ycen_absmax = g.absmax;
+    sa.recip = recip ? 1 : 0;
+    sa.cs = g.cs;
+    gram_scale_kernel<<<(unsigned)((c1 - c0 + 127) / 128), 128, 0, stream>>>(sa);
+    return cudaGetLastError();
+}
+
+int64_t gram_chunk_rows(const Bucket& b, int ctas_per_chunk) {
+    // row chunks: <= max_chunk_rows() rows, enough CTAs for every SM
+    const int64_t ld = b.ld;
+    const int64_t want = std::max<int64_t>(1, (4 * (int64_t)b.sm_count + ctas_per_chunk - 1) / std::max(1, ctas_per_chunk));
+    int64_t chunk = (ld + want - 1) / want;
+    chunk = std::min<int64_t>(max_chunk_rows(), std::max<int64_t>(1024, chunk));
+    return (chunk + kRowPad - 1) / kRowPad * kRowPad;
+}
+
+int gram_tiles128(const std::vector<TileCoord>& tiles64) {
+    std::vector<std::pair<int, int>> t;
+    for (const TileCoord& c : tiles64) t.push_back({c.bi >> 1, c.bj >> 1});
+    std::sort(t.begin(), t.end());
+    return (int)(std::unique(t.begin(), t.end()) - t.begin());
+}
+
 cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoord* d_tiles64,
                                 const std::vector<TileCoord>& tiles64, bool recip, float eps,
-                                double* d_moments, cudaStream_t stream, int* host_err, int prep_mode) {
+                                double* d_moments, cudaStream_t stream, int* host_err, int prep_mode,
+                                int64_t chunk_rows) {
     *host_err = 0;
     const int64_t f = b.f, ld = b.ld, n = b.n;
     const int nb128 = (int)((f + kGT - 1) / kGT);
@@ -1446,79 +1543,43 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
         }
     }
     const int ctas_per_chunk = pairs_on ? 2 * (int)pairs.size() : nt;
-    // row chunks: <= max_chunk_rows() rows, enough CTAs for every SM
-    int64_t want = std::max<int64_t>(1, (4 * (int64_t)b.sm_count + ctas_per_chunk - 1) / ctas_per_chunk);
-    int64_t chunk = (ld + want - 1) / want;
-    chunk = std::min<int64_t>(max_chunk_rows(), std::max<int64_t>(1024, chunk));
-    chunk = (chunk + kRowPad - 1) / kRowPad * kRowPad;
+    const int64_t chunk = chunk_rows > 0 ? chunk_rows : gram_chunk_rows(b, ctas_per_chunk);
     const int n_chunks = (int)((ld + chunk - 1) / chunk);
 
-    // scratch: partial | lut | tiles128 | colparts | cs | err/absmax (same layout for both
-    // moment groups of one call, so the second group reuses the first one's statistics)
+    // scratch of this tile set: partial | lut | tiles128 | pairs; the per-column state (scales,
+    // scaled target, error flag) lives in its own buffer, shared by both moment groups of a
+    // call and by every tile set of a streamed call
     size_t part_bytes = (size_t)n_chunks * nt * 3 * kGT * kGT * sizeof(float);
     size_t off_lut = (part_bytes + 255) / 256 * 256;
     size_t off_t128 = (off_lut + lut.size() * sizeof(int) + 255) / 256 * 256;
-    // statistics pass: about 8 CTAs per SM, row spans of whole 2048-row passes
-    const int stat_cols = (recip || prep_mode == GRAM_PREP_BOTH) ? kStatColsRecip : kStatCols;
-    const int64_t col_groups = (f + stat_cols - 1) / stat_cols;
-    int splits = (int)std::max<int64_t>(1, std::min<int64_t>((8 * (int64_t)b.sm_count + col_groups - 1) / col_groups,
-                                                             (ld + 2047) / 2048));
-    splits = std::min(splits, 256);
     size_t off_pairs = (off_t128 + t128.size() * sizeof(TileCoord) + 255) / 256 * 256;
-    size_t off_colp = (off_pairs + t128.size() * sizeof(PairCoord) + 255) / 256 * 256;
-    size_t off_cs = (off_colp + (size_t)f * splits * sizeof(GramColPart) + 255) / 256 * 256;
-    size_t off_ys = (off_cs + (size_t)f * 12 * sizeof(double) + 255) / 256 * 256;
-    size_t off_err = (off_ys + (size_t)ld * sizeof(float) + 255) / 256 * 256;
-    size_t total = off_err + 256;
+    size_t total = (off_pairs + t128.size() * sizeof(PairCoord) + 255) / 256 * 256;
     cudaError_t e = ensure(b.gram, total);
+    if (e != cudaSuccess) return e;
+    GramCols gc;
+    e = gram_cols(b, gc);
     if (e != cudaSuccess) return e;
     char* base = (char*)b.gram.ptr;
     float* partial = (float*)base;
     int* d_lut = (int*)(base + off_lut);
     TileCoord* d_t128 = (TileCoord*)(base + off_t128);
     PairCoord* d_pairs = (PairCoord*)(base + off_pairs);
-    GramColPart* colp = (GramColPart*)(base + off_colp);
-    double* d_cs = (double*)(base + off_cs);
-    float* d_ys = (float*)(base + off_ys);
-    int* d_err = (int*)(base + off_err);
-    unsigned* d_absmax = (unsigned*)(base + off_err + 64);
+    double* d_cs = gc.cs;
+    float* d_ys = gc.ys;
+    int* d_err = gc.err;
 
     e = cudaMemcpyAsync(d_lut, lut.data(), lut.size() * sizeof(int), cudaMemcpyHostToDevice, stream);
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(d_t128, t128.data(), t128.size() * sizeof(TileCoord), cudaMemcpyHostToDevice, stream);
     if (e == cudaSuccess && pairs_on)
         e = cudaMemcpyAsync(d_pairs, pairs.data(), pairs.size() * sizeof(PairCoord), cudaMemcpyHostToDevice, stream);
-    if (e == cudaSuccess) e = cudaMemsetAsync(d_err, 0, 128, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(d_err, 0, 64, stream);  // the flag only: absmax follows at +64
     if (e != cudaSuccess) return e;
 
     if (prep_mode != GRAM_PREP_DONE) {
-        // one pass over the columns: column sums (the epilogue's statistics) and ranges (and
-        // the divide side's sums) -> power-of-two scales; no host round trip
-        const bool both = prep_mode == GRAM_PREP_BOTH;
-        const int64_t span = ((ld + splits - 1) / splits + 2047) / 2048 * 2048;
-        KernelTimer timer(stream, GAFIME_KERNEL_GRAM_PREP);
-        e = cudaMemsetAsync(d_absmax, 0, sizeof(unsigned), stream);
-        if (e != cudaSuccess) return e;
-        absmax_kernel<<<2 * b.sm_count, 256, 0, stream>>>(cs.d_ycen, ld, d_absmax);
-        if (recip || both)
-            gram_stats_kernel<kStatColsRecip, true><<<dim3((unsigned)((f + kStatColsRecip - 1) / kStatColsRecip),
-                                                          (unsigned)splits),
-                                                     256, 0, stream>>>(cs.d_x, ld, n, f, cs.d_ycen, eps, span, colp);
-        else
-            gram_stats_kernel<kStatCols, false><<<dim3((unsigned)((f + kStatCols - 1) / kStatCols), (unsigned)splits),
-                                                  256, 0, stream>>>(cs.d_x, ld, n, f, cs.d_ycen, eps, span, colp);
-        GramScaleArgs sa;
-        sa.part = colp;
-        sa.splits = splits;
-        sa.f = f;
-        sa.n = n;
-        sa.colstats = const_cast<double*>(cs.d_col);
-        sa.ycen_absmax = d_absmax;
-        sa.recip = (recip || both) ? 1 : 0;
-        sa.cs = d_cs;
-        gram_scale_kernel<<<(unsigned)((f + 127) / 128), 128, 0, stream>>>(sa);
-        scale_rows_kernel<<<2 * b.sm_count, 256, 0, stream>>>(cs.d_ycen, ld, d_absmax, d_ys);
-        e = cudaGetLastError();
+        e = gram_prep_target(b, cs, stream);
+        if (e == cudaSuccess)
+            e = gram_prep_columns(b, cs, recip || prep_mode == GRAM_PREP_BOTH, eps, 0, f, stream);
         if (e != cudaSuccess) return e;
     }
 

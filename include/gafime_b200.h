@@ -226,6 +226,23 @@ int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact_types, int
                          double* out_score, int* out_count);
 
 /*
+ * NEW.  gafime_contiguous_bucket_upload(bucket, h_data, h_mask) followed by
+ * gafime_allpairs_topk(bucket, ...), with the host-to-device copy overlapped with the
+ * scoring: the target goes first, then the features in 128-column blocks on a copy stream,
+ * and the tiles each block completes are scored while the next block is in flight.  The
+ * reference uploads the whole bucket before any launch (native_cuda_backend.py:339-352,
+ * contiguous_layout.rs:64-156).  h_data is the upload's layout ([F0 | ... | F_{F-1} | y],
+ * n floats each); pinned host memory is what lets the copies overlap.  Same results as the
+ * two calls (the same kernels on the same data and row chunks); non-finite input returns
+ * GAFIME_ERROR_INVALID_ARGS like the upload's check.  Pearson with center = 0 on the
+ * tensor-core path streams; other metrics and modes run the two calls.
+ */
+int gafime_allpairs_topk_host(ContiguousBucket bucket, const float* h_data, const uint8_t* h_mask,
+                              const int* interact_types, int n_ops, int metric, int center,
+                              float div_eps, int mi_bins, int k, int shard_id, int n_shards,
+                              int32_t* out_i, int32_t* out_j, double* out_score, int* out_count);
+
+/*
  * NEW.  Signed score of every pair i<j for one operator, in row-major
  * upper-triangle order (p = i*F - i*(i+1)/2 + j - i - 1), P = F*(F-1)/2 entries.
  * Serves Backend.score_combos (gafime/backends/base.py:67-78) when the combo list

@@ -487,3 +487,50 @@ def test_mi_min_max_filter_edge_columns(native, oracle):
     with bucket_for(native, X, y) as b:
         got = b.scores("multiply", metric="mutual_info", center=True, mi_bins=16)
     np.testing.assert_allclose(got, want, rtol=0, atol=1e-5)
+
+
+@pytest.mark.parametrize("n,f", [(5000, 300), (20000, 129), (777, 64), (3000, 2), (40000, 256)])
+def test_streamed_upload_topk_equals_upload_then_topk(native, n, f):
+    """The copy of each 128-column block overlapped with the tiles it completes: the same
+    statistics, row chunks and moments as upload + topk, so bit-identical results."""
+    rng = np.random.default_rng(n + f)
+    X = np.hstack([rng.standard_normal((n, f - f // 2)), rng.lognormal(0, 1, (n, f // 2))]).astype(np.float32)
+    y = (X[:, 0] * X[:, f - 1] + rng.standard_normal(n) > 0).astype(np.float32)
+    packed = native.pack_columns(X, y)
+    k = min(50, f * (f - 1) // 2)
+    for ops in (OPS, ["multiply"], ["divide"]):
+        with native.Bucket(n, f) as a, native.Bucket(n, f) as s:
+            a.upload_packed(packed)
+            want = a.topk(ops, k, div_eps=1e-6)
+            got = s.topk_from_host(packed, ops, k, div_eps=1e-6)
+            for op in ops:
+                for u, v in zip(got[op], want[op]):
+                    np.testing.assert_array_equal(u, v)
+            # the bucket holds the data afterwards, like an upload
+            np.testing.assert_array_equal(s.scores("add"), a.scores("add"))
+    with native.Bucket(n, f) as a, native.Bucket(n, f) as s:
+        a.upload_packed(packed)
+        for shard in range(3):
+            want = a.topk(["multiply"], k, shard_id=shard, n_shards=3)
+            got = s.topk_from_host(packed, ["multiply"], k, shard_id=shard, n_shards=3)
+            for u, v in zip(got["multiply"], want["multiply"]):
+                np.testing.assert_array_equal(u, v)
+
+
+def test_streamed_upload_rejects_non_finite(native):
+    rng = np.random.default_rng(9)
+    X = rng.standard_normal((1000, 140)).astype(np.float32)
+    y = rng.standard_normal(1000).astype(np.float32)
+    for where in ((3, 135), (999, 0)):
+        Xb = X.copy()
+        Xb[where] = np.nan
+        with native.Bucket(1000, 140) as s:
+            with pytest.raises(native.GafimeError) as e:
+                s.topk_from_host(native.pack_columns(Xb, y), ["multiply"], 5)
+            assert e.value.code == -1
+    yb = y.copy()
+    yb[10] = np.inf
+    with native.Bucket(1000, 140) as s:
+        with pytest.raises(native.GafimeError):
+            s.topk_from_host(native.pack_columns(X, yb), ["multiply"], 5)
+        s.topk_from_host(native.pack_columns(X, y), ["multiply"], 5)  # a finite upload clears it
