@@ -22,7 +22,11 @@ OBJ_DIR = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libgafime_cuda.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
+# -fno-tree-loop-vectorize: g++ 13.3's loop vectorizer miscompiles a short loop that fills
+# per-operator arrays from a two-entry table (a wrong element read, reproduced standalone at
+# -O3); host code here is not throughput-bound, so the host side is built without it.
+NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fno-tree-loop-vectorize",
+              "--expt-relaxed-constexpr",
               "-ccbin", "/usr/bin/g++"]
 
 
