@@ -48,7 +48,7 @@ EXPORTED = (
     "gafime_pipeline_init", "gafime_pipeline_submit", "gafime_pipeline_poll", "gafime_pipeline_wait",
     "gafime_pipeline_pending", "gafime_pipeline_flush", "gafime_pipeline_free", "gafime_pearson_cuda",
     "gafime_contiguous_bucket_upload_target", "gafime_contiguous_bucket_gather", "gafime_spearman_scores",
-    "gafime_allpairs_topk_host",
+    "gafime_allpairs_topk_host", "gafime_contiguous_bucket_upload_rows",
 )
 
 # kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
@@ -94,6 +94,7 @@ def _bind(lib: ctypes.CDLL) -> None:
         "gafime_contiguous_bucket_upload_target": ([_vp, _vp], _i),
         "gafime_contiguous_bucket_gather": ([_vp, _vp, _vp, ctypes.c_int32, _vp, _i64], _i),
         "gafime_spearman_scores": ([_vp, _vp, _vp, _i64, _i, _i, _f, _vp], _i),
+        "gafime_contiguous_bucket_upload_rows": ([_vp, _vp, _vp, _vp], _i),
         "gafime_allpairs_topk_host": ([_vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _i, _i, _vp, _vp, _vp, _vp],
                                       _i),
         "gafime_allpairs_scores_noalloc": ([_vp, _i64, _vp, _i, _i, _i, _f, _vp, _vp], _i),
@@ -204,6 +205,16 @@ class Bucket:
 
     def upload(self, X: np.ndarray, y: np.ndarray, mask: Optional[np.ndarray] = None) -> None:
         self.upload_packed(pack_columns(X, y), mask)
+
+    def upload_rows(self, X: np.ndarray, y: np.ndarray, mask: Optional[np.ndarray] = None) -> None:
+        """Upload a row-major (n, F) matrix; the transpose to columns runs on the device."""
+        Xr = np.ascontiguousarray(X, dtype=np.float32)
+        yv = np.ascontiguousarray(y, dtype=np.float32)
+        if Xr.shape != (self.n, self.f) or yv.shape != (self.n,):
+            raise ValueError(f"X must be ({self.n}, {self.f}) and y ({self.n},)")
+        m = self._mask if mask is None else np.ascontiguousarray(mask, dtype=np.uint8)
+        check("gafime_contiguous_bucket_upload_rows",
+              self.lib.gafime_contiguous_bucket_upload_rows(self.handle, _ptr(Xr), _ptr(yv), _ptr(m)))
 
     def set_target(self, y: np.ndarray) -> None:
         """Replace only the target (n floats); the features stay resident."""

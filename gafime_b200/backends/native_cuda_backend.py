@@ -209,7 +209,7 @@ class _Resident:
         self.all_cols = tuple(range(f))
         self.full = _native.Bucket(n, f, device=device)
         try:
-            self.full.upload(X, y)
+            self.full.upload_rows(X, y)  # transposed to columns on the device
         except Exception:
             self.full.free()
             raise

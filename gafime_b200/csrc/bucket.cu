@@ -381,6 +381,26 @@ __global__ void gather_mask_kernel(const uint8_t* __restrict__ src, const int64_
         dst[r] = src[rows ? rows[r] : r];
 }
 
+// Row-major rows [r0, r0 + rows) x F (row stride F) -> the bucket's column-major layout.
+// 32 x 32 tiles through shared memory: coalesced reads along the row, coalesced writes
+// along the column.
+__global__ void __launch_bounds__(256) rows_to_columns_kernel(const float* __restrict__ src, int64_t rows,
+                                                              int64_t f, float* __restrict__ dst, int64_t ld,
+                                                              int64_t r0) {
+    __shared__ float tile[32][33];
+    const int64_t c_base = (int64_t)blockIdx.x * 32, r_base = (int64_t)blockIdx.y * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+    for (int k = ty; k < 32; k += 8) {
+        const int64_t r = r_base + k, c = c_base + tx;
+        tile[k][tx] = (r < rows && c < f) ? src[r * f + c] : 0.f;
+    }
+    __syncthreads();
+    for (int k = ty; k < 32; k += 8) {
+        const int64_t c = c_base + k, r = r_base + tx;
+        if (c < f && r < rows) dst[c * ld + r0 + r] = tile[tx][k];
+    }
+}
+
 }  // namespace gafime
 
 using namespace gafime;
@@ -496,6 +516,47 @@ int gafime_contiguous_bucket_upload(ContiguousBucket bucket, const float* h_data
     if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return status_from(e);
     // validate the new data at ingest: the all-pairs calls accept finite input only
+    b->finite_state = -1;
+    bool finite = true;
+    KernelTimer timer(b->stream, GAFIME_KERNEL_FINITE_CHECK);
+    return check_finite(*b, &finite);
+}
+
+int gafime_contiguous_bucket_upload_rows(ContiguousBucket bucket, const float* h_rows, const float* h_y,
+                                         const uint8_t* h_mask) {
+    if (!bucket || !h_rows || !h_y || !h_mask) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket* b = (Bucket*)bucket;
+    cudaSetDevice(b->device);
+    const int64_t f = b->f, n = b->n, ld = b->ld;
+    // row chunks of at most 64 MB through two staging buffers: the copy of one chunk overlaps
+    // the transpose of the previous one
+    const int64_t chunk = std::max<int64_t>(32, std::min<int64_t>(n, ((int64_t)16 << 20) / f) / 32 * 32);
+    cudaError_t e = ensure(b->gather, 2 * (size_t)chunk * f * sizeof(float));
+    if (e != cudaSuccess) return status_from(e);
+    float* stage[2] = {(float*)b->gather.ptr, (float*)b->gather.ptr + chunk * f};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    for (int s = 0; s < 2 && e == cudaSuccess; ++s) e = cudaEventCreateWithFlags(&done[s], cudaEventDisableTiming);
+    int q = 0;
+    for (int64_t r0 = 0; r0 < n && e == cudaSuccess; r0 += chunk, q ^= 1) {
+        const int64_t rows = std::min<int64_t>(chunk, n - r0);
+        // the staging buffer's previous transpose must be done before it is overwritten
+        e = cudaEventSynchronize(done[q]);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(stage[q], h_rows + r0 * f, (size_t)rows * f * sizeof(float), cudaMemcpyHostToDevice,
+                                b->stream);
+        if (e != cudaSuccess) break;
+        dim3 grid((unsigned)((f + 31) / 32), (unsigned)((rows + 31) / 32));
+        rows_to_columns_kernel<<<grid, 256, 0, b->stream>>>(stage[q], rows, f, b->d_data, ld, r0);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaEventRecord(done[q], b->stream);
+    }
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(b->d_data + f * ld, h_y, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, b->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(b->d_mask, h_mask, (size_t)n, cudaMemcpyHostToDevice, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    for (int s = 0; s < 2; ++s)
+        if (done[s]) cudaEventDestroy(done[s]);
+    if (e != cudaSuccess) return status_from(e);
     b->finite_state = -1;
     bool finite = true;
     KernelTimer timer(b->stream, GAFIME_KERNEL_FINITE_CHECK);

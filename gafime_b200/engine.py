@@ -25,7 +25,7 @@ class GafimeEngine:
 
     def analyze(self, X, y, feature_names: Optional[Iterable[str]] = None) -> DiagnosticReport:
         cfg = self.config
-        X_arr, y_arr, names = coerce_inputs(X, y, feature_names)
+        X_arr, y_arr, names = coerce_inputs(X, y, feature_names, keep_float32=True)
         warnings = validate_budget(X_arr.shape[1], cfg.budget)
         backend, more = resolve_backend(cfg, X_arr, y_arr)
         warnings.extend(more)

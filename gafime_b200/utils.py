@@ -9,8 +9,11 @@ import numpy as np
 from .config import ComputeBudget
 
 
-def coerce_inputs(X, y, feature_names: Optional[Sequence[str]] = None
+def coerce_inputs(X, y, feature_names: Optional[Sequence[str]] = None, keep_float32: bool = False
                   ) -> Tuple[np.ndarray, np.ndarray, List[str]]:
+    """The reference's checks and float64 arrays.  keep_float32: float32 input stays float32
+    (the engine's GPU path scores fp32 columns, and fp32 -> fp64 -> fp32 is the identity, so
+    the double-size copy would change nothing but the time)."""
     Xa, ya = np.asarray(X), np.asarray(y)
     if Xa.ndim != 2:
         raise ValueError("X must be a 2D array-like of shape (n_samples, n_features).")
@@ -22,8 +25,8 @@ def coerce_inputs(X, y, feature_names: Optional[Sequence[str]] = None
         raise ValueError("X and y must be numeric.")
     if not (np.isfinite(Xa).all() and np.isfinite(ya).all()):
         raise ValueError("X and y must be finite (no NaN or inf).")
-    Xa = np.ascontiguousarray(Xa, dtype=np.float64)
-    ya = np.ascontiguousarray(ya, dtype=np.float64)
+    Xa = np.ascontiguousarray(Xa, dtype=np.float32 if keep_float32 and Xa.dtype == np.float32 else np.float64)
+    ya = np.ascontiguousarray(ya, dtype=np.float32 if keep_float32 and ya.dtype == np.float32 else np.float64)
     if feature_names is None:
         names = [f"f{i}" for i in range(Xa.shape[1])]
     else:

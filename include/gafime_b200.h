@@ -325,6 +325,15 @@ int gafime_spearman_scores(ContiguousBucket bucket, const int32_t* feat_a, const
                            int64_t n_combos, int interact_type, int center, float div_eps,
                            double* out_scores);
 
+/* NEW.  gafime_contiguous_bucket_upload from the caller's row-major matrix: h_rows holds
+ * n_samples rows of n_features floats (X[i, f] at h_rows[i * n_features + f], numpy's C
+ * order), h_y n_samples floats, h_mask n_samples bytes.  The rows are copied in chunks and
+ * transposed into the bucket's column layout on the device, so the caller does not build the
+ * column-major host buffer (the reference's backend transposes on the host:
+ * native_cuda_backend.py:339-342).  Checks the data like the upload. */
+int gafime_contiguous_bucket_upload_rows(ContiguousBucket bucket, const float* h_rows, const float* h_y,
+                                         const uint8_t* h_mask);
+
 /* NEW.  Replace only the target of an uploaded bucket with n_samples floats from the host
  * (the features stay resident).  Permutation tests re-score the same matrix against
  * permuted targets; the reference re-uploads matrix and target per call

@@ -64,3 +64,12 @@ def test_gpu_backend_fails_loudly_without_a_gpu():
     from gafime_b200 import GafimeSelector
     with pytest.raises(RuntimeError):
         GafimeSelector(k=2).fit(np.random.rand(20, 4), np.random.rand(20))
+
+
+def test_coerce_keeps_float32_only_when_asked():
+    X32 = np.arange(6, dtype=np.float32).reshape(3, 2)
+    Xa, ya, _ = coerce_inputs(X32, np.ones(3, dtype=np.float32), keep_float32=True)
+    assert Xa.dtype == np.float32 and ya.dtype == np.float32
+    np.testing.assert_array_equal(Xa, X32)
+    Xb, _, _ = coerce_inputs(X32.astype(np.float64), [1, 2, 3], keep_float32=True)
+    assert Xb.dtype == np.float64

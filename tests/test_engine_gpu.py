@@ -95,7 +95,8 @@ def test_engine_uploads_the_matrix_once(golden, monkeypatch):
     from gafime_b200 import EngineConfig, GafimeEngine, _native
     from gafime_b200.config import ComputeBudget
     calls = {"upload": 0, "target": 0, "gather": 0}
-    up, tgt, gat = _native.Bucket.upload_packed, _native.Bucket.set_target, _native.Bucket.gather.__func__
+    up, rows, tgt = _native.Bucket.upload_packed, _native.Bucket.upload_rows, _native.Bucket.set_target
+    gat = _native.Bucket.gather.__func__
 
     def count(name, fn):
         def wrapped(*a, **k):
@@ -103,6 +104,7 @@ def test_engine_uploads_the_matrix_once(golden, monkeypatch):
             return fn(*a, **k)
         return wrapped
     monkeypatch.setattr(_native.Bucket, "upload_packed", count("upload", up))
+    monkeypatch.setattr(_native.Bucket, "upload_rows", count("upload", rows))
     monkeypatch.setattr(_native.Bucket, "set_target", count("target", tgt))
     monkeypatch.setattr(_native.Bucket, "gather", classmethod(count("gather", gat)))
     g = golden("engine_report.npz")

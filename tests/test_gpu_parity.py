@@ -534,3 +534,25 @@ def test_streamed_upload_rejects_non_finite(native):
         with pytest.raises(native.GafimeError):
             s.topk_from_host(native.pack_columns(X, yb), ["multiply"], 5)
         s.topk_from_host(native.pack_columns(X, y), ["multiply"], 5)  # a finite upload clears it
+
+
+@pytest.mark.parametrize("n,f", [(100_000, 256), (33, 5), (70_001, 129), (1, 3)])
+def test_upload_rows_equals_column_upload(native, n, f):
+    """Row-major upload transposed on the device: the same bucket as the column upload."""
+    rng = np.random.default_rng(n + f)
+    X = rng.standard_normal((n, f)).astype(np.float32)
+    y = rng.standard_normal(n).astype(np.float32)
+    with native.Bucket(n, f) as a, native.Bucket(n, f) as r:
+        a.upload(X, y)
+        r.upload_rows(X, y)
+        if f > 1 and n > 1:
+            np.testing.assert_array_equal(r.scores("multiply"), a.scores("multiply"))
+            np.testing.assert_array_equal(r.unary_scores(), a.unary_scores())
+        for c in range(0, f, max(1, f // 7)):
+            np.testing.assert_array_equal(r.compute_pair(c, (c + 1) % f), a.compute_pair(c, (c + 1) % f))
+    Xb = X.copy()
+    Xb[n // 2, f - 1] = np.inf
+    with native.Bucket(n, f) as r:
+        r.upload_rows(Xb, y)
+        with pytest.raises(native.GafimeError):
+            r.topk(["multiply"], 1)
