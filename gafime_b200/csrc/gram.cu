@@ -339,7 +339,8 @@ struct StepOps {
 // is a power of two).  Rows are processed in packed pairs (f32x2).
 template <bool kMask, bool kB, bool kRecip>
 __device__ __forceinline__ void convert_step(const unsigned char* raw, const unsigned char* ysm, int m, int h,
-                                             int valid, const ConvCols& k, float eps, StepOps& o) {
+                                             int valid, const ConvCols& k, float eps, StepOps& o,
+                                             int b_off = kRawBox) {
     float x[8];
     uint64_t x2[4], v2[4], t2[4];
     load_raw8(raw, m, h, x);
@@ -360,7 +361,7 @@ __device__ __forceinline__ void convert_step(const unsigned char* raw, const uns
     split8(v2, o.x);
     split8(t2, o.q);
     if (kB) {
-        load_raw8(raw + kRawBox, m, h, x);
+        load_raw8(raw + b_off, m, h, x);
         if (kRecip) {
             #pragma unroll
             for (int r = 0; r < 8; ++r) x[r] = safe_recip(x[r], eps);
@@ -407,6 +408,7 @@ struct ConvCtx {
     int64_t rows_left;           // n - first row of the chunk
     float eps;
     int* err;
+    int b_off;                   // B raw tile in a stage: kRawBox, or 0 when it is the A tile
 };
 
 // The steps k = grp, grp + kGroups, ... of one converter thread.  kB: convert the B block
@@ -420,11 +422,11 @@ __device__ __forceinline__ void conv_loop(const ConvCtx& c, const ConvCols& kc, 
         const unsigned char* ysm = c.ys0 + rs * kYsBytes;
         StepOps o;
         if (k < c.n_full) {
-            convert_step<false, kB, kRecip>(raw, ysm, c.m, c.h, kGK, kc, c.eps, o);
+            convert_step<false, kB, kRecip>(raw, ysm, c.m, c.h, kGK, kc, c.eps, o, c.b_off);
         } else {
             const int64_t left = c.rows_left - (int64_t)k * kGK;
             const int valid = left <= 0 ? 0 : (int)left;   // < kGK here
-            convert_step<true, kB, kRecip>(raw, ysm, c.m, c.h, valid, kc, c.eps, o);
+            convert_step<true, kB, kRecip>(raw, ysm, c.m, c.h, valid, kc, c.eps, o, c.b_off);
         }
         // the operand stage must be free: the MMAs of step k - kOpStages have completed
         if (k >= kOpStages && !warp_wait(c.oempty0 + 8 * os, ((k / kOpStages) - 1) & 1, c.err, 6, c.lane)) return;
@@ -474,8 +476,10 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const TileCoord tc = a.tiles[blockIdx.x];
-    // the multiply group's diagonal tiles load and convert one block (A and B are the same)
-    const bool b_same = (tc.bi == tc.bj) && !a.recip;
+    // diagonal tiles load one raw block (A and B columns are the same); the multiply group's
+    // also converts it once (its B operand is A's)
+    const bool raw_same = tc.bi == tc.bj;
+    const bool b_same = raw_same && !a.recip;
     const int64_t r0 = (int64_t)blockIdx.y * a.chunk_rows;
     const int64_t r1 = min(r0 + a.chunk_rows, a.rows);
     const int nk = r1 > r0 ? (int)((r1 - r0) / kGK) : 0;
@@ -507,7 +511,7 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
     if (warp == 0) {
         if (lane == 0) {
             // producer: raw fp32 column tiles + 16 scaled ycen values per step
-            const uint32_t bytes = (b_same ? (uint32_t)kRawBox : (uint32_t)kRawStageBytes) + (uint32_t)(kGK * 4);
+            const uint32_t bytes = (raw_same ? (uint32_t)kRawBox : (uint32_t)kRawStageBytes) + (uint32_t)(kGK * 4);
             int issued = 0;
             bool ok = true;
             for (int k = 0; k < nk; ++k) {
@@ -519,7 +523,7 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
                 const uint32_t st = smem_u32(raw0 + s * kRawStageBytes);
                 const int64_t row = r0 + (int64_t)k * kGK;
                 tma_load_2d(st, &xmap, full, (int)row, tc.bi * kGT);
-                if (!b_same) tma_load_2d(st + kRawBox, &xmap, full, (int)row, tc.bj * kGT);
+                if (!raw_same) tma_load_2d(st + kRawBox, &xmap, full, (int)row, tc.bj * kGT);
                 bulk_load(smem_u32(ys0 + s * kYsBytes), a.ys + row, (uint32_t)(kGK * 4), full);
                 ++issued;
             }
@@ -595,6 +599,7 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
         }
         cx.eps = a.eps;
         cx.err = a.err;
+        cx.b_off = raw_same ? 0 : kRawBox;
         if (b_same) conv_loop<false, false>(cx, kc, grp);
         else if (a.recip) conv_loop<true, true>(cx, kc, grp);
         else conv_loop<true, false>(cx, kc, grp);
