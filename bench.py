@@ -194,35 +194,71 @@ NCU_TRAFFIC_BYTES = {
 
 
 class ClockSampler:
+    """nvidia-smi clock and throttle-reason samples around the timed region.  Sampling runs
+    before the region starts (start() waits for the first sample) and stop() waits for one
+    sample after it ends, so even a region shorter than the sampling interval is covered;
+    the reported samples are those taken from the region's start to one interval after its
+    end (or the first one after its start when none fell inside)."""
+
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    INTERVAL_MS = 50
 
     def __init__(self, device: int):
         self.device = device
         self.proc = None
+        self.lines = []
+        self.thread = None
+        self.t_begin = self.t_end = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.monotonic(), line))
 
     def start(self):
+        import threading
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.device)],
+                 "-lms", str(self.INTERVAL_MS), "-i", str(self.device)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        deadline = time.monotonic() + 3.0
+        while not self.lines and time.monotonic() < deadline and self.proc.poll() is None:
+            time.sleep(0.005)
+
+    def begin(self):
+        self.t_begin = time.monotonic()
+
+    def end(self):
+        self.t_end = time.monotonic()
 
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        t_end = self.t_end if self.t_end is not None else time.monotonic()
+        t_begin = self.t_begin if self.t_begin is not None else t_end
+        deadline = time.monotonic() + 1.0
+        while not any(t >= t_end for t, _ in list(self.lines)) and time.monotonic() < deadline:
+            time.sleep(0.005)
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        taken = [(t, l) for t, l in self.lines if t_begin <= t <= t_end + self.INTERVAL_MS / 1e3]
+        if not taken:
+            taken = [(t, l) for t, l in self.lines if t >= t_begin][:1]
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
+        for _, line in taken:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -236,7 +272,8 @@ class ClockSampler:
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "window_ms": round((t_end - t_begin) * 1e3, 1)}
 
 
 # --------------------------------------------------------------- CPU arm ----
@@ -507,7 +544,9 @@ def run_ours(args):
     clocks = ClockSampler(local)
     clocks.start()
     _native.profile_enable(True)
+    clocks.begin()
     ms = timed(step, args.steps)
+    clocks.end()
     _native.profile_enable(False)
     kernel_ms = {}
     for kname in _native.KERNEL_IDS:
