@@ -498,20 +498,27 @@ def run_ours(args):
                           mi_bins=w["bins"], shard_id=rank, n_shards=world)
         return gather_merge(res)
 
+    # candidate exchange buffers, allocated once: pinned host staging and device tensors
+    cand_host = torch.empty(len(ops) * 3 * k, dtype=torch.float64, pin_memory=True)
+    cand_all_host = torch.empty(world * len(ops) * 3 * k, dtype=torch.float64, pin_memory=True)
+    cand_dev = torch.empty(len(ops) * 3 * k, dtype=torch.float64, device="cuda") if world > 1 else None
+    cand_all_dev = torch.empty(world * len(ops) * 3 * k, dtype=torch.float64, device="cuda") if world > 1 else None
+
     def gather_merge(res):
         if world == 1:
             return res
         # all-gather every shard's candidates over NCCL, then the deterministic merge
-        flat = np.full((len(ops), 3, k), -1.0)
+        flat = cand_host.numpy().reshape(len(ops), 3, k)
+        flat.fill(-1.0)
         for o, op in enumerate(ops):
             i, j, s = res[op]
             flat[o, 0, :len(i)] = i
             flat[o, 1, :len(j)] = j
             flat[o, 2, :len(s)] = s
-        t = torch.from_numpy(flat.reshape(-1)).cuda()
-        out = torch.empty(world * t.numel(), dtype=torch.float64, device="cuda")
-        dist.all_gather_into_tensor(out, t)
-        allc = out.cpu().numpy().reshape(world, len(ops), 3, k)
+        cand_dev.copy_(cand_host, non_blocking=True)
+        dist.all_gather_into_tensor(cand_all_dev, cand_dev)
+        cand_all_host.copy_(cand_all_dev)
+        allc = cand_all_host.numpy().reshape(world, len(ops), 3, k)
         merged = {}
         for o, op in enumerate(ops):
             c = allc[:, o].transpose(1, 0, 2).reshape(3, -1)

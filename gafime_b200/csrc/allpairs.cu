@@ -489,6 +489,9 @@ int streamed_topk(Bucket& b, const float* h_data, const uint8_t* h_mask, const i
 
     bool need[2] = {false, false};
     for (int o = 0; o < n_ops; ++o) need[ops[o] == GAFIME_INTERACT_DIV ? 1 : 0] = true;
+    // the column blocks this shard's tiles read get their statistics; the rest is only checked
+    std::vector<char> used((size_t)nb, 0);
+    for (const TileCoord& t : plan.tiles) used[(size_t)(t.bi / 2)] = used[(size_t)(t.bj / 2)] = 1;
     const size_t per_tile = (size_t)3 * kTilePairs;
     e = ensure(b.moments, 2 * std::max(1, nt) * per_tile * sizeof(double));
     if (e != cudaSuccess) return status_from(e);
@@ -498,7 +501,7 @@ int streamed_topk(Bucket& b, const float* h_data, const uint8_t* h_mask, const i
         const int64_t c0 = (int64_t)J * kBlock, c1 = std::min<int64_t>(f, c0 + kBlock);
         e = cudaStreamWaitEvent(b.stream, b.arrived[(size_t)J], 0);
         if (e == cudaSuccess) e = launch_finite_check(b.d_data + c0 * ld, (c1 - c0) * ld, flag, b.sm_count, b.stream);
-        if (e == cudaSuccess) e = gram_prep_columns(b, cs, need[1], div_eps, c0, c1, b.stream);
+        if (e == cudaSuccess && used[(size_t)J]) e = gram_prep_columns(b, cs, need[1], div_eps, c0, c1, b.stream);
         if (e != cudaSuccess) return status_from(e);
         int t1 = t0;
         while (t1 < nt && arrival_block(plan.tiles[(size_t)t1]) == J) ++t1;

@@ -1584,7 +1584,20 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     if (prep_mode != GRAM_PREP_DONE) {
         e = gram_prep_target(b, cs, stream);
         if (e == cudaSuccess)
-            e = gram_prep_columns(b, cs, recip || prep_mode == GRAM_PREP_BOTH, eps, 0, f, stream);
+        {
+            // only the 128-column blocks this call's tiles read (a shard of many GPUs needs a
+            // few of them); runs of consecutive blocks go in one launch
+            std::vector<char> used((size_t)nb128, 0);
+            for (const TileCoord& t : t128) used[(size_t)t.bi] = used[(size_t)t.bj] = 1;
+            for (int B0 = 0; B0 < nb128 && e == cudaSuccess;) {
+                if (!used[(size_t)B0]) { ++B0; continue; }
+                int B1 = B0;
+                while (B1 < nb128 && used[(size_t)B1]) ++B1;
+                e = gram_prep_columns(b, cs, recip || prep_mode == GRAM_PREP_BOTH, eps, (int64_t)B0 * kGT,
+                                      std::min<int64_t>(f, (int64_t)B1 * kGT), stream);
+                B0 = B1;
+            }
+        }
         if (e != cudaSuccess) return e;
     }
 
