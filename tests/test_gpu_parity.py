@@ -2,7 +2,7 @@
 
 Tolerances (stated per test):
   * Pearson: |r_gpu - r_oracle| <= 1e-4 * |r_oracle| + 1e-6 for every pair -- the
-    north-star bound is 1e-4 relative; the 1e-6 absolute floor covers pairs with
+    required bound is 1e-4 relative; the 1e-6 absolute floor covers pairs with
     |r| ~ 1e-3 and below, where relative error is meaningless.
   * MI: 1e-5 absolute.
   * top-k: identical pair sets except pairs whose oracle score ties the k-th score
