@@ -157,7 +157,8 @@ int queue_epilogue(Bucket& b, const ColumnStats& cs, const TileCoord* d_tiles, i
 // information writes n_tiles lists.
 int score_ops(Bucket& b, const ColumnStats& cs, const Plan& plan, const TileCoord* d_tiles,
               const int* ops, int n_ops, int metric, int center, float div_eps, int mi_bins,
-              int k_pad, int sub_lists, Cand* const* cands, double* all_scores) {
+              int k_pad, int sub_lists, Cand* const* cands, double* all_scores, int* gram_used) {
+    *gram_used = 0;
     const int nt = (int)plan.tiles.size();
     if (nt == 0) return GAFIME_SUCCESS;
     cudaError_t e;
@@ -177,17 +178,21 @@ int score_ops(Bucket& b, const ColumnStats& cs, const Plan& plan, const TileCoor
     int group_splits[2] = {plan.splits, plan.splits};
     for (int o = 0; o < n_ops; ++o) need[ops[o] == GAFIME_INTERACT_DIV ? 1 : 0] = true;
     const bool tensor = gram_path_enabled(b);
+    if (tensor) {
+        // the Gram kernels' error flag is read once by the caller after its final copy
+        e = gram_error_reset(b, b.stream);
+        if (e != cudaSuccess) return status_from(e);
+        *gram_used = 1;
+    }
     for (int g = 0; g < 2; ++g) {
         if (!need[g]) continue;
         if (tensor) {
-            int gerr = 0;
             // one operand preparation serves both groups when both are scored
             const int prep = (g == 0 && need[1]) ? GRAM_PREP_BOTH : (g == 1 && need[0]) ? GRAM_PREP_DONE
                                                                                       : GRAM_PREP_OWN;
-            e = launch_gram_moments(b, cs, d_tiles, plan.tiles, g == 1, div_eps, mom[g], b.stream, &gerr,
+            e = launch_gram_moments(b, cs, d_tiles, plan.tiles, g == 1, div_eps, mom[g], b.stream, nullptr,
                                     prep);
             if (e != cudaSuccess) return status_from(e);
-            if (gerr) return GAFIME_ERROR_KERNEL_FAILED;
             group_splits[g] = 1;
         } else {
             KernelTimer timer(b.stream, GAFIME_KERNEL_PAIR_MOMENTS);
@@ -202,6 +207,15 @@ int score_ops(Bucket& b, const ColumnStats& cs, const Plan& plan, const TileCoor
 
 int merge_and_copy(Bucket& b, Cand* const* cands, Cand* const* tmp, int n_lists, int k, int k_pad, int n_ops,
                    size_t per_op, int32_t* out_i, int32_t* out_j, double* out_score, int* out_count);
+
+// GAFIME_ERROR_KERNEL_FAILED when a Gram kernel of this call recorded a wait timeout
+int gram_status(Bucket& b, int gram_used) {
+    if (!gram_used) return GAFIME_SUCCESS;
+    int err = 0;
+    cudaError_t e = gram_error_read(b, b.stream, &err);
+    if (e != cudaSuccess) return status_from(e);
+    return err ? GAFIME_ERROR_KERNEL_FAILED : GAFIME_SUCCESS;
+}
 
 int upload_tiles(Bucket& b, const Plan& plan, TileCoord** d_tiles) {
     size_t bytes = std::max<size_t>(1, plan.tiles.size()) * sizeof(TileCoord);
@@ -263,11 +277,15 @@ extern "C" int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact
         cands[o] = (Cand*)b.cands.ptr + per_op * o;
         tmp[o] = (Cand*)b.cands2.ptr + per_op * o;
     }
+    int gram_used = 0;
     st = score_ops(b, cs, plan, d_tiles, interact_types, n_ops, metric, center, div_eps, mi_bins,
-                   k_pad, sub_lists, cands, nullptr);
+                   k_pad, sub_lists, cands, nullptr, &gram_used);
     if (st != GAFIME_SUCCESS) return st;
-
-    return merge_and_copy(b, cands, tmp, n_lists, k, k_pad, n_ops, per_op, out_i, out_j, out_score, out_count);
+    st = merge_and_copy(b, cands, tmp, n_lists, k, k_pad, n_ops, per_op, out_i, out_j, out_score, out_count);
+    if (st == GAFIME_SUCCESS) st = gram_status(b, gram_used);
+    if (st != GAFIME_SUCCESS)
+        for (int o = 0; o < n_ops; ++o) out_count[o] = 0;
+    return st;
 }
 
 namespace gafime {
@@ -336,13 +354,15 @@ extern "C" int gafime_allpairs_scores(ContiguousBucket bucket, int interact_type
     cudaError_t e = ensure(b.scores, (size_t)P * sizeof(double));
     if (e != cudaSuccess) return status_from(e);
     Cand* none[1] = {nullptr};
+    int gram_used = 0;
     st = score_ops(b, cs, plan, d_tiles, &interact_type, 1, metric, center, div_eps, mi_bins, 1, 1,
-                   none, (double*)b.scores.ptr);
+                   none, (double*)b.scores.ptr, &gram_used);
     if (st != GAFIME_SUCCESS) return st;
     e = cudaMemcpyAsync(out_scores, b.scores.ptr, (size_t)P * sizeof(double), cudaMemcpyDeviceToHost,
                         b.stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b.stream);
-    return status_from(e);
+    if (e != cudaSuccess) return status_from(e);
+    return gram_status(b, gram_used);
 }
 
 namespace gafime {
@@ -496,6 +516,8 @@ int streamed_topk(Bucket& b, const float* h_data, const uint8_t* h_mask, const i
     e = ensure(b.moments, 2 * std::max(1, nt) * per_tile * sizeof(double));
     if (e != cudaSuccess) return status_from(e);
     double* mom[2] = {(double*)b.moments.ptr, (double*)b.moments.ptr + std::max(1, nt) * per_tile};
+    e = gram_error_reset(b, b.stream);
+    if (e != cudaSuccess) return status_from(e);
     int t0 = 0;
     for (int J = 0; J < nb; ++J) {
         const int64_t c0 = (int64_t)J * kBlock, c1 = std::min<int64_t>(f, c0 + kBlock);
@@ -509,11 +531,9 @@ int streamed_topk(Bucket& b, const float* h_data, const uint8_t* h_mask, const i
         const std::vector<TileCoord> sub(plan.tiles.begin() + t0, plan.tiles.begin() + t1);
         for (int g2 = 0; g2 < 2; ++g2) {
             if (!need[g2]) continue;
-            int gerr = 0;
             e = launch_gram_moments(b, cs, d_tiles + t0, sub, g2 == 1, div_eps, mom[g2] + (size_t)t0 * per_tile,
-                                    b.stream, &gerr, GRAM_PREP_DONE, chunk);
+                                    b.stream, nullptr, GRAM_PREP_DONE, chunk);
             if (e != cudaSuccess) return status_from(e);
-            if (gerr) return GAFIME_ERROR_KERNEL_FAILED;
         }
         t0 = t1;
     }
@@ -536,7 +556,11 @@ int streamed_topk(Bucket& b, const float* h_data, const uint8_t* h_mask, const i
     st = queue_epilogue(b, cs, d_tiles, nt, ops, n_ops, mom[0], 1, mom[1], 1, k_pad, sub_lists, cands, nullptr);
     if (st != GAFIME_SUCCESS) return st;
     st = merge_and_copy(b, cands, tmp, n_lists, k, k_pad, n_ops, per_op, out_i, out_j, out_score, out_count);
-    if (st != GAFIME_SUCCESS) return st;
+    if (st == GAFIME_SUCCESS) st = gram_status(b, 1);
+    if (st != GAFIME_SUCCESS) {
+        for (int o = 0; o < n_ops; ++o) out_count[o] = 0;
+        return st;
+    }
     // the ingest check of an upload: results over non-finite data are discarded
     int h = 0;
     e = cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, b.stream);

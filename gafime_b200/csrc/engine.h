@@ -122,6 +122,10 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
                                 double* d_moments, cudaStream_t stream, int* host_err, int prep_mode,
                                 int64_t chunk_rows = 0);
 int64_t gram_chunk_rows(const Bucket& b, int ctas_per_chunk);
+// host_err null: launch_gram_moments neither clears nor reads the Gram kernels' error flag
+// (no host sync); the caller clears it before its launches and reads it once at the end.
+cudaError_t gram_error_reset(Bucket& b, cudaStream_t stream);
+cudaError_t gram_error_read(Bucket& b, cudaStream_t stream, int* host_err);
 int gram_tiles128(const std::vector<TileCoord>& tiles64);
 
 // Scoring epilogue + per-tile top-k (select.cu).

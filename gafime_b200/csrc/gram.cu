@@ -1511,7 +1511,7 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
                                 const std::vector<TileCoord>& tiles64, bool recip, float eps,
                                 double* d_moments, cudaStream_t stream, int* host_err, int prep_mode,
                                 int64_t chunk_rows) {
-    *host_err = 0;
+    if (host_err) *host_err = 0;
     const int64_t f = b.f, ld = b.ld, n = b.n;
     const int nb128 = (int)((f + kGT - 1) / kGT);
     // 128-tiles that cover this shard's 64-tiles
@@ -1578,7 +1578,8 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
         e = cudaMemcpyAsync(d_t128, t128.data(), t128.size() * sizeof(TileCoord), cudaMemcpyHostToDevice, stream);
     if (e == cudaSuccess && pairs_on)
         e = cudaMemcpyAsync(d_pairs, pairs.data(), pairs.size() * sizeof(PairCoord), cudaMemcpyHostToDevice, stream);
-    if (e == cudaSuccess) e = cudaMemsetAsync(d_err, 0, 64, stream);  // the flag only: absmax follows at +64
+    // the flag only (absmax follows at +64); with host_err null the caller clears and reads it
+    if (e == cudaSuccess && host_err) e = cudaMemsetAsync(d_err, 0, 64, stream);
     if (e != cudaSuccess) return e;
 
     if (prep_mode != GRAM_PREP_DONE) {
@@ -1674,11 +1675,27 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
         gram_reduce_kernel<<<dim3((unsigned)tiles64.size(), kTilePairs / 256), 256, 0, stream>>>(ra);
     }
     e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess || !host_err) return e;
     int h_err = 0;
     e = cudaMemcpyAsync(&h_err, d_err, sizeof(int), cudaMemcpyDeviceToHost, stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
     *host_err = h_err;
+    return e;
+}
+
+cudaError_t gram_error_reset(Bucket& b, cudaStream_t stream) {
+    GramCols g;
+    cudaError_t e = gram_cols(b, g);
+    return e == cudaSuccess ? cudaMemsetAsync(g.err, 0, 64, stream) : e;
+}
+
+cudaError_t gram_error_read(Bucket& b, cudaStream_t stream, int* host_err) {
+    GramCols g;
+    cudaError_t e = gram_cols(b, g);
+    int h = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&h, g.err, sizeof(int), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    *host_err = h;
     return e;
 }
 
