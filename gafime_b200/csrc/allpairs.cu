@@ -50,11 +50,12 @@ std::vector<TileCoord> shard_tiles(int64_t f, int shard_id, int n_shards) {
         int64_t w;
         int order, ns;
         TileCoord sub[4];
+        int BI, BJ;   // its two 128-column blocks
     };
     std::vector<Block> blocks;
     for (int BI = 0; BI < nb2; ++BI)
         for (int BJ = BI; BJ < nb2; ++BJ) {
-            Block blk{0, (int)blocks.size(), 0, {}};
+            Block blk{0, (int)blocks.size(), 0, {}, BI, BJ};
             for (int da = 0; da < 2; ++da)
                 for (int db = 0; db < 2; ++db) {
                     int bi = 2 * BI + da, bj = 2 * BJ + db;
@@ -69,15 +70,57 @@ std::vector<TileCoord> shard_tiles(int64_t f, int shard_id, int n_shards) {
     std::stable_sort(blocks.begin(), blocks.end(),
                      [](const Block& x, const Block& y) { return x.w > y.w; });
     std::vector<int64_t> load((size_t)n_shards, 0);
-    std::vector<TileCoord> mine;
-    for (const Block& blk : blocks) {
+    std::vector<int> owner(blocks.size());
+    for (size_t x = 0; x < blocks.size(); ++x) {
         int best = 0;
         for (int s = 1; s < n_shards; ++s)
             if (load[(size_t)s] < load[(size_t)best]) best = s;
-        load[(size_t)best] += blk.w;
-        if (best == shard_id)
-            for (int q = 0; q < blk.ns; ++q) mine.push_back(blk.sub[q]);
+        load[(size_t)best] += blocks[x].w;
+        owner[x] = best;
     }
+    // Locality: a shard prepares the 128-column blocks its tiles read, so swap blocks of equal
+    // pair count between two shards while that lowers the larger, then the summed, number of
+    // column blocks the two read (the loads do not change).  Fixed scan order: every process
+    // arrives at the same assignment.  Skipped for very wide matrices (quadratic scan).
+    if (n_shards > 1 && blocks.size() <= 2048) {
+        auto reads = [&](int s, int skip, int add) {
+            std::vector<char> used((size_t)nb2, 0);
+            int c = 0;
+            auto mark = [&](int x) {
+                for (int B : {blocks[(size_t)x].BI, blocks[(size_t)x].BJ})
+                    if (!used[(size_t)B]) { used[(size_t)B] = 1; ++c; }
+            };
+            for (size_t x = 0; x < blocks.size(); ++x)
+                if (owner[x] == s && (int)x != skip) mark((int)x);
+            if (add >= 0) mark(add);
+            return c;
+        };
+        for (int pass = 0; pass < 64; ++pass) {
+            bool swapped = false;
+            for (int a = 0; a < n_shards && !swapped; ++a)
+                for (int b = a + 1; b < n_shards && !swapped; ++b) {
+                    const int ra = reads(a, -1, -1), rb = reads(b, -1, -1);
+                    for (size_t x = 0; x < blocks.size() && !swapped; ++x) {
+                        if (owner[x] != a) continue;
+                        for (size_t y = 0; y < blocks.size() && !swapped; ++y) {
+                            if (owner[y] != b || blocks[y].w != blocks[x].w) continue;
+                            const int na = reads(a, (int)x, (int)y), nbr = reads(b, (int)y, (int)x);
+                            if (std::max(na, nbr) < std::max(ra, rb) ||
+                                (std::max(na, nbr) == std::max(ra, rb) && na + nbr < ra + rb)) {
+                                owner[x] = b;
+                                owner[y] = a;
+                                swapped = true;
+                            }
+                        }
+                    }
+                }
+            if (!swapped) break;
+        }
+    }
+    std::vector<TileCoord> mine;
+    for (size_t x = 0; x < blocks.size(); ++x)
+        if (owner[x] == shard_id)
+            for (int q = 0; q < blocks[x].ns; ++q) mine.push_back(blocks[x].sub[q]);
     return mine;
 }
 

@@ -265,8 +265,10 @@ int gafime_unary_scores(ContiguousBucket bucket, int metric, int mi_bins, double
  * pairs i in [64 bi, 64 bi + 64) x j in [64 bj, 64 bj + 64), i < j) that shard shard_id
  * of n_shards scores in gafime_allpairs_topk.  The pair space is dealt out in 128 x 128
  * blocks (the tensor-core tile) in decreasing pair count (ties in row-major order), each
- * to the shard with the fewest pairs so far (ties: lowest id), so every process derives
- * the same split without communicating; a shard scores the 64-tiles inside its blocks.  out_tiles receives
+ * to the shard with the fewest pairs so far (ties: lowest id); then blocks of equal pair
+ * count trade shards while that lowers the number of 128-column blocks a shard reads (its
+ * statistics pass covers those).  Every process derives the same split without
+ * communicating; a shard scores the 64-tiles inside its blocks.  out_tiles receives
  * 2 * *out_count ints (bi, bj); returns GAFIME_ERROR_INVALID_ARGS with *out_count set
  * when max_tiles is too small.
  */

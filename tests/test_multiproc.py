@@ -83,3 +83,15 @@ def test_shards_partition_the_pair_space():
         assert len(seen) == f * (f - 1) // 2
         if f >= 724:  # enough tiles for the greedy split to balance within 10 %
             assert max(loads) <= 1.1 * (f * (f - 1) / 2) / world
+
+
+def test_shards_read_few_column_blocks():
+    """Blocks of equal pair count trade shards toward fewer 128-column blocks per shard
+    (each shard's statistics pass covers the blocks it reads); the loads are unchanged."""
+    from gafime_b200 import _native
+    for f, world, most in ((724, 8, 3), (512, 4, 3), (362, 2, 3)):
+        reads = []
+        for r in range(world):
+            t = _native.shard_tiles(f, r, world)
+            reads.append(len({int(x) // 2 for x in np.asarray(t).reshape(-1)}))
+        assert max(reads) <= most, reads
