@@ -635,6 +635,11 @@ def run_ours(args):
                "sample": arm.describe(units, dt)}
 
     h2d = packed.nbytes + mask.nbytes
+    if world > 1 and w["metric"] == "pearson" and not w["center"]:
+        # a shard's streamed call copies the target and the 128-column blocks its tiles read
+        blocks = {int(x) // 2 for x in np.asarray(_native.shard_tiles(f, rank, world)).reshape(-1)}
+        cols = sum(min(128, f - 128 * B) for B in blocks)
+        h2d = (cols + 1) * n * 4 + mask.nbytes
     d2h = len(ops) * k * (4 + 4 + 8) + len(ops) * 4
     line = {
         "metric": METRIC_NAME, "value": value, "unit": "evals/s", "n_gpus": world,

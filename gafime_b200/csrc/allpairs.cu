@@ -502,12 +502,24 @@ int streamed_topk(Bucket& b, const float* h_data, const uint8_t* h_mask, const i
     const int nb = (int)((f + kBlock - 1) / kBlock);
     cudaError_t e = ensure_copy_stream(b, (size_t)nb + 1);
     if (e != cudaSuccess) return status_from(e);
+    // tiles of this shard ordered by the block that completes them
+    Plan plan = make_plan(b, shard_id, n_shards);
+    std::stable_sort(plan.tiles.begin(), plan.tiles.end(),
+                     [](const TileCoord& x, const TileCoord& z) { return arrival_block(x) < arrival_block(z); });
+    const int nt = (int)plan.tiles.size();
+    // the column blocks this shard's tiles read are the ones copied (all of them for one
+    // shard, or when the shard has no tile and the call is a plain upload)
+    std::vector<char> used((size_t)nb, nt == 0 ? 1 : 0);
+    for (const TileCoord& t : plan.tiles) used[(size_t)(t.bi / 2)] = used[(size_t)(t.bj / 2)] = 1;
+    bool all_blocks = true;
+    for (int J = 0; J < nb; ++J) all_blocks = all_blocks && used[(size_t)J];
     // the target and the fold mask first, then the column blocks in order
     float* y = b.d_data + f * ld;
     e = cudaMemcpyAsync(y, h_data + f * n, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, b.copy_stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(b.d_mask, h_mask, (size_t)n, cudaMemcpyHostToDevice, b.copy_stream);
     if (e == cudaSuccess) e = cudaEventRecord(b.arrived[(size_t)nb], b.copy_stream);
     for (int J = 0; J < nb && e == cudaSuccess; ++J) {
+        if (!used[(size_t)J]) continue;
         const int64_t c0 = (int64_t)J * kBlock, c1 = std::min<int64_t>(f, c0 + kBlock);
         e = cudaMemcpy2DAsync(b.d_data + c0 * ld, (size_t)ld * sizeof(float), h_data + c0 * n,
                               (size_t)n * sizeof(float), (size_t)n * sizeof(float), (size_t)(c1 - c0),
@@ -516,12 +528,6 @@ int streamed_topk(Bucket& b, const float* h_data, const uint8_t* h_mask, const i
     }
     if (e != cudaSuccess) return status_from(e);
     b.finite_state = -1;
-
-    // tiles of this shard ordered by the block that completes them
-    Plan plan = make_plan(b, shard_id, n_shards);
-    std::stable_sort(plan.tiles.begin(), plan.tiles.end(),
-                     [](const TileCoord& x, const TileCoord& z) { return arrival_block(x) < arrival_block(z); });
-    const int nt = (int)plan.tiles.size();
     if (nt == 0) {
         // nothing to score on this shard: the upload alone, checked as an upload is
         e = cudaStreamSynchronize(b.copy_stream);
@@ -552,9 +558,6 @@ int streamed_topk(Bucket& b, const float* h_data, const uint8_t* h_mask, const i
 
     bool need[2] = {false, false};
     for (int o = 0; o < n_ops; ++o) need[ops[o] == GAFIME_INTERACT_DIV ? 1 : 0] = true;
-    // the column blocks this shard's tiles read get their statistics; the rest is only checked
-    std::vector<char> used((size_t)nb, 0);
-    for (const TileCoord& t : plan.tiles) used[(size_t)(t.bi / 2)] = used[(size_t)(t.bj / 2)] = 1;
     const size_t per_tile = (size_t)3 * kTilePairs;
     e = ensure(b.moments, 2 * std::max(1, nt) * per_tile * sizeof(double));
     if (e != cudaSuccess) return status_from(e);
@@ -563,10 +566,11 @@ int streamed_topk(Bucket& b, const float* h_data, const uint8_t* h_mask, const i
     if (e != cudaSuccess) return status_from(e);
     int t0 = 0;
     for (int J = 0; J < nb; ++J) {
+        if (!used[(size_t)J]) continue;  // no tile of this shard reads it: not copied
         const int64_t c0 = (int64_t)J * kBlock, c1 = std::min<int64_t>(f, c0 + kBlock);
         e = cudaStreamWaitEvent(b.stream, b.arrived[(size_t)J], 0);
         if (e == cudaSuccess) e = launch_finite_check(b.d_data + c0 * ld, (c1 - c0) * ld, flag, b.sm_count, b.stream);
-        if (e == cudaSuccess && used[(size_t)J]) e = gram_prep_columns(b, cs, need[1], div_eps, c0, c1, b.stream);
+        if (e == cudaSuccess) e = gram_prep_columns(b, cs, need[1], div_eps, c0, c1, b.stream);
         if (e != cudaSuccess) return status_from(e);
         int t1 = t0;
         while (t1 < nt && arrival_block(plan.tiles[(size_t)t1]) == J) ++t1;
@@ -609,7 +613,8 @@ int streamed_topk(Bucket& b, const float* h_data, const uint8_t* h_mask, const i
     e = cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, b.stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b.stream);
     if (e != cudaSuccess) return status_from(e);
-    b.finite_state = h == 0 ? 1 : 0;
+    // a shard that copied part of the matrix leaves the rest unchecked for later calls
+    b.finite_state = h != 0 ? 0 : (all_blocks ? 1 : -1);
     if (h != 0) {
         for (int o = 0; o < n_ops; ++o) out_count[o] = 0;
         return GAFIME_ERROR_INVALID_ARGS;

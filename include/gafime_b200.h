@@ -235,7 +235,10 @@ int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact_types, int
  * n floats each); pinned host memory is what lets the copies overlap.  Same results as the
  * two calls (the same kernels on the same data and row chunks); non-finite input returns
  * GAFIME_ERROR_INVALID_ARGS like the upload's check.  Pearson with center = 0 on the
- * tensor-core path streams; other metrics and modes run the two calls.
+ * tensor-core path streams; other metrics and modes run the two calls.  With n_shards > 1
+ * only the 128-column blocks that this shard's tiles read are copied and checked (a
+ * process of a multi-GPU job moves its share of the matrix); the bucket's other columns
+ * keep what they held, so a later call of another kind on this bucket needs a full upload.
  */
 int gafime_allpairs_topk_host(ContiguousBucket bucket, const float* h_data, const uint8_t* h_mask,
                               const int* interact_types, int n_ops, int metric, int center,

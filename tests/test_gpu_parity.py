@@ -556,3 +556,29 @@ def test_upload_rows_equals_column_upload(native, n, f):
         r.upload_rows(Xb, y)
         with pytest.raises(native.GafimeError):
             r.topk(["multiply"], 1)
+
+
+def test_sharded_streamed_call_copies_and_checks_its_blocks_only(native):
+    """With n_shards > 1 a streamed call moves (and checks) only the column blocks its
+    tiles read: a NaN in a block it does not read leaves its result unchanged."""
+    rng = np.random.default_rng(13)
+    n, f, shards = 4000, 724, 8
+    X = rng.standard_normal((n, f)).astype(np.float32)
+    y = rng.standard_normal(n).astype(np.float32)
+    for shard in range(shards):
+        tiles = native.shard_tiles(f, shard, shards)
+        read = {int(v) // 2 for v in np.asarray(tiles).reshape(-1)}
+        unread = [B for B in range((f + 127) // 128) if B not in read]
+        if not unread:
+            continue
+        Xb = X.copy()
+        Xb[7, 128 * unread[0]] = np.nan
+        with native.Bucket(n, f) as a, native.Bucket(n, f) as s:
+            a.upload(X, y)
+            want = a.topk(["multiply"], 20, shard_id=shard, n_shards=shards)["multiply"]
+            got = s.topk_from_host(native.pack_columns(Xb, y), ["multiply"], 20, shard_id=shard,
+                                   n_shards=shards)["multiply"]
+            for u, v in zip(got, want):
+                np.testing.assert_array_equal(u, v)
+        return
+    pytest.fail("no shard leaves a column block unread")
