@@ -1295,29 +1295,53 @@ struct GramReduceArgs {
 
 // grid (n_tiles64, 16): 256 pairs of one 64-tile per CTA, consecutive threads on
 // consecutive rows m of the partials (coalesced), chunks added in a fixed order.
+// Block (t, y): pairs q = 64 y .. 64 y + 63 of 64-tile t; the four 64-thread groups add
+// the chunk partials of four consecutive chunk ranges, then group 0 adds the four range
+// sums in range order (a fixed order: deterministic) and undoes scales and centring.
+constexpr int kRedParts = 4;
 __global__ void __launch_bounds__(256) gram_reduce_kernel(GramReduceArgs a) {
+    __shared__ double red[3][kRedParts][64];
     const int t = blockIdx.x;
     const TileCoord tc = a.tiles64[t];
     const int I = tc.bi >> 1, J = tc.bj >> 1;
     const int t128 = a.lut[I * a.nb128 + J];
     const double n = (double)a.n;
     double* out = a.moments + (int64_t)t * 3 * kTilePairs;
-    const int q = blockIdx.y * blockDim.x + threadIdx.x;   // 0 .. 4095
+    const int part = threadIdx.x >> 6;
+    const int q = blockIdx.y * 64 + (threadIdx.x & 63);   // 0 .. 4095
     const int lj = q / kTile, li = q % kTile;
     const int e = li * kTile + lj;
     const int m = (tc.bi & 1) * kTile + li, nn = (tc.bj & 1) * kTile + lj;
     const int64_t i = (int64_t)tc.bi * kTile + li, j = (int64_t)tc.bj * kTile + lj;
+    const bool live = t128 >= 0 && i < a.f && j < a.f;
+    {
+        double C = 0.0, Q = 0.0, W = 0.0;
+        if (live) {
+            const int per = (a.n_chunks + kRedParts - 1) / kRedParts;
+            const int c0 = part * per, c1 = min(a.n_chunks, c0 + per);
+            const float* p = a.partial + (int64_t)t128 * 3 * kGT * kGT + (int64_t)nn * kGT + m;
+            const int64_t cstride = (int64_t)a.n_tiles128 * 3 * kGT * kGT;
+            #pragma unroll 4
+            for (int ch = c0; ch < c1; ++ch) {
+                const float* pc = p + ch * cstride;
+                C += (double)pc[0];
+                Q += (double)pc[(int64_t)kGT * kGT];
+                W += (double)pc[(int64_t)2 * kGT * kGT];
+            }
+        }
+        red[0][part][threadIdx.x & 63] = C;
+        red[1][part][threadIdx.x & 63] = Q;
+        red[2][part][threadIdx.x & 63] = W;
+    }
+    __syncthreads();
+    if (part != 0) return;
     double S1 = 0.0, Q = 0.0, S3 = 0.0;
-    if (t128 >= 0 && i < a.f && j < a.f) {
+    if (live) {
         double C = 0.0, W = 0.0;
-        const float* p = a.partial + (int64_t)t128 * 3 * kGT * kGT + (int64_t)nn * kGT + m;
-        const int64_t cstride = (int64_t)a.n_tiles128 * 3 * kGT * kGT;
-        #pragma unroll 4
-        for (int ch = 0; ch < a.n_chunks; ++ch) {
-            const float* pc = p + ch * cstride;
-            C += (double)pc[0];
-            Q += (double)pc[(int64_t)kGT * kGT];
-            W += (double)pc[(int64_t)2 * kGT * kGT];
+        for (int r = 0; r < kRedParts; ++r) {
+            C += red[0][r][threadIdx.x];
+            Q += red[1][r][threadIdx.x];
+            W += red[2][r][threadIdx.x];
         }
         const double* ci = a.cs + i * 12;
         const double* cj = a.cs + j * 12;
@@ -1672,7 +1696,7 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     ra.moments = d_moments;
     {
         KernelTimer timer(stream, GAFIME_KERNEL_GRAM_REDUCE);
-        gram_reduce_kernel<<<dim3((unsigned)tiles64.size(), kTilePairs / 256), 256, 0, stream>>>(ra);
+        gram_reduce_kernel<<<dim3((unsigned)tiles64.size(), kTilePairs / 64), 256, 0, stream>>>(ra);
     }
     e = cudaGetLastError();
     if (e != cudaSuccess || !host_err) return e;
