@@ -216,6 +216,24 @@ __global__ void col_combine_kernel(const double* __restrict__ part, int cols, in
     colstats[c * 4 + 3] = v[0] / (double)n;
 }
 
+// col_combine_kernel with one block per column: thread t adds splits t, t + 256, ... in
+// order, then a fixed-order tree over the threads (deterministic); many splits (a single
+// tall column) no longer run through one thread.
+__global__ void __launch_bounds__(256) col_combine_block_kernel(const double* __restrict__ part, int splits,
+                                                                int64_t n, double* __restrict__ colstats) {
+    __shared__ double red[3 * 256];
+    const int c = blockIdx.x;
+    double v[3] = {0.0, 0.0, 0.0};
+    for (int s = threadIdx.x; s < splits; s += 256)
+        for (int m = 0; m < 3; ++m) v[m] += part[((int64_t)c * splits + s) * 3 + m];
+    block_reduce_fixed<3>(v, red);
+    if (threadIdx.x != 0) return;
+    colstats[c * 4 + 0] = v[0];
+    colstats[c * 4 + 1] = v[1];
+    colstats[c * 4 + 2] = v[2];
+    colstats[c * 4 + 3] = v[0] / (double)n;
+}
+
 // ystats = {n, sum y, var_y, mean y} from the target column's (sum, sumsq).
 // var_y = syy - sy^2/n as native_cuda_backend.py:481 and gafime_core.cpp:496.
 __global__ void ystats_kernel(const double* __restrict__ ycol, int64_t n, double* __restrict__ ystats) {
@@ -278,8 +296,8 @@ static cudaError_t column_sums(Bucket& b, const float* x, int64_t cols, const fl
     dim3 grid((unsigned)cols, (unsigned)splits);
     col_partial_kernel<<<grid, 256, 0, b.stream>>>(x, b.ld, b.n, ycen, span,
                                                    (double*)b.stats_part.ptr);
-    col_combine_kernel<<<(unsigned)((cols + 127) / 128), 128, 0, b.stream>>>(
-        (const double*)b.stats_part.ptr, (int)cols, splits, b.n, colstats);
+    col_combine_block_kernel<<<(unsigned)cols, 256, 0, b.stream>>>((const double*)b.stats_part.ptr, splits, b.n,
+                                                                    colstats);
     return cudaGetLastError();
 }
 
