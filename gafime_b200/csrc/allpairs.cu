@@ -14,6 +14,9 @@
 #include <string.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <vector>
 
 #include "engine.h"
@@ -43,7 +46,7 @@ int64_t tile_pairs(int bi, int bj, int64_t f) {
 // row-major order), each to the shard with the fewest pairs so far (ties: lowest shard
 // id); a shard scores the 64-tiles inside its blocks.  Every process derives the same
 // split without communication.
-std::vector<TileCoord> shard_tiles(int64_t f, int shard_id, int n_shards) {
+static std::vector<TileCoord> compute_shard_tiles(int64_t f, int shard_id, int n_shards) {
     int nb = (int)((f + kTile - 1) / kTile);
     int nb2 = (nb + 1) / 2;
     struct Block {
@@ -81,35 +84,44 @@ std::vector<TileCoord> shard_tiles(int64_t f, int shard_id, int n_shards) {
     // Locality: a shard prepares the 128-column blocks its tiles read, so swap blocks of equal
     // pair count between two shards while that lowers the larger, then the summed, number of
     // column blocks the two read (the loads do not change).  Fixed scan order: every process
-    // arrives at the same assignment.  Skipped for very wide matrices (quadratic scan).
+    // arrives at the same assignment.  Per-shard counts of the owned blocks touching each
+    // column block make a trial swap O(1); skipped for very wide matrices.
     if (n_shards > 1 && blocks.size() <= 2048) {
-        auto reads = [&](int s, int skip, int add) {
-            std::vector<char> used((size_t)nb2, 0);
-            int c = 0;
-            auto mark = [&](int x) {
-                for (int B : {blocks[(size_t)x].BI, blocks[(size_t)x].BJ})
-                    if (!used[(size_t)B]) { used[(size_t)B] = 1; ++c; }
-            };
-            for (size_t x = 0; x < blocks.size(); ++x)
-                if (owner[x] == s && (int)x != skip) mark((int)x);
-            if (add >= 0) mark(add);
-            return c;
+        std::vector<int> cnt((size_t)n_shards * nb2, 0), reads((size_t)n_shards, 0);
+        // multiplicities: a diagonal block counts its column block twice, consistently
+        auto add = [&](int s, int x, int d) {
+            for (int B : {blocks[(size_t)x].BI, blocks[(size_t)x].BJ}) {
+                int& c = cnt[(size_t)s * nb2 + B];
+                if (d > 0 && c++ == 0) ++reads[(size_t)s];
+                if (d < 0 && --c == 0) --reads[(size_t)s];
+            }
         };
+        for (size_t x = 0; x < blocks.size(); ++x) add(owner[x], (int)x, +1);
         for (int pass = 0; pass < 64; ++pass) {
             bool swapped = false;
             for (int a = 0; a < n_shards && !swapped; ++a)
                 for (int b = a + 1; b < n_shards && !swapped; ++b) {
-                    const int ra = reads(a, -1, -1), rb = reads(b, -1, -1);
+                    const int ra = reads[(size_t)a], rb = reads[(size_t)b];
                     for (size_t x = 0; x < blocks.size() && !swapped; ++x) {
                         if (owner[x] != a) continue;
                         for (size_t y = 0; y < blocks.size() && !swapped; ++y) {
                             if (owner[y] != b || blocks[y].w != blocks[x].w) continue;
-                            const int na = reads(a, (int)x, (int)y), nbr = reads(b, (int)y, (int)x);
+                            // trial swap
+                            add(a, (int)x, -1);
+                            add(b, (int)y, -1);
+                            add(a, (int)y, +1);
+                            add(b, (int)x, +1);
+                            const int na = reads[(size_t)a], nbr = reads[(size_t)b];
                             if (std::max(na, nbr) < std::max(ra, rb) ||
                                 (std::max(na, nbr) == std::max(ra, rb) && na + nbr < ra + rb)) {
                                 owner[x] = b;
                                 owner[y] = a;
                                 swapped = true;
+                            } else {
+                                add(a, (int)y, -1);
+                                add(b, (int)x, -1);
+                                add(a, (int)x, +1);
+                                add(b, (int)y, +1);
                             }
                         }
                     }
@@ -122,6 +134,23 @@ std::vector<TileCoord> shard_tiles(int64_t f, int shard_id, int n_shards) {
         if (owner[x] == shard_id)
             for (int q = 0; q < blocks[x].ns; ++q) mine.push_back(blocks[x].sub[q]);
     return mine;
+}
+
+// The assignment depends on (f, shard_id, n_shards) only: computed once per process and kept.
+std::vector<TileCoord> shard_tiles(int64_t f, int shard_id, int n_shards) {
+    static std::mutex mu;
+    static std::map<std::tuple<int64_t, int, int>, std::vector<TileCoord>> memo;
+    const auto key = std::make_tuple(f, shard_id, n_shards);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = memo.find(key);
+        if (it != memo.end()) return it->second;
+    }
+    std::vector<TileCoord> t = compute_shard_tiles(f, shard_id, n_shards);
+    std::lock_guard<std::mutex> lock(mu);
+    if (memo.size() > 256) memo.clear();
+    memo[key] = t;
+    return t;
 }
 
 namespace {
