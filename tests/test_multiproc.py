@@ -95,3 +95,18 @@ def test_shards_read_few_column_blocks():
             t = _native.shard_tiles(f, r, world)
             reads.append(len({int(x) // 2 for x in np.asarray(t).reshape(-1)}))
         assert max(reads) <= most, reads
+
+
+def test_shard_assignment_is_cheap_for_wide_matrices():
+    """The assignment runs on the host before every sharded call: bounded work, kept per
+    process (8000 columns over 8 shards: well under a second for all shards)."""
+    import time
+    from gafime_b200 import _native
+    t = time.perf_counter()
+    for r in range(8):
+        _native.shard_tiles(8000, r, 8)
+    assert time.perf_counter() - t < 2.0
+    t = time.perf_counter()
+    for r in range(8):
+        _native.shard_tiles(8000, r, 8)
+    assert time.perf_counter() - t < 0.1
