@@ -277,7 +277,7 @@ __global__ void finite_kernel(const float* __restrict__ x, int64_t cols, int64_t
 }
 
 static int split_count(int64_t cols, int64_t n, int sm) {
-    int64_t want = (4 * (int64_t)sm + cols - 1) / cols;
+    int64_t want = (16 * (int64_t)sm + cols - 1) / cols;  // ~16 CTAs per SM of column passes
     int64_t max_by_rows = (n + 4095) / 4096;
     if (want > max_by_rows) want = max_by_rows;
     if (want < 1) want = 1;
