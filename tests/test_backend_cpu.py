@@ -64,3 +64,28 @@ def test_one_upload_target_only_replacement_and_subset_eviction(resident):
     assert tmp.n == 3 and ("gather", (3, 4), True) in FakeBucket.log
     r.free()
     assert full.freed and all(b.freed for b in made)
+
+
+def test_stability_resampled_path_draws_the_same_rows():
+    """A backend with score_resampled gets the same bootstrap rows (same generator draws) as
+    the reference's X[idx], y[idx] path."""
+    from gafime_b200.backends.base import Backend
+    from gafime_b200.metrics import MetricSuite
+    from gafime_b200.validation import StabilityAnalyzer
+
+    class Plain(Backend):
+        def score_combos(self, X, y, combos, suite):
+            return {c: {"pearson": float(np.sum(X[:, c[0]] * y))} for c in combos}
+
+    class Resampling(Plain):
+        def score_resampled(self, X, y, rows, combos, suite):
+            return self.score_combos(X[rows], y[rows], combos, suite)
+
+    rng0 = np.random.default_rng(4)
+    X = rng0.standard_normal((50, 3))
+    y = rng0.standard_normal(50)
+    suite = MetricSuite(["pearson"])
+    a = StabilityAnalyzer(suite, Plain()).assess(X, y, [(0,), (2,)], 3, np.random.default_rng(9))
+    b = StabilityAnalyzer(suite, Resampling()).assess(X, y, [(0,), (2,)], 3, np.random.default_rng(9))
+    assert [(r.combo, r.metrics_mean, r.metrics_std) for r in a] == \
+        [(r.combo, r.metrics_mean, r.metrics_std) for r in b]
