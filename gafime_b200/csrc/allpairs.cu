@@ -523,9 +523,9 @@ cudaError_t ensure_copy_stream(Bucket& b, size_t n_events) {
 // that block J completes.  Same results as gafime_contiguous_bucket_upload followed by
 // gafime_allpairs_topk (the per-column statistics and every tile's moments are computed by
 // the same kernels on the same data; only the launch order differs).
-int streamed_topk(Bucket& b, const float* h_data, const uint8_t* h_mask, const int* ops, int n_ops, float div_eps,
-                  int k, int shard_id, int n_shards, int32_t* out_i, int32_t* out_j, double* out_score,
-                  int* out_count) {
+int streamed_topk_body(Bucket& b, const float* h_data, const uint8_t* h_mask, const int* ops, int n_ops,
+                       float div_eps, int k, int shard_id, int n_shards, int32_t* out_i, int32_t* out_j,
+                       double* out_score, int* out_count) {
     const int64_t f = b.f, n = b.n, ld = b.ld;
     constexpr int64_t kBlock = 2 * kTile;  // the 128-column block of the tensor-core Gram tile
     const int nb = (int)((f + kBlock - 1) / kBlock);
@@ -649,6 +649,17 @@ int streamed_topk(Bucket& b, const float* h_data, const uint8_t* h_mask, const i
         return GAFIME_ERROR_INVALID_ARGS;
     }
     return GAFIME_SUCCESS;
+}
+
+// streamed_topk_body, and on a failed call the copy stream drained before returning: the
+// caller may free or refill its host buffers as soon as the call returns
+int streamed_topk(Bucket& b, const float* h_data, const uint8_t* h_mask, const int* ops, int n_ops, float div_eps,
+                  int k, int shard_id, int n_shards, int32_t* out_i, int32_t* out_j, double* out_score,
+                  int* out_count) {
+    const int st = streamed_topk_body(b, h_data, h_mask, ops, n_ops, div_eps, k, shard_id, n_shards, out_i, out_j,
+                                      out_score, out_count);
+    if (st != GAFIME_SUCCESS && b.copy_stream) cudaStreamSynchronize(b.copy_stream);
+    return st;
 }
 
 }  // namespace
