@@ -571,7 +571,11 @@ int gafime_contiguous_bucket_upload_rows(ContiguousBucket bucket, const float* h
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(b->d_data + f * ld, h_y, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, b->stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(b->d_mask, h_mask, (size_t)n, cudaMemcpyHostToDevice, b->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    {
+        // also after a failure: no copy from the caller's buffers is left in flight
+        const cudaError_t es = cudaStreamSynchronize(b->stream);
+        if (e == cudaSuccess) e = es;
+    }
     for (int s = 0; s < 2; ++s)
         if (done[s]) cudaEventDestroy(done[s]);
     if (e != cudaSuccess) return status_from(e);
@@ -596,17 +600,19 @@ int gafime_contiguous_bucket_upload_target(ContiguousBucket bucket, const float*
         return check_finite(*b, &finite);
     }
     e = ensure(b->flags, 64);
-    if (e != cudaSuccess) return status_from(e);
-    int* flag = (int*)b->flags.ptr;
     int h = 0;
-    e = cudaMemsetAsync(flag, 0, sizeof(int), b->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync((int*)b->flags.ptr, 0, sizeof(int), b->stream);
     if (e == cudaSuccess) {
         KernelTimer timer(b->stream, GAFIME_KERNEL_FINITE_CHECK);
-        finite4_kernel<<<b->sm_count, 256, 0, b->stream>>>((const float4*)y, b->ld / 4, flag);
+        finite4_kernel<<<b->sm_count, 256, 0, b->stream>>>((const float4*)y, b->ld / 4, (int*)b->flags.ptr);
         e = cudaGetLastError();
     }
-    if (e == cudaSuccess) e = cudaMemcpyAsync(&h, flag, sizeof(int), cudaMemcpyDeviceToHost, b->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&h, b->flags.ptr, sizeof(int), cudaMemcpyDeviceToHost, b->stream);
+    {
+        // also after a failure: the copy of h_y is not left in flight
+        const cudaError_t es = cudaStreamSynchronize(b->stream);
+        if (e == cudaSuccess) e = es;
+    }
     if (e != cudaSuccess) return status_from(e);
     b->finite_state = h == 0 ? 1 : 0;
     return GAFIME_SUCCESS;
