@@ -531,7 +531,11 @@ int gafime_contiguous_bucket_upload(ContiguousBucket bucket, const float* h_data
                                       (size_t)(b->f + 1), cudaMemcpyHostToDevice, b->stream);
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(b->d_mask, h_mask, (size_t)b->n, cudaMemcpyHostToDevice, b->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    {
+        // also after a failure: no copy from the caller's buffers is left in flight
+        const cudaError_t es = cudaStreamSynchronize(b->stream);
+        if (e == cudaSuccess) e = es;
+    }
     if (e != cudaSuccess) return status_from(e);
     // validate the new data at ingest: the all-pairs calls accept finite input only
     b->finite_state = -1;
