@@ -582,3 +582,19 @@ def test_sharded_streamed_call_copies_and_checks_its_blocks_only(native):
                 np.testing.assert_array_equal(u, v)
         return
     pytest.fail("no shard leaves a column block unread")
+
+
+@pytest.mark.xfail(strict=False, reason=(
+    "S2 = sum (a op b)^2 is accumulated without centring: pairs whose conditioning "
+    "S2 / (S2 - S1^2/n) exceeds ~300 (columns ~30 standard deviations from zero) can miss "
+    "the 1e-4 bound, about 3e-7 * kappa relative; an exact re-score of those pairs is not built"))
+@pytest.mark.parametrize("op", ["multiply", "divide"])
+def test_columns_far_from_zero_hold_the_bound(native, oracle, op):
+    """Columns 100 standard deviations from zero (kappa ~1e3 to 1e4), a known limit."""
+    rng = np.random.default_rng(5)
+    n, f = 40000, 8
+    X = (100.0 + rng.standard_normal((n, f)) * rng.uniform(0.5, 2.0, f)).astype(np.float32)
+    y = (rng.random(n) < 1 / (1 + np.exp(-(X[:, 1] - X[:, 1].mean())))).astype(np.float32)
+    want = oracle.raw_pearson(X, y, op, div_eps=1e-6)
+    with bucket_for(native, X, y) as b:
+        assert_pearson_close(b.scores(op, div_eps=1e-6), want)

@@ -1,0 +1,146 @@
+"""Numerical model of the tensor-core Gram path (gafime_b200/csrc/gram.cu), checked on the CPU.
+
+The model restates the kernel's arithmetic in numpy:
+  * per column: mean rounded to fp32, power-of-two scales with |value| <= 2^14, operands
+    v = fl32(s (a - mean)) for C and W, q = fl32(a^2) s_q for Q, W's B operand fl32(v ycen s_y);
+  * each operand split into hi = fp16(v) and lo = fp16(v - hi); a Gram is hi.hi + hi.lo + lo.hi;
+  * products exact, each 16-row step added to an fp32 accumulator, chunks of 8192 rows,
+    chunk partials summed in fp64; the centring is undone in fp64 as gram_reduce_kernel does.
+It is compared with the oracle's fp64 Pearson of fl32(a op b) (the reference CPU library's
+semantics).  What it shows:
+  * two fp16 terms hold the 1e-4 Pearson bound on normal and lognormal columns with a wide
+    margin, and one term does not (why every operand is split);
+  * the error grows with the pair's conditioning kappa = S2 / (S2 - S1^2 / n), because
+    S2 = sum (a g(b))^2 is accumulated uncentred: about 3e-7 * kappa relative.  Columns
+    whose mean is ~30 standard deviations from zero or more (kappa above ~300) can miss the
+    bound on this path.
+"""
+import numpy as np
+import pytest
+
+STEP, CHUNK = 16, 8192
+
+
+def _pow2_scale(m):
+    m = np.asarray(m, dtype=np.float64)
+    ok = (m > 0) & np.isfinite(m)
+    _, e = np.frexp(16384.0 / np.where(ok, m, 1.0))
+    return np.where(ok, np.ldexp(1.0, e - 1), 1.0)
+
+
+def _gram(A, B, terms):
+    """sum over rows of A[:, i] * B[:, j] with the kernel's operand split and accumulation."""
+    ah32 = A.astype(np.float16).astype(np.float32)
+    bh32 = B.astype(np.float16).astype(np.float32)
+    ops = [(ah32.astype(np.float64), bh32.astype(np.float64))]
+    if terms == 2:
+        al = (A - ah32).astype(np.float16).astype(np.float64)
+        bl = (B - bh32).astype(np.float16).astype(np.float64)
+        ops += [(ops[0][0], bl), (al, ops[0][1])]
+    n = A.shape[0]
+    total = np.zeros((A.shape[1], B.shape[1]))
+    for c0 in range(0, n, CHUNK):
+        c1 = min(n, c0 + CHUNK)
+        pad = (-(c1 - c0)) % STEP
+
+        def steps(M):
+            M = M[c0:c1]
+            if pad:
+                M = np.vstack([M, np.zeros((pad, M.shape[1]))])
+            return M.reshape(-1, STEP, M.shape[1])
+
+        per_step = sum(np.einsum("skf,skg->sfg", steps(a), steps(b)) for a, b in ops)
+        # np.add.accumulate adds in order in fp32: one rounding per step, as the accumulator
+        total += np.add.accumulate(per_step.astype(np.float32), axis=0)[-1]
+    return total
+
+
+def gram_model_pearson(X, y, op, eps, terms=2):
+    """Signed Pearson of every pair (i, j) as the Gram path computes it (matrix [i, j])."""
+    n = X.shape[0]
+    if op == "divide":
+        d = np.where(np.abs(X) < np.float32(eps), np.copysign(np.float32(eps), X), X).astype(np.float32)
+        g = (np.float32(1.0) / d).astype(np.float32)
+    else:
+        g = X
+    ycen = (y.astype(np.float64) - y.astype(np.float64).mean()).astype(np.float32)
+    _, e = np.frexp(1.0 / np.abs(ycen).max())
+    s_y = np.ldexp(1.0, e - 1)
+    ys = (ycen * np.float32(s_y)).astype(np.float32)
+
+    def operands(c):
+        total = c.astype(np.float64).sum(0)
+        mu = (total / n).astype(np.float32).astype(np.float64)
+        dev = np.maximum(np.abs(c.max(0) - mu), np.abs(mu - c.min(0))) * (1 + 1e-6)
+        s = _pow2_scale(dev)
+        s_q = _pow2_scale(np.maximum(c.max(0).astype(np.float64) ** 2, c.min(0).astype(np.float64) ** 2)
+                          * (1 + 1e-6))
+        v = (c.astype(np.float64) * s - mu * s).astype(np.float32)      # fma: one rounding
+        q = (c * c).astype(np.float32) * s_q.astype(np.float32)         # exact power-of-two scale
+        return total, mu, s, s_q, v, q
+
+    sa, mua, sxa, sqa, va, qa = operands(X)
+    sg, mug, sxg, sqg, vg, qg = operands(g)
+    C = _gram(va, vg, terms) / np.outer(sxa, sxg)
+    Q = _gram(qa, qg, terms) / np.outer(sqa, sqg)
+    W = _gram(va, (vg * ys[:, None]).astype(np.float32), terms) / np.outer(sxa, sxg * s_y)
+    yc = ycen.astype(np.float64)
+    Ua, Ug, sum_y = X.astype(np.float64).T @ yc, g.astype(np.float64).T @ yc, yc.sum()
+    S1 = C + np.outer(mua, sg - n * mug) + np.outer(sa - n * mua, mug) + n * np.outer(mua, mug)
+    S3 = W + np.outer(mua, Ug) + np.outer(Ua, mug) - np.outer(mua, mug) * sum_y
+    var_x = Q - S1 * S1 / n
+    var_y = (yc * yc).sum() - sum_y * sum_y / n
+    with np.errstate(invalid="ignore", divide="ignore"):  # the diagonal i = j (a / a is constant)
+        return (S3 - S1 * sum_y / n) / np.sqrt(var_x * var_y)
+
+
+def _mixed(seed, n=40000, f=24):
+    rng = np.random.default_rng(seed)
+    X = np.hstack([rng.standard_normal((n, f // 2)), rng.lognormal(0, 1, (n, f // 2))]).astype(np.float32)
+    y = (rng.random(n) < 0.5 + 0.3 * np.tanh(X[:, 3] * X[:, 17])).astype(np.float32)
+    return X, y
+
+
+def _bound_ratio(got, want):
+    return np.max(np.abs(got - want) / (1e-4 * np.abs(want) + 1e-6))
+
+
+@pytest.mark.parametrize("op", ["multiply", "divide"])
+def test_two_fp16_terms_hold_the_pearson_bound(oracle, op):
+    X, y = _mixed(0)
+    pi, pj = oracle.all_pairs(X.shape[1])
+    want = oracle.raw_pearson(X, y, op, pi, pj, div_eps=1e-6)
+    got = gram_model_pearson(X, y, op, 1e-6, terms=2)[pi, pj]
+    assert _bound_ratio(got, want) < 0.05   # ~0.01 of the bound
+
+
+@pytest.mark.parametrize("op", ["multiply", "divide"])
+def test_one_fp16_term_misses_it(oracle, op):
+    X, y = _mixed(0)
+    pi, pj = oracle.all_pairs(X.shape[1])
+    want = oracle.raw_pearson(X, y, op, pi, pj, div_eps=1e-6)
+    got = gram_model_pearson(X, y, op, 1e-6, terms=1)[pi, pj]
+    assert not np.all(np.abs(got - want) <= 1e-4 * np.abs(want) + 1e-6)
+
+
+def test_error_follows_pair_conditioning(oracle):
+    """|error| <= 1e-6 * kappa * |r| + 1e-7 on columns offset from zero by 3 to 100
+    standard deviations (measured: within a fifth of that); at 10 (kappa up to ~200) every
+    pair holds the bound, at 100 (kappa ~1e3 to 1e4) some pair misses it."""
+    rng = np.random.default_rng(5)
+    n, f = 40000, 8
+    pi, pj = oracle.all_pairs(f)
+    within = {}
+    for off in (3.0, 10.0, 100.0):
+        X = (off + rng.standard_normal((n, f)) * rng.uniform(0.5, 2.0, f)).astype(np.float32)
+        y = (rng.random(n) < 1 / (1 + np.exp(-(X[:, 1] - X[:, 1].mean())))).astype(np.float32)
+        for op in ("multiply", "divide"):
+            want, st = oracle.raw_pearson(X, y, op, pi, pj, div_eps=1e-6, with_stats=True)
+            kappa = st[:, 3] / (st[:, 3] - st[:, 1] ** 2 / st[:, 0])
+            got = gram_model_pearson(X, y, op, 1e-6)[pi, pj]
+            err = np.abs(got - want)
+            assert np.all(err <= 1e-6 * kappa * np.abs(want) + 1e-7), (off, op)
+            within[(off, op)] = bool(np.all(err <= 1e-4 * np.abs(want) + 1e-6))
+    assert within[(3.0, "multiply")] and within[(3.0, "divide")]
+    assert within[(10.0, "multiply")] and within[(10.0, "divide")]
+    assert not (within[(100.0, "multiply")] and within[(100.0, "divide")])
