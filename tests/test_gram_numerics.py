@@ -11,9 +11,9 @@ semantics).  What it shows:
   * two fp16 terms hold the 1e-4 Pearson bound on normal and lognormal columns with a wide
     margin, and one term does not (why every operand is split);
   * the error grows with the pair's conditioning kappa = S2 / (S2 - S1^2 / n), because
-    S2 = sum (a g(b))^2 is accumulated uncentred: about 3e-7 * kappa relative.  Columns
-    whose mean is ~30 standard deviations from zero or more (kappa above ~300) can miss the
-    bound on this path.
+    S2 = sum (a g(b))^2 is accumulated uncentred: up to ~3e-7 * kappa relative here, and
+    the CUDA-core path's fp32 runs (modelled too) behave alike.  Columns whose mean is
+    ~30 standard deviations from zero or more (kappa above ~300) can miss the bound.
 """
 import numpy as np
 import pytest
@@ -123,24 +123,64 @@ def test_one_fp16_term_misses_it(oracle, op):
     assert not np.all(np.abs(got - want) <= 1e-4 * np.abs(want) + 1e-6)
 
 
-def test_error_follows_pair_conditioning(oracle):
-    """|error| <= 1e-6 * kappa * |r| + 1e-7 on columns offset from zero by 3 to 100
-    standard deviations (measured: within a fifth of that); at 10 (kappa up to ~200) every
-    pair holds the bound, at 100 (kappa ~1e3 to 1e4) some pair misses it."""
+def cuda_core_model_pearson(X, y, op, eps, pi, pj, run=256):
+    """Signed Pearson of the listed pairs as the CUDA-core moment path computes it
+    (gafime_b200/csrc/moments.cu): x = fl32(a op b), fp32 sums over runs of 256 rows, fp64
+    across runs.  Within a run the model adds rows in order; the kernel's order differs."""
+    n = X.shape[0]
+    ycen = (y.astype(np.float64) - y.astype(np.float64).mean()).astype(np.float32)
+    pad = (-n) % run
+    yr = np.concatenate([ycen, np.zeros(pad, np.float32)]).reshape(-1, run)
+    yc = ycen.astype(np.float64)
+    sum_y = yc.sum()
+    var_y = (yc * yc).sum() - sum_y * sum_y / n
+
+    def runs_sum(M):
+        return np.add.accumulate(M.astype(np.float32), axis=1)[:, -1].astype(np.float64).sum()
+
+    out = np.empty(len(pi))
+    for p, (i, j) in enumerate(zip(pi, pj)):
+        a, b = X[:, i], X[:, j]
+        if op == "divide":
+            d = np.where(np.abs(b) < np.float32(eps), np.copysign(np.float32(eps), b), b).astype(np.float32)
+            x = (a / d).astype(np.float32)
+        else:
+            x = (a * b).astype(np.float32)
+        xr = np.concatenate([x, np.zeros(pad, np.float32)]).reshape(-1, run)
+        S1, S2, S3 = runs_sum(xr), runs_sum(xr * xr), runs_sum(xr * yr)
+        out[p] = (S3 - S1 * sum_y / n) / np.sqrt((S2 - S1 * S1 / n) * var_y)
+    return out
+
+
+def _offset_cases(oracle):
+    """Columns offset from zero by 3, 10 and 100 standard deviations (kappa up to ~5, ~60
+    and ~8e3), with the oracle's scores and every pair's kappa."""
     rng = np.random.default_rng(5)
     n, f = 40000, 8
     pi, pj = oracle.all_pairs(f)
-    within = {}
     for off in (3.0, 10.0, 100.0):
         X = (off + rng.standard_normal((n, f)) * rng.uniform(0.5, 2.0, f)).astype(np.float32)
         y = (rng.random(n) < 1 / (1 + np.exp(-(X[:, 1] - X[:, 1].mean())))).astype(np.float32)
         for op in ("multiply", "divide"):
             want, st = oracle.raw_pearson(X, y, op, pi, pj, div_eps=1e-6, with_stats=True)
             kappa = st[:, 3] / (st[:, 3] - st[:, 1] ** 2 / st[:, 0])
+            yield off, op, X, y, pi, pj, want, kappa
+
+
+@pytest.mark.parametrize("path", ["gram", "cuda_core"])
+def test_error_follows_pair_conditioning(oracle, path):
+    """|error| <= 1e-6 * kappa * |r| + 1e-7 on both moment paths (measured: within a fifth
+    of that); 3 and 10 standard deviations out every pair holds the bound, 100 out some
+    pair misses it."""
+    within = {}
+    for off, op, X, y, pi, pj, want, kappa in _offset_cases(oracle):
+        if path == "gram":
             got = gram_model_pearson(X, y, op, 1e-6)[pi, pj]
-            err = np.abs(got - want)
-            assert np.all(err <= 1e-6 * kappa * np.abs(want) + 1e-7), (off, op)
-            within[(off, op)] = bool(np.all(err <= 1e-4 * np.abs(want) + 1e-6))
+        else:
+            got = cuda_core_model_pearson(X, y, op, 1e-6, pi, pj)
+        err = np.abs(got - want)
+        assert np.all(err <= 1e-6 * kappa * np.abs(want) + 1e-7), (off, op)
+        within[(off, op)] = bool(np.all(err <= 1e-4 * np.abs(want) + 1e-6))
     assert within[(3.0, "multiply")] and within[(3.0, "divide")]
     assert within[(10.0, "multiply")] and within[(10.0, "divide")]
     assert not (within[(100.0, "multiply")] and within[(100.0, "divide")])
