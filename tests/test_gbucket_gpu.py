@@ -69,6 +69,36 @@ def test_bucket_compute_matches_reference_cpu(lib, golden):
         b.free()
 
 
+def _train_r(st):
+    """Train-fold Pearson from the 12 float stats (n, sx, sy, sxx, syy, sxy first), the
+    formula of fused_kernel.py:236-264."""
+    n, sx, sy, sxx, syy, sxy = (float(v) for v in st[:6])
+    den = np.sqrt((n * sxx - sx * sx) * (n * syy - sy * sy))
+    return (n * sxy - sx * sy) / den if den > 0 else 0.0
+
+
+def test_mixed_interaction_chain(lib, oracle):
+    """A * B then + C against A * B * C on a target made of A * B + C, as the reference's
+    per-pair interaction test does (tests/test_perpair_interactions.py:21-82): both chains'
+    stats equal the oracle's, and the mixed chain's train r beats the all-multiply one's by
+    more than 0.1."""
+    rng = np.random.default_rng(42)
+    n = 10000
+    A, B, C = (rng.standard_normal(n).astype(np.float32) for _ in range(3))
+    y = (A * B + C + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    mask = rng.integers(0, 5, n, dtype=np.uint8)
+    b = Small(lib, np.column_stack([A, B, C]), y, mask)
+    try:
+        got = {inter: b.compute([0, 1, 2], [0, 0, 0], inter, 0) for inter in ((0, 1), (0, 0))}
+    finally:
+        b.free()
+    for inter, (rc, st) in got.items():
+        assert rc == 0
+        want = oracle.chain_stats([A, B, C], y, mask, [0, 0, 0], list(inter), 0)
+        np.testing.assert_allclose(st, want, rtol=RTOL, atol=ATOL, err_msg=str(inter))
+    assert _train_r(got[(0, 1)][1]) > _train_r(got[(0, 0)][1]) + 0.1
+
+
 def test_fused_interaction_matches_reference_cpu(lib, golden):
     g = golden("chains.npz")
     vf = int(g["val_fold"])
