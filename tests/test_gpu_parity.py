@@ -368,6 +368,21 @@ def test_interaction_materialiser_matches_oracle(native, golden, oracle):
     np.testing.assert_array_equal(native.feature_interaction(X, m, combos), oracle.feature_interaction(X, m, combos))
 
 
+@pytest.mark.parametrize("n,f,n_combos,size", [(10, 10, 5, 2), (1, 50, 10, 3), (1023, 127, 200, 2),
+                                               (4096, 4096, 64, 2)])
+def test_interaction_materialiser_smoke_shapes(native, oracle, n, f, n_combos, size):
+    """The reference's kernel smoke scenarios (tests/smoke_tests/verify_kernel.py): a 10 x 10
+    sanity case, a single row, prime dimensions, a 4096 x 4096 matrix; combos of distinct
+    features drawn at random, bit-identical to the oracle."""
+    rng = np.random.default_rng(42)
+    X = rng.standard_normal((n, f)).astype(np.float32)
+    m = X.mean(axis=0).astype(np.float32)
+    combos = [rng.choice(f, size=size, replace=False).tolist() for _ in range(n_combos)]
+    got = native.feature_interaction(X, m, combos)
+    assert got.shape == (n, n_combos)
+    np.testing.assert_array_equal(got, oracle.feature_interaction(X, m, combos))
+
+
 def test_interaction_materialiser_rejects_bad_arguments(native):
     import ctypes
     lib = native.load()
