@@ -660,7 +660,11 @@ int gafime_contiguous_bucket_gather(ContiguousBucket dst, ContiguousBucket src, 
     gather_mask_kernel<<<(unsigned)std::min<int64_t>((n_rows + 255) / 256, 4 * d->sm_count), 256, 0, d->stream>>>(
         s->d_mask, d_rows, n_rows, d->d_mask);
     e = cudaGetLastError();
-    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+    {
+        // also after a failure: the copy of the caller's row ids is not left in flight
+        const cudaError_t es = cudaStreamSynchronize(d->stream);
+        if (e == cudaSuccess) e = es;
+    }
     if (e != cudaSuccess) return status_from(e);
     // rows of finite data are finite; anything else is checked like an upload
     d->finite_state = s->finite_state == 1 ? 1 : -1;
