@@ -118,3 +118,31 @@ def test_pipeline_null_handles(lib):
     assert lib.gafime_pipeline_free(None) == 0
     assert lib.gafime_pipeline_poll(None, None, None) == -1
     assert lib.gafime_pipeline_init(None, 0, None) == -1
+
+
+def test_host_entry_points_check_their_arguments(lib):
+    """gafime_shard_tiles and gafime_topk_merge run on the host: bad arguments return -1,
+    a too-small tile buffer reports the count it needs, a NaN score ranks last."""
+    from gafime_b200 import _native
+    cnt = ctypes.c_int(-7)
+    out = np.zeros(2 * 64, dtype=np.int32)
+    p = out.ctypes.data
+    assert lib.gafime_shard_tiles(300, 0, 0, p, 64, ctypes.byref(cnt)) == -1   # no shards
+    assert lib.gafime_shard_tiles(300, 3, 3, p, 64, ctypes.byref(cnt)) == -1   # shard id out of range
+    assert lib.gafime_shard_tiles(300, 0, 1, None, 64, ctypes.byref(cnt)) == -1
+    assert lib.gafime_shard_tiles(300, 0, 1, p, 64, None) == -1
+    assert lib.gafime_shard_tiles(300, 0, 1, p, 2, ctypes.byref(cnt)) == -1    # 15 tiles needed
+    assert cnt.value == 15
+    assert lib.gafime_shard_tiles(300, 0, 1, p, 64, ctypes.byref(cnt)) == 0 and cnt.value == 15
+    o = np.zeros(4, dtype=np.int32)
+    s = np.zeros(4)
+    n = ctypes.c_int(0)
+    args = (o.ctypes.data, o.ctypes.data, s.ctypes.data, ctypes.byref(n))
+    assert lib.gafime_topk_merge(None, None, None, ctypes.c_int64(3), 2, *args) == -1
+    assert lib.gafime_topk_merge(None, None, None, ctypes.c_int64(0), 0, *args) == -1
+    assert lib.gafime_topk_merge(None, None, None, ctypes.c_int64(0), 2, *args) == 0 and n.value == 0
+    ci = np.array([0, 1, 2], dtype=np.int32)
+    cj = np.array([9, 8, 7], dtype=np.int32)
+    i, j, sc = _native.merge_topk(ci, cj, np.array([np.nan, -0.2, 0.1]), 3)
+    assert list(zip(i.tolist(), j.tolist())) == [(1, 8), (2, 7), (0, 9)]
+    assert np.isnan(sc[2])
