@@ -13,7 +13,8 @@ semantics).  What it shows:
   * the error grows with the pair's conditioning kappa = S2 / (S2 - S1^2 / n), because
     S2 = sum (a g(b))^2 is accumulated uncentred: up to ~3e-7 * kappa relative here, and
     the CUDA-core path's fp32 runs (modelled too) behave alike.  Columns whose mean is
-    ~30 standard deviations from zero or more (kappa above ~300) can miss the bound.
+    ~30 standard deviations from zero or more (kappa above ~300) can miss the bound in
+    raw-operator scoring; centred-product scoring removes the offset first and holds it.
 """
 import numpy as np
 import pytest
@@ -184,3 +185,17 @@ def test_error_follows_pair_conditioning(oracle, path):
     assert within[(3.0, "multiply")] and within[(3.0, "divide")]
     assert within[(10.0, "multiply")] and within[(10.0, "divide")]
     assert not (within[(100.0, "multiply")] and within[(100.0, "divide")])
+
+
+def test_centred_product_scoring_is_unaffected(oracle):
+    """The engine's centred-product semantics multiply fl32(a - mean) copies (the CUDA-core
+    path with centring): 100 standard deviations out, every pair holds the bound."""
+    rng = np.random.default_rng(5)
+    n, f = 40000, 8
+    pi, pj = oracle.all_pairs(f)
+    X = (100.0 + rng.standard_normal((n, f)) * rng.uniform(0.5, 2.0, f)).astype(np.float32)
+    y = (rng.random(n) < 1 / (1 + np.exp(-(X[:, 1] - X[:, 1].mean())))).astype(np.float32)
+    want, _ = oracle.centred_scores(X, y, pi, pj)
+    Xc = (X.astype(np.float64) - X.astype(np.float64).mean(axis=0)).astype(np.float32)
+    got = cuda_core_model_pearson(Xc, y, "multiply", 1e-6, pi, pj)
+    assert _bound_ratio(got, want) < 0.05
