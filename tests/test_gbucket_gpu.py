@@ -99,6 +99,28 @@ def test_mixed_interaction_chain(lib, oracle):
     assert _train_r(got[(0, 1)][1]) > _train_r(got[(0, 0)][1]) + 0.1
 
 
+def test_planted_product_is_detected(lib, oracle):
+    """The reference's signal-detection check (tests/scientific_benchmark.py:160-229): with
+    y = f0 * f1 + noise, the chain f0 * f1 has |train r| > 0.9 and f0 * noise, f1 * noise
+    stay below 0.1; the stats equal the oracle's."""
+    rng = np.random.RandomState(42)
+    n = 10000
+    cols = [rng.randn(n).astype(np.float32) for _ in range(3)]
+    y = (cols[0] * cols[1] + rng.randn(n) * 0.1).astype(np.float32)
+    mask = np.random.default_rng(42).integers(0, 5, size=n, dtype=np.uint8)
+    b = Small(lib, np.column_stack(cols), y, mask)
+    try:
+        got = {pair: b.compute(list(pair), [0, 0], [0], 0) for pair in ((0, 1), (0, 2), (1, 2))}
+    finally:
+        b.free()
+    for pair, (rc, st) in got.items():
+        assert rc == 0
+        want = oracle.chain_stats([cols[c] for c in pair], y, mask, [0, 0], [0], 0)
+        np.testing.assert_allclose(st, want, rtol=RTOL, atol=ATOL, err_msg=str(pair))
+    assert abs(_train_r(got[(0, 1)][1])) > 0.9
+    assert abs(_train_r(got[(0, 2)][1])) < 0.1 and abs(_train_r(got[(1, 2)][1])) < 0.1
+
+
 def test_fused_interaction_matches_reference_cpu(lib, golden):
     g = golden("chains.npz")
     vf = int(g["val_fold"])
