@@ -324,6 +324,27 @@ def test_wide_table_properties(native, oracle):
     assert {(int(a), int(c)) for a, c in zip(gi[:16], gj[:16])} == want
 
 
+def test_banking_table_properties(native, oracle):
+    """Config 4's shape (256 Zipf(1.1) integer codes of cardinality 2-1000 + 256 N(0,1)
+    columns, y = 0.5 c7 x300 + 0.3 x301 x302 + noise, multiply, k = 1000) at 3e5 rows:
+    every one of the 130,816 pair scores matches the oracle, the top-k equals the oracle's
+    modulo ties, and (7, 300) ranks first."""
+    from bench import fill_config4
+    n, f, k = 300_000, 512, 1000
+    packed = np.empty((f + 1, n), dtype=np.float32)
+    fill_config4(packed, n)
+    X, y = packed[:f].T, packed[f]
+    with native.Bucket(n, f) as b:
+        b.upload_packed(packed)
+        gi, gj, gs = b.topk(["multiply"], k)["multiply"]
+        allsc = b.scores("multiply")
+    pi, pj = oracle.all_pairs(f)
+    want = oracle.raw_pearson(X, y, "multiply", pi, pj)
+    assert_pearson_close(allsc, want)
+    assert_topk_equivalent(gi, gj, want, pi, pj, k)
+    assert (int(gi[0]), int(gj[0])) == (7, 300)
+
+
 _CUDA_CORE_SCRIPT = r"""
 import sys, numpy as np
 sys.path.insert(0, sys.argv[1])
