@@ -345,6 +345,28 @@ def test_banking_table_properties(native, oracle):
     assert (int(gi[0]), int(gj[0])) == (7, 300)
 
 
+def test_three_class_mi_table_properties(native, oracle):
+    """Config 3's shape (128 N(0,1) columns, 3-class target from argmax of x5 x9, x12 + x60
+    and noise; centred multiply; MI with 32 bins; k = 50) at 1e6 rows: every pair's MI
+    matches the oracle to 1e-5, the top-k equals the oracle's modulo ties, and (5, 9) then
+    (12, 60) rank first."""
+    rng = np.random.default_rng(3)
+    n, f, k = 1_000_000, 128, 50
+    X = rng.standard_normal((n, f), dtype=np.float32)
+    e = rng.standard_normal((4, n), dtype=np.float32)
+    s0 = X[:, 5].astype(np.float64) * X[:, 9] + 0.5 * e[0]
+    s1 = X[:, 12].astype(np.float64) + X[:, 60] + 0.5 * e[1]
+    y = np.argmax(np.stack([s0, s1, e[2] + 0.5 * e[3]]), axis=0).astype(np.float32)
+    with bucket_for(native, X, y) as b:
+        gi, gj, gs = b.topk(["multiply"], k, metric="mutual_info", center=True, mi_bins=32)["multiply"]
+        allmi = b.scores("multiply", metric="mutual_info", center=True, mi_bins=32)
+    pi, pj = oracle.all_pairs(f)
+    want = oracle.pair_mi(X, y, "multiply", center=True, mi_bins=32)
+    np.testing.assert_allclose(allmi, want, rtol=0, atol=1e-5)
+    assert_topk_equivalent(gi, gj, want, pi, pj, k, rtol=0, atol=1e-5)
+    assert [(int(a), int(c)) for a, c in zip(gi[:2], gj[:2])] == [(5, 9), (12, 60)]
+
+
 _CUDA_CORE_SCRIPT = r"""
 import sys, numpy as np
 sys.path.insert(0, sys.argv[1])
