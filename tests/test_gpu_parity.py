@@ -384,7 +384,6 @@ def test_interaction_materialiser_smoke_shapes(native, oracle, n, f, n_combos, s
 
 
 def test_interaction_materialiser_rejects_bad_arguments(native):
-    import ctypes
     lib = native.load()
     X = np.zeros((4, 3), np.float32)
     m = np.zeros(3, np.float32)
