@@ -349,6 +349,18 @@ def main():
     pad = np.array([list(c) + [-1] * (2 - len(c)) for c in scombos], dtype=np.int32)
     np.savez_compressed(os.path.join(HERE, "spearman.npz"), X=Xs, y3=ys3, yc=ysc, combos=pad, width=width,
                         spearman=spear)
+    # --- safe-divide divisors at the clamp (cpu_backend.cpp:93-94, eps = 1e-8): signed
+    # zeros, values below, at and above eps, subnormals; a column on the scale of eps --------
+    rng = np.random.default_rng(13)
+    nd = 96
+    special = np.array([0.0, -0.0, 5e-9, -5e-9, 1e-8, -1e-8, 2e-8, -2e-8, 1e-40, -1e-40, 1e-30, -3.0],
+                       dtype=np.float32)
+    Xd = np.column_stack([rng.standard_normal(nd).astype(np.float32), np.resize(special, nd),
+                          np.resize(special[::-1], nd),
+                          (rng.standard_normal(nd) * 1e-8).astype(np.float32)]).astype(np.float32)
+    yd = (rng.random(nd) < 0.5).astype(np.float32)
+    rawd = np.stack([ref_raw_stats(cpu, Xd, yd, op) for op in range(4)])
+    np.savez_compressed(os.path.join(HERE, "divisors.npz"), X=Xd, y=yd, ref_stats=rawd)
     print("wrote fixtures to", HERE)
 
 

@@ -71,6 +71,17 @@ def test_edge_cases_match_reference(golden, oracle):
         np.testing.assert_array_equal(stn.astype(np.float32), g["ref_stats_nan"][op_id][:, :6])
 
 
+def test_divisors_at_the_clamp_match_reference(golden, oracle):
+    """Safe divide at its clamp (cpu_backend.cpp:93-94, eps = 1e-8): -0.0 becomes -eps
+    (copysign), values below eps are replaced, eps itself is kept, subnormals are clamped;
+    every operator's stats equal the reference library's after its float cast."""
+    g = golden("divisors.npz")
+    assert np.signbit(g["X"][1, 1]) and g["X"][1, 1] == 0.0
+    for op_id, op in enumerate(OPS):
+        _, st = oracle.raw_pearson(g["X"], g["y"], op, div_eps=1e-8, with_stats=True)
+        np.testing.assert_array_equal(st.astype(np.float32), g["ref_stats"][op_id][:, :6])
+
+
 def test_topk_tie_order_is_pair_ascending(oracle):
     s = np.array([0.5, -0.5, 0.2, 0.5])
     pi = np.array([3, 0, 1, 0], dtype=np.int32)
