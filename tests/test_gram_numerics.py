@@ -14,7 +14,11 @@ semantics).  What it shows:
     S2 = sum (a g(b))^2 is accumulated uncentred: up to ~3e-7 * kappa relative here, and
     the CUDA-core path's fp32 runs (modelled too) behave alike.  Columns whose mean is
     ~30 standard deviations from zero or more (kappa above ~300) can miss the bound in
-    raw-operator scoring; centred-product scoring removes the offset first and holds it.
+    raw-operator scoring; centred-product scoring removes the offset first and holds it;
+  * products tiny against both columns lose their variance through S1, which is rebuilt
+    from a Gram of centred columns (the clamp fixture's multiply (1, 2));
+  * an error estimate from what the scoring epilogue holds (a pair's S1 and S2 and the
+    columns' spreads) flags exactly the pairs to re-score exactly.
 """
 import numpy as np
 import pytest
@@ -56,8 +60,9 @@ def _gram(A, B, terms):
     return total
 
 
-def gram_model_pearson(X, y, op, eps, terms=2):
-    """Signed Pearson of every pair (i, j) as the Gram path computes it (matrix [i, j])."""
+def gram_model_moments(X, y, op, eps, terms=2):
+    """The Gram path's raw moments of every pair (matrices [i, j]): S1 = sum x, S2 = sum x^2,
+    S3 = sum x ycen, with g(b) the B operand's column values, sum ycen and n var_y."""
     n = X.shape[0]
     if op == "divide":
         d = np.where(np.abs(X) < np.float32(eps), np.copysign(np.float32(eps), X), X).astype(np.float32)
@@ -89,10 +94,16 @@ def gram_model_pearson(X, y, op, eps, terms=2):
     Ua, Ug, sum_y = X.astype(np.float64).T @ yc, g.astype(np.float64).T @ yc, yc.sum()
     S1 = C + np.outer(mua, sg - n * mug) + np.outer(sa - n * mua, mug) + n * np.outer(mua, mug)
     S3 = W + np.outer(mua, Ug) + np.outer(Ua, mug) - np.outer(mua, mug) * sum_y
-    var_x = Q - S1 * S1 / n
     var_y = (yc * yc).sum() - sum_y * sum_y / n
+    return S1, Q, S3, g, sum_y, var_y
+
+
+def gram_model_pearson(X, y, op, eps, terms=2):
+    """Signed Pearson of every pair (i, j) as the Gram path computes it (matrix [i, j])."""
+    n = X.shape[0]
+    S1, S2, S3, _, sum_y, var_y = gram_model_moments(X, y, op, eps, terms)
     with np.errstate(invalid="ignore", divide="ignore"):  # the diagonal i = j (a / a is constant)
-        return (S3 - S1 * sum_y / n) / np.sqrt(var_x * var_y)
+        return (S3 - S1 * sum_y / n) / np.sqrt((S2 - S1 * S1 / n) * var_y)
 
 
 def _mixed(seed, n=40000, f=24):
@@ -199,3 +210,54 @@ def test_centred_product_scoring_is_unaffected(oracle):
     Xc = (X.astype(np.float64) - X.astype(np.float64).mean(axis=0)).astype(np.float32)
     got = cuda_core_model_pearson(Xc, y, "multiply", 1e-6, pi, pj)
     assert _bound_ratio(got, want) < 0.05
+
+
+def error_estimate_flags(S1, S2, n, sd_a, sd_g, c=1e-6, tau=1e-4):
+    """Pairs whose estimated Gram rounding of n var_x = S2 - S1^2 / n exceeds tau of it.
+    Two terms, one per limit mode: c * S2 (S2 is accumulated uncentred) and the rounding of
+    S1, which is rebuilt from a Gram of centred columns, e1 = c * sqrt(n) * sd_a * sd_g,
+    entering var_x as 2 |S1| e1 / n + e1^2 / n.  Only what the epilogue holds is used: the
+    pair's S1 and S2 and the columns' spreads."""
+    e1 = c * np.sqrt(n) * sd_a * sd_g
+    err = c * S2 + 2.0 * np.abs(S1) * e1 / n + e1 * e1 / n
+    return err > tau * np.maximum(S2 - S1 * S1 / n, 0.0)
+
+
+def test_error_estimate_flags_every_pair_the_path_misses(oracle, golden):
+    """With c = 1e-6 (about four times the rounding the model shows) and tau = 1e-4, the
+    estimate flags every pair of the model that misses the 1e-4 Pearson bound: offset
+    columns (large kappa) and the clamp fixture's tiny products.  It flags none on
+    normal/lognormal columns, Zipf codes, or columns 10 standard deviations out.  This is
+    the accuracy guard's criterion, to run in the scoring epilogue with an exact re-score
+    of the flagged pairs."""
+    rng = np.random.default_rng(4)
+    n = 40000
+    codes = np.stack([np.minimum(rng.zipf(1.1, n) - 1, rng.integers(2, 1000) - 1) for _ in range(6)], 1)
+    Xc = np.hstack([codes, rng.standard_normal((n, 6))]).astype(np.float32)
+    yc = (0.5 * Xc[:, 1] * Xc[:, 7] + rng.standard_normal(n)).astype(np.float32)
+    cases = [("mixed", *_mixed(0)), ("codes", Xc, yc)]
+    for off in (10.0, 100.0):
+        r = np.random.default_rng(int(off))
+        X = (off + r.standard_normal((n, 8)) * r.uniform(0.5, 2.0, 8)).astype(np.float32)
+        y = (r.random(n) < 1 / (1 + np.exp(-(X[:, 1] - X[:, 1].mean())))).astype(np.float32)
+        cases.append((f"offset {off:g}", X, y))
+    d = golden("divisors.npz")
+    cases.append(("clamp fixture", d["X"], d["y"]))
+    missed_any = False
+    for name, X, y in cases:
+        m, f = X.shape
+        pi, pj = oracle.all_pairs(f)
+        for op in ("multiply", "divide"):
+            want = oracle.raw_pearson(X, y, op, pi, pj, div_eps=1e-8)
+            S1, S2, S3, g, sum_y, var_y = gram_model_moments(X, y, op, 1e-8)
+            S1, S2, S3 = S1[pi, pj], S2[pi, pj], S3[pi, pj]
+            with np.errstate(invalid="ignore", divide="ignore"):
+                got = (S3 - S1 * sum_y / m) / np.sqrt((S2 - S1 * S1 / m) * var_y)
+            bad = ~(np.abs(got - want) <= 1e-4 * np.abs(want) + 1e-6)   # NaN counts as bad
+            flags = error_estimate_flags(S1, S2, m, X.astype(np.float64).std(axis=0)[pi],
+                                         g.astype(np.float64).std(axis=0)[pj])
+            assert not np.any(bad & ~flags), (name, op)
+            missed_any |= bool(bad.any())
+            if name in ("mixed", "codes", "offset 10"):
+                assert not flags.any(), (name, op, int(flags.sum()))
+    assert missed_any   # the cases do contain pairs the path gets wrong
