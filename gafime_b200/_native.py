@@ -48,14 +48,14 @@ EXPORTED = (
     "gafime_pipeline_init", "gafime_pipeline_submit", "gafime_pipeline_poll", "gafime_pipeline_wait",
     "gafime_pipeline_pending", "gafime_pipeline_flush", "gafime_pipeline_free", "gafime_pearson_cuda",
     "gafime_contiguous_bucket_upload_target", "gafime_contiguous_bucket_gather", "gafime_spearman_scores",
-    "gafime_allpairs_topk_host", "gafime_contiguous_bucket_upload_rows",
+    "gafime_allpairs_topk_host", "gafime_contiguous_bucket_upload_rows", "gafime_allpairs_rescored",
 )
 
 # kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
 KERNEL_IDS = {"column_stats": 1, "pair_moments": 2, "epilogue_topk": 3, "merge": 4,
               "mi_pass1": 5, "mi_pass2": 6, "mi_finish": 7, "legacy_pair": 8,
               "finite_check": 9, "gram_tc": 10, "gram_prep": 11, "gram_reduce": 12,
-              "mi_class_copy": 13}
+              "mi_class_copy": 13, "guard": 14}
 
 
 class GafimeError(RuntimeError):
@@ -99,6 +99,7 @@ def _bind(lib: ctypes.CDLL) -> None:
                                       _i),
         "gafime_allpairs_scores_noalloc": ([_vp, _i64, _vp, _i, _i, _i, _f, _vp, _vp], _i),
         "gafime_unary_scores": ([_vp, _i, _i, _vp], _i),
+        "gafime_allpairs_rescored": ([_vp, ctypes.POINTER(_i64)], _i),
         "gafime_shard_tiles": ([_i, _i, _i, _vp, _i, _ip], _i),
         "gafime_feature_interaction_cuda": ([_vp, _vp, _vp, _vp, _vp, ctypes.c_int32, ctypes.c_int32,
                                              ctypes.c_int32], _i),
@@ -241,6 +242,13 @@ class Bucket:
         return dst
 
     # -- scoring ------------------------------------------------------------------
+    def rescored(self) -> int:
+        """(pair, operator) Pearson scores the last all-pairs call took from the accuracy
+        guard's exact re-score (fp64 sums of fl32(a op b) per row)."""
+        c = ctypes.c_int64(0)
+        check("gafime_allpairs_rescored", self.lib.gafime_allpairs_rescored(self.handle, ctypes.byref(c)))
+        return int(c.value)
+
     def compute_pair(self, a: int, b: int, op_a: int = 0, op_b: int = 0, interact: int = 0,
                      val_fold_id: int = 255) -> np.ndarray:
         stats = np.zeros(12, dtype=np.float32)

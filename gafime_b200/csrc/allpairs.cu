@@ -195,9 +195,12 @@ int prepare(Bucket& b, int center, int metric, ColumnStats& cs, bool pair_scorin
 
 // Pearson per pair of every operator from the moments of its group (0: multiply / add /
 // subtract, 1: divide) and the per-list top-k (or every score into all_scores).
+// Before it, the accuracy guard flags the pairs whose moments may have lost the 1e-4
+// bound and re-scores them exactly (guard.cu); gram: the moments come from the tensor-core
+// Gram path.
 int queue_epilogue(Bucket& b, const ColumnStats& cs, const TileCoord* d_tiles, int nt, const int* ops, int n_ops,
                    const double* mom_mul, int splits_mul, const double* mom_div, int splits_div, int k_pad,
-                   int sub_lists, Cand* const* cands, double* all_scores) {
+                   int sub_lists, Cand* const* cands, double* all_scores, float div_eps, bool gram) {
     EpilogueArgs a;
     memset(&a, 0, sizeof(a));
     for (int o = 0; o < n_ops; ++o) {
@@ -217,6 +220,51 @@ int queue_epilogue(Bucket& b, const ColumnStats& cs, const TileCoord* d_tiles, i
     a.sub_lists = sub_lists;
     a.all_scores = all_scores;
     cudaError_t e;
+    {
+        // guard scratch: the re-score counter (first, where queue_rescored_read finds it),
+        // flags (bytes), exact scores and the re-score list
+        const size_t pairs = (size_t)n_ops * nt * kTilePairs;
+        const size_t off_count = 0, off_flags = 256;
+        const size_t off_exact = (off_flags + pairs + 255) / 256 * 256;
+        const size_t off_list = off_exact + pairs * sizeof(double);
+        e = ensure(b.guard, off_list + pairs * sizeof(uint2));
+        if (e != cudaSuccess) return status_from(e);
+        char* base = (char*)b.guard.ptr;
+        GuardArgs g;
+        memset(&g, 0, sizeof(g));
+        RescoreArgs r;
+        memset(&r, 0, sizeof(r));
+        for (int o = 0; o < n_ops; ++o) {
+            g.moments[o] = a.moments[o];
+            g.splits[o] = a.splits[o];
+            g.op[o] = r.op[o] = ops[o];
+        }
+        g.n_ops = n_ops;
+        g.tiles = r.tiles = d_tiles;
+        g.n_tiles = r.n_tiles = nt;
+        g.f = b.f;
+        g.colstats = cs.d_col;
+        g.ystats = r.ystats = cs.d_y;
+        g.gram = gram ? 1 : 0;
+        g.gstats = gram ? gram_col_state(b) : nullptr;
+        g.flags = (uint8_t*)(base + off_flags);
+        g.count = (unsigned long long*)(base + off_count);
+        g.list = (uint2*)(base + off_list);
+        r.x = cs.d_x;
+        r.y = b.d_data + b.f * b.ld;
+        r.ld = b.ld;
+        r.n = b.n;
+        r.eps = div_eps;
+        r.count = g.count;
+        r.list = g.list;
+        r.exact = (double*)(base + off_exact);
+        a.guard_flags = g.flags;
+        a.exact = r.exact;
+        KernelTimer timer(b.stream, GAFIME_KERNEL_GUARD);
+        e = launch_guard(g, r, b.sm_count, b.stream);
+        if (e != cudaSuccess) return status_from(e);
+        b.guard_ran = true;
+    }
     {
         KernelTimer timer(b.stream, GAFIME_KERNEL_EPILOGUE_TOPK);
         e = launch_epilogue_topk(a, b.stream);
@@ -274,11 +322,25 @@ int score_ops(Bucket& b, const ColumnStats& cs, const Plan& plan, const TileCoor
         }
     }
     return queue_epilogue(b, cs, d_tiles, nt, ops, n_ops, mom[0], group_splits[0], mom[1], group_splits[1], k_pad,
-                          sub_lists, cands, all_scores);
+                          sub_lists, cands, all_scores, div_eps, tensor);
 }
 
 int merge_and_copy(Bucket& b, Cand* const* cands, Cand* const* tmp, int n_lists, int k, int k_pad, int n_ops,
                    size_t per_op, int32_t* out_i, int32_t* out_j, double* out_score, int* out_count);
+
+// The guard's re-score count of this call: copied into the bucket's pinned staging on its
+// stream (queue), read after the caller's synchronize (finish).  MI calls run no guard and
+// leave the counter untouched, so they report 0.
+cudaError_t queue_rescored_read(Bucket& b) {
+    unsigned long long* h = reinterpret_cast<unsigned long long*>(b.h_pinned + 63);
+    *h = 0;
+    if (!b.guard_ran) return cudaSuccess;
+    return cudaMemcpyAsync(h, b.guard.ptr, sizeof(unsigned long long), cudaMemcpyDeviceToHost, b.stream);
+}
+
+void finish_rescored_read(Bucket& b) {
+    b.last_rescored += (int64_t)*reinterpret_cast<unsigned long long*>(b.h_pinned + 63);
+}
 
 // GAFIME_ERROR_KERNEL_FAILED when a Gram kernel of this call recorded a wait timeout
 int gram_status(Bucket& b, int gram_used) {
@@ -326,6 +388,8 @@ extern "C" int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact
     cudaSetDevice(b.device);
     for (int o = 0; o < n_ops; ++o) out_count[o] = 0;
 
+    b.last_rescored = 0;
+    b.guard_ran = false;
     Plan plan = make_plan(b, shard_id, n_shards);
     const int nt = (int)plan.tiles.size();
     if (nt == 0) return GAFIME_SUCCESS;
@@ -380,8 +444,11 @@ int merge_and_copy(Bucket& b, Cand* const* cands, Cand* const* tmp, int n_lists,
                             cudaMemcpyDeviceToHost, b.stream);
         if (e != cudaSuccess) return status_from(e);
     }
+    e = queue_rescored_read(b);
+    if (e != cudaSuccess) return status_from(e);
     e = cudaStreamSynchronize(b.stream);
     if (e != cudaSuccess) return status_from(e);
+    finish_rescored_read(b);
     for (int o = 0; o < n_ops; ++o) {
         int cnt = 0;
         for (int c = 0; c < k; ++c) {
@@ -414,6 +481,8 @@ extern "C" int gafime_allpairs_scores(ContiguousBucket bucket, int interact_type
     Bucket& b = *(Bucket*)bucket;
     if (b.f >= 65536) return GAFIME_ERROR_INVALID_ARGS;
     cudaSetDevice(b.device);
+    b.last_rescored = 0;
+    b.guard_ran = false;
     int64_t P = b.f * (b.f - 1) / 2;
     if (P == 0) return GAFIME_SUCCESS;
     Plan plan = make_plan(b, 0, 1);
@@ -432,8 +501,10 @@ extern "C" int gafime_allpairs_scores(ContiguousBucket bucket, int interact_type
     if (st != GAFIME_SUCCESS) return st;
     e = cudaMemcpyAsync(out_scores, b.scores.ptr, (size_t)P * sizeof(double), cudaMemcpyDeviceToHost,
                         b.stream);
+    if (e == cudaSuccess && metric == GAFIME_METRIC_PEARSON) e = queue_rescored_read(b);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b.stream);
     if (e != cudaSuccess) return status_from(e);
+    if (metric == GAFIME_METRIC_PEARSON) finish_rescored_read(b);
     return gram_status(b, gram_used);
 }
 
@@ -629,7 +700,8 @@ int streamed_topk_body(Bucket& b, const float* h_data, const uint8_t* h_mask, co
         cands[o] = (Cand*)b.cands.ptr + per_op * o;
         tmp[o] = (Cand*)b.cands2.ptr + per_op * o;
     }
-    st = queue_epilogue(b, cs, d_tiles, nt, ops, n_ops, mom[0], 1, mom[1], 1, k_pad, sub_lists, cands, nullptr);
+    st = queue_epilogue(b, cs, d_tiles, nt, ops, n_ops, mom[0], 1, mom[1], 1, k_pad, sub_lists, cands, nullptr,
+                        div_eps, true);
     if (st != GAFIME_SUCCESS) return st;
     st = merge_and_copy(b, cands, tmp, n_lists, k, k_pad, n_ops, per_op, out_i, out_j, out_score, out_count);
     if (st == GAFIME_SUCCESS) st = gram_status(b, 1);
@@ -681,6 +753,8 @@ extern "C" int gafime_allpairs_topk_host(ContiguousBucket bucket, const float* h
     Bucket& b = *(Bucket*)bucket;
     if (b.f >= 65536) return GAFIME_ERROR_INVALID_ARGS;
     cudaSetDevice(b.device);
+    b.last_rescored = 0;
+    b.guard_ran = false;
     for (int o = 0; o < n_ops; ++o) out_count[o] = 0;
     // the tensor-core Pearson path streams; the others score after a plain upload
     if (metric == GAFIME_METRIC_PEARSON && center == 0 && gram_path_enabled(b) && b.f >= 2)
@@ -690,4 +764,10 @@ extern "C" int gafime_allpairs_topk_host(ContiguousBucket bucket, const float* h
     if (st != GAFIME_SUCCESS) return st;
     return gafime_allpairs_topk(bucket, interact_types, n_ops, metric, center, div_eps, mi_bins, k, shard_id,
                                 n_shards, out_i, out_j, out_score, out_count);
+}
+
+extern "C" int gafime_allpairs_rescored(ContiguousBucket bucket, int64_t* out_count) {
+    if (!bucket || !out_count) return GAFIME_ERROR_INVALID_ARGS;
+    *out_count = ((Bucket*)bucket)->last_rescored;
+    return GAFIME_SUCCESS;
 }

@@ -54,7 +54,10 @@ struct Bucket {
     int sm_count = 148;
     // scratch
     DeviceBuf stats_part, stats, ycen, xcen, moments, cands, cands2, scores, flags, tiles, mi,
-        mi_hist, mi_mm, mi_xs, mi_split, gather, rank, gram, gram_cols;
+        mi_hist, mi_mm, mi_xs, mi_split, gather, rank, gram, gram_cols, guard;
+    // (pair, operator) scores the accuracy guard re-scored exactly in the last all-pairs call
+    int64_t last_rescored = 0;
+    bool guard_ran = false;      // the guard's counter (start of `guard`) belongs to this call
 };
 
 // Grow a scratch buffer to at least `bytes`; returns cudaSuccess or an error.
@@ -127,6 +130,9 @@ int64_t gram_chunk_rows(const Bucket& b, int ctas_per_chunk);
 cudaError_t gram_error_reset(Bucket& b, cudaStream_t stream);
 cudaError_t gram_error_read(Bucket& b, cudaStream_t stream, int* host_err);
 int gram_tiles128(const std::vector<TileCoord>& tiles64);
+// Per-column state of the Gram path (12 doubles per column; [6] sum g, [7] sum g^2 of the
+// divide side g = 1/safe(x)), valid after gram_prep_columns of this call.
+const double* gram_col_state(Bucket& b);
 
 // Scoring epilogue + per-tile top-k (select.cu).
 struct EpilogueArgs {
@@ -145,8 +151,45 @@ struct EpilogueArgs {
     int k_pad;                   // power of two >= k, <= 4096
     int sub_lists;               // candidate lists per tile (power of two, 4096 / sub_lists >= k_pad)
     double* all_scores;          // nullable, [P] triangle order (n_ops = 1)
+    // accuracy guard (guard.cu), nullable: a pair whose flag is set takes its exact score
+    const uint8_t* guard_flags;  // [n_ops][n_tiles][kTilePairs]
+    const double* exact;         // [n_ops][n_tiles][kTilePairs], written for flagged pairs only
 };
 cudaError_t launch_epilogue_topk(const EpilogueArgs& a, cudaStream_t stream);
+
+// Accuracy guard of the Pearson epilogue (guard.cu): flags the pairs whose estimated
+// rounding of n var_x is not small against it, and re-scores them exactly (fp64 sums of
+// fl32(a op b) per row, the reference CPU arithmetic).
+struct GuardArgs {
+    const double* moments[4];
+    int splits[4];
+    int op[4];
+    int n_ops;
+    const TileCoord* tiles;
+    int n_tiles;
+    int64_t f;
+    const double* colstats;      // [f*4]
+    const double* ystats;        // [4]
+    const double* gstats;        // Gram column state (12 doubles per column), required when gram
+    int gram;                    // moments from the tensor-core Gram path (S1 from centred Grams)
+    uint8_t* flags;              // out: [n_ops][n_tiles][kTilePairs]
+    unsigned long long* count;   // out: flagged entries (cleared by launch_guard)
+    uint2* list;                 // out: [capacity] (t * kTilePairs + e, operator index)
+};
+struct RescoreArgs {
+    const float* x;              // matrix the pair kernels read (f columns of ld floats)
+    const float* y;              // raw target (n floats, 16-byte aligned)
+    int64_t ld, n;               // column stride, rows
+    float eps;
+    int op[4];
+    const TileCoord* tiles;
+    int n_tiles;
+    const double* ystats;        // [4]
+    const unsigned long long* count;
+    const uint2* list;
+    double* exact;               // out: [n_ops][n_tiles][kTilePairs]
+};
+cudaError_t launch_guard(const GuardArgs& g, const RescoreArgs& r, int sm_count, cudaStream_t stream);
 // Candidate lists per tile for a top-k call: enough CTAs to fill the GPU.
 int epilogue_sub_lists(int n_tiles, int k_pad, int sm_count);
 

@@ -1713,6 +1713,11 @@ cudaError_t gram_error_reset(Bucket& b, cudaStream_t stream) {
     return e == cudaSuccess ? cudaMemsetAsync(g.err, 0, 64, stream) : e;
 }
 
+const double* gram_col_state(Bucket& b) {
+    GramCols g;
+    return gram_cols(b, g) == cudaSuccess ? g.cs : nullptr;
+}
+
 cudaError_t gram_error_read(Bucket& b, cudaStream_t stream, int* host_err) {
     GramCols g;
     cudaError_t e = gram_cols(b, g);

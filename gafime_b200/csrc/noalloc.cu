@@ -8,14 +8,19 @@
 // synchronisation that cudaMalloc/cudaFree may perform.  Such a caller passes its own
 // device input and output buffers, and this entry point keeps every intermediate
 // (column statistics, the centred target, per-tile moment partials, the tile list, the
-// finite-input flag) in one file-scope __device__ array of fixed size.
+// finite-input flag, the accuracy guard's flags, re-score list and exact scores, a copy of
+// the target) in one file-scope __device__ array of fixed size.  The moments come from the
+// CUDA-core pair-moment kernel (fp32 products in runs of 256 rows, fp64 across runs); the
+// pairs it cannot hold to 1e-4 are re-scored exactly, as in gafime_allpairs_scores.
 //
 // The array costs kScratchBytes (32 MiB) of device memory on every GPU where the
 // library is loaded, for the life of the process.  It is shared by all calls, so two
 // calls whose work overlaps on the GPU (different streams or threads) race on it; run
-// them one after the other.  The first call on each device looks up the array's device
+// them one after the other.  The first call on each device (and the first after that
+// device's context was re-created, e.g. by cudaDeviceReset) looks up the array's device
 // address with cudaGetSymbolAddress (see device_scratch below); make that first call
 // before any stream capture begins.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -30,7 +35,8 @@ namespace {
 
 constexpr int kMaxFeatures = GAFIME_NOALLOC_MAX_FEATURES;       // 256 -> at most 10 pair tiles
 constexpr int64_t kMaxRows = GAFIME_NOALLOC_MAX_ROWS;           // 2,097,152 padded rows
-constexpr int kMaxTileSplits = 170;                              // tiles x row splits
+constexpr int kMaxTileSplits = 150;                              // tiles x row splits
+constexpr int kMaxTiles = 10;                                    // 64-tiles of 256 features
 constexpr int kMaxColSplits = 2048;                              // (column, split) partials
 
 // Scratch layout (byte offsets, each 256-aligned).
@@ -45,8 +51,20 @@ constexpr size_t kPartBytes = (size_t)kMaxColSplits * 3 * sizeof(double);
 constexpr size_t kTilesOff = (kPartOff + kPartBytes + 255) / 256 * 256;
 constexpr size_t kTilesBytes = 64 * sizeof(TileCoord);
 constexpr size_t kFlagOff = (kTilesOff + kTilesBytes + 255) / 256 * 256;
+constexpr size_t kYOff = kFlagOff + 256;                         // copy of the target (16-byte aligned)
+constexpr size_t kYBytes = (size_t)kMaxRows * sizeof(float);
+constexpr size_t kGuardCountOff = (kYOff + kYBytes + 255) / 256 * 256;
+constexpr size_t kGuardFlagsOff = kGuardCountOff + 256;
+constexpr size_t kGuardFlagsBytes = (size_t)kMaxTiles * kTilePairs;
+constexpr size_t kGuardExactOff = (kGuardFlagsOff + kGuardFlagsBytes + 255) / 256 * 256;
+constexpr size_t kGuardExactBytes = (size_t)kMaxTiles * kTilePairs * sizeof(double);
+constexpr size_t kGuardListOff = (kGuardExactOff + kGuardExactBytes + 255) / 256 * 256;
+constexpr size_t kGuardListBytes = (size_t)kMaxTiles * kTilePairs * sizeof(uint2);
+constexpr size_t kScratchEnd = kGuardListOff + kGuardListBytes;
 constexpr size_t kScratchBytes = 32u << 20;
-static_assert(kFlagOff + 256 <= kScratchBytes, "no-alloc scratch layout exceeds its array");
+static_assert(kScratchEnd <= kScratchBytes, "no-alloc scratch layout exceeds its array");
+static_assert((kMaxFeatures + kTile - 1) / kTile * ((kMaxFeatures + kTile - 1) / kTile + 1) / 2 <= kMaxTiles,
+              "guard regions hold every tile");
 
 // The scratch itself.  Host code must not use this name as a pointer: on the host it
 // only stands for the symbol; device_scratch() returns its real device address.
@@ -55,23 +73,61 @@ __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 unsigned char* g_addr[kMaxDevices] = {};
+CUcontext g_ctx[kMaxDevices] = {};
+
+// The driver's current context (the device's primary context under the runtime), read
+// through the runtime's driver entry point so the library needs no libcuda link.
+CUcontext current_context() {
+    using GetCurrent = CUresult (*)(CUcontext*);
+    static GetCurrent fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<GetCurrent>(p);
+    });
+    CUcontext c = nullptr;
+    if (fn) fn(&c);
+    return c;
+}
 
 // Device address of g_noalloc_scratch on the current device, looked up once per device
-// (with that device current) and cached.
+// (with that device current) and cached.  The cache is keyed on the device's context as
+// well: cudaDeviceReset ends the context, and the new one loads the module again at a new
+// address, which the next call then looks up.
 cudaError_t device_scratch(unsigned char** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_addr[dev]) {
+    // a thread the runtime has not bound to the context yet reads none: look up again
+    const CUcontext ctx = current_context();
+    if (!g_addr[dev] || !ctx || g_ctx[dev] != ctx) {
         void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);   // initialises the context if needed
         if (e != cudaSuccess) return e;
         g_addr[dev] = static_cast<unsigned char*>(p);
+        g_ctx[dev] = current_context();
     }
     *out = g_addr[dev];
     return cudaSuccess;
+}
+
+// Input check over the caller's matrix: rows below n must be finite, rows n .. ld-1 must be
+// zero (the moment kernel sums every row of a column).  flag |= 1 otherwise.
+__global__ void noalloc_input_check_kernel(const float* __restrict__ x, int64_t cols, int64_t ld, int64_t n,
+                                           int* __restrict__ flag) {
+    const int64_t total = cols * ld;
+    int bad = 0;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const float v = x[e];
+        bad |= (e % ld < n) ? !isfinite(v) : (v != 0.0f);
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(flag, 1);
 }
 
 // Upper-triangle 64 x 64 tiles in row-major order (one thread; at most 10 tiles).
@@ -118,15 +174,17 @@ extern "C" int gafime_allpairs_scores_noalloc(const float* d_x, int64_t ld, cons
     double* part = reinterpret_cast<double*>(base + kPartOff);
     TileCoord* tiles = reinterpret_cast<TileCoord*>(base + kTilesOff);
     int* flag = reinterpret_cast<int*>(base + kFlagOff);
+    float* y_copy = reinterpret_cast<float*>(base + kYOff);
 
     int dev = 0, sm = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sm, cudaDevAttrMultiProcessorCount, dev);
 
-    // finite inputs only, as gafime_allpairs_scores (the flag must start at zero)
+    // finite inputs only, as gafime_allpairs_scores, and zero padding rows (the flag must
+    // start at zero)
     e = cudaMemsetAsync(flag, 0, sizeof(int), s);
     if (e != cudaSuccess) return status_from(e);
-    finite_kernel<<<4 * sm, 256, 0, s>>>(d_x, f, ld, n, flag);
+    noalloc_input_check_kernel<<<4 * sm, 256, 0, s>>>(d_x, f, ld, n, flag);
     finite_kernel<<<4 * sm, 256, 0, s>>>(d_y, 1, n, n, flag);
     int h_flag = 0;
     e = cudaMemcpyAsync(&h_flag, flag, sizeof(int), cudaMemcpyDeviceToHost, s);
@@ -162,6 +220,7 @@ extern "C" int gafime_allpairs_scores_noalloc(const float* d_x, int64_t ld, cons
                             interact_type == GAFIME_INTERACT_DIV, div_eps, moments, s);
     if (e != cudaSuccess) return status_from(e);
     EpilogueArgs a;
+    memset(&a, 0, sizeof(a));
     a.moments[0] = moments;
     a.splits[0] = splits;
     a.op[0] = interact_type;
@@ -175,6 +234,40 @@ extern "C" int gafime_allpairs_scores_noalloc(const float* d_x, int64_t ld, cons
     a.k_pad = 1;
     a.sub_lists = 1;
     a.all_scores = d_scores_out;
+    {
+        // accuracy guard and exact re-score, as the allocating entry points run them (the
+        // re-score reads the target from a 16-byte aligned copy in the scratch array)
+        GuardArgs g;
+        memset(&g, 0, sizeof(g));
+        RescoreArgs r;
+        memset(&r, 0, sizeof(r));
+        g.moments[0] = moments;
+        g.splits[0] = splits;
+        g.op[0] = r.op[0] = interact_type;
+        g.n_ops = 1;
+        g.tiles = r.tiles = tiles;
+        g.n_tiles = r.n_tiles = nt;
+        g.f = f;
+        g.colstats = colstats;
+        g.ystats = r.ystats = ystats;
+        g.gram = 0;
+        g.flags = reinterpret_cast<uint8_t*>(base + kGuardFlagsOff);
+        g.count = reinterpret_cast<unsigned long long*>(base + kGuardCountOff);
+        g.list = reinterpret_cast<uint2*>(base + kGuardListOff);
+        r.x = d_x;
+        r.y = y_copy;
+        r.ld = ld;
+        r.n = n;
+        r.eps = div_eps;
+        r.count = g.count;
+        r.list = g.list;
+        r.exact = reinterpret_cast<double*>(base + kGuardExactOff);
+        e = cudaMemcpyAsync(y_copy, d_y, (size_t)n * sizeof(float), cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess) e = launch_guard(g, r, sm, s);
+        if (e != cudaSuccess) return status_from(e);
+        a.guard_flags = g.flags;
+        a.exact = r.exact;
+    }
     e = launch_epilogue_topk(a, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     return status_from(e);

@@ -82,6 +82,11 @@ __global__ void __launch_bounds__(kEpiThreads) epilogue_topk_kernel(EpilogueArgs
                 cov = S3;
             }
             c.score = pearson(n, sx, sxx, cov, var_y);
+            if (a.guard_flags) {
+                // a pair the accuracy guard flagged takes its exact re-score (guard.cu)
+                const int64_t g = ((int64_t)oi * a.n_tiles + t) * kTilePairs + e;
+                if (a.guard_flags[g]) c.score = a.exact[g];
+            }
             c.pid = (uint32_t)(i * f + j);
             if (a.all_scores) {
                 int64_t p = i * f - i * (i + 1) / 2 + (j - i - 1);

@@ -255,6 +255,18 @@ int gafime_allpairs_scores(ContiguousBucket bucket, int interact_type, int metri
                            float div_eps, int mi_bins, double* out_scores);
 
 /*
+ * NEW.  Number of (pair, operator) Pearson scores that the last gafime_allpairs_topk,
+ * gafime_allpairs_topk_host or gafime_allpairs_scores call on this bucket took from an
+ * exact re-score.  The pair moments come from fp32 accumulations; an accuracy guard
+ * estimates each pair's rounding of its interaction's variance (the pair's sum of squares
+ * for columns far from zero, the columns' spreads for products tiny against them) and
+ * re-scores the pairs where it is not small against that variance with fp64 sums of
+ * fl32(a op b) per row, the reference CPU arithmetic (cpu_backend.cpp:87-103,274-293).
+ * 0 for mutual information and on data with well-conditioned pairs.
+ */
+int gafime_allpairs_rescored(ContiguousBucket bucket, int64_t* out_count);
+
+/*
  * NEW.  Score of every single feature (unary combo) against the target, F entries:
  * Pearson of the raw column (pearson_from_sums, gafime_core.cpp:179-198) or equal-width
  * mutual information of the raw column (gafime_core.cpp:559-569 with k == 1).  Serves
@@ -304,6 +316,7 @@ int gafime_topk_merge(const int32_t* cand_i, const int32_t* cand_j, const double
 #define GAFIME_KERNEL_GRAM_PREP 11
 #define GAFIME_KERNEL_GRAM_REDUCE 12
 #define GAFIME_KERNEL_MI_CLASS_COPY 13
+#define GAFIME_KERNEL_GUARD 14
 
 /* NEW.  enable = 1: drop any previous records, then bracket every engine kernel
  * launch with CUDA events on its stream.  enable = 0: stop recording (the records
