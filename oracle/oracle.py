@@ -9,6 +9,8 @@ Makefile beside it); this file loads it with ctypes and adds the selection step:
 
 * ``raw_pearson``      -- kernel-API semantics (``src/cpu/cpu_backend.cpp:87-103,229-295``,
   fp64 sums kept) + Pearson of ``native_cuda_backend.py:471-486``.
+* ``gram_raw_pearson`` -- the same sums for multiply over every pair as fp64 BLAS Grams
+  (exact products), for matrices where the per-pair loop is too slow.
 * ``centred_scores``   -- ``gafime_core.score_combos`` semantics for 2-combos
   (``gafime_core/src/gafime_core.cpp:425-623``): centred Pearson and equal-width MI.
 * ``topk``             -- stable selection by |score| descending
@@ -109,6 +111,47 @@ def raw_pearson(X: np.ndarray, y: np.ndarray, op: str, pi=None, pj=None,
         flat, ld, yv, n, pi, pj, len(pi), OP_IDS[op], np.float32(div_eps), out,
         stats.ctypes.data if with_stats else None)
     return (out, stats) if with_stats else out
+
+
+def gram_raw_pearson(cols: np.ndarray, y: np.ndarray, n_rows: Optional[int] = None,
+                     chunk_elems: int = 1 << 25) -> np.ndarray:
+    """Signed raw-operator Pearson of x = a * b for every pair i < j of the columns of
+    ``cols`` (F x n float32, one column per row of the array), as fp64 Gram matrices.
+
+    The reference sums, per pair, x, x^2 and x*y over the rows in fp64
+    (``src/cpu/cpu_backend.cpp:229-295``) with x rounded to fp32 (``cpu_backend.cpp:100-101``);
+    here the same three sums are entries of X^T X, (X o X)^T (X o X) and X^T diag(y) X
+    computed by fp64 BLAS in row chunks, with x = a * b exact (a 24-bit by 24-bit product
+    fits fp64).  It differs from the element-rounded sums only by the rounding of x, so it
+    serves as the every-pair oracle where the per-pair loop is too slow (1e7 x 512,
+    2e6 x 2048); the tests pin it against ``raw_pearson`` on the pairs they check."""
+    cols = np.asarray(cols)
+    f, n = cols.shape
+    if n_rows is not None:
+        n = int(n_rows)
+    yv = np.asarray(y, dtype=np.float64)[:n]
+    chunk = max(1024, chunk_elems // max(1, f))
+    G1 = np.zeros((f, f))
+    G2 = np.zeros((f, f))
+    G3 = np.zeros((f, f))
+    for r0 in range(0, n, chunk):
+        r1 = min(n, r0 + chunk)
+        A = cols[:, r0:r1].astype(np.float64)
+        G1 += A @ A.T
+        G3 += (A * yv[r0:r1]) @ A.T
+        A *= A
+        G2 += A @ A.T
+    pi, pj = np.triu_indices(f, k=1)
+    S1, S2, S3 = G1[pi, pj], G2[pi, pj], G3[pi, pj]
+    sy, syy = yv.sum(), (yv * yv).sum()
+    var_x = S2 - S1 * S1 / n
+    var_y = syy - sy * sy / n
+    cov = S3 - S1 * sy / n
+    d = var_x * var_y
+    out = np.zeros(len(pi))
+    ok = d > 0.0
+    out[ok] = cov[ok] / np.sqrt(d[ok])
+    return out
 
 
 def centred_scores(X: np.ndarray, y: np.ndarray, pi=None, pj=None, pearson: bool = True,

@@ -165,3 +165,22 @@ def test_spearman_matches_gafime_core(golden, oracle, target):
     combos = [tuple(int(v) for v in c if v >= 0) for c in g["combos"]]
     got = oracle.spearman(g["X"], g[target], combos)
     np.testing.assert_allclose(got, g["spearman"][0 if target == "y3" else 1], rtol=0, atol=1e-13)
+
+
+def test_gram_oracle_matches_the_element_rounded_oracle(golden, oracle):
+    """The fp64 Gram restatement (exact products) equals the per-pair element-rounded
+    restatement within the parity tolerance on normal, lognormal and Zipf-code columns, and
+    the latter is pinned to the reference's cpu_backend.cpp (raw_ops.npz)."""
+    rng = np.random.default_rng(3)
+    n = 20000
+    codes = np.minimum(np.floor((1.0 - rng.random((n, 8)) * (1.0 - 900.0 ** -0.1)) ** -10.0) - 1.0, 899.0)
+    X = np.hstack([rng.standard_normal((n, 8)), rng.lognormal(0.0, 1.0, (n, 8)), codes]).astype(np.float32)
+    y = (0.3 * X[:, 1] * X[:, 9] + rng.standard_normal(n)).astype(np.float32)
+    got = oracle.gram_raw_pearson(np.ascontiguousarray(X.T), y, chunk_elems=1 << 16)
+    want = oracle.raw_pearson(X, y, "multiply")
+    assert np.all(np.abs(got - want) <= 1e-4 * np.abs(want) + 1e-6)
+    g = golden("raw_ops.npz")
+    Xg, yg = g["X"], g["y"]
+    got = oracle.gram_raw_pearson(np.ascontiguousarray(Xg.T), yg)
+    want = oracle.raw_pearson(Xg, yg, "multiply")
+    assert np.all(np.abs(got - want) <= 1e-4 * np.abs(want) + 1e-6)
