@@ -1,8 +1,12 @@
 #!/usr/bin/env python
 """All-pairs feature-pair x row scoring throughput on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload config2]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload config5]
                     [--impl ours|reference]
+
+The default workload is the 2e6 x 2048 wide table (2,096,128 pairs, multiply, |Pearson|,
+k = 1000), a fixed job split across the GPUs (strong scaling); the other configurations
+run with --workload.
 
 One step = one pass of the hot path over the workload: column statistics, the
 pair-moment kernels, the scoring epilogue with top-k, the device merge, the D2H of
@@ -183,12 +187,13 @@ def measured_peaks():
 
 
 # Per-launch DRAM traffic of the dominant kernel from one ncu capture
-# (dram__bytes_read.sum + dram__bytes_write.sum); see profiles/ for the command.
+# (dram__bytes_read.sum + dram__bytes_write.sum), with the command that made it recorded
+# beside the capture's summary.
 NCU_TRAFFIC_BYTES = {
-    # profiles/pair_moments_config2.md: mul-group launch, 1.0298 GB read + 5.09 MB written
+    # CUDA-core moment kernel, multiply-group launch: 1.0298 GB read + 5.09 MB written
     ("config2", "pair_moments"): 1.0349e9,
-    # profiles/gram_fused_config2.md: 250k-row capture (258 MB read: the fp32 matrix once;
-    # ~86 MB of chunk partials written) scaled by the rows processed to 1e6 rows
+    # Gram kernel, 250k-row capture (258 MB read: the fp32 matrix once; ~86 MB of chunk
+    # partials written) scaled by the rows processed to 1e6 rows
     ("config2", "gram_tc"): 1.376e9,
 }
 
@@ -585,6 +590,7 @@ def run_ours(args):
     all_ms, all_launches = _native.profile_read("all")
     clk = clocks.stop()
     result = step()
+    rescored = bucket.rescored()   # pairs the accuracy guard re-scored exactly in one step
     per_step_kernels = count_library_kernels(score)  # no collective inside the trace
 
     # e2e: the same step through the C ABI from pinned host buffers, upload included
@@ -680,6 +686,8 @@ def run_ours(args):
         "e2e": {"value": e2e_value, "unit": "evals/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
         "kernels": kernel_ms,
+        # (pair, operator) scores taken from the accuracy guard's exact re-score per step
+        "rescored_pairs_per_step": rescored,
         # library kernels in the timed region: one step's launches from a CUDA activity trace
         # taken after it, times the steps (the library's timer scopes, which may hold several
         # kernels each, when no trace could be taken)
@@ -703,7 +711,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config5")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rows", type=int, default=0,
