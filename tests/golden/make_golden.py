@@ -4,7 +4,7 @@ Run here, where the reference sources are present:
 
     make -C oracle ref                      # compiles the reference's cpu_backend.cpp
                                             # and gafime_core.cpp, unmodified, into oracle/_ref/
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref DIR]   (default $GAFIME_REFERENCE_DIR, else /root/reference)
 
 Every expected value in the fixtures comes from the reference itself:
 
@@ -121,7 +121,7 @@ def sha(a: np.ndarray) -> str:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("GAFIME_REFERENCE_DIR", "/root/reference"))
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     core = _load_core()

@@ -6,6 +6,9 @@ import re
 import numpy as np
 import pytest
 
+# where the reference sources are read (they exist only where the reference is checked out)
+REFERENCE_DIR = os.environ.get("GAFIME_REFERENCE_DIR", "/root/reference")
+
 from conftest import REPO
 
 HEADER = os.path.join(REPO, "include", "gafime_b200.h")
@@ -81,7 +84,7 @@ def test_reference_backend_ctypes_setup_binds_this_library(lib):
     sources are present; the setup only sets ctypes signatures)."""
     import importlib
     import sys
-    ref = "/root/reference"
+    ref = REFERENCE_DIR
     if not os.path.isdir(os.path.join(ref, "gafime")):
         pytest.skip("reference sources not present")
     sys.path.insert(0, ref)
@@ -99,7 +102,7 @@ def test_reference_fused_kernel_wrappers_bind_this_library(lib):
     (gafime/backends/fused_kernel.py:375-393, 532-602) bind every symbol they need."""
     import importlib
     import sys
-    ref = "/root/reference"
+    ref = REFERENCE_DIR
     if not os.path.isdir(os.path.join(ref, "gafime")):
         pytest.skip("reference sources not present")
     sys.path.insert(0, ref)
