@@ -522,35 +522,23 @@ def run_ours(args):
         return bucket.topk(ops, k, metric=w["metric"], center=w["center"], div_eps=w["eps"],
                            mi_bins=w["bins"], shard_id=rank, n_shards=world)
 
+    # Multi-GPU candidate exchange on device buffers: each rank's top-k lists stay on its GPU
+    # (topk_device, queued on the bucket's stream), NCCL all-gathers them on that stream, and
+    # the gathered lists are merged on the device; one host copy of the k best per step.
+    L = _native.list_len(k)
+    if world > 1:
+        cand_dev = torch.empty(len(ops) * L * 2, dtype=torch.int64, device="cuda")        # 16-byte records
+        cand_all = torch.empty(world * len(ops) * L * 2, dtype=torch.int64, device="cuda")
+        bucket_stream = torch.cuda.ExternalStream(bucket.stream_ptr())
+
     def step():
-        return gather_merge(score())
-
-    # candidate exchange buffers, allocated once: pinned host staging and device tensors
-    cand_host = torch.empty(len(ops) * 3 * k, dtype=torch.float64, pin_memory=True)
-    cand_all_host = torch.empty(world * len(ops) * 3 * k, dtype=torch.float64, pin_memory=True)
-    cand_dev = torch.empty(len(ops) * 3 * k, dtype=torch.float64, device="cuda") if world > 1 else None
-    cand_all_dev = torch.empty(world * len(ops) * 3 * k, dtype=torch.float64, device="cuda") if world > 1 else None
-
-    def gather_merge(res):
         if world == 1:
-            return res
-        # all-gather every shard's candidates over NCCL, then the deterministic merge
-        flat = cand_host.numpy().reshape(len(ops), 3, k)
-        flat.fill(-1.0)
-        for o, op in enumerate(ops):
-            i, j, s = res[op]
-            flat[o, 0, :len(i)] = i
-            flat[o, 1, :len(j)] = j
-            flat[o, 2, :len(s)] = s
-        cand_dev.copy_(cand_host, non_blocking=True)
-        dist.all_gather_into_tensor(cand_all_dev, cand_dev)
-        cand_all_host.copy_(cand_all_dev)
-        allc = cand_all_host.numpy().reshape(world, len(ops), 3, k)
-        merged = {}
-        for o, op in enumerate(ops):
-            c = allc[:, o].transpose(1, 0, 2).reshape(3, -1)
-            merged[op] = _native.merge_topk(c[0].astype(np.int32), c[1].astype(np.int32), c[2], k)
-        return merged
+            return score()
+        bucket.topk_device(ops, k, cand_dev.data_ptr(), metric=w["metric"], center=w["center"],
+                           div_eps=w["eps"], mi_bins=w["bins"], shard_id=rank, n_shards=world)
+        with torch.cuda.stream(bucket_stream):
+            dist.all_gather_into_tensor(cand_all, cand_dev)
+        return bucket.merge_device(cand_all.data_ptr(), world, ops, k)
 
     def timed(loop_fn, steps):
         if world > 1:
@@ -592,14 +580,43 @@ def run_ours(args):
     result = step()
     rescored = bucket.rescored()   # pairs the accuracy guard re-scored exactly in one step
     per_step_kernels = count_library_kernels(score)  # no collective inside the trace
+    # library kernel time per step on every rank (the step is the slowest rank's)
+    rank_kernel_ms = [all_ms / args.steps]
+    multi_check = None
+    if world > 1:
+        t = torch.tensor([all_ms / args.steps], dtype=torch.float64, device="cuda")
+        allt = torch.empty(world, dtype=torch.float64, device="cuda")
+        dist.all_gather_into_tensor(allt, t)
+        rank_kernel_ms = allt.cpu().tolist()
+        if rank == 0:
+            # the N ranks' merged top-k against one GPU's top-k of the whole matrix
+            single = bucket.topk(ops, k, metric=w["metric"], center=w["center"], div_eps=w["eps"],
+                                 mi_bins=w["bins"])
+            same = all(np.array_equal(u, v) for op in ops for u, v in zip(result[op], single[op]))
+            multi_check = "merged top-k of %d ranks %s the single-GPU top-k" % (world, "equals" if same else
+                                                                                 "DIFFERS FROM")
+        dist.barrier()
 
     # e2e: the same step through the C ABI from pinned host buffers, upload included
     # (gafime_allpairs_topk_host: the copy of each column block overlapped with the scoring
-    # of the tiles it completes)
+    # of the tiles it completes); with N > 1 the shards' results are exchanged from the host
+    # copies every rank holds after that call (all-gather of 16-byte records, device merge)
     def e2e_step():
         res = bucket.topk_from_host(packed, ops, k, metric=w["metric"], center=w["center"], div_eps=w["eps"],
                                     mi_bins=w["bins"], shard_id=rank, n_shards=world, mask=mask)
-        return gather_merge(res)
+        if world == 1:
+            return res
+        rec = np.zeros((len(ops), L, 2), dtype=np.int64)
+        for o, op in enumerate(ops):
+            i, j, sc = res[op]
+            rec[o, :, 1] = np.int64(0xFFFFFFFF)
+            rec[o, :len(i), 0] = np.asarray(sc, dtype=np.float64).view(np.int64)
+            rec[o, :len(i), 1] = (i.astype(np.int64) * f + j.astype(np.int64))
+        cand_dev.copy_(torch.from_numpy(rec.reshape(-1)))
+        with torch.cuda.stream(bucket_stream):
+            bucket_stream.wait_stream(torch.cuda.current_stream())
+            dist.all_gather_into_tensor(cand_all, cand_dev)
+        return bucket.merge_device(cand_all.data_ptr(), world, ops, k)
 
     for _ in range(max(1, args.warmup // 2)):
         e2e_step()
@@ -688,6 +705,9 @@ def run_ours(args):
         "kernels": kernel_ms,
         # (pair, operator) scores taken from the accuracy guard's exact re-score per step
         "rescored_pairs_per_step": rescored,
+        "rank_kernel_ms_per_step": {"min": min(rank_kernel_ms), "max": max(rank_kernel_ms),
+                                    "per_rank": rank_kernel_ms},
+        "multi_gpu_check": multi_check,
         # library kernels in the timed region: one step's launches from a CUDA activity trace
         # taken after it, times the steps (the library's timer scopes, which may hold several
         # kernels each, when no trace could be taken)

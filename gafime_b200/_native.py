@@ -49,6 +49,7 @@ EXPORTED = (
     "gafime_pipeline_pending", "gafime_pipeline_flush", "gafime_pipeline_free", "gafime_pearson_cuda",
     "gafime_contiguous_bucket_upload_target", "gafime_contiguous_bucket_gather", "gafime_spearman_scores",
     "gafime_allpairs_topk_host", "gafime_contiguous_bucket_upload_rows", "gafime_allpairs_rescored",
+    "gafime_allpairs_topk_device", "gafime_topk_merge_device",
 )
 
 # kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
@@ -100,6 +101,8 @@ def _bind(lib: ctypes.CDLL) -> None:
         "gafime_allpairs_scores_noalloc": ([_vp, _i64, _vp, _i, _i, _i, _f, _vp, _vp], _i),
         "gafime_unary_scores": ([_vp, _i, _i, _vp], _i),
         "gafime_allpairs_rescored": ([_vp, ctypes.POINTER(_i64)], _i),
+        "gafime_allpairs_topk_device": ([_vp, _vp, _i, _i, _i, _f, _i, _i, _i, _i, _vp], _i),
+        "gafime_topk_merge_device": ([_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp], _i),
         "gafime_shard_tiles": ([_i, _i, _i, _vp, _i, _ip], _i),
         "gafime_feature_interaction_cuda": ([_vp, _vp, _vp, _vp, _vp, ctypes.c_int32, ctypes.c_int32,
                                              ctypes.c_int32], _i),
@@ -165,6 +168,14 @@ def device_info(device_id: int = 0) -> Dict[str, object]:
         device_id, name, ctypes.byref(mem), ctypes.byref(major), ctypes.byref(minor)))
     return {"name": name.value.decode(), "memory_mb": mem.value,
             "compute_capability": (major.value, minor.value)}
+
+
+def list_len(k: int) -> int:
+    """Candidate records per operator of a topk_device list: the power of two >= k."""
+    p = 1
+    while p < k:
+        p <<= 1
+    return p
 
 
 def pack_columns(X: np.ndarray, y: np.ndarray, out: Optional[np.ndarray] = None) -> np.ndarray:
@@ -270,6 +281,35 @@ class Bucket:
             self.handle, _ptr(ids), n_ops, METRIC[metric], int(bool(center)), float(div_eps),
             int(mi_bins), int(k), int(shard_id), int(n_shards), _ptr(oi), _ptr(oj), _ptr(os_),
             _ptr(cnt)))
+        out = {}
+        for o, name in enumerate(ops):
+            c = int(cnt[o])
+            sl = slice(o * k, o * k + c)
+            out[name] = (oi[sl].copy(), oj[sl].copy(), os_[sl].copy())
+        return out
+
+    def topk_device(self, ops: Sequence[str], k: int, d_cands: int, metric: str = "pearson",
+                    center: bool = False, div_eps: float = 1e-8, mi_bins: int = 16, shard_id: int = 0,
+                    n_shards: int = 1) -> None:
+        """Queue this shard's top-k on the bucket's stream; d_cands (a device address) receives
+        len(ops) * list_len(k) 16-byte candidate records.  Finish with merge_device."""
+        ids = np.array([INTERACT[o] for o in ops], dtype=np.int32)
+        check("gafime_allpairs_topk_device", self.lib.gafime_allpairs_topk_device(
+            self.handle, _ptr(ids), len(ids), METRIC[metric], int(bool(center)), float(div_eps), int(mi_bins),
+            int(k), int(shard_id), int(n_shards), ctypes.c_void_p(int(d_cands))))
+
+    def merge_device(self, d_gathered: int, n_shards: int, ops: Sequence[str],
+                     k: int) -> Dict[str, Tuple[np.ndarray, np.ndarray, np.ndarray]]:
+        """Merge n_shards gathered topk_device blocks (device address) on the bucket's stream
+        and return the k best per operator, as topk does."""
+        n_ops = len(ops)
+        oi = np.empty(n_ops * k, dtype=np.int32)
+        oj = np.empty(n_ops * k, dtype=np.int32)
+        os_ = np.empty(n_ops * k, dtype=np.float64)
+        cnt = np.zeros(n_ops, dtype=np.int32)
+        check("gafime_topk_merge_device", self.lib.gafime_topk_merge_device(
+            self.handle, ctypes.c_void_p(int(d_gathered)), int(n_shards), n_ops, int(k), _ptr(oi), _ptr(oj),
+            _ptr(os_), _ptr(cnt)))
         out = {}
         for o, name in enumerate(ops):
             c = int(cnt[o])

@@ -370,40 +370,126 @@ int upload_tiles(Bucket& b, const Plan& plan, TileCoord** d_tiles) {
 
 using namespace gafime;
 
-extern "C" int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact_types, int n_ops,
-                                    int metric, int center, float div_eps, int mi_bins, int k,
-                                    int shard_id, int n_shards, int32_t* out_i, int32_t* out_j,
-                                    double* out_score, int* out_count) {
+namespace gafime {
+namespace {
+
+int check_topk_args(ContiguousBucket bucket, const int* interact_types, int n_ops, int metric, float div_eps,
+                    int mi_bins, int k, int shard_id, int n_shards) {
     if (!bucket || !interact_types || n_ops < 1 || n_ops > 4 || k < 1 || k > GAFIME_ALLPAIRS_MAX_K ||
-        n_shards < 1 || shard_id < 0 || shard_id >= n_shards || !out_i || !out_j || !out_score ||
-        !out_count)
+        n_shards < 1 || shard_id < 0 || shard_id >= n_shards)
         return GAFIME_ERROR_INVALID_ARGS;
     if (metric != GAFIME_METRIC_PEARSON && metric != GAFIME_METRIC_MUTUAL_INFO) return GAFIME_ERROR_INVALID_ARGS;
     if (metric == GAFIME_METRIC_MUTUAL_INFO && (mi_bins < 2 || mi_bins > 255)) return GAFIME_ERROR_INVALID_ARGS;
     if (!(div_eps > 0.0f)) return GAFIME_ERROR_INVALID_ARGS;
     for (int o = 0; o < n_ops; ++o)
         if (!valid_op(interact_types[o])) return GAFIME_ERROR_INVALID_ARGS;
-    Bucket& b = *(Bucket*)bucket;
-    if (b.f >= 65536) return GAFIME_ERROR_INVALID_ARGS;  // pair id i*F + j must fit 32 bits
-    cudaSetDevice(b.device);
-    for (int o = 0; o < n_ops; ++o) out_count[o] = 0;
+    if (((Bucket*)bucket)->f >= 65536) return GAFIME_ERROR_INVALID_ARGS;  // pair id i*F + j must fit 32 bits
+    return GAFIME_SUCCESS;
+}
 
+// The scoring of one top-k call, queued on the bucket's stream without a host sync: the
+// per-list candidates of every operator land in cands[o] (n_lists lists of k_pad entries;
+// tmp[o] is the merge's second buffer).  nt == 0 (no tile in this shard) queues nothing.
+struct TopkQueued {
+    Cand* cands[4];
+    Cand* tmp[4];
+    int n_lists = 0, k_pad = 1, nt = 0, gram_used = 0;
+    size_t per_op = 0;
+};
+
+int queue_topk(Bucket& b, const int* ops, int n_ops, int metric, int center, float div_eps, int mi_bins, int k,
+               int shard_id, int n_shards, TopkQueued& q) {
     b.last_rescored = 0;
     b.guard_ran = false;
     Plan plan = make_plan(b, shard_id, n_shards);
-    const int nt = (int)plan.tiles.size();
-    if (nt == 0) return GAFIME_SUCCESS;
+    q.nt = (int)plan.tiles.size();
+    q.k_pad = next_pow2(k);
+    if (q.nt == 0) return GAFIME_SUCCESS;
     ColumnStats cs;
     int st = prepare(b, center, metric, cs, true);
     if (st != GAFIME_SUCCESS) return st;
     TileCoord* d_tiles = nullptr;
     st = upload_tiles(b, plan, &d_tiles);
     if (st != GAFIME_SUCCESS) return st;
+    const int sub_lists = metric == GAFIME_METRIC_PEARSON ? epilogue_sub_lists(q.nt, q.k_pad, b.sm_count) : 1;
+    q.n_lists = q.nt * sub_lists;
+    q.per_op = (size_t)q.n_lists * q.k_pad;
+    cudaError_t e = ensure(b.cands, q.per_op * n_ops * sizeof(Cand));
+    if (e == cudaSuccess) e = ensure(b.cands2, q.per_op * n_ops * sizeof(Cand));
+    if (e != cudaSuccess) return status_from(e);
+    for (int o = 0; o < n_ops; ++o) {
+        q.cands[o] = (Cand*)b.cands.ptr + q.per_op * o;
+        q.tmp[o] = (Cand*)b.cands2.ptr + q.per_op * o;
+    }
+    return score_ops(b, cs, plan, d_tiles, ops, n_ops, metric, center, div_eps, mi_bins, q.k_pad, sub_lists,
+                     q.cands, nullptr, &q.gram_used);
+}
 
+}  // namespace
+}  // namespace gafime
+
+extern "C" int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact_types, int n_ops,
+                                    int metric, int center, float div_eps, int mi_bins, int k,
+                                    int shard_id, int n_shards, int32_t* out_i, int32_t* out_j,
+                                    double* out_score, int* out_count) {
+    int st = check_topk_args(bucket, interact_types, n_ops, metric, div_eps, mi_bins, k, shard_id, n_shards);
+    if (st != GAFIME_SUCCESS) return st;
+    if (!out_i || !out_j || !out_score || !out_count) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket& b = *(Bucket*)bucket;
+    cudaSetDevice(b.device);
+    for (int o = 0; o < n_ops; ++o) out_count[o] = 0;
+    TopkQueued q;
+    st = queue_topk(b, interact_types, n_ops, metric, center, div_eps, mi_bins, k, shard_id, n_shards, q);
+    if (st != GAFIME_SUCCESS || q.nt == 0) return st;
+    st = merge_and_copy(b, q.cands, q.tmp, q.n_lists, k, q.k_pad, n_ops, q.per_op, out_i, out_j, out_score,
+                        out_count);
+    if (st == GAFIME_SUCCESS) st = gram_status(b, q.gram_used);
+    if (st != GAFIME_SUCCESS)
+        for (int o = 0; o < n_ops; ++o) out_count[o] = 0;
+    return st;
+}
+
+extern "C" int gafime_allpairs_topk_device(ContiguousBucket bucket, const int* interact_types, int n_ops,
+                                           int metric, int center, float div_eps, int mi_bins, int k,
+                                           int shard_id, int n_shards, void* d_cands) {
+    int st = check_topk_args(bucket, interact_types, n_ops, metric, div_eps, mi_bins, k, shard_id, n_shards);
+    if (st != GAFIME_SUCCESS) return st;
+    if (!d_cands || ((uintptr_t)d_cands & 15) != 0) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket& b = *(Bucket*)bucket;
+    cudaSetDevice(b.device);
+    TopkQueued q;
+    st = queue_topk(b, interact_types, n_ops, metric, center, div_eps, mi_bins, k, shard_id, n_shards, q);
+    if (st != GAFIME_SUCCESS) return st;
+    b.pending_gram = q.gram_used;
+    Cand* out = static_cast<Cand*>(d_cands);
+    cudaError_t e;
+    if (q.nt == 0) {
+        // no tile on this shard: empty lists (score 0, no pair) for the exchange
+        e = fill_empty_lists(out, (size_t)n_ops * q.k_pad, b.stream);
+    } else {
+        Cand* fin = nullptr;
+        {
+            KernelTimer timer(b.stream, GAFIME_KERNEL_MERGE);
+            e = merge_candidates(q.cands[0], q.tmp[0], q.n_lists, q.k_pad, n_ops, q.per_op, &fin, b.stream);
+        }
+        for (int o = 0; o < n_ops && e == cudaSuccess; ++o)
+            e = cudaMemcpyAsync(out + (size_t)o * q.k_pad, fin + q.per_op * o, sizeof(Cand) * q.k_pad,
+                                cudaMemcpyDeviceToDevice, b.stream);
+    }
+    return status_from(e);
+}
+
+extern "C" int gafime_topk_merge_device(ContiguousBucket bucket, const void* d_gathered, int n_shards, int n_ops,
+                                        int k, int32_t* out_i, int32_t* out_j, double* out_score,
+                                        int* out_count) {
+    if (!bucket || !d_gathered || ((uintptr_t)d_gathered & 15) != 0 || n_shards < 1 || n_ops < 1 || n_ops > 4 ||
+        k < 1 || k > GAFIME_ALLPAIRS_MAX_K || !out_i || !out_j || !out_score || !out_count)
+        return GAFIME_ERROR_INVALID_ARGS;
+    Bucket& b = *(Bucket*)bucket;
+    cudaSetDevice(b.device);
+    for (int o = 0; o < n_ops; ++o) out_count[o] = 0;
     const int k_pad = next_pow2(k);
-    const int sub_lists = metric == GAFIME_METRIC_PEARSON ? epilogue_sub_lists(nt, k_pad, b.sm_count) : 1;
-    const int n_lists = nt * sub_lists;
-    size_t per_op = (size_t)n_lists * k_pad;
+    const size_t per_op = (size_t)n_shards * k_pad;
     cudaError_t e = ensure(b.cands, per_op * n_ops * sizeof(Cand));
     if (e == cudaSuccess) e = ensure(b.cands2, per_op * n_ops * sizeof(Cand));
     if (e != cudaSuccess) return status_from(e);
@@ -413,12 +499,12 @@ extern "C" int gafime_allpairs_topk(ContiguousBucket bucket, const int* interact
         cands[o] = (Cand*)b.cands.ptr + per_op * o;
         tmp[o] = (Cand*)b.cands2.ptr + per_op * o;
     }
-    int gram_used = 0;
-    st = score_ops(b, cs, plan, d_tiles, interact_types, n_ops, metric, center, div_eps, mi_bins,
-                   k_pad, sub_lists, cands, nullptr, &gram_used);
-    if (st != GAFIME_SUCCESS) return st;
-    st = merge_and_copy(b, cands, tmp, n_lists, k, k_pad, n_ops, per_op, out_i, out_j, out_score, out_count);
-    if (st == GAFIME_SUCCESS) st = gram_status(b, gram_used);
+    // [shard][op][k_pad] (the all-gather's order) -> [op][shard][k_pad] (the merge's)
+    e = reorder_shard_lists(static_cast<const Cand*>(d_gathered), cands[0], n_shards, n_ops, k_pad, b.stream);
+    if (e != cudaSuccess) return status_from(e);
+    int st = merge_and_copy(b, cands, tmp, n_shards, k, k_pad, n_ops, per_op, out_i, out_j, out_score, out_count);
+    if (st == GAFIME_SUCCESS) st = gram_status(b, b.pending_gram);
+    b.pending_gram = 0;
     if (st != GAFIME_SUCCESS)
         for (int o = 0; o < n_ops; ++o) out_count[o] = 0;
     return st;
@@ -635,8 +721,10 @@ int streamed_topk_body(Bucket& b, const float* h_data, const uint8_t* h_mask, co
         bool finite = true;
         return check_finite(b, &finite);
     }
-    // the row chunks the whole tile set would get (same partial sums as an unstreamed call)
+    // the row chunks and the Gram kernel the whole tile set would get (same partial sums as an
+    // unstreamed call)
     const int64_t chunk = gram_chunk_rows(b, gram_tiles128(plan.tiles));
+    const int planes = gram_use_planes(b, plan.tiles) ? 1 : 0;
     TileCoord* d_tiles = nullptr;
     int st = upload_tiles(b, plan, &d_tiles);
     if (st != GAFIME_SUCCESS) return st;
@@ -679,7 +767,7 @@ int streamed_topk_body(Bucket& b, const float* h_data, const uint8_t* h_mask, co
         for (int g2 = 0; g2 < 2; ++g2) {
             if (!need[g2]) continue;
             e = launch_gram_moments(b, cs, d_tiles + t0, sub, g2 == 1, div_eps, mom[g2] + (size_t)t0 * per_tile,
-                                    b.stream, nullptr, GRAM_PREP_DONE, chunk);
+                                    b.stream, nullptr, GRAM_PREP_DONE, chunk, planes);
             if (e != cudaSuccess) return status_from(e);
         }
         t0 = t1;

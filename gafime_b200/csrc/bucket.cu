@@ -709,7 +709,7 @@ int gafime_contiguous_bucket_free(ContiguousBucket bucket) {
     if (b->stream) cudaStreamSynchronize(b->stream);
     DeviceBuf* bufs[] = {&b->stats_part, &b->stats, &b->ycen, &b->xcen, &b->moments, &b->cands,
                          &b->cands2, &b->scores, &b->flags, &b->tiles, &b->mi, &b->mi_hist, &b->mi_mm, &b->mi_xs, &b->mi_split, &b->gather, &b->rank, &b->gram_cols,
-                         &b->gram};
+                         &b->gram, &b->gram_planes, &b->guard};
     for (DeviceBuf* d : bufs) release(*d);
     if (b->d_data) cudaFree(b->d_data);
     if (b->d_mask) cudaFree(b->d_mask);

@@ -54,10 +54,11 @@ struct Bucket {
     int sm_count = 148;
     // scratch
     DeviceBuf stats_part, stats, ycen, xcen, moments, cands, cands2, scores, flags, tiles, mi,
-        mi_hist, mi_mm, mi_xs, mi_split, gather, rank, gram, gram_cols, guard;
+        mi_hist, mi_mm, mi_xs, mi_split, gather, rank, gram, gram_cols, gram_planes, guard;
     // (pair, operator) scores the accuracy guard re-scored exactly in the last all-pairs call
     int64_t last_rescored = 0;
     bool guard_ran = false;      // the guard's counter (start of `guard`) belongs to this call
+    int pending_gram = 0;        // a device top-k ran Gram kernels whose error flag is still unread
 };
 
 // Grow a scratch buffer to at least `bytes`; returns cudaSuccess or an error.
@@ -120,10 +121,15 @@ cudaError_t gram_prep_columns(Bucket& b, const ColumnStats& cs, bool recip, floa
 // chunk_rows > 0 fixes the row chunk of the tiles (a streamed call launches its tiles in
 // several sets and keeps the chunking the whole set would get: gram_chunk_rows of the
 // whole set's 128-tile count, gram_tiles128).
+// use_planes: 1 the B-planes kernel, 0 the fused kernel, -1 chosen from this tile set
+// (gram_use_planes); a streamed call decides once for its whole tile set.
 cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoord* d_tiles64,
                                 const std::vector<TileCoord>& tiles64, bool recip, float eps,
                                 double* d_moments, cudaStream_t stream, int* host_err, int prep_mode,
-                                int64_t chunk_rows = 0);
+                                int64_t chunk_rows = 0, int use_planes = -1);
+// True when a tile set reuses its B blocks enough for the B-planes kernel (or when
+// GAFIME_GRAM_KERNEL forces it).
+bool gram_use_planes(const Bucket& b, const std::vector<TileCoord>& tiles64);
 int64_t gram_chunk_rows(const Bucket& b, int ctas_per_chunk);
 // host_err null: launch_gram_moments neither clears nor reads the Gram kernels' error flag
 // (no host sync); the caller clears it before its launches and reads it once at the end.
@@ -199,6 +205,10 @@ int epilogue_sub_lists(int n_tiles, int k_pad, int sm_count);
 // op_stride entries further.
 cudaError_t merge_candidates(Cand* buf, Cand* tmp, int n_lists, int k_pad, int n_ops, size_t op_stride,
                              Cand** final_list, cudaStream_t stream);
+// n entries of "no pair" (the empty list a shard without tiles contributes)
+cudaError_t fill_empty_lists(Cand* out, size_t n, cudaStream_t stream);
+// Gathered shard lists [shard][op][k_pad] -> [op][shard][k_pad]
+cudaError_t reorder_shard_lists(const Cand* in, Cand* out, int n_shards, int n_ops, int k_pad, cudaStream_t stream);
 
 // Mutual-information scoring (mi.cu): centred product, equal-width bins.
 // cs must hold raw-column statistics (means of the uncentred columns).

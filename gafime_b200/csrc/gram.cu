@@ -36,6 +36,8 @@
 // bandwidth, not the tensor pipe, bounds a 128 x 128 tile with both operands there).  The
 // raw fp32 matrix is read once per tile and chunk (concurrent tiles of one chunk share it
 // through L2); no operand planes exist in HBM.
+// Wide tables take gram_planes_kernel instead (below): the B operands are converted once per
+// call into fp16 planes in HBM and TMA-loaded, and only the A block is converted in-kernel.
 // gram_reduce_kernel then adds the chunk partials in fp64 in a fixed order, undoes the scales
 // and the centring, and writes the raw moments S1 = sum a g(b), S2 = Q, S3 = sum a g(b) ycen
 // that select.cu's epilogue scores.
@@ -133,6 +135,20 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking test: the single producer and MMA threads poll, so they go on as soon as the
+// phase completes (a thread suspended in try_wait may be woken later than that)
+__device__ __forceinline__ bool mbar_try_spin(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -146,6 +162,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
     const uint64_t t0 = global_ns();
     for (long long i = 1; i < kSpinLimit; ++i) {
         if (mbar_try(bar, parity)) return true;
+        if ((i & 15) == 0 && global_ns() - t0 > kWaitLimitNs) break;
+    }
+    atomicCAS(err, 0, code);
+    return false;
+}
+
+// Bounded wait of the single producer / MMA threads: polls without suspending
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, int* err, int code) {
+    if (mbar_try_spin(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (long long i = 1; i < kSpinLimit; ++i) {
+        if (mbar_try_spin(bar, parity)) return true;
         if ((i & 15) == 0 && global_ns() - t0 > kWaitLimitNs) break;
     }
     atomicCAS(err, 0, code);
@@ -516,7 +544,7 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
             bool ok = true;
             for (int k = 0; k < nk; ++k) {
                 const int s = k % kRawStages;
-                if (k >= kRawStages && !(ok = mbar_wait(rempty0 + 8 * s, ((k / kRawStages) - 1) & 1, a.err, 1)))
+                if (k >= kRawStages && !(ok = mbar_wait_spin(rempty0 + 8 * s, ((k / kRawStages) - 1) & 1, a.err, 1)))
                     break;
                 const uint32_t full = rfull0 + 8 * s;
                 mbar_expect_tx(full, bytes);
@@ -536,7 +564,7 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
             // MMA issuer: A operands from tensor memory, B operands from shared memory
             for (int k = 0; k < nk; ++k) {
                 const int s = k % kOpStages;
-                if (!mbar_wait(ofull0 + 8 * s, (k / kOpStages) & 1, a.err, 2)) break;
+                if (!mbar_wait_spin(ofull0 + 8 * s, (k / kOpStages) & 1, a.err, 2)) break;
                 tc_fence_after();
                 const uint32_t ta = tmem + kTmemA + (uint32_t)(s * kTmemAStride);
                 const uint32_t bst = smem_u32(bop0 + s * kBStageBytes);
@@ -639,254 +667,117 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
     }
 }
 
-// ---- the CTA-pair Gram kernel (cta_group::2) ----------------------------------------
+// ---- the wide-table Gram kernel: B operands from per-call planes --------------------------
 //
-// A cluster of two CTAs computes a 256 x 128 block of pairs: CTA r holds the A operands of
-// its own 128-column block I_r in its tensor memory (rows r*128 .. r*128+127 of the
-// M = 256 MMA), and half of every B operand in its shared memory (the MMA reads the two
-// halves from the two CTAs):
-//   N = 256 [C | W] operand: CTA 0 holds s b' (the C half), CTA 1 holds s b' * s_y ycen
-//   N = 128 Q operand:       CTA r holds s_q g(b)^2 of B columns r*64 .. r*64+63
-// so each SM converts half of the B work of the single-CTA kernel and its tensor cores
-// read half the B bytes from shared memory.  CTA 0's MMA thread issues the cta_group::2
-// MMAs for the pair; both CTAs' converters arrive on CTA 0's "operand full" barrier (CTA 1
-// remotely), and tcgen05.commit multicasts "operand free" and "accumulators done" to both.
+// In a wide table every 128-column block is the B block of many tiles (16 at 2048
+// columns), and converting it inside each of them is what binds gram_fused_kernel (the
+// converter warps' issue and shared-memory traffic).  Here the B side is converted once per
+// call by gram_bplanes_kernel into six fp16 planes in HBM,
+//     BH/BL = split(s b'),  WBH/WBL = split((s b') (s_y ycen)),  BQH/BQL = split(s_q g(b)^2)
+// (exactly the fused kernel's B-side arithmetic), laid out step-major -- plane, 16-row step,
+// column, 16 rows -- with the 32-byte swizzle already applied, so the 128 x 16 operand tile of
+// a block and step is one contiguous 4 KB run that a plain bulk copy moves into the K-major
+// layout the MMAs read (column-major planes made every tile 128 separate 32-byte pieces 4 MB
+// apart, and those loads bound the kernel).  BH and WBH land side by side, so [C | W] is one
+// N = 256 MMA as in the fused kernel: three N = 256 and three N = 128 MMAs per 16-row step,
+// the same accumulators (TMEM columns 0-127 C, 128-255 W, 256-383 Q) and the same chunk
+// partials, reduced by gram_reduce_kernel.  The converters handle the A block only and write
+// four A operands (XH/XL = split(s_x a'), QH/QL = split(s_q a^2)) to tensor memory, which
+// leaves room for four A stages (the whole of tensor memory): four converter groups work on
+// four steps at once.  Two groups of eight warps, each converting every other step, kept the
+// tensor pipe ~55 % busy: a group's conversion latency, not bandwidth, paced the steps.
+//
+// One CTA = one tile x one chunk of <= 8192 rows, 18 warps:
+//   warp 0      TMA: raw fp32 A tiles (64-byte swizzle) -> 8-stage ring read by the converters;
+//               six fp16 B plane tiles (bulk copies of swizzled 4 KB runs) -> 5-stage ring read
+//               by the MMAs
+//   warp 1      TMEM allocation; one thread issues the six MMAs of a step, then commits the
+//               ring stage (B planes read) and the A stage (TMEM operands read)
+//   warps 2-17  four converter groups of 4 warps (one per TMEM lane quarter; a thread
+//               converts one A column over the step's 16 rows), group g taking the steps
+//               k = g mod 4 into A stage k % 4, so four steps convert at once; groups 0 and
+//               1 drain the accumulators at the end
+// Every wait is bounded as in gram_fused_kernel.
 
-struct PairCoord {
-    int i0, i1, j;   // A blocks of CTA 0 and CTA 1, B block
-    int t0, t1;      // partial slots of tiles (i0, j), (i1, j); -1: not needed
-};
+constexpr int kBPlanes = 6;                                       // BH WBH BL WBL BQH BQL
+constexpr int kPRawStages = 8;                                    // raw A tiles (read by the converters)
+constexpr int kPBStages = 5;                                      // B plane tiles (read by the MMAs)
+constexpr int kPBStageBytes = kBPlanes * kOpBytes;                // 24 KB
+constexpr uint32_t kPTmemA = 384;                                 // after C | W | Q
+constexpr uint32_t kPTmemAStride = 32;                            // XH XL QH QL: 8 columns each
+constexpr int kPAStages = 4;
+constexpr int kPGroups = 4;                                       // converter groups (one step each in flight)
+constexpr int kPConvWarps = 4;                                    // warps per group: one per TMEM lane quarter
+static_assert(2 + kPGroups * kPConvWarps == kGramThreads / 32, "warp roles");
+static_assert(kPGroups <= kPAStages, "every group in flight has its own A stage");
+// A parity wait is only sound when its barrier's previous phase has completed.  A group's wait
+// on raw stage k % kPRawStages follows its own wait on the same stage's previous phase (step
+// k - kPRawStages) only when that step was the same group's: the ring depth must be a multiple
+// of the number of groups.  (The B ring has one waiter, the MMA thread, in step order.)
+static_assert(kPRawStages % kPGroups == 0, "raw ring phases stay with one converter group");
+// + up to 1023 bytes to align the base to 1024, + the barriers and the TMEM address slot
+constexpr size_t kPBarBytes = (size_t)(2 * kPRawStages + 2 * kPBStages + 2 * kPAStages + 1) * 8 + 8;
+constexpr size_t kPlanesSmem = (size_t)kPRawStages * kRawBox + (size_t)kPBStages * kPBStageBytes + 1024 + kPBarBytes;
+static_assert(kPlanesSmem <= 232448, "shared memory per CTA");
+static_assert(kPTmemA + kPAStages * kPTmemAStride <= kTmemCols, "tensor memory columns");
+static_assert(kRawBox % 1024 == 0 && kPBStageBytes % 1024 == 0, "ring stages keep the swizzle alignment");
 
-struct PairArgs {
-    const PairCoord* pairs;
-    int n_slots;              // partial slots per chunk
-    int64_t chunk_rows, rows, n, f;
-    const float* ys;
-    const double* cs;
-    int recip;
-    float eps;
-    float* partial;           // [chunk][slot][3][128 n][128 m]
+struct PlanesArgs {
+    const TileCoord* tiles;   // 128-blocks (bi, bj), bi <= bj
+    int n_tiles;
+    int64_t chunk_rows;       // multiple of kGK
+    int64_t rows;             // padded rows (ld)
+    int64_t n, f;
+    int64_t f_pad;            // columns per plane (a multiple of 128)
+    int64_t steps;            // 16-row steps per plane (ld / 16)
+    const __half* planes;     // [plane][step][f_pad][16] fp16, 32-byte swizzled (gram_bplanes_kernel)
+    const double* cs;         // per-column scales and means (12 doubles per column)
+    float* partial;           // [chunk][tile][3][128 n][128 m]
     int* err;
 };
 
-constexpr int kPBStageBytes = 2 * kOpBytes + kOpBytes;   // N256 half hi+lo (4 KB each), Q half hi+lo (2 KB each)
-constexpr int kPB_H = 0, kPB_L = kOpBytes, kPB_QH = 2 * kOpBytes, kPB_QL = 2 * kOpBytes + kOpBytes / 2;
-constexpr int kPRawStages = 8;
-constexpr size_t kPairSmem = (size_t)kPRawStages * (kRawStageBytes + kYsBytes) + (size_t)kOpStages * kPBStageBytes +
-                             1024 + 256;
-static_assert(kPairSmem <= 232448, "shared memory per CTA");
-// kind::f16 instruction descriptors with M = 256 (cta_group::2)
-constexpr uint32_t kIdescP256 = (1u << 4) | ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
-constexpr uint32_t kIdescP128 = (1u << 4) | ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
-
-__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
-                                          uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
-        ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-// arrive on both CTAs' copy of a barrier once every tcgen05 op issued so far has completed
-__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
-    asm volatile(
-        "{\n\t.reg .b16 m;\n\t"
-        "mov.b16 m, 3;\n\t"
-        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}"
-        ::"r"(bar)
-        : "memory");
-}
-
-// arrive on the barrier at the same shared-memory offset in CTA `rank` of the cluster
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar, uint32_t rank) {
-    asm volatile(
-        "{\n\t.reg .b32 ra;\n\t"
-        "mapa.shared::cluster.u32 ra, %0, %1;\n\t"
-        "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n\t}"
-        ::"r"(bar), "r"(rank)
-        : "memory");
-}
-
-// Bounded wait with cluster-scope acquire (arrivals come from both CTAs of the pair)
-__device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(kSuspendNs)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int* err, int code) {
-    if (mbar_try_cluster(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
-    for (long long i = 1; i < kSpinLimit; ++i) {
-        if (mbar_try_cluster(bar, parity)) return true;
-        if ((i & 15) == 0 && global_ns() - t0 > kWaitLimitNs) break;
-    }
-    atomicCAS(err, 0, code);
-    return false;
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-struct PairOps {
-    Split8 x, q;    // A: s_x a', s_q a^2
-    Split8 bn;      // B, N = 256 half: s b' (CTA 0) or s b' * s_y ycen (CTA 1)
-    Split8 bq;      // B, Q half: s_q g(b)^2 (threads of the CTA's 64 columns)
-};
-
-// One step of one converter thread of a CTA pair: column m, K half h.  kSame: the B block
-// is the A block (multiply group, I_r == J); kRecip: B operand 1/safe(b); kQ: this thread's
-// column is in the CTA's Q half.
-template <bool kMask, bool kSame, bool kRecip>
-__device__ __forceinline__ void convert_pair_step(const unsigned char* raw, const unsigned char* ysm, int m, int h,
-                                                  int valid, int rank, bool q_half, const ConvCols& k, float eps,
-                                                  PairOps& o) {
+// A operands of one column and K half for one step (rows at or beyond `valid` zeroed).
+template <bool kMask>
+__device__ __forceinline__ void convert_a(const unsigned char* raw, int m, int h, int valid, float sxa, float nmua,
+                                          float sqa, Split8& xo, Split8& qo) {
     float x[8];
     uint64_t x2[4], v2[4], t2[4];
     load_raw8(raw, m, h, x);
     #pragma unroll
     for (int p = 0; p < 4; ++p) x2[p] = pk(x[2 * p], x[2 * p + 1]);
-    {
-        const uint64_t sx = pk(k.sx_a, k.sx_a), nmu = pk(-k.mus_a, -k.mus_a), sq = pk(k.sq_a, k.sq_a);
-        #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-            v2[p] = fma2(x2[p], sx, nmu);
-            t2[p] = mul2(mul2(x2[p], x2[p]), sq);
-            if (kMask) {
-                const bool v0 = 8 * h + 2 * p < valid, v1 = 8 * h + 2 * p + 1 < valid;
-                const float2 c = upk(v2[p]), q = upk(t2[p]);
-                v2[p] = pk(v0 ? c.x : 0.f, v1 ? c.y : 0.f);
-                t2[p] = pk(v0 ? q.x : 0.f, v1 ? q.y : 0.f);
-            }
-        }
-        split8(v2, o.x);
-        split8(t2, o.q);
-    }
-    if (!kSame) {
-        load_raw8(raw + kRawBox, m, h, x);
-        if (kRecip) {
-            #pragma unroll
-            for (int r = 0; r < 8; ++r) x[r] = safe_recip(x[r], eps);
-        }
-        #pragma unroll
-        for (int p = 0; p < 4; ++p) x2[p] = pk(x[2 * p], x[2 * p + 1]);
-        const uint64_t sxb = pk(k.sx_b, k.sx_b), nmub = pk(-k.mus_b, -k.mus_b), sqb = pk(k.sq_b, k.sq_b);
-        #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-            v2[p] = fma2(x2[p], sxb, nmub);
-            t2[p] = mul2(mul2(x2[p], x2[p]), sqb);
-            if (kMask) {
-                const bool v0 = 8 * h + 2 * p < valid, v1 = 8 * h + 2 * p + 1 < valid;
-                const float2 c = upk(v2[p]), q = upk(t2[p]);
-                v2[p] = pk(v0 ? c.x : 0.f, v1 ? c.y : 0.f);
-                t2[p] = pk(v0 ? q.x : 0.f, v1 ? q.y : 0.f);
-            }
-        }
-        if (q_half) split8(t2, o.bq);
-    } else if (q_half) {
-        o.bq = o.q;
-    }
-    if (rank == 1) {
-        const float4 y0 = *reinterpret_cast<const float4*>(ysm + 32 * h);
-        const float4 y1 = *reinterpret_cast<const float4*>(ysm + 32 * h + 16);
-        v2[0] = mul2(v2[0], pk(y0.x, y0.y));
-        v2[1] = mul2(v2[1], pk(y0.z, y0.w));
-        v2[2] = mul2(v2[2], pk(y1.x, y1.y));
-        v2[3] = mul2(v2[3], pk(y1.z, y1.w));
-        split8(v2, o.bn);
-    } else if (!kSame) {
-        split8(v2, o.bn);
-    } else {
-        o.bn = o.x;
-    }
-}
-
-struct PairCtx {
-    const unsigned char* raw0;
-    const unsigned char* ys0;
-    unsigned char* bop0;
-    uint32_t rfull0, rempty0, ofull0, oempty0;
-    uint32_t tmem_a;   // tmem + lane quarter + kTmemA + 4h
-    int m, h, lane, rank;
-    bool q_half;
-    int nk, n_full;
-    int64_t rows_left;
-    float eps;
-    int* err;
-};
-
-template <bool kSame, bool kRecip>
-__device__ __forceinline__ void pair_conv_loop(const PairCtx& c, const ConvCols& kc, int grp) {
-    for (int k = grp; k < c.nk; k += kGroups) {
-        const int rs = k % kPRawStages, os = k % kOpStages;
-        if (!warp_wait(c.rfull0 + 8 * rs, (k / kPRawStages) & 1, c.err, 5, c.lane)) return;
-        const unsigned char* raw = c.raw0 + rs * kRawStageBytes;
-        const unsigned char* ysm = c.ys0 + rs * kYsBytes;
-        PairOps o;
-        if (k < c.n_full) {
-            convert_pair_step<false, kSame, kRecip>(raw, ysm, c.m, c.h, kGK, c.rank, c.q_half, kc, c.eps, o);
-        } else {
-            const int64_t left = c.rows_left - (int64_t)k * kGK;
-            const int valid = left <= 0 ? 0 : (int)left;
-            convert_pair_step<true, kSame, kRecip>(raw, ysm, c.m, c.h, valid, c.rank, c.q_half, kc, c.eps, o);
-        }
-        // this CTA's operand stage is free once the pair's MMAs of step k - kOpStages completed
-        if (k >= kOpStages && !warp_wait(c.oempty0 + 8 * os, ((k / kOpStages) - 1) & 1, c.err, 6, c.lane)) return;
-        tc_fence_after();
-        const uint32_t ta = c.tmem_a + (uint32_t)(os * kTmemAStride);
-        tmem_st4(ta + 0 * 8, o.x.hi);
-        tmem_st4(ta + 1 * 8, o.x.lo);
-        tmem_st4(ta + 2 * 8, o.q.hi);
-        tmem_st4(ta + 3 * 8, o.q.lo);
-        unsigned char* sb = c.bop0 + os * kPBStageBytes;
-        store_half(sb + kPB_H, c.m, c.h, o.bn.hi);
-        store_half(sb + kPB_L, c.m, c.h, o.bn.lo);
-        if (c.q_half) {
-            const int mq = c.m - 64 * c.rank;   // row of the CTA's 64-row Q half
-            store_half(sb + kPB_QH, mq, c.h, o.bq.hi);
-            store_half(sb + kPB_QL, mq, c.h, o.bq.lo);
-        }
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-        fence_async_smem();
-        tc_fence_before();
-        __syncwarp();
-        if (c.lane == 0) {
-            // CTA 0's barrier counts both CTAs' converter warps
-            if (c.rank == 0) mbar_arrive(c.ofull0 + 8 * os);
-            else mbar_arrive_cluster(c.ofull0 + 8 * os, 0);
-            // the raw stage is released after the stores that consume it
-            mbar_arrive(c.rempty0 + 8 * rs);
+    const uint64_t sx = pk(sxa, sxa), nmu = pk(nmua, nmua), sq = pk(sqa, sqa);
+    #pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        v2[p] = fma2(x2[p], sx, nmu);              // s_x (a - mean)
+        t2[p] = mul2(mul2(x2[p], x2[p]), sq);      // s_q a^2
+        if (kMask) {
+            const bool v0 = 8 * h + 2 * p < valid, v1 = 8 * h + 2 * p + 1 < valid;
+            const float2 c = upk(v2[p]), q = upk(t2[p]);
+            v2[p] = pk(v0 ? c.x : 0.f, v1 ? c.y : 0.f);
+            t2[p] = pk(v0 ? q.x : 0.f, v1 ? q.y : 0.f);
         }
     }
+    split8(v2, xo);
+    split8(t2, qo);
 }
 
 __global__ void __launch_bounds__(kGramThreads, 1)
-gram_pair_kernel(const __grid_constant__ CUtensorMap xmap, const PairArgs a) {
+gram_planes_kernel(const __grid_constant__ CUtensorMap xmap, const PlanesArgs a) {
     extern __shared__ __align__(1024) unsigned char gsmem_raw[];
     unsigned char* smem = (unsigned char*)(((uintptr_t)gsmem_raw + 1023) & ~(uintptr_t)1023);
-    unsigned char* raw0 = smem;
-    unsigned char* bop0 = raw0 + kPRawStages * kRawStageBytes;
-    unsigned char* ys0 = bop0 + kOpStages * kPBStageBytes;
-    uint64_t* bars = (uint64_t*)(ys0 + kPRawStages * kYsBytes);
+    unsigned char* rawring = smem;                                // [stage][raw A tile]
+    unsigned char* bring = rawring + kPRawStages * kRawBox;       // [stage][BH WBH BL WBL BQH BQL]
+    uint64_t* bars = (uint64_t*)(bring + kPBStages * kPBStageBytes);
+    // rfull[R], rempty[R], bfull[B], bempty[B], afull[A], aempty[A], accum
     const uint32_t rfull0 = smem_u32(bars), rempty0 = smem_u32(bars + kPRawStages);
-    const uint32_t ofull0 = smem_u32(bars + 2 * kPRawStages), oempty0 = smem_u32(bars + 2 * kPRawStages + kOpStages);
-    const uint32_t accum = smem_u32(bars + 2 * kPRawStages + 2 * kOpStages);
-    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * kPRawStages + 2 * kOpStages + 1);
+    const uint32_t bfull0 = smem_u32(bars + 2 * kPRawStages), bempty0 = smem_u32(bars + 2 * kPRawStages + kPBStages);
+    const uint32_t afull0 = smem_u32(bars + 2 * kPRawStages + 2 * kPBStages);
+    const uint32_t aempty0 = afull0 + 8 * kPAStages;
+    const uint32_t accum = aempty0 + 8 * kPAStages;
+    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * kPRawStages + 2 * kPBStages + 2 * kPAStages + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int rank = (int)(blockIdx.x & 1);   // cluster dims (2, 1, 1)
-    const PairCoord pc = a.pairs[blockIdx.x >> 1];
-    const int blk_a = rank ? pc.i1 : pc.i0;
-    const int slot = rank ? pc.t1 : pc.t0;
-    const bool same = (blk_a == pc.j) && !a.recip;
+    const TileCoord tc = a.tiles[blockIdx.x];
     const int64_t r0 = (int64_t)blockIdx.y * a.chunk_rows;
     const int64_t r1 = min(r0 + a.chunk_rows, a.rows);
     const int nk = r1 > r0 ? (int)((r1 - r0) / kGK) : 0;
@@ -894,132 +785,157 @@ gram_pair_kernel(const __grid_constant__ CUtensorMap xmap, const PairArgs a) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < kPRawStages; ++s) {
             mbar_init(rfull0 + 8 * s, 1);
-            mbar_init(rempty0 + 8 * s, kConvWarps);
+            mbar_init(rempty0 + 8 * s, kPConvWarps);   // the step's converter warps
         }
-        for (int s = 0; s < kOpStages; ++s) {
-            mbar_init(ofull0 + 8 * s, 2 * kConvWarps);   // used in CTA 0: both CTAs' warps
-            mbar_init(oempty0 + 8 * s, 1);
+        for (int s = 0; s < kPBStages; ++s) {
+            mbar_init(bfull0 + 8 * s, 1);
+            mbar_init(bempty0 + 8 * s, 1);             // the step's MMA commit
+        }
+        for (int s = 0; s < kPAStages; ++s) {
+            mbar_init(afull0 + 8 * s, kPConvWarps);
+            mbar_init(aempty0 + 8 * s, 1);
         }
         mbar_init(accum, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kTmemCols)
                      : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
     __syncthreads();
-    // both CTAs' barriers are initialised before any remote arrive
-    cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
         if (lane == 0) {
-            const uint32_t bytes = (same ? (uint32_t)kRawBox : (uint32_t)kRawStageBytes) + (uint32_t)(kGK * 4);
             int issued = 0;
             bool ok = true;
             for (int k = 0; k < nk; ++k) {
-                const int s = k % kPRawStages;
-                if (k >= kPRawStages && !(ok = mbar_wait(rempty0 + 8 * s, ((k / kPRawStages) - 1) & 1, a.err, 1)))
+                const int rs = k % kPRawStages, bs = k % kPBStages;
+                if (k >= kPRawStages &&
+                    !(ok = mbar_wait_spin(rempty0 + 8 * rs, ((k / kPRawStages) - 1) & 1, a.err, 1)))
                     break;
-                const uint32_t full = rfull0 + 8 * s;
-                mbar_expect_tx(full, bytes);
-                const uint32_t st = smem_u32(raw0 + s * kRawStageBytes);
+                if (k >= kPBStages && !(ok = mbar_wait_spin(bempty0 + 8 * bs, ((k / kPBStages) - 1) & 1, a.err, 1)))
+                    break;
                 const int64_t row = r0 + (int64_t)k * kGK;
-                tma_load_2d(st, &xmap, full, (int)row, blk_a * kGT);
-                if (!same) tma_load_2d(st + kRawBox, &xmap, full, (int)row, pc.j * kGT);
-                bulk_load(smem_u32(ys0 + s * kYsBytes), a.ys + row, (uint32_t)(kGK * 4), full);
+                mbar_expect_tx(rfull0 + 8 * rs, (uint32_t)kRawBox);
+                tma_load_2d(smem_u32(rawring + rs * kRawBox), &xmap, rfull0 + 8 * rs, (int)row, tc.bi * kGT);
+                // plane tile (p, step, B block): 4 KB contiguous, already swizzled
+                const int64_t step = row / kGK;
+                const uint32_t bst = smem_u32(bring + bs * kPBStageBytes);
+                mbar_expect_tx(bfull0 + 8 * bs, (uint32_t)kPBStageBytes);
+                #pragma unroll
+                for (int p = 0; p < kBPlanes; ++p)
+                    bulk_load(bst + p * kOpBytes,
+                              a.planes + (((int64_t)p * a.steps + step) * a.f_pad + (int64_t)tc.bj * kGT) * kGK,
+                              (uint32_t)kOpBytes, bfull0 + 8 * bs);
                 ++issued;
             }
-            if (!ok)
+            if (!ok) {
+                // drain this CTA's copies still in flight before it exits
                 for (int k = max(0, issued - kPRawStages); k < issued; ++k)
                     mbar_wait(rfull0 + 8 * (k % kPRawStages), (k / kPRawStages) & 1, a.err, 4);
+                for (int k = max(0, issued - kPBStages); k < issued; ++k)
+                    mbar_wait(bfull0 + 8 * (k % kPBStages), (k / kPBStages) & 1, a.err, 4);
+            }
         }
     } else if (warp == 1) {
-        if (rank == 0 && lane == 0) {
+        if (lane == 0) {
             for (int k = 0; k < nk; ++k) {
-                const int s = k % kOpStages;
-                if (!mbar_wait_cluster(ofull0 + 8 * s, (k / kOpStages) & 1, a.err, 2)) break;
+                const int bs = k % kPBStages, as = k % kPAStages;
+                if (!mbar_wait_spin(afull0 + 8 * as, (k / kPAStages) & 1, a.err, 2)) break;
+                if (!mbar_wait_spin(bfull0 + 8 * bs, (k / kPBStages) & 1, a.err, 2)) break;
                 tc_fence_after();
-                const uint32_t ta = tmem + kTmemA + (uint32_t)(s * kTmemAStride);
-                const uint32_t bst = smem_u32(bop0 + s * kPBStageBytes);
-                const uint64_t bH = umma_desc(bst + kPB_H), bL = umma_desc(bst + kPB_L);
-                const uint64_t bQH = umma_desc(bst + kPB_QH), bQL = umma_desc(bst + kPB_QL);
+                const uint32_t ta = tmem + kPTmemA + (uint32_t)(as * kPTmemAStride);
+                const uint32_t bst = smem_u32(bring + bs * kPBStageBytes);
+                // [BH | WBH] and [BL | WBL] are 256 consecutive K-major rows: N = 256 operands
+                const uint64_t bH = umma_desc(bst), bL = umma_desc(bst + 2 * kOpBytes);
+                const uint64_t bQH = umma_desc(bst + 4 * kOpBytes), bQL = umma_desc(bst + 5 * kOpBytes);
                 const uint32_t acc = k > 0 ? 1u : 0u;
-                umma_pair(tmem + kTmemCW, ta + 0 * 8, bH, kIdescP256, acc);
-                umma_pair(tmem + kTmemCW, ta + 0 * 8, bL, kIdescP256, 1u);
-                umma_pair(tmem + kTmemCW, ta + 1 * 8, bH, kIdescP256, 1u);
-                umma_pair(tmem + kTmemQ, ta + 2 * 8, bQH, kIdescP128, acc);
-                umma_pair(tmem + kTmemQ, ta + 2 * 8, bQL, kIdescP128, 1u);
-                umma_pair(tmem + kTmemQ, ta + 3 * 8, bQH, kIdescP128, 1u);
-                umma_commit_pair(oempty0 + 8 * s);
+                umma_ta(tmem + kTmemCW, ta + 0, bH, kIdesc256, acc);   // [C|W]: XH.[BH|WBH]
+                umma_ta(tmem + kTmemCW, ta + 0, bL, kIdesc256, 1u);    //        XH.[BL|WBL]
+                umma_ta(tmem + kTmemCW, ta + 8, bH, kIdesc256, 1u);    //        XL.[BH|WBH]
+                umma_ta(tmem + kTmemQ, ta + 16, bQH, kIdesc, acc);     // Q:     QH.BQH
+                umma_ta(tmem + kTmemQ, ta + 16, bQL, kIdesc, 1u);      //        QH.BQL
+                umma_ta(tmem + kTmemQ, ta + 24, bQH, kIdesc, 1u);      //        QL.BQH
+                umma_commit(bempty0 + 8 * bs);   // the B planes of this stage have been read
+                umma_commit(aempty0 + 8 * as);   // and the A operands of this TMEM stage
             }
-            umma_commit_pair(accum);
+            umma_commit(accum);  // all issued MMAs complete (also on the error path)
         }
     } else {
-        const int cw = (warp - 2) % kConvWarps;
-        const int grp = (warp - 2) / kConvWarps;
+        // converter group grp (warps 2 + 4 grp .. 5 + 4 grp) converts the steps k = grp mod 4,
+        // into A stage k % 4; thread = column m of the A block (its TMEM lane), all 16 rows
+        const int grp = (warp - 2) / kPConvWarps;
         const int quarter = warp & 3;
-        const int h = cw >> 2;
         const int m = quarter * 32 + lane;
         const uint32_t tlane = (uint32_t)(quarter * 32) << 16;
-        const int64_t col_a = (int64_t)blk_a * kGT + m, col_b = (int64_t)pc.j * kGT + m;
-        ConvCols kc{0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const int64_t col_a = (int64_t)tc.bi * kGT + m;
+        float sxa = 0.f, sqa = 0.f, nmua = 0.f;
         if (col_a < a.f) {
             const double* c = a.cs + col_a * 12;
-            kc.sx_a = (float)c[0];
-            kc.sq_a = (float)c[1];
-            kc.mus_a = (float)c[9] * kc.sx_a;
+            sxa = (float)c[0];
+            sqa = (float)c[1];
+            nmua = -((float)c[9] * sxa);
         }
-        if (col_b < a.f) {
-            const double* c = a.cs + col_b * 12;
-            const int o = a.recip ? 3 : 0;
-            kc.sx_b = (float)c[o];
-            kc.sq_b = (float)c[o + 1];
-            kc.mus_b = (float)c[a.recip ? 5 : 9] * kc.sx_b;
+        const int64_t rows_left = a.n - r0;
+        const int64_t full_steps = rows_left / kGK;
+        const int n_full = full_steps <= 0 ? 0 : (full_steps >= nk ? nk : (int)full_steps);
+        const uint32_t tbase = tmem + tlane + kPTmemA;
+        for (int k = grp; k < nk; k += kPGroups) {
+            const int rs = k % kPRawStages, as = k % kPAStages;
+            if (!warp_wait(rfull0 + 8 * rs, (k / kPRawStages) & 1, a.err, 5, lane)) break;
+            const unsigned char* raw = rawring + rs * kRawBox;
+            Split8 xo0, qo0, xo1, qo1;
+            if (k < n_full) {
+                convert_a<false>(raw, m, 0, kGK, sxa, nmua, sqa, xo0, qo0);
+                convert_a<false>(raw, m, 1, kGK, sxa, nmua, sqa, xo1, qo1);
+            } else {
+                const int64_t left = rows_left - (int64_t)k * kGK;
+                const int valid = left <= 0 ? 0 : (int)left;
+                convert_a<true>(raw, m, 0, valid, sxa, nmua, sqa, xo0, qo0);
+                convert_a<true>(raw, m, 1, valid, sxa, nmua, sqa, xo1, qo1);
+            }
+            // the A stage must be free: the MMAs of step k - 4 have completed
+            if (k >= kPAStages && !warp_wait(aempty0 + 8 * as, ((k / kPAStages) - 1) & 1, a.err, 6, lane)) break;
+            tc_fence_after();
+            const uint32_t ta = tbase + (uint32_t)(as * kPTmemAStride);
+            tmem_st4(ta + 0, xo0.hi);
+            tmem_st4(ta + 4, xo1.hi);
+            tmem_st4(ta + 8, xo0.lo);
+            tmem_st4(ta + 12, xo1.lo);
+            tmem_st4(ta + 16, qo0.hi);
+            tmem_st4(ta + 20, qo1.hi);
+            tmem_st4(ta + 24, qo0.lo);
+            tmem_st4(ta + 28, qo1.lo);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(afull0 + 8 * as);
+                // the raw A tile has been consumed (its values are in the stores above)
+                mbar_arrive(rempty0 + 8 * rs);
+            }
         }
-        PairCtx cx;
-        cx.raw0 = raw0;
-        cx.ys0 = ys0;
-        cx.bop0 = bop0;
-        cx.rfull0 = rfull0;
-        cx.rempty0 = rempty0;
-        cx.ofull0 = ofull0;
-        cx.oempty0 = oempty0;
-        cx.tmem_a = tmem + tlane + kTmemA + 4 * h;
-        cx.m = m;
-        cx.h = h;
-        cx.lane = lane;
-        cx.rank = rank;
-        cx.q_half = (m >> 6) == rank;
-        cx.nk = nk;
-        cx.rows_left = a.n - r0;
-        {
-            const int64_t full = cx.rows_left / kGK;
-            cx.n_full = full <= 0 ? 0 : (full >= nk ? nk : (int)full);
-        }
-        cx.eps = a.eps;
-        cx.err = a.err;
-        if (same) pair_conv_loop<true, false>(cx, kc, grp);
-        else if (a.recip) pair_conv_loop<false, true>(cx, kc, grp);
-        else pair_conv_loop<false, false>(cx, kc, grp);
-        if (grp == 0) {
+        if (grp < 2) {
+            // groups 0 and 1 drain the accumulators: the two warps of a lane quarter take
+            // alternate 32-column chunks
             const bool done = warp_wait(accum, 0, a.err, 3, lane);
             tc_fence_after();
-            if (done && nk > 0 && slot >= 0) {
-                float* out = a.partial + ((int64_t)blockIdx.y * a.n_slots + slot) * 3 * kGT * kGT;
+            if (done && nk > 0) {
+                float* out = a.partial + ((int64_t)blockIdx.y * a.n_tiles + blockIdx.x) * 3 * kGT * kGT;
                 #pragma unroll 1
-                for (int idx = h; idx < 3 * kGT / 32; idx += 2) {
+                for (int idx = grp; idx < 3 * kGT / 32; idx += 2) {
+                    // partial [C | Q | W]: C at TMEM column 0, W at 128, Q at 256
                     const int gi = idx >> 2, cc = (idx & 3) * 32;
                     const uint32_t tcol = (gi == 0 ? kTmemCW : gi == 1 ? kTmemQ : kTmemCW + kGT) + (uint32_t)cc;
-                    const int c0 = idx * 32;
                     float tt[32];
                     tmem_ld32(tmem + tlane + tcol, tt);
-                    float* op = out + (int64_t)c0 * kGT + m;
+                    float* op = out + (int64_t)(idx * 32) * kGT + m;
                     #pragma unroll
                     for (int c = 0; c < 32; ++c) op[(int64_t)c * kGT] = tt[c];
                 }
@@ -1029,17 +945,87 @@ gram_pair_kernel(const __grid_constant__ CUtensorMap xmap, const PairArgs a) {
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
-        // every MMA of the pair (which reads both CTAs' shared memory and writes both TMEMs)
-        // has completed before either CTA frees TMEM or exits
         if (lane == 0) mbar_wait(accum, 0, a.err, 7);
         __syncwarp();
-    }
-    __syncthreads();
-    cluster_sync_all();
-    if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
                      : "memory");
+    }
+}
+
+// B planes of columns [c0, c0 + 8 gridDim.y) (< f_pad), rows [256 blockIdx.x, +256): warp w
+// converts column c0 + 8 blockIdx.y + w, thread = 8 rows (one K half of one 16-row step),
+// read as two float4 (a warp reads 1 KB of one column); columns at or beyond f and rows at
+// or beyond n are zero.  The arithmetic is gram_fused_kernel's B-side conversion:
+// b' = fma(v, s, -fl32(mean) s), b' (s_y ycen), v^2 s_q, with v = x or 1/safe(x), each split
+// into hi and lo fp16 planes (order BH WBH BL WBL BQH BQL).  Layout: the 16 rows of
+// step t of column c are 32 bytes at ((plane * steps + t) * f_pad + c) * 16 halves, K half h
+// in 16-byte chunk h ^ ((c >> 2) & 1) (the 32-byte swizzle of a 128-row K-major tile whose
+// rows are the columns c).  The CTA's 4 planes x 16 steps x 8 columns go through shared
+// memory so the stores are 256-byte runs.
+template <bool kRecip>
+__global__ void __launch_bounds__(256) gram_bplanes_kernel(const float* __restrict__ x, int64_t ld, int64_t n,
+                                                           int64_t f, int64_t c0, int64_t f_pad,
+                                                           const double* __restrict__ cs,
+                                                           const float* __restrict__ ys, float eps,
+                                                           __half* __restrict__ planes) {
+    __shared__ uint4 stage[kBPlanes][16][8][2];   // [plane][step][column][chunk]: 24 KB
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t cb = c0 + (int64_t)blockIdx.y * 8;   // first column of this CTA
+    const int64_t c = cb + w;
+    const int64_t r = (int64_t)blockIdx.x * 256 + lane * 8;
+    uint4 o[kBPlanes];
+    #pragma unroll
+    for (int p = 0; p < kBPlanes; ++p) o[p] = make_uint4(0, 0, 0, 0);
+    if (c < f) {
+        const float4 u0 = __ldg(reinterpret_cast<const float4*>(x + c * ld + r));
+        const float4 u1 = __ldg(reinterpret_cast<const float4*>(x + c * ld + r + 4));
+        const float4 y0 = __ldg(reinterpret_cast<const float4*>(ys + r));
+        const float4 y1 = __ldg(reinterpret_cast<const float4*>(ys + r + 4));
+        float v[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+        if (kRecip) {
+            #pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = safe_recip(v[e], eps);
+        }
+        const double* cc = cs + c * 12;
+        const float s = (float)cc[kRecip ? 3 : 0], sq = (float)cc[kRecip ? 4 : 1];
+        const float mus = (float)cc[kRecip ? 5 : 9] * s;
+        const uint64_t s2 = pk(s, s), nmu = pk(-mus, -mus), sq2 = pk(sq, sq);
+        uint64_t v2[4], t2[4];
+        #pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const uint64_t x2 = pk(v[2 * p], v[2 * p + 1]);
+            v2[p] = fma2(x2, s2, nmu);
+            t2[p] = mul2(mul2(x2, x2), sq2);
+            const bool k0 = r + 2 * p < n, k1 = r + 2 * p + 1 < n;
+            const float2 cv = upk(v2[p]), qv = upk(t2[p]);
+            v2[p] = pk(k0 ? cv.x : 0.f, k1 ? cv.y : 0.f);
+            t2[p] = pk(k0 ? qv.x : 0.f, k1 ? qv.y : 0.f);
+        }
+        Split8 b, w, q;
+        split8(v2, b);
+        split8(t2, q);
+        v2[0] = mul2(v2[0], pk(y0.x, y0.y));
+        v2[1] = mul2(v2[1], pk(y0.z, y0.w));
+        v2[2] = mul2(v2[2], pk(y1.x, y1.y));
+        v2[3] = mul2(v2[3], pk(y1.z, y1.w));
+        split8(v2, w);
+        o[0] = make_uint4(b.hi[0], b.hi[1], b.hi[2], b.hi[3]);
+        o[1] = make_uint4(w.hi[0], w.hi[1], w.hi[2], w.hi[3]);
+        o[2] = make_uint4(b.lo[0], b.lo[1], b.lo[2], b.lo[3]);
+        o[3] = make_uint4(w.lo[0], w.lo[1], w.lo[2], w.lo[3]);
+        o[4] = make_uint4(q.hi[0], q.hi[1], q.hi[2], q.hi[3]);
+        o[5] = make_uint4(q.lo[0], q.lo[1], q.lo[2], q.lo[3]);
+    }
+    const int chunk = (lane & 1) ^ (int)((c >> 2) & 1);
+    #pragma unroll
+    for (int p = 0; p < kBPlanes; ++p) stage[p][lane >> 1][w][chunk] = o[p];
+    __syncthreads();
+    const int64_t steps = ld / kGK, t0 = (int64_t)blockIdx.x * 16;
+    uint4* out = reinterpret_cast<uint4*>(planes);
+    for (int q = threadIdx.x; q < kBPlanes * 16 * 16; q += 256) {
+        const int p = q >> 8, st = (q >> 4) & 15, e = q & 15;   // e: column (e >> 1), chunk (e & 1)
+        out[(((int64_t)p * steps + t0 + st) * f_pad + cb) * 2 + e] = stage[p][st][e >> 1][e & 1];
     }
 }
 
@@ -1412,17 +1398,20 @@ int64_t max_chunk_rows() {
 
 }  // namespace
 
-// CTA-pair Gram kernel (cta_group::2) when GAFIME_GRAM_PAIRS=1.  Off by default: it
-// halves each SM's B-operand conversion and shared-memory traffic, but the two CTAs of a
-// pair wait on each other every step, and on the measured workloads (1e6 x 256 and
-// 2e6 x 2048) it is 3-35 % slower than the single-CTA kernel.
-bool gram_pairs_enabled() {
+// The B-planes kernel is opt-in (GAFIME_GRAM_KERNEL=planes; =fused forces the fused kernel).
+// Measured on the 2e6 x 2048 table it runs the Gram tiles in 92 ms against the fused
+// kernel's 104 ms, but writing the planes costs 17 ms, so the fused kernel stays the
+// default at every width.  kPlanesMinReuse (tiles per distinct B block) is the rule the
+// default would use once the planes pay for themselves.
+constexpr double kPlanesMinReuse = 1e30;
+
+int gram_kernel_env() {
     static int env = -1;
     if (env < 0) {
-        const char* v = getenv("GAFIME_GRAM_PAIRS");
-        env = (v && std::string(v) == "1") ? 1 : 0;
+        const char* v = getenv("GAFIME_GRAM_KERNEL");
+        env = !v ? 0 : std::string(v) == "fused" ? 1 : std::string(v) == "planes" ? 2 : 0;
     }
-    return env != 0;
+    return env;
 }
 
 bool gram_path_enabled(const Bucket& b) {
@@ -1531,10 +1520,30 @@ int gram_tiles128(const std::vector<TileCoord>& tiles64) {
     return (int)(std::unique(t.begin(), t.end()) - t.begin());
 }
 
+bool gram_use_planes(const Bucket& b, const std::vector<TileCoord>& tiles64) {
+    const int env = gram_kernel_env();
+    if (env != 0) return env == 2;
+    const int nb128 = (int)((b.f + kGT - 1) / kGT);
+    std::vector<char> seen((size_t)nb128 * nb128, 0), bcol((size_t)nb128, 0);
+    int tiles = 0, bblocks = 0;
+    for (const TileCoord& t : tiles64) {
+        const int I = t.bi >> 1, J = t.bj >> 1;
+        if (!seen[(size_t)I * nb128 + J]) {
+            seen[(size_t)I * nb128 + J] = 1;
+            ++tiles;
+        }
+        if (!bcol[(size_t)J]) {
+            bcol[(size_t)J] = 1;
+            ++bblocks;
+        }
+    }
+    return bblocks > 0 && (double)tiles / bblocks >= kPlanesMinReuse;
+}
+
 cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoord* d_tiles64,
                                 const std::vector<TileCoord>& tiles64, bool recip, float eps,
                                 double* d_moments, cudaStream_t stream, int* host_err, int prep_mode,
-                                int64_t chunk_rows) {
+                                int64_t chunk_rows, int use_planes) {
     if (host_err) *host_err = 0;
     const int64_t f = b.f, ld = b.ld, n = b.n;
     const int nb128 = (int)((f + kGT - 1) / kGT);
@@ -1550,41 +1559,24 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     }
     const int nt = (int)t128.size();
     if (nt == 0) return cudaSuccess;
-    // CTA pairs (cta_group::2): the 128-tiles of one B block J, two A blocks per pair; an odd
-    // one out is paired with itself and its second result discarded
-    const bool pairs_on = gram_pairs_enabled();
-    std::vector<PairCoord> pairs;
-    if (pairs_on) {
-        std::vector<std::vector<std::pair<int, int>>> by_j(nb128);
-        for (int s = 0; s < nt; ++s) by_j[t128[s].bj].push_back({t128[s].bi, s});
-        for (int J = 0; J < nb128; ++J) {
-            auto& v = by_j[J];
-            std::sort(v.begin(), v.end());
-            for (size_t q = 0; q < v.size(); q += 2) {
-                PairCoord pc;
-                pc.j = J;
-                pc.i0 = v[q].first;
-                pc.t0 = v[q].second;
-                pc.i1 = q + 1 < v.size() ? v[q + 1].first : v[q].first;
-                pc.t1 = q + 1 < v.size() ? v[q + 1].second : -1;
-                pairs.push_back(pc);
-            }
-        }
-    }
-    const int ctas_per_chunk = pairs_on ? 2 * (int)pairs.size() : nt;
-    const int64_t chunk = chunk_rows > 0 ? chunk_rows : gram_chunk_rows(b, ctas_per_chunk);
+    const bool planes = use_planes < 0 ? gram_use_planes(b, tiles64) : use_planes != 0;
+    const int64_t chunk = chunk_rows > 0 ? chunk_rows : gram_chunk_rows(b, nt);
     const int n_chunks = (int)((ld + chunk - 1) / chunk);
 
-    // scratch of this tile set: partial | lut | tiles128 | pairs; the per-column state (scales,
-    // scaled target, error flag) lives in its own buffer, shared by both moment groups of a
-    // call and by every tile set of a streamed call
+    // scratch of this tile set: partial | lut | tiles128; the per-column state (scales, scaled
+    // target, error flag) lives in its own buffer, shared by both moment groups of a call and
+    // by every tile set of a streamed call, and the B planes in theirs
     size_t part_bytes = (size_t)n_chunks * nt * 3 * kGT * kGT * sizeof(float);
     size_t off_lut = (part_bytes + 255) / 256 * 256;
     size_t off_t128 = (off_lut + lut.size() * sizeof(int) + 255) / 256 * 256;
-    size_t off_pairs = (off_t128 + t128.size() * sizeof(TileCoord) + 255) / 256 * 256;
-    size_t total = (off_pairs + t128.size() * sizeof(PairCoord) + 255) / 256 * 256;
+    size_t total = (off_t128 + t128.size() * sizeof(TileCoord) + 255) / 256 * 256;
     cudaError_t e = ensure(b.gram, total);
     if (e != cudaSuccess) return e;
+    const int64_t f_pad = (int64_t)nb128 * kGT;
+    if (planes) {
+        e = ensure(b.gram_planes, (size_t)kBPlanes * f_pad * ld * sizeof(__half));
+        if (e != cudaSuccess) return e;
+    }
     GramCols gc;
     e = gram_cols(b, gc);
     if (e != cudaSuccess) return e;
@@ -1592,7 +1584,6 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     float* partial = (float*)base;
     int* d_lut = (int*)(base + off_lut);
     TileCoord* d_t128 = (TileCoord*)(base + off_t128);
-    PairCoord* d_pairs = (PairCoord*)(base + off_pairs);
     double* d_cs = gc.cs;
     float* d_ys = gc.ys;
     int* d_err = gc.err;
@@ -1600,8 +1591,6 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     e = cudaMemcpyAsync(d_lut, lut.data(), lut.size() * sizeof(int), cudaMemcpyHostToDevice, stream);
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(d_t128, t128.data(), t128.size() * sizeof(TileCoord), cudaMemcpyHostToDevice, stream);
-    if (e == cudaSuccess && pairs_on)
-        e = cudaMemcpyAsync(d_pairs, pairs.data(), pairs.size() * sizeof(PairCoord), cudaMemcpyHostToDevice, stream);
     // the flag only (absmax follows at +64); with host_err null the caller clears and reads it
     if (e == cudaSuccess && host_err) e = cudaMemsetAsync(d_err, 0, 64, stream);
     if (e != cudaSuccess) return e;
@@ -1628,50 +1617,65 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
 
     CUtensorMap xmap;
     if (!make_x_map(&xmap, cs.d_x, ld, f)) return cudaErrorInvalidValue;
-    GramArgs ga;
-    ga.tiles = d_t128;
-    ga.n_tiles = nt;
-    ga.chunk_rows = chunk;
-    ga.rows = ld;
-    ga.n = n;
-    ga.f = f;
-    ga.ys = d_ys;
-    ga.cs = d_cs;
-    ga.recip = recip ? 1 : 0;
-    ga.eps = eps;
-    ga.partial = partial;
-    ga.err = d_err;
-    if (pairs_on) {
-        PairArgs pa;
-        pa.pairs = d_pairs;
-        pa.n_slots = nt;
+    if (planes) {
+        // the B planes of the blocks this set reads as B (runs of consecutive blocks per launch)
+        __half* d_planes = (__half*)b.gram_planes.ptr;
+        std::vector<char> bused((size_t)nb128, 0);
+        for (const TileCoord& t : t128) bused[(size_t)t.bj] = 1;
+        {
+            KernelTimer timer(stream, GAFIME_KERNEL_GRAM_PREP);
+            for (int B0 = 0; B0 < nb128;) {
+                if (!bused[(size_t)B0]) { ++B0; continue; }
+                int B1 = B0;
+                while (B1 < nb128 && bused[(size_t)B1]) ++B1;
+                // grid: 256-row slabs x 8-column groups (at most 32768 groups per launch)
+                for (int64_t c0 = (int64_t)B0 * kGT; c0 < (int64_t)B1 * kGT; c0 += 8 * 32768) {
+                    const int64_t cols = std::min<int64_t>(8 * 32768, (int64_t)B1 * kGT - c0);
+                    const dim3 grid((unsigned)(ld / 256), (unsigned)(cols / 8));
+                    if (recip)
+                        gram_bplanes_kernel<true><<<grid, 256, 0, stream>>>(cs.d_x, ld, n, f, c0, f_pad, d_cs, d_ys,
+                                                                           eps, d_planes);
+                    else
+                        gram_bplanes_kernel<false><<<grid, 256, 0, stream>>>(cs.d_x, ld, n, f, c0, f_pad, d_cs, d_ys,
+                                                                            eps, d_planes);
+                }
+                B0 = B1;
+            }
+        }
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        PlanesArgs pa;
+        pa.steps = ld / kGK;
+        pa.planes = d_planes;
+        pa.tiles = d_t128;
+        pa.n_tiles = nt;
         pa.chunk_rows = chunk;
         pa.rows = ld;
         pa.n = n;
         pa.f = f;
-        pa.ys = d_ys;
+        pa.f_pad = f_pad;
         pa.cs = d_cs;
-        pa.recip = recip ? 1 : 0;
-        pa.eps = eps;
         pa.partial = partial;
         pa.err = d_err;
-        e = cudaFuncSetAttribute(gram_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPairSmem);
+        e = cudaFuncSetAttribute(gram_planes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPlanesSmem);
         if (e != cudaSuccess) return e;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)(2 * pairs.size()), (unsigned)n_chunks);
-        cfg.blockDim = dim3(kGramThreads);
-        cfg.dynamicSmemBytes = kPairSmem;
-        cfg.stream = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
         KernelTimer timer(stream, GAFIME_KERNEL_GRAM_TC);
-        e = cudaLaunchKernelEx(&cfg, gram_pair_kernel, xmap, pa);
+        gram_planes_kernel<<<dim3((unsigned)nt, (unsigned)n_chunks), kGramThreads, kPlanesSmem, stream>>>(xmap, pa);
+        e = cudaGetLastError();
     } else {
+        GramArgs ga;
+        ga.tiles = d_t128;
+        ga.n_tiles = nt;
+        ga.chunk_rows = chunk;
+        ga.rows = ld;
+        ga.n = n;
+        ga.f = f;
+        ga.ys = d_ys;
+        ga.cs = d_cs;
+        ga.recip = recip ? 1 : 0;
+        ga.eps = eps;
+        ga.partial = partial;
+        ga.err = d_err;
         e = cudaFuncSetAttribute(gram_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGramSmem);
         if (e != cudaSuccess) return e;
         KernelTimer timer(stream, GAFIME_KERNEL_GRAM_TC);

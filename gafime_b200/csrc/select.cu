@@ -155,7 +155,39 @@ __global__ void __launch_bounds__(1024) merge_kernel(const Cand* __restrict__ in
     for (int e = threadIdx.x; e < k_pad; e += blockDim.x) out[(int64_t)g * k_pad + e] = s[e];
 }
 
+__global__ void fill_empty_kernel(Cand* out, size_t n) {
+    for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (size_t)gridDim.x * blockDim.x) {
+        Cand c;
+        c.score = 0.0;
+        c.pid = kNoPair;
+        c.pad = 0;
+        out[e] = c;
+    }
+}
+
+__global__ void reorder_kernel(const Cand* __restrict__ in, Cand* __restrict__ out, int n_shards, int n_ops,
+                               int k_pad) {
+    const size_t total = (size_t)n_shards * n_ops * k_pad;
+    for (size_t x = (size_t)blockIdx.x * blockDim.x + threadIdx.x; x < total; x += (size_t)gridDim.x * blockDim.x) {
+        const size_t s = x / ((size_t)n_ops * k_pad), o = (x / k_pad) % n_ops, e = x % k_pad;
+        out[(o * n_shards + s) * k_pad + e] = in[x];
+    }
+}
+
 }  // namespace
+
+cudaError_t fill_empty_lists(Cand* out, size_t n, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    fill_empty_kernel<<<(unsigned)std::min<size_t>(1024, (n + 255) / 256), 256, 0, stream>>>(out, n);
+    return cudaGetLastError();
+}
+
+cudaError_t reorder_shard_lists(const Cand* in, Cand* out, int n_shards, int n_ops, int k_pad, cudaStream_t stream) {
+    const size_t total = (size_t)n_shards * n_ops * k_pad;
+    reorder_kernel<<<(unsigned)std::min<size_t>(1024, (total + 255) / 256), 256, 0, stream>>>(in, out, n_shards, n_ops,
+                                                                                           k_pad);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_epilogue_topk(const EpilogueArgs& a, cudaStream_t stream) {
     if (a.n_tiles <= 0) return cudaSuccess;

@@ -246,6 +246,30 @@ int gafime_allpairs_topk_host(ContiguousBucket bucket, const float* h_data, cons
                               int32_t* out_i, int32_t* out_j, double* out_score, int* out_count);
 
 /*
+ * NEW.  gafime_allpairs_topk for one shard with the result left on the device, for the
+ * candidate exchange of a multi-GPU job (the all-gather runs on device buffers, with no
+ * host copy in between).  Queues the scoring on the bucket's stream
+ * (gafime_contiguous_bucket_stream) and returns without waiting for it.  d_cands (device,
+ * 16-byte aligned) receives, per operator, next_pow2(k) candidate records of 16 bytes
+ * (fp64 signed score, uint32 pair id i * F + j, 4 bytes padding) sorted by |score|
+ * descending then pair id ascending; empty slots have pair id 0xFFFFFFFF.  Finish with
+ * gafime_topk_merge_device on the same bucket, which reports any kernel failure.
+ */
+int gafime_allpairs_topk_device(ContiguousBucket bucket, const int* interact_types, int n_ops,
+                                int metric, int center, float div_eps, int mi_bins, int k,
+                                int shard_id, int n_shards, void* d_cands);
+
+/*
+ * NEW.  Device merge of n_shards shards' gafime_allpairs_topk_device lists, as they lie after
+ * an all-gather: d_gathered holds n_shards blocks of n_ops lists of next_pow2(k) records.
+ * Orders them on the bucket's stream (after the work queued there, so an all-gather run on
+ * that stream is waited for), copies the k best per operator to the host in the layout of
+ * gafime_allpairs_topk and waits for them.  Same ranking as gafime_topk_merge.
+ */
+int gafime_topk_merge_device(ContiguousBucket bucket, const void* d_gathered, int n_shards, int n_ops, int k,
+                             int32_t* out_i, int32_t* out_j, double* out_score, int* out_count);
+
+/*
  * NEW.  Signed score of every pair i<j for one operator, in row-major
  * upper-triangle order (p = i*F - i*(i+1)/2 + j - i - 1), P = F*(F-1)/2 entries.
  * Serves Backend.score_combos (gafime/backends/base.py:67-78) when the combo list

@@ -223,6 +223,35 @@ def test_shards_merge_to_the_single_process_topk(native):
                 np.testing.assert_array_equal(ms, full[op][2])
 
 
+def test_device_lists_merge_to_the_single_process_topk(native):
+    """The multi-GPU exchange on device buffers: each shard's gafime_allpairs_topk_device
+    lists, laid side by side as an all-gather leaves them, merge on the device
+    (gafime_topk_merge_device) to the single-process top-k, including shards with no tile
+    (9 shards of 200 columns: more shards than 128-column block pairs)."""
+    import torch
+    rng = np.random.default_rng(12)
+    X = rng.standard_normal((4000, 200)).astype(np.float32)
+    y = rng.standard_normal(4000).astype(np.float32)
+    ops, k = ["multiply", "divide"], 50
+    L = native.list_len(k)
+    with bucket_for(native, X, y) as b:
+        full = b.topk(ops, k, div_eps=1e-6)
+        for n_shards in (1, 2, 3, 9):
+            gathered = torch.zeros(n_shards * len(ops) * L * 2, dtype=torch.int64, device="cuda")
+            for s in range(n_shards):
+                part = torch.zeros(len(ops) * L * 2, dtype=torch.int64, device="cuda")
+                torch.cuda.synchronize()
+                b.topk_device(ops, k, part.data_ptr(), div_eps=1e-6, shard_id=s, n_shards=n_shards)
+                torch.cuda.synchronize()
+                b.merge_device(part.data_ptr(), 1, ops, k)   # a lone shard's own lists merge too
+                gathered[s * len(ops) * L * 2:(s + 1) * len(ops) * L * 2] = part
+            torch.cuda.synchronize()
+            got = b.merge_device(gathered.data_ptr(), n_shards, ops, k)
+            for op in ops:
+                for u, v in zip(got[op], full[op]):
+                    np.testing.assert_array_equal(u, v)
+
+
 def test_non_finite_input_is_rejected(native):
     X = np.ones((100, 4), dtype=np.float32)
     X[5, 2] = np.nan
@@ -329,28 +358,31 @@ def test_tensor_core_moments_match_cuda_core_kernel(native, tmp_path):
             assert_pearson_close(b.scores(op, div_eps=1e-6), ref[op])
 
 
-def test_cta_pair_gram_kernel_matches_cuda_core_kernel(native, tmp_path):
-    """The opt-in CTA-pair (cta_group::2) Gram kernel (GAFIME_GRAM_PAIRS=1, a separate
-    process) scores like the CUDA-core kernel, including an odd tile count per B block (the
-    self-paired CTA) and a ragged last block."""
+@pytest.mark.parametrize("kernel", ["planes", "fused"])
+def test_each_gram_kernel_matches_cuda_core_kernel(native, tmp_path, kernel):
+    """Both tensor-core Gram kernels, each forced with GAFIME_GRAM_KERNEL in a separate process
+    (the B-planes kernel is otherwise chosen for wide tables only), score like the CUDA-core
+    kernel for all four operators, with a ragged last column block and a ragged last row
+    chunk."""
     import os
     import subprocess
     import sys
     rng = np.random.default_rng(23)
-    n, f = 50_000, 300
+    n, f = 50_003, 300
     X = np.hstack([rng.standard_normal((n, 150)), rng.lognormal(0, 1, (n, 150))]).astype(np.float32)
     y = (X[:, 11] * X[:, 200] + rng.standard_normal(n) > 1.0).astype(np.float32)
+    X[:, 5] += 40.0   # one column far from zero: the accuracy guard on each kernel
     src = tmp_path / "in.npz"
     np.savez(src, X=X, y=y)
     repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     outs = {}
-    for name, extra in (("pairs", {"GAFIME_GRAM_PAIRS": "1"}), ("cuda_core", {"GAFIME_PAIR_MOMENTS": "cuda-core"})):
+    for name, extra in ((kernel, {"GAFIME_GRAM_KERNEL": kernel}), ("cuda_core", {"GAFIME_PAIR_MOMENTS": "cuda-core"})):
         dst = tmp_path / f"{name}.npz"
         subprocess.run([sys.executable, "-c", _CUDA_CORE_SCRIPT, repo, str(src), str(dst)],
                        env=dict(os.environ, **extra), check=True, timeout=600)
         outs[name] = np.load(dst)
     for op in OPS:
-        assert_pearson_close(outs["pairs"][op], outs["cuda_core"][op])
+        assert_pearson_close(outs[kernel][op], outs["cuda_core"][op])
 
 
 def test_interaction_materialiser_matches_oracle(native, golden, oracle):
@@ -689,3 +721,30 @@ def test_guard_rescore_matches_the_oracle_on_a_mixed_table(native, oracle):
             assert_topk_equivalent(i, j, want, pi, pj, 25)
             pos = {(int(a), int(c)): p for p, (a, c) in enumerate(zip(pi, pj))}
             assert_pearson_close(sc, np.array([want[pos[(int(a), int(c))]] for a, c in zip(i, j)]))
+
+
+def test_wide_table_matches_the_oracle_and_streams_identically(native, oracle):
+    """1024 columns (8 column blocks): multiply and divide against the oracle on the top-k and
+    on sampled pairs, and the streamed call equal to upload + top-k (with the B-planes kernel
+    forced, test_each_gram_kernel_matches_cuda_core_kernel covers that kernel)."""
+    rng = np.random.default_rng(29)
+    n, f = 20_000, 1024
+    X = np.hstack([rng.standard_normal((n, 512)), rng.lognormal(0, 1, (n, 512))]).astype(np.float32)
+    y = (X[:, 3] * X[:, 700] + rng.standard_normal(n) > 0.5).astype(np.float32)
+    pi, pj = np.triu_indices(f, k=1)
+    sample = np.random.default_rng(0).choice(len(pi), 3000, replace=False)
+    with bucket_for(native, X, y) as b:
+        for op in ("multiply", "divide"):
+            allsc = b.scores(op, div_eps=1e-6)
+            ws = oracle.raw_pearson(X, y, op, pi[sample].astype(np.int32), pj[sample].astype(np.int32),
+                                    div_eps=1e-6)
+            assert_pearson_close(allsc[sample], ws)
+            gi, gj, gs = b.topk([op], 64, div_eps=1e-6)[op]
+            assert_pearson_close(gs, oracle.raw_pearson(X, y, op, gi.astype(np.int32), gj.astype(np.int32),
+                                                        div_eps=1e-6))
+        want = b.topk(["multiply", "divide"], 64, div_eps=1e-6)
+    with native.Bucket(n, f) as s:
+        got = s.topk_from_host(native.pack_columns(X, y), ["multiply", "divide"], 64, div_eps=1e-6)
+    for op in ("multiply", "divide"):
+        for u, v in zip(got[op], want[op]):
+            np.testing.assert_array_equal(u, v)
