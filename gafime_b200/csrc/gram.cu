@@ -728,9 +728,8 @@ struct PlanesArgs {
     int64_t chunk_rows;       // multiple of kGK
     int64_t rows;             // padded rows (ld)
     int64_t n, f;
-    int64_t f_pad;            // columns per plane (a multiple of 128)
-    int64_t steps;            // 16-row steps per plane (ld / 16)
-    const __half* planes;     // [plane][step][f_pad][16] fp16, 32-byte swizzled (gram_bplanes_kernel)
+    int64_t nb;               // 128-column blocks (f_pad / 128)
+    const __half* planes;     // [step][block][plane][128][16] fp16, 32-byte swizzled (gram_bplanes_kernel)
     const double* cs;         // per-column scales and means (12 doubles per column)
     float* partial;           // [chunk][tile][3][128 n][128 m]
     int* err;
@@ -824,15 +823,14 @@ gram_planes_kernel(const __grid_constant__ CUtensorMap xmap, const PlanesArgs a)
                 const int64_t row = r0 + (int64_t)k * kGK;
                 mbar_expect_tx(rfull0 + 8 * rs, (uint32_t)kRawBox);
                 tma_load_2d(smem_u32(rawring + rs * kRawBox), &xmap, rfull0 + 8 * rs, (int)row, tc.bi * kGT);
-                // plane tile (p, step, B block): 4 KB contiguous, already swizzled
+                // the six plane tiles of (step, B block): one contiguous 24 KB run, already
+                // swizzled -- one copy per step (the copy engine takes few operations at a time,
+                // so six 4 KB copies per step starved the pipeline)
                 const int64_t step = row / kGK;
                 const uint32_t bst = smem_u32(bring + bs * kPBStageBytes);
                 mbar_expect_tx(bfull0 + 8 * bs, (uint32_t)kPBStageBytes);
-                #pragma unroll
-                for (int p = 0; p < kBPlanes; ++p)
-                    bulk_load(bst + p * kOpBytes,
-                              a.planes + (((int64_t)p * a.steps + step) * a.f_pad + (int64_t)tc.bj * kGT) * kGK,
-                              (uint32_t)kOpBytes, bfull0 + 8 * bs);
+                bulk_load(bst, a.planes + (step * a.nb + tc.bj) * (int64_t)(kPBStageBytes / 2), (uint32_t)kPBStageBytes,
+                          bfull0 + 8 * bs);
                 ++issued;
             }
             if (!ok) {
@@ -958,11 +956,12 @@ gram_planes_kernel(const __grid_constant__ CUtensorMap xmap, const PlanesArgs a)
 // read as two float4 (a warp reads 1 KB of one column); columns at or beyond f and rows at
 // or beyond n are zero.  The arithmetic is gram_fused_kernel's B-side conversion:
 // b' = fma(v, s, -fl32(mean) s), b' (s_y ycen), v^2 s_q, with v = x or 1/safe(x), each split
-// into hi and lo fp16 planes (order BH WBH BL WBL BQH BQL).  Layout: the 16 rows of
-// step t of column c are 32 bytes at ((plane * steps + t) * f_pad + c) * 16 halves, K half h
-// in 16-byte chunk h ^ ((c >> 2) & 1) (the 32-byte swizzle of a 128-row K-major tile whose
-// rows are the columns c).  The CTA's 4 planes x 16 steps x 8 columns go through shared
-// memory so the stores are 256-byte runs.
+// into hi and lo fp16 planes (order BH WBH BL WBL BQH BQL).  Layout: step-major, then
+// 128-column block, then plane: the 16 rows of step t of column c = 128 J + m are 32 bytes at
+// ((t * nb + J) * 6 + plane) * 2048 + m * 16 halves, K half h in 16-byte chunk
+// h ^ ((m >> 2) & 1) (the 32-byte swizzle of a 128-row K-major tile whose rows are the
+// columns), so the six tiles of one step and block are one contiguous 24 KB run.  The CTA's
+// 6 planes x 16 steps x 8 columns go through shared memory so the stores are 256-byte runs.
 template <bool kRecip>
 __global__ void __launch_bounds__(256) gram_bplanes_kernel(const float* __restrict__ x, int64_t ld, int64_t n,
                                                            int64_t f, int64_t c0, int64_t f_pad,
@@ -1021,11 +1020,12 @@ __global__ void __launch_bounds__(256) gram_bplanes_kernel(const float* __restri
     #pragma unroll
     for (int p = 0; p < kBPlanes; ++p) stage[p][lane >> 1][w][chunk] = o[p];
     __syncthreads();
-    const int64_t steps = ld / kGK, t0 = (int64_t)blockIdx.x * 16;
+    const int64_t nb = f_pad / kGT, t0 = (int64_t)blockIdx.x * 16, J = cb / kGT, m0 = cb % kGT;
     uint4* out = reinterpret_cast<uint4*>(planes);
     for (int q = threadIdx.x; q < kBPlanes * 16 * 16; q += 256) {
         const int p = q >> 8, st = (q >> 4) & 15, e = q & 15;   // e: column (e >> 1), chunk (e & 1)
-        out[(((int64_t)p * steps + t0 + st) * f_pad + cb) * 2 + e] = stage[p][st][e >> 1][e & 1];
+        // in uint4: a 4 KB tile is 256, one column's step 2
+        out[(((t0 + st) * nb + J) * kBPlanes + p) * 256 + m0 * 2 + e] = stage[p][st][e >> 1][e & 1];
     }
 }
 
@@ -1645,7 +1645,7 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
         PlanesArgs pa;
-        pa.steps = ld / kGK;
+        pa.nb = f_pad / kGT;
         pa.planes = d_planes;
         pa.tiles = d_t128;
         pa.n_tiles = nt;
@@ -1653,7 +1653,6 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
         pa.rows = ld;
         pa.n = n;
         pa.f = f;
-        pa.f_pad = f_pad;
         pa.cs = d_cs;
         pa.partial = partial;
         pa.err = d_err;
