@@ -143,6 +143,10 @@ WORKLOADS = {
     "config3": dict(n=4_000_000, f=128, ops=["multiply"], metric="mutual_info", center=True, k=50,
                     eps=1e-8, bins=32, desc="4e6 x 128 N(0,1), 3-class y, centred multiply, "
                                             "MI 32 equal-width bins, k=50"),
+    "config3q": dict(n=4_000_000, f=128, ops=["multiply"], metric="mutual_info_quantile", center=True, k=50,
+                     eps=1e-8, bins=32, desc="4e6 x 128 N(0,1), 3-class y, centred multiply, "
+                                             "MI 32 quantile bins on the interaction (no reference "
+                                             "counterpart), k=50"),
     "config4": dict(n=10_000_000, f=512, ops=["multiply"], metric="pearson", center=False, k=1000,
                     eps=1e-8, bins=16, desc="1e7 x 512 (256 Zipf codes + 256 N(0,1)), multiply, "
                                             "|Pearson|, k=1000"),
@@ -157,9 +161,9 @@ def build_packed(name: str, packed: np.ndarray):
     n, f = w["n"], w["f"]
     if name == "config2" and packed.shape[0] - 1 != f:
         fill_config2_scaled(packed, n)
-    elif name in ("config1", "config2", "config3"):
+    elif name in ("config1", "config2", "config3", "config3q"):
         X, y = make_config1() if name == "config1" else \
-            {"config2": make_config2, "config3": make_config3}[name](n=packed.shape[1])
+            {"config2": make_config2, "config3": make_config3, "config3q": make_config3}[name](n=packed.shape[1])
         packed[:f] = X.T
         packed[f] = y
     elif name == "config4":
@@ -344,6 +348,8 @@ class CpuArm:
         if self.w["metric"] == "pearson" and not self.w["center"]:
             self.lib = _ref_cpu_lib()
             self.mode = "perpair" if self.lib is not None else "port_raw"
+        elif self.w["metric"] == "mutual_info_quantile":
+            self.mode = "port_quantile"   # the reference has no quantile-bin mode
         else:
             self.core = _ref_core()
             self.mode = "core" if self.core is not None else "port_centred"
@@ -389,6 +395,10 @@ class CpuArm:
             self.core.score_combos(self._Xrow, self._y64, idx, off, [metric], self.w["bins"])
             return float(len(combos) * n)
         Xcol = self.packed[:self.f].T
+        if self.mode == "port_quantile":
+            self.orc.pair_mi_quantile(Xcol, self.y, ops[0], center=self.w["center"], mi_bins=self.w["bins"],
+                                      pi=self.pi[sample].astype(np.int32), pj=self.pj[sample].astype(np.int32))
+            return float(len(sample) * n)
         if self.mode == "port_raw":
             for op in ops:
                 self.orc.raw_pearson(Xcol, self.y, op, self.pi[sample].astype(np.int32),
@@ -424,7 +434,8 @@ class CpuArm:
         n_pairs = max(1, units // len(self.w["ops"]))
         what = {"perpair": "gafime_fused_interaction_perpair_cpu (src/cpu/cpu_backend.cpp, OpenMP over rows)",
                 "core": "gafime_core.score_combos (OpenMP over pairs)",
-                "port_raw": "oracle port raw_pearson", "port_centred": "oracle port centred_scores"}[self.mode]
+                "port_raw": "oracle port raw_pearson", "port_centred": "oracle port centred_scores",
+                "port_quantile": "oracle port pair_mi_quantile (the reference has no quantile bins)"}[self.mode]
         return (f"{what}: {n_pairs} random pairs x {len(self.w['ops'])} operator(s) x "
                 f"{self.n} rows in {dt:.1f} s")
 

@@ -29,7 +29,7 @@ ERRORS = {
 # interaction ids, interfaces.h:83-88
 INTERACT = {"multiply": 0, "add": 1, "subtract": 2, "divide": 3, "max": 4, "min": 5}
 # metric ids, gafime_core.cpp:28-33
-METRIC = {"pearson": 0, "mutual_info": 2}
+METRIC = {"pearson": 0, "mutual_info": 2, "mutual_info_quantile": 12}
 MAX_K = 4096
 
 # Every symbol include/gafime_b200.h declares.

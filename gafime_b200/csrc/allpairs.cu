@@ -177,6 +177,9 @@ Plan make_plan(const Bucket& b, int shard_id, int n_shards) {
 }
 
 bool valid_op(int op) { return op >= GAFIME_INTERACT_MULT && op <= GAFIME_INTERACT_DIV; }
+bool valid_metric(int m) {
+    return m == GAFIME_METRIC_PEARSON || m == GAFIME_METRIC_MUTUAL_INFO || m == GAFIME_METRIC_MUTUAL_INFO_QUANTILE;
+}
 
 // Column statistics for one call.  Mutual information centres on the fly from the
 // raw-column means, so it always asks for uncentred statistics.
@@ -282,6 +285,14 @@ int score_ops(Bucket& b, const ColumnStats& cs, const Plan& plan, const TileCoor
     const int nt = (int)plan.tiles.size();
     if (nt == 0) return GAFIME_SUCCESS;
     cudaError_t e;
+    if (metric == GAFIME_METRIC_MUTUAL_INFO_QUANTILE) {
+        for (int o = 0; o < n_ops; ++o) {
+            e = launch_mi_quantile(b, cs, center != 0, ops[o], div_eps, mi_bins, plan.tiles, d_tiles, k_pad,
+                                   cands[o], all_scores, b.stream);
+            if (e != cudaSuccess) return status_from(e);
+        }
+        return GAFIME_SUCCESS;
+    }
     if (metric == GAFIME_METRIC_MUTUAL_INFO) {
         for (int o = 0; o < n_ops; ++o) {
             e = launch_mi_scores(b, cs, center != 0, ops[o], div_eps, mi_bins, d_tiles, nt, k_pad,
@@ -378,8 +389,8 @@ int check_topk_args(ContiguousBucket bucket, const int* interact_types, int n_op
     if (!bucket || !interact_types || n_ops < 1 || n_ops > 4 || k < 1 || k > GAFIME_ALLPAIRS_MAX_K ||
         n_shards < 1 || shard_id < 0 || shard_id >= n_shards)
         return GAFIME_ERROR_INVALID_ARGS;
-    if (metric != GAFIME_METRIC_PEARSON && metric != GAFIME_METRIC_MUTUAL_INFO) return GAFIME_ERROR_INVALID_ARGS;
-    if (metric == GAFIME_METRIC_MUTUAL_INFO && (mi_bins < 2 || mi_bins > 255)) return GAFIME_ERROR_INVALID_ARGS;
+    if (!valid_metric(metric)) return GAFIME_ERROR_INVALID_ARGS;
+    if (metric != GAFIME_METRIC_PEARSON && (mi_bins < 2 || mi_bins > 255)) return GAFIME_ERROR_INVALID_ARGS;
     if (!(div_eps > 0.0f)) return GAFIME_ERROR_INVALID_ARGS;
     for (int o = 0; o < n_ops; ++o)
         if (!valid_op(interact_types[o])) return GAFIME_ERROR_INVALID_ARGS;
@@ -561,8 +572,8 @@ int merge_and_copy(Bucket& b, Cand* const* cands, Cand* const* tmp, int n_lists,
 extern "C" int gafime_allpairs_scores(ContiguousBucket bucket, int interact_type, int metric,
                                       int center, float div_eps, int mi_bins, double* out_scores) {
     if (!bucket || !out_scores || !valid_op(interact_type)) return GAFIME_ERROR_INVALID_ARGS;
-    if (metric != GAFIME_METRIC_PEARSON && metric != GAFIME_METRIC_MUTUAL_INFO) return GAFIME_ERROR_INVALID_ARGS;
-    if (metric == GAFIME_METRIC_MUTUAL_INFO && (mi_bins < 2 || mi_bins > 255)) return GAFIME_ERROR_INVALID_ARGS;
+    if (!valid_metric(metric)) return GAFIME_ERROR_INVALID_ARGS;
+    if (metric != GAFIME_METRIC_PEARSON && (mi_bins < 2 || mi_bins > 255)) return GAFIME_ERROR_INVALID_ARGS;
     if (!(div_eps > 0.0f)) return GAFIME_ERROR_INVALID_ARGS;
     Bucket& b = *(Bucket*)bucket;
     if (b.f >= 65536) return GAFIME_ERROR_INVALID_ARGS;
@@ -833,8 +844,8 @@ extern "C" int gafime_allpairs_topk_host(ContiguousBucket bucket, const float* h
         k > GAFIME_ALLPAIRS_MAX_K || n_shards < 1 || shard_id < 0 || shard_id >= n_shards || !out_i || !out_j ||
         !out_score || !out_count)
         return GAFIME_ERROR_INVALID_ARGS;
-    if (metric != GAFIME_METRIC_PEARSON && metric != GAFIME_METRIC_MUTUAL_INFO) return GAFIME_ERROR_INVALID_ARGS;
-    if (metric == GAFIME_METRIC_MUTUAL_INFO && (mi_bins < 2 || mi_bins > 255)) return GAFIME_ERROR_INVALID_ARGS;
+    if (!valid_metric(metric)) return GAFIME_ERROR_INVALID_ARGS;
+    if (metric != GAFIME_METRIC_PEARSON && (mi_bins < 2 || mi_bins > 255)) return GAFIME_ERROR_INVALID_ARGS;
     if (!(div_eps > 0.0f)) return GAFIME_ERROR_INVALID_ARGS;
     for (int o = 0; o < n_ops; ++o)
         if (!valid_op(interact_types[o])) return GAFIME_ERROR_INVALID_ARGS;

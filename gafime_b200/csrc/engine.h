@@ -216,6 +216,12 @@ cudaError_t launch_mi_scores(Bucket& b, const ColumnStats& cs, bool centred, int
                              int mi_bins, const TileCoord* d_tiles, int n_tiles, int k_pad,
                              Cand* cands, double* all_scores, cudaStream_t stream);
 
+// Mutual information with quantile bins on the interaction (mi.cu): exact order-statistic
+// cut points per pair, equal-width y bins; candidate lists / all_scores as launch_mi_scores.
+cudaError_t launch_mi_quantile(Bucket& b, const ColumnStats& cs, bool centred, int op, float div_eps, int mi_bins,
+                               const std::vector<TileCoord>& tiles, const TileCoord* d_tiles, int k_pad,
+                               Cand* cands, double* all_scores, cudaStream_t stream);
+
 // Unary (single-feature) mutual information of every raw column against y
 // (gafime_core.cpp:559-569 with k == 1: the raw column, no centring).
 cudaError_t launch_mi_unary(Bucket& b, int mi_bins, double* d_out, cudaStream_t stream);

@@ -26,6 +26,8 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <cub/device/device_radix_sort.cuh>
+
 #include <algorithm>
 #include <vector>
 
@@ -802,6 +804,273 @@ cudaError_t launch_mi_unary(Bucket& b, int mi_bins, double* d_out, cudaStream_t 
     }
     unary_finish_kernel<<<(unsigned)((b.f + 127) / 128), 128, 0, stream>>>(
         b.f, b.n, mm, hist, yb.counts, yb.map, bins, U, yb.ready, d_out);
+    return cudaGetLastError();
+}
+
+// ---- mutual information with quantile bins on the interaction -------------------------
+//
+// No counterpart in the reference, which bins equal-width only (gafime_core.cpp:200-226).
+// Definition (restated in the oracle, which is the only check of it): the cut points of a
+// pair are the order statistics t_b = sorted[floor(b n / bins)], b = 1 .. bins-1, of its n
+// interaction values x; the bin of x is the number of cut points t_b <= x (ties share a bin,
+// repeated cut points leave bins empty); a constant interaction scores 0.  y is binned
+// equal-width as in the reference, and the MI sum is mi_finish_kernel's.
+// Device plan, per batch of pairs: the interaction of every row as an order-preserving 64-bit
+// key of its fp64 value (-0 made +0, so equal values have equal keys); one exact device
+// radix sort per pair; the cut keys read at the ranks; then one pass over the unsorted keys
+// bins each row by binary search among the cut keys into a joint histogram (shared-memory
+// counters per CTA, added into the pair's histogram), and the MI per pair.
+
+namespace {
+
+constexpr int kQRows = 4096;   // rows per CTA of the binning pass
+
+__device__ __forceinline__ unsigned long long okey(double v) {
+    v = v + 0.0;   // -0 -> +0
+    const unsigned long long u = (unsigned long long)__double_as_longlong(v);
+    return (u >> 63) ? ~u : (u | 0x8000000000000000ull);
+}
+
+struct QArgs {
+    const float* x;            // bucket matrix (raw), ld rows per column
+    int64_t ld, n;
+    const double* colstats;    // mean at [c*4 + 3]
+    const int2* pairs;         // [batch] (i, j)
+    int centred, op;
+    float eps;
+    unsigned long long* keys;  // [batch][n]
+};
+
+template <int OP>
+__device__ __forceinline__ double q_interaction(float a, float b, double ma, double mb, int centred, float eps) {
+    if (centred) return combine_t<OP>((double)a - ma, (double)b - mb, (double)eps);
+    return (double)combine_t<OP>(a, b, eps);
+}
+
+// grid (ceil(n / 256), batch): keys of pair blockIdx.y
+template <int OP>
+__global__ void __launch_bounds__(256) q_keys_kernel(QArgs a) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= a.n) return;
+    const int2 pr = a.pairs[blockIdx.y];
+    const double ma = a.centred ? a.colstats[(int64_t)pr.x * 4 + 3] : 0.0;
+    const double mb = a.centred ? a.colstats[(int64_t)pr.y * 4 + 3] : 0.0;
+    const double v = q_interaction<OP>(a.x[(int64_t)pr.x * a.ld + r], a.x[(int64_t)pr.y * a.ld + r], ma, mb,
+                                       a.centred, a.eps);
+    a.keys[(int64_t)blockIdx.y * a.n + r] = okey(v);
+}
+
+// one thread per (pair, cut): cut keys t_b = sorted[floor(b n / bins)], and whether the pair
+// is constant (sorted[0] == sorted[n - 1]) in cut slot bins - 1
+__global__ void q_cuts_kernel(const unsigned long long* sorted, int64_t n, int bins, int batch,
+                              unsigned long long* cuts) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= batch * bins) return;
+    const int p = t / bins, b = t % bins;
+    const unsigned long long* s = sorted + (int64_t)p * n;
+    if (b == 0)
+        cuts[(int64_t)p * bins + bins - 1] = s[0] == s[n - 1] ? 1ull : 0ull;
+    else
+        cuts[(int64_t)p * bins + b - 1] = s[(int64_t)b * n / bins];
+}
+
+// grid (ceil(n / kQRows), batch): joint histogram [bins][U] of pair blockIdx.y, counts added
+// into hist[p] with integer atomics (order-free)
+__global__ void __launch_bounds__(256) q_hist_kernel(const unsigned long long* keys, int64_t n,
+                                                     const uint8_t* __restrict__ ycode,
+                                                     const unsigned long long* cuts, int bins, int U,
+                                                     unsigned* hist) {
+    extern __shared__ unsigned qsm[];
+    unsigned long long* cut = reinterpret_cast<unsigned long long*>(qsm);   // [bins - 1]
+    unsigned* h = qsm + 2 * bins;                                          // [bins][U]
+    const int p = blockIdx.y;
+    for (int b = threadIdx.x; b < bins - 1; b += blockDim.x) cut[b] = cuts[(int64_t)p * bins + b];
+    for (int c = threadIdx.x; c < bins * U; c += blockDim.x) h[c] = 0;
+    __syncthreads();
+    const unsigned long long* kp = keys + (int64_t)p * n;
+    const int64_t r0 = (int64_t)blockIdx.x * kQRows, r1 = min(r0 + kQRows, n);
+    for (int64_t r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+        const unsigned long long k = kp[r];
+        int lo = 0, hi = bins - 1;   // number of cut keys <= k
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (cut[mid] <= k) lo = mid + 1; else hi = mid;
+        }
+        atomicAdd(&h[lo * U + ycode[r]], 1u);
+    }
+    __syncthreads();
+    unsigned* g = hist + (int64_t)p * bins * U;
+    for (int c = threadIdx.x; c < bins * U; c += blockDim.x)
+        if (h[c]) atomicAdd(&g[c], h[c]);
+}
+
+// one thread per pair: MI in fp64, the summation order of mi_finish_kernel
+__global__ void q_mi_kernel(const unsigned* hist, const unsigned long long* cuts, const unsigned* ycounts,
+                            const int* map, int bins, int U, int ready, int64_t n, int batch, const int64_t* slot,
+                            double* scores) {
+    const int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= batch) return;
+    double py[256];
+    for (int b = 0; b < bins; ++b) {
+        const int c = map[b];
+        if (c != 255) py[c] = (double)ycounts[b];
+    }
+    double mi = 0.0;
+    if (ready && cuts[(int64_t)p * bins + bins - 1] == 0ull) {
+        const double inv_total = 1.0 / (double)n, inv_total_sq = inv_total * inv_total;
+        const unsigned* h = hist + (int64_t)p * bins * U;
+        for (int bx = 0; bx < bins; ++bx) {
+            double px = 0.0;
+            for (int u = 0; u < U; ++u) px += (double)h[bx * U + u];
+            if (px == 0.0) continue;
+            for (int u = 0; u < U; ++u) {
+                const double count = (double)h[bx * U + u];
+                if (count <= 0.0) continue;
+                const double pr = count * inv_total;
+                const double expected = (px * py[u]) * inv_total_sq;
+                if (expected > 0.0) mi += pr * log(pr / expected);
+            }
+        }
+    }
+    scores[slot[p]] = mi;   // the pair's place in the tile layout
+}
+
+// per-tile candidate lists from a dense score array [tile][kTilePairs] (the MI finish's
+// ranking: bitonic top-k of the tile), and every score in triangle order when asked
+__global__ void __launch_bounds__(256) q_lists_kernel(const double* scores, const TileCoord* tiles, int64_t f,
+                                                      int k_pad, Cand* cands, double* all_scores) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    Cand* s = reinterpret_cast<Cand*>(smem_raw);
+    const int t = blockIdx.x;
+    const TileCoord tc = tiles[t];
+    for (int e = threadIdx.x; e < kTilePairs; e += blockDim.x) {
+        const int64_t i = (int64_t)tc.bi * kTile + e / kTile, j = (int64_t)tc.bj * kTile + e % kTile;
+        Cand c;
+        c.pad = 0;
+        if (i < j && j < f) {
+            c.score = scores[(int64_t)t * kTilePairs + e];
+            c.pid = (uint32_t)(i * f + j);
+            if (all_scores) all_scores[i * f - i * (i + 1) / 2 + (j - i - 1)] = c.score;
+        } else {
+            c.score = 0.0;
+            c.pid = kNoPair;
+        }
+        s[e] = c;
+    }
+    if (cands == nullptr) return;
+    __syncthreads();
+    bitonic_sort(s, kTilePairs);
+    Cand* out = cands + (int64_t)t * k_pad;
+    for (int e = threadIdx.x; e < k_pad; e += blockDim.x) out[e] = s[e];
+}
+
+}  // namespace
+
+cudaError_t launch_mi_quantile(Bucket& b, const ColumnStats& cs, bool centred, int op, float div_eps, int mi_bins,
+                               const std::vector<TileCoord>& tiles, const TileCoord* d_tiles, int k_pad,
+                               Cand* cands, double* all_scores, cudaStream_t stream) {
+    const int bins = mi_bins;
+    const int n_tiles = (int)tiles.size();
+    if (n_tiles == 0) return cudaSuccess;
+    YBins yb;
+    cudaError_t e = prepare_ybins(b, bins, yb, stream);
+    if (e != cudaSuccess) return e;
+    const int U = yb.U;
+    if ((size_t)bins * U * sizeof(unsigned) + 2 * (size_t)bins * sizeof(unsigned) > 160 * 1024)
+        return cudaErrorInvalidValue;   // the joint histogram of a CTA must fit in shared memory
+    const int64_t n = b.n, f = b.f;
+    // the pairs of the tiles, in tile-major order (pair q = tile * kTilePairs + e)
+    std::vector<int2> pairs;
+    std::vector<int64_t> slot;
+    for (int t = 0; t < n_tiles; ++t)
+        for (int e2 = 0; e2 < kTilePairs; ++e2) {
+            const int64_t i = (int64_t)tiles[t].bi * kTile + e2 / kTile, j = (int64_t)tiles[t].bj * kTile + e2 % kTile;
+            if (i < j && j < f) {
+                pairs.push_back(make_int2((int)i, (int)j));
+                slot.push_back((int64_t)t * kTilePairs + e2);
+            }
+        }
+    const int64_t P = (int64_t)pairs.size();
+    // pairs per batch: keys (two copies) under ~3 GiB, at most 65535 (grid.y)
+    const int64_t batch = std::max<int64_t>(1, std::min<int64_t>({P, 65535, ((int64_t)3 << 30) / (16 * n)}));
+    size_t temp_bytes = 0;
+    cub::DeviceRadixSort::SortKeys(nullptr, temp_bytes, (const unsigned long long*)nullptr,
+                                   (unsigned long long*)nullptr, (int)n);
+    const size_t off_keys2 = ((size_t)batch * n * 8 + 255) / 256 * 256;
+    const size_t off_temp = off_keys2 + ((size_t)batch * n * 8 + 255) / 256 * 256;
+    const size_t off_cuts = off_temp + (temp_bytes + 255) / 256 * 256;
+    const size_t off_hist = off_cuts + ((size_t)batch * bins * 8 + 255) / 256 * 256;
+    const size_t off_scores = off_hist + ((size_t)batch * bins * U * 4 + 255) / 256 * 256;
+    const size_t off_pairs = off_scores + ((size_t)n_tiles * kTilePairs * 8 + 255) / 256 * 256;
+    const size_t off_slot = off_pairs + ((size_t)P * sizeof(int2) + 255) / 256 * 256;
+    const size_t total = off_slot + (size_t)P * sizeof(int64_t);
+    e = ensure(b.rank, total);
+    if (e != cudaSuccess) return e;
+    char* base = (char*)b.rank.ptr;
+    unsigned long long* keys = (unsigned long long*)base;
+    unsigned long long* keys2 = (unsigned long long*)(base + off_keys2);
+    void* temp = base + off_temp;
+    unsigned long long* cuts = (unsigned long long*)(base + off_cuts);
+    unsigned* hist = (unsigned*)(base + off_hist);
+    double* scores = (double*)(base + off_scores);
+    int2* d_pairs = (int2*)(base + off_pairs);
+    int64_t* d_slot = (int64_t*)(base + off_slot);
+    e = cudaMemcpyAsync(d_pairs, pairs.data(), (size_t)P * sizeof(int2), cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(d_slot, slot.data(), (size_t)P * sizeof(int64_t), cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(scores, 0, (size_t)n_tiles * kTilePairs * 8, stream);
+    if (e != cudaSuccess) return e;
+    const size_t hsmem = (size_t)bins * U * sizeof(unsigned) + 2 * (size_t)bins * sizeof(unsigned);
+    e = cudaFuncSetAttribute(q_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hsmem);
+    if (e != cudaSuccess) return e;
+    for (int64_t p0 = 0; p0 < P; p0 += batch) {
+        const int nb = (int)std::min<int64_t>(batch, P - p0);
+        QArgs qa;
+        qa.x = b.d_data;
+        qa.ld = b.ld;
+        qa.n = n;
+        qa.colstats = cs.d_col;
+        qa.pairs = d_pairs + p0;
+        qa.centred = centred ? 1 : 0;
+        qa.op = op;
+        qa.eps = div_eps;
+        qa.keys = keys;
+        {
+            KernelTimer timer(stream, GAFIME_KERNEL_MI_PASS1);
+            const dim3 grid((unsigned)((n + 255) / 256), (unsigned)nb);
+            switch (op) {
+                case GAFIME_INTERACT_ADD: q_keys_kernel<GAFIME_INTERACT_ADD><<<grid, 256, 0, stream>>>(qa); break;
+                case GAFIME_INTERACT_SUB: q_keys_kernel<GAFIME_INTERACT_SUB><<<grid, 256, 0, stream>>>(qa); break;
+                case GAFIME_INTERACT_DIV: q_keys_kernel<GAFIME_INTERACT_DIV><<<grid, 256, 0, stream>>>(qa); break;
+                default: q_keys_kernel<GAFIME_INTERACT_MULT><<<grid, 256, 0, stream>>>(qa);
+            }
+            e = cudaGetLastError();
+            for (int q = 0; q < nb && e == cudaSuccess; ++q) {
+                size_t tb = temp_bytes;
+                e = cub::DeviceRadixSort::SortKeys(temp, tb, keys + (int64_t)q * n, keys2 + (int64_t)q * n, (int)n, 0,
+                                                   64, stream);
+            }
+        }
+        if (e != cudaSuccess) return e;
+        q_cuts_kernel<<<(unsigned)((nb * bins + 255) / 256), 256, 0, stream>>>(keys2, n, bins, nb, cuts);
+        e = cudaMemsetAsync(hist, 0, (size_t)nb * bins * U * 4, stream);
+        if (e != cudaSuccess) return e;
+        {
+            KernelTimer timer(stream, GAFIME_KERNEL_MI_PASS2);
+            if (yb.ready)
+                q_hist_kernel<<<dim3((unsigned)((n + kQRows - 1) / kQRows), (unsigned)nb), 256, hsmem, stream>>>(
+                    keys, n, yb.ycode, cuts, bins, U, hist);
+        }
+        q_mi_kernel<<<(unsigned)((nb + 127) / 128), 128, 0, stream>>>(hist, cuts, yb.counts, yb.map, bins, U,
+                                                                      yb.ready, n, nb, d_slot + p0, scores);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    const size_t lsmem = sizeof(Cand) * kTilePairs;
+    e = cudaFuncSetAttribute(q_lists_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lsmem);
+    if (e != cudaSuccess) return e;
+    KernelTimer timer(stream, GAFIME_KERNEL_MI_FINISH);
+    q_lists_kernel<<<n_tiles, 256, lsmem, stream>>>(scores, d_tiles, f, k_pad, cands, all_scores);
     return cudaGetLastError();
 }
 

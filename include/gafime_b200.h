@@ -66,6 +66,13 @@ extern "C" {
 /* NEW: metric ids, same numbering as gafime_core's MetricId (gafime_core.cpp:28-33) */
 #define GAFIME_METRIC_PEARSON 0
 #define GAFIME_METRIC_MUTUAL_INFO 2
+/* NEW -- no counterpart in the reference (its bins are equal-width only).  Mutual information
+ * with QUANTILE bins on the interaction: the cut points of a pair are the order statistics
+ * sorted[floor(b n / mi_bins)], b = 1 .. mi_bins-1, of its n values, a value's bin is the
+ * number of cut points <= it; y is binned equal-width as for GAFIME_METRIC_MUTUAL_INFO.
+ * Exact (one device sort per pair), so much slower than the equal-width mode.  Accepted by
+ * gafime_allpairs_topk / _topk_host / _topk_device / _scores wherever a metric is. */
+#define GAFIME_METRIC_MUTUAL_INFO_QUANTILE 12
 
 /* NEW: largest k the all-pairs top-k returns per operator */
 #define GAFIME_ALLPAIRS_MAX_K 4096

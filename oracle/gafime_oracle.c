@@ -43,6 +43,10 @@
  *     features are all invalid) yields 1.  cpu_backend.cpp:316-370 agrees on every combo
  *     whose features are valid (it writes 0 for the degenerate ones).
  *
+ *  7. Mutual information with quantile bins on the interaction (a mode this build adds; the
+ *     reference has equal-width bins only, so it is parity unpinned): order-statistic cut
+ *     points, equal-width y bins, the reference's MI sum.
+ *
  *  6. Mutual information of any operator (raw fp32 or centred fp64 interaction) and of raw
  *     columns, and Spearman rank correlation (rankdata with average ties and the Pearson of
  *     ranks, gafime_core.cpp:156-177,503-517,595-607), for unaries and pairs.
@@ -203,6 +207,116 @@ static double or_mutual_info(const double* x, int64_t n, int bins, const int32_t
         }
     }
     return mi;
+}
+
+static int or_cmp_double(const void* a, const void* b) {
+    const double x = *(const double*)a, y = *(const double*)b;
+    return x < y ? -1 : (x > y ? 1 : 0);
+}
+
+/* Mutual information with QUANTILE bins on the interaction (no counterpart in the
+ * reference, which bins equal-width only: gafime_core.cpp:200-226).  Definition used by
+ * this build: sort the n values; the cut points are the order statistics
+ * t_b = sorted[floor(b n / bins)] for b = 1 .. bins-1; the bin of x is the number of cut
+ * points t_b <= x (ties share a bin, repeated cut points leave bins empty); a constant
+ * interaction scores 0.  The y bins and the MI sum (natural log, bx-major, then by) are
+ * those of mutual_info_from_vector (gafime_core.cpp:267-333). */
+static double or_mutual_info_quantile(const double* x, int64_t n, int bins, const int32_t* y_bins,
+                                      double* sorted, double* cuts, double* joint, double* p_x,
+                                      double* p_y) {
+    if (bins < 2 || n == 0) return 0.0;
+    memcpy(sorted, x, (size_t)n * sizeof(double));
+    qsort(sorted, (size_t)n, sizeof(double), or_cmp_double);
+    if (sorted[0] == sorted[n - 1]) return 0.0;
+    for (int b = 1; b < bins; ++b) cuts[b - 1] = sorted[(int64_t)b * n / bins];
+    size_t b2 = (size_t)bins * (size_t)bins;
+    memset(joint, 0, b2 * sizeof(double));
+    memset(p_x, 0, (size_t)bins * sizeof(double));
+    memset(p_y, 0, (size_t)bins * sizeof(double));
+    for (int64_t i = 0; i < n; ++i) {
+        /* number of cut points <= x[i] (upper bound in the sorted cuts) */
+        int lo = 0, hi = bins - 1;
+        while (lo < hi) {
+            int mid = (lo + hi) / 2;
+            if (cuts[mid] <= x[i]) lo = mid + 1; else hi = mid;
+        }
+        const int xb = lo, yb = y_bins[i];
+        joint[(size_t)xb * bins + yb] += 1.0;
+        p_x[xb] += 1.0;
+        p_y[yb] += 1.0;
+    }
+    double inv_total = 1.0 / (double)n;
+    double inv_total_sq = inv_total * inv_total;
+    double mi = 0.0;
+    for (int bx = 0; bx < bins; ++bx) {
+        for (int by = 0; by < bins; ++by) {
+            double count = joint[(size_t)bx * bins + by];
+            if (count <= 0.0) continue;
+            double p = count * inv_total;
+            double expected = (p_x[bx] * p_y[by]) * inv_total_sq;
+            if (expected > 0.0) mi += p * log(p / expected);
+        }
+    }
+    return mi;
+}
+
+/* Quantile-bin mutual information of x = X[:,i] op X[:,j] (centred in fp64 when center is
+ * set, else the fp32 kernel-API interaction) against equal-width y bins, per pair. */
+int gafime_oracle_pair_mi_quantile(const float* X, int64_t ld, const float* y, int64_t n, int64_t f_count,
+                                   const int32_t* pi, const int32_t* pj, int64_t n_pairs, int op, float eps,
+                                   int center, int mi_bins, double* out_mi) {
+    double* means = (double*)malloc((size_t)(f_count > 0 ? f_count : 1) * sizeof(double));
+    double* yd = (double*)malloc((size_t)(n > 0 ? n : 1) * sizeof(double));
+    int32_t* y_bins = (int32_t*)malloc((size_t)(n > 0 ? n : 1) * sizeof(int32_t));
+    if (!means || !yd || !y_bins) {
+        free(means); free(yd); free(y_bins);
+        return -3;
+    }
+    if (center) gafime_oracle_column_means(X, ld, n, f_count, means);
+    for (int64_t r = 0; r < n; ++r) yd[r] = (double)y[r];
+    const int ready = or_build_bins(yd, n, mi_bins, y_bins);
+    int status = 0;
+#pragma omp parallel
+    {
+        double* inter = (double*)malloc((size_t)(n > 0 ? n : 1) * sizeof(double));
+        double* sorted = (double*)malloc((size_t)(n > 0 ? n : 1) * sizeof(double));
+        size_t nb = mi_bins >= 2 ? (size_t)mi_bins : 2;
+        double* joint = (double*)malloc(nb * nb * sizeof(double));
+        double* p_x = (double*)malloc(nb * sizeof(double));
+        double* p_y = (double*)malloc(nb * sizeof(double));
+        double* cuts = (double*)malloc(nb * sizeof(double));
+        if (!inter || !sorted || !joint || !p_x || !p_y || !cuts) {
+#pragma omp atomic write
+            status = -3;
+        } else {
+#pragma omp for schedule(dynamic, 8)
+            for (int64_t p = 0; p < n_pairs; ++p) {
+                const float* ca = X + (int64_t)pi[p] * ld;
+                const float* cb = X + (int64_t)pj[p] * ld;
+                for (int64_t r = 0; r < n; ++r) {
+                    if (center) {
+                        double a = (double)ca[r] - means[pi[p]], b = (double)cb[r] - means[pj[p]];
+                        double v;
+                        switch (op) {
+                            case OR_ADD: v = a + b; break;
+                            case OR_SUB: v = a - b; break;
+                            case OR_DIV: v = a / (fabs(b) < (double)eps ? copysign((double)eps, b) : b); break;
+                            default: v = a * b;
+                        }
+                        inter[r] = v;
+                    } else {
+                        inter[r] = (double)or_combine(ca[r], cb[r], op, eps);
+                    }
+                }
+                out_mi[p] = ready ? or_mutual_info_quantile(inter, n, mi_bins, y_bins, sorted, cuts, joint, p_x,
+                                                            p_y)
+                                  : 0.0;
+            }
+        }
+        free(inter); free(sorted); free(joint); free(p_x); free(p_y); free(cuts);
+    }
+    free(means); free(yd); free(y_bins);
+    return status;
 }
 
 /* Centred-product scores for pairs (i, j) as gafime_core.score_combos computes

@@ -63,6 +63,10 @@ def lib() -> ctypes.CDLL:
             _f32p, ctypes.c_int64, _f32p, ctypes.c_int64, ctypes.c_int64, _i32p, _i32p,
             ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int, _f64p]
         _LIB.gafime_oracle_pair_mi.restype = ctypes.c_int
+        _LIB.gafime_oracle_pair_mi_quantile.argtypes = [
+            _f32p, ctypes.c_int64, _f32p, ctypes.c_int64, ctypes.c_int64, _i32p, _i32p,
+            ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int, _f64p]
+        _LIB.gafime_oracle_pair_mi_quantile.restype = ctypes.c_int
         _LIB.gafime_oracle_unary_mi.argtypes = [
             _f32p, ctypes.c_int64, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, _f64p]
         _LIB.gafime_oracle_unary_mi.restype = ctypes.c_int
@@ -186,6 +190,25 @@ def pair_mi(X: np.ndarray, y: np.ndarray, op: str = "multiply", center: bool = T
     out = np.empty(len(pi), dtype=np.float64)
     rc = lib().gafime_oracle_pair_mi(flat, ld, yv, n, f, pi, pj, len(pi), OP_IDS[op],
                                      np.float32(div_eps), int(center), int(mi_bins), out)
+    if rc != 0:
+        raise MemoryError("oracle allocation failed")
+    return out
+
+
+def pair_mi_quantile(X: np.ndarray, y: np.ndarray, op: str = "multiply", center: bool = True,
+                     mi_bins: int = 16, div_eps: float = 1e-8, pi=None, pj=None) -> np.ndarray:
+    """Mutual information with quantile bins on the interaction (order-statistic cut points
+    sorted[floor(b n / bins)], bin = number of cut points <= x) against equal-width y bins.
+    The reference has no quantile mode: this restatement is the definition, unpinned."""
+    flat, ld, n, f = _colmajor(X)
+    if pi is None:
+        pi, pj = all_pairs(f)
+    pi = np.ascontiguousarray(pi, dtype=np.int32)
+    pj = np.ascontiguousarray(pj, dtype=np.int32)
+    yv = np.ascontiguousarray(y, dtype=np.float32)
+    out = np.empty(len(pi), dtype=np.float64)
+    rc = lib().gafime_oracle_pair_mi_quantile(flat, ld, yv, n, f, pi, pj, len(pi), OP_IDS[op],
+                                              np.float32(div_eps), int(center), int(mi_bins), out)
     if rc != 0:
         raise MemoryError("oracle allocation failed")
     return out

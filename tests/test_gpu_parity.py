@@ -748,3 +748,28 @@ def test_wide_table_matches_the_oracle_and_streams_identically(native, oracle):
     for op in ("multiply", "divide"):
         for u, v in zip(got[op], want[op]):
             np.testing.assert_array_equal(u, v)
+
+
+@pytest.mark.parametrize("op,center", [("multiply", True), ("add", False), ("divide", False)])
+def test_quantile_mi_matches_the_oracle(native, oracle, op, center):
+    """Mutual information with quantile bins on the interaction (a mode the reference does not
+    have; the oracle's restatement is its definition): every pair's score at 1e-5 absolute
+    and the top-k set, on a table with a planted product, tied integer codes (repeated cut
+    points), a constant column (a constant interaction for multiply) and a 3-class target."""
+    rng = np.random.default_rng(31)
+    n, f, k = 20_000, 24, 20
+    X = rng.standard_normal((n, f)).astype(np.float32)
+    X[:, 6:10] = rng.integers(0, 4, (n, 4)).astype(np.float32)
+    X[:, 11] = 0.0
+    s0 = X[:, 2].astype(np.float64) * X[:, 5] + 0.5 * rng.standard_normal(n)
+    y = np.argmax(np.stack([s0, X[:, 3] + 0.5 * rng.standard_normal(n), rng.standard_normal(n)]), axis=0)
+    y = y.astype(np.float32)
+    pi, pj = np.triu_indices(f, k=1)
+    want = oracle.pair_mi_quantile(X, y, op, center=center, mi_bins=32, div_eps=1e-6)
+    with bucket_for(native, X, y) as b:
+        got = b.scores(op, metric="mutual_info_quantile", center=center, mi_bins=32, div_eps=1e-6)
+        gi, gj, gs = b.topk([op], k, metric="mutual_info_quantile", center=center, mi_bins=32, div_eps=1e-6)[op]
+    np.testing.assert_allclose(got, want, rtol=0, atol=1e-5)
+    assert_topk_equivalent(gi, gj, want, pi, pj, k, rtol=0, atol=1e-5)
+    if op == "multiply":
+        assert (int(gi[0]), int(gj[0])) == (2, 5)
