@@ -1,7 +1,7 @@
 /*
  * gafime_oracle.c -- CPU restatement of GAFIME's pair-scoring arithmetic.
  *
- * TEST INFRASTRUCTURE ONLY.  This file is the checker for the CUDA path: only
+ * TEST INFRASTRUCTURE ONLY.  This file is the oracle for the CUDA path: only
  * tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg may load it.
  * The product (gafime_b200/) never calls it and has no CPU fallback.
  *
@@ -43,7 +43,7 @@
  *     features are all invalid) yields 1.  cpu_backend.cpp:316-370 agrees on every combo
  *     whose features are valid (it writes 0 for the degenerate ones).
  *
- *  7. Mutual information with quantile bins on the interaction (a mode this build adds; the
+ *  7. Mutual information with quantile bins on the interaction (a mode this library adds; the
  *     reference has equal-width bins only, so it is parity unpinned): order-statistic cut
  *     points, equal-width y bins, the reference's MI sum.
  *
@@ -216,7 +216,7 @@ static int or_cmp_double(const void* a, const void* b) {
 
 /* Mutual information with QUANTILE bins on the interaction (no counterpart in the
  * reference, which bins equal-width only: gafime_core.cpp:200-226).  Definition used by
- * this build: sort the n values; the cut points are the order statistics
+ * this library: sort the n values; the cut points are the order statistics
  * t_b = sorted[floor(b n / bins)] for b = 1 .. bins-1; the bin of x is the number of cut
  * points t_b <= x (ties share a bin, repeated cut points leave bins empty); a constant
  * interaction scores 0.  The y bins and the MI sum (natural log, bx-major, then by) are

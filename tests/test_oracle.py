@@ -3,7 +3,7 @@
 The fixtures come from tests/golden/make_golden.py (gafime_core.score_combos,
 GafimeSelector.fit, the reference numpy metrics and cpu_backend.cpp compiled
 unmodified).  If the oracle disagrees with them it cannot be trusted as the
-checker of the CUDA path.
+oracle of the CUDA path.
 """
 import numpy as np
 import pytest
