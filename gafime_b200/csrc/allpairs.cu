@@ -129,6 +129,67 @@ static std::vector<TileCoord> compute_shard_tiles(int64_t f, int shard_id, int n
             if (!swapped) break;
         }
     }
+    // Grouped alternative: split the 128-column blocks into g contiguous groups; a unit is
+    // every block of one group pair (Ga, Gb), a <= b, so a shard owning units of few groups
+    // reads few column blocks (at 2048 columns over 8 shards, g = 4 gives each shard one
+    // cross-group unit or two in-group units: 8 of 16 blocks, against up to 16 above).
+    // Units in decreasing pair count go to the least-loaded shard (ties: lowest id).  Taken
+    // when its busiest shard has no more pairs than the assignment above (0.5 % slack) and
+    // reads fewer column blocks; every process derives the same choice.
+    if (n_shards > 1) {
+        auto stats = [&](const std::vector<int>& own, int64_t* max_load, int* max_reads) {
+            std::vector<int64_t> ld((size_t)n_shards, 0);
+            std::vector<std::vector<char>> rd((size_t)n_shards, std::vector<char>((size_t)nb2, 0));
+            for (size_t x = 0; x < blocks.size(); ++x) {
+                ld[(size_t)own[x]] += blocks[x].w;
+                rd[(size_t)own[x]][(size_t)blocks[x].BI] = rd[(size_t)own[x]][(size_t)blocks[x].BJ] = 1;
+            }
+            *max_load = 0;
+            *max_reads = 0;
+            for (int sh = 0; sh < n_shards; ++sh) {
+                *max_load = std::max(*max_load, ld[(size_t)sh]);
+                int r = 0;
+                for (char c : rd[(size_t)sh]) r += c;
+                *max_reads = std::max(*max_reads, r);
+            }
+        };
+        int64_t best_load = 0;
+        int best_reads = 0;
+        stats(owner, &best_load, &best_reads);
+        for (int g = 2; g <= nb2; ++g) {
+            if ((int64_t)g * (g + 1) / 2 < n_shards) continue;
+            std::vector<int> grp((size_t)nb2);
+            for (int B = 0; B < nb2; ++B) grp[(size_t)B] = (int)((int64_t)B * g / nb2);
+            const int units = g * (g + 1) / 2;
+            std::vector<int64_t> uw((size_t)units, 0);
+            auto uid = [&](int ga, int gb) { return ga * g - ga * (ga - 1) / 2 + (gb - ga); };
+            for (const Block& blk : blocks) uw[(size_t)uid(grp[(size_t)blk.BI], grp[(size_t)blk.BJ])] += blk.w;
+            std::vector<int> order((size_t)units);
+            for (int u = 0; u < units; ++u) order[(size_t)u] = u;
+            std::stable_sort(order.begin(), order.end(),
+                             [&](int x, int y) { return uw[(size_t)x] > uw[(size_t)y]; });
+            std::vector<int64_t> sl((size_t)n_shards, 0);
+            std::vector<int> uown((size_t)units, 0);
+            for (int u : order) {
+                int bs = 0;
+                for (int sh = 1; sh < n_shards; ++sh)
+                    if (sl[(size_t)sh] < sl[(size_t)bs]) bs = sh;
+                sl[(size_t)bs] += uw[(size_t)u];
+                uown[(size_t)u] = bs;
+            }
+            std::vector<int> own(blocks.size());
+            for (size_t x = 0; x < blocks.size(); ++x)
+                own[x] = uown[(size_t)uid(grp[(size_t)blocks[x].BI], grp[(size_t)blocks[x].BJ])];
+            int64_t ml = 0;
+            int mr = 0;
+            stats(own, &ml, &mr);
+            if ((double)ml <= 1.005 * (double)best_load && mr < best_reads) {
+                owner = own;
+                best_load = std::max(best_load, ml);
+                best_reads = mr;
+            }
+        }
+    }
     std::vector<TileCoord> mine;
     for (size_t x = 0; x < blocks.size(); ++x)
         if (owner[x] == shard_id)

@@ -89,12 +89,30 @@ def test_shards_read_few_column_blocks():
     """Blocks of equal pair count trade shards toward fewer 128-column blocks per shard
     (each shard's statistics pass covers the blocks it reads); the loads are unchanged."""
     from gafime_b200 import _native
-    for f, world, most in ((724, 8, 3), (512, 4, 3), (362, 2, 3)):
+    for f, world, most in ((724, 8, 3), (512, 4, 3), (362, 2, 3), (2048, 8, 8), (2048, 4, 12)):
         reads = []
         for r in range(world):
             t = _native.shard_tiles(f, r, world)
             reads.append(len({int(x) // 2 for x in np.asarray(t).reshape(-1)}))
         assert max(reads) <= most, reads
+
+
+def test_grouped_assignment_balances_the_wide_table():
+    """At 2048 columns the pair space goes out in group-pair units: over 8 shards each holds
+    one cross-group unit or two in-group units (8 of 16 column blocks), within 0.1 % of the
+    mean pair count; over 4 shards 12 blocks each."""
+    from gafime_b200 import _native
+    f = 2048
+    total = f * (f - 1) // 2
+    for world, blocks in ((8, 8), (4, 12)):
+        loads = []
+        for r in range(world):
+            pi, pj = _native.shard_pairs(f, r, world)
+            loads.append(len(pi))
+            t = _native.shard_tiles(f, r, world)
+            assert len({int(x) // 2 for x in np.asarray(t).reshape(-1)}) == blocks
+        assert sum(loads) == total
+        assert max(loads) <= 1.001 * total / world
 
 
 def test_shard_assignment_is_cheap_for_wide_matrices():
