@@ -610,6 +610,15 @@ def run_ours(args):
             same = all(np.array_equal(u, v) for op in ops for u, v in zip(result[op], single[op]))
             multi_check = "merged top-k of %d ranks %s the single-GPU top-k" % (world, "equals" if same else
                                                                                  "DIFFERS FROM")
+            if not same:
+                # what differs: pairs out of place, largest score gap position by position
+                diff = []
+                for op in ops:
+                    (ri, rj, rs), (si, sj, ss) = result[op], single[op]
+                    moved = int(np.sum((ri != si) | (rj != sj)))
+                    gap = float(np.max(np.abs(rs - ss))) if len(rs) == len(ss) and len(rs) else float("nan")
+                    diff.append("%s: %d pairs moved, max |score gap| %.3g" % (op, moved, gap))
+                multi_check += " (" + "; ".join(diff) + ")"
         dist.barrier()
 
     # e2e: the same step through the C ABI from pinned host buffers, upload included

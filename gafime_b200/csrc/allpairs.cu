@@ -225,8 +225,11 @@ struct Plan {
 Plan make_plan(const Bucket& b, int shard_id, int n_shards) {
     Plan p;
     p.tiles = shard_tiles(b.f, shard_id, n_shards);
-    int nt = (int)p.tiles.size();
-    int splits = nt > 0 ? std::max(1, b.sm_count / nt) : 1;
+    // row splits from the whole matrix's tile count (not this shard's), so a pair's partial
+    // sums cover the same rows on every shard count
+    const int64_t nb = (b.f + kTile - 1) / kTile;
+    const int64_t all_tiles = std::max<int64_t>(1, nb * (nb + 1) / 2);
+    int splits = (int)std::max<int64_t>(1, b.sm_count / all_tiles);
     // at least 1024 rows per split
     int64_t max_splits = std::max<int64_t>(1, b.ld / 1024);
     if (splits > max_splits) splits = (int)max_splits;
@@ -793,9 +796,9 @@ int streamed_topk_body(Bucket& b, const float* h_data, const uint8_t* h_mask, co
         bool finite = true;
         return check_finite(b, &finite);
     }
-    // the row chunks and the Gram kernel the whole tile set would get (same partial sums as an
-    // unstreamed call)
-    const int64_t chunk = gram_chunk_rows(b, gram_tiles128(plan.tiles));
+    // the row chunks of the matrix and the Gram kernel the whole tile set would get (same
+    // partial sums as an unstreamed call)
+    const int64_t chunk = gram_chunk_rows(b);
     const int planes = gram_use_planes(b, plan.tiles) ? 1 : 0;
     TileCoord* d_tiles = nullptr;
     int st = upload_tiles(b, plan, &d_tiles);

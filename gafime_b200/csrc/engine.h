@@ -118,9 +118,8 @@ bool gram_path_enabled(const Bucket& b);
 cudaError_t gram_prep_target(Bucket& b, const ColumnStats& cs, cudaStream_t stream);
 cudaError_t gram_prep_columns(Bucket& b, const ColumnStats& cs, bool recip, float eps, int64_t c0, int64_t c1,
                               cudaStream_t stream);
-// chunk_rows > 0 fixes the row chunk of the tiles (a streamed call launches its tiles in
-// several sets and keeps the chunking the whole set would get: gram_chunk_rows of the
-// whole set's 128-tile count, gram_tiles128).
+// chunk_rows > 0 fixes the row chunk of the tiles; 0 takes gram_chunk_rows, which depends
+// on the matrix alone (every shard and every streamed tile set gets the same chunks).
 // use_planes: 1 the B-planes kernel, 0 the fused kernel, -1 chosen from this tile set
 // (gram_use_planes); a streamed call decides once for its whole tile set.
 cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoord* d_tiles64,
@@ -130,12 +129,11 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
 // True when a tile set reuses its B blocks enough for the B-planes kernel (or when
 // GAFIME_GRAM_KERNEL forces it).
 bool gram_use_planes(const Bucket& b, const std::vector<TileCoord>& tiles64);
-int64_t gram_chunk_rows(const Bucket& b, int ctas_per_chunk);
+int64_t gram_chunk_rows(const Bucket& b);
 // host_err null: launch_gram_moments neither clears nor reads the Gram kernels' error flag
 // (no host sync); the caller clears it before its launches and reads it once at the end.
 cudaError_t gram_error_reset(Bucket& b, cudaStream_t stream);
 cudaError_t gram_error_read(Bucket& b, cudaStream_t stream, int* host_err);
-int gram_tiles128(const std::vector<TileCoord>& tiles64);
 // Per-column state of the Gram path (12 doubles per column; [6] sum g, [7] sum g^2 of the
 // divide side g = 1/safe(x)), valid after gram_prep_columns of this call.
 const double* gram_col_state(Bucket& b);

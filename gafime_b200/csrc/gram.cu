@@ -1504,20 +1504,18 @@ cudaError_t gram_prep_columns(Bucket& b, const ColumnStats& cs, bool recip, floa
     return cudaGetLastError();
 }
 
-int64_t gram_chunk_rows(const Bucket& b, int ctas_per_chunk) {
-    // row chunks: <= max_chunk_rows() rows, enough CTAs for every SM
+int64_t gram_chunk_rows(const Bucket& b) {
+    // row chunks: <= max_chunk_rows() rows, about four CTAs per SM over the whole matrix's
+    // 128-tiles.  The chunk follows from the matrix alone, never from the tiles of one shard
+    // or one streamed set, so every pair's fp32 partial sums cover the same rows whichever
+    // shard scores it: a sharded top-k is bit-identical to the single-GPU one.
     const int64_t ld = b.ld;
-    const int64_t want = std::max<int64_t>(1, (4 * (int64_t)b.sm_count + ctas_per_chunk - 1) / std::max(1, ctas_per_chunk));
+    const int64_t nb128 = (b.f + kGT - 1) / kGT;
+    const int64_t all_tiles = std::max<int64_t>(1, nb128 * (nb128 + 1) / 2);
+    const int64_t want = std::max<int64_t>(1, (4 * (int64_t)b.sm_count + all_tiles - 1) / all_tiles);
     int64_t chunk = (ld + want - 1) / want;
     chunk = std::min<int64_t>(max_chunk_rows(), std::max<int64_t>(1024, chunk));
     return (chunk + kRowPad - 1) / kRowPad * kRowPad;
-}
-
-int gram_tiles128(const std::vector<TileCoord>& tiles64) {
-    std::vector<std::pair<int, int>> t;
-    for (const TileCoord& c : tiles64) t.push_back({c.bi >> 1, c.bj >> 1});
-    std::sort(t.begin(), t.end());
-    return (int)(std::unique(t.begin(), t.end()) - t.begin());
 }
 
 bool gram_use_planes(const Bucket& b, const std::vector<TileCoord>& tiles64) {
@@ -1560,7 +1558,7 @@ cudaError_t launch_gram_moments(Bucket& b, const ColumnStats& cs, const TileCoor
     const int nt = (int)t128.size();
     if (nt == 0) return cudaSuccess;
     const bool planes = use_planes < 0 ? gram_use_planes(b, tiles64) : use_planes != 0;
-    const int64_t chunk = chunk_rows > 0 ? chunk_rows : gram_chunk_rows(b, nt);
+    const int64_t chunk = chunk_rows > 0 ? chunk_rows : gram_chunk_rows(b);
     const int n_chunks = (int)((ld + chunk - 1) / chunk);
 
     // scratch of this tile set: partial | lut | tiles128; the per-column state (scales, scaled

@@ -252,6 +252,33 @@ def test_device_lists_merge_to_the_single_process_topk(native):
                     np.testing.assert_array_equal(u, v)
 
 
+def test_shards_sum_the_same_row_chunks_as_one_gpu(native):
+    """Bit-identity of a sharded top-k on a table whose row chunking would change with the
+    number of tiles a shard holds (200,000 rows, 300 columns: 6 tensor-core tiles, chunks
+    well under the 8192-row cap).  The chunks follow from the matrix alone, so every shard
+    count gives the single-GPU scores bit for bit."""
+    import torch
+    rng = np.random.default_rng(21)
+    X = rng.standard_normal((200_000, 300)).astype(np.float32)
+    y = (X[:, 3] * X[:, 200] + rng.standard_normal(200_000)).astype(np.float32)
+    ops, k = ["multiply", "add", "divide"], 40
+    L = native.list_len(k)
+    with bucket_for(native, X, y) as b:
+        full = b.topk(ops, k, div_eps=1e-6)
+        assert (int(full["multiply"][0][0]), int(full["multiply"][1][0])) == (3, 200)
+        for n_shards in (2, 3):
+            gathered = torch.zeros(n_shards * len(ops) * L * 2, dtype=torch.int64, device="cuda")
+            for s in range(n_shards):
+                part = gathered[s * len(ops) * L * 2:(s + 1) * len(ops) * L * 2]
+                torch.cuda.synchronize()
+                b.topk_device(ops, k, part.data_ptr(), div_eps=1e-6, shard_id=s, n_shards=n_shards)
+            torch.cuda.synchronize()
+            got = b.merge_device(gathered.data_ptr(), n_shards, ops, k)
+            for op in ops:
+                for u, v in zip(got[op], full[op]):
+                    np.testing.assert_array_equal(u, v)
+
+
 def test_non_finite_input_is_rejected(native):
     X = np.ones((100, 4), dtype=np.float32)
     X[5, 2] = np.nan
