@@ -21,15 +21,19 @@
 // warps:
 //   warp 0      TMA: raw fp32 column tiles (128 columns x 16 rows, 64-byte swizzle, no
 //               multicast) of the A block and, off the diagonal, the B block, plus 16 scaled
-//               ycen values (plain bulk copy) -> 6-stage raw ring
-//   warp 1      TMEM allocation; one thread issues the six MMAs of each step (A operands
-//               from tensor memory, B operands from shared memory) and commits the operand
-//               stage back to its "empty" barrier
+//               ycen values (plain bulk copy) -> 8-stage raw ring
+//   warp 1      TMEM allocation; one thread waits for a super-step (two consecutive steps'
+//               operands), issues their twelve MMAs (A operands from tensor memory, B
+//               operands from shared memory) and commits the pair of operand stages back
+//               to its "empty" barrier
 //   warps 2-17  two converter groups of 8 warps, taking alternate steps; one column of each
 //               block and one 8-row K half per thread, in the TMEM lane quarter of its
 //               warp: centre, scale and split the values, write the four A rows to tensor
 //               memory (tcgen05.st) and the six B rows to K-major fp16 tiles (32-byte
-//               swizzle) in shared memory, 4-stage operand ring.  Diagonal tiles of the
+//               swizzle) in shared memory, 4-stage operand ring handed out in pairs.  The
+//               MMA thread shares its SM sub-partition with four converter warps, so its
+//               loop is issue-bound: one wait and commit per step (instead of per pair)
+//               kept the tensor pipe ~40 % idle.  Diagonal tiles of the
 //               multiply group load and convert one block only.  After the last step group 0
 //               drains TMEM (tcgen05.ld) into fp32 chunk partials.
 // Keeping A in tensor memory halves the shared-memory reads of the MMAs (shared-memory
@@ -67,7 +71,7 @@ namespace {
 
 constexpr int kGT = 128;                      // Gram tile edge (columns)
 constexpr int kGK = 16;                       // rows per step (one MMA K step)
-constexpr int kRawStages = 6;
+constexpr int kRawStages = 8;
 constexpr int kOpStages = 4;                  // A operands in TMEM + B operands in shared memory
 constexpr int kRawBox = kGT * kGK * 4;        // one fp32 column tile: 128 columns x 16 rows
 constexpr int kRawStageBytes = 2 * kRawBox;   // A block + B block
@@ -83,6 +87,13 @@ constexpr uint32_t kTmemAStride = 32;         // XH XL QH QL: 8 columns each
 constexpr int kConvWarps = 8;                 // warps per converter group (column x K half per thread)
 constexpr int kGroups = 2;                    // converter groups, interleaved over the steps
 constexpr int kGramThreads = (2 + kGroups * kConvWarps) * 32;
+// Super-steps: the operand ring hands out pairs of consecutive steps (step 2j from converter
+// group 0, step 2j + 1 from group 1), so the MMA thread waits, and commits, once per twelve
+// MMAs.  Its per-step loop competes for issue slots with the converter warps of its SM
+// sub-partition; one wait and commit per step cost about 40 % of the tensor pipe's time.
+constexpr int kSuper = 2;                     // steps per super-stage
+constexpr int kSuperStages = kOpStages / kSuper;
+static_assert(kSuper == kGroups && kOpStages % kSuper == 0, "a super-step is one step of each converter group");
 constexpr uint32_t kTmemCols = 512;
 constexpr long long kSpinLimit = 1LL << 24;
 constexpr uint32_t kSuspendNs = 20000;           // try_wait suspend-time hint
@@ -275,6 +286,16 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int* er
     return ok != 0;
 }
 
+// The same with lane 0 polling (test_wait) instead of suspending: the fused kernel's
+// converters sit on the chain MMA completion -> operand stores -> next MMAs, where a
+// suspended thread's wake-up latency costs tensor-pipe time.
+__device__ __forceinline__ bool warp_wait_poll(uint32_t bar, uint32_t parity, int* err, int code, int lane) {
+    int ok = 1;
+    if (lane == 0) ok = mbar_wait_spin(bar, parity, err, code) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    return ok != 0;
+}
+
 // 8 consecutive rows (one K half) of one column as hi and lo fp16 pairs
 struct Split8 {
     uint32_t hi[4], lo[4];
@@ -440,12 +461,16 @@ struct ConvCtx {
 };
 
 // The steps k = grp, grp + kGroups, ... of one converter thread.  kB: convert the B block
-// (off the multiply group's diagonal); kRecip: the B operand is 1/safe(b).
+// (off the multiply group's diagonal); kRecip: the B operand is 1/safe(b).  Step k belongs to
+// super-step k / kSuper, whose stage pair ss = (k / kSuper) % kSuperStages holds operand
+// stages 2 ss and 2 ss + 1 (= k % kOpStages).  Every warp of both groups waits on every
+// phase of each super-stage's "empty" barrier, in order, so its parity waits are sound.
 template <bool kB, bool kRecip>
 __device__ __forceinline__ void conv_loop(const ConvCtx& c, const ConvCols& kc, int grp) {
     for (int k = grp; k < c.nk; k += kGroups) {
         const int rs = k % kRawStages, os = k % kOpStages;
-        if (!warp_wait(c.rfull0 + 8 * rs, (k / kRawStages) & 1, c.err, 5, c.lane)) return;
+        const int j = k / kSuper, ss = j % kSuperStages;
+        if (!warp_wait_poll(c.rfull0 + 8 * rs, (k / kRawStages) & 1, c.err, 5, c.lane)) return;
         const unsigned char* raw = c.raw0 + rs * kRawStageBytes;
         const unsigned char* ysm = c.ys0 + rs * kYsBytes;
         StepOps o;
@@ -456,8 +481,25 @@ __device__ __forceinline__ void conv_loop(const ConvCtx& c, const ConvCols& kc, 
             const int valid = left <= 0 ? 0 : (int)left;   // < kGK here
             convert_step<true, kB, kRecip>(raw, ysm, c.m, c.h, valid, kc, c.eps, o, c.b_off);
         }
-        // the operand stage must be free: the MMAs of step k - kOpStages have completed
-        if (k >= kOpStages && !warp_wait(c.oempty0 + 8 * os, ((k / kOpStages) - 1) & 1, c.err, 6, c.lane)) return;
+        {
+            // Every value read from the raw stage is now in registers: hand the stage back to
+            // the producer before waiting for an operand stage, so the raw ring keeps
+            // prefetching while the MMAs drain.  `dep` is computed from every converted word
+            // (each depends on the loads of its rows), so no lane reaches the warp barrier,
+            // and lane 0 no release, before that lane's shared-memory loads have returned.
+            uint32_t dep = 0;
+            #pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                dep ^= o.x.hi[p] ^ o.q.hi[p] ^ o.wb.hi[p];
+                if (kB) dep ^= o.b.hi[p] ^ o.bq.hi[p];
+            }
+            asm volatile("" ::"r"(dep) : "memory");
+            __syncwarp();
+            if (c.lane == 0) mbar_arrive(c.rempty0 + 8 * rs);
+        }
+        // the super-stage must be free: the MMAs of super-step j - kSuperStages have completed
+        if (j >= kSuperStages && !warp_wait_poll(c.oempty0 + 8 * ss, ((j / kSuperStages) - 1) & 1, c.err, 6, c.lane))
+            return;
         tc_fence_after();
         const uint32_t ta = c.tmem_a + (uint32_t)(os * kTmemAStride);
         tmem_st4(ta + 0 * 8, o.x.hi);
@@ -477,14 +519,16 @@ __device__ __forceinline__ void conv_loop(const ConvCtx& c, const ConvCols& kc, 
         fence_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (c.lane == 0) {
-            mbar_arrive(c.ofull0 + 8 * os);
-            // The raw stage goes back to the producer only now: every value read from it
-            // has been consumed by the stores above (a release issued right after the
-            // shared loads let the next TMA copy overwrite the stage before those loads
-            // had completed).
-            mbar_arrive(c.rempty0 + 8 * rs);
-        }
+        if (c.lane == 0) mbar_arrive(c.ofull0 + 8 * ss);
+    }
+    if (grp == kGroups - 1 && (c.nk % kSuper) != 0) {
+        // the last super-step has no step for this group: arrive for it all the same (after
+        // the same wait, so the arrival counts toward that super-step's phase)
+        const int j = c.nk / kSuper, ss = j % kSuperStages;
+        if (j >= kSuperStages && !warp_wait_poll(c.oempty0 + 8 * ss, ((j / kSuperStages) - 1) & 1, c.err, 6, c.lane))
+            return;
+        __syncwarp();
+        if (c.lane == 0) mbar_arrive(c.ofull0 + 8 * ss);
     }
 }
 
@@ -517,8 +561,8 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
             mbar_init(rfull0 + 8 * s, 1);
             mbar_init(rempty0 + 8 * s, kConvWarps);
         }
-        for (int s = 0; s < kOpStages; ++s) {
-            mbar_init(ofull0 + 8 * s, kConvWarps);
+        for (int s = 0; s < kSuperStages; ++s) {
+            mbar_init(ofull0 + 8 * s, kConvWarps * kGroups);   // one arrival per converter warp
             mbar_init(oempty0 + 8 * s, 1);
         }
         mbar_init(accum, 1);
@@ -561,24 +605,35 @@ gram_fused_kernel(const __grid_constant__ CUtensorMap xmap, const GramArgs a) {
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            // MMA issuer: A operands from tensor memory, B operands from shared memory
-            for (int k = 0; k < nk; ++k) {
-                const int s = k % kOpStages;
-                if (!mbar_wait_spin(ofull0 + 8 * s, (k / kOpStages) & 1, a.err, 2)) break;
+            // MMA issuer: A operands from tensor memory, B operands from shared memory.  The
+            // descriptors of stage s differ from stage 0's only in the start-address field
+            // (shared addresses stay below 2^18, so the 14-bit field never carries).
+            const uint64_t d0 = umma_desc(smem_u32(bop0));
+            const int nj = (nk + kSuper - 1) / kSuper;
+            for (int j = 0; j < nj; ++j) {
+                // one wait and one commit per super-step (both steps' operands)
+                const int ss = j % kSuperStages;
+                if (!mbar_wait_spin(ofull0 + 8 * ss, (j / kSuperStages) & 1, a.err, 2)) break;
                 tc_fence_after();
-                const uint32_t ta = tmem + kTmemA + (uint32_t)(s * kTmemAStride);
-                const uint32_t bst = smem_u32(bop0 + s * kBStageBytes);
-                // [b' | ycen b'] tiles are 256 consecutive K-major rows: one N = 256 MMA
-                const uint64_t bH = umma_desc(bst + kBH), bL = umma_desc(bst + kBL);
-                const uint64_t bQH = umma_desc(bst + kBQH), bQL = umma_desc(bst + kBQL);
-                const uint32_t acc = k > 0 ? 1u : 0u;
-                umma_ta(tmem + kTmemCW, ta + 0 * 8, bH, kIdesc256, acc);   // [C|W]: XH.[BH|WBH]
-                umma_ta(tmem + kTmemCW, ta + 0 * 8, bL, kIdesc256, 1u);    //        XH.[BL|WBL]
-                umma_ta(tmem + kTmemCW, ta + 1 * 8, bH, kIdesc256, 1u);    //        XL.[BH|WBH]
-                umma_ta(tmem + kTmemQ, ta + 2 * 8, bQH, kIdesc, acc);      // Q:     QH.BQH
-                umma_ta(tmem + kTmemQ, ta + 2 * 8, bQL, kIdesc, 1u);       //        QH.BQL
-                umma_ta(tmem + kTmemQ, ta + 3 * 8, bQH, kIdesc, 1u);       //        QL.BQH
-                umma_commit(oempty0 + 8 * s);  // operand stage free once these MMAs have read it
+                #pragma unroll
+                for (int e = 0; e < kSuper; ++e) {
+                    const int k = j * kSuper + e;
+                    if (k >= nk) break;
+                    const int s = ss * kSuper + e;   // == k % kOpStages
+                    const uint32_t ta = tmem + kTmemA + (uint32_t)(s * kTmemAStride);
+                    const uint64_t ds = d0 + (uint64_t)((s * kBStageBytes) >> 4);
+                    // [b' | ycen b'] tiles are 256 consecutive K-major rows: one N = 256 MMA
+                    const uint64_t bH = ds + (kBH >> 4), bL = ds + (kBL >> 4);
+                    const uint64_t bQH = ds + (kBQH >> 4), bQL = ds + (kBQL >> 4);
+                    const uint32_t acc = k > 0 ? 1u : 0u;
+                    umma_ta(tmem + kTmemCW, ta + 0 * 8, bH, kIdesc256, acc);   // [C|W]: XH.[BH|WBH]
+                    umma_ta(tmem + kTmemCW, ta + 0 * 8, bL, kIdesc256, 1u);    //        XH.[BL|WBL]
+                    umma_ta(tmem + kTmemCW, ta + 1 * 8, bH, kIdesc256, 1u);    //        XL.[BH|WBH]
+                    umma_ta(tmem + kTmemQ, ta + 2 * 8, bQH, kIdesc, acc);      // Q:     QH.BQH
+                    umma_ta(tmem + kTmemQ, ta + 2 * 8, bQL, kIdesc, 1u);       //        QH.BQL
+                    umma_ta(tmem + kTmemQ, ta + 3 * 8, bQH, kIdesc, 1u);       //        QL.BQH
+                }
+                umma_commit(oempty0 + 8 * ss);  // super-stage free once these MMAs have read it
             }
             umma_commit(accum);  // all issued MMAs complete (also on the error path)
         }
