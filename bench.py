@@ -288,7 +288,7 @@ class ClockSampler:
         taken = [(t, l) for t, l in self.lines if t_begin <= t <= t_end + self.INTERVAL_MS / 1e3]
         if not taken:
             taken = [(t, l) for t, l in self.lines if t >= t_begin][:1]
-        sm, smax, reasons = [], [], set()
+        sm, smax, watts, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for _, line in taken:
             parts = [p.strip() for p in line.split(",")]
@@ -299,11 +299,16 @@ class ClockSampler:
                 smax.append(float(parts[2]))
             except ValueError:
                 continue
+            try:
+                watts.append(float(parts[3]))
+            except ValueError:
+                pass
             for nm, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None,
+                "power_w": statistics.median(watts) if watts else None,
                 "reasons": sorted(reasons), "samples": len(sm),
                 "window_ms": round((t_end - t_begin) * 1e3, 1)}
 
