@@ -199,10 +199,10 @@ NCU_TRAFFIC_BYTES = {
     # Gram kernel, 250k-row capture (258 MB read: the fp32 matrix once; ~86 MB of chunk
     # partials written) scaled by the rows processed to 1e6 rows
     ("config2", "gram_tc"): 1.376e9,
-    # Gram kernel on the 2048-column table, 250k-row capture (4.10 GB read: the fp32 matrix
-    # about twice, L2 hit rate 78 %; 0.82 GB of chunk partials written) scaled by the rows
+    # Gram kernel on the 2048-column table, 250k-row capture (4.02 GB read: the fp32 matrix
+    # about twice, L2 hit rate 79 %; 0.80 GB of chunk partials written) scaled by the rows
     # processed to 2e6 rows
-    ("config5", "gram_tc"): 3.934e10,
+    ("config5", "gram_tc"): 3.854e10,
 }
 
 
