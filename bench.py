@@ -96,19 +96,36 @@ def fill_config4(packed: np.ndarray, n: int):
     packed[512] = y.astype(np.float32)
 
 
-def fill_config5(packed: np.ndarray, n: int):
-    """2048 N(0,1) columns written column by column; 16 planted pairs with
-    |beta| in linspace(0.05, 0.5); Bernoulli(sigmoid(sum beta x_a x_b)) target."""
-    rng = np.random.default_rng(0)
+def config5_column(c: int, n: int) -> np.ndarray:
+    """Column c of the wide table: N(0,1) from its own seeded generator, so any subset of
+    columns can be built alone (a rank builds only the column blocks its shard reads)."""
+    return np.random.default_rng(50_000 + c).standard_normal(n, dtype=np.float32)
+
+
+def fill_config5(packed: np.ndarray, n: int, cols=None):
+    """2048 N(0,1) columns (one seeded generator per column, built on all host threads); 16
+    planted pairs with |beta| in linspace(0.05, 0.5); Bernoulli(sigmoid(sum beta x_a x_b))
+    target.  cols: the columns to write (default all); the target is always written, from
+    the planted columns whether or not they are among cols."""
+    from concurrent.futures import ThreadPoolExecutor
     f = packed.shape[0] - 1
-    for c in range(f):
-        packed[c] = rng.standard_normal(n, dtype=np.float32)
+    rng = np.random.default_rng(5)
     idx = rng.permutation(f)[:32].reshape(16, 2)
     beta = np.linspace(0.05, 0.5, 16) * rng.choice([-1.0, 1.0], 16)
+    want = list(range(f)) if cols is None else sorted(set(int(c) for c in cols))
+
+    def put(c):
+        packed[c] = config5_column(c, n)
+
+    with ThreadPoolExecutor(max(1, min(32, os.cpu_count() or 1))) as ex:
+        list(ex.map(put, want))
+    have = set(want)
     logit = np.zeros(n)
     for (a, b), w in zip(idx, beta):
-        logit += w * packed[a].astype(np.float64) * packed[b]
-    packed[f] = (rng.random(n) < 1.0 / (1.0 + np.exp(-logit))).astype(np.float32)
+        xa = packed[a] if a in have else config5_column(int(a), n)
+        xb = packed[b] if b in have else config5_column(int(b), n)
+        logit += w * xa.astype(np.float64) * xb
+    packed[f] = (np.random.default_rng(6).random(n) < 1.0 / (1.0 + np.exp(-logit))).astype(np.float32)
     return idx
 
 
@@ -529,13 +546,58 @@ def run_ours(args):
         f = scaled_width(world)
     scaling = "weak" if args.workload == "config2" else "strong"
 
-    packed_t = torch.empty((f + 1, n), dtype=torch.float32, pin_memory=True)
-    packed = packed_t.numpy()
-    build_packed(args.workload, packed)
+    # Sharded ingest over NVLink (N > 1 and F divisible by N): rank r owns features
+    # [r F/N, (r+1) F/N).  Each step it copies only those from the host (with the target and
+    # the mask), and an in-place NCCL all-gather on the bucket's stream fills in the rest of
+    # its replica, so the host links carry the matrix once in total at any N.
+    nvl = world > 1 and f % world == 0
+    c0, c1 = (rank * f // world, (rank + 1) * f // world) if nvl else (0, f)
+    # Host input.  A rank other than 0 of a sharded wide-table run builds and pins only its
+    # own features and the target; the rest of its buffer is never written and holds no
+    # memory.  Rank 0 builds the whole table: it also checks the merged top-k against one
+    # GPU's.
+    pinned_ranges = []
+    partial = nvl and args.workload == "config5" and rank != 0
+    if not partial:
+        packed_t = torch.empty((f + 1, n), dtype=torch.float32, pin_memory=True)
+        packed = packed_t.numpy()
+        build_packed(args.workload, packed)
+    else:
+        packed = np.empty((f + 1, n), dtype=np.float32)
+        fill_config5(packed, n, cols=range(c0, c1))
+        cudart = torch.cuda.cudart()
+        for r0, r1 in ((c0, c1), (f, f + 1)):
+            ptr, size = packed[r0].ctypes.data, (r1 - r0) * n * 4
+            err = cudart.cudaHostRegister(ptr, size, 0)
+            if int(err) != 0:
+                raise RuntimeError(f"cudaHostRegister of rows {r0}-{r1} failed: {err}")
+            pinned_ranges.append(ptr)
     mask = np.zeros(n, dtype=np.uint8)
 
     bucket = _native.Bucket(n, f, device=local)
-    bucket.upload_packed(packed, mask)
+    if nvl:
+        bucket_stream = torch.cuda.ExternalStream(bucket.stream_ptr())
+        ptr, ld = bucket.device_columns(0, f)
+
+        class _DeviceColumns:   # the bucket's features 0..F-1 as one flat device array
+            __cuda_array_interface__ = {"shape": (f * ld,), "typestr": "<f4", "data": (ptr, False),
+                                        "version": 3, "stream": None}
+
+        replica = torch.as_tensor(_DeviceColumns(), device="cuda")
+        own = replica[c0 * ld:c1 * ld]
+
+    def ingest():
+        # this step's host->device copy: own features + target + mask, then NVLink all-gather
+        bucket.upload_columns(packed[c0:c1], c0, packed[f], mask)
+        with torch.cuda.stream(bucket_stream):
+            dist.all_gather_into_tensor(replica, own)
+        bucket.mark_updated()
+
+    if nvl:
+        ingest()
+        torch.cuda.synchronize()
+    else:
+        bucket.upload_packed(packed, mask)
 
     def score():
         # this rank's library call (every kernel of the step that is this library's)
@@ -626,11 +688,16 @@ def run_ours(args):
                 multi_check += " (" + "; ".join(diff) + ")"
         dist.barrier()
 
-    # e2e: the same step through the C ABI from pinned host buffers, upload included
-    # (gafime_allpairs_topk_host: the copy of each column block overlapped with the scoring
-    # of the tiles it completes); with N > 1 the shards' results are exchanged from the host
-    # copies every rank holds after that call (all-gather of 16-byte records, device merge)
+    # e2e: the same step through the C ABI from pinned host buffers, upload included.
+    # One GPU: gafime_allpairs_topk_host (the copy of each column block overlapped with the
+    # scoring of the tiles it completes).  N GPUs with F divisible by N: each rank copies its
+    # own features, NVLink all-gathers the replica, then the device step of the timed region.
+    # Otherwise each shard's streamed call copies the blocks it reads and the results are
+    # exchanged from the host copies every rank holds (all-gather of 16-byte records).
     def e2e_step():
+        if nvl:
+            ingest()
+            return step()
         res = bucket.topk_from_host(packed, ops, k, metric=w["metric"], center=w["center"], div_eps=w["eps"],
                                     mi_bins=w["bins"], shard_id=rank, n_shards=world, mask=mask)
         if world == 1:
@@ -718,7 +785,10 @@ def run_ours(args):
                "sample": arm.describe(units, dt)}
 
     h2d = packed.nbytes + mask.nbytes
-    if world > 1 and w["metric"] == "pearson" and not w["center"]:
+    if nvl:
+        # own features + target per rank (the rest arrives over NVLink)
+        h2d = (c1 - c0 + 1) * n * 4 + mask.nbytes
+    elif world > 1 and w["metric"] == "pearson" and not w["center"]:
         # a shard's streamed call copies the target and the 128-column blocks its tiles read
         blocks = {int(x) // 2 for x in np.asarray(_native.shard_tiles(f, rank, world)).reshape(-1)}
         cols = sum(min(128, f - 128 * B) for B in blocks)
@@ -757,6 +827,10 @@ def run_ours(args):
         line["top3"] = top
         print(json.dumps(line), flush=True)
     bucket.free()
+    if pinned_ranges:
+        torch.cuda.synchronize()
+        for ptr in pinned_ranges:
+            torch.cuda.cudart().cudaHostUnregister(ptr)
     if world > 1:
         dist.destroy_process_group()
     return 0

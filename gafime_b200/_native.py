@@ -49,7 +49,8 @@ EXPORTED = (
     "gafime_pipeline_pending", "gafime_pipeline_flush", "gafime_pipeline_free", "gafime_pearson_cuda",
     "gafime_contiguous_bucket_upload_target", "gafime_contiguous_bucket_gather", "gafime_spearman_scores",
     "gafime_allpairs_topk_host", "gafime_contiguous_bucket_upload_rows", "gafime_allpairs_rescored",
-    "gafime_allpairs_topk_device", "gafime_topk_merge_device",
+    "gafime_allpairs_topk_device", "gafime_topk_merge_device", "gafime_contiguous_bucket_upload_columns",
+    "gafime_contiguous_bucket_device_columns", "gafime_contiguous_bucket_mark_updated",
 )
 
 # kernel ids of the timing registry (GAFIME_KERNEL_* in the header)
@@ -96,6 +97,10 @@ def _bind(lib: ctypes.CDLL) -> None:
         "gafime_contiguous_bucket_gather": ([_vp, _vp, _vp, ctypes.c_int32, _vp, _i64], _i),
         "gafime_spearman_scores": ([_vp, _vp, _vp, _i64, _i, _i, _f, _vp], _i),
         "gafime_contiguous_bucket_upload_rows": ([_vp, _vp, _vp, _vp], _i),
+        "gafime_contiguous_bucket_upload_columns": ([_vp, _vp, _i64, _i64, _vp, _vp], _i),
+        "gafime_contiguous_bucket_device_columns": ([_vp, _i64, _i64, ctypes.POINTER(_vp),
+                                                     ctypes.POINTER(_i64)], _i),
+        "gafime_contiguous_bucket_mark_updated": ([_vp], _i),
         "gafime_allpairs_topk_host": ([_vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _i, _i, _i, _vp, _vp, _vp, _vp],
                                       _i),
         "gafime_allpairs_scores_noalloc": ([_vp, _i64, _vp, _i, _i, _i, _f, _vp, _vp], _i),
@@ -227,6 +232,29 @@ class Bucket:
         m = self._mask if mask is None else np.ascontiguousarray(mask, dtype=np.uint8)
         check("gafime_contiguous_bucket_upload_rows",
               self.lib.gafime_contiguous_bucket_upload_rows(self.handle, _ptr(Xr), _ptr(yv), _ptr(m)))
+
+    def upload_columns(self, cols: np.ndarray, c0: int, y: np.ndarray, mask: Optional[np.ndarray] = None) -> None:
+        """Sharded ingest: copy features c0 .. c0 + len(cols) - 1 (cols: (c, n) float32,
+        C-contiguous, ideally pinned), the target and the mask, queued on the bucket's stream
+        without waiting; a collective on device_columns() fills the other features."""
+        if cols.dtype != np.float32 or not cols.flags.c_contiguous or cols.ndim != 2 or cols.shape[1] != self.n:
+            raise ValueError(f"cols must be a C-contiguous float32 (c, {self.n}) array")
+        yv = np.ascontiguousarray(y, dtype=np.float32)
+        m = self._mask if mask is None else np.ascontiguousarray(mask, dtype=np.uint8)
+        self._keep = (cols, yv, m)   # alive until the queued copies have run
+        check("gafime_contiguous_bucket_upload_columns", self.lib.gafime_contiguous_bucket_upload_columns(
+            self.handle, _ptr(cols), int(c0), int(c0) + cols.shape[0], _ptr(yv), _ptr(m)))
+
+    def device_columns(self, c0: int, c1: int) -> Tuple[int, int]:
+        """(device address of feature c0, floats between consecutive features)."""
+        p, ld = ctypes.c_void_p(0), ctypes.c_int64(0)
+        check("gafime_contiguous_bucket_device_columns", self.lib.gafime_contiguous_bucket_device_columns(
+            self.handle, int(c0), int(c1), ctypes.byref(p), ctypes.byref(ld)))
+        return int(p.value or 0), int(ld.value)
+
+    def mark_updated(self) -> None:
+        """Features were written through device_columns(): re-check them before scoring."""
+        check("gafime_contiguous_bucket_mark_updated", self.lib.gafime_contiguous_bucket_mark_updated(self.handle))
 
     def set_target(self, y: np.ndarray) -> None:
         """Replace only the target (n floats); the features stay resident."""

@@ -544,6 +544,42 @@ int gafime_contiguous_bucket_upload(ContiguousBucket bucket, const float* h_data
     return check_finite(*b, &finite);
 }
 
+int gafime_contiguous_bucket_upload_columns(ContiguousBucket bucket, const float* h_cols, int64_t c0, int64_t c1,
+                                            const float* h_y, const uint8_t* h_mask) {
+    if (!bucket || !h_y || !h_mask) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket* b = (Bucket*)bucket;
+    if (c0 < 0 || c1 < c0 || c1 > b->f || (c1 > c0 && !h_cols)) return GAFIME_ERROR_INVALID_ARGS;
+    cudaSetDevice(b->device);
+    // queued on the bucket's stream, where a collective that fills the other features runs
+    cudaError_t e = cudaSuccess;
+    if (c1 > c0)
+        e = cudaMemcpy2DAsync(b->d_data + c0 * b->ld, (size_t)b->ld * sizeof(float), h_cols,
+                              (size_t)b->n * sizeof(float), (size_t)b->n * sizeof(float), (size_t)(c1 - c0),
+                              cudaMemcpyHostToDevice, b->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(b->d_data + b->f * b->ld, h_y, (size_t)b->n * sizeof(float), cudaMemcpyHostToDevice,
+                            b->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(b->d_mask, h_mask, (size_t)b->n, cudaMemcpyHostToDevice, b->stream);
+    b->finite_state = -1;   // checked by the next scoring call
+    return e == cudaSuccess ? GAFIME_SUCCESS : status_from(e);
+}
+
+int gafime_contiguous_bucket_device_columns(ContiguousBucket bucket, int64_t c0, int64_t c1, float** d_ptr,
+                                            int64_t* ld) {
+    if (!bucket || !d_ptr || !ld) return GAFIME_ERROR_INVALID_ARGS;
+    Bucket* b = (Bucket*)bucket;
+    if (c0 < 0 || c1 < c0 || c1 > b->f) return GAFIME_ERROR_INVALID_ARGS;
+    *d_ptr = b->d_data + c0 * b->ld;
+    *ld = b->ld;
+    return GAFIME_SUCCESS;
+}
+
+int gafime_contiguous_bucket_mark_updated(ContiguousBucket bucket) {
+    if (!bucket) return GAFIME_ERROR_INVALID_ARGS;
+    ((Bucket*)bucket)->finite_state = -1;
+    return GAFIME_SUCCESS;
+}
+
 int gafime_contiguous_bucket_upload_rows(ContiguousBucket bucket, const float* h_rows, const float* h_y,
                                          const uint8_t* h_mask) {
     if (!bucket || !h_rows || !h_y || !h_mask) return GAFIME_ERROR_INVALID_ARGS;

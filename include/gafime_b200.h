@@ -400,6 +400,31 @@ int gafime_contiguous_bucket_upload_target(ContiguousBucket bucket, const float*
 int gafime_contiguous_bucket_gather(ContiguousBucket dst, ContiguousBucket src, const int32_t* cols,
                                     int32_t n_cols, const int64_t* rows, int64_t n_rows);
 
+/* NEW.  Sharded ingest of a bucket replicated on several GPUs (one process per GPU): each
+ * rank copies only features [c0, c1) from the host with this call, and a collective over
+ * NVLink (an all-gather on the bucket's stream, on the device range that
+ * gafime_contiguous_bucket_device_columns reports) fills in the others, so the host link
+ * carries the matrix once however many GPUs hold it.  h_cols holds features c0..c1-1 as
+ * (c1 - c0) x n_samples floats (the same layout as rows c0..c1-1 of the upload's h_data),
+ * h_y the n_samples target values and h_mask the fold mask, all ideally pinned.  The copies
+ * are queued on the bucket's stream and the call returns without waiting for them; the
+ * caller keeps the host buffers intact until that stream has passed them.  The data is
+ * checked for non-finite values by the next scoring call, as after an upload. */
+int gafime_contiguous_bucket_upload_columns(ContiguousBucket bucket, const float* h_cols, int64_t c0, int64_t c1,
+                                            const float* h_y, const uint8_t* h_mask);
+
+/* NEW.  Device address of feature c0 of a bucket and the distance between consecutive
+ * features in floats (*ld >= n_samples; rows n_samples..ld-1 of every feature are zero and
+ * stay zero).  Features c0..c1-1 are the contiguous range [*d_ptr, *d_ptr + (c1 - c0) * ld),
+ * which a collective may fill in place; the caller then calls
+ * gafime_contiguous_bucket_mark_updated before scoring. */
+int gafime_contiguous_bucket_device_columns(ContiguousBucket bucket, int64_t c0, int64_t c1, float** d_ptr,
+                                            int64_t* ld);
+
+/* NEW.  Declares that features were written through gafime_contiguous_bucket_device_columns:
+ * the next scoring call checks the whole matrix for non-finite values again. */
+int gafime_contiguous_bucket_mark_updated(ContiguousBucket bucket);
+
 /* ------------------------------------------- NEW: no device allocation ---- */
 
 /* Largest problem gafime_allpairs_scores_noalloc accepts. */

@@ -279,6 +279,47 @@ def test_shards_sum_the_same_row_chunks_as_one_gpu(native):
                     np.testing.assert_array_equal(u, v)
 
 
+def test_sharded_ingest_by_column_ranges(native):
+    """The sharded-ingest entry points on one GPU: features uploaded range by range
+    (gafime_contiguous_bucket_upload_columns, as the ranks of a replicated bucket do before
+    their all-gather) score exactly like one upload; gafime_contiguous_bucket_device_columns
+    reports feature c at base + c * ld; a value written through that address and declared
+    with gafime_contiguous_bucket_mark_updated is checked by the next scoring call."""
+    import torch
+    rng = np.random.default_rng(31)
+    n, f = 5000, 300
+    X = rng.standard_normal((n, f)).astype(np.float32)
+    y = rng.standard_normal(n).astype(np.float32)
+    packed = np.ascontiguousarray(np.vstack([X.T, y[None, :]]))
+    with bucket_for(native, X, y) as ref:
+        want = ref.topk(["multiply", "divide"], 30, div_eps=1e-6)
+    with native.Bucket(n, f) as b:
+        for c0, c1 in ((0, 100), (100, 128), (128, 300)):
+            b.upload_columns(packed[c0:c1], c0, packed[f])
+        torch.cuda.synchronize()
+        got = b.topk(["multiply", "divide"], 30, div_eps=1e-6)
+        for op in ("multiply", "divide"):
+            for u, v in zip(got[op], want[op]):
+                np.testing.assert_array_equal(u, v)
+        p0, ld = b.device_columns(0, f)
+        p7, ld7 = b.device_columns(7, 8)
+        assert ld == ld7 >= n and p7 == p0 + 7 * ld * 4
+
+        class _Col:   # feature 7 on the device
+            __cuda_array_interface__ = {"shape": (ld,), "typestr": "<f4", "data": (p7, False),
+                                        "version": 3, "stream": None}
+
+        col = torch.as_tensor(_Col(), device="cuda")
+        assert torch.equal(col[:n].cpu(), torch.from_numpy(X[:, 7]))
+        assert not col[n:].any()          # padding rows are zero
+        col[11] = float("nan")
+        torch.cuda.synchronize()
+        b.mark_updated()
+        with pytest.raises(native.GafimeError) as e:
+            b.topk(["multiply"], 3)
+        assert e.value.code == -1
+
+
 def test_non_finite_input_is_rejected(native):
     X = np.ones((100, 4), dtype=np.float32)
     X[5, 2] = np.nan

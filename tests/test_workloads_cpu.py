@@ -51,3 +51,17 @@ def test_config5_planted_pairs():
     idx = bench.fill_config5(packed, n)
     assert idx.shape == (16, 2) and len(np.unique(idx)) == 32   # 16 pairs of distinct columns
     assert set(np.unique(packed[2048])) == {0.0, 1.0}
+
+
+def test_config5_column_subset_matches_the_full_table():
+    """A rank of a sharded run builds only the column blocks its shard reads: those columns
+    and the target equal the full build's, and the other columns are left untouched."""
+    n = 3000
+    full = np.empty((2049, n), dtype=np.float32)
+    bench.fill_config5(full, n)
+    cols = list(range(128, 384)) + list(range(1920, 2048))
+    part = np.zeros((2049, n), dtype=np.float32)
+    bench.fill_config5(part, n, cols=cols)
+    assert np.array_equal(part[cols], full[cols])
+    assert np.array_equal(part[2048], full[2048])
+    assert not part[:128].any() and not part[384:1920].any()
