@@ -4,7 +4,7 @@
 // one launch + memset + D2H + sync per pair) and its Rust pair enumeration
 // (src/cpu/gafime_cpu/src/batch_launcher.rs:216-247, smart_scheduler.rs:78-176) with:
 //   1. fp64 column statistics (bucket.cu), once per call;
-//   2. upper-triangle 64 x 64 pair tiles, assigned to shards by pair count;
+//   2. upper-triangle 64 x 64 pair tiles, assigned to shards by tile work and column reads;
 //   3. split-K over rows so every SM has work, fp64 partials per (tile, split);
 //   4. the scoring epilogue with a per-tile bitonic top-k, one launch per operator;
 //   5. a device merge of the per-tile lists and one small D2H per operator.
@@ -42,10 +42,14 @@ int64_t tile_pairs(int bi, int bj, int64_t f) {
 }  // namespace
 
 // Upper-triangle 64 x 64 tiles of this shard.  The pair space is dealt out in
-// 128 x 128 blocks (the tensor-core Gram tile): blocks in decreasing pair count (ties in
-// row-major order), each to the shard with the fewest pairs so far (ties: lowest shard
-// id); a shard scores the 64-tiles inside its blocks.  Every process derives the same
-// split without communication.
+// 128 x 128 blocks (the tensor-core Gram tile): blocks in decreasing work (ties in
+// row-major order), each to the shard with the least work so far (ties: lowest shard id);
+// a shard scores the 64-tiles inside its blocks.  A block's work is the number of 64-tiles
+// it holds (4 off the diagonal, 3 on it), not its pair count: a tile costs the same
+// whether its pairs are distinct or mirrored, and a diagonal 128-tile on the Gram path
+// measured ~0.8 of an off-diagonal one (0.5 by pair count, which left the shards that
+// held the diagonal 5-9 % slower).  Every process derives the same split without
+// communication.
 static std::vector<TileCoord> compute_shard_tiles(int64_t f, int shard_id, int n_shards) {
     int nb = (int)((f + kTile - 1) / kTile);
     int nb2 = (nb + 1) / 2;
@@ -63,10 +67,9 @@ static std::vector<TileCoord> compute_shard_tiles(int64_t f, int shard_id, int n
                 for (int db = 0; db < 2; ++db) {
                     int bi = 2 * BI + da, bj = 2 * BJ + db;
                     if (bi > bj || bi >= nb || bj >= nb) continue;
-                    int64_t p = tile_pairs(bi, bj, f);
-                    if (p == 0) continue;
+                    if (tile_pairs(bi, bj, f) == 0) continue;
                     blk.sub[blk.ns++] = {bi, bj};
-                    blk.w += p;
+                    blk.w += 1;   // work: one 64-tile
                 }
             if (blk.w > 0) blocks.push_back(blk);
         }
@@ -82,7 +85,7 @@ static std::vector<TileCoord> compute_shard_tiles(int64_t f, int shard_id, int n
         owner[x] = best;
     }
     // Locality: a shard prepares the 128-column blocks its tiles read, so swap blocks of equal
-    // pair count between two shards while that lowers the larger, then the summed, number of
+    // work between two shards while that lowers the larger, then the summed, number of
     // column blocks the two read (the loads do not change).  Fixed scan order: every process
     // arrives at the same assignment.  Per-shard counts of the owned blocks touching each
     // column block make a trial swap O(1); skipped for very wide matrices.
@@ -129,33 +132,37 @@ static std::vector<TileCoord> compute_shard_tiles(int64_t f, int shard_id, int n
             if (!swapped) break;
         }
     }
-    // Grouped alternative: split the 128-column blocks into g contiguous groups; a unit is
-    // every block of one group pair (Ga, Gb), a <= b, so a shard owning units of few groups
-    // reads few column blocks (at 2048 columns over 8 shards, g = 4 gives each shard one
-    // cross-group unit or two in-group units: 8 of 16 blocks, against up to 16 above).
-    // Units in decreasing pair count go to the least-loaded shard (ties: lowest id).  Taken
-    // when its busiest shard has no more pairs than the assignment above (0.5 % slack) and
-    // reads fewer column blocks; every process derives the same choice.
+    // A shard's time is its tile work plus the preparation of every 128-column block its
+    // tiles read (statistics and operand scales over all rows of the block): per 64-tile
+    // ~0.2 ms and per block ~0.15 ms at 2e6 rows on the Gram path, both proportional to the
+    // rows.  cost = 4 work + 3 reads; a plan costs its busiest shard's cost.
     if (n_shards > 1) {
-        auto stats = [&](const std::vector<int>& own, int64_t* max_load, int* max_reads) {
+        auto plan_cost = [&](const std::vector<int>& own, int64_t* max_cost, int* max_reads) {
             std::vector<int64_t> ld((size_t)n_shards, 0);
             std::vector<std::vector<char>> rd((size_t)n_shards, std::vector<char>((size_t)nb2, 0));
             for (size_t x = 0; x < blocks.size(); ++x) {
                 ld[(size_t)own[x]] += blocks[x].w;
                 rd[(size_t)own[x]][(size_t)blocks[x].BI] = rd[(size_t)own[x]][(size_t)blocks[x].BJ] = 1;
             }
-            *max_load = 0;
+            *max_cost = 0;
             *max_reads = 0;
             for (int sh = 0; sh < n_shards; ++sh) {
-                *max_load = std::max(*max_load, ld[(size_t)sh]);
                 int r = 0;
                 for (char c : rd[(size_t)sh]) r += c;
+                *max_cost = std::max(*max_cost, 4 * ld[(size_t)sh] + 3 * (int64_t)r);
                 *max_reads = std::max(*max_reads, r);
             }
         };
-        int64_t best_load = 0;
+        // Grouped alternatives: split the 128-column blocks into g contiguous groups; a unit is
+        // every block of one group pair (Ga, Gb), a <= b, so a shard owning units of few
+        // groups reads few column blocks.  Units in decreasing work go to the least-loaded
+        // shard (ties: lowest id).  The cheapest plan is kept (ties: the earlier one).
+        const std::vector<int> greedy = owner;
+        std::vector<int> grouped;
+        std::vector<std::vector<int>> starts;   // every grouped plan, searched when few blocks
+        const bool search_all = blocks.size() <= 512;
+        int64_t best_cost = INT64_MAX;
         int best_reads = 0;
-        stats(owner, &best_load, &best_reads);
         for (int g = 2; g <= nb2; ++g) {
             if ((int64_t)g * (g + 1) / 2 < n_shards) continue;
             std::vector<int> grp((size_t)nb2);
@@ -180,13 +187,100 @@ static std::vector<TileCoord> compute_shard_tiles(int64_t f, int shard_id, int n
             std::vector<int> own(blocks.size());
             for (size_t x = 0; x < blocks.size(); ++x)
                 own[x] = uown[(size_t)uid(grp[(size_t)blocks[x].BI], grp[(size_t)blocks[x].BJ])];
-            int64_t ml = 0;
+            int64_t mc = 0;
             int mr = 0;
-            stats(own, &ml, &mr);
-            if ((double)ml <= 1.005 * (double)best_load && mr < best_reads) {
-                owner = own;
-                best_load = std::max(best_load, ml);
+            plan_cost(own, &mc, &mr);
+            if (search_all) starts.push_back(own);
+            if (mc < best_cost || (mc == best_cost && mr < best_reads)) {
+                grouped = own;
+                best_cost = mc;
                 best_reads = mr;
+            }
+        }
+        // Local search: move a block off the costliest shard (lowest id on ties) to the shard
+        // where the larger of the two new costs is smallest, or swap two blocks, while that
+        // lowers the costliest shard's cost.  Run from the greedy plan and from every grouped
+        // plan (only the cheapest grouped one above 512 blocks); the cheapest result is kept
+        // (ties: fewer column blocks, then the earlier start).  Fixed scan order: every process
+        // arrives at the same plan.
+        auto improve = [&](std::vector<int>& own) {
+            if (blocks.size() > 4096) return;
+            std::vector<int> cnt((size_t)n_shards * nb2, 0), reads((size_t)n_shards, 0);
+            std::vector<int64_t> work((size_t)n_shards, 0);
+            auto add = [&](int sh, int x, int d) {
+                work[(size_t)sh] += d * blocks[(size_t)x].w;
+                for (int B : {blocks[(size_t)x].BI, blocks[(size_t)x].BJ}) {
+                    int& c = cnt[(size_t)sh * nb2 + B];
+                    if (d > 0 && c++ == 0) ++reads[(size_t)sh];
+                    if (d < 0 && --c == 0) --reads[(size_t)sh];
+                }
+            };
+            auto cost = [&](int sh) { return 4 * work[(size_t)sh] + 3 * (int64_t)reads[(size_t)sh]; };
+            for (size_t x = 0; x < blocks.size(); ++x) add(own[x], (int)x, +1);
+            for (size_t it = 0; it < 4 * blocks.size(); ++it) {
+                int m = 0;
+                for (int sh = 1; sh < n_shards; ++sh)
+                    if (cost(sh) > cost(m)) m = sh;
+                const int64_t cm = cost(m);
+                int64_t best = cm;
+                int bx = -1, by = -1, bt = -1;
+                for (size_t x = 0; x < blocks.size(); ++x) {
+                    if (own[x] != m) continue;
+                    for (int t = 0; t < n_shards; ++t) {
+                        if (t == m) continue;
+                        add(m, (int)x, -1);
+                        add(t, (int)x, +1);
+                        const int64_t c = std::max(cost(m), cost(t));
+                        if (c < best) { best = c; bx = (int)x; by = -1; bt = t; }
+                        add(t, (int)x, -1);
+                        add(m, (int)x, +1);
+                    }
+                }
+                if (bx < 0) {   // swaps, only when no single move helps
+                    for (size_t x = 0; x < blocks.size() && bx < 0; ++x) {
+                        if (own[x] != m) continue;
+                        for (size_t y = 0; y < blocks.size(); ++y) {
+                            const int t = own[y];
+                            if (t == m || blocks[y].w >= blocks[x].w) continue;
+                            add(m, (int)x, -1);
+                            add(t, (int)y, -1);
+                            add(m, (int)y, +1);
+                            add(t, (int)x, +1);
+                            const int64_t c = std::max(cost(m), cost(t));
+                            add(t, (int)x, -1);
+                            add(m, (int)y, -1);
+                            add(t, (int)y, +1);
+                            add(m, (int)x, +1);
+                            if (c < best) { best = c; bx = (int)x; by = (int)y; bt = t; }
+                        }
+                    }
+                }
+                if (bx < 0) break;
+                add(m, bx, -1);
+                add(bt, bx, +1);
+                own[(size_t)bx] = bt;
+                if (by >= 0) {
+                    add(bt, by, -1);
+                    add(m, by, +1);
+                    own[(size_t)by] = m;
+                }
+            }
+        };
+        if (!search_all && !grouped.empty()) starts.push_back(grouped);
+        owner = greedy;
+        improve(owner);
+        int64_t cbest = 0;
+        int rbest = 0;
+        plan_cost(owner, &cbest, &rbest);
+        for (std::vector<int>& st : starts) {
+            improve(st);
+            int64_t c = 0;
+            int r = 0;
+            plan_cost(st, &c, &r);
+            if (c < cbest || (c == cbest && r < rbest)) {
+                owner = st;
+                cbest = c;
+                rbest = r;
             }
         }
     }

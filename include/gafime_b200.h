@@ -310,11 +310,12 @@ int gafime_unary_scores(ContiguousBucket bucket, int metric, int mi_bins, double
  * NEW.  Host only.  The 64 x 64 pair tiles (block row bi, block column bj, bi <= bj;
  * pairs i in [64 bi, 64 bi + 64) x j in [64 bj, 64 bj + 64), i < j) that shard shard_id
  * of n_shards scores in gafime_allpairs_topk.  The pair space is dealt out in 128 x 128
- * blocks (the tensor-core tile) in decreasing pair count (ties in row-major order), each
- * to the shard with the fewest pairs so far (ties: lowest id); then blocks of equal pair
- * count trade shards while that lowers the number of 128-column blocks a shard reads (its
- * statistics pass covers those).  Every process derives the same split without
- * communicating; a shard scores the 64-tiles inside its blocks.  out_tiles receives
+ * blocks (the tensor-core tile).  A shard's cost is 4 x the 64-tiles it computes (a block
+ * holds 4, or 3 on the diagonal) + 3 x the 128-column blocks its tiles read (its statistics
+ * pass covers those); the plan with the lowest busiest-shard cost is kept, from a
+ * least-loaded greedy split and group-pair splits, each refined by moving and swapping
+ * blocks.  Every process derives the same split without communicating; a shard scores the
+ * 64-tiles inside its blocks.  out_tiles receives
  * 2 * *out_count ints (bi, bj); returns GAFIME_ERROR_INVALID_ARGS with *out_count set
  * when max_tiles is too small.
  */

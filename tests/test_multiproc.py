@@ -81,15 +81,19 @@ def test_shards_partition_the_pair_space():
             seen |= pairs
             loads.append(len(pairs))
         assert len(seen) == f * (f - 1) // 2
-        if f >= 724:  # enough tiles for the greedy split to balance within 10 %
-            assert max(loads) <= 1.1 * (f * (f - 1) / 2) / world
+        if f >= 724:
+            # the plan balances tile work (64 x 64 tiles computed, 3 or 4 per 128-block), not
+            # pair counts: the busiest shard is within one block of the mean
+            tiles = [len(_native.shard_tiles(f, r, world)) for r in range(world)]
+            assert sum(tiles) == ((f + 63) // 64) * ((f + 63) // 64 + 1) // 2
+            assert max(tiles) <= sum(tiles) / world + 4, tiles
 
 
 def test_shards_read_few_column_blocks():
-    """Blocks of equal pair count trade shards toward fewer 128-column blocks per shard
-    (each shard's statistics pass covers the blocks it reads); the loads are unchanged."""
+    """A shard prepares every 128-column block its tiles read, so the plan's cost counts
+    those blocks beside the tile work and the plans keep them few."""
     from gafime_b200 import _native
-    for f, world, most in ((724, 8, 3), (512, 4, 3), (362, 2, 3), (2048, 8, 8), (2048, 4, 12)):
+    for f, world, most in ((724, 8, 3), (512, 4, 3), (362, 2, 3), (2048, 8, 11), (2048, 4, 12)):
         reads = []
         for r in range(world):
             t = _native.shard_tiles(f, r, world)
@@ -97,22 +101,28 @@ def test_shards_read_few_column_blocks():
         assert max(reads) <= most, reads
 
 
-def test_grouped_assignment_balances_the_wide_table():
-    """At 2048 columns the pair space goes out in group-pair units: over 8 shards each holds
-    one cross-group unit or two in-group units (8 of 16 column blocks), within 0.1 % of the
-    mean pair count; over 4 shards 12 blocks each."""
+def test_wide_table_plan_balances_work_and_reads():
+    """At 2048 columns (136 Gram tiles: 16 diagonal of 3 work units, 120 of 4) the plan
+    costs a shard 4 x its 64-tiles + 3 x the 128-column blocks it reads.  Over 4 shards every
+    shard gets 132 tiles and reads 12 of 16 blocks; over 8, 65-67 tiles and at most 11
+    blocks, the busiest shard within 1 % of the mean cost."""
     from gafime_b200 import _native
     f = 2048
     total = f * (f - 1) // 2
-    for world, blocks in ((8, 8), (4, 12)):
-        loads = []
+    for world in (4, 8):
+        tiles, reads, pairs = [], [], 0
         for r in range(world):
-            pi, pj = _native.shard_pairs(f, r, world)
-            loads.append(len(pi))
-            t = _native.shard_tiles(f, r, world)
-            assert len({int(x) // 2 for x in np.asarray(t).reshape(-1)}) == blocks
-        assert sum(loads) == total
-        assert max(loads) <= 1.001 * total / world
+            t = np.asarray(_native.shard_tiles(f, r, world)).reshape(-1)
+            tiles.append(len(t) // 2)
+            reads.append(len({int(x) // 2 for x in t}))
+            pairs += len(_native.shard_pairs(f, r, world)[0])
+        assert pairs == total and sum(tiles) == 528
+        cost = [4 * a + 3 * b for a, b in zip(tiles, reads)]
+        if world == 4:
+            assert tiles == [132] * 4 and reads == [12] * 4
+        else:
+            assert min(tiles) >= 65 and max(tiles) <= 67 and max(reads) <= 11, (tiles, reads)
+            assert max(cost) <= 1.01 * sum(cost) / world, cost
 
 
 def test_shard_assignment_is_cheap_for_wide_matrices():
